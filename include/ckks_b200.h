@@ -1,0 +1,168 @@
+/*
+ * ckks_b200.h -- C ABI of the B200 CKKS evaluation engine.
+ *
+ * This is the drop-in boundary for the server-side hot path of the encrypted
+ * DNAGPT block driver.  The reference binds FIDESlib's OpenFHE-compatible C++
+ * API (`#include <fideslib.hpp>`, `using namespace fideslib`) from
+ *   fhe/gpu_real_scheme_b/src/real_dnagpt_fides_scheme_b_simd_full_t103_depth13_
+ *   digits3_ring65536_cpudiagcache_t123.cpp            ("T123.cpp" below)
+ * Every entry point names the reference call it replaces.  Plain pointers and
+ * sizes only; no CUDA or torch types cross the boundary (device pointers are
+ * passed as uint64_t* to device memory where stated).
+ *
+ * Conventions
+ *  - Every function returns CKKS_OK (0) or a CKKS_E* status; the message of
+ *    the last failure on the calling thread is ckks_last_error().  (The
+ *    reference reports failures as C++ exceptions, mapped to exit code 2 in
+ *    T123.cpp:1757-1761.)
+ *  - Levels follow OpenFHE: level 0 is a fresh ciphertext with all Q limbs;
+ *    each Rescale raises the level by one and drops one limb.
+ *  - Operations are asynchronous on the context's CUDA stream; functions that
+ *    return data to the host (export, decode) synchronise it.  A context is not
+ *    thread-safe; use one context per host thread.
+ *  - Output handles may alias inputs.
+ *  - Multiplications do not rescale.  ckks_rescale is explicit; the FLEXIBLEAUTO
+ *    behaviour of EvalMult (rescale-before-multiply, level alignment) is
+ *    provided by the host-side evaluator above this ABI.
+ */
+#ifndef CKKS_B200_H
+#define CKKS_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define CKKS_OK 0
+#define CKKS_EARG 1      /* invalid argument / shape mismatch */
+#define CKKS_ESTATE 2    /* missing prerequisite (e.g. no keys yet) */
+#define CKKS_ECUDA 3     /* CUDA runtime error */
+#define CKKS_EKEY 4      /* rotation / relinearisation key not generated */
+#define CKKS_ELEVEL 5    /* no limb left to drop / level mismatch */
+#define CKKS_ESCALE 6    /* operand scales differ */
+#define CKKS_ECAPACITY 7 /* size above a fixed capacity */
+
+typedef struct ckks_ctx ckks_ctx; /* CryptoContext<DCRTPoly> + keys */
+typedef struct ckks_ct ckks_ct;   /* Ciphertext<DCRTPoly> (device resident) */
+typedef struct ckks_pt ckks_pt;   /* Plaintext (device resident, NTT form) */
+
+/* CCParams<CryptoContextCKKSRNS> (T123.cpp:1602-1614) */
+typedef struct {
+  int log_n;            /* SetRingDim(2^log_n), T123.cpp:1613 */
+  int limbs;            /* Q limbs = SetMultiplicativeDepth(d) + 1, T123.cpp:1605 */
+  int dnum;             /* SetNumLargeDigits, T123.cpp:1611 (HYBRID, :1610) */
+  int first_mod_bits;   /* SetFirstModSize, T123.cpp:1607 */
+  int scale_mod_bits;   /* SetScalingModSize, T123.cpp:1606 (FLEXIBLEAUTO, :1608) */
+  int special_mod_bits; /* bit size of the HYBRID special primes */
+  uint64_t seed;        /* seeds every sampler: keys and encryptions */
+  int device;           /* SetDevices({gpu}), T123.cpp:1614 */
+} ckks_params;
+
+const char* ckks_last_error(void);
+
+/* GenCryptoContext + Enable(PKE, KEYSWITCH, LEVELEDSHE, ADVANCEDSHE) (T123.cpp:1616-1620) */
+int ckks_ctx_create(const ckks_params* params, ckks_ctx** out);
+int ckks_ctx_destroy(ckks_ctx* ctx);
+/* GetRingDimension (T123.cpp:1627); also Q limbs, special limbs K, digit size alpha */
+int ckks_ctx_info(const ckks_ctx* ctx, int* ring_dim, int* limbs, int* special, int* alpha);
+/* the prime chain: limbs Q primes then K special primes */
+int ckks_ctx_moduli(const ckks_ctx* ctx, uint64_t* out, int count);
+/* FLEXIBLEAUTO scaling factor of a fresh encoding at `level` */
+double ckks_ctx_scale(const ckks_ctx* ctx, int level);
+/* Synchronize() (T123.cpp:1626, 1662, 1671) */
+int ckks_sync(ckks_ctx* ctx);
+/* the cudaStream_t the context enqueues on (for event timing by callers) */
+void* ckks_ctx_stream(ckks_ctx* ctx);
+
+/* KeyGen + LoadContext(publicKey) (T123.cpp:1622, 1625) */
+int ckks_keygen(ckks_ctx* ctx);
+/* EvalMultKeyGen (T123.cpp:1623) */
+int ckks_relin_keygen(ckks_ctx* ctx);
+/* EvalRotateKeyGen(sk, indices) (T123.cpp:1624; index set :455-481) */
+int ckks_rotkey_gen(ckks_ctx* ctx, const int* indices, int count);
+/* key material to host: which = 0 secret (P*N), 1 public (2*L*N),
+ * 2 relinearisation key, 3 rotation key for index k (dnum*2*(L+K)*N words) */
+int ckks_key_export(ckks_ctx* ctx, int which, int k, uint64_t* host, size_t words);
+
+int ckks_ct_create(ckks_ctx* ctx, ckks_ct** out);
+int ckks_ct_destroy(ckks_ct* ct);
+int ckks_pt_create(ckks_ctx* ctx, ckks_pt** out);
+int ckks_pt_destroy(ckks_pt* pt);
+/* GetLevel (T123.cpp:787, 1367) and the scale / noise degree bookkeeping */
+int ckks_ct_level(const ckks_ct* ct);
+int ckks_ct_limbs(const ckks_ct* ct);
+double ckks_ct_scale(const ckks_ct* ct);
+int ckks_ct_noise_deg(const ckks_ct* ct);
+int ckks_pt_limbs(const ckks_pt* pt);
+double ckks_pt_scale(const ckks_pt* pt);
+int ckks_ct_set_scale(ckks_ct* ct, double scale, int noise_deg);
+
+/* limb import/export: host layout c0 limbs then c1 limbs, N words each.
+ * (FIDESlib has no ciphertext serialization; docs/hybrid/tasks.md:2652-2706) */
+int ckks_ct_export(ckks_ctx* ctx, const ckks_ct* ct, uint64_t* host, size_t words);
+int ckks_ct_import(ckks_ctx* ctx, ckks_ct* ct, const uint64_t* host, int limbs, double scale, int noise_deg);
+int ckks_pt_export(ckks_ctx* ctx, const ckks_pt* pt, uint64_t* host, size_t words);
+int ckks_pt_import(ckks_ctx* ctx, ckks_pt* pt, const uint64_t* host, int limbs, double scale);
+int ckks_ct_copy(ckks_ctx* ctx, const ckks_ct* src, ckks_ct* dst);
+
+/* MakeCKKSPackedPlaintext(values, 1, level, nullptr, N/2) (T123.cpp:955-960,
+ * 1053-1055); count <= N/2 real slots, the rest zero */
+int ckks_encode(ckks_ctx* ctx, const double* values, int count, int level, ckks_pt* out);
+/* encoding at an explicit limb count and scale */
+int ckks_encode_at(ckks_ctx* ctx, const double* values, int count, int limbs, double scale, ckks_pt* out);
+/* GetRealPackedValue (T123.cpp:525-526); count <= N/2 */
+int ckks_decode(ckks_ctx* ctx, const ckks_pt* pt, double* out, int count);
+/* Encrypt(publicKey, pt) (T123.cpp:531, 1659) */
+int ckks_encrypt(ckks_ctx* ctx, const ckks_pt* pt, ckks_ct* out);
+/* Decrypt(secretKey, ct, &pt) (T123.cpp:523, 1680) */
+int ckks_decrypt(ckks_ctx* ctx, const ckks_ct* ct, ckks_pt* out);
+/* the counter that selects the next encryption's randomness */
+int ckks_set_encrypt_counter(ckks_ctx* ctx, uint64_t counter);
+uint64_t ckks_get_encrypt_counter(const ckks_ctx* ctx);
+
+/* EvalAdd / EvalSub (T123.cpp:820, 854, 872, 1171) */
+int ckks_add(ckks_ctx* ctx, const ckks_ct* a, const ckks_ct* b, ckks_ct* out);
+int ckks_sub(ckks_ctx* ctx, const ckks_ct* a, const ckks_ct* b, ckks_ct* out);
+int ckks_add_pt(ckks_ctx* ctx, const ckks_ct* a, const ckks_pt* p, ckks_ct* out);
+/* EvalAdd(ct, double) (T123.cpp:1173): adds round(value * scale) to every slot */
+int ckks_add_scalar(ckks_ctx* ctx, const ckks_ct* a, double value, ckks_ct* out);
+/* EvalMult(ct, pt) (T123.cpp:1149-1152), no rescale */
+int ckks_mul_pt(ckks_ctx* ctx, const ckks_ct* a, const ckks_pt* p, ckks_ct* out);
+/* EvalMult(ct, ct) = tensor + relinearisation (T123.cpp:1144-1147), no rescale */
+int ckks_mul_ct(ckks_ctx* ctx, const ckks_ct* a, const ckks_ct* b, ckks_ct* out);
+/* multiply by an integer constant (scale unchanged) */
+int ckks_mul_int(ckks_ctx* ctx, const ckks_ct* a, int64_t k, ckks_ct* out);
+/* Rescale (FLEXIBLEAUTO, implicit in T123.cpp:1608): divide by the last prime */
+int ckks_rescale(ckks_ctx* ctx, const ckks_ct* a, ckks_ct* out);
+/* drop limbs down to `limbs` without scaling (LevelReduce) */
+int ckks_drop_limbs(ckks_ctx* ctx, const ckks_ct* a, int limbs, ckks_ct* out);
+/* EvalRotate(ct, k), left rotation by k slots (T123.cpp:1286-1288, 1304-1309) */
+int ckks_rotate(ckks_ctx* ctx, const ckks_ct* a, int k, ckks_ct* out);
+/* EvalFastRotation(ct, k[], M, nullptr): one ModUp shared by `count`
+ * rotations (T123.cpp:1183-1203, 1343-1362) */
+int ckks_rotate_hoisted(ckks_ctx* ctx, const ckks_ct* a, const int* k, int count, ckks_ct* const* outs);
+/* AccumulateSum(ct, count, stride) (T123.cpp:1154-1159; key ladder :444-453) */
+int ckks_accumulate_sum(ckks_ctx* ctx, const ckks_ct* a, int count, int stride, ckks_ct* out);
+
+/* Kernel timer (the reference's per-call-site Profiler buckets,
+ * fhe/gpu_real_scheme_b/src/real_dnagpt_fides_scheme_b_lintransform.cpp:627-629,
+ * 797-824): when on, every kernel launch is bracketed by CUDA events on the
+ * context stream.  The report is JSON text
+ * {"<kernel>": {"launches": n, "ms": t, "bytes": algorithmic bytes}, ...};
+ * returns the length written (truncated to `size`) or -1. */
+int ckks_profile_enable(ckks_ctx* ctx, int on);
+int ckks_profile_reset(ckks_ctx* ctx);
+int ckks_profile_report(ckks_ctx* ctx, char* buf, size_t size);
+
+/* Limb-level kernels on caller-owned DEVICE buffers (uint64 residues,
+ * limb-major, N words per limb), for parity checks and kernel benchmarks.
+ * Limb i of `data` is taken modulo Q prime first_prime + i. */
+int ckks_ntt_forward_device(ckks_ctx* ctx, uint64_t* data, int nlimbs, int first_prime);
+int ckks_ntt_inverse_device(ckks_ctx* ctx, uint64_t* data, int nlimbs, int first_prime);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* CKKS_B200_H */

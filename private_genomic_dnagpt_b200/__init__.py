@@ -1,0 +1,445 @@
+"""B200-native CKKS evaluation engine for the encrypted DNAGPT block hot path.
+
+The compute path is ``libckks_b200.so`` (hand-written sm_100a CUDA behind the C
+ABI in ``include/ckks_b200.h``).  This module binds that ABI with ctypes and
+mirrors, for Python callers and tests, the OpenFHE-compatible surface the
+reference block driver programs against
+(fhe/gpu_real_scheme_b/src/real_dnagpt_fides_scheme_b_simd_full_t103_depth13_
+digits3_ring65536_cpudiagcache_t123.cpp, "T123.cpp"):
+
+    cc = GenCryptoContext(CCParams(...))          # T123.cpp:1602-1621
+    cc.KeyGen(); cc.EvalMultKeyGen(); cc.EvalRotateKeyGen(idx)
+    pt = cc.MakeCKKSPackedPlaintext(values, level=0)
+    ct = cc.Encrypt(pt); cc.Decrypt(ct).GetRealPackedValue()
+    cc.EvalAdd / EvalSub / EvalMult / EvalRotate / EvalFastRotation /
+    cc.AccumulateSum / cc.Rescale / ct.GetLevel()
+
+EvalMult follows FLEXIBLEAUTO: operands carrying a product's scale are
+rescaled first and the operand with more limbs is brought down to the other's
+level before the product; results are left unrescaled.  Errors surface as
+``CKKSError`` (the reference raises C++ exceptions, T123.cpp:1757-1761).
+
+There is no CPU fallback: importing works without a GPU, but creating a
+context needs the CUDA library and a device, and fails loudly otherwise.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import os
+from dataclasses import dataclass
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(HERE, "libckks_b200.so")
+HEADER = os.path.join(os.path.dirname(HERE), "include", "ckks_b200.h")
+
+_u64p = ctypes.POINTER(ctypes.c_uint64)
+_f64p = ctypes.POINTER(ctypes.c_double)
+_vp = ctypes.c_void_p
+
+
+class CKKSError(RuntimeError):
+    def __init__(self, code: int, msg: str):
+        super().__init__(f"[{code}] {msg}")
+        self.code = code
+
+
+class ckks_params(ctypes.Structure):
+    _fields_ = [
+        ("log_n", ctypes.c_int),
+        ("limbs", ctypes.c_int),
+        ("dnum", ctypes.c_int),
+        ("first_mod_bits", ctypes.c_int),
+        ("scale_mod_bits", ctypes.c_int),
+        ("special_mod_bits", ctypes.c_int),
+        ("seed", ctypes.c_uint64),
+        ("device", ctypes.c_int),
+    ]
+
+
+# (name, restype, argtypes) for every symbol of include/ckks_b200.h
+_SIGS = [
+    ("ckks_last_error", ctypes.c_char_p, []),
+    ("ckks_ctx_create", ctypes.c_int, [ctypes.POINTER(ckks_params), ctypes.POINTER(_vp)]),
+    ("ckks_ctx_destroy", ctypes.c_int, [_vp]),
+    ("ckks_ctx_info", ctypes.c_int, [_vp] + [ctypes.POINTER(ctypes.c_int)] * 4),
+    ("ckks_ctx_moduli", ctypes.c_int, [_vp, _u64p, ctypes.c_int]),
+    ("ckks_ctx_scale", ctypes.c_double, [_vp, ctypes.c_int]),
+    ("ckks_sync", ctypes.c_int, [_vp]),
+    ("ckks_ctx_stream", _vp, [_vp]),
+    ("ckks_keygen", ctypes.c_int, [_vp]),
+    ("ckks_relin_keygen", ctypes.c_int, [_vp]),
+    ("ckks_rotkey_gen", ctypes.c_int, [_vp, ctypes.POINTER(ctypes.c_int), ctypes.c_int]),
+    ("ckks_key_export", ctypes.c_int, [_vp, ctypes.c_int, ctypes.c_int, _u64p, ctypes.c_size_t]),
+    ("ckks_ct_create", ctypes.c_int, [_vp, ctypes.POINTER(_vp)]),
+    ("ckks_ct_destroy", ctypes.c_int, [_vp]),
+    ("ckks_pt_create", ctypes.c_int, [_vp, ctypes.POINTER(_vp)]),
+    ("ckks_pt_destroy", ctypes.c_int, [_vp]),
+    ("ckks_ct_level", ctypes.c_int, [_vp]),
+    ("ckks_ct_limbs", ctypes.c_int, [_vp]),
+    ("ckks_ct_scale", ctypes.c_double, [_vp]),
+    ("ckks_ct_noise_deg", ctypes.c_int, [_vp]),
+    ("ckks_pt_limbs", ctypes.c_int, [_vp]),
+    ("ckks_pt_scale", ctypes.c_double, [_vp]),
+    ("ckks_ct_set_scale", ctypes.c_int, [_vp, ctypes.c_double, ctypes.c_int]),
+    ("ckks_ct_export", ctypes.c_int, [_vp, _vp, _u64p, ctypes.c_size_t]),
+    ("ckks_ct_import", ctypes.c_int, [_vp, _vp, _u64p, ctypes.c_int, ctypes.c_double, ctypes.c_int]),
+    ("ckks_pt_export", ctypes.c_int, [_vp, _vp, _u64p, ctypes.c_size_t]),
+    ("ckks_pt_import", ctypes.c_int, [_vp, _vp, _u64p, ctypes.c_int, ctypes.c_double]),
+    ("ckks_ct_copy", ctypes.c_int, [_vp, _vp, _vp]),
+    ("ckks_encode", ctypes.c_int, [_vp, _f64p, ctypes.c_int, ctypes.c_int, _vp]),
+    ("ckks_encode_at", ctypes.c_int, [_vp, _f64p, ctypes.c_int, ctypes.c_int, ctypes.c_double, _vp]),
+    ("ckks_decode", ctypes.c_int, [_vp, _vp, _f64p, ctypes.c_int]),
+    ("ckks_encrypt", ctypes.c_int, [_vp, _vp, _vp]),
+    ("ckks_decrypt", ctypes.c_int, [_vp, _vp, _vp]),
+    ("ckks_set_encrypt_counter", ctypes.c_int, [_vp, ctypes.c_uint64]),
+    ("ckks_get_encrypt_counter", ctypes.c_uint64, [_vp]),
+    ("ckks_add", ctypes.c_int, [_vp, _vp, _vp, _vp]),
+    ("ckks_sub", ctypes.c_int, [_vp, _vp, _vp, _vp]),
+    ("ckks_add_pt", ctypes.c_int, [_vp, _vp, _vp, _vp]),
+    ("ckks_add_scalar", ctypes.c_int, [_vp, _vp, ctypes.c_double, _vp]),
+    ("ckks_mul_pt", ctypes.c_int, [_vp, _vp, _vp, _vp]),
+    ("ckks_mul_ct", ctypes.c_int, [_vp, _vp, _vp, _vp]),
+    ("ckks_mul_int", ctypes.c_int, [_vp, _vp, ctypes.c_int64, _vp]),
+    ("ckks_rescale", ctypes.c_int, [_vp, _vp, _vp]),
+    ("ckks_drop_limbs", ctypes.c_int, [_vp, _vp, ctypes.c_int, _vp]),
+    ("ckks_rotate", ctypes.c_int, [_vp, _vp, ctypes.c_int, _vp]),
+    ("ckks_rotate_hoisted", ctypes.c_int, [_vp, _vp, ctypes.POINTER(ctypes.c_int), ctypes.c_int,
+                                           ctypes.POINTER(_vp)]),
+    ("ckks_accumulate_sum", ctypes.c_int, [_vp, _vp, ctypes.c_int, ctypes.c_int, _vp]),
+    ("ckks_profile_enable", ctypes.c_int, [_vp, ctypes.c_int]),
+    ("ckks_profile_reset", ctypes.c_int, [_vp]),
+    ("ckks_profile_report", ctypes.c_int, [_vp, ctypes.c_char_p, ctypes.c_size_t]),
+    ("ckks_ntt_forward_device", ctypes.c_int, [_vp, _vp, ctypes.c_int, ctypes.c_int]),
+    ("ckks_ntt_inverse_device", ctypes.c_int, [_vp, _vp, ctypes.c_int, ctypes.c_int]),
+]
+
+_lib = None
+
+
+def lib():
+    """Loads libckks_b200.so (building it first if absent)."""
+    global _lib
+    if _lib is None:
+        if not os.path.exists(LIB_PATH):
+            from .build import build
+            build()
+        L = ctypes.CDLL(LIB_PATH)
+        for name, res, args in _SIGS:
+            f = getattr(L, name)
+            f.restype = res
+            f.argtypes = args
+        _lib = L
+    return _lib
+
+
+def exported_symbols() -> list[str]:
+    return [s[0] for s in _SIGS]
+
+
+def _check(rc: int):
+    if rc != 0:
+        raise CKKSError(rc, lib().ckks_last_error().decode())
+
+
+def _u64(a: np.ndarray):
+    assert a.dtype == np.uint64 and a.flags["C_CONTIGUOUS"]
+    return a.ctypes.data_as(_u64p)
+
+
+@dataclass
+class CCParams:
+    """CCParams<CryptoContextCKKSRNS> fields used by T123.cpp:1602-1614."""
+    ring_dim_log: int = 16
+    limbs: int = 24            # multiplicative depth + 1
+    dnum: int = 3              # SetNumLargeDigits
+    first_mod_bits: int = 60   # SetFirstModSize
+    scale_mod_bits: int = 50   # SetScalingModSize
+    special_mod_bits: int = 60
+    seed: int = 1
+    device: int = 0
+
+
+class Plaintext:
+    def __init__(self, cc: "CryptoContext"):
+        self.cc = cc
+        h = _vp()
+        _check(lib().ckks_pt_create(cc.h, ctypes.byref(h)))
+        self.h = h
+
+    def __del__(self):
+        try:
+            if self.h:
+                lib().ckks_pt_destroy(self.h)
+                self.h = None
+        except Exception:
+            pass
+
+    @property
+    def limbs(self) -> int:
+        return lib().ckks_pt_limbs(self.h)
+
+    @property
+    def scale(self) -> float:
+        return lib().ckks_pt_scale(self.h)
+
+    def GetRealPackedValue(self, length: int | None = None) -> np.ndarray:
+        n = self.cc.slots if length is None else length
+        out = np.zeros(n, np.float64)
+        _check(lib().ckks_decode(self.cc.h, self.h, out.ctypes.data_as(_f64p), n))
+        return out
+
+    def limbs_array(self) -> np.ndarray:
+        out = np.zeros((self.limbs, self.cc.N), np.uint64)
+        _check(lib().ckks_pt_export(self.cc.h, self.h, _u64(out), out.size))
+        return out
+
+
+class Ciphertext:
+    def __init__(self, cc: "CryptoContext"):
+        self.cc = cc
+        h = _vp()
+        _check(lib().ckks_ct_create(cc.h, ctypes.byref(h)))
+        self.h = h
+
+    def __del__(self):
+        try:
+            if self.h:
+                lib().ckks_ct_destroy(self.h)
+                self.h = None
+        except Exception:
+            pass
+
+    def GetLevel(self) -> int:
+        return lib().ckks_ct_level(self.h)
+
+    @property
+    def limbs(self) -> int:
+        return lib().ckks_ct_limbs(self.h)
+
+    @property
+    def scale(self) -> float:
+        return lib().ckks_ct_scale(self.h)
+
+    @property
+    def noise_deg(self) -> int:
+        return lib().ckks_ct_noise_deg(self.h)
+
+    def limbs_array(self) -> np.ndarray:
+        out = np.zeros((2, self.limbs, self.cc.N), np.uint64)
+        _check(lib().ckks_ct_export(self.cc.h, self.h, _u64(out), out.size))
+        return out
+
+
+class CryptoContext:
+    """GenCryptoContext result: parameters, device tables and keys."""
+
+    def __init__(self, params: CCParams):
+        p = ckks_params(params.ring_dim_log, params.limbs, params.dnum, params.first_mod_bits,
+                        params.scale_mod_bits, params.special_mod_bits, params.seed, params.device)
+        h = _vp()
+        _check(lib().ckks_ctx_create(ctypes.byref(p), ctypes.byref(h)))
+        self.h = h
+        self.params = params
+        n, L, K, a = (ctypes.c_int(), ctypes.c_int(), ctypes.c_int(), ctypes.c_int())
+        _check(lib().ckks_ctx_info(h, ctypes.byref(n), ctypes.byref(L), ctypes.byref(K), ctypes.byref(a)))
+        self.N, self.L, self.K, self.alpha = n.value, L.value, K.value, a.value
+        self.slots = self.N // 2
+        m = np.zeros(self.L + self.K, np.uint64)
+        _check(lib().ckks_ctx_moduli(h, _u64(m), m.size))
+        self.moduli = m
+
+    def __del__(self):
+        try:
+            if self.h:
+                lib().ckks_ctx_destroy(self.h)
+                self.h = None
+        except Exception:
+            pass
+
+    # -- setup -----------------------------------------------------------
+    def GetRingDimension(self) -> int:
+        return self.N
+
+    def GetCyclotomicOrder(self) -> int:
+        return 2 * self.N
+
+    def scale_at(self, level: int) -> float:
+        return lib().ckks_ctx_scale(self.h, level)
+
+    def KeyGen(self):
+        _check(lib().ckks_keygen(self.h))
+
+    def EvalMultKeyGen(self):
+        _check(lib().ckks_relin_keygen(self.h))
+
+    def EvalRotateKeyGen(self, indices):
+        idx = (ctypes.c_int * len(indices))(*[int(i) for i in indices])
+        _check(lib().ckks_rotkey_gen(self.h, idx, len(indices)))
+
+    def Synchronize(self):
+        _check(lib().ckks_sync(self.h))
+
+    def profile(self, on: bool = True):
+        _check(lib().ckks_profile_enable(self.h, 1 if on else 0))
+
+    def profile_reset(self):
+        _check(lib().ckks_profile_reset(self.h))
+
+    def profile_report(self) -> dict:
+        import json
+        n = lib().ckks_profile_report(self.h, None, 0)
+        if n < 0:
+            raise CKKSError(-1, lib().ckks_last_error().decode())
+        buf = ctypes.create_string_buffer(n + 1)
+        lib().ckks_profile_report(self.h, buf, n + 1)
+        return json.loads(buf.value.decode())
+
+    def stream_handle(self) -> int:
+        return lib().ckks_ctx_stream(self.h) or 0
+
+    def key_array(self, which: int, k: int = 0) -> np.ndarray:
+        P = self.L + self.K
+        beta = -(-self.L // self.alpha)
+        shapes = {0: (P, self.N), 1: (2, self.L, self.N), 2: (beta, 2, P, self.N), 3: (beta, 2, P, self.N)}
+        out = np.zeros(shapes[which], np.uint64)
+        _check(lib().ckks_key_export(self.h, which, k, _u64(out), out.size))
+        return out
+
+    # -- client ------------------------------------------------------------
+    def MakeCKKSPackedPlaintext(self, values, level: int = 0, scale: float | None = None,
+                                limbs: int | None = None) -> Plaintext:
+        v = np.ascontiguousarray(values, np.float64)
+        pt = Plaintext(self)
+        if scale is None and limbs is None:
+            _check(lib().ckks_encode(self.h, v.ctypes.data_as(_f64p), v.size, level, pt.h))
+        else:
+            lb = self.L - level if limbs is None else limbs
+            sc = self.scale_at(self.L - lb) if scale is None else scale
+            _check(lib().ckks_encode_at(self.h, v.ctypes.data_as(_f64p), v.size, lb, sc, pt.h))
+        return pt
+
+    def Encrypt(self, pt: Plaintext) -> Ciphertext:
+        ct = Ciphertext(self)
+        _check(lib().ckks_encrypt(self.h, pt.h, ct.h))
+        return ct
+
+    def Decrypt(self, ct: Ciphertext) -> Plaintext:
+        pt = Plaintext(self)
+        _check(lib().ckks_decrypt(self.h, ct.h, pt.h))
+        return pt
+
+    def set_encrypt_counter(self, c: int):
+        _check(lib().ckks_set_encrypt_counter(self.h, c))
+
+    def import_ct(self, arr: np.ndarray, scale: float, deg: int = 1) -> Ciphertext:
+        arr = np.ascontiguousarray(arr, np.uint64)
+        ct = Ciphertext(self)
+        _check(lib().ckks_ct_import(self.h, ct.h, _u64(arr), arr.shape[1], scale, deg))
+        return ct
+
+    def import_pt(self, arr: np.ndarray, scale: float) -> Plaintext:
+        arr = np.ascontiguousarray(arr, np.uint64)
+        pt = Plaintext(self)
+        _check(lib().ckks_pt_import(self.h, pt.h, _u64(arr), arr.shape[0], scale))
+        return pt
+
+    # -- raw ops (no scale management) ------------------------------------
+    def _new(self) -> Ciphertext:
+        return Ciphertext(self)
+
+    def add(self, a, b):
+        o = self._new(); _check(lib().ckks_add(self.h, a.h, b.h, o.h)); return o
+
+    def sub(self, a, b):
+        o = self._new(); _check(lib().ckks_sub(self.h, a.h, b.h, o.h)); return o
+
+    def mul_pt(self, a, p):
+        o = self._new(); _check(lib().ckks_mul_pt(self.h, a.h, p.h, o.h)); return o
+
+    def mul_ct(self, a, b):
+        o = self._new(); _check(lib().ckks_mul_ct(self.h, a.h, b.h, o.h)); return o
+
+    def mul_int(self, a, k: int):
+        o = self._new(); _check(lib().ckks_mul_int(self.h, a.h, int(k), o.h)); return o
+
+    def rescale(self, a):
+        o = self._new(); _check(lib().ckks_rescale(self.h, a.h, o.h)); return o
+
+    def drop_limbs(self, a, limbs: int):
+        o = self._new(); _check(lib().ckks_drop_limbs(self.h, a.h, limbs, o.h)); return o
+
+    # -- OpenFHE-named evaluation (FLEXIBLEAUTO) ----------------------------
+    def Rescale(self, ct: Ciphertext) -> Ciphertext:
+        return self.rescale(ct)
+
+    def _to_deg1(self, ct: Ciphertext) -> Ciphertext:
+        return self.rescale(ct) if ct.noise_deg >= 2 else ct
+
+    def _level_reduce(self, ct: Ciphertext, limbs: int) -> Ciphertext:
+        """Brings a degree-1 ciphertext down to `limbs` limbs at that level's scale."""
+        if ct.limbs == limbs:
+            return ct
+        target = self.scale_at(self.L - limbs)
+        ql = float(self.moduli[ct.limbs - 1])
+        c = int(round(target * ql / ct.scale))
+        t = self.mul_int(ct, c)
+        _check(lib().ckks_ct_set_scale(t.h, ct.scale * c, 2))
+        t = self.rescale(t)
+        if t.limbs > limbs:
+            t = self.drop_limbs(t, limbs)
+        return t
+
+    def _align(self, a: Ciphertext, b: Ciphertext):
+        if a.noise_deg != b.noise_deg:
+            a, b = self._to_deg1(a), self._to_deg1(b)
+        if a.limbs != b.limbs:
+            if a.noise_deg != 1:
+                a, b = self._to_deg1(a), self._to_deg1(b)
+            lo = min(a.limbs, b.limbs)
+            a, b = self._level_reduce(a, lo), self._level_reduce(b, lo)
+        return a, b
+
+    def EvalAdd(self, a: Ciphertext, b) -> Ciphertext:
+        if isinstance(b, (int, float)):
+            o = self._new(); _check(lib().ckks_add_scalar(self.h, a.h, float(b), o.h)); return o
+        if isinstance(b, Plaintext):
+            o = self._new(); _check(lib().ckks_add_pt(self.h, a.h, b.h, o.h)); return o
+        a, b = self._align(a, b)
+        return self.add(a, b)
+
+    def EvalSub(self, a: Ciphertext, b) -> Ciphertext:
+        if isinstance(b, (int, float)):
+            return self.EvalAdd(a, -float(b))
+        a, b = self._align(a, b)
+        return self.sub(a, b)
+
+    def EvalMult(self, a: Ciphertext, b) -> Ciphertext:
+        a = self._to_deg1(a)
+        if isinstance(b, Plaintext):
+            return self.mul_pt(a, b)
+        if isinstance(b, (list, tuple, np.ndarray)):
+            pt = self.MakeCKKSPackedPlaintext(b, level=a.GetLevel())
+            return self.mul_pt(a, pt)
+        b = self._to_deg1(b)
+        a, b = self._align(a, b)
+        return self.mul_ct(a, b)
+
+    def EvalRotate(self, ct: Ciphertext, k: int) -> Ciphertext:
+        o = self._new(); _check(lib().ckks_rotate(self.h, ct.h, int(k), o.h)); return o
+
+    def EvalFastRotation(self, ct: Ciphertext, indices) -> list[Ciphertext]:
+        outs = [self._new() for _ in indices]
+        idx = (ctypes.c_int * len(indices))(*[int(i) for i in indices])
+        hs = (_vp * len(indices))(*[o.h for o in outs])
+        _check(lib().ckks_rotate_hoisted(self.h, ct.h, idx, len(indices), hs))
+        return outs
+
+    def AccumulateSum(self, ct: Ciphertext, count: int, stride: int) -> Ciphertext:
+        o = self._new(); _check(lib().ckks_accumulate_sum(self.h, ct.h, count, stride, o.h)); return o
+
+
+def GenCryptoContext(params: CCParams) -> CryptoContext:
+    return CryptoContext(params)

@@ -1,0 +1,747 @@
+// capi.cu -- the extern "C" boundary declared in include/ckks_b200.h.
+// Each entry point validates its arguments, runs the device pipeline on the
+// context's stream and converts C++ exceptions into status codes.
+#include <cmath>
+#include <cstdio>
+#include <cstring>
+#include <utility>
+
+#include "../../include/ckks_b200.h"
+#include "ckks_internal.hpp"
+
+using ckks::Context;
+using ckks::DevPoly;
+using ckks::Error;
+
+struct ckks_ctx {
+  std::unique_ptr<Context> c;
+};
+struct ckks_ct {
+  ckks_ctx* owner = nullptr;
+  DevPoly p;
+};
+struct ckks_pt {
+  ckks_ctx* owner = nullptr;
+  DevPoly p;
+};
+
+namespace {
+
+thread_local std::string g_error;
+
+template <typename F>
+int guard(F&& f) {
+  try {
+    f();
+    return CKKS_OK;
+  } catch (const Error& e) {
+    g_error = e.what();
+    return e.code;
+  } catch (const std::exception& e) {
+    g_error = e.what();
+    return CKKS_EARG;
+  } catch (...) {
+    g_error = "unknown error";
+    return CKKS_EARG;
+  }
+}
+
+void need(bool ok, int code, const char* msg) {
+  if (!ok) throw Error(code, msg);
+}
+
+Context& C(ckks_ctx* x) {
+  need(x && x->c, CKKS_EARG, "null context");
+  return *x->c;
+}
+
+void same_ctx(ckks_ctx* x, const ckks_ct* a) {
+  need(a != nullptr, CKKS_EARG, "null ciphertext");
+  need(a->owner == x, CKKS_EARG, "ciphertext belongs to another context");
+  need(a->p.data != nullptr && a->p.limbs > 0, CKKS_ESTATE, "ciphertext holds no data");
+}
+
+void same_ctx(ckks_ctx* x, const ckks_pt* a) {
+  need(a != nullptr, CKKS_EARG, "null plaintext");
+  need(a->owner == x, CKKS_EARG, "plaintext belongs to another context");
+  need(a->p.data != nullptr && a->p.limbs > 0, CKKS_ESTATE, "plaintext holds no data");
+}
+
+// moves a freshly computed object into the caller's handle
+void take(DevPoly& dst, DevPoly& src) {
+  std::swap(dst.ctx, src.ctx);
+  std::swap(dst.data, src.data);
+  std::swap(dst.npolys, src.npolys);
+  std::swap(dst.cap, src.cap);
+  std::swap(dst.limbs, src.limbs);
+  std::swap(dst.scale, src.scale);
+  std::swap(dst.deg, src.deg);
+}
+
+size_t stride(const DevPoly& p) { return (size_t)p.cap * p.ctx->N; }
+
+void check_scales(double a, double b) {
+  const double rel = std::fabs(a - b) / std::fmax(std::fabs(a), std::fabs(b));
+  if (!(rel <= 1e-9)) throw Error(CKKS_ESCALE, "operand scales differ");
+}
+
+void ew_ct_ct(Context& c, ckks::EwOp op, const ckks_ct* a, const ckks_ct* b, ckks_ct* out) {
+  need(a->p.limbs == b->p.limbs, CKKS_ELEVEL, "operands at different levels");
+  need(a->p.deg == b->p.deg, CKKS_ESCALE, "operands with different noise degree");
+  check_scales(a->p.scale, b->p.scale);
+  const int limbs = a->p.limbs;
+  DevPoly tmp;
+  DevPoly* dst = &out->p;
+  const bool alias_ok = (out == a || out == b) && out->p.cap >= limbs;
+  if (!alias_ok) {
+    tmp.ensure(&c, 2, limbs);
+    dst = &tmp;
+  }
+  ckks::ew_binary(c, op, a->p.data, stride(a->p), b->p.data, stride(b->p), dst->data, stride(*dst), 2, limbs,
+                  c.stream);
+  dst->limbs = limbs;
+  dst->scale = a->p.scale;
+  dst->deg = a->p.deg;
+  if (dst == &tmp) take(out->p, tmp);
+}
+
+// rotations of `a` by ks[0..n) into outs (fresh buffers, then moved)
+void rotate_many(Context& c, const ckks_ct* a, const int* ks, int n, ckks_ct* const* outs) {
+  const int limbs = a->p.limbs, N = c.N, E = limbs + c.K;
+  const int beta = c.levels[limbs].beta;
+  std::vector<uint32_t> gs(n);
+  bool any = false;
+  for (int r = 0; r < n; ++r) {
+    gs[r] = c.galois(ks[r]);
+    if (gs[r] != 1u) {
+      any = true;
+      if (!c.rot_key(gs[r])) throw Error(CKKS_EKEY, "rotation key not generated for index " + std::to_string(ks[r]));
+    }
+  }
+  std::vector<DevPoly> res(n);
+  uint64_t* ext = nullptr;
+  uint64_t* acc = nullptr;
+  if (any) {
+    ext = (uint64_t*)c.alloc(sizeof(uint64_t) * (size_t)beta * E * N);
+    acc = (uint64_t*)c.alloc(sizeof(uint64_t) * 2 * (size_t)E * N);
+    ckks::modup(c, a->p.poly(1), limbs, ext, c.stream);
+  }
+  for (int r = 0; r < n; ++r) {
+    res[r].ensure(&c, 2, limbs);
+    if (gs[r] == 1u) {
+      ckks::ew_binary(c, ckks::EwOp::Copy, a->p.data, stride(a->p), nullptr, 0, res[r].data, stride(res[r]), 2,
+                      limbs, c.stream);
+    } else {
+      ckks::ks_inner(c, ext, limbs, c.rot_key(gs[r]), gs[r], acc, c.stream);
+      ckks::moddown2(c, acc, limbs, a->p.poly(0), gs[r], nullptr, res[r].poly(0), res[r].poly(1), c.stream);
+    }
+    res[r].limbs = limbs;
+    res[r].scale = a->p.scale;
+    res[r].deg = a->p.deg;
+  }
+  c.release(ext);
+  c.release(acc);
+  for (int r = 0; r < n; ++r) {
+    outs[r]->owner = a->owner;
+    take(outs[r]->p, res[r]);
+  }
+}
+
+}  // namespace
+
+extern "C" {
+
+const char* ckks_last_error(void) { return g_error.c_str(); }
+
+int ckks_ctx_create(const ckks_params* params, ckks_ctx** out) {
+  return guard([&] {
+    need(params && out, CKKS_EARG, "null argument");
+    ckks::Params p;
+    p.log_n = params->log_n;
+    p.limbs = params->limbs;
+    p.dnum = params->dnum;
+    p.first_mod_bits = params->first_mod_bits;
+    p.scale_mod_bits = params->scale_mod_bits;
+    p.special_mod_bits = params->special_mod_bits;
+    p.seed = params->seed;
+    p.device = params->device;
+    auto* x = new ckks_ctx;
+    try {
+      x->c = std::make_unique<Context>(p);
+    } catch (...) {
+      delete x;
+      throw;
+    }
+    *out = x;
+  });
+}
+
+int ckks_ctx_destroy(ckks_ctx* ctx) {
+  return guard([&] { delete ctx; });
+}
+
+int ckks_ctx_info(const ckks_ctx* ctx, int* ring_dim, int* limbs, int* special, int* alpha) {
+  return guard([&] {
+    need(ctx && ctx->c, CKKS_EARG, "null context");
+    const Context& c = *ctx->c;
+    if (ring_dim) *ring_dim = c.N;
+    if (limbs) *limbs = c.L;
+    if (special) *special = c.K;
+    if (alpha) *alpha = c.alpha;
+  });
+}
+
+int ckks_ctx_moduli(const ckks_ctx* ctx, uint64_t* out, int count) {
+  return guard([&] {
+    need(ctx && ctx->c && out, CKKS_EARG, "null argument");
+    const Context& c = *ctx->c;
+    need(count >= 0 && count <= c.P, CKKS_EARG, "count above L+K");
+    std::memcpy(out, c.moduli.data(), sizeof(uint64_t) * count);
+  });
+}
+
+double ckks_ctx_scale(const ckks_ctx* ctx, int level) {
+  if (!ctx || !ctx->c) return 0.0;
+  const Context& c = *ctx->c;
+  const int limbs = c.L - level;
+  if (limbs < 1 || limbs > c.L) return 0.0;
+  return c.scales[limbs];
+}
+
+int ckks_sync(ckks_ctx* ctx) {
+  return guard([&] { CKKS_CUDA(cudaStreamSynchronize(C(ctx).stream)); });
+}
+
+void* ckks_ctx_stream(ckks_ctx* ctx) { return (ctx && ctx->c) ? (void*)ctx->c->stream : nullptr; }
+
+int ckks_keygen(ckks_ctx* ctx) {
+  return guard([&] { ckks::keygen_secret_public(C(ctx)); });
+}
+
+int ckks_relin_keygen(ckks_ctx* ctx) {
+  return guard([&] {
+    Context& c = C(ctx);
+    need(c.d_sk != nullptr, CKKS_ESTATE, "secret key not generated");
+    uint64_t* s2 = (uint64_t*)c.alloc(sizeof(uint64_t) * (size_t)c.P * c.N);
+    // s^2 over every prime (NTT form)
+    ckks::ew_binary(c, ckks::EwOp::Mul, c.d_sk, 0, c.d_sk, 0, s2, 0, 1, c.P, c.stream);
+    uint64_t* key = ckks::make_switch_key(c, s2, 1u);
+    c.release(s2);
+    if (c.d_rlk) cudaFree(c.d_rlk);
+    c.d_rlk = key;
+  });
+}
+
+int ckks_rotkey_gen(ckks_ctx* ctx, const int* indices, int count) {
+  return guard([&] {
+    Context& c = C(ctx);
+    need(c.d_sk != nullptr, CKKS_ESTATE, "secret key not generated");
+    need(count >= 0 && (count == 0 || indices), CKKS_EARG, "bad index list");
+    uint64_t* sg = (uint64_t*)c.alloc(sizeof(uint64_t) * (size_t)c.P * c.N);
+    for (int i = 0; i < count; ++i) {
+      const uint32_t g = c.galois(indices[i]);
+      if (g == 1u || c.rot_key(g)) continue;
+      ckks::automorphism(c, c.d_sk, sg, c.P, g, c.stream);
+      c.rot_keys[g] = ckks::make_switch_key(c, sg, 0x100u + g);
+    }
+    c.release(sg);
+    CKKS_CUDA(cudaStreamSynchronize(c.stream));
+  });
+}
+
+int ckks_key_export(ckks_ctx* ctx, int which, int k, uint64_t* host, size_t words) {
+  return guard([&] {
+    Context& c = C(ctx);
+    need(host != nullptr, CKKS_EARG, "null buffer");
+    const uint64_t* src = nullptr;
+    size_t n = 0;
+    switch (which) {
+      case 0: src = c.d_sk; n = (size_t)c.P * c.N; break;
+      case 1: src = c.d_pk; n = 2 * (size_t)c.L * c.N; break;
+      case 2: src = c.d_rlk; n = c.key_words(); break;
+      case 3: src = c.rot_key(c.galois(k)); n = c.key_words(); break;
+      default: throw Error(CKKS_EARG, "unknown key kind");
+    }
+    need(src != nullptr, CKKS_EKEY, "key not generated");
+    need(words >= n, CKKS_EARG, "host buffer too small");
+    CKKS_CUDA(cudaMemcpyAsync(host, src, sizeof(uint64_t) * n, cudaMemcpyDeviceToHost, c.stream));
+    CKKS_CUDA(cudaStreamSynchronize(c.stream));
+  });
+}
+
+int ckks_ct_create(ckks_ctx* ctx, ckks_ct** out) {
+  return guard([&] {
+    C(ctx);
+    need(out != nullptr, CKKS_EARG, "null argument");
+    auto* t = new ckks_ct;
+    t->owner = ctx;
+    *out = t;
+  });
+}
+
+int ckks_ct_destroy(ckks_ct* ct) {
+  return guard([&] { delete ct; });
+}
+
+int ckks_pt_create(ckks_ctx* ctx, ckks_pt** out) {
+  return guard([&] {
+    C(ctx);
+    need(out != nullptr, CKKS_EARG, "null argument");
+    auto* t = new ckks_pt;
+    t->owner = ctx;
+    *out = t;
+  });
+}
+
+int ckks_pt_destroy(ckks_pt* pt) {
+  return guard([&] { delete pt; });
+}
+
+int ckks_ct_level(const ckks_ct* ct) {
+  if (!ct || !ct->p.ctx) return -1;
+  return ct->p.ctx->L - ct->p.limbs;
+}
+int ckks_ct_limbs(const ckks_ct* ct) { return ct ? ct->p.limbs : -1; }
+double ckks_ct_scale(const ckks_ct* ct) { return ct ? ct->p.scale : 0.0; }
+int ckks_ct_noise_deg(const ckks_ct* ct) { return ct ? ct->p.deg : -1; }
+int ckks_pt_limbs(const ckks_pt* pt) { return pt ? pt->p.limbs : -1; }
+double ckks_pt_scale(const ckks_pt* pt) { return pt ? pt->p.scale : 0.0; }
+
+int ckks_ct_set_scale(ckks_ct* ct, double scale, int noise_deg) {
+  return guard([&] {
+    need(ct != nullptr && scale > 0.0 && noise_deg >= 1, CKKS_EARG, "bad scale");
+    ct->p.scale = scale;
+    ct->p.deg = noise_deg;
+  });
+}
+
+int ckks_ct_export(ckks_ctx* ctx, const ckks_ct* ct, uint64_t* host, size_t words) {
+  return guard([&] {
+    Context& c = C(ctx);
+    same_ctx(ctx, ct);
+    const size_t per = (size_t)ct->p.limbs * c.N;
+    need(host && words >= 2 * per, CKKS_EARG, "host buffer too small");
+    for (int p = 0; p < 2; ++p)
+      CKKS_CUDA(cudaMemcpyAsync(host + p * per, ct->p.poly(p), sizeof(uint64_t) * per, cudaMemcpyDeviceToHost,
+                                c.stream));
+    CKKS_CUDA(cudaStreamSynchronize(c.stream));
+  });
+}
+
+int ckks_ct_import(ckks_ctx* ctx, ckks_ct* ct, const uint64_t* host, int limbs, double scale, int noise_deg) {
+  return guard([&] {
+    Context& c = C(ctx);
+    need(ct && ct->owner == ctx && host, CKKS_EARG, "bad argument");
+    need(limbs >= 1 && limbs <= c.L, CKKS_EARG, "limb count outside 1..L");
+    DevPoly tmp;
+    tmp.ensure(&c, 2, limbs);
+    const size_t per = (size_t)limbs * c.N;
+    for (int p = 0; p < 2; ++p)
+      CKKS_CUDA(cudaMemcpyAsync(tmp.poly(p), host + p * per, sizeof(uint64_t) * per, cudaMemcpyHostToDevice,
+                                c.stream));
+    tmp.limbs = limbs;
+    tmp.scale = scale;
+    tmp.deg = noise_deg;
+    take(ct->p, tmp);
+  });
+}
+
+int ckks_pt_export(ckks_ctx* ctx, const ckks_pt* pt, uint64_t* host, size_t words) {
+  return guard([&] {
+    Context& c = C(ctx);
+    same_ctx(ctx, pt);
+    const size_t per = (size_t)pt->p.limbs * c.N;
+    need(host && words >= per, CKKS_EARG, "host buffer too small");
+    CKKS_CUDA(cudaMemcpyAsync(host, pt->p.data, sizeof(uint64_t) * per, cudaMemcpyDeviceToHost, c.stream));
+    CKKS_CUDA(cudaStreamSynchronize(c.stream));
+  });
+}
+
+int ckks_pt_import(ckks_ctx* ctx, ckks_pt* pt, const uint64_t* host, int limbs, double scale) {
+  return guard([&] {
+    Context& c = C(ctx);
+    need(pt && pt->owner == ctx && host, CKKS_EARG, "bad argument");
+    need(limbs >= 1 && limbs <= c.L, CKKS_EARG, "limb count outside 1..L");
+    DevPoly tmp;
+    tmp.ensure(&c, 1, limbs);
+    CKKS_CUDA(cudaMemcpyAsync(tmp.data, host, sizeof(uint64_t) * (size_t)limbs * c.N, cudaMemcpyHostToDevice,
+                              c.stream));
+    tmp.limbs = limbs;
+    tmp.scale = scale;
+    take(pt->p, tmp);
+  });
+}
+
+int ckks_ct_copy(ckks_ctx* ctx, const ckks_ct* src, ckks_ct* dst) {
+  return guard([&] {
+    Context& c = C(ctx);
+    same_ctx(ctx, src);
+    need(dst && dst->owner == ctx, CKKS_EARG, "bad destination");
+    if (src == dst) return;
+    DevPoly tmp;
+    tmp.ensure(&c, 2, src->p.limbs);
+    ckks::ew_binary(c, ckks::EwOp::Copy, src->p.data, stride(src->p), nullptr, 0, tmp.data, stride(tmp), 2,
+                    src->p.limbs, c.stream);
+    tmp.limbs = src->p.limbs;
+    tmp.scale = src->p.scale;
+    tmp.deg = src->p.deg;
+    take(dst->p, tmp);
+  });
+}
+
+int ckks_encode_at(ckks_ctx* ctx, const double* values, int count, int limbs, double scale, ckks_pt* out) {
+  return guard([&] {
+    Context& c = C(ctx);
+    need(out && out->owner == ctx, CKKS_EARG, "bad plaintext handle");
+    need(values || count == 0, CKKS_EARG, "null values");
+    need(count >= 0 && count <= c.N / 2, CKKS_EARG, "more values than slots");
+    need(limbs >= 1 && limbs <= c.L, CKKS_EARG, "limb count outside 1..L");
+    need(scale > 0.0 && std::isfinite(scale), CKKS_EARG, "bad scale");
+    for (int i = 0; i < count; ++i) need(std::isfinite(values[i]), CKKS_EARG, "non-finite value");
+    const int n = c.N / 2;
+    double* dv = (double*)c.alloc(sizeof(double) * n);
+    CKKS_CUDA(cudaMemsetAsync(dv, 0, sizeof(double) * n, c.stream));
+    if (count) CKKS_CUDA(cudaMemcpyAsync(dv, values, sizeof(double) * count, cudaMemcpyHostToDevice, c.stream));
+    DevPoly tmp;
+    tmp.ensure(&c, 1, limbs);
+    ckks::encode(c, dv, limbs, scale, tmp.data, c.stream);
+    tmp.limbs = limbs;
+    tmp.scale = scale;
+    c.release(dv);
+    CKKS_CUDA(cudaStreamSynchronize(c.stream));  // host values may be released on return
+    take(out->p, tmp);
+  });
+}
+
+int ckks_encode(ckks_ctx* ctx, const double* values, int count, int level, ckks_pt* out) {
+  if (!ctx || !ctx->c) {
+    g_error = "null context";
+    return CKKS_EARG;
+  }
+  const Context& c = *ctx->c;
+  const int limbs = c.L - level;
+  if (limbs < 1 || limbs > c.L) {
+    g_error = "level outside 0..L-1";
+    return CKKS_EARG;
+  }
+  return ckks_encode_at(ctx, values, count, limbs, c.scales[limbs], out);
+}
+
+int ckks_decode(ckks_ctx* ctx, const ckks_pt* pt, double* out, int count) {
+  return guard([&] {
+    Context& c = C(ctx);
+    same_ctx(ctx, pt);
+    need(out != nullptr && count >= 0 && count <= c.N / 2, CKKS_EARG, "bad output buffer");
+    const int n = c.N / 2;
+    double* dv = (double*)c.alloc(sizeof(double) * n);
+    ckks::decode(c, pt->p.data, pt->p.limbs, pt->p.scale, dv, c.stream);
+    if (count) CKKS_CUDA(cudaMemcpyAsync(out, dv, sizeof(double) * count, cudaMemcpyDeviceToHost, c.stream));
+    c.release(dv);
+    CKKS_CUDA(cudaStreamSynchronize(c.stream));
+  });
+}
+
+int ckks_encrypt(ckks_ctx* ctx, const ckks_pt* pt, ckks_ct* out) {
+  return guard([&] {
+    Context& c = C(ctx);
+    same_ctx(ctx, pt);
+    need(out && out->owner == ctx, CKKS_EARG, "bad ciphertext handle");
+    DevPoly tmp;
+    tmp.ensure(&c, 2, pt->p.limbs);
+    ckks::encrypt(c, pt->p.data, pt->p.limbs, c.enc_counter++, tmp.poly(0), tmp.poly(1));
+    tmp.limbs = pt->p.limbs;
+    tmp.scale = pt->p.scale;
+    tmp.deg = 1;
+    take(out->p, tmp);
+  });
+}
+
+int ckks_decrypt(ckks_ctx* ctx, const ckks_ct* ct, ckks_pt* out) {
+  return guard([&] {
+    Context& c = C(ctx);
+    same_ctx(ctx, ct);
+    need(out && out->owner == ctx, CKKS_EARG, "bad plaintext handle");
+    DevPoly tmp;
+    tmp.ensure(&c, 1, ct->p.limbs);
+    ckks::decrypt(c, ct->p.poly(0), ct->p.poly(1), ct->p.limbs, tmp.data);
+    tmp.limbs = ct->p.limbs;
+    tmp.scale = ct->p.scale;
+    take(out->p, tmp);
+  });
+}
+
+int ckks_set_encrypt_counter(ckks_ctx* ctx, uint64_t counter) {
+  return guard([&] { C(ctx).enc_counter = counter; });
+}
+
+uint64_t ckks_get_encrypt_counter(const ckks_ctx* ctx) { return (ctx && ctx->c) ? ctx->c->enc_counter : 0; }
+
+int ckks_add(ckks_ctx* ctx, const ckks_ct* a, const ckks_ct* b, ckks_ct* out) {
+  return guard([&] {
+    Context& c = C(ctx);
+    same_ctx(ctx, a);
+    same_ctx(ctx, b);
+    need(out && out->owner == ctx, CKKS_EARG, "bad output handle");
+    ew_ct_ct(c, ckks::EwOp::Add, a, b, out);
+  });
+}
+
+int ckks_sub(ckks_ctx* ctx, const ckks_ct* a, const ckks_ct* b, ckks_ct* out) {
+  return guard([&] {
+    Context& c = C(ctx);
+    same_ctx(ctx, a);
+    same_ctx(ctx, b);
+    need(out && out->owner == ctx, CKKS_EARG, "bad output handle");
+    ew_ct_ct(c, ckks::EwOp::Sub, a, b, out);
+  });
+}
+
+int ckks_add_pt(ckks_ctx* ctx, const ckks_ct* a, const ckks_pt* p, ckks_ct* out) {
+  return guard([&] {
+    Context& c = C(ctx);
+    same_ctx(ctx, a);
+    same_ctx(ctx, p);
+    need(out && out->owner == ctx, CKKS_EARG, "bad output handle");
+    need(p->p.limbs >= a->p.limbs, CKKS_ELEVEL, "plaintext has fewer limbs than the ciphertext");
+    check_scales(a->p.scale, p->p.scale);
+    const int limbs = a->p.limbs;
+    DevPoly tmp;
+    tmp.ensure(&c, 2, limbs);
+    ckks::ew_binary(c, ckks::EwOp::Add, a->p.data, 0, p->p.data, 0, tmp.data, 0, 1, limbs, c.stream);
+    ckks::ew_binary(c, ckks::EwOp::Copy, a->p.poly(1), 0, nullptr, 0, tmp.poly(1), 0, 1, limbs, c.stream);
+    tmp.limbs = limbs;
+    tmp.scale = a->p.scale;
+    tmp.deg = a->p.deg;
+    take(out->p, tmp);
+  });
+}
+
+int ckks_add_scalar(ckks_ctx* ctx, const ckks_ct* a, double value, ckks_ct* out) {
+  return guard([&] {
+    Context& c = C(ctx);
+    same_ctx(ctx, a);
+    need(out && out->owner == ctx, CKKS_EARG, "bad output handle");
+    need(std::isfinite(value), CKKS_EARG, "non-finite scalar");
+    const int limbs = a->p.limbs;
+    DevPoly tmp;
+    tmp.ensure(&c, 2, limbs);
+    ckks::ew_binary(c, ckks::EwOp::Copy, a->p.data, stride(a->p), nullptr, 0, tmp.data, stride(tmp), 2, limbs,
+                    c.stream);
+    const double r = std::rint(value * a->p.scale);
+    std::vector<uint64_t> res(limbs);
+    for (int l = 0; l < limbs; ++l) res[l] = ckks::host_double_to_res(r, c.moduli[l]);
+    ckks::ew_add_const(c, tmp.data, limbs, res, c.stream);
+    tmp.limbs = limbs;
+    tmp.scale = a->p.scale;
+    tmp.deg = a->p.deg;
+    take(out->p, tmp);
+  });
+}
+
+int ckks_mul_pt(ckks_ctx* ctx, const ckks_ct* a, const ckks_pt* p, ckks_ct* out) {
+  return guard([&] {
+    Context& c = C(ctx);
+    same_ctx(ctx, a);
+    same_ctx(ctx, p);
+    need(out && out->owner == ctx, CKKS_EARG, "bad output handle");
+    need(p->p.limbs >= a->p.limbs, CKKS_ELEVEL, "plaintext has fewer limbs than the ciphertext");
+    const int limbs = a->p.limbs;
+    DevPoly tmp;
+    DevPoly* dst = &out->p;
+    if (!(out == a && out->p.cap >= limbs)) {
+      tmp.ensure(&c, 2, limbs);
+      dst = &tmp;
+    }
+    ckks::ew_mul_pt(c, a->p.data, stride(a->p), p->p.data, dst->data, stride(*dst), 2, limbs, c.stream);
+    dst->limbs = limbs;
+    dst->scale = a->p.scale * p->p.scale;
+    dst->deg = a->p.deg + 1;
+    if (dst == &tmp) take(out->p, tmp);
+  });
+}
+
+int ckks_mul_int(ckks_ctx* ctx, const ckks_ct* a, int64_t k, ckks_ct* out) {
+  return guard([&] {
+    Context& c = C(ctx);
+    same_ctx(ctx, a);
+    need(out && out->owner == ctx, CKKS_EARG, "bad output handle");
+    const int limbs = a->p.limbs;
+    std::vector<uint64_t> res(limbs);
+    for (int l = 0; l < limbs; ++l) res[l] = ckks::host_int_to_res(k, c.moduli[l]);
+    DevPoly tmp;
+    tmp.ensure(&c, 2, limbs);
+    ckks::ew_mul_const(c, a->p.data, stride(a->p), tmp.data, stride(tmp), 2, limbs, res, c.stream);
+    tmp.limbs = limbs;
+    tmp.scale = a->p.scale;
+    tmp.deg = a->p.deg;
+    take(out->p, tmp);
+  });
+}
+
+int ckks_mul_ct(ckks_ctx* ctx, const ckks_ct* a, const ckks_ct* b, ckks_ct* out) {
+  return guard([&] {
+    Context& c = C(ctx);
+    same_ctx(ctx, a);
+    same_ctx(ctx, b);
+    need(out && out->owner == ctx, CKKS_EARG, "bad output handle");
+    need(c.d_rlk != nullptr, CKKS_EKEY, "relinearisation key not generated");
+    need(a->p.limbs == b->p.limbs, CKKS_ELEVEL, "operands at different levels");
+    const int limbs = a->p.limbs, N = c.N, E = limbs + c.K;
+    const int beta = c.levels[limbs].beta;
+    const size_t S = (size_t)limbs * N;
+    uint64_t* d = (uint64_t*)c.alloc(sizeof(uint64_t) * 3 * S);
+    ckks::tensor(c, a->p.poly(0), a->p.poly(1), b->p.poly(0), b->p.poly(1), d, d + S, d + 2 * S, limbs, c.stream);
+    uint64_t* ext = (uint64_t*)c.alloc(sizeof(uint64_t) * (size_t)beta * E * N);
+    uint64_t* acc = (uint64_t*)c.alloc(sizeof(uint64_t) * 2 * (size_t)E * N);
+    ckks::modup(c, d + 2 * S, limbs, ext, c.stream);
+    ckks::ks_inner(c, ext, limbs, c.d_rlk, 1u, acc, c.stream);
+    DevPoly tmp;
+    tmp.ensure(&c, 2, limbs);
+    ckks::moddown2(c, acc, limbs, d, 1u, d + S, tmp.poly(0), tmp.poly(1), c.stream);
+    tmp.limbs = limbs;
+    tmp.scale = a->p.scale * b->p.scale;
+    tmp.deg = a->p.deg + b->p.deg;
+    c.release(d);
+    c.release(ext);
+    c.release(acc);
+    take(out->p, tmp);
+  });
+}
+
+int ckks_rescale(ckks_ctx* ctx, const ckks_ct* a, ckks_ct* out) {
+  return guard([&] {
+    Context& c = C(ctx);
+    same_ctx(ctx, a);
+    need(out && out->owner == ctx, CKKS_EARG, "bad output handle");
+    const int limbs = a->p.limbs;
+    need(limbs >= 2, CKKS_ELEVEL, "no limb left to rescale");
+    DevPoly tmp;
+    tmp.ensure(&c, 2, limbs - 1);
+    ckks::rescale(c, a->p.data, stride(a->p), 2, limbs, tmp.data, stride(tmp), c.stream);
+    tmp.limbs = limbs - 1;
+    tmp.scale = a->p.scale / (double)c.moduli[limbs - 1];
+    tmp.deg = a->p.deg > 1 ? a->p.deg - 1 : 1;
+    take(out->p, tmp);
+  });
+}
+
+int ckks_drop_limbs(ckks_ctx* ctx, const ckks_ct* a, int limbs, ckks_ct* out) {
+  return guard([&] {
+    Context& c = C(ctx);
+    same_ctx(ctx, a);
+    need(out && out->owner == ctx, CKKS_EARG, "bad output handle");
+    need(limbs >= 1 && limbs <= a->p.limbs, CKKS_ELEVEL, "cannot add limbs");
+    DevPoly tmp;
+    tmp.ensure(&c, 2, limbs);
+    ckks::ew_binary(c, ckks::EwOp::Copy, a->p.data, stride(a->p), nullptr, 0, tmp.data, stride(tmp), 2, limbs,
+                    c.stream);
+    tmp.limbs = limbs;
+    tmp.scale = a->p.scale;
+    tmp.deg = a->p.deg;
+    take(out->p, tmp);
+  });
+}
+
+int ckks_rotate(ckks_ctx* ctx, const ckks_ct* a, int k, ckks_ct* out) {
+  return guard([&] {
+    Context& c = C(ctx);
+    same_ctx(ctx, a);
+    need(out && out->owner == ctx, CKKS_EARG, "bad output handle");
+    ckks_ct* outs[1] = {out};
+    rotate_many(c, a, &k, 1, outs);
+  });
+}
+
+int ckks_rotate_hoisted(ckks_ctx* ctx, const ckks_ct* a, const int* k, int count, ckks_ct* const* outs) {
+  return guard([&] {
+    Context& c = C(ctx);
+    same_ctx(ctx, a);
+    need(count >= 0 && (count == 0 || (k && outs)), CKKS_EARG, "bad index list");
+    for (int i = 0; i < count; ++i) need(outs[i] && outs[i]->owner == ctx, CKKS_EARG, "bad output handle");
+    rotate_many(c, a, k, count, outs);
+  });
+}
+
+int ckks_accumulate_sum(ckks_ctx* ctx, const ckks_ct* a, int count, int stride_, ckks_ct* out) {
+  return guard([&] {
+    Context& c = C(ctx);
+    same_ctx(ctx, a);
+    need(out && out->owner == ctx, CKKS_EARG, "bad output handle");
+    need(count >= 1, CKKS_EARG, "count must be positive");
+    const int limbs = a->p.limbs;
+    ckks_ct acc;
+    acc.owner = ctx;
+    acc.p.ensure(&c, 2, limbs);
+    ckks::ew_binary(c, ckks::EwOp::Copy, a->p.data, stride(a->p), nullptr, 0, acc.p.data, stride(acc.p), 2, limbs,
+                    c.stream);
+    acc.p.limbs = limbs;
+    acc.p.scale = a->p.scale;
+    acc.p.deg = a->p.deg;
+    ckks_ct rots[3];
+    ckks_ct* outs[3] = {&rots[0], &rots[1], &rots[2]};
+    for (int i = 0; i < 3; ++i) rots[i].owner = ctx;
+    for (long step = 1; step < count; step *= 4) {
+      int ks[3], n = 0;
+      for (int m = 1; m < 4 && step * m < count; ++m) ks[n++] = (int)(stride_ * step * m);
+      rotate_many(c, &acc, ks, n, outs);
+      for (int r = 0; r < n; ++r)
+        ckks::ew_binary(c, ckks::EwOp::Add, acc.p.data, stride(acc.p), rots[r].p.data, stride(rots[r].p),
+                        acc.p.data, stride(acc.p), 2, limbs, c.stream);
+    }
+    take(out->p, acc.p);
+  });
+}
+
+int ckks_profile_enable(ckks_ctx* ctx, int on) {
+  return guard([&] { C(ctx).prof.on = on != 0; });
+}
+
+int ckks_profile_reset(ckks_ctx* ctx) {
+  return guard([&] { C(ctx).prof.reset(); });
+}
+
+int ckks_profile_report(ckks_ctx* ctx, char* buf, size_t size) {
+  std::string js;
+  const int rc = guard([&] {
+    auto t = C(ctx).prof.report();
+    js = "{";
+    bool first = true;
+    char tmp[256];
+    for (auto& kv : t) {
+      std::snprintf(tmp, sizeof tmp, "%s\"%s\": {\"launches\": %ld, \"ms\": %.6f, \"bytes\": %.1f}",
+                    first ? "" : ", ", kv.first.c_str(), kv.second.launches, kv.second.ms, kv.second.bytes);
+      js += tmp;
+      first = false;
+    }
+    js += "}";
+  });
+  if (rc != CKKS_OK) return -1;
+  if (buf && size) {
+    const size_t n = js.size() < size - 1 ? js.size() : size - 1;
+    std::memcpy(buf, js.data(), n);
+    buf[n] = 0;
+  }
+  return (int)js.size();
+}
+
+int ckks_ntt_forward_device(ckks_ctx* ctx, uint64_t* data, int nlimbs, int first_prime) {
+  return guard([&] {
+    Context& c = C(ctx);
+    need(data && nlimbs >= 0 && first_prime >= 0 && first_prime + nlimbs <= c.P, CKKS_EARG, "bad limb range");
+    ckks::LimbMap m{nlimbs, nlimbs, c.L, 0, first_prime};
+    ckks::ntt_forward(c, data, nlimbs, m, c.stream);
+    CKKS_CUDA(cudaGetLastError());
+  });
+}
+
+int ckks_ntt_inverse_device(ckks_ctx* ctx, uint64_t* data, int nlimbs, int first_prime) {
+  return guard([&] {
+    Context& c = C(ctx);
+    need(data && nlimbs >= 0 && first_prime >= 0 && first_prime + nlimbs <= c.P, CKKS_EARG, "bad limb range");
+    ckks::LimbMap m{nlimbs, nlimbs, c.L, 0, first_prime};
+    ckks::ntt_inverse(c, data, nlimbs, m, c.stream);
+    CKKS_CUDA(cudaGetLastError());
+  });
+}
+
+}  // extern "C"

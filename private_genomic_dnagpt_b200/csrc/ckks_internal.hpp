@@ -1,0 +1,244 @@
+// ckks_internal.hpp -- engine-internal types shared by the CUDA translation
+// units: the device-resident context (prime chain, NTT and conversion
+// tables, keys), ciphertext/plaintext objects and the kernel launchers.
+#pragma once
+#include <cuda_runtime.h>
+
+#include <cstdint>
+#include <map>
+#include <memory>
+#include <stdexcept>
+#include <string>
+#include <vector>
+
+#include "modarith.cuh"
+
+namespace ckks {
+
+struct Error : std::runtime_error {
+  int code;
+  Error(int c, const std::string& m) : std::runtime_error(m), code(c) {}
+};
+
+// status codes returned through the C ABI
+enum : int {
+  kOk = 0,
+  kErrArgument = 1,
+  kErrState = 2,
+  kErrCuda = 3,
+  kErrKeyMissing = 4,
+  kErrLevel = 5,
+  kErrScale = 6,
+  kErrCapacity = 7,
+};
+
+void cuda_check(cudaError_t e, const char* what);
+#define CKKS_CUDA(x) ::ckks::cuda_check((x), #x)
+
+// Maps batch limb index -> global prime index.  A batch holds polynomials of
+// `nper` limbs each; the first `lq` limbs of every polynomial are the Q primes
+// 0..lq-1, the rest are the special primes L..L+nper-lq-1.  With
+// skip_alpha > 0, polynomial p skips its limbs [p*skip_alpha, (p+1)*skip_alpha)
+// that lie below lq (the ModUp digit's own limbs, already in NTT form).
+struct LimbMap {
+  int nper;
+  int lq;
+  int L;
+  int skip_alpha;
+  int q0 = 0;  // first Q prime of each polynomial (rescale transforms limb l-1 alone)
+  __host__ __device__ int prime(int limb) const {
+    const int t = limb % nper;
+    return t < lq ? q0 + t : L + (t - lq);
+  }
+  __host__ __device__ bool skipped(int limb) const {
+    if (skip_alpha <= 0) return false;
+    const int p = limb / nper, t = limb % nper;
+    const int lo = p * skip_alpha;
+    const int hi = (lo + skip_alpha < lq) ? lo + skip_alpha : lq;
+    return t >= lo && t < hi;
+  }
+  static LimbMap q(int lq, int L) { return {lq, lq, L, 0, 0}; }
+  static LimbMap ext(int lq, int K, int L) { return {lq + K, lq, L, 0, 0}; }
+  static LimbMap ponly(int K, int L) { return {K, 0, L, 0, 0}; }
+  static LimbMap single(int prime) { return {1, 1, 0, 0, prime}; }
+};
+
+struct Params {
+  int log_n = 16;
+  int limbs = 24;  // L: Q primes at the top level
+  int dnum = 3;
+  int first_mod_bits = 60;
+  int scale_mod_bits = 50;
+  int special_mod_bits = 60;
+  uint64_t seed = 1;
+  int device = 0;
+};
+
+// constants of one level (number of Q limbs l) for ModUp / ModDown / Rescale
+struct LevelTables {
+  int limbs = 0;
+  int beta = 0;
+  // ModUp, per digit j and source i: (Qhat_{j,i})^-1 mod q_i as Shoup pair
+  ulonglong2* d_up_hatinv = nullptr;  // [beta][alpha]
+  // ModUp, per digit j, source i, extended target t: Qhat_{j,i} mod m_t
+  uint64_t* d_up_hat = nullptr;  // [beta][alpha][l+K]
+  // ModDown: Phat_k mod q_t
+  uint64_t* d_down_phat = nullptr;  // [K][l]
+  ulonglong2* d_down_pinv = nullptr;  // [l] P^-1 mod q_t
+  // Rescale: q_{l-1}^-1 mod q_i, i < l-1
+  ulonglong2* d_rescale_inv = nullptr;  // [l-1]
+};
+
+// Per-context kernel timer: when enabled, every launch site records a CUDA
+// event pair on the launching stream together with the launch's algorithmic
+// bytes; report() folds them into per-kernel launch counts, device time and
+// bytes.  Disabled, a scope costs one branch.
+class Profiler {
+ public:
+  bool on = false;
+  struct Totals {
+    long launches = 0;
+    double ms = 0.0;
+    double bytes = 0.0;
+  };
+  void begin(const char* name, double bytes, cudaStream_t st);
+  void end(cudaStream_t st);
+  std::map<std::string, Totals> report();  // synchronises pending events
+  void reset();
+  ~Profiler();
+
+ private:
+  struct Rec {
+    const char* name;
+    double bytes;
+    cudaEvent_t a, b;
+  };
+  std::vector<Rec> pending_;
+  std::vector<cudaEvent_t> pool_;
+  std::map<std::string, Totals> totals_;
+  cudaEvent_t get();
+};
+
+class Context;
+struct ProfScope {
+  Profiler& p;
+  cudaStream_t st;
+  bool on;
+  ProfScope(const Context& c, const char* name, double bytes, cudaStream_t s);
+  ~ProfScope();
+};
+
+class Context {
+ public:
+  explicit Context(const Params& p);
+  ~Context();
+  Context(const Context&) = delete;
+  Context& operator=(const Context&) = delete;
+
+  Params params;
+  int logN, N, L, K, alpha, beta_top, P;
+  std::vector<uint64_t> moduli;  // L + K
+  std::vector<uint64_t> psi;
+  std::vector<double> scales;  // [limbs], 1..L
+  cudaStream_t stream = nullptr;
+
+  // device tables
+  Mod* d_mods = nullptr;            // [P]
+  ulonglong2* d_tw = nullptr;       // [P][N] forward (w, w')
+  ulonglong2* d_itw = nullptr;      // [P][N] inverse (w, w')
+  ulonglong2* d_ninv = nullptr;     // [P]
+  ulonglong2* d_w1ninv = nullptr;   // [P]
+  ulonglong2* d_pmod = nullptr;     // [P] P mod q_t (Shoup pair), 0 for special primes
+  double2* d_ksi = nullptr;         // [2N+1]
+  uint32_t* d_rot_group = nullptr;  // [N/2]
+  ulonglong2* d_phatinv = nullptr;  // [K] (P/p_k)^-1 mod p_k
+  std::vector<LevelTables> levels;  // index = limbs (1..L)
+
+  // keys (device, NTT form)
+  uint64_t* d_sk = nullptr;   // [P][N]
+  uint64_t* d_pk = nullptr;   // [2][L][N]
+  uint64_t* d_rlk = nullptr;  // [beta_top][2][P][N]
+  std::map<uint32_t, uint64_t*> rot_keys;  // galois element -> key
+  uint64_t enc_counter = 0;
+
+  size_t key_words() const { return (size_t)beta_top * 2 * P * N; }
+  uint32_t galois(int k) const;
+  const uint64_t* rot_key(uint32_t g) const;
+
+  void* alloc(size_t bytes) const;
+  void release(void* p) const;
+
+  mutable Profiler prof;
+  double limb_bytes() const { return 8.0 * N; }
+};
+
+inline ProfScope::ProfScope(const Context& c, const char* name, double bytes, cudaStream_t s)
+    : p(c.prof), st(s), on(c.prof.on) {
+  if (on) p.begin(name, bytes, s);
+}
+inline ProfScope::~ProfScope() {
+  if (on) p.end(st);
+}
+
+// A ciphertext or plaintext living in device memory.  c0 occupies limbs
+// [0, cap) and c1 limbs [cap, 2 cap) of `data`; the first `limbs` of each are
+// live (rescale shrinks `limbs` without moving data).
+struct DevPoly {
+  Context* ctx = nullptr;
+  uint64_t* data = nullptr;
+  int npolys = 0;
+  int cap = 0;
+  int limbs = 0;
+  double scale = 1.0;
+  int deg = 1;  // noise-scale degree (1 fresh, 2 after a product)
+  ~DevPoly();
+  void ensure(Context* c, int np, int limbs_needed);
+  uint64_t* poly(int i) const { return data + (size_t)i * cap * ctx->N; }
+};
+
+// ---- kernel launchers ----------------------------------------------------
+void ntt_forward(const Context& c, uint64_t* data, int nlimbs, LimbMap map, cudaStream_t st);
+void ntt_inverse(const Context& c, uint64_t* data, int nlimbs, LimbMap map, cudaStream_t st);
+
+// element-wise over `limbs` Q limbs of `npolys` polynomials with strides
+enum class EwOp : int { Add = 0, Sub = 1, Mul = 2, Neg = 3, Copy = 4 };
+void ew_binary(const Context& c, EwOp op, const uint64_t* a, size_t sa, const uint64_t* b, size_t sb, uint64_t* o,
+               size_t so, int npolys, int limbs, cudaStream_t st);
+// o = a * pt (pt shared by both polys)
+void ew_mul_pt(const Context& c, const uint64_t* a, size_t sa, const uint64_t* pt, uint64_t* o, size_t so,
+               int npolys, int limbs, cudaStream_t st);
+// o = a * k (per-limb constants given as host residues)
+void ew_mul_const(const Context& c, const uint64_t* a, size_t sa, uint64_t* o, size_t so, int npolys, int limbs,
+                  const std::vector<uint64_t>& k_res, cudaStream_t st);
+void ew_add_const(const Context& c, uint64_t* a, int limbs, const std::vector<uint64_t>& k_res, cudaStream_t st);
+void tensor(const Context& c, const uint64_t* a0, const uint64_t* a1, const uint64_t* b0, const uint64_t* b1,
+            uint64_t* d0, uint64_t* d1, uint64_t* d2, int limbs, cudaStream_t st);
+
+// key switching
+void modup(const Context& c, const uint64_t* d_ntt, int limbs, uint64_t* ext, cudaStream_t st);
+void ks_inner(const Context& c, const uint64_t* ext, int limbs, const uint64_t* key, uint32_t g, uint64_t* acc,
+              cudaStream_t st);
+// out_p = moddown(acc_p), plus add0 permuted by g (p = 0) and add1 (p = 1)
+// when given; acc holds 2 polys of limbs+K limbs and is consumed
+void moddown2(const Context& c, uint64_t* acc, int limbs, const uint64_t* add0, uint32_t g_add0,
+              const uint64_t* add1, uint64_t* out0, uint64_t* out1, cudaStream_t st);
+void automorphism(const Context& c, const uint64_t* a, uint64_t* o, int nlimbs, uint32_t g, cudaStream_t st);
+// rescale npolys polynomials (stride in words) of `limbs` limbs to limbs-1
+void rescale(const Context& c, const uint64_t* x, size_t sx, int npolys, int limbs, uint64_t* out, size_t so,
+             cudaStream_t st);
+
+// keys / sampling / client
+void keygen_secret_public(Context& c);
+uint64_t* make_switch_key(Context& c, const uint64_t* s_from, uint32_t key_id);
+void encrypt(Context& c, const uint64_t* pt, int limbs, uint64_t counter, uint64_t* c0, uint64_t* c1);
+void decrypt(const Context& c, const uint64_t* c0, const uint64_t* c1, int limbs, uint64_t* pt);
+
+// canonical embedding
+void encode(const Context& c, const double* d_values, int limbs, double scale, uint64_t* out, cudaStream_t st);
+void decode(const Context& c, const uint64_t* pt, int limbs, double scale, double* d_values, cudaStream_t st);
+
+// integer / double residues on the host
+uint64_t host_double_to_res(double r, uint64_t q);
+uint64_t host_int_to_res(int64_t k, uint64_t q);
+
+}  // namespace ckks

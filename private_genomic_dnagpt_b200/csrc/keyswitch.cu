@@ -1,0 +1,264 @@
+// keyswitch.cu -- hybrid key switching (ModUp, key inner product, ModDown)
+// and Rescale.
+//
+// Key switching of d (l limbs, NTT form) with dnum digits of alpha limbs:
+//   ModUp:   iNTT(d); for digit j, every limb outside the digit receives
+//            sum_i [d_i * Qhat_{j,i}^-1]_{q_i} * Qhat_{j,i} mod m_t (approximate
+//            fast basis conversion), then NTT; the digit's own limbs are the
+//            input limbs unchanged.  ext: beta x (l+K) limbs.
+//   inner:   acc_{0,1}[t] = sum_j ext_j[t][pi_g(n)] * key_j^{b,a}[t][n] with
+//            128-bit accumulation and one reduction; pi_g is the NTT-domain
+//            automorphism (identity for relinearisation), so a hoisted set of
+//            rotations shares one ModUp.
+//   ModDown: iNTT of the K special limbs, conversion P -> Q_l, NTT, and
+//            (acc - conv) * P^-1 (+ the permuted c0 for a rotation).
+// The same steps, in the same order, are restated on the CPU by the oracle;
+// every residue is canonical, so the limbs agree exactly.
+#include "ckks_internal.hpp"
+
+namespace ckks {
+
+namespace {
+
+constexpr int kThreads = 256;
+constexpr int kMaxAlpha = 16;
+constexpr int kMaxK = 16;
+
+// y_i = d_i * hatinv_i for the digit's limbs, then every other extended
+// limb t gets sum_i y_i * hat[i][t] mod m_t; digit limbs copy the NTT input.
+__global__ void __launch_bounds__(kThreads) modup_conv_kernel(const uint64_t* __restrict__ dc,
+                                                              const uint64_t* __restrict__ d_ntt,
+                                                              uint64_t* __restrict__ ext, int limbs, int L, int K,
+                                                              int alpha, int logN, const Mod* __restrict__ mods,
+                                                              const ulonglong2* __restrict__ hatinv,
+                                                              const uint64_t* __restrict__ hat) {
+  const int N = 1 << logN;
+  const int n = blockIdx.x * kThreads + threadIdx.x;
+  if (n >= N) return;
+  const int j = blockIdx.y;
+  const int E = limbs + K;
+  const int lo = j * alpha;
+  const int hi = min(lo + alpha, limbs);
+  const int cnt = hi - lo;
+  uint64_t y[kMaxAlpha];
+#pragma unroll
+  for (int i = 0; i < kMaxAlpha; ++i) {
+    if (i < cnt) {
+      const ulonglong2 hv = hatinv[j * alpha + i];
+      y[i] = mul_shoup(dc[(size_t)(lo + i) * N + n], hv.x, hv.y, mods[lo + i].q);
+    }
+  }
+  uint64_t* ej = ext + (size_t)j * E * N;
+  for (int t = 0; t < E; ++t) {
+    if (t >= lo && t < hi) {
+      ej[(size_t)t * N + n] = d_ntt[(size_t)t * N + n];
+      continue;
+    }
+    const int pt = t < limbs ? t : L + (t - limbs);
+    const Mod m = mods[pt];
+    U128 acc{0, 0};
+    const uint64_t* h = hat + (size_t)j * alpha * E + t;
+#pragma unroll
+    for (int i = 0; i < kMaxAlpha; ++i) {
+      if (i < cnt) mac_wide(acc, y[i], __ldg(h + (size_t)i * E));
+    }
+    ej[(size_t)t * N + n] = reduce128(acc, m);
+  }
+}
+
+__global__ void __launch_bounds__(kThreads) ks_inner_kernel(const uint64_t* __restrict__ ext,
+                                                            const uint64_t* __restrict__ key,
+                                                            uint64_t* __restrict__ acc, int limbs, int L, int K,
+                                                            int P, int beta, uint32_t g, int logN,
+                                                            const Mod* __restrict__ mods) {
+  const int N = 1 << logN;
+  const int n = blockIdx.x * kThreads + threadIdx.x;
+  if (n >= N) return;
+  const int t = blockIdx.y;
+  const int E = limbs + K;
+  const int pt = t < limbs ? t : L + (t - limbs);
+  const Mod m = mods[pt];
+  const uint32_t src = (g == 1u) ? (uint32_t)n : auto_index((uint32_t)n, g, logN);
+  U128 s0{0, 0}, s1{0, 0};
+  for (int j = 0; j < beta; ++j) {
+    const uint64_t v = ext[((size_t)j * E + t) * N + src];
+    const uint64_t kb = key[((size_t)j * 2 * P + pt) * N + n];
+    const uint64_t ka = key[((size_t)j * 2 * P + P + pt) * N + n];
+    mac_wide(s0, v, kb);
+    mac_wide(s1, v, ka);
+  }
+  acc[(size_t)t * N + n] = reduce128(s0, m);
+  acc[((size_t)E + t) * N + n] = reduce128(s1, m);
+}
+
+// conv[p][t] = sum_k [x_k * phatinv_k]_{p_k} * phat[k][t] mod q_t for both polys
+__global__ void __launch_bounds__(kThreads) moddown_conv_kernel(const uint64_t* __restrict__ acc,
+                                                                uint64_t* __restrict__ conv, int limbs, int L,
+                                                                int K, int logN, const Mod* __restrict__ mods,
+                                                                const ulonglong2* __restrict__ phatinv,
+                                                                const uint64_t* __restrict__ phat) {
+  const int N = 1 << logN;
+  const int n = blockIdx.x * kThreads + threadIdx.x;
+  if (n >= N) return;
+  const int p = blockIdx.y;
+  const int E = limbs + K;
+  const uint64_t* xp = acc + ((size_t)p * E + limbs) * N;  // the K special limbs (coefficient form)
+  uint64_t y[kMaxK];
+#pragma unroll
+  for (int k = 0; k < kMaxK; ++k) {
+    if (k < K) {
+      const ulonglong2 hv = phatinv[k];
+      y[k] = mul_shoup(xp[(size_t)k * N + n], hv.x, hv.y, mods[L + k].q);
+    }
+  }
+  uint64_t* o = conv + (size_t)p * limbs * N;
+  for (int t = 0; t < limbs; ++t) {
+    U128 s{0, 0};
+#pragma unroll
+    for (int k = 0; k < kMaxK; ++k) {
+      if (k < K) mac_wide(s, y[k], __ldg(phat + (size_t)k * limbs + t));
+    }
+    o[(size_t)t * N + n] = reduce128(s, mods[t]);
+  }
+}
+
+// out_p[t] = (acc_p[t] - conv_p[t]) * P^-1, plus add0[t][pi_g(n)] for p = 0
+// and add1[t][n] for p = 1 when given
+__global__ void __launch_bounds__(kThreads) moddown_combine_kernel(const uint64_t* __restrict__ acc,
+                                                                   const uint64_t* __restrict__ conv,
+                                                                   const uint64_t* __restrict__ add0, uint32_t g,
+                                                                   const uint64_t* __restrict__ add1,
+                                                                   uint64_t* __restrict__ out0,
+                                                                   uint64_t* __restrict__ out1, int limbs, int K,
+                                                                   int logN, const Mod* __restrict__ mods,
+                                                                   const ulonglong2* __restrict__ pinv) {
+  const int N = 1 << logN;
+  const int n = blockIdx.x * kThreads + threadIdx.x;
+  if (n >= N) return;
+  const int t = blockIdx.y % limbs, p = blockIdx.y / limbs;
+  const int E = limbs + K;
+  const uint64_t q = mods[t].q;
+  const ulonglong2 pv = pinv[t];
+  const uint64_t a = acc[((size_t)p * E + t) * N + n];
+  const uint64_t cv = conv[((size_t)p * limbs + t) * N + n];
+  uint64_t r = mul_shoup(sub_mod(a, cv, q), pv.x, pv.y, q);
+  if (p == 0) {
+    if (add0) {
+      const uint32_t src = (g == 1u) ? (uint32_t)n : auto_index((uint32_t)n, g, logN);
+      r = add_mod(r, add0[(size_t)t * N + src], q);
+    }
+    out0[(size_t)t * N + n] = r;
+  } else {
+    if (add1) r = add_mod(r, add1[(size_t)t * N + n], q);
+    out1[(size_t)t * N + n] = r;
+  }
+}
+
+// tmp[p][i] = last_p mod q_i (coefficient form), i < limbs-1
+__global__ void __launch_bounds__(kThreads) rescale_spread_kernel(const uint64_t* __restrict__ last,
+                                                                  uint64_t* __restrict__ tmp, int limbs, int logN,
+                                                                  const Mod* __restrict__ mods) {
+  const int N = 1 << logN;
+  const int n = blockIdx.x * kThreads + threadIdx.x;
+  if (n >= N) return;
+  const int lo = limbs - 1;
+  const int i = blockIdx.y % lo, p = blockIdx.y / lo;
+  const uint64_t v = last[(size_t)p * N + n];
+  tmp[((size_t)p * lo + i) * N + n] = reduce128(U128{v, 0}, mods[i]);
+}
+
+__global__ void __launch_bounds__(kThreads) rescale_combine_kernel(const uint64_t* __restrict__ x, size_t sx,
+                                                                   const uint64_t* __restrict__ tmp,
+                                                                   uint64_t* __restrict__ out, size_t so,
+                                                                   int limbs, int logN,
+                                                                   const Mod* __restrict__ mods,
+                                                                   const ulonglong2* __restrict__ inv) {
+  const int N = 1 << logN;
+  const int n = blockIdx.x * kThreads + threadIdx.x;
+  if (n >= N) return;
+  const int lo = limbs - 1;
+  const int i = blockIdx.y % lo, p = blockIdx.y / lo;
+  const uint64_t q = mods[i].q;
+  const ulonglong2 iv = inv[i];
+  const uint64_t a = x[p * sx + (size_t)i * N + n];
+  const uint64_t b = tmp[((size_t)p * lo + i) * N + n];
+  out[p * so + (size_t)i * N + n] = mul_shoup(sub_mod(a, b, q), iv.x, iv.y, q);
+}
+
+}  // namespace
+
+void modup(const Context& c, const uint64_t* d_ntt, int limbs, uint64_t* ext, cudaStream_t st) {
+  if (c.alpha > kMaxAlpha) throw Error(kErrArgument, "alpha above 16 is not supported");
+  const int N = c.N, E = limbs + c.K;
+  const LevelTables& lt = c.levels[limbs];
+  uint64_t* dc = (uint64_t*)c.alloc(sizeof(uint64_t) * (size_t)limbs * N);
+  CKKS_CUDA(cudaMemcpyAsync(dc, d_ntt, sizeof(uint64_t) * (size_t)limbs * N, cudaMemcpyDeviceToDevice, st));
+  ntt_inverse(c, dc, limbs, LimbMap::q(limbs, c.L), st);
+  const dim3 grid((N + kThreads - 1) / kThreads, lt.beta);
+  // reads the input limbs (coefficient form for the sources, NTT form for the
+  // copied ones) and writes every extended limb of every digit
+  ProfScope ps(c, "modup_conv", (2.0 * limbs + (double)lt.beta * E) * c.limb_bytes(), st);
+  modup_conv_kernel<<<grid, kThreads, 0, st>>>(dc, d_ntt, ext, limbs, c.L, c.K, c.alpha, c.logN, c.d_mods,
+                                               lt.d_up_hatinv, lt.d_up_hat);
+  CKKS_CUDA(cudaGetLastError());
+  LimbMap m = LimbMap::ext(limbs, c.K, c.L);
+  m.skip_alpha = c.alpha;
+  ntt_forward(c, ext, lt.beta * E, m, st);
+  c.release(dc);
+}
+
+void ks_inner(const Context& c, const uint64_t* ext, int limbs, const uint64_t* key, uint32_t g, uint64_t* acc,
+              cudaStream_t st) {
+  const LevelTables& lt = c.levels[limbs];
+  const dim3 grid((c.N + kThreads - 1) / kThreads, limbs + c.K);
+  const double E = limbs + c.K;
+  ProfScope ps(c, "ks_inner", (3.0 * lt.beta * E + 2.0 * E) * c.limb_bytes(), st);
+  ks_inner_kernel<<<grid, kThreads, 0, st>>>(ext, key, acc, limbs, c.L, c.K, c.P, lt.beta, g, c.logN, c.d_mods);
+  CKKS_CUDA(cudaGetLastError());
+}
+
+void moddown2(const Context& c, uint64_t* acc, int limbs, const uint64_t* add0, uint32_t g_add0,
+              const uint64_t* add1, uint64_t* out0, uint64_t* out1, cudaStream_t st) {
+  if (c.K > kMaxK) throw Error(kErrArgument, "more than 16 special primes is not supported");
+  const int N = c.N, E = limbs + c.K;
+  const LevelTables& lt = c.levels[limbs];
+  for (int p = 0; p < 2; ++p) ntt_inverse(c, acc + ((size_t)p * E + limbs) * N, c.K, LimbMap::ponly(c.K, c.L), st);
+  uint64_t* conv = (uint64_t*)c.alloc(sizeof(uint64_t) * 2 * (size_t)limbs * N);
+  const dim3 g1((N + kThreads - 1) / kThreads, 2);
+  ProfScope ps1(c, "moddown_conv", (2.0 * c.K + 2.0 * limbs) * c.limb_bytes(), st);
+  moddown_conv_kernel<<<g1, kThreads, 0, st>>>(acc, conv, limbs, c.L, c.K, c.logN, c.d_mods, c.d_phatinv,
+                                               lt.d_down_phat);
+  CKKS_CUDA(cudaGetLastError());
+  ntt_forward(c, conv, 2 * limbs, LimbMap::q(limbs, c.L), st);
+  const dim3 g2((N + kThreads - 1) / kThreads, 2 * limbs);
+  ProfScope ps2(c, "moddown_combine", ((add0 ? 1.0 : 0.0) + (add1 ? 1.0 : 0.0) + 6.0) * limbs * c.limb_bytes(), st);
+  moddown_combine_kernel<<<g2, kThreads, 0, st>>>(acc, conv, add0, g_add0, add1, out0, out1, limbs, c.K, c.logN, c.d_mods,
+                                                  lt.d_down_pinv);
+  CKKS_CUDA(cudaGetLastError());
+  c.release(conv);
+}
+
+void rescale(const Context& c, const uint64_t* x, size_t sx, int npolys, int limbs, uint64_t* out, size_t so,
+             cudaStream_t st) {
+  if (limbs < 2) throw Error(kErrLevel, "cannot rescale a single-limb ciphertext");
+  const int N = c.N, lo = limbs - 1;
+  const LevelTables& lt = c.levels[limbs];
+  uint64_t* last = (uint64_t*)c.alloc(sizeof(uint64_t) * (size_t)npolys * N);
+  for (int p = 0; p < npolys; ++p)
+    CKKS_CUDA(cudaMemcpyAsync(last + (size_t)p * N, x + p * sx + (size_t)lo * N, sizeof(uint64_t) * N,
+                              cudaMemcpyDeviceToDevice, st));
+  ntt_inverse(c, last, npolys, LimbMap::single(lo), st);
+  uint64_t* tmp = (uint64_t*)c.alloc(sizeof(uint64_t) * (size_t)npolys * lo * N);
+  const dim3 g1((N + kThreads - 1) / kThreads, npolys * lo);
+  ProfScope ps1(c, "rescale_spread", (1.0 + lo) * npolys * c.limb_bytes(), st);
+  rescale_spread_kernel<<<g1, kThreads, 0, st>>>(last, tmp, limbs, c.logN, c.d_mods);
+  CKKS_CUDA(cudaGetLastError());
+  ntt_forward(c, tmp, npolys * lo, LimbMap::q(lo, c.L), st);
+  ProfScope ps2(c, "rescale_combine", 3.0 * npolys * lo * c.limb_bytes(), st);
+  rescale_combine_kernel<<<g1, kThreads, 0, st>>>(x, sx, tmp, out, so, limbs, c.logN, c.d_mods, lt.d_rescale_inv);
+  CKKS_CUDA(cudaGetLastError());
+  c.release(last);
+  c.release(tmp);
+}
+
+}  // namespace ckks

@@ -1,0 +1,247 @@
+"""Parity of the CUDA engine against the CPU oracle, through the C ABI.
+
+Integer work is compared bit for bit (every limb of every key, plaintext and
+ciphertext), floating-point decode within 1e-12 absolute on unit-range slots.
+Same seeds, same parameters, same call order -> identical limbs.
+"""
+
+import numpy as np
+import pytest
+
+from oracle import Oracle
+
+pytestmark = pytest.mark.gpu
+
+import private_genomic_dnagpt_b200 as eng  # noqa: E402
+
+
+def ladder_keys(count, stride):
+    keys, step = [], 1
+    while step < count:
+        keys += [stride * step * m for m in range(1, 4) if step * m < count]
+        step *= 4
+    return keys
+
+
+def make_pair(logN, L, dnum, seed, rot=(), relin=True):
+    o = Oracle(logN=logN, L=L, dnum=dnum, seed=seed)
+    cc = eng.GenCryptoContext(eng.CCParams(ring_dim_log=logN, limbs=L, dnum=dnum, seed=seed))
+    o.keygen()
+    cc.KeyGen()
+    if relin:
+        o.relin_keygen()
+        cc.EvalMultKeyGen()
+    if rot:
+        o.rot_keygen(list(rot))
+        cc.EvalRotateKeyGen(list(rot))
+    return o, cc
+
+
+ROT = [1, 2, 3, 5, -1, -7, 8, 64, 100] + ladder_keys(64, 4) + ladder_keys(16, 32)
+
+
+@pytest.fixture(scope="module")
+def pair10():
+    return make_pair(10, 6, 3, 21, rot=sorted(set(ROT)))
+
+
+@pytest.mark.parametrize("logN,L,dnum", [(10, 6, 3), (12, 8, 4), (13, 5, 2), (16, 24, 3), (15, 16, 2), (17, 8, 4)])
+def test_prime_chain_matches(logN, L, dnum):
+    o = Oracle(logN=logN, L=L, dnum=dnum, seed=1)
+    cc = eng.GenCryptoContext(eng.CCParams(ring_dim_log=logN, limbs=L, dnum=dnum, seed=1))
+    assert np.array_equal(o.moduli, cc.moduli)
+    assert cc.K == o.K and cc.alpha == o.alpha
+    for lvl in range(L):
+        assert cc.scale_at(lvl) == o.scale(L - lvl)
+
+
+@pytest.mark.parametrize("logN", [6, 7, 10, 12, 15, 16, 17])
+def test_ntt_bit_exact(logN):
+    import torch
+    L = 3
+    o = Oracle(logN=logN, L=L, dnum=1, seed=2)
+    cc = eng.GenCryptoContext(eng.CCParams(ring_dim_log=logN, limbs=L, dnum=1, seed=2))
+    rng = np.random.default_rng(logN)
+    P = L + o.K
+    a = np.stack([rng.integers(0, int(o.moduli[i]), o.N, dtype=np.uint64) for i in range(P)])
+    ref = np.stack([o.ntt(a[i], i) for i in range(P)])
+    dev = torch.from_numpy(a.view(np.int64).copy()).cuda()
+    torch.cuda.synchronize()
+    eng._check(eng.lib().ckks_ntt_forward_device(cc.h, dev.data_ptr(), P, 0))
+    cc.Synchronize()
+    got = dev.cpu().numpy().view(np.uint64)
+    assert np.array_equal(got, ref)
+    eng._check(eng.lib().ckks_ntt_inverse_device(cc.h, dev.data_ptr(), P, 0))
+    cc.Synchronize()
+    assert np.array_equal(dev.cpu().numpy().view(np.uint64), a)
+    # a sub-range starting at a later prime
+    dev2 = torch.from_numpy(a[2:4].view(np.int64).copy()).cuda()
+    torch.cuda.synchronize()
+    eng._check(eng.lib().ckks_ntt_forward_device(cc.h, dev2.data_ptr(), 2, 2))
+    cc.Synchronize()
+    assert np.array_equal(dev2.cpu().numpy().view(np.uint64), ref[2:4])
+
+
+@pytest.mark.parametrize("logN", [10, 16])
+def test_encode_bit_exact_and_decode(logN):
+    L = 4
+    o = Oracle(logN=logN, L=L, dnum=2, seed=3)
+    cc = eng.GenCryptoContext(eng.CCParams(ring_dim_log=logN, limbs=L, dnum=2, seed=3))
+    rng = np.random.default_rng(7)
+    for vals in (rng.standard_normal(o.N // 2), rng.uniform(-4, 4, o.N // 2) * 1e3, np.zeros(o.N // 2)):
+        for lvl in (0, 1, 3):
+            pt = cc.MakeCKKSPackedPlaintext(vals, level=lvl)
+            ref = o.encode(vals, L - lvl)
+            assert np.array_equal(pt.limbs_array(), ref)
+            dec = pt.GetRealPackedValue()
+            dref = o.decode(ref, o.scale(L - lvl))
+            assert np.abs(dec - dref).max() <= 1e-12 * max(1.0, np.abs(dref).max())
+    # values above 2^63 after scaling (exact mantissa * 2^e path)
+    big = np.zeros(o.N // 2)
+    big[:3] = [3.0e6, -7.5e5, 1.25]
+    pt = cc.MakeCKKSPackedPlaintext(big, limbs=2, scale=2.0 ** 60)
+    assert np.array_equal(pt.limbs_array(), o.encode(big, 2, scale=2.0 ** 60))
+
+
+def test_partial_slot_vector_is_zero_padded(pair10):
+    o, cc = pair10
+    vals = np.arange(5, dtype=np.float64)
+    pt = cc.MakeCKKSPackedPlaintext(vals)
+    full = np.zeros(o.N // 2)
+    full[:5] = vals
+    assert np.array_equal(pt.limbs_array(), o.encode(full, o.L))
+
+
+def test_keys_bit_exact(pair10):
+    o, cc = pair10
+    assert np.array_equal(cc.key_array(0), o.secret_key())
+    assert np.array_equal(cc.key_array(1), o.public_key())
+    assert np.array_equal(cc.key_array(2), o.switch_key(0))
+    for k in (1, -1, 64):
+        assert np.array_equal(cc.key_array(3, k), o.switch_key(k))
+
+
+def test_encrypt_decrypt_bit_exact(pair10):
+    o, cc = pair10
+    rng = np.random.default_rng(8)
+    x = rng.uniform(-1, 1, o.N // 2)
+    cc.set_encrypt_counter(40)
+    for lvl in (0, 2):
+        ct = cc.Encrypt(cc.MakeCKKSPackedPlaintext(x, level=lvl))
+        ref = o.encrypt(o.encode(x, o.L - lvl), 40 + lvl // 2)
+        assert np.array_equal(ct.limbs_array(), ref)
+        assert np.array_equal(cc.Decrypt(ct).limbs_array(), o.decrypt(ref))
+        assert np.abs(cc.Decrypt(ct).GetRealPackedValue() - x).max() < 1e-8
+
+
+def _fresh(o, cc, seed, limbs):
+    x = np.random.default_rng(seed).uniform(-1, 1, o.N // 2)
+    ref = o.encrypt(o.encode(x, limbs), 1000 + seed)
+    return x, ref, cc.import_ct(ref, o.scale(limbs))
+
+
+def test_elementwise_bit_exact(pair10):
+    o, cc = pair10
+    L = o.L
+    x, rx, cx = _fresh(o, cc, 1, L)
+    y, ry, cy = _fresh(o, cc, 2, L)
+    assert np.array_equal(cc.add(cx, cy).limbs_array(), o.add(rx, ry))
+    assert np.array_equal(cc.sub(cx, cy).limbs_array(), o.sub(rx, ry))
+    p = o.encode(y, L)
+    assert np.array_equal(cc.mul_pt(cx, cc.import_pt(p, o.scale(L))).limbs_array(), o.mul_pt(rx, p))
+    assert np.array_equal(cc.mul_int(cx, -12345).limbs_array(), o.mul_int(rx, -12345))
+    got = cc.EvalAdd(cx, 0.375).limbs_array()
+    assert np.array_equal(got, o.add_const(rx, 0.375, o.scale(L)))
+
+
+@pytest.mark.parametrize("limbs", [6, 4, 2, 1])
+def test_mul_ct_relin_bit_exact(pair10, limbs):
+    o, cc = pair10
+    x, rx, cx = _fresh(o, cc, 3, limbs)
+    y, ry, cy = _fresh(o, cc, 4, limbs)
+    got = cc.mul_ct(cx, cy)
+    ref = o.mul_ct(rx, ry)
+    assert np.array_equal(got.limbs_array(), ref)
+    if limbs >= 2:
+        assert np.array_equal(cc.rescale(got).limbs_array(), o.rescale(ref))
+
+
+@pytest.mark.parametrize("k", [1, 2, -1, 5, 100, -7])
+@pytest.mark.parametrize("limbs", [6, 3])
+def test_rotate_bit_exact(pair10, k, limbs):
+    o, cc = pair10
+    x, rx, cx = _fresh(o, cc, 5, limbs)
+    got = cc.EvalRotate(cx, k)
+    assert np.array_equal(got.limbs_array(), o.rotate(rx, k))
+    dec = cc.Decrypt(got).GetRealPackedValue()
+    assert np.abs(dec - np.roll(x, -k)).max() < 1e-8
+
+
+def test_hoisted_and_inplace(pair10):
+    o, cc = pair10
+    x, rx, cx = _fresh(o, cc, 6, o.L)
+    ks = [1, 2, 3, 0, 8]
+    outs = cc.EvalFastRotation(cx, ks)
+    ref = o.rotate_hoisted(rx, ks)
+    for i in range(len(ks)):
+        assert np.array_equal(outs[i].limbs_array(), ref[i])
+    # output aliasing the input
+    eng._check(eng.lib().ckks_rotate(cc.h, cx.h, 5, cx.h))
+    assert np.array_equal(cx.limbs_array(), o.rotate(rx, 5))
+
+
+@pytest.mark.parametrize("count,stride", [(64, 4), (16, 32)])
+def test_accumulate_sum_bit_exact(pair10, count, stride):
+    o, cc = pair10
+    x, rx, cx = _fresh(o, cc, 7, o.L)
+    got = cc.AccumulateSum(cx, count, stride)
+    assert np.array_equal(got.limbs_array(), o.accumulate_sum(rx, count, stride))
+
+
+def test_errors_are_reported(pair10):
+    o, cc = pair10
+    x, rx, cx = _fresh(o, cc, 8, 3)
+    y, ry, cy = _fresh(o, cc, 9, 2)
+    with pytest.raises(eng.CKKSError) as e:
+        cc.EvalRotate(cx, 77)
+    assert e.value.code == 4
+    with pytest.raises(eng.CKKSError) as e:
+        cc.add(cx, cy)
+    assert e.value.code == 5
+    one = cc.import_ct(ry[:, :1], o.scale(1))
+    with pytest.raises(eng.CKKSError) as e:
+        cc.rescale(one)
+    assert e.value.code == 5
+    with pytest.raises(eng.CKKSError):
+        cc.MakeCKKSPackedPlaintext(np.zeros(o.N))  # more values than slots
+
+
+def test_flexibleauto_chain_accuracy(pair10):
+    """(x*y + x) * y via EvalMult/EvalAdd with automatic rescale / level alignment."""
+    o, cc = pair10
+    rng = np.random.default_rng(10)
+    x = rng.uniform(-1, 1, o.N // 2)
+    y = rng.uniform(-1, 1, o.N // 2)
+    cx = cc.Encrypt(cc.MakeCKKSPackedPlaintext(x))
+    cy = cc.Encrypt(cc.MakeCKKSPackedPlaintext(y))
+    t = cc.EvalMult(cx, cy)
+    t = cc.EvalAdd(t, cx)
+    t = cc.EvalMult(t, cy)
+    t = cc.Rescale(t)
+    got = cc.Decrypt(t).GetRealPackedValue()
+    assert np.abs(got - (x * y + x) * y).max() < 1e-6
+
+
+def test_full_size_rotation_bit_exact():
+    """N = 2^16, 24 limbs, dnum 3 (the block configuration)."""
+    o, cc = make_pair(16, 24, 3, 5, rot=[1, 8], relin=False)
+    assert np.array_equal(cc.key_array(3, 8), o.switch_key(8))
+    x = np.random.default_rng(11).uniform(-1, 1, o.N // 2)
+    cc.set_encrypt_counter(3)
+    ct = cc.Encrypt(cc.MakeCKKSPackedPlaintext(x))
+    ref = o.encrypt(o.encode(x, 24), 3)
+    assert np.array_equal(ct.limbs_array(), ref)
+    got = cc.EvalRotate(ct, 8)
+    assert np.array_equal(got.limbs_array(), o.rotate(ref, 8))
+    dec = cc.Decrypt(got).GetRealPackedValue()
+    assert np.abs(dec - np.roll(x, -8)).max() < 1e-6
