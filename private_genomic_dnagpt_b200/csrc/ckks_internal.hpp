@@ -46,21 +46,23 @@ struct LimbMap {
   int L;
   int skip_alpha;
   int q0 = 0;  // first Q prime of each polynomial (rescale transforms limb l-1 alone)
+  int skip_q = 0;  // nonzero: skip every Q limb (transform only the special limbs)
   __host__ __device__ int prime(int limb) const {
     const int t = limb % nper;
     return t < lq ? q0 + t : L + (t - lq);
   }
   __host__ __device__ bool skipped(int limb) const {
+    if (skip_q && limb % nper < lq) return true;
     if (skip_alpha <= 0) return false;
     const int p = limb / nper, t = limb % nper;
     const int lo = p * skip_alpha;
     const int hi = (lo + skip_alpha < lq) ? lo + skip_alpha : lq;
     return t >= lo && t < hi;
   }
-  static LimbMap q(int lq, int L) { return {lq, lq, L, 0, 0}; }
-  static LimbMap ext(int lq, int K, int L) { return {lq + K, lq, L, 0, 0}; }
-  static LimbMap ponly(int K, int L) { return {K, 0, L, 0, 0}; }
-  static LimbMap single(int prime) { return {1, 1, 0, 0, prime}; }
+  static LimbMap q(int lq, int L) { return {lq, lq, L, 0, 0, 0}; }
+  static LimbMap ext(int lq, int K, int L) { return {lq + K, lq, L, 0, 0, 0}; }
+  static LimbMap ponly(int K, int L) { return {K, 0, L, 0, 0, 0}; }
+  static LimbMap single(int prime) { return {1, 1, 0, 0, prime, 0}; }
 };
 
 struct Params {
@@ -87,6 +89,10 @@ struct LevelTables {
   ulonglong2* d_down_pinv = nullptr;  // [l] P^-1 mod q_t
   // Rescale: q_{l-1}^-1 mod q_i, i < l-1
   ulonglong2* d_rescale_inv = nullptr;  // [l-1]
+  // ModUp pre-scaling folded into the inverse NTT of d: limb i of digit j
+  // leaves the transform multiplied by Qhat_{j,i}^-1
+  ulonglong2* d_up_scale_a = nullptr;  // [l] Qhat^-1 * n^-1
+  ulonglong2* d_up_scale_b = nullptr;  // [l] Qhat^-1 * Winv[1] * n^-1
 };
 
 // Per-context kernel timer: when enabled, every launch site records a CUDA
@@ -101,8 +107,8 @@ class Profiler {
     double ms = 0.0;
     double bytes = 0.0;
   };
-  void begin(const char* name, double bytes, cudaStream_t st);
-  void end(cudaStream_t st);
+  size_t begin(const char* name, double bytes, cudaStream_t st);
+  void end(size_t idx, cudaStream_t st);
   std::map<std::string, Totals> report();  // synchronises pending events
   void reset();
   ~Profiler();
@@ -124,6 +130,7 @@ struct ProfScope {
   Profiler& p;
   cudaStream_t st;
   bool on;
+  size_t idx = 0;
   ProfScope(const Context& c, const char* name, double bytes, cudaStream_t s);
   ~ProfScope();
 };
@@ -152,6 +159,8 @@ class Context {
   double2* d_ksi = nullptr;         // [2N+1]
   uint32_t* d_rot_group = nullptr;  // [N/2]
   ulonglong2* d_phatinv = nullptr;  // [K] (P/p_k)^-1 mod p_k
+  ulonglong2* d_down_scale_a = nullptr;  // [K] Phat_k^-1 * n^-1 (ModDown pre-scaling)
+  ulonglong2* d_down_scale_b = nullptr;  // [K] Phat_k^-1 * Winv[1] * n^-1
   std::vector<LevelTables> levels;  // index = limbs (1..L)
 
   // keys (device, NTT form)
@@ -174,10 +183,10 @@ class Context {
 
 inline ProfScope::ProfScope(const Context& c, const char* name, double bytes, cudaStream_t s)
     : p(c.prof), st(s), on(c.prof.on) {
-  if (on) p.begin(name, bytes, s);
+  if (on) idx = p.begin(name, bytes, s);
 }
 inline ProfScope::~ProfScope() {
-  if (on) p.end(st);
+  if (on) p.end(idx, st);
 }
 
 // A ciphertext or plaintext living in device memory.  c0 occupies limbs
@@ -198,7 +207,10 @@ struct DevPoly {
 
 // ---- kernel launchers ----------------------------------------------------
 void ntt_forward(const Context& c, uint64_t* data, int nlimbs, LimbMap map, cudaStream_t st);
-void ntt_inverse(const Context& c, uint64_t* data, int nlimbs, LimbMap map, cudaStream_t st);
+// inverse transform; with scale_a/scale_b (indexed by prime - scale_base:
+// c*n^-1 and c*Winv[1]*n^-1 as Shoup pairs) it returns the coefficients times c
+void ntt_inverse(const Context& c, uint64_t* data, int nlimbs, LimbMap map, cudaStream_t st,
+                 const ulonglong2* scale_a = nullptr, const ulonglong2* scale_b = nullptr, int scale_base = 0);
 
 // element-wise over `limbs` Q limbs of `npolys` polynomials with strides
 enum class EwOp : int { Add = 0, Sub = 1, Mul = 2, Neg = 3, Copy = 4 };

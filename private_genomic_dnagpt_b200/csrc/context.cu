@@ -246,6 +246,16 @@ Context::Context(const Params& p) : params(p) {
       phatinv[k] = shoup_pair(invm(prod, pk), pk);
     }
     d_phatinv = upload(phatinv);
+    std::vector<ulonglong2> sa(K), sb(K);
+    for (int k = 0; k < K; ++k) {
+      const uint64_t pk = moduli[L + k];
+      const uint64_t ni = invm((uint64_t)N, pk);
+      const uint64_t w1 = mulm(ni, itw[(size_t)(L + k) * N + 1].x, pk);
+      sa[k] = shoup_pair(mulm(phatinv[k].x, ni, pk), pk);
+      sb[k] = shoup_pair(mulm(phatinv[k].x, w1, pk), pk);
+    }
+    d_down_scale_a = upload(sa);
+    d_down_scale_b = upload(sb);
   }
 
   // canonical embedding tables
@@ -293,6 +303,19 @@ Context::Context(const Params& p) : params(p) {
       }
     }
     t.d_up_hatinv = upload(hatinv);
+    {
+      std::vector<ulonglong2> sa(l), sb(l);
+      for (int i = 0; i < l; ++i) {
+        const int j = i / alpha;
+        const uint64_t qi = moduli[i];
+        const uint64_t hv = hatinv[(size_t)j * alpha + (i - j * alpha)].x;
+        const uint64_t ni = invm((uint64_t)N, qi);
+        sa[i] = shoup_pair(mulm(hv, ni, qi), qi);
+        sb[i] = shoup_pair(mulm(hv, mulm(ni, itw[(size_t)i * N + 1].x, qi), qi), qi);
+      }
+      t.d_up_scale_a = upload(sa);
+      t.d_up_scale_b = upload(sb);
+    }
     t.d_up_hat = upload(hat);
     std::vector<uint64_t> phat((size_t)K * l);
     std::vector<ulonglong2> pinv(l);
@@ -336,7 +359,11 @@ Context::~Context() {
     cudaFree(t.d_down_phat);
     cudaFree(t.d_down_pinv);
     cudaFree(t.d_rescale_inv);
+    cudaFree(t.d_up_scale_a);
+    cudaFree(t.d_up_scale_b);
   }
+  cudaFree(d_down_scale_a);
+  cudaFree(d_down_scale_b);
   cudaFree(d_mods);
   cudaFree(d_tw);
   cudaFree(d_itw);
@@ -360,21 +387,26 @@ cudaEvent_t Profiler::get() {
   return e;
 }
 
-void Profiler::begin(const char* name, double bytes, cudaStream_t st) {
+size_t Profiler::begin(const char* name, double bytes, cudaStream_t st) {
   Rec r{name, bytes, get(), get()};
-  cudaEventRecord(r.a, st);
+  CKKS_CUDA(cudaEventRecord(r.a, st));
   pending_.push_back(r);
+  return pending_.size() - 1;
 }
 
-void Profiler::end(cudaStream_t st) {
-  if (!pending_.empty()) cudaEventRecord(pending_.back().b, st);
+void Profiler::end(size_t idx, cudaStream_t st) {
+  if (idx < pending_.size()) cudaEventRecord(pending_[idx].b, st);
 }
 
 std::map<std::string, Profiler::Totals> Profiler::report() {
   for (Rec& r : pending_) {
-    cudaEventSynchronize(r.b);
     float ms = 0.f;
-    cudaEventElapsedTime(&ms, r.a, r.b);
+    if (cudaEventSynchronize(r.b) != cudaSuccess || cudaEventElapsedTime(&ms, r.a, r.b) != cudaSuccess) {
+      cudaGetLastError();  // an unrecorded pair is dropped, not reported
+      pool_.push_back(r.a);
+      pool_.push_back(r.b);
+      continue;
+    }
     Totals& t = totals_[r.name];
     t.launches += 1;
     t.ms += ms;

@@ -24,45 +24,56 @@ constexpr int kThreads = 256;
 constexpr int kMaxAlpha = 16;
 constexpr int kMaxK = 16;
 
-// y_i = d_i * hatinv_i for the digit's limbs, then every other extended
-// limb t gets sum_i y_i * hat[i][t] mod m_t; digit limbs copy the NTT input.
-__global__ void __launch_bounds__(kThreads) modup_conv_kernel(const uint64_t* __restrict__ dc,
+// ModUp conversion.  y holds [d_i * Qhat_{j,i}^-1]_{q_i} (the scaling is
+// folded into the inverse NTT); each thread owns two adjacent coefficients
+// and kTargets extended limbs of one digit, so the MAC chains of 2 x kTargets
+// outputs interleave.  Chunk 0 also copies the digit's own NTT-form limbs.
+constexpr int kTargets = 4;
+
+template <int MAXA>
+__global__ void __launch_bounds__(kThreads) modup_conv_kernel(const uint64_t* __restrict__ y,
                                                               const uint64_t* __restrict__ d_ntt,
                                                               uint64_t* __restrict__ ext, int limbs, int L, int K,
-                                                              int alpha, int logN, const Mod* __restrict__ mods,
-                                                              const ulonglong2* __restrict__ hatinv,
+                                                              int alpha, int logN, int nchunks,
+                                                              const Mod* __restrict__ mods,
                                                               const uint64_t* __restrict__ hat) {
   const int N = 1 << logN;
-  const int n = blockIdx.x * kThreads + threadIdx.x;
+  const int n = 2 * (blockIdx.x * kThreads + threadIdx.x);
   if (n >= N) return;
-  const int j = blockIdx.y;
+  const int j = blockIdx.y / nchunks, chunk = blockIdx.y % nchunks;
   const int E = limbs + K;
   const int lo = j * alpha;
   const int hi = min(lo + alpha, limbs);
   const int cnt = hi - lo;
-  uint64_t y[kMaxAlpha];
-#pragma unroll
-  for (int i = 0; i < kMaxAlpha; ++i) {
-    if (i < cnt) {
-      const ulonglong2 hv = hatinv[j * alpha + i];
-      y[i] = mul_shoup(dc[(size_t)(lo + i) * N + n], hv.x, hv.y, mods[lo + i].q);
-    }
-  }
   uint64_t* ej = ext + (size_t)j * E * N;
-  for (int t = 0; t < E; ++t) {
-    if (t >= lo && t < hi) {
-      ej[(size_t)t * N + n] = d_ntt[(size_t)t * N + n];
-      continue;
-    }
-    const int pt = t < limbs ? t : L + (t - limbs);
-    const Mod m = mods[pt];
-    U128 acc{0, 0};
-    const uint64_t* h = hat + (size_t)j * alpha * E + t;
+  ulonglong2 yv[MAXA];
 #pragma unroll
-    for (int i = 0; i < kMaxAlpha; ++i) {
-      if (i < cnt) mac_wide(acc, y[i], __ldg(h + (size_t)i * E));
+  for (int i = 0; i < MAXA; ++i)
+    if (i < cnt) yv[i] = *reinterpret_cast<const ulonglong2*>(y + (size_t)(lo + i) * N + n);
+  if (chunk == 0) {
+    for (int i = lo; i < hi; ++i)
+      *reinterpret_cast<ulonglong2*>(ej + (size_t)i * N + n) =
+          *reinterpret_cast<const ulonglong2*>(d_ntt + (size_t)i * N + n);
+  }
+  const int others = E - cnt;
+#pragma unroll
+  for (int p = 0; p < kTargets; ++p) {
+    const int tt = chunk * kTargets + p;
+    if (tt >= others) break;
+    const int t = tt < lo ? tt : tt + cnt;
+    const int pt = t < limbs ? t : L + (t - limbs);
+    const uint64_t* h = hat + (size_t)j * alpha * E + t;
+    U128 a0{0, 0}, a1{0, 0};
+#pragma unroll
+    for (int i = 0; i < MAXA; ++i) {
+      if (i < cnt) {
+        const uint64_t hv = __ldg(h + (size_t)i * E);
+        mac_wide(a0, yv[i].x, hv);
+        mac_wide(a1, yv[i].y, hv);
+      }
     }
-    ej[(size_t)t * N + n] = reduce128(acc, m);
+    const Mod m = mods[pt];
+    *reinterpret_cast<ulonglong2*>(ej + (size_t)t * N + n) = make_ulonglong2(reduce128(a0, m), reduce128(a1, m));
   }
 }
 
@@ -91,34 +102,41 @@ __global__ void __launch_bounds__(kThreads) ks_inner_kernel(const uint64_t* __re
   acc[((size_t)E + t) * N + n] = reduce128(s1, m);
 }
 
-// conv[p][t] = sum_k [x_k * phatinv_k]_{p_k} * phat[k][t] mod q_t for both polys
+// ModDown conversion: conv[p][t] = sum_k y_k * Phat_k mod q_t, where the K
+// special limbs of acc_p already hold y_k = [x_k * Phat_k^-1]_{p_k} in
+// coefficient form (scaling folded into their inverse NTT).
+template <int MAXK>
 __global__ void __launch_bounds__(kThreads) moddown_conv_kernel(const uint64_t* __restrict__ acc,
                                                                 uint64_t* __restrict__ conv, int limbs, int L,
-                                                                int K, int logN, const Mod* __restrict__ mods,
-                                                                const ulonglong2* __restrict__ phatinv,
+                                                                int K, int logN, int nchunks,
+                                                                const Mod* __restrict__ mods,
                                                                 const uint64_t* __restrict__ phat) {
   const int N = 1 << logN;
-  const int n = blockIdx.x * kThreads + threadIdx.x;
+  const int n = 2 * (blockIdx.x * kThreads + threadIdx.x);
   if (n >= N) return;
-  const int p = blockIdx.y;
+  const int p = blockIdx.y / nchunks, chunk = blockIdx.y % nchunks;
   const int E = limbs + K;
-  const uint64_t* xp = acc + ((size_t)p * E + limbs) * N;  // the K special limbs (coefficient form)
-  uint64_t y[kMaxK];
+  const uint64_t* xp = acc + ((size_t)p * E + limbs) * N;
+  ulonglong2 yv[MAXK];
 #pragma unroll
-  for (int k = 0; k < kMaxK; ++k) {
-    if (k < K) {
-      const ulonglong2 hv = phatinv[k];
-      y[k] = mul_shoup(xp[(size_t)k * N + n], hv.x, hv.y, mods[L + k].q);
-    }
-  }
+  for (int k = 0; k < MAXK; ++k)
+    if (k < K) yv[k] = *reinterpret_cast<const ulonglong2*>(xp + (size_t)k * N + n);
   uint64_t* o = conv + (size_t)p * limbs * N;
-  for (int t = 0; t < limbs; ++t) {
-    U128 s{0, 0};
 #pragma unroll
-    for (int k = 0; k < kMaxK; ++k) {
-      if (k < K) mac_wide(s, y[k], __ldg(phat + (size_t)k * limbs + t));
+  for (int pp = 0; pp < kTargets; ++pp) {
+    const int t = chunk * kTargets + pp;
+    if (t >= limbs) break;
+    U128 a0{0, 0}, a1{0, 0};
+#pragma unroll
+    for (int k = 0; k < MAXK; ++k) {
+      if (k < K) {
+        const uint64_t hv = __ldg(phat + (size_t)k * limbs + t);
+        mac_wide(a0, yv[k].x, hv);
+        mac_wide(a1, yv[k].y, hv);
+      }
     }
-    o[(size_t)t * N + n] = reduce128(s, mods[t]);
+    const Mod m = mods[t];
+    *reinterpret_cast<ulonglong2*>(o + (size_t)t * N + n) = make_ulonglong2(reduce128(a0, m), reduce128(a1, m));
   }
 }
 
@@ -193,13 +211,20 @@ void modup(const Context& c, const uint64_t* d_ntt, int limbs, uint64_t* ext, cu
   const LevelTables& lt = c.levels[limbs];
   uint64_t* dc = (uint64_t*)c.alloc(sizeof(uint64_t) * (size_t)limbs * N);
   CKKS_CUDA(cudaMemcpyAsync(dc, d_ntt, sizeof(uint64_t) * (size_t)limbs * N, cudaMemcpyDeviceToDevice, st));
-  ntt_inverse(c, dc, limbs, LimbMap::q(limbs, c.L), st);
-  const dim3 grid((N + kThreads - 1) / kThreads, lt.beta);
-  // reads the input limbs (coefficient form for the sources, NTT form for the
-  // copied ones) and writes every extended limb of every digit
-  ProfScope ps(c, "modup_conv", (2.0 * limbs + (double)lt.beta * E) * c.limb_bytes(), st);
-  modup_conv_kernel<<<grid, kThreads, 0, st>>>(dc, d_ntt, ext, limbs, c.L, c.K, c.alpha, c.logN, c.d_mods,
-                                               lt.d_up_hatinv, lt.d_up_hat);
+  ntt_inverse(c, dc, limbs, LimbMap::q(limbs, c.L), st, lt.d_up_scale_a, lt.d_up_scale_b);
+  const int nchunks = (E - std::min(c.alpha, limbs) + kTargets - 1) / kTargets;
+  const dim3 grid((N / 2 + kThreads - 1) / kThreads, lt.beta * nchunks);
+  {
+    // reads the input limbs (coefficient form for the sources, NTT form for
+    // the copied ones) and writes every extended limb of every digit
+    ProfScope ps(c, "modup_conv", (2.0 * limbs + (double)lt.beta * E) * c.limb_bytes(), st);
+    auto kern = c.alpha <= 4 ? modup_conv_kernel<4>
+                : c.alpha <= 8 ? modup_conv_kernel<8>
+                : c.alpha <= 12 ? modup_conv_kernel<12>
+                                : modup_conv_kernel<16>;
+    kern<<<grid, kThreads, 0, st>>>(dc, d_ntt, ext, limbs, c.L, c.K, c.alpha, c.logN, nchunks, c.d_mods,
+                                    lt.d_up_hat);
+  }
   CKKS_CUDA(cudaGetLastError());
   LimbMap m = LimbMap::ext(limbs, c.K, c.L);
   m.skip_alpha = c.alpha;
@@ -222,18 +247,30 @@ void moddown2(const Context& c, uint64_t* acc, int limbs, const uint64_t* add0, 
   if (c.K > kMaxK) throw Error(kErrArgument, "more than 16 special primes is not supported");
   const int N = c.N, E = limbs + c.K;
   const LevelTables& lt = c.levels[limbs];
-  for (int p = 0; p < 2; ++p) ntt_inverse(c, acc + ((size_t)p * E + limbs) * N, c.K, LimbMap::ponly(c.K, c.L), st);
+  // both polynomials' special limbs in one launch (the Q limbs are skipped)
+  LimbMap pm = LimbMap::ext(limbs, c.K, c.L);
+  pm.skip_q = 1;
+  ntt_inverse(c, acc, 2 * E, pm, st, c.d_down_scale_a, c.d_down_scale_b, c.L);
   uint64_t* conv = (uint64_t*)c.alloc(sizeof(uint64_t) * 2 * (size_t)limbs * N);
-  const dim3 g1((N + kThreads - 1) / kThreads, 2);
-  ProfScope ps1(c, "moddown_conv", (2.0 * c.K + 2.0 * limbs) * c.limb_bytes(), st);
-  moddown_conv_kernel<<<g1, kThreads, 0, st>>>(acc, conv, limbs, c.L, c.K, c.logN, c.d_mods, c.d_phatinv,
-                                               lt.d_down_phat);
+  const int nchunks = (limbs + kTargets - 1) / kTargets;
+  const dim3 g1((N / 2 + kThreads - 1) / kThreads, 2 * nchunks);
+  {
+    ProfScope ps1(c, "moddown_conv", (2.0 * c.K + 2.0 * limbs) * c.limb_bytes(), st);
+    auto kern = c.K <= 4 ? moddown_conv_kernel<4>
+                : c.K <= 8 ? moddown_conv_kernel<8>
+                : c.K <= 12 ? moddown_conv_kernel<12>
+                            : moddown_conv_kernel<16>;
+    kern<<<g1, kThreads, 0, st>>>(acc, conv, limbs, c.L, c.K, c.logN, nchunks, c.d_mods, lt.d_down_phat);
+  }
   CKKS_CUDA(cudaGetLastError());
   ntt_forward(c, conv, 2 * limbs, LimbMap::q(limbs, c.L), st);
   const dim3 g2((N + kThreads - 1) / kThreads, 2 * limbs);
-  ProfScope ps2(c, "moddown_combine", ((add0 ? 1.0 : 0.0) + (add1 ? 1.0 : 0.0) + 6.0) * limbs * c.limb_bytes(), st);
-  moddown_combine_kernel<<<g2, kThreads, 0, st>>>(acc, conv, add0, g_add0, add1, out0, out1, limbs, c.K, c.logN, c.d_mods,
-                                                  lt.d_down_pinv);
+  {
+    ProfScope ps2(c, "moddown_combine", ((add0 ? 1.0 : 0.0) + (add1 ? 1.0 : 0.0) + 6.0) * limbs * c.limb_bytes(),
+                  st);
+    moddown_combine_kernel<<<g2, kThreads, 0, st>>>(acc, conv, add0, g_add0, add1, out0, out1, limbs, c.K, c.logN,
+                                                    c.d_mods, lt.d_down_pinv);
+  }
   CKKS_CUDA(cudaGetLastError());
   c.release(conv);
 }
@@ -250,12 +287,17 @@ void rescale(const Context& c, const uint64_t* x, size_t sx, int npolys, int lim
   ntt_inverse(c, last, npolys, LimbMap::single(lo), st);
   uint64_t* tmp = (uint64_t*)c.alloc(sizeof(uint64_t) * (size_t)npolys * lo * N);
   const dim3 g1((N + kThreads - 1) / kThreads, npolys * lo);
-  ProfScope ps1(c, "rescale_spread", (1.0 + lo) * npolys * c.limb_bytes(), st);
-  rescale_spread_kernel<<<g1, kThreads, 0, st>>>(last, tmp, limbs, c.logN, c.d_mods);
+  {
+    ProfScope ps1(c, "rescale_spread", (1.0 + lo) * npolys * c.limb_bytes(), st);
+    rescale_spread_kernel<<<g1, kThreads, 0, st>>>(last, tmp, limbs, c.logN, c.d_mods);
+  }
   CKKS_CUDA(cudaGetLastError());
   ntt_forward(c, tmp, npolys * lo, LimbMap::q(lo, c.L), st);
-  ProfScope ps2(c, "rescale_combine", 3.0 * npolys * lo * c.limb_bytes(), st);
-  rescale_combine_kernel<<<g1, kThreads, 0, st>>>(x, sx, tmp, out, so, limbs, c.logN, c.d_mods, lt.d_rescale_inv);
+  {
+    ProfScope ps2(c, "rescale_combine", 3.0 * npolys * lo * c.limb_bytes(), st);
+    rescale_combine_kernel<<<g1, kThreads, 0, st>>>(x, sx, tmp, out, so, limbs, c.logN, c.d_mods,
+                                                    lt.d_rescale_inv);
+  }
   CKKS_CUDA(cudaGetLastError());
   c.release(last);
   c.release(tmp);

@@ -32,28 +32,27 @@ __device__ __forceinline__ U128 mul_wide(uint64_t a, uint64_t b) {
 }
 
 __device__ __forceinline__ void add_wide(U128& acc, U128 x) {
-  uint64_t lo = acc.lo + x.lo;
-  acc.hi += x.hi + (lo < x.lo ? 1ull : 0ull);
-  acc.lo = lo;
+  asm("add.cc.u64 %0, %0, %2;\n\taddc.u64 %1, %1, %3;" : "+l"(acc.lo), "+l"(acc.hi) : "l"(x.lo), "l"(x.hi));
 }
 
-// acc += a*b (128-bit)
+// acc += a*b (128-bit) as one carry chain: mad.lo.cc + madc.hi
 __device__ __forceinline__ void mac_wide(U128& acc, uint64_t a, uint64_t b) {
-  add_wide(acc, mul_wide(a, b));
+  asm("mad.lo.cc.u64 %0, %2, %3, %0;\n\tmadc.hi.u64 %1, %2, %3, %1;"
+      : "+l"(acc.lo), "+l"(acc.hi)
+      : "l"(a), "l"(b));
 }
 
 __device__ __forceinline__ uint64_t reduce128(U128 x, const Mod& m) {
   const uint64_t carry = __umul64hi(x.lo, m.r0);
-  // a = x.lo * r1 + carry
-  uint64_t a_lo = x.lo * m.r1;
-  uint64_t a_hi = __umul64hi(x.lo, m.r1);
-  a_lo += carry;
-  a_hi += (a_lo < carry) ? 1ull : 0ull;
-  // b = x.hi * r0 + a_lo
-  uint64_t b_lo = x.hi * m.r0;
-  uint64_t b_hi = __umul64hi(x.hi, m.r0);
-  b_lo += a_lo;
-  b_hi += (b_lo < a_lo) ? 1ull : 0ull;
+  // a = x.lo * r1 + carry ; b = x.hi * r0 + lo(a) ; qe = x.hi * r1 + hi(a) + hi(b)
+  uint64_t a_lo, a_hi, b_lo, b_hi;
+  asm("mad.lo.cc.u64 %0, %2, %3, %4;\n\tmadc.hi.u64 %1, %2, %3, 0;"
+      : "=l"(a_lo), "=l"(a_hi)
+      : "l"(x.lo), "l"(m.r1), "l"(carry));
+  asm("mad.lo.cc.u64 %0, %2, %3, %4;\n\tmadc.hi.u64 %1, %2, %3, 0;"
+      : "=l"(b_lo), "=l"(b_hi)
+      : "l"(x.hi), "l"(m.r0), "l"(a_lo));
+  (void)b_lo;
   const uint64_t qe = x.hi * m.r1 + a_hi + b_hi;
   uint64_t r = x.lo - qe * m.q;
   return r >= m.q ? r - m.q : r;

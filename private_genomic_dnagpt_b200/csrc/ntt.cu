@@ -30,6 +30,11 @@ struct PassArgs {
   const Mod* mods;
   const ulonglong2* ninv_last;  // [P] (n^-1, shoup) ; inverse only
   const ulonglong2* w1_ninv;    // [P] (Winv[1] * n^-1, shoup) ; inverse only
+  // optional per-batch-limb replacements of (n^-1, Winv[1] n^-1): the inverse
+  // transform then returns x * c_l for a constant c_l folded into its last stage
+  const ulonglong2* scale_a;
+  const ulonglong2* scale_b;
+  int scale_base;
   LimbMap map;
   int logN;
   int per_cta;  // columns (strided) or blocks (contiguous) per CTA
@@ -38,6 +43,24 @@ struct PassArgs {
 __device__ __forceinline__ int group_size(int s_log, int gi) {
   const int rem = s_log - 3 * gi;
   return rem < 3 ? rem : 3;
+}
+
+// Harvey butterflies.  Forward (Cooley-Tukey): values in [0, 4q);
+// inverse (Gentleman-Sande): values in [0, 2q).  The last pass returns
+// canonical residues in [0, q).
+__device__ __forceinline__ void ct_bfly(uint64_t& x, uint64_t& y, ulonglong2 w, uint64_t q, uint64_t q2) {
+  uint64_t a = x >= q2 ? x - q2 : x;
+  const uint64_t t = mul_shoup_lazy(y, w.x, w.y, q);
+  x = a + t;
+  y = a + q2 - t;
+}
+
+__device__ __forceinline__ void gs_bfly(uint64_t& x, uint64_t& y, ulonglong2 w, uint64_t q, uint64_t q2) {
+  uint64_t s = x + y;
+  s = s >= q2 ? s - q2 : s;
+  const uint64_t d = x + q2 - y;
+  x = s;
+  y = mul_shoup_lazy(d, w.x, w.y, q);
 }
 
 template <int S_LOG, bool INV, bool STRIDED>
@@ -52,8 +75,8 @@ __global__ void __launch_bounds__(kThreads) ntt_pass_kernel(uint64_t* __restrict
   if (a.map.skipped(limb)) return;
   const int N = 1 << a.logN;
   uint64_t* poly = data + (size_t)limb * N;
-  const Mod md = a.mods[prime];
-  const uint64_t q = md.q;
+  const uint64_t q = a.mods[prime].q;
+  const uint64_t q2 = 2 * q;
   const ulonglong2* tw = a.tw + (size_t)prime * N;
 
   const int tid = threadIdx.x;
@@ -68,9 +91,12 @@ __global__ void __launch_bounds__(kThreads) ntt_pass_kernel(uint64_t* __restrict
   }
   const int sub_global = blockIdx.x * per + lane_idx;  // column or block index
   const int stride = N >> S_LOG;                         // strided: distance between rows
-  // twiddle prefix: global stage offset and block index for contiguous passes
   const int gs0 = STRIDED ? 0 : (a.logN - S_LOG);
   const uint32_t prefix = STRIDED ? 0u : (uint32_t)sub_global;
+  // the strided pass holds the first stages (forward) / the last stages
+  // (inverse); the contiguous pass the others
+  const bool first_pass = (STRIDED != INV);
+  const bool last_pass = !first_pass;
 
   auto gaddr = [&](int r) -> size_t {
     return STRIDED ? (size_t)r * stride + sub_global : (size_t)sub_global * S + r;
@@ -81,17 +107,12 @@ __global__ void __launch_bounds__(kThreads) ntt_pass_kernel(uint64_t* __restrict
 
   uint64_t x[8];
 
-  auto tw_index = [&](int st, int r) -> uint32_t {
-    return (1u << (gs0 + st)) + (prefix << st) + ((uint32_t)r >> (S_LOG - st));
-  };
-
-  // process stage group gi on registers; `first`/`last` select global I/O
 #pragma unroll
   for (int step = 0; step < NG; ++step) {
     const int gi = INV ? (NG - 1 - step) : step;
     const int G = group_size(S_LOG, gi);
     const int st0 = 3 * gi;
-    const int D = S >> (st0 + G);  // smallest distance (unit stride)
+    const int D = S >> (st0 + G);  // smallest distance inside a unit
     const int units_per_thread = 8 >> G;
     const int usz = 1 << G;
     // load
@@ -100,61 +121,47 @@ __global__ void __launch_bounds__(kThreads) ntt_pass_kernel(uint64_t* __restrict
       if (j >= units_per_thread * usz) break;
       const int uj = j / usz, k = j % usz;
       const int u = sub_t + uj * T;
-      const int base = (u / D) * (D << G) + (u % D);
-      const int r = base + k * D;
-      if (step == 0)
-        x[j] = poly[gaddr(r)];
-      else
-        x[j] = sm[saddr(r)];
+      const int r = (u / D) * (D << G) + (u % D) + k * D;
+      x[j] = (step == 0) ? poly[gaddr(r)] : sm[saddr(r)];
     }
-    // butterflies
+    // butterflies; the twiddle of pair (k, k+h) at stage st0+rr is
+    // tw[2^(gs0+st) + prefix*2^st + B*2^rr + (k >> (G-rr))], B = u / D
 #pragma unroll
     for (int uj = 0; uj < 8; ++uj) {
       if (uj >= units_per_thread) break;
       const int u = sub_t + uj * T;
-      const int base = (u / D) * (D << G) + (u % D);
+      const uint32_t B = (uint32_t)(u / D);
       uint64_t* xu = x + uj * usz;
-      if (!INV) {
 #pragma unroll
-        for (int rr = 0; rr < 3; ++rr) {
-          if (rr >= G) break;
-          const int st = st0 + rr;
-          const int h = 1 << (G - 1 - rr);
+      for (int it = 0; it < 3; ++it) {
+        const int rr = INV ? (G - 1 - it) : it;
+        if (rr < 0 || it >= G) break;
+        const int st = st0 + rr;
+        const int h = 1 << (G - 1 - rr);
+        const bool final_stage = INV && STRIDED && st == 0;
+        const uint32_t idx0 = (1u << (gs0 + st)) + (prefix << st) + (B << rr);
+        ulonglong2 w[4];
+        if (!final_stage) {
 #pragma unroll
-          for (int k = 0; k < 8; ++k) {
-            if (k >= usz) break;
-            if (k & h) continue;
-            const int r = base + k * D;
-            const ulonglong2 w = __ldg(tw + tw_index(st, r));
-            const uint64_t u0 = xu[k];
-            const uint64_t v0 = mul_shoup(xu[k + h], w.x, w.y, q);
-            xu[k] = add_mod(u0, v0, q);
-            xu[k + h] = sub_mod(u0, v0, q);
-          }
+          for (int j = 0; j < 4; ++j)
+            if (j < (1 << rr)) w[j] = __ldg(tw + idx0 + j);
         }
-      } else {
 #pragma unroll
-        for (int rr = 2; rr >= 0; --rr) {
-          if (rr >= G) continue;
-          const int st = st0 + rr;
-          const int h = 1 << (G - 1 - rr);
-          const bool final_stage = STRIDED && st == 0;
-#pragma unroll
-          for (int k = 0; k < 8; ++k) {
-            if (k >= usz) break;
-            if (k & h) continue;
-            const int r = base + k * D;
+        for (int k = 0; k < 8; ++k) {
+          if (k >= usz) break;
+          if (k & h) continue;
+          if (!INV) {
+            ct_bfly(xu[k], xu[k + h], w[k >> (G - rr)], q, q2);
+          } else if (!final_stage) {
+            gs_bfly(xu[k], xu[k + h], w[k >> (G - rr)], q, q2);
+          } else {
+            const ulonglong2 c0 = a.scale_a ? __ldg(a.scale_a + (prime - a.scale_base)) : __ldg(a.ninv_last + prime);
+            const ulonglong2 c1 = a.scale_b ? __ldg(a.scale_b + (prime - a.scale_base)) : __ldg(a.w1_ninv + prime);
             const uint64_t u0 = xu[k], v0 = xu[k + h];
-            if (final_stage) {
-              const ulonglong2 ni = __ldg(a.ninv_last + prime);
-              const ulonglong2 wn = __ldg(a.w1_ninv + prime);
-              xu[k] = mul_shoup(add_mod(u0, v0, q), ni.x, ni.y, q);
-              xu[k + h] = mul_shoup(sub_mod(u0, v0, q), wn.x, wn.y, q);
-            } else {
-              const ulonglong2 w = __ldg(tw + tw_index(st, r));
-              xu[k] = add_mod(u0, v0, q);
-              xu[k + h] = mul_shoup(sub_mod(u0, v0, q), w.x, w.y, q);
-            }
+            const uint64_t s0 = mul_shoup_lazy(u0 + v0, c0.x, c0.y, q);
+            const uint64_t d0 = mul_shoup_lazy(u0 + q2 - v0, c1.x, c1.y, q);
+            xu[k] = s0 >= q ? s0 - q : s0;
+            xu[k + h] = d0 >= q ? d0 - q : d0;
           }
         }
       }
@@ -167,8 +174,7 @@ __global__ void __launch_bounds__(kThreads) ntt_pass_kernel(uint64_t* __restrict
         if (j >= units_per_thread * usz) break;
         const int uj = j / usz, k = j % usz;
         const int u = sub_t + uj * T;
-        const int base = (u / D) * (D << G) + (u % D);
-        sm[saddr(base + k * D)] = x[j];
+        sm[saddr((u / D) * (D << G) + (u % D) + k * D)] = x[j];
       }
       __syncthreads();
     } else {
@@ -177,8 +183,13 @@ __global__ void __launch_bounds__(kThreads) ntt_pass_kernel(uint64_t* __restrict
         if (j >= units_per_thread * usz) break;
         const int uj = j / usz, k = j % usz;
         const int u = sub_t + uj * T;
-        const int base = (u / D) * (D << G) + (u % D);
-        poly[gaddr(base + k * D)] = x[j];
+        uint64_t v = x[j];
+        if (last_pass && !INV) {  // forward output: [0, 4q) -> [0, q)
+          v = v >= q2 ? v - q2 : v;
+          v = v >= q ? v - q : v;
+        }
+        // inverse output of the final stage is already canonical
+        poly[gaddr((u / D) * (D << G) + (u % D) + k * D)] = v;
       }
     }
   }
@@ -248,7 +259,8 @@ void ntt_forward(const Context& c, uint64_t* data, int nlimbs, LimbMap map, cuda
   CKKS_CUDA(cudaGetLastError());
 }
 
-void ntt_inverse(const Context& c, uint64_t* data, int nlimbs, LimbMap map, cudaStream_t st) {
+void ntt_inverse(const Context& c, uint64_t* data, int nlimbs, LimbMap map, cudaStream_t st,
+                 const ulonglong2* scale_a, const ulonglong2* scale_b, int scale_base) {
   if (nlimbs <= 0) return;
   const double bytes = live_limbs(map, nlimbs) * c.limb_bytes();
   PassArgs a{};
@@ -256,6 +268,9 @@ void ntt_inverse(const Context& c, uint64_t* data, int nlimbs, LimbMap map, cuda
   a.mods = c.d_mods;
   a.ninv_last = c.d_ninv;
   a.w1_ninv = c.d_w1ninv;
+  a.scale_a = scale_a;
+  a.scale_b = scale_b;
+  a.scale_base = scale_base;
   a.map = map;
   a.logN = c.logN;
   const int s1 = c.logN / 2, s2 = c.logN - s1;

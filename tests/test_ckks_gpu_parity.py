@@ -245,3 +245,21 @@ def test_full_size_rotation_bit_exact():
     assert np.array_equal(got.limbs_array(), o.rotate(ref, 8))
     dec = cc.Decrypt(got).GetRealPackedValue()
     assert np.abs(dec - np.roll(x, -8)).max() < 1e-6
+
+
+def test_profiler_reports_every_rotation_kernel(pair10):
+    o, cc = pair10
+    x, rx, cx = _fresh(o, cc, 12, o.L)
+    cc.profile(True)
+    cc.profile_reset()
+    for _ in range(3):
+        cc.EvalRotate(cx, 1)
+    rep = cc.profile_report()
+    cc.profile(False)
+    for k in ("ntt_fwd_rows", "ntt_fwd_cols", "ntt_inv_cols", "ntt_inv_rows", "modup_conv", "ks_inner",
+              "moddown_conv", "moddown_combine"):
+        assert rep[k]["launches"] >= 3 and rep[k]["ms"] > 0 and rep[k]["bytes"] > 0
+    assert rep["ks_inner"]["launches"] == 3
+    # operations keep working after the profiler is switched off
+    got = cc.EvalRotate(cx, 2)
+    assert np.array_equal(got.limbs_array(), o.rotate(rx, 2))
