@@ -212,7 +212,9 @@ void modup(const Context& c, const uint64_t* d_ntt, int limbs, uint64_t* ext, cu
   uint64_t* dc = (uint64_t*)c.alloc(sizeof(uint64_t) * (size_t)limbs * N);
   CKKS_CUDA(cudaMemcpyAsync(dc, d_ntt, sizeof(uint64_t) * (size_t)limbs * N, cudaMemcpyDeviceToDevice, st));
   ntt_inverse(c, dc, limbs, LimbMap::q(limbs, c.L), st, lt.d_up_scale_a, lt.d_up_scale_b);
-  const int nchunks = (E - std::min(c.alpha, limbs) + kTargets - 1) / kTargets;
+  // the last digit may hold fewer than alpha limbs and so has the most targets
+  const int min_cnt = limbs - (lt.beta - 1) * c.alpha;
+  const int nchunks = (E - min_cnt + kTargets - 1) / kTargets;
   const dim3 grid((N / 2 + kThreads - 1) / kThreads, lt.beta * nchunks);
   {
     // reads the input limbs (coefficient form for the sources, NTT form for

@@ -232,6 +232,20 @@ def test_flexibleauto_chain_accuracy(pair10):
     assert np.abs(got - (x * y + x) * y).max() < 1e-6
 
 
+@pytest.mark.parametrize("logN,L,dnum", [(12, 8, 3), (11, 7, 2), (11, 10, 4)])
+def test_partial_last_digit_keyswitch_bit_exact(logN, L, dnum):
+    """Digit sizes that do not divide the limb count (last digit shorter)."""
+    o, cc = make_pair(logN, L, dnum, 9, rot=[1, -2], relin=True)
+    for limbs in (L, L - 1, 2):
+        x, rx, cx = _fresh(o, cc, 13, limbs)
+        assert np.array_equal(cc.EvalRotate(cx, 1).limbs_array(), o.rotate(rx, 1))
+        assert np.array_equal(cc.EvalRotate(cx, -2).limbs_array(), o.rotate(rx, -2))
+        y, ry, cy = _fresh(o, cc, 14, limbs)
+        assert np.array_equal(cc.mul_ct(cx, cy).limbs_array(), o.mul_ct(rx, ry))
+        dec = cc.Decrypt(cc.EvalRotate(cx, 1)).GetRealPackedValue()
+        assert np.abs(dec - np.roll(x, -1)).max() < 1e-7
+
+
 def test_full_size_rotation_bit_exact():
     """N = 2^16, 24 limbs, dnum 3 (the block configuration)."""
     o, cc = make_pair(16, 24, 3, 5, rot=[1, 8], relin=False)
