@@ -162,6 +162,17 @@ int ckks_profile_report(ckks_ctx* ctx, char* buf, size_t size);
 int ckks_ntt_forward_device(ckks_ctx* ctx, uint64_t* data, int nlimbs, int first_prime);
 int ckks_ntt_inverse_device(ckks_ctx* ctx, uint64_t* data, int nlimbs, int first_prime);
 
+/* EvalRotate for callers that cannot allocate device memory (graph
+ * capture, allocation-free request paths, fixed memory budgets).  No
+ * counterpart in the reference: it has no allocation-free entry point.
+ * in_dev / out_dev: device buffers of 2*limbs*N words (c0 limbs then c1
+ * limbs, NTT form), not overlapping.  Key-switching temporaries come from one
+ * 128 MiB array compiled into the library (held by every GPU that loads it);
+ * larger requests fail with CKKS_ECAPACITY.  No cudaMalloc/cudaFree.  The
+ * first call on a device looks up the array's address (make it before any
+ * stream capture); calls that overlap on the GPU race on the shared array. */
+int ckks_rotate_noalloc(ckks_ctx* ctx, const uint64_t* in_dev, int limbs, int k, uint64_t* out_dev);
+
 #ifdef __cplusplus
 }
 #endif

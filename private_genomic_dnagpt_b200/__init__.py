@@ -113,6 +113,7 @@ _SIGS = [
     ("ckks_profile_reset", ctypes.c_int, [_vp]),
     ("ckks_profile_report", ctypes.c_int, [_vp, ctypes.c_char_p, ctypes.c_size_t]),
     ("ckks_ntt_forward_device", ctypes.c_int, [_vp, _vp, ctypes.c_int, ctypes.c_int]),
+    ("ckks_rotate_noalloc", ctypes.c_int, [_vp, _vp, ctypes.c_int, ctypes.c_int, _vp]),
     ("ckks_ntt_inverse_device", ctypes.c_int, [_vp, _vp, ctypes.c_int, ctypes.c_int]),
 ]
 

@@ -7,23 +7,13 @@
 #include <utility>
 
 #include "../../include/ckks_b200.h"
+#include "capi_types.hpp"
 #include "ckks_internal.hpp"
 
 using ckks::Context;
 using ckks::DevPoly;
 using ckks::Error;
 
-struct ckks_ctx {
-  std::unique_ptr<Context> c;
-};
-struct ckks_ct {
-  ckks_ctx* owner = nullptr;
-  DevPoly p;
-};
-struct ckks_pt {
-  ckks_ctx* owner = nullptr;
-  DevPoly p;
-};
 
 namespace {
 
@@ -148,6 +138,8 @@ void rotate_many(Context& c, const ckks_ct* a, const int* ks, int n, ckks_ct* co
 }
 
 }  // namespace
+
+void ckks::set_last_error(const std::string& msg) { g_error = msg; }
 
 extern "C" {
 

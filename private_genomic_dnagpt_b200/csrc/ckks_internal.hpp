@@ -234,6 +234,10 @@ void ks_inner(const Context& c, const uint64_t* ext, int limbs, const uint64_t* 
 // when given; acc holds 2 polys of limbs+K limbs and is consumed
 void moddown2(const Context& c, uint64_t* acc, int limbs, const uint64_t* add0, uint32_t g_add0,
               const uint64_t* add1, uint64_t* out0, uint64_t* out1, cudaStream_t st);
+// the same with caller-provided scratch: dc holds limbs*N words, conv 2*limbs*N
+void modup_with(const Context& c, const uint64_t* d_ntt, int limbs, uint64_t* ext, uint64_t* dc, cudaStream_t st);
+void moddown2_with(const Context& c, uint64_t* acc, int limbs, const uint64_t* add0, uint32_t g_add0,
+                   const uint64_t* add1, uint64_t* out0, uint64_t* out1, uint64_t* conv, cudaStream_t st);
 void automorphism(const Context& c, const uint64_t* a, uint64_t* o, int nlimbs, uint32_t g, cudaStream_t st);
 // rescale npolys polynomials (stride in words) of `limbs` limbs to limbs-1
 void rescale(const Context& c, const uint64_t* x, size_t sx, int npolys, int limbs, uint64_t* out, size_t so,

@@ -305,4 +305,62 @@ void rescale(const Context& c, const uint64_t* x, size_t sx, int npolys, int lim
   c.release(tmp);
 }
 
+// ModUp / ModDown with caller-provided scratch (limbs*N words for ModUp's
+// transformed copy of d, 2*limbs*N words for ModDown's conversion output);
+// same kernels and order as modup() / moddown2(), no allocation.
+void modup_with(const Context& c, const uint64_t* d_ntt, int limbs, uint64_t* ext, uint64_t* dc, cudaStream_t st) {
+  if (c.alpha > kMaxAlpha) throw Error(kErrArgument, "alpha above 16 is not supported");
+  const int N = c.N, E = limbs + c.K;
+  const LevelTables& lt = c.levels[limbs];
+  CKKS_CUDA(cudaMemcpyAsync(dc, d_ntt, sizeof(uint64_t) * (size_t)limbs * N, cudaMemcpyDeviceToDevice, st));
+  ntt_inverse(c, dc, limbs, LimbMap::q(limbs, c.L), st, lt.d_up_scale_a, lt.d_up_scale_b);
+  // the last digit may hold fewer than alpha limbs and so has the most targets
+  const int min_cnt = limbs - (lt.beta - 1) * c.alpha;
+  const int nchunks = (E - min_cnt + kTargets - 1) / kTargets;
+  const dim3 grid((N / 2 + kThreads - 1) / kThreads, lt.beta * nchunks);
+  {
+    ProfScope ps(c, "modup_conv", (2.0 * limbs + (double)lt.beta * E) * c.limb_bytes(), st);
+    auto kern = c.alpha <= 4 ? modup_conv_kernel<4>
+                : c.alpha <= 8 ? modup_conv_kernel<8>
+                : c.alpha <= 12 ? modup_conv_kernel<12>
+                                : modup_conv_kernel<16>;
+    kern<<<grid, kThreads, 0, st>>>(dc, d_ntt, ext, limbs, c.L, c.K, c.alpha, c.logN, nchunks, c.d_mods,
+                                    lt.d_up_hat);
+  }
+  CKKS_CUDA(cudaGetLastError());
+  LimbMap m = LimbMap::ext(limbs, c.K, c.L);
+  m.skip_alpha = c.alpha;
+  ntt_forward(c, ext, lt.beta * E, m, st);
+}
+
+void moddown2_with(const Context& c, uint64_t* acc, int limbs, const uint64_t* add0, uint32_t g_add0,
+                   const uint64_t* add1, uint64_t* out0, uint64_t* out1, uint64_t* conv, cudaStream_t st) {
+  if (c.K > kMaxK) throw Error(kErrArgument, "more than 16 special primes is not supported");
+  const int N = c.N, E = limbs + c.K;
+  const LevelTables& lt = c.levels[limbs];
+  LimbMap pm = LimbMap::ext(limbs, c.K, c.L);
+  pm.skip_q = 1;
+  ntt_inverse(c, acc, 2 * E, pm, st, c.d_down_scale_a, c.d_down_scale_b, c.L);
+  const int nchunks = (limbs + kTargets - 1) / kTargets;
+  const dim3 g1((N / 2 + kThreads - 1) / kThreads, 2 * nchunks);
+  {
+    ProfScope ps1(c, "moddown_conv", (2.0 * c.K + 2.0 * limbs) * c.limb_bytes(), st);
+    auto kern = c.K <= 4 ? moddown_conv_kernel<4>
+                : c.K <= 8 ? moddown_conv_kernel<8>
+                : c.K <= 12 ? moddown_conv_kernel<12>
+                            : moddown_conv_kernel<16>;
+    kern<<<g1, kThreads, 0, st>>>(acc, conv, limbs, c.L, c.K, c.logN, nchunks, c.d_mods, lt.d_down_phat);
+  }
+  CKKS_CUDA(cudaGetLastError());
+  ntt_forward(c, conv, 2 * limbs, LimbMap::q(limbs, c.L), st);
+  const dim3 g2((N + kThreads - 1) / kThreads, 2 * limbs);
+  {
+    ProfScope ps2(c, "moddown_combine", ((add0 ? 1.0 : 0.0) + (add1 ? 1.0 : 0.0) + 6.0) * limbs * c.limb_bytes(),
+                  st);
+    moddown_combine_kernel<<<g2, kThreads, 0, st>>>(acc, conv, add0, g_add0, add1, out0, out1, limbs, c.K, c.logN,
+                                                    c.d_mods, lt.d_down_pinv);
+  }
+  CKKS_CUDA(cudaGetLastError());
+}
+
 }  // namespace ckks
