@@ -162,6 +162,32 @@ int ckks_profile_report(ckks_ctx* ctx, char* buf, size_t size);
 int ckks_ntt_forward_device(ckks_ctx* ctx, uint64_t* data, int nlimbs, int first_prime);
 int ckks_ntt_inverse_device(ckks_ctx* ctx, uint64_t* data, int nlimbs, int first_prime);
 
+/* ---- encrypted transformer block (the reference's EncryptedEvaluator and
+ * Client, T123.cpp:509-948) ------------------------------------------------
+ * Weights are float64 in PyTorch [out, in] layout, as the reference fixture
+ * stores them (ln1/ln2 gains [D], attn_qkv [3D, D], attn_proj [D, D],
+ * mlp_fc [MLP, D], mlp_proj [D, MLP]; bias-free, fhe/realweights/manual.py).
+ * Tokens are packed 32 per ciphertext, lane-innermost. */
+typedef struct ckks_block ckks_block;
+int ckks_block_create(ckks_ctx* ctx, const double* ln1, const double* attn_qkv, const double* attn_proj,
+                      const double* ln2, const double* mlp_fc, const double* mlp_proj, int d_model, int heads,
+                      int mlp_dim, int tokens, ckks_block** out);
+int ckks_block_destroy(ckks_block* b);
+/* rotation indices the block needs (required_rotation_keys, T123.cpp:455-481);
+ * returns the count, writes up to cap */
+int ckks_block_rotation_indices(const ckks_block* b, int* out, int cap);
+/* client encrypt -> server block evaluation with client refreshes -> client
+ * decrypt; x and y are [tokens, d_model] float64 (T123.cpp:1642-1694) */
+int ckks_block_forward(ckks_block* b, const double* x, int tokens, double* y);
+/* operation counts and stage seconds of the last forward, JSON text */
+int ckks_block_report(const ckks_block* b, char* buf, size_t size);
+/* host-only schedule helpers: causal lane shifts of a (query group, key
+ * group) tile (simd_layout.py:386-406) and one BSGS diagonal as slot values
+ * (T123.cpp:1018-1046) */
+int ckks_schedule_active_shifts(int tokens, int batch, int qg, int kg, int* out, int cap);
+int ckks_schedule_diagonal(const double* W, int out_dim, int in_dim, int ld, int pack_width, int batch, int n1, int g,
+                           int j, double* out_slots);
+
 /* EvalRotate for callers that cannot allocate device memory (graph
  * capture, allocation-free request paths, fixed memory budgets).  No
  * counterpart in the reference: it has no allocation-free entry point.

@@ -103,7 +103,13 @@ class CryptoContextImpl {
     check(ckks_ctx_create(&q, &h_));
     check(ckks_ctx_info(h_, &n_, &limbs_, &special_, &alpha_));
   }
-  ~CryptoContextImpl() { ckks_ctx_destroy(h_); }
+  // non-owning view of an existing context
+  explicit CryptoContextImpl(ckks_ctx* existing) : h_(existing), owns_(false) {
+    check(ckks_ctx_info(h_, &n_, &limbs_, &special_, &alpha_));
+  }
+  ~CryptoContextImpl() {
+    if (owns_) ckks_ctx_destroy(h_);
+  }
   CryptoContextImpl(const CryptoContextImpl&) = delete;
   CryptoContextImpl& operator=(const CryptoContextImpl&) = delete;
 
@@ -128,6 +134,7 @@ class CryptoContextImpl {
     check(ckks_encode_at(h_, v.data(), (int)v.size(), limbs, scale, pt->handle()));
     return pt;
   }
+  Ciphertext fresh() { return std::make_shared<CiphertextImpl>(h_); }
   Ciphertext Encrypt(const Plaintext& pt) {
     auto ct = fresh();
     check(ckks_encrypt(h_, pt->handle(), ct->handle()));
@@ -219,7 +226,6 @@ class CryptoContextImpl {
   }
 
  private:
-  Ciphertext fresh() { return std::make_shared<CiphertextImpl>(h_); }
   Ciphertext deg1(const Ciphertext& a) { return a->noise_deg() >= 2 ? Rescale(a) : a; }
   std::pair<Ciphertext, Ciphertext> align(Ciphertext a, Ciphertext b) {
     if (a->noise_deg() != b->noise_deg()) {
@@ -237,6 +243,7 @@ class CryptoContextImpl {
   }
 
   ckks_ctx* h_ = nullptr;
+  bool owns_ = true;
   int n_ = 0, limbs_ = 0, special_ = 0, alpha_ = 0;
 };
 

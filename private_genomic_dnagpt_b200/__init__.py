@@ -114,6 +114,13 @@ _SIGS = [
     ("ckks_profile_report", ctypes.c_int, [_vp, ctypes.c_char_p, ctypes.c_size_t]),
     ("ckks_ntt_forward_device", ctypes.c_int, [_vp, _vp, ctypes.c_int, ctypes.c_int]),
     ("ckks_rotate_noalloc", ctypes.c_int, [_vp, _vp, ctypes.c_int, ctypes.c_int, _vp]),
+    ("ckks_block_create", ctypes.c_int, [_vp] + [_f64p] * 6 + [ctypes.c_int] * 4 + [ctypes.POINTER(_vp)]),
+    ("ckks_block_destroy", ctypes.c_int, [_vp]),
+    ("ckks_block_rotation_indices", ctypes.c_int, [_vp, ctypes.POINTER(ctypes.c_int), ctypes.c_int]),
+    ("ckks_block_forward", ctypes.c_int, [_vp, _f64p, ctypes.c_int, _f64p]),
+    ("ckks_block_report", ctypes.c_int, [_vp, ctypes.c_char_p, ctypes.c_size_t]),
+    ("ckks_schedule_active_shifts", ctypes.c_int, [ctypes.c_int] * 4 + [ctypes.POINTER(ctypes.c_int), ctypes.c_int]),
+    ("ckks_schedule_diagonal", ctypes.c_int, [_f64p] + [ctypes.c_int] * 8 + [_f64p]),
     ("ckks_ntt_inverse_device", ctypes.c_int, [_vp, _vp, ctypes.c_int, ctypes.c_int]),
 ]
 
@@ -444,3 +451,72 @@ class CryptoContext:
 
 def GenCryptoContext(params: CCParams) -> CryptoContext:
     return CryptoContext(params)
+
+
+def _f64(a: np.ndarray):
+    assert a.dtype == np.float64 and a.flags["C_CONTIGUOUS"]
+    return a.ctypes.data_as(_f64p)
+
+
+class EncryptedBlock:
+    """One encrypted DNAGPT block (EncryptedEvaluator + Client of the
+    reference driver) bound to a context.  ``forward(x)`` encrypts x
+    ([tokens, D] float64), evaluates the block with client refreshes and
+    returns the decrypted output."""
+
+    def __init__(self, cc: CryptoContext, weights: dict, tokens: int, heads: int = 12):
+        self.cc = cc
+        self._w = {k: np.ascontiguousarray(weights[k], np.float64) for k in
+                   ("ln1", "attn_qkv", "attn_proj", "ln2", "mlp_fc", "mlp_proj")}
+        D = self._w["ln1"].shape[0]
+        M = self._w["mlp_fc"].shape[0]
+        self.D, self.tokens = D, tokens
+        h = _vp()
+        _check(lib().ckks_block_create(cc.h, _f64(self._w["ln1"]), _f64(self._w["attn_qkv"]),
+                                       _f64(self._w["attn_proj"]), _f64(self._w["ln2"]), _f64(self._w["mlp_fc"]),
+                                       _f64(self._w["mlp_proj"]), D, heads, M, tokens, ctypes.byref(h)))
+        self.h = h
+
+    def __del__(self):
+        try:
+            if self.h:
+                lib().ckks_block_destroy(self.h)
+                self.h = None
+        except Exception:
+            pass
+
+    def rotation_indices(self) -> list[int]:
+        n = lib().ckks_block_rotation_indices(self.h, None, 0)
+        buf = (ctypes.c_int * n)()
+        lib().ckks_block_rotation_indices(self.h, buf, n)
+        return list(buf)
+
+    def forward(self, x: np.ndarray) -> np.ndarray:
+        x = np.ascontiguousarray(x, np.float64)
+        y = np.zeros_like(x)
+        _check(lib().ckks_block_forward(self.h, _f64(x), x.shape[0], _f64(y)))
+        return y
+
+    def report(self) -> dict:
+        import json
+        n = lib().ckks_block_report(self.h, None, 0)
+        buf = ctypes.create_string_buffer(n + 1)
+        lib().ckks_block_report(self.h, buf, n + 1)
+        return json.loads(buf.value.decode())
+
+
+def schedule_active_shifts(tokens: int, batch: int, qg: int, kg: int) -> list[int]:
+    buf = (ctypes.c_int * batch)()
+    n = lib().ckks_schedule_active_shifts(tokens, batch, qg, kg, buf, batch)
+    if n < 0:
+        raise CKKSError(1, "bad tile")
+    return list(buf)[:n]
+
+
+def schedule_diagonal(W: np.ndarray, out_dim: int, in_dim: int, pack_width: int, batch: int, n1: int, g: int,
+                      j: int) -> np.ndarray:
+    W = np.ascontiguousarray(W, np.float64)
+    out = np.zeros(pack_width * batch, np.float64)
+    _check(lib().ckks_schedule_diagonal(_f64(W), out_dim, in_dim, W.shape[1], pack_width, batch, n1, g, j,
+                                        _f64(out)))
+    return out

@@ -1,0 +1,722 @@
+// block.cu -- one encrypted DNAGPT transformer block (pre-LN, bias-free) on
+// the engine: the server-side schedule of the reference's
+// EncryptedEvaluator::evaluate with its client refreshes
+// (fhe/gpu_real_scheme_b/src/real_dnagpt_fides_scheme_b_simd_full_t103_depth13_
+//  digits3_ring65536_cpudiagcache_t123.cpp, "T123.cpp", :762-948 and :509-715).
+//
+// Layout: B tokens per ciphertext, lane-innermost,
+//   slot(feature f, lane t) = f * B + t,  f < PW = N / (2B),
+// so a rotation by B*k moves every token's features by k without crossing
+// tokens (T123.cpp:419-426 with one copy; simd_layout.py:55-81).  With B = 32
+// the T = 103 tokens take 4 ciphertexts (32, 32, 32, 7).
+//
+// Per token group, in order (T123.cpp:780-923):
+//   LN1      AccumulateSum over features -> mean, centered, centered^2 ->
+//            AccumulateSum -> variance; the client returns 1/sqrt(var + eps);
+//            the LN gain is folded into the next weight matrix (x W^T with
+//            W' = W diag(gamma)).
+//   QKV      one hoisted baby-step set, three fused BSGS products (n1 = n2 = 32).
+//   scores   for every causal (query group, key group, lane shift delta):
+//            Q * lane_shift(K, delta), then a window sum over each head's 64
+//            features (rotations by B*2^i); the client reads score(q, k, head)
+//            at feature 64*head and runs the exact float64 softmax
+//            (T123.cpp:629-665).
+//   context  the client encrypts the weight tile of every alignment; the
+//            server accumulates tile * lane_shift(V, delta).
+//   O proj   BSGS; residual1 = x + O.
+//   LN2      as LN1.
+//   MLP      fc in PW-row chunks (BSGS each); the client applies exact
+//            tanh-GELU (T123.cpp:190-194); down projection per chunk; sum;
+//            block output = residual1 + MLP.
+// Fresh ciphertexts (inputs and client refreshes) are encrypted at the level
+// that leaves exactly the depth still needed plus two limbs at every
+// decryption, so the key switches run on 3..11 limbs of the 24-limb chain.
+#include <algorithm>
+#include <chrono>
+#include <cmath>
+#include <cstdio>
+#include <cstring>
+#include <map>
+#include <string>
+#include <vector>
+
+#include "../../include/ckks_b200.h"
+#include "../../include/ckks_b200.hpp"
+#include "capi_types.hpp"
+#include "ckks_internal.hpp"
+
+using ckks_b200::Ciphertext;
+using ckks_b200::Plaintext;
+
+namespace blk {
+
+constexpr int kThreads = 256;
+constexpr int kMaxBaby = 32;
+constexpr int kGiantsPerBlock = 8;
+
+struct Shape {
+  int T = 103, B = 32, D = 768, H = 12, HD = 64, MLP = 3072;
+  int PW = 1024, n1 = 32, n2 = 32, groups = 4;
+  int count(int g) const { return std::min(B, T - g * B); }
+};
+
+// lane shifts delta whose (query lane, key lane) pairs include a causal pair
+// (simd_layout.py:386-406, T123.cpp:483-507)
+std::vector<int> active_shifts(int T, int B, int qg, int kg) {
+  const int qs = qg * B, ks = kg * B;
+  const int qc = std::min(B, T - qs), kc = std::min(B, T - ks);
+  std::vector<int> out;
+  for (int d = 0; d < B; ++d) {
+    for (int ql = 0; ql < qc; ++ql) {
+      const int kl = (ql + d) % B;
+      if (kl < kc && ks + kl <= qs + ql) {
+        out.push_back(d);
+        break;
+      }
+    }
+  }
+  return out;
+}
+
+// value of BSGS diagonal (g, j) at `feature`, pre-rotated by the giant step:
+// W[rolled][(rolled + n1 g + j) mod PW] with rolled = (feature - n1 g) mod PW,
+// zero outside the matrix (T123.cpp:1018-1046, simd_layout.py:161-178)
+__host__ __device__ inline double diag_value(const double* W, int out_dim, int in_dim, int ld, int PW, int n1, int g,
+                                             int j, int feature) {
+  const int rolled = (feature + PW - (n1 * g) % PW) % PW;
+  const int col = (rolled + n1 * g + j) % PW;
+  return (rolled < out_dim && col < in_dim) ? W[(size_t)rolled * ld + col] : 0.0;
+}
+
+__global__ void __launch_bounds__(kThreads) diag_values_kernel(const double* __restrict__ W, int out_dim, int in_dim,
+                                                               int ld, int PW, int B, int n1, int d0,
+                                                               double* __restrict__ vals) {
+  const int slots = PW * B;
+  const int s = blockIdx.x * kThreads + threadIdx.x;
+  if (s >= slots) return;
+  const int d = d0 + blockIdx.y;
+  vals[(size_t)blockIdx.y * slots + s] = diag_value(W, out_dim, in_dim, ld, PW, n1, d / n1, d % n1, s / B);
+}
+
+struct BabyPtrs {
+  const uint64_t* c0[kMaxBaby];
+  const uint64_t* c1[kMaxBaby];
+};
+struct InnerPtrs {
+  uint64_t* c0[kMaxBaby];
+  uint64_t* c1[kMaxBaby];
+};
+
+// inner_g = sum_j diag[g n1 + j] * baby_j for kGiantsPerBlock giant steps per
+// CTA: each baby residue is loaded once and feeds 2 x 8 MAC chains; the
+// diagonals stream from HBM once per product.
+__global__ void __launch_bounds__(kThreads) bsgs_inner_kernel(BabyPtrs babies, int n1,
+                                                              const uint64_t* __restrict__ diag, InnerPtrs out,
+                                                              int limbs, int logN, int n2,
+                                                              const ckks::Mod* __restrict__ mods) {
+  const int N = 1 << logN;
+  const int n = blockIdx.x * kThreads + threadIdx.x;
+  if (n >= N) return;
+  const int l = blockIdx.y;
+  const int g0 = blockIdx.z * kGiantsPerBlock;
+  const size_t limb_off = (size_t)l * N + n;
+  ckks::U128 a0[kGiantsPerBlock], a1[kGiantsPerBlock];
+#pragma unroll
+  for (int i = 0; i < kGiantsPerBlock; ++i) a0[i] = a1[i] = ckks::U128{0, 0};
+  const size_t diag_stride = (size_t)limbs * N;
+  for (int j = 0; j < n1; ++j) {
+    const uint64_t b0 = babies.c0[j][limb_off];
+    const uint64_t b1 = babies.c1[j][limb_off];
+#pragma unroll
+    for (int i = 0; i < kGiantsPerBlock; ++i) {
+      if (g0 + i < n2) {
+        const uint64_t dv = diag[(size_t)((g0 + i) * n1 + j) * diag_stride + limb_off];
+        ckks::mac_wide(a0[i], dv, b0);
+        ckks::mac_wide(a1[i], dv, b1);
+      }
+    }
+  }
+  const ckks::Mod m = mods[l];
+#pragma unroll
+  for (int i = 0; i < kGiantsPerBlock; ++i) {
+    if (g0 + i < n2) {
+      out.c0[g0 + i][limb_off] = ckks::reduce128(a0[i], m);
+      out.c1[g0 + i][limb_off] = ckks::reduce128(a1[i], m);
+    }
+  }
+}
+
+double now_s() {
+  return std::chrono::duration<double>(std::chrono::steady_clock::now().time_since_epoch()).count();
+}
+
+}  // namespace blk
+
+struct ckks_block {
+  ckks_ctx* ctx;
+  ckks_b200::CryptoContextImpl cc;
+  ckks::Context& C;
+  blk::Shape s;
+  int LX = 11;  // limbs of the encrypted input; all other levels follow from it
+  // device copies of the weights (gain folded), [out, in] row-major
+  double* d_qkv = nullptr;
+  double* d_proj = nullptr;
+  double* d_fc = nullptr;
+  double* d_proj2 = nullptr;
+  int nfc = 3;
+  struct Diag {
+    uint64_t* data = nullptr;
+    int limbs = 0;
+    double scale = 0.0;
+  };
+  std::map<std::pair<int, int>, Diag> diags;  // (weight id, limbs) -> encoded diagonals
+  std::map<std::pair<int, int>, Plaintext> masks;
+  // counters (the reference pins the same kinds, T123.cpp:1698-1744)
+  std::map<std::string, long> count;
+  std::map<std::string, double> seconds;
+  double client_seconds = 0.0;
+
+  ckks_block(ckks_ctx* c, const blk::Shape& shape) : ctx(c), cc(c), C(*c->c), s(shape) {}
+  ~ckks_block() {
+    for (auto& kv : diags) C.release(kv.second.data);
+    cudaFree(d_qkv);
+    cudaFree(d_proj);
+    cudaFree(d_fc);
+    cudaFree(d_proj2);
+  }
+
+  double S(int limbs) const { return C.scales[limbs]; }
+
+  // ---- client role (T123.cpp:509-715) -------------------------------------
+  Ciphertext client_encrypt(const std::vector<double>& v, int limbs) {
+    const double t0 = blk::now_s();
+    auto ct = cc.Encrypt(cc.MakePlaintextAt(v, limbs, S(limbs)));
+    client_seconds += blk::now_s() - t0;
+    return ct;
+  }
+  std::vector<double> client_decrypt(const Ciphertext& ct) {
+    const double t0 = blk::now_s();
+    auto v = cc.Decrypt(ct)->GetRealPackedValue();
+    client_seconds += blk::now_s() - t0;
+    return v;
+  }
+
+  // ---- server helpers -------------------------------------------------------
+  Ciphertext rs(const Ciphertext& a) { return cc.Rescale(a); }
+  Ciphertext mul_pt_rs(const Ciphertext& a, const Plaintext& p) {
+    ++count["ct_plain"];
+    return rs(cc.EvalMult(a, p));
+  }
+  Ciphertext mul_ct_rs(const Ciphertext& a, const Ciphertext& b) {
+    ++count["ct_ct"];
+    return rs(cc.EvalMult(a, b));
+  }
+  Ciphertext reduce_to(const Ciphertext& a, int limbs) {
+    if (a->limbs() == limbs) return a;
+    ++count["level_reduce"];
+    return cc.LevelReduce(a, limbs);
+  }
+  Ciphertext rot(const Ciphertext& a, int k) {
+    ++count["rotations"];
+    return cc.EvalRotate(a, k);
+  }
+  Ciphertext add(const Ciphertext& a, const Ciphertext& b) { return cc.EvalAdd(a, b); }
+
+  // plaintext of per-feature values, the same on every lane
+  Plaintext feature_plain(int id, const std::vector<double>& per_feature, int limbs) {
+    auto key = std::make_pair(id, limbs);
+    auto it = masks.find(key);
+    if (it != masks.end()) return it->second;
+    std::vector<double> v((size_t)s.PW * s.B, 0.0);
+    for (int f = 0; f < s.PW; ++f)
+      for (int t = 0; t < s.B; ++t) v[(size_t)f * s.B + t] = per_feature[f];
+    auto p = cc.MakePlaintextAt(v, limbs, S(limbs));
+    masks[key] = p;
+    return p;
+  }
+  Plaintext lane_plain(int id, int delta, bool lower, int limbs) {
+    auto key = std::make_pair(1000 + 2 * delta + (lower ? 1 : 0), limbs);
+    auto it = masks.find(key);
+    if (it != masks.end()) return it->second;
+    std::vector<double> v((size_t)s.PW * s.B, 0.0);
+    for (int f = 0; f < s.PW; ++f)
+      for (int t = 0; t < s.B; ++t) v[(size_t)f * s.B + t] = ((t < s.B - delta) == lower) ? 1.0 : 0.0;
+    (void)id;
+    auto p = cc.MakePlaintextAt(v, limbs, S(limbs));
+    masks[key] = p;
+    return p;
+  }
+
+  Ciphertext feature_sum(const Ciphertext& x) {
+    ++count["accumulate_sum"];
+    return cc.AccumulateSum(x, s.PW, s.B);
+  }
+
+  // LayerNorm without the gain (folded into the next product): returns
+  // centered / sqrt(var + eps) at limbs(x) - 2 (T123.cpp:1168-1181)
+  Ciphertext layernorm(const Ciphertext& x, int active, const char* stage) {
+    const int lx = x->limbs();
+    std::vector<double> invd(s.PW, 0.0);
+    for (int f = 0; f < s.D; ++f) invd[f] = 1.0 / s.D;
+    const Ciphertext mean = mul_pt_rs(feature_sum(x), feature_plain(1, invd, lx));
+    const Ciphertext centered = cc.EvalSub(reduce_to(x, lx - 1), mean);
+    const Ciphertext sq = mul_ct_rs(centered, centered);
+    Ciphertext var = mul_pt_rs(feature_sum(sq), feature_plain(1, invd, lx - 2));
+    var = cc.EvalAdd(var, 1e-5);
+    // client: exact inverse square root on every slot (T123.cpp:514-538)
+    std::vector<double> v = client_decrypt(var);
+    for (double& e : v) e = 1.0 / std::sqrt(e);
+    const Ciphertext inv = client_encrypt(v, lx - 1);
+    ++count["client_round_trips"];
+    count["client_logical_instances"] += active;
+    (void)stage;
+    return mul_ct_rs(centered, inv);
+  }
+
+  // output[f, t] = input[f, (t + delta) mod B]: two rotations, two masks, one
+  // add (simd_layout.py:142-158, T123.cpp:1297-1314)
+  Ciphertext lane_shift(const Ciphertext& x, int delta) {
+    const int l = x->limbs();
+    ++count["rotations"];
+    ++count["rotations"];
+    auto r = cc.EvalFastRotation(x, {delta, delta - s.B});
+    const Ciphertext a = cc.EvalMult(r[0], lane_plain(0, delta, true, l));
+    const Ciphertext b = cc.EvalMult(r[1], lane_plain(0, delta, false, l));
+    count["ct_plain"] += 2;
+    return rs(cc.EvalAdd(a, b));
+  }
+
+  // sum of the hd features of every head, left at the head's first feature
+  Ciphertext head_window_sum(Ciphertext h) {
+    for (int w = 1; w < s.HD; w <<= 1) h = add(h, rot(h, s.B * w));
+    return h;
+  }
+
+  // weight id -> (device matrix, out_dim, in_dim, leading dimension)
+  void weight_view(int id, const double*& W, int& out_dim, int& in_dim, int& ld) const {
+    const int D = s.D;
+    if (id < 3) {
+      W = d_qkv + (size_t)id * D * D;
+      out_dim = D;
+      in_dim = D;
+      ld = D;
+    } else if (id == 3) {
+      W = d_proj;
+      out_dim = D;
+      in_dim = D;
+      ld = D;
+    } else if (id < 4 + nfc) {
+      const int c = id - 4;
+      W = d_fc + (size_t)c * s.PW * D;
+      out_dim = std::min(s.PW, s.MLP - c * s.PW);
+      in_dim = D;
+      ld = D;
+    } else {
+      const int c = id - 4 - nfc;
+      W = d_proj2 + (size_t)c * s.PW;
+      out_dim = D;
+      in_dim = std::min(s.PW, s.MLP - c * s.PW);
+      ld = s.MLP;
+    }
+  }
+
+  // all n1 * n2 diagonals of weight `id`, encoded once per use level on the
+  // device and kept (the reference encodes them on the host, T123.cpp:1005-1059)
+  const Diag& diagonals(int id, int limbs) {
+    auto key = std::make_pair(id, limbs);
+    auto it = diags.find(key);
+    if (it != diags.end()) {
+      ++count["diagonal_cache_hits"];
+      return it->second;
+    }
+    ++count["diagonal_cache_misses"];
+    const double t0 = blk::now_s();
+    const double* W;
+    int od, id_, ld;
+    weight_view(id, W, od, id_, ld);
+    const int nd = s.n1 * s.n2, slots = s.PW * s.B;
+    const size_t stride = (size_t)limbs * C.N;
+    Diag dg;
+    dg.limbs = limbs;
+    dg.scale = S(limbs);
+    dg.data = (uint64_t*)C.alloc(sizeof(uint64_t) * nd * stride);
+    const int chunk = 128;
+    double* vals = (double*)C.alloc(sizeof(double) * (size_t)chunk * slots);
+    for (int d0 = 0; d0 < nd; d0 += chunk) {
+      const int cnt = std::min(chunk, nd - d0);
+      blk::diag_values_kernel<<<dim3((slots + blk::kThreads - 1) / blk::kThreads, cnt), blk::kThreads, 0,
+                                  C.stream>>>(W, od, id_, ld, s.PW, s.B, s.n1, d0, vals);
+      CKKS_CUDA(cudaGetLastError());
+      ckks::encode_batch(C, vals, cnt, limbs, dg.scale, dg.data + (size_t)d0 * stride, stride, C.stream);
+    }
+    C.release(vals);
+    seconds["diagonal_encode"] += blk::now_s() - t0;
+    return diags.emplace(key, dg).first->second;
+  }
+
+  std::vector<Ciphertext> babies_of(const Ciphertext& x) {
+    std::vector<int> idx;
+    for (int j = 1; j < s.n1; ++j) idx.push_back(s.B * j);
+    auto r = cc.EvalFastRotation(x, idx);
+    count["rotations"] += (long)idx.size();
+    std::vector<Ciphertext> b{x};
+    b.insert(b.end(), r.begin(), r.end());
+    return b;
+  }
+
+  // x W^T for weight `id` from the baby-step rotations of x (T123.cpp:1264-1295)
+  Ciphertext bsgs(const std::vector<Ciphertext>& baby, int id) {
+    ++count["matrix_products"];
+    count["ct_plain"] += (long)s.n1 * s.n2;
+    const int limbs = baby[0]->limbs();
+    const Diag& dg = diagonals(id, limbs);
+    blk::BabyPtrs bp{};
+    for (int j = 0; j < s.n1; ++j) {
+      const ckks::DevPoly& p = baby[j]->handle()->p;
+      if (p.limbs != limbs) throw ckks::Error(CKKS_ELEVEL, "baby steps at different levels");
+      bp.c0[j] = p.data;
+      bp.c1[j] = p.data + (size_t)p.cap * C.N;
+    }
+    const double sc = baby[0]->scale() * dg.scale;
+    std::vector<Ciphertext> inner(s.n2);
+    blk::InnerPtrs ip{};
+    for (int g = 0; g < s.n2; ++g) {
+      inner[g] = cc.fresh();
+      ckks::DevPoly& p = inner[g]->handle()->p;
+      p.ensure(&C, 2, limbs);
+      p.limbs = limbs;
+      p.scale = sc;
+      p.deg = baby[0]->noise_deg() + 1;
+      ip.c0[g] = p.data;
+      ip.c1[g] = p.data + (size_t)p.cap * C.N;
+    }
+    {
+      ckks::ProfScope ps(C, "bsgs_inner",
+                         ((double)s.n1 * s.n2 * limbs + 2.0 * s.n1 * limbs + 2.0 * s.n2 * limbs) * C.limb_bytes(),
+                         C.stream);
+      const dim3 grid((C.N + blk::kThreads - 1) / blk::kThreads, limbs,
+                      (s.n2 + blk::kGiantsPerBlock - 1) / blk::kGiantsPerBlock);
+      blk::bsgs_inner_kernel<<<grid, blk::kThreads, 0, C.stream>>>(bp, s.n1, dg.data, ip, limbs, C.logN, s.n2,
+                                                                   C.d_mods);
+    }
+    CKKS_CUDA(cudaGetLastError());
+    Ciphertext acc = inner[0];
+    for (int g = 1; g < s.n2; ++g) acc = add(acc, rot(inner[g], s.B * s.n1 * g));
+    return rs(acc);
+  }
+
+  void forward(const double* x, int T, double* y);
+  std::vector<int> rotation_indices() const;
+};
+
+std::vector<int> ckks_block::rotation_indices() const {
+  const int slots = s.PW * s.B;
+  auto canon = [&](long k) {
+    long r = k % slots;
+    if (r < 0) r += slots;
+    if (r > slots / 2) r -= slots;
+    return (int)r;
+  };
+  std::vector<int> v;
+  for (int j = 1; j < s.n1; ++j) v.push_back(canon((long)s.B * j));
+  for (int g = 1; g < s.n2; ++g) v.push_back(canon((long)s.B * s.n1 * g));
+  for (long step = 1; step < s.PW; step *= 4)  // AccumulateSum ladder (T123.cpp:444-453)
+    for (int m = 1; m < 4 && step * m < s.PW; ++m) v.push_back(canon((long)s.B * step * m));
+  for (int d = 1; d < s.B; ++d) {
+    v.push_back(canon(d));
+    v.push_back(canon(d - s.B));
+  }
+  for (int w = 1; w < s.HD; w <<= 1) v.push_back(canon((long)s.B * w));
+  std::sort(v.begin(), v.end());
+  v.erase(std::unique(v.begin(), v.end()), v.end());
+  v.erase(std::remove(v.begin(), v.end(), 0), v.end());
+  return v;
+}
+
+void ckks_block::forward(const double* x, int T, double* y) {
+  if (T != s.T) throw ckks::Error(CKKS_EARG, "token count differs from the block's");
+  const int G = s.groups, B = s.B, D = s.D, PW = s.PW, H = s.H, HD = s.HD;
+  count.clear();
+  seconds.clear();
+  client_seconds = 0.0;
+  const double t_start = blk::now_s();
+  auto stamp = [&](const char* k, double& t) {
+    cc.Synchronize();
+    const double n = blk::now_s();
+    seconds[k] += n - t;
+    t = n;
+  };
+  double t = t_start;
+  // client: pack and encrypt the embeddings (T123.cpp:1642-1661)
+  std::vector<Ciphertext> xin(G);
+  for (int g = 0; g < G; ++g) {
+    std::vector<double> v((size_t)PW * B, 0.0);
+    for (int tl = 0; tl < s.count(g); ++tl)
+      for (int f = 0; f < D; ++f) v[(size_t)f * B + tl] = x[(size_t)(g * B + tl) * D + f];
+    xin[g] = client_encrypt(v, LX);
+  }
+  stamp("encrypt_inputs", t);
+
+  // LN1 + QKV
+  std::vector<Ciphertext> Q(G), K(G), V(G);
+  for (int g = 0; g < G; ++g) {
+    const Ciphertext nrm = layernorm(xin[g], s.count(g), "ln1");
+    const auto baby = babies_of(nrm);
+    Q[g] = bsgs(baby, 0);
+    K[g] = bsgs(baby, 1);
+    V[g] = bsgs(baby, 2);
+  }
+  stamp("ln1_qkv", t);
+
+  // scores
+  const int lk = Q[0]->limbs() - 1;  // shifted key / value level
+  std::vector<std::vector<std::vector<double>>> scores(
+      T, std::vector<std::vector<double>>(H, std::vector<double>(T, std::nan(""))));
+  std::vector<Ciphertext> Qr(G);
+  for (int g = 0; g < G; ++g) Qr[g] = reduce_to(Q[g], lk);
+  const double inv_sqrt_hd = 1.0 / std::sqrt((double)HD);
+  for (int kg = 0; kg < G; ++kg) {
+    std::map<int, Ciphertext> ks;
+    for (int qg = kg; qg < G; ++qg)
+      for (int d : blk::active_shifts(T, B, qg, kg))
+        if (!ks.count(d)) ks[d] = d ? lane_shift(K[kg], d) : reduce_to(K[kg], lk);
+    count["cached_key_lane_shifts"] += (long)ks.size() - (ks.count(0) ? 1 : 0);
+    for (int qg = kg; qg < G; ++qg) {
+      for (int d : blk::active_shifts(T, B, qg, kg)) {
+        const Ciphertext prod = head_window_sum(mul_ct_rs(Qr[qg], ks[d]));
+        const std::vector<double> v = client_decrypt(prod);
+        ++count["score_tile_decryptions"];
+        ++count["client_round_trips"];
+        for (int ql = 0; ql < s.count(qg); ++ql) {
+          const int kl = (ql + d) % B;
+          const int q = qg * B + ql, k = kg * B + kl;
+          if (kl >= s.count(kg) || k > q) continue;
+          for (int h = 0; h < H; ++h) {
+            scores[q][h][k] = v[(size_t)(h * HD) * B + ql] * inv_sqrt_hd;
+            ++count["client_logical_instances"];
+          }
+        }
+      }
+    }
+  }
+  stamp("scores", t);
+  // client: exact causal softmax in float64 (T123.cpp:629-665)
+  const double tc = blk::now_s();
+  std::vector<std::vector<std::vector<double>>> prob(T, std::vector<std::vector<double>>(H, std::vector<double>(T, 0.0)));
+  for (int q = 0; q < T; ++q)
+    for (int h = 0; h < H; ++h) {
+      double mx = -INFINITY;
+      for (int k = 0; k <= q; ++k) {
+        if (!std::isfinite(scores[q][h][k])) throw ckks::Error(CKKS_ESTATE, "missing causal attention score");
+        mx = std::max(mx, scores[q][h][k]);
+      }
+      double den = 0.0;
+      for (int k = 0; k <= q; ++k) den += std::exp(scores[q][h][k] - mx);
+      for (int k = 0; k <= q; ++k) prob[q][h][k] = std::exp(scores[q][h][k] - mx) / den;
+    }
+  client_seconds += blk::now_s() - tc;
+
+  // context: client weight tiles x shifted values (T123.cpp:838-860)
+  std::vector<Ciphertext> ctx(G);
+  for (int kg = 0; kg < G; ++kg) {
+    std::map<int, Ciphertext> vs;
+    for (int qg = kg; qg < G; ++qg)
+      for (int d : blk::active_shifts(T, B, qg, kg))
+        if (!vs.count(d)) vs[d] = d ? lane_shift(V[kg], d) : reduce_to(V[kg], lk);
+    count["cached_value_lane_shifts"] += (long)vs.size() - (vs.count(0) ? 1 : 0);
+    for (int qg = kg; qg < G; ++qg) {
+      for (int d : blk::active_shifts(T, B, qg, kg)) {
+        std::vector<double> w((size_t)PW * B, 0.0);
+        for (int ql = 0; ql < s.count(qg); ++ql) {
+          const int kl = (ql + d) % B;
+          const int q = qg * B + ql, k = kg * B + kl;
+          if (kl >= s.count(kg) || k > q) continue;
+          for (int f = 0; f < D; ++f) w[(size_t)f * B + ql] = prob[q][f / HD][k];
+        }
+        const Ciphertext wt = client_encrypt(w, lk);
+        ++count["weight_tile_encryptions"];
+        ++count["client_round_trips"];
+        const Ciphertext c = mul_ct_rs(wt, vs[d]);
+        ctx[qg] = ctx[qg] ? add(ctx[qg], c) : c;
+      }
+    }
+  }
+  stamp("context", t);
+
+  // O projection, residual, LN2, MLP
+  std::vector<Ciphertext> out(G);
+  for (int g = 0; g < G; ++g) {
+    const Ciphertext o = bsgs(babies_of(ctx[g]), 3);
+    const Ciphertext r1 = add(reduce_to(xin[g], o->limbs()), o);
+    const Ciphertext n2 = layernorm(r1, s.count(g), "ln2");
+    const auto fb = babies_of(n2);
+    const int gelu_limbs = 3;
+    Ciphertext mlp;
+    for (int c = 0; c < nfc; ++c) {
+      const Ciphertext hc = bsgs(fb, 4 + c);
+      // client: exact tanh-GELU on the active lanes (T123.cpp:540-568)
+      std::vector<double> v = client_decrypt(hc);
+      std::vector<double> gv((size_t)PW * B, 0.0);
+      const int odim = std::min(PW, s.MLP - c * PW);
+      for (int f = 0; f < odim; ++f)
+        for (int tl = 0; tl < s.count(g); ++tl) {
+          const double u = v[(size_t)f * B + tl];
+          gv[(size_t)f * B + tl] = 0.5 * u * (1.0 + std::tanh(0.7978845608028654 * (u + 0.044715 * u * u * u)));
+        }
+      ++count["client_round_trips"];
+      count["client_logical_instances"] += (long)odim * s.count(g);
+      const Ciphertext ge = client_encrypt(gv, gelu_limbs);
+      const Ciphertext pc = bsgs(babies_of(ge), 4 + nfc + c);
+      mlp = c ? add(mlp, pc) : pc;
+    }
+    out[g] = add(reduce_to(r1, mlp->limbs()), mlp);
+  }
+  stamp("oproj_ln2_mlp", t);
+
+  // client: decrypt and unpack (T123.cpp:1675-1694)
+  for (int g = 0; g < G; ++g) {
+    const std::vector<double> v = client_decrypt(out[g]);
+    for (int tl = 0; tl < s.count(g); ++tl)
+      for (int f = 0; f < D; ++f) y[(size_t)(g * B + tl) * D + f] = v[(size_t)f * B + tl];
+  }
+  stamp("decrypt_outputs", t);
+  seconds["total"] = blk::now_s() - t_start;
+  seconds["client"] = client_seconds;
+  count["output_limbs"] = out[0]->limbs();
+  count["input_limbs"] = LX;
+}
+
+namespace {
+template <typename F>
+int bguard(F&& f) {
+  try {
+    f();
+    return CKKS_OK;
+  } catch (const ckks::Error& e) {
+    ckks::set_last_error(e.what());
+    return e.code;
+  } catch (const ckks_b200::Error& e) {
+    ckks::set_last_error(e.what());
+    return e.code;
+  } catch (const std::exception& e) {
+    ckks::set_last_error(e.what());
+    return CKKS_EARG;
+  }
+}
+
+double* upload_matrix(const std::vector<double>& v) {
+  double* d = nullptr;
+  CKKS_CUDA(cudaMalloc(&d, sizeof(double) * v.size()));
+  CKKS_CUDA(cudaMemcpy(d, v.data(), sizeof(double) * v.size(), cudaMemcpyHostToDevice));
+  return d;
+}
+}  // namespace
+
+extern "C" {
+
+int ckks_block_create(ckks_ctx* ctx, const double* ln1, const double* attn_qkv, const double* attn_proj,
+                      const double* ln2, const double* mlp_fc, const double* mlp_proj, int d_model, int heads,
+                      int mlp_dim, int tokens, ckks_block** out) {
+  return bguard([&] {
+    if (!ctx || !ctx->c || !out) throw ckks::Error(CKKS_EARG, "null argument");
+    if (!ln1 || !attn_qkv || !attn_proj || !ln2 || !mlp_fc || !mlp_proj) throw ckks::Error(CKKS_EARG, "null weight");
+    ckks::Context& C = *ctx->c;
+    blk::Shape s;
+    s.D = d_model;
+    s.H = heads;
+    s.MLP = mlp_dim;
+    s.T = tokens;
+    if (d_model <= 0 || heads <= 0 || d_model % heads || mlp_dim <= 0 || tokens <= 0)
+      throw ckks::Error(CKKS_EARG, "bad block shape");
+    s.HD = d_model / heads;
+    s.B = 32;
+    s.PW = C.N / 2 / s.B;
+    if (s.PW < d_model || (s.HD & (s.HD - 1))) throw ckks::Error(CKKS_EARG, "shape does not fit the slot layout");
+    s.n1 = 32;
+    while (s.n1 * s.n1 > s.PW) s.n1 >>= 1;
+    s.n2 = s.PW / s.n1;
+    if (s.n1 > blk::kMaxBaby) throw ckks::Error(CKKS_EARG, "too many baby steps");
+    s.groups = (tokens + s.B - 1) / s.B;
+    auto* b = new ckks_block(ctx, s);
+    try {
+      b->nfc = (mlp_dim + s.PW - 1) / s.PW;
+      const int D = d_model;
+      std::vector<double> qkv((size_t)3 * D * D), fc((size_t)mlp_dim * D);
+      for (int r = 0; r < 3 * D; ++r)
+        for (int c = 0; c < D; ++c) qkv[(size_t)r * D + c] = attn_qkv[(size_t)r * D + c] * ln1[c];
+      for (int r = 0; r < mlp_dim; ++r)
+        for (int c = 0; c < D; ++c) fc[(size_t)r * D + c] = mlp_fc[(size_t)r * D + c] * ln2[c];
+      b->d_qkv = upload_matrix(qkv);
+      b->d_proj = upload_matrix(std::vector<double>(attn_proj, attn_proj + (size_t)D * D));
+      b->d_fc = upload_matrix(fc);
+      b->d_proj2 = upload_matrix(std::vector<double>(mlp_proj, mlp_proj + (size_t)D * mlp_dim));
+      if (C.L < b->LX) throw ckks::Error(CKKS_ELEVEL, "the block needs 11 Q limbs");
+    } catch (...) {
+      delete b;
+      throw;
+    }
+    *out = b;
+  });
+}
+
+int ckks_block_destroy(ckks_block* b) {
+  return bguard([&] { delete b; });
+}
+
+int ckks_block_rotation_indices(const ckks_block* b, int* out, int cap) {
+  if (!b) return -1;
+  const auto v = b->rotation_indices();
+  for (int i = 0; i < (int)v.size() && i < cap; ++i) out[i] = v[i];
+  return (int)v.size();
+}
+
+int ckks_block_forward(ckks_block* b, const double* x, int tokens, double* y) {
+  return bguard([&] {
+    if (!b || !x || !y) throw ckks::Error(CKKS_EARG, "null argument");
+    b->forward(x, tokens, y);
+  });
+}
+
+int ckks_block_report(const ckks_block* b, char* buf, size_t size) {
+  if (!b) return -1;
+  std::string js = "{\"counts\": {";
+  bool first = true;
+  for (auto& kv : b->count) {
+    js += (first ? "\"" : ", \"") + kv.first + "\": " + std::to_string(kv.second);
+    first = false;
+  }
+  js += "}, \"seconds\": {";
+  first = true;
+  char tmp[64];
+  for (auto& kv : b->seconds) {
+    std::snprintf(tmp, sizeof tmp, "%.6f", kv.second);
+    js += (first ? "\"" : ", \"") + kv.first + "\": " + tmp;
+    first = false;
+  }
+  js += "}}";
+  if (buf && size) {
+    const size_t n = std::min(js.size(), size - 1);
+    std::memcpy(buf, js.data(), n);
+    buf[n] = 0;
+  }
+  return (int)js.size();
+}
+
+int ckks_schedule_active_shifts(int tokens, int batch, int qg, int kg, int* out, int cap) {
+  if (tokens <= 0 || batch <= 0 || qg < kg || kg < 0 || qg * batch >= tokens) return -1;
+  const auto v = blk::active_shifts(tokens, batch, qg, kg);
+  for (int i = 0; i < (int)v.size() && i < cap; ++i) out[i] = v[i];
+  return (int)v.size();
+}
+
+int ckks_schedule_diagonal(const double* W, int out_dim, int in_dim, int ld, int pack_width, int batch, int n1,
+                           int g, int j, double* out_slots) {
+  if (!W || !out_slots || out_dim > pack_width || in_dim > pack_width || n1 <= 0 || pack_width % n1) return CKKS_EARG;
+  for (int f = 0; f < pack_width; ++f) {
+    const double v = blk::diag_value(W, out_dim, in_dim, ld, pack_width, n1, g, j, f);
+    for (int t = 0; t < batch; ++t) out_slots[(size_t)f * batch + t] = v;
+  }
+  return CKKS_OK;
+}
+
+}  // extern "C"

@@ -251,6 +251,9 @@ void decrypt(const Context& c, const uint64_t* c0, const uint64_t* c1, int limbs
 
 // canonical embedding
 void encode(const Context& c, const double* d_values, int limbs, double scale, uint64_t* out, cudaStream_t st);
+// batch x (N/2) device values -> batch plaintexts of `limbs` limbs, out_stride words apart
+void encode_batch(const Context& c, const double* d_values, int batch, int limbs, double scale, uint64_t* out,
+                  size_t out_stride, cudaStream_t st);
 void decode(const Context& c, const uint64_t* pt, int limbs, double scale, double* d_values, cudaStream_t st);
 
 // integer / double residues on the host

@@ -1,0 +1,79 @@
+"""Generates the golden fixtures in this directory from the reference's own
+Python modules (run in a container that has the reference tree at
+/root/reference; the fixtures are committed, the tree is not needed later).
+
+  plain_block_t8.npz  fhe/realweights/manual.py block_reference on the seeded
+                      synthetic block (seed 3, T = 8) -- pins oracle/plain_block.py
+  simd_layout_b32.json + simd_layout_b32.npz
+                      fhe/gpu_real_scheme_b/simd_layout.py at batch width 32,
+                      one copy (the 32-tokens-per-ciphertext layout): slot map,
+                      lane shift, active alignments and protocol / operation
+                      counts at T = 103, a reduced-size BSGS transform and
+                      score / context tiles.
+"""
+
+import json
+import os
+import sys
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+ROOT = os.path.dirname(os.path.dirname(HERE))
+REF = "/root/reference"
+sys.path.insert(0, ROOT)
+sys.path.insert(0, os.path.join(REF, "fhe", "gpu_real_scheme_b"))
+sys.path.insert(0, os.path.join(REF, "fhe", "realweights"))
+
+import manual  # noqa: E402  (reference: fhe/realweights/manual.py)
+import simd_layout as sl  # noqa: E402  (reference: fhe/gpu_real_scheme_b/simd_layout.py)
+
+from oracle.plain_block import synthetic_input, synthetic_weights  # noqa: E402
+from tests.golden.inputs import layout_inputs  # noqa: E402
+
+
+def plain_block():
+    w = synthetic_weights(3)
+    x = synthetic_input(4, 8)
+    ref = manual.block_reference(x, {"ln1": w["ln1"], "attn_qkv": w["attn_qkv"], "attn_proj": w["attn_proj"],
+                                     "ln2": w["ln2"], "mlp_fc": w["mlp_fc"], "mlp_proj": w["mlp_proj"]})
+    np.savez_compressed(os.path.join(HERE, "plain_block_t8.npz"), seed_weights=3, seed_input=4,
+                        block_output=ref["block_output"], ln1_output=ref["ln1_output"],
+                        attention_scores=ref["attention_scores"], residual1=ref["residual1"])
+
+
+def layout():
+    B, T = 32, 103
+    out = {"batch_width": B, "tokens": T, "copies": 1}
+    out["slots"] = [[c, f, t, sl.physical_slot(c, f, t, B, copies=1)] for c, f, t in
+                    [(0, 0, 0), (0, 0, 31), (0, 1, 0), (0, 767, 5), (0, 1023, 31)]]
+    groups = -(-T // B)
+    out["active_weight_shifts"] = {
+        f"{qg},{kg}": list(sl.active_weight_shifts(qg * B, min(B, T - qg * B), kg * B, min(B, T - kg * B), B))
+        for qg in range(groups) for kg in range(qg + 1)}
+    pc = sl.protocol_counts(T, B)
+    out["protocol_counts"] = {k: getattr(pc, k) for k in ("token_groups", "score_tile_decryptions",
+                                                          "weight_tile_encryptions", "layernorm1_crossings",
+                                                          "layernorm2_crossings", "gelu_crossings")}
+    sc = sl.server_operation_counts(T, B)
+    out["server_operation_counts"] = {k: getattr(sc, k) for k in sc.__dataclass_fields__}
+    vals = np.arange(19 * B, dtype=np.float64)
+    arrays = {"lane_shift_in": vals}
+    for d in (0, 1, 5, 31, -3):
+        arrays[f"lane_shift_{d}"] = sl.lane_shift(vals, d, B)
+    tok, W, q, k, weights, values = layout_inputs()
+    # reduced BSGS: dimension 48 padded to 64, 8 baby steps, one copy
+    arrays["bsgs_out"] = sl.bsgs_matmul_tokens(tok, W, B, dimension=48, pack_width=64, copies=1, bsgs_n1=8,
+                                               max_complex_slots=64 * B)
+    # score tile and context tiles at the block's head shape, one copy
+    arrays["score_tile"] = sl.score_tile(q, k, B, copies=1)
+    arrays["ctx_out"] = sl.context_from_weight_tiles(weights, values, B, copies=1)
+    with open(os.path.join(HERE, "simd_layout_b32.json"), "w") as f:
+        json.dump(out, f, indent=1, sort_keys=True)
+    np.savez_compressed(os.path.join(HERE, "simd_layout_b32.npz"), **arrays)
+
+
+if __name__ == "__main__":
+    plain_block()
+    layout()
+    print("golden fixtures written")
