@@ -143,6 +143,14 @@ int ckks_rotate(ckks_ctx* ctx, const ckks_ct* a, int k, ckks_ct* out);
 /* EvalFastRotation(ct, k[], M, nullptr): one ModUp shared by `count`
  * rotations (T123.cpp:1183-1203, 1343-1362) */
 int ckks_rotate_hoisted(ckks_ctx* ctx, const ckks_ct* a, const int* k, int count, ckks_ct* const* outs);
+/* Batched forms: `count` independent operations at one limb count, run as
+ * one launch sequence per stage (up to 32 per sequence).  They replace loops
+ * of EvalRotate / EvalMult / Rescale calls over independent ciphertexts
+ * (the reference issues them one at a time, T123.cpp:795-860). */
+int ckks_rotate_batch(ckks_ctx* ctx, const ckks_ct* const* in, const int* k, int count, ckks_ct* const* outs);
+int ckks_mul_ct_batch(ckks_ctx* ctx, const ckks_ct* const* a, const ckks_ct* const* b, int count,
+                      ckks_ct* const* outs);
+int ckks_rescale_batch(ckks_ctx* ctx, const ckks_ct* const* in, int count, ckks_ct* const* outs);
 /* AccumulateSum(ct, count, stride) (T123.cpp:1154-1159; key ladder :444-453) */
 int ckks_accumulate_sum(ckks_ctx* ctx, const ckks_ct* a, int count, int stride, ckks_ct* out);
 

@@ -199,6 +199,44 @@ class CryptoContextImpl {
     check(ckks_rotate_hoisted(h_, a->handle(), k.data(), (int)k.size(), hs.data()));
     return outs;
   }
+  // independent rotations / products / rescales at one limb count, batched
+  std::vector<Ciphertext> EvalRotateBatch(const std::vector<Ciphertext>& a, const std::vector<int>& k) {
+    std::vector<Ciphertext> outs;
+    std::vector<const ckks_ct*> in;
+    std::vector<ckks_ct*> hs;
+    for (size_t i = 0; i < a.size(); ++i) {
+      outs.push_back(fresh());
+      in.push_back(a[i]->handle());
+      hs.push_back(outs.back()->handle());
+    }
+    check(ckks_rotate_batch(h_, in.data(), k.data(), (int)a.size(), hs.data()));
+    return outs;
+  }
+  std::vector<Ciphertext> EvalMultBatch(const std::vector<Ciphertext>& a, const std::vector<Ciphertext>& b) {
+    std::vector<Ciphertext> outs;
+    std::vector<const ckks_ct*> x, y;
+    std::vector<ckks_ct*> hs;
+    for (size_t i = 0; i < a.size(); ++i) {
+      outs.push_back(fresh());
+      x.push_back(a[i]->handle());
+      y.push_back(b[i]->handle());
+      hs.push_back(outs.back()->handle());
+    }
+    check(ckks_mul_ct_batch(h_, x.data(), y.data(), (int)a.size(), hs.data()));
+    return outs;
+  }
+  std::vector<Ciphertext> RescaleBatch(const std::vector<Ciphertext>& a) {
+    std::vector<Ciphertext> outs;
+    std::vector<const ckks_ct*> in;
+    std::vector<ckks_ct*> hs;
+    for (size_t i = 0; i < a.size(); ++i) {
+      outs.push_back(fresh());
+      in.push_back(a[i]->handle());
+      hs.push_back(outs.back()->handle());
+    }
+    check(ckks_rescale_batch(h_, in.data(), (int)a.size(), hs.data()));
+    return outs;
+  }
   Ciphertext AccumulateSum(const Ciphertext& a, int count, int stride) {
     auto o = fresh();
     check(ckks_accumulate_sum(h_, a->handle(), count, stride, o->handle()));

@@ -108,6 +108,11 @@ _SIGS = [
     ("ckks_rotate", ctypes.c_int, [_vp, _vp, ctypes.c_int, _vp]),
     ("ckks_rotate_hoisted", ctypes.c_int, [_vp, _vp, ctypes.POINTER(ctypes.c_int), ctypes.c_int,
                                            ctypes.POINTER(_vp)]),
+    ("ckks_rotate_batch", ctypes.c_int, [_vp, ctypes.POINTER(_vp), ctypes.POINTER(ctypes.c_int), ctypes.c_int,
+                                         ctypes.POINTER(_vp)]),
+    ("ckks_mul_ct_batch", ctypes.c_int, [_vp, ctypes.POINTER(_vp), ctypes.POINTER(_vp), ctypes.c_int,
+                                         ctypes.POINTER(_vp)]),
+    ("ckks_rescale_batch", ctypes.c_int, [_vp, ctypes.POINTER(_vp), ctypes.c_int, ctypes.POINTER(_vp)]),
     ("ckks_accumulate_sum", ctypes.c_int, [_vp, _vp, ctypes.c_int, ctypes.c_int, _vp]),
     ("ckks_profile_enable", ctypes.c_int, [_vp, ctypes.c_int]),
     ("ckks_profile_reset", ctypes.c_int, [_vp]),
@@ -443,6 +448,26 @@ class CryptoContext:
         idx = (ctypes.c_int * len(indices))(*[int(i) for i in indices])
         hs = (_vp * len(indices))(*[o.h for o in outs])
         _check(lib().ckks_rotate_hoisted(self.h, ct.h, idx, len(indices), hs))
+        return outs
+
+    def rotate_batch(self, cts, ks) -> list[Ciphertext]:
+        outs = [self._new() for _ in cts]
+        n = len(cts)
+        _check(lib().ckks_rotate_batch(self.h, (_vp * n)(*[c.h for c in cts]), (ctypes.c_int * n)(*ks), n,
+                                       (_vp * n)(*[o.h for o in outs])))
+        return outs
+
+    def mul_ct_batch(self, a, b) -> list[Ciphertext]:
+        outs = [self._new() for _ in a]
+        n = len(a)
+        _check(lib().ckks_mul_ct_batch(self.h, (_vp * n)(*[c.h for c in a]), (_vp * n)(*[c.h for c in b]), n,
+                                       (_vp * n)(*[o.h for o in outs])))
+        return outs
+
+    def rescale_batch(self, cts) -> list[Ciphertext]:
+        outs = [self._new() for _ in cts]
+        n = len(cts)
+        _check(lib().ckks_rescale_batch(self.h, (_vp * n)(*[c.h for c in cts]), n, (_vp * n)(*[o.h for o in outs])))
         return outs
 
     def AccumulateSum(self, ct: Ciphertext, count: int, stride: int) -> Ciphertext:

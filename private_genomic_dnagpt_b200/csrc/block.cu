@@ -52,7 +52,6 @@ namespace blk {
 
 constexpr int kThreads = 256;
 constexpr int kMaxBaby = 32;
-constexpr int kGiantsPerBlock = 8;
 
 struct Shape {
   int T = 103, B = 32, D = 768, H = 12, HD = 64, MLP = 3072;
@@ -107,43 +106,51 @@ struct InnerPtrs {
   uint64_t* c1[kMaxBaby];
 };
 
-// inner_g = sum_j diag[g n1 + j] * baby_j for kGiantsPerBlock giant steps per
-// CTA: each baby residue is loaded once and feeds 2 x 8 MAC chains; the
-// diagonals stream from HBM once per product.
-__global__ void __launch_bounds__(kThreads) bsgs_inner_kernel(BabyPtrs babies, int n1,
-                                                              const uint64_t* __restrict__ diag, InnerPtrs out,
-                                                              int limbs, int logN, int n2,
-                                                              const ckks::Mod* __restrict__ mods) {
+// Encoded diagonals are stored tile-major, [limb][coefficient tile][diagonal]
+// [kThreads residues], so that one CTA of the product streams one contiguous
+// span: this transposes a chunk of plaintext-major encodings into place.
+__global__ void __launch_bounds__(kThreads) diag_tile_kernel(const uint64_t* __restrict__ src, int cnt, int d0,
+                                                             int ndiag, int limbs, int logN,
+                                                             uint64_t* __restrict__ dst) {
   const int N = 1 << logN;
-  const int n = blockIdx.x * kThreads + threadIdx.x;
-  if (n >= N) return;
-  const int l = blockIdx.y;
-  const int g0 = blockIdx.z * kGiantsPerBlock;
-  const size_t limb_off = (size_t)l * N + n;
-  ckks::U128 a0[kGiantsPerBlock], a1[kGiantsPerBlock];
-#pragma unroll
-  for (int i = 0; i < kGiantsPerBlock; ++i) a0[i] = a1[i] = ckks::U128{0, 0};
-  const size_t diag_stride = (size_t)limbs * N;
+  const int ntiles = N / kThreads;
+  const int tile = blockIdx.x, l = blockIdx.y, dd = blockIdx.z;
+  if (dd >= cnt) return;
+  const uint64_t v = src[((size_t)dd * limbs + l) * N + (size_t)tile * kThreads + threadIdx.x];
+  dst[(((size_t)l * ntiles + tile) * ndiag + (d0 + dd)) * kThreads + threadIdx.x] = v;
+}
+
+// inner_g = sum_j diag[g n1 + j] * baby_j.  One CTA = one giant step g, one
+// 256-coefficient tile of one limb; each thread owns two adjacent
+// coefficients (16-byte loads) and four 128-bit MAC chains, so the kernel
+// runs at full occupancy.  Consecutive CTAs share the tile, so the baby
+// residues they re-read stay in L2; each giant's 32 diagonals of the tile are
+// one contiguous 64 KiB span of the tile-major diagonal store.
+constexpr int kBsgsThreads = 128;
+
+__global__ void __launch_bounds__(kBsgsThreads) bsgs_inner_kernel(BabyPtrs babies, int n1,
+                                                                  const uint64_t* __restrict__ diag, InnerPtrs out,
+                                                                  int limbs, int logN, int n2,
+                                                                  const ckks::Mod* __restrict__ mods) {
+  const int N = 1 << logN;
+  const int g = blockIdx.x, tile = blockIdx.y, l = blockIdx.z;
+  const int c = 2 * threadIdx.x;  // coefficient within the tile
+  const size_t off = (size_t)l * N + (size_t)tile * kThreads + c;
+  const int ndiag = n1 * n2;
+  const uint64_t* dtile = diag + (((size_t)l * (N / kThreads) + tile) * ndiag + (size_t)g * n1) * kThreads + c;
+  ckks::U128 a00{0, 0}, a01{0, 0}, a10{0, 0}, a11{0, 0};
   for (int j = 0; j < n1; ++j) {
-    const uint64_t b0 = babies.c0[j][limb_off];
-    const uint64_t b1 = babies.c1[j][limb_off];
-#pragma unroll
-    for (int i = 0; i < kGiantsPerBlock; ++i) {
-      if (g0 + i < n2) {
-        const uint64_t dv = diag[(size_t)((g0 + i) * n1 + j) * diag_stride + limb_off];
-        ckks::mac_wide(a0[i], dv, b0);
-        ckks::mac_wide(a1[i], dv, b1);
-      }
-    }
+    const ulonglong2 b0 = *reinterpret_cast<const ulonglong2*>(babies.c0[j] + off);
+    const ulonglong2 b1 = *reinterpret_cast<const ulonglong2*>(babies.c1[j] + off);
+    const ulonglong2 dv = __ldg(reinterpret_cast<const ulonglong2*>(dtile + (size_t)j * kThreads));
+    ckks::mac_wide(a00, dv.x, b0.x);
+    ckks::mac_wide(a01, dv.y, b0.y);
+    ckks::mac_wide(a10, dv.x, b1.x);
+    ckks::mac_wide(a11, dv.y, b1.y);
   }
   const ckks::Mod m = mods[l];
-#pragma unroll
-  for (int i = 0; i < kGiantsPerBlock; ++i) {
-    if (g0 + i < n2) {
-      out.c0[g0 + i][limb_off] = ckks::reduce128(a0[i], m);
-      out.c1[g0 + i][limb_off] = ckks::reduce128(a1[i], m);
-    }
-  }
+  *reinterpret_cast<ulonglong2*>(out.c0[g] + off) = make_ulonglong2(ckks::reduce128(a00, m), ckks::reduce128(a01, m));
+  *reinterpret_cast<ulonglong2*>(out.c1[g] + off) = make_ulonglong2(ckks::reduce128(a10, m), ckks::reduce128(a11, m));
 }
 
 double now_s() {
@@ -176,14 +183,23 @@ struct ckks_block {
   std::map<std::string, double> seconds;
   double client_seconds = 0.0;
 
+  bool orphaned = false;
+
   ckks_block(ckks_ctx* c, const blk::Shape& shape) : ctx(c), cc(c), C(*c->c), s(shape) {}
-  ~ckks_block() {
+  // device resources; called once, by the destructor or by the context's
+  void release_device() {
+    if (orphaned) return;
     for (auto& kv : diags) C.release(kv.second.data);
+    diags.clear();
+    masks.clear();
     cudaFree(d_qkv);
     cudaFree(d_proj);
     cudaFree(d_fc);
     cudaFree(d_proj2);
+    d_qkv = d_proj = d_fc = d_proj2 = nullptr;
+    orphaned = true;
   }
+  ~ckks_block() { release_device(); }
 
   double S(int limbs) const { return C.scales[limbs]; }
 
@@ -286,9 +302,51 @@ struct ckks_block {
     return rs(cc.EvalAdd(a, b));
   }
 
-  // sum of the hd features of every head, left at the head's first feature
-  Ciphertext head_window_sum(Ciphertext h) {
-    for (int w = 1; w < s.HD; w <<= 1) h = add(h, rot(h, s.B * w));
+  // lane shifts of x for every delta in `deltas` (0 -> x brought to the
+  // shifted level): one hoisted ModUp for all 2 |deltas| rotations, batched
+  // masks, one batched rescale
+  std::map<int, Ciphertext> lane_shifts(const Ciphertext& x, const std::vector<int>& deltas, int target_limbs) {
+    std::map<int, Ciphertext> out;
+    std::vector<int> idx, ds;
+    for (int d : deltas) {
+      if (d == 0) {
+        out[0] = reduce_to(x, target_limbs);
+        continue;
+      }
+      ds.push_back(d);
+      idx.push_back(d);
+      idx.push_back(d - s.B);
+    }
+    if (ds.empty()) return out;
+    count["rotations"] += (long)idx.size();
+    const auto r = cc.EvalFastRotation(x, idx);
+    const int l = x->limbs();
+    std::vector<Ciphertext> sums;
+    for (size_t i = 0; i < ds.size(); ++i) {
+      const Ciphertext a = cc.EvalMult(r[2 * i], lane_plain(0, ds[i], true, l));
+      const Ciphertext b = cc.EvalMult(r[2 * i + 1], lane_plain(0, ds[i], false, l));
+      count["ct_plain"] += 2;
+      sums.push_back(cc.EvalAdd(a, b));
+    }
+    const auto rs_ = cc.RescaleBatch(sums);
+    for (size_t i = 0; i < ds.size(); ++i) out[ds[i]] = rs_[i];
+    return out;
+  }
+
+  // products a[i] * b[i], rescaled, batched
+  std::vector<Ciphertext> mul_ct_rs_batch(const std::vector<Ciphertext>& a, const std::vector<Ciphertext>& b) {
+    count["ct_ct"] += (long)a.size();
+    return cc.RescaleBatch(cc.EvalMultBatch(a, b));
+  }
+
+  // sum of the hd features of every head, left at the head's first feature,
+  // for a batch of ciphertexts (rotations by B*2^i, batched per step)
+  std::vector<Ciphertext> head_window_sums(std::vector<Ciphertext> h) {
+    for (int w = 1; w < s.HD; w <<= 1) {
+      count["rotations"] += (long)h.size();
+      const auto r = cc.EvalRotateBatch(h, std::vector<int>(h.size(), s.B * w));
+      for (size_t i = 0; i < h.size(); ++i) h[i] = add(h[i], r[i]);
+    }
     return h;
   }
 
@@ -342,14 +400,19 @@ struct ckks_block {
     dg.data = (uint64_t*)C.alloc(sizeof(uint64_t) * nd * stride);
     const int chunk = 128;
     double* vals = (double*)C.alloc(sizeof(double) * (size_t)chunk * slots);
+    uint64_t* enc = (uint64_t*)C.alloc(sizeof(uint64_t) * (size_t)chunk * stride);
     for (int d0 = 0; d0 < nd; d0 += chunk) {
       const int cnt = std::min(chunk, nd - d0);
       blk::diag_values_kernel<<<dim3((slots + blk::kThreads - 1) / blk::kThreads, cnt), blk::kThreads, 0,
                                   C.stream>>>(W, od, id_, ld, s.PW, s.B, s.n1, d0, vals);
       CKKS_CUDA(cudaGetLastError());
-      ckks::encode_batch(C, vals, cnt, limbs, dg.scale, dg.data + (size_t)d0 * stride, stride, C.stream);
+      ckks::encode_batch(C, vals, cnt, limbs, dg.scale, enc, stride, C.stream);
+      blk::diag_tile_kernel<<<dim3(C.N / blk::kThreads, limbs, cnt), blk::kThreads, 0, C.stream>>>(
+          enc, cnt, d0, nd, limbs, C.logN, dg.data);
+      CKKS_CUDA(cudaGetLastError());
     }
     C.release(vals);
+    C.release(enc);
     seconds["diagonal_encode"] += blk::now_s() - t0;
     return diags.emplace(key, dg).first->second;
   }
@@ -394,14 +457,19 @@ struct ckks_block {
       ckks::ProfScope ps(C, "bsgs_inner",
                          ((double)s.n1 * s.n2 * limbs + 2.0 * s.n1 * limbs + 2.0 * s.n2 * limbs) * C.limb_bytes(),
                          C.stream);
-      const dim3 grid((C.N + blk::kThreads - 1) / blk::kThreads, limbs,
-                      (s.n2 + blk::kGiantsPerBlock - 1) / blk::kGiantsPerBlock);
-      blk::bsgs_inner_kernel<<<grid, blk::kThreads, 0, C.stream>>>(bp, s.n1, dg.data, ip, limbs, C.logN, s.n2,
-                                                                   C.d_mods);
+      const dim3 grid(s.n2, C.N / blk::kThreads, limbs);
+      blk::bsgs_inner_kernel<<<grid, blk::kBsgsThreads, 0, C.stream>>>(bp, s.n1, dg.data, ip, limbs, C.logN, s.n2,
+                                                                       C.d_mods);
     }
     CKKS_CUDA(cudaGetLastError());
+    // giant-step rotations of the n2 - 1 inner sums, batched
+    std::vector<Ciphertext> gin(inner.begin() + 1, inner.end());
+    std::vector<int> gk;
+    for (int g = 1; g < s.n2; ++g) gk.push_back(s.B * s.n1 * g);
+    count["rotations"] += (long)gk.size();
+    const auto grot = cc.EvalRotateBatch(gin, gk);
     Ciphertext acc = inner[0];
-    for (int g = 1; g < s.n2; ++g) acc = add(acc, rot(inner[g], s.B * s.n1 * g));
+    for (const auto& r : grot) acc = add(acc, r);
     return rs(acc);
   }
 
@@ -456,6 +524,12 @@ void ckks_block::forward(const double* x, int T, double* y) {
     xin[g] = client_encrypt(v, LX);
   }
   stamp("encrypt_inputs", t);
+  // device-timed span from encrypted inputs resident to encrypted outputs
+  // resident (client refreshes included: the stream waits on them)
+  cudaEvent_t ev0, ev1;
+  CKKS_CUDA(cudaEventCreate(&ev0));
+  CKKS_CUDA(cudaEventCreate(&ev1));
+  CKKS_CUDA(cudaEventRecord(ev0, C.stream));
 
   // LN1 + QKV
   std::vector<Ciphertext> Q(G), K(G), V(G);
@@ -476,25 +550,33 @@ void ckks_block::forward(const double* x, int T, double* y) {
   for (int g = 0; g < G; ++g) Qr[g] = reduce_to(Q[g], lk);
   const double inv_sqrt_hd = 1.0 / std::sqrt((double)HD);
   for (int kg = 0; kg < G; ++kg) {
-    std::map<int, Ciphertext> ks;
+    std::vector<int> need;
     for (int qg = kg; qg < G; ++qg)
       for (int d : blk::active_shifts(T, B, qg, kg))
-        if (!ks.count(d)) ks[d] = d ? lane_shift(K[kg], d) : reduce_to(K[kg], lk);
+        if (std::find(need.begin(), need.end(), d) == need.end()) need.push_back(d);
+    auto ks = lane_shifts(K[kg], need, lk);
     count["cached_key_lane_shifts"] += (long)ks.size() - (ks.count(0) ? 1 : 0);
-    for (int qg = kg; qg < G; ++qg) {
+    std::vector<Ciphertext> qa, kb;
+    std::vector<std::pair<int, int>> tag;  // (query group, delta)
+    for (int qg = kg; qg < G; ++qg)
       for (int d : blk::active_shifts(T, B, qg, kg)) {
-        const Ciphertext prod = head_window_sum(mul_ct_rs(Qr[qg], ks[d]));
-        const std::vector<double> v = client_decrypt(prod);
-        ++count["score_tile_decryptions"];
-        ++count["client_round_trips"];
-        for (int ql = 0; ql < s.count(qg); ++ql) {
-          const int kl = (ql + d) % B;
-          const int q = qg * B + ql, k = kg * B + kl;
-          if (kl >= s.count(kg) || k > q) continue;
-          for (int h = 0; h < H; ++h) {
-            scores[q][h][k] = v[(size_t)(h * HD) * B + ql] * inv_sqrt_hd;
-            ++count["client_logical_instances"];
-          }
+        qa.push_back(Qr[qg]);
+        kb.push_back(ks[d]);
+        tag.emplace_back(qg, d);
+      }
+    const auto sums = head_window_sums(mul_ct_rs_batch(qa, kb));
+    for (size_t i = 0; i < sums.size(); ++i) {
+      const int qg = tag[i].first, d = tag[i].second;
+      const std::vector<double> v = client_decrypt(sums[i]);
+      ++count["score_tile_decryptions"];
+      ++count["client_round_trips"];
+      for (int ql = 0; ql < s.count(qg); ++ql) {
+        const int kl = (ql + d) % B;
+        const int q = qg * B + ql, k = kg * B + kl;
+        if (kl >= s.count(kg) || k > q) continue;
+        for (int h = 0; h < H; ++h) {
+          scores[q][h][k] = v[(size_t)(h * HD) * B + ql] * inv_sqrt_hd;
+          ++count["client_logical_instances"];
         }
       }
     }
@@ -519,11 +601,14 @@ void ckks_block::forward(const double* x, int T, double* y) {
   // context: client weight tiles x shifted values (T123.cpp:838-860)
   std::vector<Ciphertext> ctx(G);
   for (int kg = 0; kg < G; ++kg) {
-    std::map<int, Ciphertext> vs;
+    std::vector<int> need;
     for (int qg = kg; qg < G; ++qg)
       for (int d : blk::active_shifts(T, B, qg, kg))
-        if (!vs.count(d)) vs[d] = d ? lane_shift(V[kg], d) : reduce_to(V[kg], lk);
+        if (std::find(need.begin(), need.end(), d) == need.end()) need.push_back(d);
+    auto vs = lane_shifts(V[kg], need, lk);
     count["cached_value_lane_shifts"] += (long)vs.size() - (vs.count(0) ? 1 : 0);
+    std::vector<Ciphertext> wa, vb;
+    std::vector<int> qtag;
     for (int qg = kg; qg < G; ++qg) {
       for (int d : blk::active_shifts(T, B, qg, kg)) {
         std::vector<double> w((size_t)PW * B, 0.0);
@@ -533,12 +618,17 @@ void ckks_block::forward(const double* x, int T, double* y) {
           if (kl >= s.count(kg) || k > q) continue;
           for (int f = 0; f < D; ++f) w[(size_t)f * B + ql] = prob[q][f / HD][k];
         }
-        const Ciphertext wt = client_encrypt(w, lk);
+        wa.push_back(client_encrypt(w, lk));
         ++count["weight_tile_encryptions"];
         ++count["client_round_trips"];
-        const Ciphertext c = mul_ct_rs(wt, vs[d]);
-        ctx[qg] = ctx[qg] ? add(ctx[qg], c) : c;
+        vb.push_back(vs[d]);
+        qtag.push_back(qg);
       }
+    }
+    const auto prods = mul_ct_rs_batch(wa, vb);
+    for (size_t i = 0; i < prods.size(); ++i) {
+      const int qg = qtag[i];
+      ctx[qg] = ctx[qg] ? add(ctx[qg], prods[i]) : prods[i];
     }
   }
   stamp("context", t);
@@ -571,7 +661,15 @@ void ckks_block::forward(const double* x, int T, double* y) {
     }
     out[g] = add(reduce_to(r1, mlp->limbs()), mlp);
   }
+  CKKS_CUDA(cudaEventRecord(ev1, C.stream));
   stamp("oproj_ln2_mlp", t);
+  {
+    float ms = 0.f;
+    CKKS_CUDA(cudaEventElapsedTime(&ms, ev0, ev1));
+    seconds["evaluate_events"] = ms / 1e3;
+    cudaEventDestroy(ev0);
+    cudaEventDestroy(ev1);
+  }
 
   // client: decrypt and unpack (T123.cpp:1675-1694)
   for (int g = 0; g < G; ++g) {
@@ -585,6 +683,8 @@ void ckks_block::forward(const double* x, int T, double* y) {
   count["output_limbs"] = out[0]->limbs();
   count["input_limbs"] = LX;
 }
+
+void ckks::block_orphan(ckks_block* b) { b->release_device(); }
 
 namespace {
 template <typename F>
@@ -655,12 +755,23 @@ int ckks_block_create(ckks_ctx* ctx, const double* ln1, const double* attn_qkv, 
       delete b;
       throw;
     }
+    {
+      std::lock_guard<std::mutex> lk(ctx->mu);
+      ctx->blocks.insert(b);
+    }
     *out = b;
   });
 }
 
 int ckks_block_destroy(ckks_block* b) {
-  return bguard([&] { delete b; });
+  return bguard([&] {
+    if (!b) return;
+    if (!b->orphaned) {
+      std::lock_guard<std::mutex> lk(b->ctx->mu);
+      b->ctx->blocks.erase(b);
+    }
+    delete b;
+  });
 }
 
 int ckks_block_rotation_indices(const ckks_block* b, int* out, int cap) {
@@ -673,6 +784,7 @@ int ckks_block_rotation_indices(const ckks_block* b, int* out, int cap) {
 int ckks_block_forward(ckks_block* b, const double* x, int tokens, double* y) {
   return bguard([&] {
     if (!b || !x || !y) throw ckks::Error(CKKS_EARG, "null argument");
+    if (b->orphaned) throw ckks::Error(CKKS_ESTATE, "the block's context was destroyed");
     b->forward(x, tokens, y);
   });
 }

@@ -95,44 +95,159 @@ void ew_ct_ct(Context& c, ckks::EwOp op, const ckks_ct* a, const ckks_ct* b, ckk
   if (dst == &tmp) take(out->p, tmp);
 }
 
-// rotations of `a` by ks[0..n) into outs (fresh buffers, then moved)
+// rotations of `a` by ks[0..n) into outs: one shared ModUp, then the inner
+// products and ModDowns of up to 32 rotations per batched launch sequence
 void rotate_many(Context& c, const ckks_ct* a, const int* ks, int n, ckks_ct* const* outs) {
-  const int limbs = a->p.limbs, N = c.N, E = limbs + c.K;
-  const int beta = c.levels[limbs].beta;
+  const int limbs = a->p.limbs;
   std::vector<uint32_t> gs(n);
-  bool any = false;
   for (int r = 0; r < n; ++r) {
     gs[r] = c.galois(ks[r]);
-    if (gs[r] != 1u) {
-      any = true;
-      if (!c.rot_key(gs[r])) throw Error(CKKS_EKEY, "rotation key not generated for index " + std::to_string(ks[r]));
-    }
+    if (gs[r] != 1u && !c.rot_key(gs[r]))
+      throw Error(CKKS_EKEY, "rotation key not generated for index " + std::to_string(ks[r]));
   }
   std::vector<DevPoly> res(n);
-  uint64_t* ext = nullptr;
-  uint64_t* acc = nullptr;
-  if (any) {
-    ext = (uint64_t*)c.alloc(sizeof(uint64_t) * (size_t)beta * E * N);
-    acc = (uint64_t*)c.alloc(sizeof(uint64_t) * 2 * (size_t)E * N);
-    ckks::modup(c, a->p.poly(1), limbs, ext, c.stream);
-  }
+  ckks::KsBatch b{};
+  auto flush = [&] {
+    if (b.M) ckks::keyswitch_batch(c, limbs, b, true, c.stream);
+    b.M = 0;
+  };
   for (int r = 0; r < n; ++r) {
     res[r].ensure(&c, 2, limbs);
-    if (gs[r] == 1u) {
-      ckks::ew_binary(c, ckks::EwOp::Copy, a->p.data, stride(a->p), nullptr, 0, res[r].data, stride(res[r]), 2,
-                      limbs, c.stream);
-    } else {
-      ckks::ks_inner(c, ext, limbs, c.rot_key(gs[r]), gs[r], acc, c.stream);
-      ckks::moddown2(c, acc, limbs, a->p.poly(0), gs[r], nullptr, res[r].poly(0), res[r].poly(1), c.stream);
-    }
     res[r].limbs = limbs;
     res[r].scale = a->p.scale;
     res[r].deg = a->p.deg;
+    if (gs[r] == 1u) {
+      ckks::ew_binary(c, ckks::EwOp::Copy, a->p.data, stride(a->p), nullptr, 0, res[r].data, stride(res[r]), 2,
+                      limbs, c.stream);
+      continue;
+    }
+    const int m = b.M++;
+    b.d[m] = a->p.poly(1);
+    b.key[m] = c.rot_key(gs[r]);
+    b.g[m] = gs[r];
+    b.add0[m] = a->p.poly(0);
+    b.add1[m] = nullptr;
+    b.out0[m] = res[r].poly(0);
+    b.out1[m] = res[r].poly(1);
+    if (b.M == ckks::kKsBatch) flush();
   }
-  c.release(ext);
-  c.release(acc);
+  flush();
   for (int r = 0; r < n; ++r) {
     outs[r]->owner = a->owner;
+    take(outs[r]->p, res[r]);
+  }
+}
+
+// independent rotations in[i] by ks[i] (all at one limb count)
+void rotate_batch(Context& c, const ckks_ct* const* in, const int* ks, int n, ckks_ct* const* outs) {
+  if (n <= 0) return;
+  const int limbs = in[0]->p.limbs;
+  std::vector<DevPoly> res(n);
+  ckks::KsBatch b{};
+  auto flush = [&] {
+    if (b.M) ckks::keyswitch_batch(c, limbs, b, false, c.stream);
+    b.M = 0;
+  };
+  for (int r = 0; r < n; ++r) {
+    const ckks_ct* a = in[r];
+    if (a->p.limbs != limbs) throw Error(CKKS_ELEVEL, "batched rotations need one limb count");
+    const uint32_t g = c.galois(ks[r]);
+    res[r].ensure(&c, 2, limbs);
+    res[r].limbs = limbs;
+    res[r].scale = a->p.scale;
+    res[r].deg = a->p.deg;
+    if (g == 1u) {
+      ckks::ew_binary(c, ckks::EwOp::Copy, a->p.data, stride(a->p), nullptr, 0, res[r].data, stride(res[r]), 2,
+                      limbs, c.stream);
+      continue;
+    }
+    if (!c.rot_key(g)) throw Error(CKKS_EKEY, "rotation key not generated for index " + std::to_string(ks[r]));
+    const int m = b.M++;
+    b.d[m] = a->p.poly(1);
+    b.key[m] = c.rot_key(g);
+    b.g[m] = g;
+    b.add0[m] = a->p.poly(0);
+    b.add1[m] = nullptr;
+    b.out0[m] = res[r].poly(0);
+    b.out1[m] = res[r].poly(1);
+    if (b.M == ckks::kKsBatch) flush();
+  }
+  flush();
+  for (int r = 0; r < n; ++r) {
+    outs[r]->owner = in[r]->owner;
+    take(outs[r]->p, res[r]);
+  }
+}
+
+// tensor + relinearisation of (a[i], b[i]) pairs at one limb count
+void mul_ct_batch(Context& c, const ckks_ct* const* a, const ckks_ct* const* bb, int n, ckks_ct* const* outs) {
+  if (n <= 0) return;
+  if (!c.d_rlk) throw Error(CKKS_EKEY, "relinearisation key not generated");
+  const int limbs = a[0]->p.limbs, N = c.N;
+  const size_t S = (size_t)limbs * N;
+  std::vector<DevPoly> res(n);
+  std::vector<uint64_t*> dbuf;
+  ckks::KsBatch b{};
+  auto flush = [&] {
+    if (b.M) ckks::keyswitch_batch(c, limbs, b, false, c.stream);
+    b.M = 0;
+    for (uint64_t* p : dbuf) c.release(p);
+    dbuf.clear();
+  };
+  for (int r = 0; r < n; ++r) {
+    if (a[r]->p.limbs != limbs || bb[r]->p.limbs != limbs)
+      throw Error(CKKS_ELEVEL, "operands at different levels");
+    uint64_t* d = (uint64_t*)c.alloc(sizeof(uint64_t) * 3 * S);
+    dbuf.push_back(d);
+    ckks::tensor(c, a[r]->p.poly(0), a[r]->p.poly(1), bb[r]->p.poly(0), bb[r]->p.poly(1), d, d + S, d + 2 * S,
+                 limbs, c.stream);
+    res[r].ensure(&c, 2, limbs);
+    res[r].limbs = limbs;
+    res[r].scale = a[r]->p.scale * bb[r]->p.scale;
+    res[r].deg = a[r]->p.deg + bb[r]->p.deg;
+    const int m = b.M++;
+    b.d[m] = d + 2 * S;
+    b.key[m] = c.d_rlk;
+    b.g[m] = 1u;
+    b.add0[m] = d;
+    b.add1[m] = d + S;
+    b.out0[m] = res[r].poly(0);
+    b.out1[m] = res[r].poly(1);
+    if (b.M == ckks::kKsBatch) flush();
+  }
+  flush();
+  for (int r = 0; r < n; ++r) {
+    outs[r]->owner = a[r]->owner;
+    take(outs[r]->p, res[r]);
+  }
+}
+
+void rescale_many(Context& c, const ckks_ct* const* in, int n, ckks_ct* const* outs) {
+  if (n <= 0) return;
+  const int limbs = in[0]->p.limbs;
+  if (limbs < 2) throw Error(CKKS_ELEVEL, "no limb left to rescale");
+  std::vector<DevPoly> res(n);
+  ckks::RsBatch b{};
+  auto flush = [&] {
+    if (b.M) ckks::rescale_batch(c, limbs, b, c.stream);
+    b.M = 0;
+  };
+  for (int r = 0; r < n; ++r) {
+    if (in[r]->p.limbs != limbs) throw Error(CKKS_ELEVEL, "batched rescale needs one limb count");
+    res[r].ensure(&c, 2, limbs - 1);
+    res[r].limbs = limbs - 1;
+    res[r].scale = in[r]->p.scale / (double)c.moduli[limbs - 1];
+    res[r].deg = in[r]->p.deg > 1 ? in[r]->p.deg - 1 : 1;
+    const int m = b.M++;
+    b.in0[m] = in[r]->p.poly(0);
+    b.in1[m] = in[r]->p.poly(1);
+    b.out0[m] = res[r].poly(0);
+    b.out1[m] = res[r].poly(1);
+    if (b.M == ckks::kKsBatch) flush();
+  }
+  flush();
+  for (int r = 0; r < n; ++r) {
+    outs[r]->owner = in[r]->owner;
     take(outs[r]->p, res[r]);
   }
 }
@@ -169,7 +284,31 @@ int ckks_ctx_create(const ckks_params* params, ckks_ctx** out) {
 }
 
 int ckks_ctx_destroy(ckks_ctx* ctx) {
-  return guard([&] { delete ctx; });
+  return guard([&] {
+    if (!ctx) return;
+    {
+      std::lock_guard<std::mutex> lk(ctx->mu);
+      // ciphertexts and plaintexts first: a block's cached plaintexts are
+      // then already detached when the block releases them below
+      for (ckks_ct* t : ctx->cts) {
+        if (t->p.data && t->p.ctx) t->p.ctx->release(t->p.data);
+        t->p.data = nullptr;
+        t->p.ctx = nullptr;
+        t->owner = nullptr;
+      }
+      for (ckks_pt* t : ctx->pts) {
+        if (t->p.data && t->p.ctx) t->p.ctx->release(t->p.data);
+        t->p.data = nullptr;
+        t->p.ctx = nullptr;
+        t->owner = nullptr;
+      }
+      ctx->cts.clear();
+      ctx->pts.clear();
+      for (ckks_block* b : ctx->blocks) ckks::block_orphan(b);
+      ctx->blocks.clear();
+    }
+    delete ctx;
+  });
 }
 
 int ckks_ctx_info(const ckks_ctx* ctx, int* ring_dim, int* limbs, int* special, int* alpha) {
@@ -267,12 +406,23 @@ int ckks_ct_create(ckks_ctx* ctx, ckks_ct** out) {
     need(out != nullptr, CKKS_EARG, "null argument");
     auto* t = new ckks_ct;
     t->owner = ctx;
+    {
+      std::lock_guard<std::mutex> lk(ctx->mu);
+      ctx->cts.insert(t);
+    }
     *out = t;
   });
 }
 
 int ckks_ct_destroy(ckks_ct* ct) {
-  return guard([&] { delete ct; });
+  return guard([&] {
+    if (!ct) return;
+    if (ct->owner) {
+      std::lock_guard<std::mutex> lk(ct->owner->mu);
+      ct->owner->cts.erase(ct);
+    }
+    delete ct;
+  });
 }
 
 int ckks_pt_create(ckks_ctx* ctx, ckks_pt** out) {
@@ -281,12 +431,23 @@ int ckks_pt_create(ckks_ctx* ctx, ckks_pt** out) {
     need(out != nullptr, CKKS_EARG, "null argument");
     auto* t = new ckks_pt;
     t->owner = ctx;
+    {
+      std::lock_guard<std::mutex> lk(ctx->mu);
+      ctx->pts.insert(t);
+    }
     *out = t;
   });
 }
 
 int ckks_pt_destroy(ckks_pt* pt) {
-  return guard([&] { delete pt; });
+  return guard([&] {
+    if (!pt) return;
+    if (pt->owner) {
+      std::lock_guard<std::mutex> lk(pt->owner->mu);
+      pt->owner->pts.erase(pt);
+    }
+    delete pt;
+  });
 }
 
 int ckks_ct_level(const ckks_ct* ct) {
@@ -578,25 +739,48 @@ int ckks_mul_ct(ckks_ctx* ctx, const ckks_ct* a, const ckks_ct* b, ckks_ct* out)
     need(out && out->owner == ctx, CKKS_EARG, "bad output handle");
     need(c.d_rlk != nullptr, CKKS_EKEY, "relinearisation key not generated");
     need(a->p.limbs == b->p.limbs, CKKS_ELEVEL, "operands at different levels");
-    const int limbs = a->p.limbs, N = c.N, E = limbs + c.K;
-    const int beta = c.levels[limbs].beta;
-    const size_t S = (size_t)limbs * N;
-    uint64_t* d = (uint64_t*)c.alloc(sizeof(uint64_t) * 3 * S);
-    ckks::tensor(c, a->p.poly(0), a->p.poly(1), b->p.poly(0), b->p.poly(1), d, d + S, d + 2 * S, limbs, c.stream);
-    uint64_t* ext = (uint64_t*)c.alloc(sizeof(uint64_t) * (size_t)beta * E * N);
-    uint64_t* acc = (uint64_t*)c.alloc(sizeof(uint64_t) * 2 * (size_t)E * N);
-    ckks::modup(c, d + 2 * S, limbs, ext, c.stream);
-    ckks::ks_inner(c, ext, limbs, c.d_rlk, 1u, acc, c.stream);
-    DevPoly tmp;
-    tmp.ensure(&c, 2, limbs);
-    ckks::moddown2(c, acc, limbs, d, 1u, d + S, tmp.poly(0), tmp.poly(1), c.stream);
-    tmp.limbs = limbs;
-    tmp.scale = a->p.scale * b->p.scale;
-    tmp.deg = a->p.deg + b->p.deg;
-    c.release(d);
-    c.release(ext);
-    c.release(acc);
-    take(out->p, tmp);
+    const ckks_ct* as[1] = {a};
+    const ckks_ct* bs[1] = {b};
+    ckks_ct* os[1] = {out};
+    mul_ct_batch(c, as, bs, 1, os);
+  });
+}
+
+int ckks_mul_ct_batch(ckks_ctx* ctx, const ckks_ct* const* a, const ckks_ct* const* b, int count,
+                      ckks_ct* const* outs) {
+  return guard([&] {
+    Context& c = C(ctx);
+    need(count >= 0 && (count == 0 || (a && b && outs)), CKKS_EARG, "bad batch");
+    for (int i = 0; i < count; ++i) {
+      same_ctx(ctx, a[i]);
+      same_ctx(ctx, b[i]);
+      need(outs[i] && outs[i]->owner == ctx, CKKS_EARG, "bad output handle");
+    }
+    mul_ct_batch(c, a, b, count, outs);
+  });
+}
+
+int ckks_rotate_batch(ckks_ctx* ctx, const ckks_ct* const* in, const int* k, int count, ckks_ct* const* outs) {
+  return guard([&] {
+    Context& c = C(ctx);
+    need(count >= 0 && (count == 0 || (in && k && outs)), CKKS_EARG, "bad batch");
+    for (int i = 0; i < count; ++i) {
+      same_ctx(ctx, in[i]);
+      need(outs[i] && outs[i]->owner == ctx, CKKS_EARG, "bad output handle");
+    }
+    rotate_batch(c, in, k, count, outs);
+  });
+}
+
+int ckks_rescale_batch(ckks_ctx* ctx, const ckks_ct* const* in, int count, ckks_ct* const* outs) {
+  return guard([&] {
+    Context& c = C(ctx);
+    need(count >= 0 && (count == 0 || (in && outs)), CKKS_EARG, "bad batch");
+    for (int i = 0; i < count; ++i) {
+      same_ctx(ctx, in[i]);
+      need(outs[i] && outs[i]->owner == ctx, CKKS_EARG, "bad output handle");
+    }
+    rescale_many(c, in, count, outs);
   });
 }
 
@@ -605,15 +789,10 @@ int ckks_rescale(ckks_ctx* ctx, const ckks_ct* a, ckks_ct* out) {
     Context& c = C(ctx);
     same_ctx(ctx, a);
     need(out && out->owner == ctx, CKKS_EARG, "bad output handle");
-    const int limbs = a->p.limbs;
-    need(limbs >= 2, CKKS_ELEVEL, "no limb left to rescale");
-    DevPoly tmp;
-    tmp.ensure(&c, 2, limbs - 1);
-    ckks::rescale(c, a->p.data, stride(a->p), 2, limbs, tmp.data, stride(tmp), c.stream);
-    tmp.limbs = limbs - 1;
-    tmp.scale = a->p.scale / (double)c.moduli[limbs - 1];
-    tmp.deg = a->p.deg > 1 ? a->p.deg - 1 : 1;
-    take(out->p, tmp);
+    need(a->p.limbs >= 2, CKKS_ELEVEL, "no limb left to rescale");
+    const ckks_ct* as[1] = {a};
+    ckks_ct* os[1] = {out};
+    rescale_many(c, as, 1, os);
   });
 }
 

@@ -47,6 +47,7 @@ struct LimbMap {
   int skip_alpha;
   int q0 = 0;  // first Q prime of each polynomial (rescale transforms limb l-1 alone)
   int skip_q = 0;  // nonzero: skip every Q limb (transform only the special limbs)
+  int skip_beta = 0;  // >0: polynomial p is digit p % skip_beta of its item (batched ModUp)
   __host__ __device__ int prime(int limb) const {
     const int t = limb % nper;
     return t < lq ? q0 + t : L + (t - lq);
@@ -55,14 +56,14 @@ struct LimbMap {
     if (skip_q && limb % nper < lq) return true;
     if (skip_alpha <= 0) return false;
     const int p = limb / nper, t = limb % nper;
-    const int lo = p * skip_alpha;
+    const int lo = (skip_beta > 0 ? p % skip_beta : p) * skip_alpha;
     const int hi = (lo + skip_alpha < lq) ? lo + skip_alpha : lq;
     return t >= lo && t < hi;
   }
-  static LimbMap q(int lq, int L) { return {lq, lq, L, 0, 0, 0}; }
-  static LimbMap ext(int lq, int K, int L) { return {lq + K, lq, L, 0, 0, 0}; }
-  static LimbMap ponly(int K, int L) { return {K, 0, L, 0, 0, 0}; }
-  static LimbMap single(int prime) { return {1, 1, 0, 0, prime, 0}; }
+  static LimbMap q(int lq, int L) { return {lq, lq, L, 0, 0, 0, 0}; }
+  static LimbMap ext(int lq, int K, int L) { return {lq + K, lq, L, 0, 0, 0, 0}; }
+  static LimbMap ponly(int K, int L) { return {K, 0, L, 0, 0, 0, 0}; }
+  static LimbMap single(int prime) { return {1, 1, 0, 0, prime, 0, 0}; }
 };
 
 struct Params {
@@ -234,6 +235,37 @@ void ks_inner(const Context& c, const uint64_t* ext, int limbs, const uint64_t* 
 // when given; acc holds 2 polys of limbs+K limbs and is consumed
 void moddown2(const Context& c, uint64_t* acc, int limbs, const uint64_t* add0, uint32_t g_add0,
               const uint64_t* add1, uint64_t* out0, uint64_t* out1, cudaStream_t st);
+// Batched key switching: up to kKsBatch independent switches at one limb
+// count in one launch sequence (ModUp, inner product, ModDown each a single
+// launch over the batch).  Item m switches d[m] with key[m]; the ModUp digits
+// are permuted by g[m] on read (1 = none); out0[m] = ModDown(acc0) +
+// add0[m][pi_g(n)], out1[m] = ModDown(acc1) + add1[m] (addends optional).
+// With shared_input every item switches d[0] and one ModUp serves all
+// (hoisted rotations).
+constexpr int kKsBatch = 32;
+struct KsBatch {
+  const uint64_t* d[kKsBatch];
+  const uint64_t* key[kKsBatch];
+  const uint64_t* add0[kKsBatch];
+  const uint64_t* add1[kKsBatch];
+  uint64_t* out0[kKsBatch];
+  uint64_t* out1[kKsBatch];
+  uint32_t g[kKsBatch];
+  int M;
+};
+void keyswitch_batch(const Context& c, int limbs, const KsBatch& b, bool shared_input, cudaStream_t st);
+
+// Batched rescale of M ciphertexts (c0, c1 pointers per item, `limbs` limbs
+// each) into outputs of limbs-1 limbs.
+struct RsBatch {
+  const uint64_t* in0[kKsBatch];
+  const uint64_t* in1[kKsBatch];
+  uint64_t* out0[kKsBatch];
+  uint64_t* out1[kKsBatch];
+  int M;
+};
+void rescale_batch(const Context& c, int limbs, const RsBatch& b, cudaStream_t st);
+
 // the same with caller-provided scratch: dc holds limbs*N words, conv 2*limbs*N
 void modup_with(const Context& c, const uint64_t* d_ntt, int limbs, uint64_t* ext, uint64_t* dc, cudaStream_t st);
 void moddown2_with(const Context& c, uint64_t* acc, int limbs, const uint64_t* add0, uint32_t g_add0,

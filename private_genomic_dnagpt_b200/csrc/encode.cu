@@ -222,7 +222,11 @@ void encode_batch(const Context& c, const double* d_values, int batch, int limbs
   round_kernel<<<g, kThreads, 0, st>>>(v, n, c.logN - 1, scale, out, out_stride, limbs, c.d_mods);
   CKKS_CUDA(cudaGetLastError());
   c.release(v);
-  for (int b = 0; b < batch; ++b) ntt_forward(c, out + (size_t)b * out_stride, limbs, LimbMap::q(limbs, c.L), st);
+  if (out_stride == (size_t)limbs * c.N) {
+    ntt_forward(c, out, batch * limbs, LimbMap::q(limbs, c.L), st);  // one launch pair for the batch
+  } else {
+    for (int b = 0; b < batch; ++b) ntt_forward(c, out + (size_t)b * out_stride, limbs, LimbMap::q(limbs, c.L), st);
+  }
 }
 
 void encode(const Context& c, const double* d_values, int limbs, double scale, uint64_t* out, cudaStream_t st) {

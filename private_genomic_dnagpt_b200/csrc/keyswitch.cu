@@ -363,4 +363,307 @@ void moddown2_with(const Context& c, uint64_t* acc, int limbs, const uint64_t* a
   CKKS_CUDA(cudaGetLastError());
 }
 
+// ---------------------------------------------------------------------------
+// Batched key switching and rescale (one launch per stage for a whole batch)
+// ---------------------------------------------------------------------------
+namespace {
+
+// dc[m] = d[m] (limbs limbs), ulonglong2 per thread
+__global__ void __launch_bounds__(kThreads) gather_kernel(KsBatch b, int limbs, int logN, uint64_t* __restrict__ dc) {
+  const int N = 1 << logN;
+  const int n = 2 * (blockIdx.x * kThreads + threadIdx.x);
+  if (n >= N) return;
+  const int l = blockIdx.y, m = blockIdx.z;
+  *reinterpret_cast<ulonglong2*>(dc + ((size_t)m * limbs + l) * N + n) =
+      *reinterpret_cast<const ulonglong2*>(b.d[m] + (size_t)l * N + n);
+}
+
+template <int MAXA>
+__global__ void __launch_bounds__(kThreads) modup_conv_batch_kernel(KsBatch b, const uint64_t* __restrict__ y_all,
+                                                                    uint64_t* __restrict__ ext_all, int limbs, int L,
+                                                                    int K, int alpha, int beta, int logN, int nchunks,
+                                                                    const Mod* __restrict__ mods,
+                                                                    const uint64_t* __restrict__ hat) {
+  const int N = 1 << logN;
+  const int n = 2 * (blockIdx.x * kThreads + threadIdx.x);
+  if (n >= N) return;
+  const int m = blockIdx.z;
+  const int j = blockIdx.y / nchunks, chunk = blockIdx.y % nchunks;
+  const int E = limbs + K;
+  const int lo = j * alpha;
+  const int hi = min(lo + alpha, limbs);
+  const int cnt = hi - lo;
+  const uint64_t* y = y_all + (size_t)m * limbs * N;
+  const uint64_t* d_ntt = b.d[m];
+  uint64_t* ej = ext_all + ((size_t)m * beta + j) * E * N;
+  ulonglong2 yv[MAXA];
+#pragma unroll
+  for (int i = 0; i < MAXA; ++i)
+    if (i < cnt) yv[i] = *reinterpret_cast<const ulonglong2*>(y + (size_t)(lo + i) * N + n);
+  if (chunk == 0) {
+    for (int i = lo; i < hi; ++i)
+      *reinterpret_cast<ulonglong2*>(ej + (size_t)i * N + n) =
+          *reinterpret_cast<const ulonglong2*>(d_ntt + (size_t)i * N + n);
+  }
+  const int others = E - cnt;
+#pragma unroll
+  for (int p = 0; p < kTargets; ++p) {
+    const int tt = chunk * kTargets + p;
+    if (tt >= others) break;
+    const int t = tt < lo ? tt : tt + cnt;
+    const int pt = t < limbs ? t : L + (t - limbs);
+    const uint64_t* h = hat + (size_t)j * alpha * E + t;
+    U128 a0{0, 0}, a1{0, 0};
+#pragma unroll
+    for (int i = 0; i < MAXA; ++i) {
+      if (i < cnt) {
+        const uint64_t hv = __ldg(h + (size_t)i * E);
+        mac_wide(a0, yv[i].x, hv);
+        mac_wide(a1, yv[i].y, hv);
+      }
+    }
+    const Mod md = mods[pt];
+    *reinterpret_cast<ulonglong2*>(ej + (size_t)t * N + n) = make_ulonglong2(reduce128(a0, md), reduce128(a1, md));
+  }
+}
+
+__global__ void __launch_bounds__(kThreads) ks_inner_batch_kernel(KsBatch b, const uint64_t* __restrict__ ext_all,
+                                                                  bool shared, uint64_t* __restrict__ acc_all,
+                                                                  int limbs, int L, int K, int P, int beta, int logN,
+                                                                  const Mod* __restrict__ mods) {
+  const int N = 1 << logN;
+  const int n = blockIdx.x * kThreads + threadIdx.x;
+  if (n >= N) return;
+  const int t = blockIdx.y, m = blockIdx.z;
+  const int E = limbs + K;
+  const int pt = t < limbs ? t : L + (t - limbs);
+  const Mod md = mods[pt];
+  const uint32_t g = b.g[m];
+  const uint64_t* ext = ext_all + (shared ? 0 : (size_t)m * beta * E * N);
+  const uint64_t* key = b.key[m];
+  const uint32_t src = (g == 1u) ? (uint32_t)n : auto_index((uint32_t)n, g, logN);
+  U128 s0{0, 0}, s1{0, 0};
+  for (int j = 0; j < beta; ++j) {
+    const uint64_t v = ext[((size_t)j * E + t) * N + src];
+    mac_wide(s0, v, key[((size_t)j * 2 * P + pt) * N + n]);
+    mac_wide(s1, v, key[((size_t)j * 2 * P + P + pt) * N + n]);
+  }
+  uint64_t* acc = acc_all + (size_t)m * 2 * E * N;
+  acc[(size_t)t * N + n] = reduce128(s0, md);
+  acc[((size_t)E + t) * N + n] = reduce128(s1, md);
+}
+
+template <int MAXK>
+__global__ void __launch_bounds__(kThreads) moddown_conv_batch_kernel(const uint64_t* __restrict__ acc_all,
+                                                                      uint64_t* __restrict__ conv_all, int limbs,
+                                                                      int L, int K, int logN, int nchunks,
+                                                                      const Mod* __restrict__ mods,
+                                                                      const uint64_t* __restrict__ phat) {
+  const int N = 1 << logN;
+  const int n = 2 * (blockIdx.x * kThreads + threadIdx.x);
+  if (n >= N) return;
+  const int m = blockIdx.z;
+  const int p = blockIdx.y / nchunks, chunk = blockIdx.y % nchunks;
+  const int E = limbs + K;
+  const uint64_t* xp = acc_all + ((size_t)(2 * m + p) * E + limbs) * N;
+  ulonglong2 yv[MAXK];
+#pragma unroll
+  for (int k = 0; k < MAXK; ++k)
+    if (k < K) yv[k] = *reinterpret_cast<const ulonglong2*>(xp + (size_t)k * N + n);
+  uint64_t* o = conv_all + (size_t)(2 * m + p) * limbs * N;
+#pragma unroll
+  for (int pp = 0; pp < kTargets; ++pp) {
+    const int t = chunk * kTargets + pp;
+    if (t >= limbs) break;
+    U128 a0{0, 0}, a1{0, 0};
+#pragma unroll
+    for (int k = 0; k < MAXK; ++k) {
+      if (k < K) {
+        const uint64_t hv = __ldg(phat + (size_t)k * limbs + t);
+        mac_wide(a0, yv[k].x, hv);
+        mac_wide(a1, yv[k].y, hv);
+      }
+    }
+    const Mod md = mods[t];
+    *reinterpret_cast<ulonglong2*>(o + (size_t)t * N + n) = make_ulonglong2(reduce128(a0, md), reduce128(a1, md));
+  }
+}
+
+__global__ void __launch_bounds__(kThreads) moddown_combine_batch_kernel(KsBatch b,
+                                                                        const uint64_t* __restrict__ acc_all,
+                                                                        const uint64_t* __restrict__ conv_all,
+                                                                        int limbs, int K, int logN,
+                                                                        const Mod* __restrict__ mods,
+                                                                        const ulonglong2* __restrict__ pinv) {
+  const int N = 1 << logN;
+  const int n = blockIdx.x * kThreads + threadIdx.x;
+  if (n >= N) return;
+  const int t = blockIdx.y % limbs, p = blockIdx.y / limbs, m = blockIdx.z;
+  const int E = limbs + K;
+  const uint64_t q = mods[t].q;
+  const ulonglong2 pv = pinv[t];
+  const uint64_t a = acc_all[((size_t)(2 * m + p) * E + t) * N + n];
+  const uint64_t cv = conv_all[((size_t)(2 * m + p) * limbs + t) * N + n];
+  uint64_t r = mul_shoup(sub_mod(a, cv, q), pv.x, pv.y, q);
+  if (p == 0) {
+    const uint64_t* add0 = b.add0[m];
+    if (add0) {
+      const uint32_t g = b.g[m];
+      const uint32_t src = (g == 1u) ? (uint32_t)n : auto_index((uint32_t)n, g, logN);
+      r = add_mod(r, add0[(size_t)t * N + src], q);
+    }
+    b.out0[m][(size_t)t * N + n] = r;
+  } else {
+    const uint64_t* add1 = b.add1[m];
+    if (add1) r = add_mod(r, add1[(size_t)t * N + n], q);
+    b.out1[m][(size_t)t * N + n] = r;
+  }
+}
+
+__global__ void __launch_bounds__(kThreads) rs_gather_last_kernel(RsBatch b, int limbs, int logN,
+                                                                  uint64_t* __restrict__ last) {
+  const int N = 1 << logN;
+  const int n = blockIdx.x * kThreads + threadIdx.x;
+  if (n >= N) return;
+  const int p = blockIdx.y, m = blockIdx.z;
+  const uint64_t* src = p ? b.in1[m] : b.in0[m];
+  last[(size_t)(2 * m + p) * N + n] = src[(size_t)(limbs - 1) * N + n];
+}
+
+__global__ void __launch_bounds__(kThreads) rs_spread_batch_kernel(const uint64_t* __restrict__ last,
+                                                                   uint64_t* __restrict__ tmp, int limbs, int logN,
+                                                                   const Mod* __restrict__ mods) {
+  const int N = 1 << logN;
+  const int n = blockIdx.x * kThreads + threadIdx.x;
+  if (n >= N) return;
+  const int lo = limbs - 1;
+  const int i = blockIdx.y % lo, p = blockIdx.y / lo, m = blockIdx.z;
+  const uint64_t v = last[(size_t)(2 * m + p) * N + n];
+  tmp[((size_t)(2 * m + p) * lo + i) * N + n] = reduce128(U128{v, 0}, mods[i]);
+}
+
+__global__ void __launch_bounds__(kThreads) rs_combine_batch_kernel(RsBatch b, const uint64_t* __restrict__ tmp,
+                                                                    int limbs, int logN, const Mod* __restrict__ mods,
+                                                                    const ulonglong2* __restrict__ inv) {
+  const int N = 1 << logN;
+  const int n = blockIdx.x * kThreads + threadIdx.x;
+  if (n >= N) return;
+  const int lo = limbs - 1;
+  const int i = blockIdx.y % lo, p = blockIdx.y / lo, m = blockIdx.z;
+  const uint64_t q = mods[i].q;
+  const ulonglong2 iv = inv[i];
+  const uint64_t* x = p ? b.in1[m] : b.in0[m];
+  uint64_t* o = p ? b.out1[m] : b.out0[m];
+  const uint64_t a = x[(size_t)i * N + n];
+  const uint64_t t = tmp[((size_t)(2 * m + p) * lo + i) * N + n];
+  o[(size_t)i * N + n] = mul_shoup(sub_mod(a, t, q), iv.x, iv.y, q);
+}
+
+}  // namespace
+
+void keyswitch_batch(const Context& c, int limbs, const KsBatch& b, bool shared, cudaStream_t st) {
+  if (c.alpha > kMaxAlpha || c.K > kMaxK) throw Error(kErrArgument, "digit size above 16 is not supported");
+  const int M = b.M;
+  if (M <= 0) return;
+  if (M > kKsBatch) throw Error(kErrArgument, "key-switch batch above 32");
+  const int N = c.N, E = limbs + c.K;
+  const LevelTables& lt = c.levels[limbs];
+  const int Mu = shared ? 1 : M;  // ModUp inputs
+  const double lb = c.limb_bytes();
+  uint64_t* dc = (uint64_t*)c.alloc(sizeof(uint64_t) * (size_t)Mu * limbs * N);
+  uint64_t* ext = (uint64_t*)c.alloc(sizeof(uint64_t) * (size_t)Mu * lt.beta * E * N);
+  uint64_t* acc = (uint64_t*)c.alloc(sizeof(uint64_t) * (size_t)M * 2 * E * N);
+  uint64_t* conv = (uint64_t*)c.alloc(sizeof(uint64_t) * (size_t)M * 2 * limbs * N);
+  // ModUp
+  {
+    ProfScope ps(c, "ks_gather", 2.0 * Mu * limbs * lb, st);
+    gather_kernel<<<dim3((N / 2 + kThreads - 1) / kThreads, limbs, Mu), kThreads, 0, st>>>(b, limbs, c.logN, dc);
+  }
+  ntt_inverse(c, dc, Mu * limbs, LimbMap::q(limbs, c.L), st, lt.d_up_scale_a, lt.d_up_scale_b);
+  const int min_cnt = limbs - (lt.beta - 1) * c.alpha;
+  const int nch_up = (E - min_cnt + kTargets - 1) / kTargets;
+  {
+    ProfScope ps(c, "modup_conv", Mu * (2.0 * limbs + (double)lt.beta * E) * lb, st);
+    auto kern = c.alpha <= 4 ? modup_conv_batch_kernel<4>
+                : c.alpha <= 8 ? modup_conv_batch_kernel<8>
+                : c.alpha <= 12 ? modup_conv_batch_kernel<12>
+                                : modup_conv_batch_kernel<16>;
+    kern<<<dim3((N / 2 + kThreads - 1) / kThreads, lt.beta * nch_up, Mu), kThreads, 0, st>>>(
+        b, dc, ext, limbs, c.L, c.K, c.alpha, lt.beta, c.logN, nch_up, c.d_mods, lt.d_up_hat);
+  }
+  CKKS_CUDA(cudaGetLastError());
+  {
+    LimbMap m = LimbMap::ext(limbs, c.K, c.L);
+    m.skip_alpha = c.alpha;
+    m.skip_beta = lt.beta;
+    ntt_forward(c, ext, Mu * lt.beta * E, m, st);
+  }
+  // key inner products
+  {
+    ProfScope ps(c, "ks_inner", M * (2.0 * lt.beta * E + 2.0 * E) * lb + Mu * (double)lt.beta * E * lb, st);
+    ks_inner_batch_kernel<<<dim3((N + kThreads - 1) / kThreads, E, M), kThreads, 0, st>>>(
+        b, ext, shared, acc, limbs, c.L, c.K, c.P, lt.beta, c.logN, c.d_mods);
+  }
+  CKKS_CUDA(cudaGetLastError());
+  // ModDown
+  {
+    LimbMap pm = LimbMap::ext(limbs, c.K, c.L);
+    pm.skip_q = 1;
+    ntt_inverse(c, acc, M * 2 * E, pm, st, c.d_down_scale_a, c.d_down_scale_b, c.L);
+  }
+  const int nch_dn = (limbs + kTargets - 1) / kTargets;
+  {
+    ProfScope ps(c, "moddown_conv", M * (2.0 * c.K + 2.0 * limbs) * lb, st);
+    auto kern = c.K <= 4 ? moddown_conv_batch_kernel<4>
+                : c.K <= 8 ? moddown_conv_batch_kernel<8>
+                : c.K <= 12 ? moddown_conv_batch_kernel<12>
+                            : moddown_conv_batch_kernel<16>;
+    kern<<<dim3((N / 2 + kThreads - 1) / kThreads, 2 * nch_dn, M), kThreads, 0, st>>>(
+        acc, conv, limbs, c.L, c.K, c.logN, nch_dn, c.d_mods, lt.d_down_phat);
+  }
+  CKKS_CUDA(cudaGetLastError());
+  ntt_forward(c, conv, M * 2 * limbs, LimbMap::q(limbs, c.L), st);
+  {
+    ProfScope ps(c, "moddown_combine", M * 8.0 * limbs * lb, st);
+    moddown_combine_batch_kernel<<<dim3((N + kThreads - 1) / kThreads, 2 * limbs, M), kThreads, 0, st>>>(
+        b, acc, conv, limbs, c.K, c.logN, c.d_mods, lt.d_down_pinv);
+  }
+  CKKS_CUDA(cudaGetLastError());
+  c.release(dc);
+  c.release(ext);
+  c.release(acc);
+  c.release(conv);
+}
+
+void rescale_batch(const Context& c, int limbs, const RsBatch& b, cudaStream_t st) {
+  if (limbs < 2) throw Error(kErrLevel, "cannot rescale a single-limb ciphertext");
+  const int M = b.M;
+  if (M <= 0) return;
+  if (M > kKsBatch) throw Error(kErrArgument, "rescale batch above 32");
+  const int N = c.N, lo = limbs - 1;
+  const LevelTables& lt = c.levels[limbs];
+  const double lb = c.limb_bytes();
+  uint64_t* last = (uint64_t*)c.alloc(sizeof(uint64_t) * (size_t)2 * M * N);
+  uint64_t* tmp = (uint64_t*)c.alloc(sizeof(uint64_t) * (size_t)2 * M * lo * N);
+  {
+    ProfScope ps(c, "rescale_gather", 4.0 * M * lb, st);
+    rs_gather_last_kernel<<<dim3((N + kThreads - 1) / kThreads, 2, M), kThreads, 0, st>>>(b, limbs, c.logN, last);
+  }
+  ntt_inverse(c, last, 2 * M, LimbMap::single(lo), st);
+  {
+    ProfScope ps(c, "rescale_spread", 2.0 * M * (1.0 + lo) * lb, st);
+    rs_spread_batch_kernel<<<dim3((N + kThreads - 1) / kThreads, 2 * lo, M), kThreads, 0, st>>>(last, tmp, limbs,
+                                                                                                 c.logN, c.d_mods);
+  }
+  ntt_forward(c, tmp, 2 * M * lo, LimbMap::q(lo, c.L), st);
+  {
+    ProfScope ps(c, "rescale_combine", 6.0 * M * lo * lb, st);
+    rs_combine_batch_kernel<<<dim3((N + kThreads - 1) / kThreads, 2 * lo, M), kThreads, 0, st>>>(
+        b, tmp, limbs, c.logN, c.d_mods, lt.d_rescale_inv);
+  }
+  CKKS_CUDA(cudaGetLastError());
+  c.release(last);
+  c.release(tmp);
+}
+
 }  // namespace ckks

@@ -277,3 +277,42 @@ def test_profiler_reports_every_rotation_kernel(pair10):
     # operations keep working after the profiler is switched off
     got = cc.EvalRotate(cx, 2)
     assert np.array_equal(got.limbs_array(), o.rotate(rx, 2))
+
+
+def test_batched_rotations_products_rescales_bit_exact(pair10):
+    """ckks_rotate_batch / ckks_mul_ct_batch / ckks_rescale_batch against the
+    oracle, with more items than one launch sequence carries (32)."""
+    o, cc = pair10
+    limbs = 5
+    keys = [1, 2, 3, 5, -1, -7, 8, 64, 100, 0]
+    items = [_fresh(o, cc, 100 + i, limbs) for i in range(37)]
+    ks = [keys[i % len(keys)] for i in range(37)]
+    outs = cc.rotate_batch([it[2] for it in items], ks)
+    for (x, rx, cx), k, out in zip(items, ks, outs):
+        assert np.array_equal(out.limbs_array(), o.rotate(rx, k))
+    prods = cc.mul_ct_batch([it[2] for it in items[:35]], [it[2] for it in items[1:36]])
+    for i, p in enumerate(prods):
+        assert np.array_equal(p.limbs_array(), o.mul_ct(items[i][1], items[i + 1][1]))
+    rs = cc.rescale_batch(prods)
+    for i, r in enumerate(rs):
+        assert np.array_equal(r.limbs_array(), o.rescale(o.mul_ct(items[i][1], items[i + 1][1])))
+    with pytest.raises(eng.CKKSError):  # one limb count per batch
+        cc.rotate_batch([items[0][2], _fresh(o, cc, 300, 3)[2]], [1, 1])
+
+
+def test_handles_survive_context_destruction_in_any_order():
+    """Destroying a context first orphans its ciphertexts, plaintexts and
+    blocks; releasing them afterwards (as a garbage collector may) is safe."""
+    import ctypes
+    cc = eng.GenCryptoContext(eng.CCParams(ring_dim_log=10, limbs=4, dnum=2, seed=3))
+    cc.KeyGen()
+    pt = cc.MakeCKKSPackedPlaintext(np.ones(8))
+    ct = cc.Encrypt(pt)
+    lib = eng.lib()
+    eng._check(lib.ckks_ctx_destroy(cc.h))
+    cc.h = None
+    # orphaned handles: destroy is a host-only release
+    assert lib.ckks_ct_destroy(ct.h) == 0
+    ct.h = None
+    assert lib.ckks_pt_destroy(pt.h) == 0
+    pt.h = None

@@ -20,12 +20,12 @@ int main() {
   auto cc = GenCryptoContext(p);
   cc->KeyGen();
   cc->EvalMultKeyGen();
-  cc->EvalRotateKeyGen({1, 2});
+  cc->EvalRotateKeyGen({1, 2, 3});  // AccumulateSum(4, 1) ladder: 1, 2, 3
   auto ct = cc->Encrypt(cc->MakeCKKSPackedPlaintext({1.0, 2.0, 3.0}));
   auto r = cc->EvalRotate(cc->EvalMult(ct, ct), 1);
   auto s = cc->AccumulateSum(cc->EvalAdd(r, 0.5), 4, 1);
   auto v = cc->Decrypt(cc->LevelReduce(s, 2))->GetRealPackedValue();
-  std::printf("%zu %u\n", v.size(), s->GetLevel());
+  std::printf("%zu %u %.9f\n", v.size(), s->GetLevel(), v[0]);
   return 0;
 }
 """
@@ -56,5 +56,8 @@ def test_cpp_layer_runs_on_the_gpu(tmp_path):
                     f"-Wl,-rpath,{os.path.dirname(lib)}"], check=True)
     r = subprocess.run([str(exe)], capture_output=True, text=True, timeout=120)
     assert r.returncode == 0, r.stderr
-    n, level = r.stdout.split()
-    assert int(n) == 2048 and int(level) >= 1
+    n, level, v0 = r.stdout.split()
+    # slots (1,2,3,0..) squared, rotated left by one, +0.5, summed over 4 slots:
+    # 4 + 9 + 0 + 0 + 4 * 0.5 = 15; the product is left unrescaled (level 0)
+    assert int(n) == 2048 and int(level) == 0
+    assert abs(float(v0) - 15.0) < 1e-6
