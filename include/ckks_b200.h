@@ -118,6 +118,13 @@ int ckks_decode(ckks_ctx* ctx, const ckks_pt* pt, double* out, int count);
 int ckks_encrypt(ckks_ctx* ctx, const ckks_pt* pt, ckks_ct* out);
 /* Decrypt(secretKey, ct, &pt) (T123.cpp:523, 1680) */
 int ckks_decrypt(ckks_ctx* ctx, const ckks_ct* ct, ckks_pt* out);
+/* Batched client role: `count` Encrypts of plaintexts at one limb count in
+ * one launch sequence (item i gets the counter the i-th of `count` successive
+ * ckks_encrypt calls would get), and `count` Decrypt + GetRealPackedValue
+ * into count x slots host doubles (the reference's client does these one
+ * ciphertext at a time, T123.cpp:514-715) */
+int ckks_encrypt_batch(ckks_ctx* ctx, const ckks_pt* const* pts, int count, ckks_ct* const* outs);
+int ckks_decrypt_decode_batch(ckks_ctx* ctx, const ckks_ct* const* cts, int count, double* out, int slots);
 /* the counter that selects the next encryption's randomness */
 int ckks_set_encrypt_counter(ckks_ctx* ctx, uint64_t counter);
 uint64_t ckks_get_encrypt_counter(const ckks_ctx* ctx);

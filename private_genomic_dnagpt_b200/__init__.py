@@ -94,6 +94,8 @@ _SIGS = [
     ("ckks_decode", ctypes.c_int, [_vp, _vp, _f64p, ctypes.c_int]),
     ("ckks_encrypt", ctypes.c_int, [_vp, _vp, _vp]),
     ("ckks_decrypt", ctypes.c_int, [_vp, _vp, _vp]),
+    ("ckks_encrypt_batch", ctypes.c_int, [_vp, ctypes.POINTER(_vp), ctypes.c_int, ctypes.POINTER(_vp)]),
+    ("ckks_decrypt_decode_batch", ctypes.c_int, [_vp, ctypes.POINTER(_vp), ctypes.c_int, _f64p, ctypes.c_int]),
     ("ckks_set_encrypt_counter", ctypes.c_int, [_vp, ctypes.c_uint64]),
     ("ckks_get_encrypt_counter", ctypes.c_uint64, [_vp]),
     ("ckks_add", ctypes.c_int, [_vp, _vp, _vp, _vp]),
@@ -343,6 +345,20 @@ class CryptoContext:
         pt = Plaintext(self)
         _check(lib().ckks_decrypt(self.h, ct.h, pt.h))
         return pt
+
+    def EncryptBatch(self, pts) -> list[Ciphertext]:
+        outs = [Ciphertext(self) for _ in pts]
+        n = len(pts)
+        _check(lib().ckks_encrypt_batch(self.h, (_vp * n)(*[p.h for p in pts]), n, (_vp * n)(*[o.h for o in outs])))
+        return outs
+
+    def DecryptDecodeBatch(self, cts, slots: int | None = None) -> np.ndarray:
+        n = len(cts)
+        k = self.slots if slots is None else slots
+        out = np.zeros((n, k), np.float64)
+        _check(lib().ckks_decrypt_decode_batch(self.h, (_vp * n)(*[c.h for c in cts]), n,
+                                               out.ctypes.data_as(_f64p), k))
+        return out
 
     def set_encrypt_counter(self, c: int):
         _check(lib().ckks_set_encrypt_counter(self.h, c))

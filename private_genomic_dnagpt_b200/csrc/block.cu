@@ -153,6 +153,95 @@ __global__ void __launch_bounds__(kBsgsThreads) bsgs_inner_kernel(BabyPtrs babie
   *reinterpret_cast<ulonglong2*>(out.c1[g] + off) = make_ulonglong2(ckks::reduce128(a10, m), ckks::reduce128(a11, m));
 }
 
+// ---- client-side float64 transforms, on the device ------------------------
+// (the reference computes these exactly in float64 on the host:
+//  1/sqrt T123.cpp:514-538, tanh-GELU :190-194/:540-568, softmax :629-665)
+__global__ void invsqrt_kernel(double* __restrict__ v, int n) {
+  const int i = blockIdx.x * kThreads + threadIdx.x;
+  if (i < n) v[i] = 1.0 / sqrt(v[i]);
+}
+
+// GELU on features < odim of lanes < count, zero elsewhere; item m = blockIdx.y
+__global__ void gelu_kernel(const double* __restrict__ in, double* __restrict__ out, int B, int odim, int count,
+                            int slots) {
+  const int i = blockIdx.x * kThreads + threadIdx.x;
+  if (i >= slots) return;
+  const size_t o = (size_t)blockIdx.y * slots + i;
+  const int f = i / B, t = i % B;
+  double r = 0.0;
+  if (f < odim && t < count) {
+    const double u = in[o];
+    r = 0.5 * u * (1.0 + tanh(0.7978845608028654 * (u + 0.044715 * u * u * u)));
+  }
+  out[o] = r;
+}
+
+// x [T, D] -> group g slot vectors (feature f, lane t) = x[g B + t][f]
+__global__ void pack_kernel(const double* __restrict__ x, double* __restrict__ vals, int T, int D, int B, int slots) {
+  const int i = blockIdx.x * kThreads + threadIdx.x;
+  if (i >= slots) return;
+  const int g = blockIdx.y, f = i / B, t = i % B, tok = g * B + t;
+  vals[(size_t)g * slots + i] = (f < D && tok < T) ? x[(size_t)tok * D + f] : 0.0;
+}
+
+__global__ void unpack_kernel(const double* __restrict__ vals, double* __restrict__ y, int T, int D, int B,
+                              int slots) {
+  const int i = blockIdx.x * kThreads + threadIdx.x;
+  if (i >= slots) return;
+  const int g = blockIdx.y, f = i / B, t = i % B, tok = g * B + t;
+  if (f < D && tok < T) y[(size_t)tok * D + f] = vals[(size_t)g * slots + i];
+}
+
+struct TileTag {
+  int qg, kg, d;
+};
+
+// score(q, k, head) from the head-window sums: feature head*HD, lane q - qg*B
+__global__ void score_gather_kernel(const double* __restrict__ vals, const TileTag* __restrict__ tags, int T, int H,
+                                    int HD, int B, int slots, double inv_sqrt_hd, double* __restrict__ scores) {
+  const int ql = threadIdx.x;  // one lane per thread, B <= blockDim
+  const int m = blockIdx.x, h = blockIdx.y;
+  if (ql >= B) return;
+  const TileTag tg = tags[m];
+  const int kl = (ql + tg.d) % B;
+  const int q = tg.qg * B + ql, k = tg.kg * B + kl;
+  if (q >= T || k >= T || k > q) return;
+  scores[((size_t)q * H + h) * T + k] = vals[(size_t)m * slots + (size_t)(h * HD) * B + ql] * inv_sqrt_hd;
+}
+
+// stable causal softmax of row (q, h) over k <= q; a missing score poisons the row
+__global__ void softmax_kernel(const double* __restrict__ scores, double* __restrict__ prob, int T, int H,
+                               int* __restrict__ bad) {
+  const int r = blockIdx.x * kThreads + threadIdx.x;
+  if (r >= T * H) return;
+  const int q = r / H;
+  const double* row = scores + (size_t)r * T;
+  double* out = prob + (size_t)r * T;
+  double mx = -INFINITY;
+  for (int k = 0; k <= q; ++k) {
+    if (!isfinite(row[k])) atomicExch(bad, 1);
+    mx = fmax(mx, row[k]);
+  }
+  double den = 0.0;
+  for (int k = 0; k <= q; ++k) den += exp(row[k] - mx);
+  for (int k = 0; k < T; ++k) out[k] = k <= q ? exp(row[k] - mx) / den : 0.0;
+}
+
+// weight tile of alignment m: (feature f, lane ql) = prob[q][f / HD][k]
+__global__ void weight_tile_kernel(const double* __restrict__ prob, const TileTag* __restrict__ tags, int T, int H,
+                                   int HD, int D, int B, int slots, double* __restrict__ vals) {
+  const int i = blockIdx.x * kThreads + threadIdx.x;
+  if (i >= slots) return;
+  const int m = blockIdx.y;
+  const TileTag tg = tags[m];
+  const int f = i / B, ql = i % B;
+  const int kl = (ql + tg.d) % B;
+  const int q = tg.qg * B + ql, k = tg.kg * B + kl;
+  double v = 0.0;
+  if (f < D && q < T && k < T && k <= q) v = prob[((size_t)q * H + f / HD) * T + k];
+  vals[(size_t)m * slots + i] = v;
+}
+
 double now_s() {
   return std::chrono::duration<double>(std::chrono::steady_clock::now().time_since_epoch()).count();
 }
@@ -203,19 +292,49 @@ struct ckks_block {
 
   double S(int limbs) const { return C.scales[limbs]; }
 
-  // ---- client role (T123.cpp:509-715) -------------------------------------
-  Ciphertext client_encrypt(const std::vector<double>& v, int limbs) {
+  // ---- client role (T123.cpp:509-715), batched on the device ---------------
+  // encode + encrypt M slot vectors held on the device (M x N/2 doubles)
+  std::vector<Ciphertext> client_encrypt(const double* dvals, int M, int limbs) {
     const double t0 = blk::now_s();
-    auto ct = cc.Encrypt(cc.MakePlaintextAt(v, limbs, S(limbs)));
+    const size_t stride = (size_t)limbs * C.N;
+    uint64_t* pt = (uint64_t*)C.alloc(sizeof(uint64_t) * (size_t)M * stride);
+    ckks::encode_batch(C, dvals, M, limbs, S(limbs), pt, stride, C.stream);
+    std::vector<Ciphertext> out(M);
+    std::vector<uint64_t*> c0(M), c1(M);
+    for (int m = 0; m < M; ++m) {
+      out[m] = cc.fresh();
+      ckks::DevPoly& p = out[m]->handle()->p;
+      p.ensure(&C, 2, limbs);
+      p.limbs = limbs;
+      p.scale = S(limbs);
+      p.deg = 1;
+      c0[m] = p.data;
+      c1[m] = p.data + (size_t)p.cap * C.N;
+    }
+    ckks::encrypt_batch(C, pt, limbs, M, c0.data(), c1.data(), C.stream);
+    C.release(pt);
     client_seconds += blk::now_s() - t0;
-    return ct;
+    return out;
   }
-  std::vector<double> client_decrypt(const Ciphertext& ct) {
+  // decrypt + decode ciphertexts of one limb count into M x N/2 doubles (device)
+  void client_decrypt(const std::vector<Ciphertext>& cts, double* dout) {
     const double t0 = blk::now_s();
-    auto v = cc.Decrypt(ct)->GetRealPackedValue();
+    const int M = (int)cts.size();
+    const int limbs = cts[0]->limbs();
+    std::vector<const uint64_t*> c0(M), c1(M);
+    std::vector<double> sc(M);
+    for (int m = 0; m < M; ++m) {
+      const ckks::DevPoly& p = cts[m]->handle()->p;
+      if (p.limbs != limbs || p.deg != 1) throw ckks::Error(CKKS_ESTATE, "client batch needs rescaled ciphertexts");
+      c0[m] = p.data;
+      c1[m] = p.data + (size_t)p.cap * C.N;
+      sc[m] = p.scale;
+    }
+    ckks::decrypt_decode_batch(C, c0.data(), c1.data(), limbs, M, sc.data(), dout, C.stream);
     client_seconds += blk::now_s() - t0;
-    return v;
   }
+  double* dbuf(size_t n) { return (double*)C.alloc(sizeof(double) * n); }
+  int slots() const { return s.PW * s.B; }
 
   // ---- server helpers -------------------------------------------------------
   Ciphertext rs(const Ciphertext& a) { return cc.Rescale(a); }
@@ -268,25 +387,33 @@ struct ckks_block {
     return cc.AccumulateSum(x, s.PW, s.B);
   }
 
-  // LayerNorm without the gain (folded into the next product): returns
-  // centered / sqrt(var + eps) at limbs(x) - 2 (T123.cpp:1168-1181)
-  Ciphertext layernorm(const Ciphertext& x, int active, const char* stage) {
-    const int lx = x->limbs();
+  // LayerNorm without the gain (folded into the next product), for a batch of
+  // token groups: the server computes centered and var + eps; the client
+  // returns 1/sqrt for every slot in one device batch; the server multiplies
+  // (T123.cpp:1168-1181).  Output at limbs(x) - 2.
+  std::vector<Ciphertext> layernorm(const std::vector<Ciphertext>& xs, const std::vector<int>& active) {
+    const int lx = xs[0]->limbs();
     std::vector<double> invd(s.PW, 0.0);
     for (int f = 0; f < s.D; ++f) invd[f] = 1.0 / s.D;
-    const Ciphertext mean = mul_pt_rs(feature_sum(x), feature_plain(1, invd, lx));
-    const Ciphertext centered = cc.EvalSub(reduce_to(x, lx - 1), mean);
-    const Ciphertext sq = mul_ct_rs(centered, centered);
-    Ciphertext var = mul_pt_rs(feature_sum(sq), feature_plain(1, invd, lx - 2));
-    var = cc.EvalAdd(var, 1e-5);
-    // client: exact inverse square root on every slot (T123.cpp:514-538)
-    std::vector<double> v = client_decrypt(var);
-    for (double& e : v) e = 1.0 / std::sqrt(e);
-    const Ciphertext inv = client_encrypt(v, lx - 1);
-    ++count["client_round_trips"];
-    count["client_logical_instances"] += active;
-    (void)stage;
-    return mul_ct_rs(centered, inv);
+    std::vector<Ciphertext> centered, sqs;
+    for (const auto& x : xs) {
+      const Ciphertext mean = mul_pt_rs(feature_sum(x), feature_plain(1, invd, lx));
+      centered.push_back(cc.EvalSub(reduce_to(x, lx - 1), mean));
+    }
+    count["ct_ct"] += (long)xs.size();
+    sqs = cc.RescaleBatch(cc.EvalMultBatch(centered, centered));
+    std::vector<Ciphertext> var;
+    for (const auto& sq : sqs) var.push_back(cc.EvalAdd(mul_pt_rs(feature_sum(sq), feature_plain(1, invd, lx - 2)), 1e-5));
+    const int M = (int)xs.size();
+    double* dv = dbuf((size_t)M * slots());
+    client_decrypt(var, dv);
+    blk::invsqrt_kernel<<<(M * slots() + blk::kThreads - 1) / blk::kThreads, blk::kThreads, 0, C.stream>>>(
+        dv, M * slots());
+    const auto inv = client_encrypt(dv, M, lx - 1);
+    C.release(dv);
+    count["client_round_trips"] += M;
+    for (int a : active) count["client_logical_instances"] += a;
+    return mul_ct_rs_batch(centered, inv);
   }
 
   // output[f, t] = input[f, (t + delta) mod B]: two rotations, two masks, one
@@ -504,6 +631,8 @@ std::vector<int> ckks_block::rotation_indices() const {
 void ckks_block::forward(const double* x, int T, double* y) {
   if (T != s.T) throw ckks::Error(CKKS_EARG, "token count differs from the block's");
   const int G = s.groups, B = s.B, D = s.D, PW = s.PW, H = s.H, HD = s.HD;
+  const int SL = slots();
+  const int nb = (SL + blk::kThreads - 1) / blk::kThreads;
   count.clear();
   seconds.clear();
   client_seconds = 0.0;
@@ -515,14 +644,16 @@ void ckks_block::forward(const double* x, int T, double* y) {
     t = n;
   };
   double t = t_start;
+  std::vector<int> active(G);
+  for (int g = 0; g < G; ++g) active[g] = s.count(g);
   // client: pack and encrypt the embeddings (T123.cpp:1642-1661)
-  std::vector<Ciphertext> xin(G);
-  for (int g = 0; g < G; ++g) {
-    std::vector<double> v((size_t)PW * B, 0.0);
-    for (int tl = 0; tl < s.count(g); ++tl)
-      for (int f = 0; f < D; ++f) v[(size_t)f * B + tl] = x[(size_t)(g * B + tl) * D + f];
-    xin[g] = client_encrypt(v, LX);
-  }
+  double* dx = dbuf((size_t)T * D);
+  CKKS_CUDA(cudaMemcpyAsync(dx, x, sizeof(double) * T * D, cudaMemcpyHostToDevice, C.stream));
+  double* dvals = dbuf((size_t)G * SL);
+  blk::pack_kernel<<<dim3(nb, G), blk::kThreads, 0, C.stream>>>(dx, dvals, T, D, B, SL);
+  const std::vector<Ciphertext> xin = client_encrypt(dvals, G, LX);
+  C.release(dvals);
+  C.release(dx);
   stamp("encrypt_inputs", t);
   // device-timed span from encrypted inputs resident to encrypted outputs
   // resident (client refreshes included: the stream waits on them)
@@ -533,133 +664,131 @@ void ckks_block::forward(const double* x, int T, double* y) {
 
   // LN1 + QKV
   std::vector<Ciphertext> Q(G), K(G), V(G);
-  for (int g = 0; g < G; ++g) {
-    const Ciphertext nrm = layernorm(xin[g], s.count(g), "ln1");
-    const auto baby = babies_of(nrm);
-    Q[g] = bsgs(baby, 0);
-    K[g] = bsgs(baby, 1);
-    V[g] = bsgs(baby, 2);
+  {
+    const auto nrm = layernorm(xin, active);
+    for (int g = 0; g < G; ++g) {
+      const auto baby = babies_of(nrm[g]);
+      Q[g] = bsgs(baby, 0);
+      K[g] = bsgs(baby, 1);
+      V[g] = bsgs(baby, 2);
+    }
   }
   stamp("ln1_qkv", t);
 
-  // scores
+  // scores: server products and head sums, client gathers them on the device
   const int lk = Q[0]->limbs() - 1;  // shifted key / value level
-  std::vector<std::vector<std::vector<double>>> scores(
-      T, std::vector<std::vector<double>>(H, std::vector<double>(T, std::nan(""))));
   std::vector<Ciphertext> Qr(G);
   for (int g = 0; g < G; ++g) Qr[g] = reduce_to(Q[g], lk);
+  double* d_scores = dbuf((size_t)T * H * T);
+  double* d_prob = dbuf((size_t)T * H * T);
+  CKKS_CUDA(cudaMemsetAsync(d_scores, 0xFF, sizeof(double) * T * H * T, C.stream));  // NaN = missing
+  std::vector<std::vector<blk::TileTag>> tags(G);
+  for (int kg = 0; kg < G; ++kg)
+    for (int qg = kg; qg < G; ++qg)
+      for (int d : blk::active_shifts(T, B, qg, kg)) tags[kg].push_back({qg, kg, d});
   const double inv_sqrt_hd = 1.0 / std::sqrt((double)HD);
   for (int kg = 0; kg < G; ++kg) {
     std::vector<int> need;
-    for (int qg = kg; qg < G; ++qg)
-      for (int d : blk::active_shifts(T, B, qg, kg))
-        if (std::find(need.begin(), need.end(), d) == need.end()) need.push_back(d);
+    for (const auto& tg : tags[kg])
+      if (std::find(need.begin(), need.end(), tg.d) == need.end()) need.push_back(tg.d);
     auto ks = lane_shifts(K[kg], need, lk);
     count["cached_key_lane_shifts"] += (long)ks.size() - (ks.count(0) ? 1 : 0);
     std::vector<Ciphertext> qa, kb;
-    std::vector<std::pair<int, int>> tag;  // (query group, delta)
-    for (int qg = kg; qg < G; ++qg)
-      for (int d : blk::active_shifts(T, B, qg, kg)) {
-        qa.push_back(Qr[qg]);
-        kb.push_back(ks[d]);
-        tag.emplace_back(qg, d);
-      }
-    const auto sums = head_window_sums(mul_ct_rs_batch(qa, kb));
-    for (size_t i = 0; i < sums.size(); ++i) {
-      const int qg = tag[i].first, d = tag[i].second;
-      const std::vector<double> v = client_decrypt(sums[i]);
-      ++count["score_tile_decryptions"];
-      ++count["client_round_trips"];
-      for (int ql = 0; ql < s.count(qg); ++ql) {
-        const int kl = (ql + d) % B;
-        const int q = qg * B + ql, k = kg * B + kl;
-        if (kl >= s.count(kg) || k > q) continue;
-        for (int h = 0; h < H; ++h) {
-          scores[q][h][k] = v[(size_t)(h * HD) * B + ql] * inv_sqrt_hd;
-          ++count["client_logical_instances"];
-        }
-      }
+    for (const auto& tg : tags[kg]) {
+      qa.push_back(Qr[tg.qg]);
+      kb.push_back(ks[tg.d]);
     }
+    const auto sums = head_window_sums(mul_ct_rs_batch(qa, kb));
+    const int M = (int)sums.size();
+    double* dv = dbuf((size_t)M * SL);
+    client_decrypt(sums, dv);
+    blk::TileTag* dt = (blk::TileTag*)C.alloc(sizeof(blk::TileTag) * M);
+    CKKS_CUDA(cudaMemcpyAsync(dt, tags[kg].data(), sizeof(blk::TileTag) * M, cudaMemcpyHostToDevice, C.stream));
+    blk::score_gather_kernel<<<dim3(M, H), 32 * ((B + 31) / 32), 0, C.stream>>>(dv, dt, T, H, HD, B, SL, inv_sqrt_hd,
+                                                                              d_scores);
+    CKKS_CUDA(cudaGetLastError());
+    C.release(dt);
+    C.release(dv);
+    count["score_tile_decryptions"] += M;
+    count["client_round_trips"] += M;
   }
   stamp("scores", t);
   // client: exact causal softmax in float64 (T123.cpp:629-665)
-  const double tc = blk::now_s();
-  std::vector<std::vector<std::vector<double>>> prob(T, std::vector<std::vector<double>>(H, std::vector<double>(T, 0.0)));
-  for (int q = 0; q < T; ++q)
-    for (int h = 0; h < H; ++h) {
-      double mx = -INFINITY;
-      for (int k = 0; k <= q; ++k) {
-        if (!std::isfinite(scores[q][h][k])) throw ckks::Error(CKKS_ESTATE, "missing causal attention score");
-        mx = std::max(mx, scores[q][h][k]);
-      }
-      double den = 0.0;
-      for (int k = 0; k <= q; ++k) den += std::exp(scores[q][h][k] - mx);
-      for (int k = 0; k <= q; ++k) prob[q][h][k] = std::exp(scores[q][h][k] - mx) / den;
-    }
-  client_seconds += blk::now_s() - tc;
+  {
+    int* bad = (int*)C.alloc(sizeof(int));
+    CKKS_CUDA(cudaMemsetAsync(bad, 0, sizeof(int), C.stream));
+    blk::softmax_kernel<<<(T * H + blk::kThreads - 1) / blk::kThreads, blk::kThreads, 0, C.stream>>>(d_scores, d_prob,
+                                                                                                       T, H, bad);
+    int hbad = 0;
+    CKKS_CUDA(cudaMemcpyAsync(&hbad, bad, sizeof(int), cudaMemcpyDeviceToHost, C.stream));
+    CKKS_CUDA(cudaStreamSynchronize(C.stream));
+    C.release(bad);
+    if (hbad) throw ckks::Error(CKKS_ESTATE, "missing/non-finite causal attention score");
+    count["client_logical_instances"] += (long)H * T * (T + 1) / 2;
+  }
 
   // context: client weight tiles x shifted values (T123.cpp:838-860)
   std::vector<Ciphertext> ctx(G);
   for (int kg = 0; kg < G; ++kg) {
     std::vector<int> need;
-    for (int qg = kg; qg < G; ++qg)
-      for (int d : blk::active_shifts(T, B, qg, kg))
-        if (std::find(need.begin(), need.end(), d) == need.end()) need.push_back(d);
+    for (const auto& tg : tags[kg])
+      if (std::find(need.begin(), need.end(), tg.d) == need.end()) need.push_back(tg.d);
     auto vs = lane_shifts(V[kg], need, lk);
     count["cached_value_lane_shifts"] += (long)vs.size() - (vs.count(0) ? 1 : 0);
-    std::vector<Ciphertext> wa, vb;
-    std::vector<int> qtag;
-    for (int qg = kg; qg < G; ++qg) {
-      for (int d : blk::active_shifts(T, B, qg, kg)) {
-        std::vector<double> w((size_t)PW * B, 0.0);
-        for (int ql = 0; ql < s.count(qg); ++ql) {
-          const int kl = (ql + d) % B;
-          const int q = qg * B + ql, k = kg * B + kl;
-          if (kl >= s.count(kg) || k > q) continue;
-          for (int f = 0; f < D; ++f) w[(size_t)f * B + ql] = prob[q][f / HD][k];
-        }
-        wa.push_back(client_encrypt(w, lk));
-        ++count["weight_tile_encryptions"];
-        ++count["client_round_trips"];
-        vb.push_back(vs[d]);
-        qtag.push_back(qg);
-      }
-    }
+    const int M = (int)tags[kg].size();
+    double* dv = dbuf((size_t)M * SL);
+    blk::TileTag* dt = (blk::TileTag*)C.alloc(sizeof(blk::TileTag) * M);
+    CKKS_CUDA(cudaMemcpyAsync(dt, tags[kg].data(), sizeof(blk::TileTag) * M, cudaMemcpyHostToDevice, C.stream));
+    blk::weight_tile_kernel<<<dim3(nb, M), blk::kThreads, 0, C.stream>>>(d_prob, dt, T, H, HD, D, B, SL, dv);
+    CKKS_CUDA(cudaGetLastError());
+    const auto wa = client_encrypt(dv, M, lk);
+    C.release(dt);
+    C.release(dv);
+    count["weight_tile_encryptions"] += M;
+    count["client_round_trips"] += M;
+    std::vector<Ciphertext> vb;
+    for (const auto& tg : tags[kg]) vb.push_back(vs[tg.d]);
     const auto prods = mul_ct_rs_batch(wa, vb);
-    for (size_t i = 0; i < prods.size(); ++i) {
-      const int qg = qtag[i];
+    for (int i = 0; i < M; ++i) {
+      const int qg = tags[kg][i].qg;
       ctx[qg] = ctx[qg] ? add(ctx[qg], prods[i]) : prods[i];
     }
   }
+  C.release(d_scores);
+  C.release(d_prob);
   stamp("context", t);
 
   // O projection, residual, LN2, MLP
-  std::vector<Ciphertext> out(G);
+  std::vector<Ciphertext> r1(G);
   for (int g = 0; g < G; ++g) {
     const Ciphertext o = bsgs(babies_of(ctx[g]), 3);
-    const Ciphertext r1 = add(reduce_to(xin[g], o->limbs()), o);
-    const Ciphertext n2 = layernorm(r1, s.count(g), "ln2");
-    const auto fb = babies_of(n2);
-    const int gelu_limbs = 3;
+    r1[g] = add(reduce_to(xin[g], o->limbs()), o);
+  }
+  const auto n2 = layernorm(r1, active);
+  std::vector<Ciphertext> out(G);
+  const int gelu_limbs = 3;
+  for (int g = 0; g < G; ++g) {
+    const auto fb = babies_of(n2[g]);
+    std::vector<Ciphertext> hc;
+    for (int c = 0; c < nfc; ++c) hc.push_back(bsgs(fb, 4 + c));
+    // client: exact tanh-GELU on the active lanes (T123.cpp:540-568)
+    double* dv = dbuf((size_t)nfc * SL);
+    client_decrypt(hc, dv);
+    for (int c = 0; c < nfc; ++c) {
+      const int odim = std::min(PW, s.MLP - c * PW);
+      blk::gelu_kernel<<<dim3(nb, 1), blk::kThreads, 0, C.stream>>>(dv + (size_t)c * SL, dv + (size_t)c * SL, B, odim,
+                                                                    s.count(g), SL);
+      count["client_logical_instances"] += (long)odim * s.count(g);
+    }
+    const auto ge = client_encrypt(dv, nfc, gelu_limbs);
+    C.release(dv);
+    count["client_round_trips"] += nfc;
     Ciphertext mlp;
     for (int c = 0; c < nfc; ++c) {
-      const Ciphertext hc = bsgs(fb, 4 + c);
-      // client: exact tanh-GELU on the active lanes (T123.cpp:540-568)
-      std::vector<double> v = client_decrypt(hc);
-      std::vector<double> gv((size_t)PW * B, 0.0);
-      const int odim = std::min(PW, s.MLP - c * PW);
-      for (int f = 0; f < odim; ++f)
-        for (int tl = 0; tl < s.count(g); ++tl) {
-          const double u = v[(size_t)f * B + tl];
-          gv[(size_t)f * B + tl] = 0.5 * u * (1.0 + std::tanh(0.7978845608028654 * (u + 0.044715 * u * u * u)));
-        }
-      ++count["client_round_trips"];
-      count["client_logical_instances"] += (long)odim * s.count(g);
-      const Ciphertext ge = client_encrypt(gv, gelu_limbs);
-      const Ciphertext pc = bsgs(babies_of(ge), 4 + nfc + c);
+      const Ciphertext pc = bsgs(babies_of(ge[c]), 4 + nfc + c);
       mlp = c ? add(mlp, pc) : pc;
     }
-    out[g] = add(reduce_to(r1, mlp->limbs()), mlp);
+    out[g] = add(reduce_to(r1[g], mlp->limbs()), mlp);
   }
   CKKS_CUDA(cudaEventRecord(ev1, C.stream));
   stamp("oproj_ln2_mlp", t);
@@ -672,10 +801,15 @@ void ckks_block::forward(const double* x, int T, double* y) {
   }
 
   // client: decrypt and unpack (T123.cpp:1675-1694)
-  for (int g = 0; g < G; ++g) {
-    const std::vector<double> v = client_decrypt(out[g]);
-    for (int tl = 0; tl < s.count(g); ++tl)
-      for (int f = 0; f < D; ++f) y[(size_t)(g * B + tl) * D + f] = v[(size_t)f * B + tl];
+  {
+    double* dv = dbuf((size_t)G * SL);
+    client_decrypt(out, dv);
+    double* dy = dbuf((size_t)T * D);
+    blk::unpack_kernel<<<dim3(nb, G), blk::kThreads, 0, C.stream>>>(dv, dy, T, D, B, SL);
+    CKKS_CUDA(cudaMemcpyAsync(y, dy, sizeof(double) * T * D, cudaMemcpyDeviceToHost, C.stream));
+    CKKS_CUDA(cudaStreamSynchronize(C.stream));
+    C.release(dv);
+    C.release(dy);
   }
   stamp("decrypt_outputs", t);
   seconds["total"] = blk::now_s() - t_start;

@@ -623,6 +623,65 @@ int ckks_decrypt(ckks_ctx* ctx, const ckks_ct* ct, ckks_pt* out) {
   });
 }
 
+int ckks_encrypt_batch(ckks_ctx* ctx, const ckks_pt* const* pts, int count, ckks_ct* const* outs) {
+  return guard([&] {
+    Context& c = C(ctx);
+    need(count >= 0 && (count == 0 || (pts && outs)), CKKS_EARG, "bad batch");
+    if (!count) return;
+    const int limbs = pts[0]->p.limbs;
+    for (int i = 0; i < count; ++i) {
+      same_ctx(ctx, pts[i]);
+      need(pts[i]->p.limbs == limbs, CKKS_ELEVEL, "batched encryption needs one limb count");
+      need(outs[i] && outs[i]->owner == ctx, CKKS_EARG, "bad output handle");
+    }
+    const size_t S = (size_t)limbs * c.N;
+    uint64_t* buf = (uint64_t*)c.alloc(sizeof(uint64_t) * S * count);
+    for (int i = 0; i < count; ++i)
+      CKKS_CUDA(cudaMemcpyAsync(buf + (size_t)i * S, pts[i]->p.data, sizeof(uint64_t) * S, cudaMemcpyDeviceToDevice,
+                                c.stream));
+    std::vector<DevPoly> res(count);
+    std::vector<uint64_t*> c0(count), c1(count);
+    for (int i = 0; i < count; ++i) {
+      res[i].ensure(&c, 2, limbs);
+      res[i].limbs = limbs;
+      res[i].scale = pts[i]->p.scale;
+      res[i].deg = 1;
+      c0[i] = res[i].poly(0);
+      c1[i] = res[i].poly(1);
+    }
+    ckks::encrypt_batch(c, buf, limbs, count, c0.data(), c1.data(), c.stream);
+    c.release(buf);
+    for (int i = 0; i < count; ++i) take(outs[i]->p, res[i]);
+  });
+}
+
+int ckks_decrypt_decode_batch(ckks_ctx* ctx, const ckks_ct* const* cts, int count, double* out, int slots) {
+  return guard([&] {
+    Context& c = C(ctx);
+    need(count >= 0 && (count == 0 || (cts && out)), CKKS_EARG, "bad batch");
+    need(slots >= 0 && slots <= c.N / 2, CKKS_EARG, "more values than slots");
+    if (!count) return;
+    const int limbs = cts[0]->p.limbs;
+    std::vector<const uint64_t*> c0(count), c1(count);
+    std::vector<double> sc(count);
+    for (int i = 0; i < count; ++i) {
+      same_ctx(ctx, cts[i]);
+      need(cts[i]->p.limbs == limbs, CKKS_ELEVEL, "batched decryption needs one limb count");
+      c0[i] = cts[i]->p.poly(0);
+      c1[i] = cts[i]->p.poly(1);
+      sc[i] = cts[i]->p.scale;
+    }
+    const int n = c.N / 2;
+    double* dv = (double*)c.alloc(sizeof(double) * (size_t)n * count);
+    ckks::decrypt_decode_batch(c, c0.data(), c1.data(), limbs, count, sc.data(), dv, c.stream);
+    if (slots)
+      CKKS_CUDA(cudaMemcpy2DAsync(out, sizeof(double) * slots, dv, sizeof(double) * n, sizeof(double) * slots, count,
+                                  cudaMemcpyDeviceToHost, c.stream));
+    c.release(dv);
+    CKKS_CUDA(cudaStreamSynchronize(c.stream));
+  });
+}
+
 int ckks_set_encrypt_counter(ckks_ctx* ctx, uint64_t counter) {
   return guard([&] { C(ctx).enc_counter = counter; });
 }

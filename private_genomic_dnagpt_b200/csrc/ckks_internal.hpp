@@ -283,6 +283,15 @@ void decrypt(const Context& c, const uint64_t* c0, const uint64_t* c1, int limbs
 
 // canonical embedding
 void encode(const Context& c, const double* d_values, int limbs, double scale, uint64_t* out, cudaStream_t st);
+// client role, batched on the device: M ciphertexts (c0/c1 pointers, one limb
+// count) -> M x N/2 decoded doubles; M plaintexts [M][limbs][N] -> M fresh
+// encryptions with counters enc_counter .. enc_counter + M - 1
+void decrypt_decode_batch(const Context& c, const uint64_t* const* c0, const uint64_t* const* c1, int limbs, int M,
+                          const double* scales_host, double* out, cudaStream_t st);
+void encrypt_batch(Context& c, const uint64_t* pts, int limbs, int M, uint64_t* const* c0, uint64_t* const* c1,
+                   cudaStream_t st);
+void decode_contiguous_batch(const Context& c, uint64_t* pts, int use, int M, const double* scales, double* out,
+                             cudaStream_t st);
 // batch x (N/2) device values -> batch plaintexts of `limbs` limbs, out_stride words apart
 void encode_batch(const Context& c, const double* d_values, int batch, int limbs, double scale, uint64_t* out,
                   size_t out_stride, cudaStream_t st);

@@ -179,6 +179,56 @@ __global__ void __launch_bounds__(kThreads) crt_kernel(const uint64_t* __restric
   v[bit_reverse((uint32_t)j, logn)] = make_double2(d[0], d[1]);
 }
 
+// batched form: item m reads x + m*use*N with scale scales[m] and writes
+// v + m*n (bit-reversed positions)
+__global__ void __launch_bounds__(kThreads) crt_batch_kernel(const uint64_t* __restrict__ x_all, int use,
+                                                             const double* __restrict__ scales,
+                                                             double2* __restrict__ v_all, int n, int logn,
+                                                             const Mod* __restrict__ mods, ulonglong2 q0inv1) {
+  const int j = blockIdx.x * kThreads + threadIdx.x;
+  if (j >= n) return;
+  const int m = blockIdx.y;
+  const int N = 2 * n;
+  const uint64_t* x = x_all + (size_t)m * use * N;
+  const double scale = scales[m];
+  const Mod m0 = mods[0], m1 = mods[1];
+  double d[2];
+  for (int h = 0; h < 2; ++h) {
+    const int i = j + h * n;
+    U128 val, Q;
+    if (use == 2) {
+      const uint64_t x0 = x[i], x1 = x[(size_t)N + i];
+      const uint64_t t = mul_shoup(sub_mod(x1, reduce128(U128{x0, 0}, m1), m1.q), q0inv1.x, q0inv1.y, m1.q);
+      val = mul_wide(m0.q, t);
+      const uint64_t lo = val.lo + x0;
+      val.hi += lo < x0 ? 1ull : 0ull;
+      val.lo = lo;
+      Q = mul_wide(m0.q, m1.q);
+    } else {
+      val = U128{x[i], 0};
+      Q = U128{m0.q, 0};
+    }
+    const U128 half{(Q.lo >> 1) | (Q.hi << 63), Q.hi >> 1};
+    const bool neg = (val.hi > half.hi) || (val.hi == half.hi && val.lo > half.lo);
+    U128 mag = val;
+    if (neg) {
+      mag.lo = Q.lo - val.lo;
+      mag.hi = Q.hi - val.hi - (Q.lo < val.lo ? 1ull : 0ull);
+    }
+    double r = __dadd_rn(__dmul_rn(__ull2double_rn(mag.hi), 18446744073709551616.0), __ull2double_rn(mag.lo));
+    if (neg) r = -r;
+    d[h] = __ddiv_rn(r, scale);
+  }
+  v_all[(size_t)m * n + bit_reverse((uint32_t)j, logn)] = make_double2(d[0], d[1]);
+}
+
+__global__ void __launch_bounds__(kThreads) take_real_batch_kernel(const double2* __restrict__ v,
+                                                                   double* __restrict__ out, int n) {
+  const int j = blockIdx.x * kThreads + threadIdx.x;
+  if (j >= n) return;
+  out[(size_t)blockIdx.y * n + j] = v[(size_t)blockIdx.y * n + j].x;
+}
+
 __global__ void __launch_bounds__(kThreads) take_real_kernel(const double2* __restrict__ v, double* __restrict__ out,
                                                              int n) {
   const int j = blockIdx.x * kThreads + threadIdx.x;
@@ -231,6 +281,28 @@ void encode_batch(const Context& c, const double* d_values, int batch, int limbs
 
 void encode(const Context& c, const double* d_values, int limbs, double scale, uint64_t* out, cudaStream_t st) {
   encode_batch(c, d_values, 1, limbs, scale, out, (size_t)limbs * c.N, st);
+}
+
+void decode_contiguous_batch(const Context& c, uint64_t* pts, int use, int M, const double* scales, double* out,
+                             cudaStream_t st) {
+  const int n = c.N / 2;
+  ntt_inverse(c, pts, M * use, LimbMap::q(use, c.L), st);
+  double2* v = (double2*)c.alloc(sizeof(double2) * (size_t)M * n);
+  const uint64_t q0 = c.moduli[0], q1 = c.moduli[1];
+  unsigned __int128 inv = 1, b = q0 % q1;
+  for (uint64_t e = q1 - 2; e; e >>= 1) {
+    if (e & 1) inv = (inv * b) % q1;
+    b = (b * b) % q1;
+  }
+  const uint64_t iv = (uint64_t)inv;
+  const ulonglong2 q0inv1 = make_ulonglong2(iv, (uint64_t)(((unsigned __int128)iv << 64) / q1));
+  const dim3 g((n + kThreads - 1) / kThreads, M);
+  crt_batch_kernel<<<g, kThreads, 0, st>>>(pts, use, scales, v, n, c.logN - 1, c.d_mods, q0inv1);
+  CKKS_CUDA(cudaGetLastError());
+  fft_forward_batch(c, v, M, st);
+  take_real_batch_kernel<<<g, kThreads, 0, st>>>(v, out, n);
+  CKKS_CUDA(cudaGetLastError());
+  c.release(v);
 }
 
 void decode(const Context& c, const uint64_t* pt, int limbs, double scale, double* d_values, cudaStream_t st) {

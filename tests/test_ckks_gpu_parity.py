@@ -316,3 +316,21 @@ def test_handles_survive_context_destruction_in_any_order():
     ct.h = None
     assert lib.ckks_pt_destroy(pt.h) == 0
     pt.h = None
+
+
+def test_batched_client_encrypt_decrypt(pair10):
+    """ckks_encrypt_batch equals successive single encryptions of the oracle
+    (counter i for item i); ckks_decrypt_decode_batch equals single decodes."""
+    o, cc = pair10
+    rng = np.random.default_rng(21)
+    xs = [rng.uniform(-1, 1, o.N // 2) for _ in range(5)]
+    pts = [cc.MakeCKKSPackedPlaintext(x, level=2) for x in xs]
+    cc.set_encrypt_counter(500)
+    cts = cc.EncryptBatch(pts)
+    for i, (x, ct) in enumerate(zip(xs, cts)):
+        assert np.array_equal(ct.limbs_array(), o.encrypt(o.encode(x, o.L - 2), 500 + i))
+    dec = cc.DecryptDecodeBatch(cts)
+    for i, ct in enumerate(cts):
+        single = cc.Decrypt(ct).GetRealPackedValue()
+        assert np.abs(dec[i] - single).max() <= 1e-12
+        assert np.abs(dec[i] - xs[i]).max() < 1e-8
