@@ -133,6 +133,10 @@ uint64_t ckks_get_encrypt_counter(const ckks_ctx* ctx);
 int ckks_add(ckks_ctx* ctx, const ckks_ct* a, const ckks_ct* b, ckks_ct* out);
 int ckks_sub(ckks_ctx* ctx, const ckks_ct* a, const ckks_ct* b, ckks_ct* out);
 int ckks_add_pt(ckks_ctx* ctx, const ckks_ct* a, const ckks_pt* p, ckks_ct* out);
+/* EvalAddMany: sum of `count` ciphertexts at one level and scale; and
+ * `count` independent sums a[i] + b[i] in one launch sequence */
+int ckks_add_many(ckks_ctx* ctx, const ckks_ct* const* in, int count, ckks_ct* out);
+int ckks_add_batch(ckks_ctx* ctx, const ckks_ct* const* a, const ckks_ct* const* b, int count, ckks_ct* const* outs);
 /* EvalAdd(ct, double) (T123.cpp:1173): adds round(value * scale) to every slot */
 int ckks_add_scalar(ckks_ctx* ctx, const ckks_ct* a, double value, ckks_ct* out);
 /* EvalMult(ct, pt) (T123.cpp:1149-1152), no rescale */

@@ -199,6 +199,27 @@ class CryptoContextImpl {
     check(ckks_rotate_hoisted(h_, a->handle(), k.data(), (int)k.size(), hs.data()));
     return outs;
   }
+  // sum of many ciphertexts at one level and scale (EvalAddMany)
+  Ciphertext EvalAddMany(const std::vector<Ciphertext>& a) {
+    std::vector<const ckks_ct*> in;
+    for (const auto& x : a) in.push_back(x->handle());
+    auto o = fresh();
+    check(ckks_add_many(h_, in.data(), (int)in.size(), o->handle()));
+    return o;
+  }
+  std::vector<Ciphertext> EvalAddBatch(const std::vector<Ciphertext>& a, const std::vector<Ciphertext>& b) {
+    std::vector<Ciphertext> outs;
+    std::vector<const ckks_ct*> x, y;
+    std::vector<ckks_ct*> hs;
+    for (size_t i = 0; i < a.size(); ++i) {
+      outs.push_back(fresh());
+      x.push_back(a[i]->handle());
+      y.push_back(b[i]->handle());
+      hs.push_back(outs.back()->handle());
+    }
+    check(ckks_add_batch(h_, x.data(), y.data(), (int)a.size(), hs.data()));
+    return outs;
+  }
   // independent rotations / products / rescales at one limb count, batched
   std::vector<Ciphertext> EvalRotateBatch(const std::vector<Ciphertext>& a, const std::vector<int>& k) {
     std::vector<Ciphertext> outs;

@@ -101,6 +101,9 @@ _SIGS = [
     ("ckks_add", ctypes.c_int, [_vp, _vp, _vp, _vp]),
     ("ckks_sub", ctypes.c_int, [_vp, _vp, _vp, _vp]),
     ("ckks_add_pt", ctypes.c_int, [_vp, _vp, _vp, _vp]),
+    ("ckks_add_many", ctypes.c_int, [_vp, ctypes.POINTER(_vp), ctypes.c_int, _vp]),
+    ("ckks_add_batch", ctypes.c_int, [_vp, ctypes.POINTER(_vp), ctypes.POINTER(_vp), ctypes.c_int,
+                                      ctypes.POINTER(_vp)]),
     ("ckks_add_scalar", ctypes.c_int, [_vp, _vp, ctypes.c_double, _vp]),
     ("ckks_mul_pt", ctypes.c_int, [_vp, _vp, _vp, _vp]),
     ("ckks_mul_ct", ctypes.c_int, [_vp, _vp, _vp, _vp]),
@@ -464,6 +467,19 @@ class CryptoContext:
         idx = (ctypes.c_int * len(indices))(*[int(i) for i in indices])
         hs = (_vp * len(indices))(*[o.h for o in outs])
         _check(lib().ckks_rotate_hoisted(self.h, ct.h, idx, len(indices), hs))
+        return outs
+
+    def EvalAddMany(self, cts) -> Ciphertext:
+        o = self._new()
+        n = len(cts)
+        _check(lib().ckks_add_many(self.h, (_vp * n)(*[c.h for c in cts]), n, o.h))
+        return o
+
+    def add_batch(self, a, b) -> list[Ciphertext]:
+        outs = [self._new() for _ in a]
+        n = len(a)
+        _check(lib().ckks_add_batch(self.h, (_vp * n)(*[c.h for c in a]), (_vp * n)(*[c.h for c in b]), n,
+                                    (_vp * n)(*[o.h for o in outs])))
         return outs
 
     def rotate_batch(self, cts, ks) -> list[Ciphertext]:

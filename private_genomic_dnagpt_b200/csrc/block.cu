@@ -472,7 +472,7 @@ struct ckks_block {
     for (int w = 1; w < s.HD; w <<= 1) {
       count["rotations"] += (long)h.size();
       const auto r = cc.EvalRotateBatch(h, std::vector<int>(h.size(), s.B * w));
-      for (size_t i = 0; i < h.size(); ++i) h[i] = add(h[i], r[i]);
+      h = cc.EvalAddBatch(h, r);
     }
     return h;
   }
@@ -594,9 +594,9 @@ struct ckks_block {
     std::vector<int> gk;
     for (int g = 1; g < s.n2; ++g) gk.push_back(s.B * s.n1 * g);
     count["rotations"] += (long)gk.size();
-    const auto grot = cc.EvalRotateBatch(gin, gk);
-    Ciphertext acc = inner[0];
-    for (const auto& r : grot) acc = add(acc, r);
+    auto terms = cc.EvalRotateBatch(gin, gk);
+    terms.insert(terms.begin(), inner[0]);
+    const Ciphertext acc = cc.EvalAddMany(terms);
     return rs(acc);
   }
 
@@ -636,6 +636,8 @@ void ckks_block::forward(const double* x, int T, double* y) {
   count.clear();
   seconds.clear();
   client_seconds = 0.0;
+  const double alloc_s0 = C.alloc_seconds;
+  const long alloc_n0 = C.alloc_calls;
   const double t_start = blk::now_s();
   auto stamp = [&](const char* k, double& t) {
     cc.Synchronize();
@@ -749,9 +751,12 @@ void ckks_block::forward(const double* x, int T, double* y) {
     std::vector<Ciphertext> vb;
     for (const auto& tg : tags[kg]) vb.push_back(vs[tg.d]);
     const auto prods = mul_ct_rs_batch(wa, vb);
-    for (int i = 0; i < M; ++i) {
-      const int qg = tags[kg][i].qg;
-      ctx[qg] = ctx[qg] ? add(ctx[qg], prods[i]) : prods[i];
+    for (int qg = kg; qg < G; ++qg) {
+      std::vector<Ciphertext> terms;
+      if (ctx[qg]) terms.push_back(ctx[qg]);
+      for (int i = 0; i < M; ++i)
+        if (tags[kg][i].qg == qg) terms.push_back(prods[i]);
+      if (!terms.empty()) ctx[qg] = terms.size() == 1 ? terms[0] : cc.EvalAddMany(terms);
     }
   }
   C.release(d_scores);
@@ -814,6 +819,9 @@ void ckks_block::forward(const double* x, int T, double* y) {
   stamp("decrypt_outputs", t);
   seconds["total"] = blk::now_s() - t_start;
   seconds["client"] = client_seconds;
+  seconds["alloc_host"] = C.alloc_seconds - alloc_s0;
+  count["alloc_calls"] = C.alloc_calls - alloc_n0;
+
   count["output_limbs"] = out[0]->limbs();
   count["input_limbs"] = LX;
 }

@@ -708,6 +708,84 @@ int ckks_sub(ckks_ctx* ctx, const ckks_ct* a, const ckks_ct* b, ckks_ct* out) {
   });
 }
 
+int ckks_add_many(ckks_ctx* ctx, const ckks_ct* const* in, int count, ckks_ct* out) {
+  return guard([&] {
+    Context& c = C(ctx);
+    need(count >= 1 && in, CKKS_EARG, "empty sum");
+    need(out && out->owner == ctx, CKKS_EARG, "bad output handle");
+    const int limbs = in[0]->p.limbs;
+    for (int i = 0; i < count; ++i) {
+      same_ctx(ctx, in[i]);
+      need(in[i]->p.limbs == limbs, CKKS_ELEVEL, "operands at different levels");
+      need(in[i]->p.deg == in[0]->p.deg, CKKS_ESCALE, "operands with different noise degree");
+      check_scales(in[0]->p.scale, in[i]->p.scale);
+    }
+    DevPoly tmp;
+    tmp.ensure(&c, 2, limbs);
+    // up to 64 inputs per launch; later launches add onto the running sum
+    // (each thread reads and writes only its own residues)
+    int i = 0;
+    bool first = true;
+    while (i < count) {
+      ckks::SumPtrs sp{};
+      int k = 0;
+      if (!first) {
+        sp.in0[k] = tmp.poly(0);
+        sp.in1[k] = tmp.poly(1);
+        ++k;
+      }
+      for (; i < count && k < ckks::kSumMax; ++i, ++k) {
+        sp.in0[k] = in[i]->p.poly(0);
+        sp.in1[k] = in[i]->p.poly(1);
+      }
+      sp.out0 = tmp.poly(0);
+      sp.out1 = tmp.poly(1);
+      ckks::add_many(c, sp, k, limbs, c.stream);
+      first = false;
+    }
+    tmp.limbs = limbs;
+    tmp.scale = in[0]->p.scale;
+    tmp.deg = in[0]->p.deg;
+    take(out->p, tmp);
+  });
+}
+
+int ckks_add_batch(ckks_ctx* ctx, const ckks_ct* const* a, const ckks_ct* const* b, int count, ckks_ct* const* outs) {
+  return guard([&] {
+    Context& c = C(ctx);
+    need(count >= 0 && (count == 0 || (a && b && outs)), CKKS_EARG, "bad batch");
+    if (!count) return;
+    const int limbs = a[0]->p.limbs;
+    std::vector<DevPoly> res(count);
+    for (int i = 0; i < count; ++i) {
+      same_ctx(ctx, a[i]);
+      same_ctx(ctx, b[i]);
+      need(outs[i] && outs[i]->owner == ctx, CKKS_EARG, "bad output handle");
+      need(a[i]->p.limbs == limbs && b[i]->p.limbs == limbs, CKKS_ELEVEL, "batched adds need one limb count");
+      need(a[i]->p.deg == b[i]->p.deg, CKKS_ESCALE, "operands with different noise degree");
+      check_scales(a[i]->p.scale, b[i]->p.scale);
+      res[i].ensure(&c, 2, limbs);
+      res[i].limbs = limbs;
+      res[i].scale = a[i]->p.scale;
+      res[i].deg = a[i]->p.deg;
+    }
+    for (int s0 = 0; s0 < count; s0 += 32) {
+      ckks::PairPtrs pp{};
+      const int M = std::min(32, count - s0);
+      for (int m = 0; m < M; ++m) {
+        pp.a0[m] = a[s0 + m]->p.poly(0);
+        pp.a1[m] = a[s0 + m]->p.poly(1);
+        pp.b0[m] = b[s0 + m]->p.poly(0);
+        pp.b1[m] = b[s0 + m]->p.poly(1);
+        pp.o0[m] = res[s0 + m].poly(0);
+        pp.o1[m] = res[s0 + m].poly(1);
+      }
+      ckks::add_pairs(c, pp, M, limbs, c.stream);
+    }
+    for (int i = 0; i < count; ++i) take(outs[i]->p, res[i]);
+  });
+}
+
 int ckks_add_pt(ckks_ctx* ctx, const ckks_ct* a, const ckks_pt* p, ckks_ct* out) {
   return guard([&] {
     Context& c = C(ctx);

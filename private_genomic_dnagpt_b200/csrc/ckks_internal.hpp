@@ -7,6 +7,8 @@
 #include <cstdint>
 #include <map>
 #include <memory>
+#include <mutex>
+#include <unordered_map>
 #include <stdexcept>
 #include <string>
 #include <vector>
@@ -180,6 +182,19 @@ class Context {
 
   mutable Profiler prof;
   double limb_bytes() const { return 8.0 * N; }
+  // host time spent in allocation calls (diagnostics)
+  mutable double alloc_seconds = 0.0;
+  mutable long alloc_calls = 0;
+
+ private:
+  // Size-bucketed cache of device blocks.  All work of a context runs on its
+  // one stream, so a block released here may be handed to the next
+  // allocation at once: kernels that use it later are ordered after every
+  // kernel that used it before.  Misses fall back to cudaMalloc.
+  mutable std::mutex mem_mu_;
+  mutable std::unordered_map<size_t, std::vector<void*>> free_;
+  mutable std::unordered_map<void*, size_t> size_of_;
+  void drop_cache() const;
 };
 
 inline ProfScope::ProfScope(const Context& c, const char* name, double bytes, cudaStream_t s)
@@ -224,6 +239,24 @@ void ew_mul_pt(const Context& c, const uint64_t* a, size_t sa, const uint64_t* p
 void ew_mul_const(const Context& c, const uint64_t* a, size_t sa, uint64_t* o, size_t so, int npolys, int limbs,
                   const std::vector<uint64_t>& k_res, cudaStream_t st);
 void ew_add_const(const Context& c, uint64_t* a, int limbs, const std::vector<uint64_t>& k_res, cudaStream_t st);
+// sums of up to 64 ciphertexts (both polynomials) and batches of up to 32 pairs
+constexpr int kSumMax = 64;
+struct SumPtrs {
+  const uint64_t* in0[kSumMax];
+  const uint64_t* in1[kSumMax];
+  uint64_t* out0;
+  uint64_t* out1;
+};
+struct PairPtrs {
+  const uint64_t* a0[32];
+  const uint64_t* a1[32];
+  const uint64_t* b0[32];
+  const uint64_t* b1[32];
+  uint64_t* o0[32];
+  uint64_t* o1[32];
+};
+void add_many(const Context& c, const SumPtrs& p, int k, int limbs, cudaStream_t st);
+void add_pairs(const Context& c, const PairPtrs& p, int M, int limbs, cudaStream_t st);
 void tensor(const Context& c, const uint64_t* a0, const uint64_t* a1, const uint64_t* b0, const uint64_t* b1,
             uint64_t* d0, uint64_t* d1, uint64_t* d2, int limbs, cudaStream_t st);
 

@@ -4,6 +4,7 @@
 // (fhe/gpu_real_scheme_b/src/real_dnagpt_fides_scheme_b_simd_full_t103_depth13_
 //  digits3_ring65536_cpudiagcache_t123.cpp:1602-1626): FLEXIBLEAUTO scale
 // chain, HYBRID key switching with dnum digits, ring dimension 2^log_n.
+#include <chrono>
 #include <cmath>
 #include <cstring>
 
@@ -338,17 +339,15 @@ Context::Context(const Params& p) : params(p) {
     t.d_rescale_inv = upload(rinv);
   }
 
-  // stream-ordered pool that keeps freed blocks for reuse
-  cudaMemPool_t pool;
-  CKKS_CUDA(cudaDeviceGetDefaultMemPool(&pool, p.device));
-  uint64_t thresh = UINT64_MAX;
-  CKKS_CUDA(cudaMemPoolSetAttribute(pool, cudaMemPoolAttrReleaseThreshold, &thresh));
   CKKS_CUDA(cudaDeviceSynchronize());
 }
 
 Context::~Context() {
   cudaSetDevice(params.device);
   cudaStreamSynchronize(stream);
+  drop_cache();
+  for (auto& kv : size_of_) cudaFree(kv.first);  // blocks still held by live objects
+  size_of_.clear();
   for (auto& kv : rot_keys) cudaFree(kv.second);
   cudaFree(d_sk);
   cudaFree(d_pk);
@@ -443,14 +442,65 @@ const uint64_t* Context::rot_key(uint32_t g) const {
   return it == rot_keys.end() ? nullptr : it->second;
 }
 
+namespace {
+// bucket: powers of two up to 1 MiB, then multiples of 256 KiB
+size_t bucket(size_t bytes) {
+  if (bytes <= 256) return 256;
+  if (bytes <= (1u << 20)) {
+    size_t b = 256;
+    while (b < bytes) b <<= 1;
+    return b;
+  }
+  const size_t g = 256u << 10;
+  return (bytes + g - 1) / g * g;
+}
+}  // namespace
+
 void* Context::alloc(size_t bytes) const {
+  const auto t0 = std::chrono::steady_clock::now();
+  const size_t b = bucket(bytes);
   void* p = nullptr;
-  CKKS_CUDA(cudaMallocAsync(&p, bytes ? bytes : 8, stream));
+  {
+    std::lock_guard<std::mutex> lk(mem_mu_);
+    auto it = free_.find(b);
+    if (it != free_.end() && !it->second.empty()) {
+      p = it->second.back();
+      it->second.pop_back();
+    }
+  }
+  if (!p) {
+    cudaError_t e = cudaMalloc(&p, b);
+    if (e == cudaErrorMemoryAllocation) {  // give cached blocks back and retry once
+      cudaGetLastError();
+      CKKS_CUDA(cudaStreamSynchronize(stream));
+      drop_cache();
+      e = cudaMalloc(&p, b);
+    }
+    CKKS_CUDA(e);
+    std::lock_guard<std::mutex> lk(mem_mu_);
+    size_of_[p] = b;
+  }
+  alloc_seconds += std::chrono::duration<double>(std::chrono::steady_clock::now() - t0).count();
+  ++alloc_calls;
   return p;
 }
 
 void Context::release(void* p) const {
-  if (p) cudaFreeAsync(p, stream);
+  if (!p) return;
+  std::lock_guard<std::mutex> lk(mem_mu_);
+  auto it = size_of_.find(p);
+  if (it == size_of_.end()) return;
+  free_[it->second].push_back(p);
+}
+
+void Context::drop_cache() const {
+  std::lock_guard<std::mutex> lk(mem_mu_);
+  for (auto& kv : free_)
+    for (void* p : kv.second) {
+      cudaFree(p);
+      size_of_.erase(p);
+    }
+  free_.clear();
 }
 
 DevPoly::~DevPoly() {

@@ -119,6 +119,39 @@ __global__ void __launch_bounds__(kEwThreads) automorphism_kernel(const uint64_t
   o[base + k] = a[base + auto_index((uint32_t)k, g, logN)];
 }
 
+// out = sum of k inputs (EvalAddMany), per limb of both polynomials
+__global__ void __launch_bounds__(kEwThreads) add_many_kernel(SumPtrs p, int k, int limbs, int logN,
+                                                              const Mod* __restrict__ mods) {
+  const int N = 1 << logN;
+  const int limb = blockIdx.y % limbs, poly = blockIdx.y / limbs;
+  const uint64_t q = mods[limb].q;
+  const size_t i = ((size_t)blockIdx.x * kEwThreads + threadIdx.x) * 2;
+  if (i >= (size_t)N) return;
+  const size_t off = (size_t)limb * N + i;
+  ulonglong2 acc = make_ulonglong2(0, 0);
+  for (int j = 0; j < k; ++j) {
+    const ulonglong2 x = *reinterpret_cast<const ulonglong2*>((poly ? p.in1[j] : p.in0[j]) + off);
+    acc.x = add_mod(acc.x, x.x, q);
+    acc.y = add_mod(acc.y, x.y, q);
+  }
+  *reinterpret_cast<ulonglong2*>((poly ? p.out1 : p.out0) + off) = acc;
+}
+
+// out_m = a_m + b_m for a batch of independent pairs
+__global__ void __launch_bounds__(kEwThreads) add_pairs_kernel(PairPtrs p, int limbs, int logN,
+                                                               const Mod* __restrict__ mods) {
+  const int N = 1 << logN;
+  const int limb = blockIdx.y % limbs, poly = blockIdx.y / limbs, m = blockIdx.z;
+  const uint64_t q = mods[limb].q;
+  const size_t i = ((size_t)blockIdx.x * kEwThreads + threadIdx.x) * 2;
+  if (i >= (size_t)N) return;
+  const size_t off = (size_t)limb * N + i;
+  const ulonglong2 x = *reinterpret_cast<const ulonglong2*>((poly ? p.a1[m] : p.a0[m]) + off);
+  const ulonglong2 y = *reinterpret_cast<const ulonglong2*>((poly ? p.b1[m] : p.b0[m]) + off);
+  *reinterpret_cast<ulonglong2*>((poly ? p.o1[m] : p.o0[m]) + off) =
+      make_ulonglong2(add_mod(x.x, y.x, q), add_mod(x.y, y.y, q));
+}
+
 ConstRes pack(const std::vector<uint64_t>& v) {
   ConstRes c{};
   if (v.size() > 96) throw Error(kErrArgument, "too many limbs");
@@ -181,6 +214,20 @@ void tensor(const Context& c, const uint64_t* a0, const uint64_t* a1, const uint
   const dim3 grid((c.N + kEwThreads - 1) / kEwThreads, limbs);
   ProfScope ps(c, "tensor", 7.0 * limbs * c.limb_bytes(), st);
   tensor_kernel<<<grid, kEwThreads, 0, st>>>(a0, a1, b0, b1, d0, d1, d2, c.logN, c.d_mods);
+  CKKS_CUDA(cudaGetLastError());
+}
+
+void add_many(const Context& c, const SumPtrs& p, int k, int limbs, cudaStream_t st) {
+  const dim3 grid((c.N / 2 + kEwThreads - 1) / kEwThreads, 2 * limbs);
+  ProfScope ps(c, "add_many", (k + 1.0) * 2 * limbs * c.limb_bytes(), st);
+  add_many_kernel<<<grid, kEwThreads, 0, st>>>(p, k, limbs, c.logN, c.d_mods);
+  CKKS_CUDA(cudaGetLastError());
+}
+
+void add_pairs(const Context& c, const PairPtrs& p, int M, int limbs, cudaStream_t st) {
+  const dim3 grid((c.N / 2 + kEwThreads - 1) / kEwThreads, 2 * limbs, M);
+  ProfScope ps(c, "add_pairs", 6.0 * M * limbs * c.limb_bytes(), st);
+  add_pairs_kernel<<<grid, kEwThreads, 0, st>>>(p, limbs, c.logN, c.d_mods);
   CKKS_CUDA(cudaGetLastError());
 }
 

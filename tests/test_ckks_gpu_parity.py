@@ -334,3 +334,15 @@ def test_batched_client_encrypt_decrypt(pair10):
         single = cc.Decrypt(ct).GetRealPackedValue()
         assert np.abs(dec[i] - single).max() <= 1e-12
         assert np.abs(dec[i] - xs[i]).max() < 1e-8
+
+
+def test_add_many_and_add_batch_bit_exact(pair10):
+    o, cc = pair10
+    items = [_fresh(o, cc, 200 + i, 4) for i in range(70)]  # more than one launch of 64
+    ref = items[0][1]
+    for it in items[1:]:
+        ref = o.add(ref, it[1])
+    assert np.array_equal(cc.EvalAddMany([it[2] for it in items]).limbs_array(), ref)
+    outs = cc.add_batch([it[2] for it in items[:35]], [it[2] for it in items[35:70]])
+    for i, out in enumerate(outs):
+        assert np.array_equal(out.limbs_array(), o.add(items[i][1], items[35 + i][1]))
