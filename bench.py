@@ -322,11 +322,15 @@ def run_engine(args):
         ct_bytes = cc.slots * 8
         h2d = (groups + 2 * groups + c.get("weight_tile_encryptions", 0) + 3 * groups) * ct_bytes
         d2h = (groups + 2 * groups + c.get("score_tile_decryptions", 0) + 3 * groups) * ct_bytes
+        metric, workload = METRIC, WORKLOAD
+        if args.tokens != TOKENS:  # profiler captures on a smaller case
+            metric = METRIC.replace(f"@{TOKENS} tok", f"@{args.tokens} tok")
+            workload = WORKLOAD.replace(f"{TOKENS} tokens", f"{args.tokens} tokens")
         line = {
-            "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+            "metric": metric, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": e2e_ms, "higher_is_better": False,
             "scaling": "weak", "vs_baseline": value / REF_A100_BLOCK_S, "dtype": "u64", "data": "synthetic",
-            "config": {"workload": WORKLOAD, "flush": "inputs > L2 (keys ~13 GB, diagonals ~26 GB)",
+            "config": {"workload": workload, "flush": "inputs > L2 (keys ~13 GB, diagonals ~26 GB)",
                        "parallelism": f"replicas{world}", "input_limbs": rep["counts"].get("input_limbs"),
                        "rel_inf_vs_plaintext": err},
             "e2e": {"value": e2e_ms / 1e3, "unit": UNIT, "h2d_bytes_per_step": h2d,
@@ -348,6 +352,79 @@ def run_engine(args):
         dist.destroy_process_group()
 
 
+def run_primitive(args):
+    """Primitive operations on one configuration of the sweep (N, L, dnum):
+    NTT, EvalRotate (single and batched), hoisted rotations, EvalMult+relin,
+    Rescale, each timed with CUDA events on the engine stream over 32
+    ciphertexts (> L2 at L >= 8).  The timed region is inside a profiler
+    range, so `ncu --profile-from-start off` on this command captures the
+    primitive kernels on a case of a few GB."""
+    import torch
+    import private_genomic_dnagpt_b200 as eng
+
+    torch.cuda.set_device(0)
+    cc = eng.GenCryptoContext(eng.CCParams(ring_dim_log=args.logn, limbs=args.limbs, dnum=args.dnum, seed=1))
+    cc.KeyGen()
+    cc.EvalMultKeyGen()
+    cc.EvalRotateKeyGen(ROT_INDICES)
+    stream = torch.cuda.ExternalStream(cc.stream_handle())
+    lib = eng.lib()
+    R, L, N = 32, args.limbs, cc.N
+    rng = np.random.default_rng(3)
+    cts = [cc.Encrypt(cc.MakeCKKSPackedPlaintext(rng.uniform(-1, 1, cc.slots))) for _ in range(R)]
+    cts2 = [cc.Encrypt(cc.MakeCKKSPackedPlaintext(rng.uniform(-1, 1, cc.slots))) for _ in range(R)]
+    outs = [eng.Ciphertext(cc) for _ in range(R)]
+    # NTT input: R ciphertexts' worth of limbs (2 R L limbs), residues below 2^49
+    ntt_buf = torch.randint(0, 1 << 49, (2 * R * L * N,), dtype=torch.int64, device="cuda")
+
+    ops = {
+        "ntt_fwd": lambda: eng._check(lib.ckks_ntt_forward_polys(cc.h, ntt_buf.data_ptr(), 2 * R, L)),
+        "ntt_inv": lambda: eng._check(lib.ckks_ntt_inverse_polys(cc.h, ntt_buf.data_ptr(), 2 * R, L)),
+        "rotate": lambda: [eng._check(lib.ckks_rotate(cc.h, cts[r].h, ROT_INDICES[r % len(ROT_INDICES)], outs[r].h))
+                           for r in range(R)],
+        "rotate_batch": lambda: cc.rotate_batch(cts, [ROT_INDICES[r % len(ROT_INDICES)] for r in range(R)]),
+        "rotate_hoisted": lambda: [cc.EvalFastRotation(cts[r], ROT_INDICES[:4]) for r in range(R // 4)],
+        "mul_relin_batch": lambda: cc.mul_ct_batch(cts, cts2),
+        "rescale_batch": lambda: cc.rescale_batch(cts),
+    }
+    units = {"ntt_fwd": 2 * R * L, "ntt_inv": 2 * R * L, "rotate": R, "rotate_batch": R,
+             "rotate_hoisted": (R // 4) * 4, "mul_relin_batch": R, "rescale_batch": R}
+    res = {}
+    torch.cuda.cudart().cudaProfilerStart()
+    with ClockSampler(0) as clk:
+        for name, fn in ops.items():
+            for _ in range(args.warmup):
+                fn()
+            cc.Synchronize()
+            e0 = torch.cuda.Event(enable_timing=True)
+            e1 = torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            for _ in range(args.steps):
+                fn()
+            e1.record(stream)
+            e1.synchronize()
+            sec = e0.elapsed_time(e1) / 1e3 / args.steps
+            res[name] = {"us_per_unit": sec / units[name] * 1e6, "units_per_step": units[name]}
+    torch.cuda.cudart().cudaProfilerStop()
+    peak, peak_kind = measured_peaks()
+    ks_b = keyswitch_bytes(L, cc.K, cc.alpha, N)
+    ntt_gbs = 2 * 8.0 * N / (res["ntt_fwd"]["us_per_unit"] * 1e-6) / 1e9
+    rot_s = res["rotate_batch"]["us_per_unit"] * 1e-6
+    line = {
+        "metric": "EvalRotate/s", "value": 1.0 / rot_s, "unit": "rotations/s", "n_gpus": 1, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": rot_s * R * 1e3, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "u64", "data": "synthetic",
+        "config": {"workload": f"primitive ops, N=2^{args.logn}, {L} limbs, dnum={args.dnum}, {R} ciphertexts",
+                   "flush": "inputs > L2", "alpha": cc.alpha, "special": cc.K},
+        "ops": res,
+        "roofline": {"kernel": "ntt_fwd", "bound": "hbm", "achieved": ntt_gbs, "peak": peak, "unit": "GB/s",
+                     "frac": ntt_gbs / peak, "peak_kind": peak_kind,
+                     "keyswitch_GBps": ks_b / rot_s / 1e9, "keyswitch_frac": ks_b / rot_s / 1e9 / peak},
+        "clocks": clk.summary(),
+    }
+    print(json.dumps(line), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -358,9 +435,16 @@ def main():
     ap.add_argument("--no-cpu", action="store_true")
     # a smaller token count only for profiler captures (the benchmark is 103)
     ap.add_argument("--tokens", type=int, default=TOKENS)
+    # primitive-operation sweep instead of the block (one configuration per run)
+    ap.add_argument("--primitive", action="store_true")
+    ap.add_argument("--logn", type=int, default=LOG_N)
+    ap.add_argument("--limbs", type=int, default=LIMBS)
+    ap.add_argument("--dnum", type=int, default=DNUM)
     args = ap.parse_args()
     if args.impl == "reference":
         run_reference(args)
+    elif args.primitive:
+        run_primitive(args)
     else:
         run_engine(args)
 

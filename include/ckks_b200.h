@@ -180,6 +180,11 @@ int ckks_profile_report(ckks_ctx* ctx, char* buf, size_t size);
  * Limb i of `data` is taken modulo Q prime first_prime + i. */
 int ckks_ntt_forward_device(ckks_ctx* ctx, uint64_t* data, int nlimbs, int first_prime);
 int ckks_ntt_inverse_device(ckks_ctx* ctx, uint64_t* data, int nlimbs, int first_prime);
+/* The same over `npolys` consecutive polynomials of `limbs` Q limbs each
+ * (limb j of every polynomial modulo Q prime j), in one launch pair: the
+ * batched shape the key switch uses. */
+int ckks_ntt_forward_polys(ckks_ctx* ctx, uint64_t* data, int npolys, int limbs);
+int ckks_ntt_inverse_polys(ckks_ctx* ctx, uint64_t* data, int npolys, int limbs);
 
 /* ---- encrypted transformer block (the reference's EncryptedEvaluator and
  * Client, T123.cpp:509-948) ------------------------------------------------

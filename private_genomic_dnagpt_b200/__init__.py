@@ -132,6 +132,8 @@ _SIGS = [
     ("ckks_schedule_active_shifts", ctypes.c_int, [ctypes.c_int] * 4 + [ctypes.POINTER(ctypes.c_int), ctypes.c_int]),
     ("ckks_schedule_diagonal", ctypes.c_int, [_f64p] + [ctypes.c_int] * 8 + [_f64p]),
     ("ckks_ntt_inverse_device", ctypes.c_int, [_vp, _vp, ctypes.c_int, ctypes.c_int]),
+    ("ckks_ntt_forward_polys", ctypes.c_int, [_vp, _vp, ctypes.c_int, ctypes.c_int]),
+    ("ckks_ntt_inverse_polys", ctypes.c_int, [_vp, _vp, ctypes.c_int, ctypes.c_int]),
 ]
 
 _lib = None

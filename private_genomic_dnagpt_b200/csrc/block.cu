@@ -351,6 +351,9 @@ struct ckks_block {
     ++count["level_reduce"];
     return cc.LevelReduce(a, limbs);
   }
+  // a at no more than `limbs` limbs: work whose result is next decrypted
+  // runs at the fewest limbs that leave two at the decryption
+  Ciphertext lower(const Ciphertext& a, int limbs) { return a->limbs() > limbs ? reduce_to(a, limbs) : a; }
   Ciphertext rot(const Ciphertext& a, int k) {
     ++count["rotations"];
     return cc.EvalRotate(a, k);
@@ -400,10 +403,15 @@ struct ckks_block {
       const Ciphertext mean = mul_pt_rs(feature_sum(x), feature_plain(1, invd, lx));
       centered.push_back(cc.EvalSub(reduce_to(x, lx - 1), mean));
     }
+    // the variance is only decrypted: square at 4 limbs, sum and scale at 3,
+    // decrypt at 2
+    std::vector<Ciphertext> low;
+    for (const auto& c : centered) low.push_back(lower(c, 4));
     count["ct_ct"] += (long)xs.size();
-    sqs = cc.RescaleBatch(cc.EvalMultBatch(centered, centered));
+    sqs = cc.RescaleBatch(cc.EvalMultBatch(low, low));
     std::vector<Ciphertext> var;
-    for (const auto& sq : sqs) var.push_back(cc.EvalAdd(mul_pt_rs(feature_sum(sq), feature_plain(1, invd, lx - 2)), 1e-5));
+    for (const auto& sq : sqs)
+      var.push_back(cc.EvalAdd(mul_pt_rs(feature_sum(sq), feature_plain(1, invd, sq->limbs())), 1e-5));
     const int M = (int)xs.size();
     double* dv = dbuf((size_t)M * slots());
     client_decrypt(var, dv);
@@ -678,9 +686,12 @@ void ckks_block::forward(const double* x, int T, double* y) {
   stamp("ln1_qkv", t);
 
   // scores: server products and head sums, client gathers them on the device
-  const int lk = Q[0]->limbs() - 1;  // shifted key / value level
+  const int lk = Q[0]->limbs() - 1;  // shifted value level
+  // scores are only decrypted: keys shifted from 4 limbs, products of 3-limb
+  // operands, head sums and decryption at 2
+  const int lks = std::min(lk, 3);
   std::vector<Ciphertext> Qr(G);
-  for (int g = 0; g < G; ++g) Qr[g] = reduce_to(Q[g], lk);
+  for (int g = 0; g < G; ++g) Qr[g] = reduce_to(Q[g], lks);
   double* d_scores = dbuf((size_t)T * H * T);
   double* d_prob = dbuf((size_t)T * H * T);
   CKKS_CUDA(cudaMemsetAsync(d_scores, 0xFF, sizeof(double) * T * H * T, C.stream));  // NaN = missing
@@ -693,7 +704,7 @@ void ckks_block::forward(const double* x, int T, double* y) {
     std::vector<int> need;
     for (const auto& tg : tags[kg])
       if (std::find(need.begin(), need.end(), tg.d) == need.end()) need.push_back(tg.d);
-    auto ks = lane_shifts(K[kg], need, lk);
+    auto ks = lane_shifts(lower(K[kg], lks + 1), need, lks);
     count["cached_key_lane_shifts"] += (long)ks.size() - (ks.count(0) ? 1 : 0);
     std::vector<Ciphertext> qa, kb;
     for (const auto& tg : tags[kg]) {

@@ -1052,4 +1052,22 @@ int ckks_ntt_inverse_device(ckks_ctx* ctx, uint64_t* data, int nlimbs, int first
   });
 }
 
+int ckks_ntt_forward_polys(ckks_ctx* ctx, uint64_t* data, int npolys, int limbs) {
+  return guard([&] {
+    Context& c = C(ctx);
+    need(data && npolys >= 0 && limbs >= 1 && limbs <= c.L, CKKS_EARG, "bad polynomial shape");
+    ckks::ntt_forward(c, data, npolys * limbs, ckks::LimbMap::q(limbs, c.L), c.stream);
+    CKKS_CUDA(cudaGetLastError());
+  });
+}
+
+int ckks_ntt_inverse_polys(ckks_ctx* ctx, uint64_t* data, int npolys, int limbs) {
+  return guard([&] {
+    Context& c = C(ctx);
+    need(data && npolys >= 0 && limbs >= 1 && limbs <= c.L, CKKS_EARG, "bad polynomial shape");
+    ckks::ntt_inverse(c, data, npolys * limbs, ckks::LimbMap::q(limbs, c.L), c.stream);
+    CKKS_CUDA(cudaGetLastError());
+  });
+}
+
 }  // extern "C"

@@ -80,6 +80,17 @@ def test_ntt_bit_exact(logN):
     eng._check(eng.lib().ckks_ntt_forward_device(cc.h, dev2.data_ptr(), 2, 2))
     cc.Synchronize()
     assert np.array_equal(dev2.cpu().numpy().view(np.uint64), ref[2:4])
+    # three polynomials of L Q limbs each in one batched launch pair
+    polys = np.concatenate([a[:L], a[:L][::-1] % o.moduli[:L, None], a[:L]])
+    dev3 = torch.from_numpy(polys.view(np.int64).copy()).cuda()
+    torch.cuda.synchronize()
+    eng._check(eng.lib().ckks_ntt_forward_polys(cc.h, dev3.data_ptr(), 3, L))
+    cc.Synchronize()
+    want = np.stack([o.ntt(polys[i], i % L) for i in range(3 * L)])
+    assert np.array_equal(dev3.cpu().numpy().view(np.uint64), want)
+    eng._check(eng.lib().ckks_ntt_inverse_polys(cc.h, dev3.data_ptr(), 3, L))
+    cc.Synchronize()
+    assert np.array_equal(dev3.cpu().numpy().view(np.uint64), polys)
 
 
 @pytest.mark.parametrize("logN", [10, 16])
