@@ -60,6 +60,13 @@ def measured_peaks():
     return 6650.0, "fallback"
 
 
+# DRAM bytes (read + write) per limb of one NTT pass, from the ncu capture of
+# a 1536-limb forward transform (profiles/ntt_pass_n65536_1536limbs.md); the
+# pass traffic grows in proportion to the limbs it transforms
+NCU_TRAFFIC_PER_LIMB = {"ntt_fwd_rows": (877.050368 + 751.248640) * 1e6 / 1536,
+                        "ntt_fwd_cols": (805.437952 + 745.955328) * 1e6 / 1536}
+
+
 def keyswitch_bytes(limbs: int, K: int, alpha: int, N: int) -> float:
     beta = -(-limbs // alpha)
     return (limbs + 2 * beta * (limbs + K) + 2 * limbs) * 8.0 * N
@@ -302,8 +309,12 @@ def run_engine(args):
         name, d = dom
         per_launch_ms = d["ms"] / d["launches"]
         achieved = (d["bytes"] / d["launches"]) / (per_launch_ms / 1e3) / 1e9
+        traffic = None
+        if name in NCU_TRAFFIC_PER_LIMB:  # limbs per launch x measured bytes per limb
+            limbs_per_launch = d["bytes"] / d["launches"] / (8.0 * (1 << LOG_N))
+            traffic = NCU_TRAFFIC_PER_LIMB[name] * limbs_per_launch
         roof = {"kernel": name, "bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
-                "frac": achieved / peak, "traffic": None, "peak_kind": peak_kind,
+                "frac": achieved / peak, "traffic": traffic, "peak_kind": peak_kind,
                 "launches": d["launches"], "ms_per_launch": per_launch_ms,
                 "share": d["ms"] / sum(v["ms"] for v in prof.values())}
 
@@ -345,6 +356,97 @@ def run_engine(args):
             "gpu_launches": launches,
             "clocks": clk.summary(),
             "cpu_baseline": cpu,
+        }
+        print(json.dumps(line), flush=True)
+    if dist is not None:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def run_model(args):
+    """Chained blocks (the two-block and 12-block configurations) with the
+    full-hidden-state client refresh between blocks and, with --head, the
+    last-token refresh into the classifier head (N - A margin).  One step is
+    one sequence through the whole model; under torchrun every rank runs its
+    own sequence (replicas, weak scaling).  Blocks beyond the diagonal-cache
+    budget of the device encode their diagonals again on every step."""
+    import torch
+    import private_genomic_dnagpt_b200 as eng
+    from oracle import plain_block
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dist = None
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=900))
+    cc = eng.GenCryptoContext(eng.CCParams(ring_dim_log=LOG_N, limbs=LIMBS, dnum=DNUM, seed=1 + rank,
+                                           device=local))
+    cc.KeyGen()
+    cc.EvalMultKeyGen()
+    ws = [plain_block.synthetic_weights(100 + b) for b in range(args.blocks)]
+    hw = plain_block.synthetic_head_weights(99) if args.head else None
+    x = plain_block.synthetic_input(6 + rank, args.tokens)
+    # diagonal caches: about 26 GB per block; keep what fits beside the keys
+    free, _ = torch.cuda.mem_get_info(local)
+    cached = args.cached_blocks if args.cached_blocks >= 0 else max(1, int((free / 2**30 - 40) // 27))
+    model = eng.EncryptedModel(cc, ws, hw, args.tokens, cached_blocks=min(cached, args.blocks))
+    cc.EvalRotateKeyGen(model.rotation_indices())
+    stream = torch.cuda.ExternalStream(cc.stream_handle())
+    h_ref, m_ref = plain_block.model(x, ws, hw)
+
+    def barrier():
+        cc.Synchronize()
+        torch.cuda.synchronize()
+        if dist is not None:
+            dist.barrier()
+
+    for _ in range(args.warmup):
+        h, m = model.forward(x)
+    err = plain_block.rel_inf(h_ref, h)
+    assert err < 1e-6, f"model hidden-state error {err}"
+    barrier()
+    steps_s, eval_s = [], []
+    with ClockSampler(local) as clk:
+        for _ in range(args.steps):
+            e0 = torch.cuda.Event(enable_timing=True)
+            e1 = torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            h, m = model.forward(x)
+            e1.record(stream)
+            e1.synchronize()
+            steps_s.append(e0.elapsed_time(e1) / 1e3)
+            ev = sum(b.report()["seconds"].get("evaluate_events", 0.0) for b in model.blocks)
+            if model.head is not None:
+                ev += model.head.report()["seconds"].get("head_total", 0.0)
+            eval_s.append(ev)
+        barrier()
+    value, e2e = float(np.mean(eval_s)), float(np.mean(steps_s))
+    if dist is not None:
+        t = torch.tensor([value, e2e], device="cuda", dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        value, e2e = float(t[0]), float(t[1])
+    if rank == 0:
+        name = f"{args.blocks} blocks" + (" + head" if args.head else "")
+        groups = -(-args.tokens // 32)
+        ct_bytes = cc.slots * 8
+        line = {
+            "metric": f"encrypted {name} latency (s) @{args.tokens} tok, N=2^16", "value": value, "unit": "s",
+            "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": e2e * 1e3,
+            "higher_is_better": False, "scaling": "weak", "vs_baseline": None, "dtype": "u64", "data": "synthetic",
+            "config": {"workload": f"{name}, one sequence per GPU, {args.tokens} tokens, D=768, 12 heads, "
+                                   f"MLP 3072, N=2^16, 24 limbs, dnum=3; full-hidden-state client refresh between "
+                                   f"blocks", "cached_blocks": model.cached_blocks,
+                       "parallelism": f"replicas{world}", "flush": "inputs > L2 (keys, diagonals)",
+                       "rel_inf_vs_plaintext": err,
+                       "margin": m, "margin_plaintext": m_ref},
+            "e2e": {"value": e2e, "unit": "s", "h2d_bytes_per_step": args.blocks * groups * ct_bytes,
+                    "d2h_bytes_per_step": args.blocks * groups * ct_bytes},
+            "per_step_s": [round(v, 4) for v in steps_s],
+            "clocks": clk.summary(),
         }
         print(json.dumps(line), flush=True)
     if dist is not None:
@@ -440,11 +542,17 @@ def main():
     ap.add_argument("--logn", type=int, default=LOG_N)
     ap.add_argument("--limbs", type=int, default=LIMBS)
     ap.add_argument("--dnum", type=int, default=DNUM)
+    # chained blocks (two-block / 12-block + head configurations)
+    ap.add_argument("--blocks", type=int, default=1)
+    ap.add_argument("--head", action="store_true")
+    ap.add_argument("--cached-blocks", type=int, default=-1)
     args = ap.parse_args()
     if args.impl == "reference":
         run_reference(args)
     elif args.primitive:
         run_primitive(args)
+    elif args.blocks > 1 or args.head:
+        run_model(args)
     else:
         run_engine(args)
 

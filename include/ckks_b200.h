@@ -205,6 +205,26 @@ int ckks_block_rotation_indices(const ckks_block* b, int* out, int cap);
 int ckks_block_forward(ckks_block* b, const double* x, int tokens, double* y);
 /* operation counts and stage seconds of the last forward, JSON text */
 int ckks_block_report(const ckks_block* b, char* buf, size_t size);
+/* drop the block's encoded BSGS diagonals and masks (about 26 GB per block
+ * at N = 2^16); the next forward encodes them again on the device */
+int ckks_block_release_cache(ckks_block* b, size_t* released_bytes);
+
+/* ---- classifier head and the multi-block model (the reference's
+ * 12blocks_head_cpudiagcache_t123_v3.cpp:452-755, multiblock/manual.py:52-80)
+ * A head object evaluates final LN -> head linear [D, D] -> SiLU (client)
+ * -> head LN -> dot with readout (the N - A margin row) on one token; it is
+ * a ckks_block handle released with ckks_block_destroy. */
+int ckks_head_create(ckks_ctx* ctx, const double* final_ln, const double* head_linear, const double* head_ln,
+                     const double* readout, int d_model, ckks_block** out);
+/* encrypted margin of one hidden state x_last [d_model], decrypted */
+int ckks_head_forward(ckks_block* head, const double* x_last, double* margin);
+/* nblocks chained blocks with the full-hidden-state client refresh between
+ * them, then the last-token refresh into `head` (may be NULL).  Blocks with
+ * index >= cached_blocks release their diagonal cache after their forward.
+ * hidden: [tokens, d_model] output of the last block. */
+int ckks_model_forward(ckks_block* const* blocks, int nblocks, ckks_block* head, const double* x, int tokens,
+                       int cached_blocks, double* hidden, double* margin);
+
 /* host-only schedule helpers: causal lane shifts of a (query group, key
  * group) tile (simd_layout.py:386-406) and one BSGS diagonal as slot values
  * (T123.cpp:1018-1046) */

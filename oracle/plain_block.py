@@ -1,11 +1,16 @@
-"""Float64 plaintext DNAGPT block: the checker for decrypted block outputs.
+"""Float64 plaintext DNAGPT block and model: the checker for decrypted
+block outputs and head margins.
 
 TEST INFRASTRUCTURE ONLY (tests/, smoke(), bench CPU legs).  Restates the
 reference's bias-free block oracle, fhe/realweights/manual.py:36-106
 (block_reference): pre-LN with gain only (eps 1e-5, manual.py:12-18),
 x @ W.T with PyTorch [out, in] weights (:21-22), causal stable softmax
 (:25-28, :64-66), tanh-GELU (:31-33), residuals (:70, :78).  Pinned against
-that function's own output by tests/golden/plain_block_*.npz.
+that function's own output by tests/golden/plain_block_*.npz.  The classifier
+head restates fhe/multiblock/manual.py:41-80 (stable SiLU,
+classifier_head_reference) with the N - A readout margin of the 12-block
+driver (real_dnagpt_fides_scheme_b_simd_full_t103_12blocks_head_cpudiagcache_
+t123_v3.cpp:544-550, 594-597); pinned by tests/golden/plain_head.npz.
 """
 
 from __future__ import annotations
@@ -52,6 +57,42 @@ def block(x, w, heads=HEADS, eps=1e-5, return_all=False):
         return {"ln1_output": h1, "qkv": qkv, "attention_scores": scores, "attention_probabilities": p,
                 "residual1": r1, "mlp_fc": fc, "block_output": out}
     return out
+
+
+def silu(x):
+    """Stable SiLU (multiblock/manual.py:41-49)."""
+    x = np.asarray(x, np.float64)
+    sig = np.empty_like(x)
+    pos = x >= 0
+    sig[pos] = 1.0 / (1.0 + np.exp(-x[pos]))
+    e = np.exp(x[~pos])
+    sig[~pos] = e / (1.0 + e)
+    return x * sig
+
+
+def head(hidden_last, hw, eps=1e-5):
+    """N - A margin of one hidden state: final LN -> head linear -> SiLU ->
+    head LN -> dot with readout (readout = readout_N - readout_A)."""
+    f = layer_norm(np.asarray(hidden_last, np.float64), hw["final_ln"], eps)
+    lin = f @ hw["head_linear"].T
+    hl = layer_norm(silu(lin), hw["head_ln"], eps)
+    return float(hl @ hw["readout"])
+
+
+def model(x, blocks_w, hw=None, heads=HEADS):
+    """Chained blocks, then the head on the last token; returns (hidden, margin)."""
+    h = np.asarray(x, np.float64)
+    for w in blocks_w:
+        h = block(h, w, heads)
+    return h, (head(h[-1], hw) if hw is not None else None)
+
+
+def synthetic_head_weights(seed: int, d=D, std=0.02):
+    """Head weights: unit LN gains, head linear N(0, std) [out, in], readout
+    margin row N(0, std)."""
+    rng = np.random.default_rng(seed)
+    return {"final_ln": np.ones(d), "head_linear": rng.normal(0.0, std, (d, d)), "head_ln": np.ones(d),
+            "readout": rng.normal(0.0, std, d)}
 
 
 def synthetic_weights(seed: int, d=D, mlp=MLP, std=0.02, gain_jitter=0.0):

@@ -129,6 +129,11 @@ _SIGS = [
     ("ckks_block_rotation_indices", ctypes.c_int, [_vp, ctypes.POINTER(ctypes.c_int), ctypes.c_int]),
     ("ckks_block_forward", ctypes.c_int, [_vp, _f64p, ctypes.c_int, _f64p]),
     ("ckks_block_report", ctypes.c_int, [_vp, ctypes.c_char_p, ctypes.c_size_t]),
+    ("ckks_block_release_cache", ctypes.c_int, [_vp, ctypes.POINTER(ctypes.c_size_t)]),
+    ("ckks_head_create", ctypes.c_int, [_vp] + [_f64p] * 4 + [ctypes.c_int, ctypes.POINTER(_vp)]),
+    ("ckks_head_forward", ctypes.c_int, [_vp, _f64p, _f64p]),
+    ("ckks_model_forward", ctypes.c_int, [ctypes.POINTER(_vp), ctypes.c_int, _vp, _f64p, ctypes.c_int, ctypes.c_int,
+                                          _f64p, _f64p]),
     ("ckks_schedule_active_shifts", ctypes.c_int, [ctypes.c_int] * 4 + [ctypes.POINTER(ctypes.c_int), ctypes.c_int]),
     ("ckks_schedule_diagonal", ctypes.c_int, [_f64p] + [ctypes.c_int] * 8 + [_f64p]),
     ("ckks_ntt_inverse_device", ctypes.c_int, [_vp, _vp, ctypes.c_int, ctypes.c_int]),
@@ -562,6 +567,91 @@ class EncryptedBlock:
         buf = ctypes.create_string_buffer(n + 1)
         lib().ckks_block_report(self.h, buf, n + 1)
         return json.loads(buf.value.decode())
+
+
+    def release_cache(self) -> int:
+        """Drop the encoded diagonals (re-encoded on the next forward);
+        returns the bytes released."""
+        n = ctypes.c_size_t(0)
+        _check(lib().ckks_block_release_cache(self.h, ctypes.byref(n)))
+        return n.value
+
+
+class EncryptedHead:
+    """The classifier head of the reference's 12-block driver
+    (EncryptedHeadEvaluator): final LN, head linear, SiLU client boundary,
+    head LN and the N - A readout margin, on one token.  ``weights`` holds
+    final_ln [D], head_linear [D, D], head_ln [D] and readout [D] (the
+    difference of the N and A rows of the readout matrix)."""
+
+    def __init__(self, cc: CryptoContext, weights: dict):
+        self.cc = cc
+        self._w = {k: np.ascontiguousarray(weights[k], np.float64) for k in
+                   ("final_ln", "head_linear", "head_ln", "readout")}
+        D = self._w["final_ln"].shape[0]
+        self.D = D
+        h = _vp()
+        _check(lib().ckks_head_create(cc.h, _f64(self._w["final_ln"]), _f64(self._w["head_linear"]),
+                                      _f64(self._w["head_ln"]), _f64(self._w["readout"]), D, ctypes.byref(h)))
+        self.h = h
+
+    def __del__(self):
+        try:
+            if self.h:
+                lib().ckks_block_destroy(self.h)
+                self.h = None
+        except Exception:
+            pass
+
+    def rotation_indices(self) -> list[int]:
+        n = lib().ckks_block_rotation_indices(self.h, None, 0)
+        buf = (ctypes.c_int * n)()
+        lib().ckks_block_rotation_indices(self.h, buf, n)
+        return list(buf)
+
+    def forward(self, x_last: np.ndarray) -> float:
+        x_last = np.ascontiguousarray(x_last, np.float64)
+        assert x_last.shape == (self.D,)
+        m = np.zeros(1, np.float64)
+        _check(lib().ckks_head_forward(self.h, _f64(x_last), _f64(m)))
+        return float(m[0])
+
+    def report(self) -> dict:
+        return EncryptedBlock.report(self)
+
+
+class EncryptedModel:
+    """Chained encrypted blocks with the full-hidden-state client refresh
+    between them, then the last-token refresh into the classifier head (the
+    reference's 12blocks_head_cpudiagcache_t123_v3.cpp driver).  Blocks with
+    index >= ``cached_blocks`` release their encoded diagonals after each
+    forward (about 26 GB per block at N = 2^16, so 12 blocks do not all fit
+    one device); None keeps every block's cache."""
+
+    def __init__(self, cc: CryptoContext, block_weights: list, head_weights: dict | None, tokens: int,
+                 heads: int = 12, cached_blocks: int | None = None):
+        self.cc = cc
+        self.blocks = [EncryptedBlock(cc, w, tokens, heads) for w in block_weights]
+        self.head = EncryptedHead(cc, head_weights) if head_weights is not None else None
+        self.tokens = tokens
+        self.cached_blocks = len(self.blocks) if cached_blocks is None else cached_blocks
+
+    def rotation_indices(self) -> list[int]:
+        s = set(self.blocks[0].rotation_indices())
+        if self.head is not None:
+            s |= set(self.head.rotation_indices())
+        return sorted(s)
+
+    def forward(self, x: np.ndarray):
+        """Returns (hidden [tokens, D] of the last block, head margin or None)."""
+        x = np.ascontiguousarray(x, np.float64)
+        hidden = np.zeros_like(x)
+        m = np.zeros(1, np.float64)
+        n = len(self.blocks)
+        hs = (_vp * n)(*[b.h for b in self.blocks])
+        _check(lib().ckks_model_forward(hs, n, self.head.h if self.head is not None else None, _f64(x),
+                                        x.shape[0], self.cached_blocks, _f64(hidden), _f64(m)))
+        return hidden, (float(m[0]) if self.head is not None else None)
 
 
 def schedule_active_shifts(tokens: int, batch: int, qg: int, kg: int) -> list[int]:

@@ -176,6 +176,25 @@ __global__ void gelu_kernel(const double* __restrict__ in, double* __restrict__ 
   out[o] = r;
 }
 
+// numerically stable SiLU on features < odim of lane 0, zero elsewhere (the
+// head's single-token boundary, 12blocks_head..._t123_v3.cpp:536-542, 740-755)
+__global__ void silu_kernel(const double* __restrict__ in, double* __restrict__ out, int B, int odim, int slots) {
+  const int i = blockIdx.x * kThreads + threadIdx.x;
+  if (i >= slots) return;
+  const int f = i / B, t = i % B;
+  double r = 0.0;
+  if (f < odim && t == 0) {
+    const double u = in[i];
+    if (u >= 0.0) {
+      r = u / (1.0 + exp(-u));
+    } else {
+      const double e = exp(u);
+      r = u * e / (1.0 + e);
+    }
+  }
+  out[i] = r;
+}
+
 // x [T, D] -> group g slot vectors (feature f, lane t) = x[g B + t][f]
 __global__ void pack_kernel(const double* __restrict__ x, double* __restrict__ vals, int T, int D, int B, int slots) {
   const int i = blockIdx.x * kThreads + threadIdx.x;
@@ -259,6 +278,10 @@ struct ckks_block {
   double* d_proj = nullptr;
   double* d_fc = nullptr;
   double* d_proj2 = nullptr;
+  // classifier head (a head object holds only these): D x D linear with the
+  // final LN gain folded in, and the N - A readout with the head LN gain
+  double* d_head = nullptr;
+  std::vector<double> readout;
   int nfc = 3;
   struct Diag {
     uint64_t* data = nullptr;
@@ -285,8 +308,26 @@ struct ckks_block {
     cudaFree(d_proj);
     cudaFree(d_fc);
     cudaFree(d_proj2);
-    d_qkv = d_proj = d_fc = d_proj2 = nullptr;
+    cudaFree(d_head);
+    d_qkv = d_proj = d_fc = d_proj2 = d_head = nullptr;
     orphaned = true;
+  }
+  // drop the encoded diagonals and masks (rebuilt on the next use); returns
+  // the bytes released
+  size_t release_cache() {
+    size_t bytes = 0;
+    for (auto& kv : diags) {
+      bytes += sizeof(uint64_t) * (size_t)s.n1 * s.n2 * kv.second.limbs * C.N;
+      C.release(kv.second.data);
+    }
+    diags.clear();
+    masks.clear();
+    return bytes;
+  }
+  size_t cache_bytes() const {
+    size_t bytes = 0;
+    for (auto& kv : diags) bytes += sizeof(uint64_t) * (size_t)s.n1 * s.n2 * kv.second.limbs * C.N;
+    return bytes;
   }
   ~ckks_block() { release_device(); }
 
@@ -488,6 +529,11 @@ struct ckks_block {
   // weight id -> (device matrix, out_dim, in_dim, leading dimension)
   void weight_view(int id, const double*& W, int& out_dim, int& in_dim, int& ld) const {
     const int D = s.D;
+    if (id == kHeadLinear) {
+      W = d_head;
+      out_dim = in_dim = ld = D;
+      return;
+    }
     if (id < 3) {
       W = d_qkv + (size_t)id * D * D;
       out_dim = D;
@@ -538,12 +584,18 @@ struct ckks_block {
     uint64_t* enc = (uint64_t*)C.alloc(sizeof(uint64_t) * (size_t)chunk * stride);
     for (int d0 = 0; d0 < nd; d0 += chunk) {
       const int cnt = std::min(chunk, nd - d0);
-      blk::diag_values_kernel<<<dim3((slots + blk::kThreads - 1) / blk::kThreads, cnt), blk::kThreads, 0,
-                                  C.stream>>>(W, od, id_, ld, s.PW, s.B, s.n1, d0, vals);
+      {
+        ckks::ProfScope ps(C, "diag_values", 8.0 * slots * cnt, C.stream);
+        blk::diag_values_kernel<<<dim3((slots + blk::kThreads - 1) / blk::kThreads, cnt), blk::kThreads, 0,
+                                    C.stream>>>(W, od, id_, ld, s.PW, s.B, s.n1, d0, vals);
+      }
       CKKS_CUDA(cudaGetLastError());
       ckks::encode_batch(C, vals, cnt, limbs, dg.scale, enc, stride, C.stream);
-      blk::diag_tile_kernel<<<dim3(C.N / blk::kThreads, limbs, cnt), blk::kThreads, 0, C.stream>>>(
-          enc, cnt, d0, nd, limbs, C.logN, dg.data);
+      {
+        ckks::ProfScope ps(C, "diag_tile", 2.0 * cnt * stride * 8.0, C.stream);
+        blk::diag_tile_kernel<<<dim3(C.N / blk::kThreads, limbs, cnt), blk::kThreads, 0, C.stream>>>(
+            enc, cnt, d0, nd, limbs, C.logN, dg.data);
+      }
       CKKS_CUDA(cudaGetLastError());
     }
     C.release(vals);
@@ -608,7 +660,9 @@ struct ckks_block {
     return rs(acc);
   }
 
+  static constexpr int kHeadLinear = 100;
   void forward(const double* x, int T, double* y);
+  double head_forward(const double* x_last);
   std::vector<int> rotation_indices() const;
 };
 
@@ -837,6 +891,46 @@ void ckks_block::forward(const double* x, int T, double* y) {
   count["input_limbs"] = LX;
 }
 
+// Classifier head on the last token's hidden state
+// (12blocks_head_cpudiagcache_t123_v3.cpp:573-609, multiblock/manual.py:52-80):
+// final LN -> head linear (BSGS) -> SiLU client boundary -> head LN -> dot
+// with (readout_N - readout_A).  The token sits in lane 0 of one ciphertext;
+// both LN gains are folded into the next linear map.  Levels: the input is
+// encrypted at 5 limbs (LN 2, linear 1, decryption at 2), the SiLU output
+// at 5 (LN 2, readout 1, decryption at 2).
+double ckks_block::head_forward(const double* x_last) {
+  const int D = s.D, B = s.B, SL = slots();
+  const int nb = (SL + blk::kThreads - 1) / blk::kThreads;
+  constexpr int kHeadLimbs = 5;
+  if (C.L < kHeadLimbs) throw ckks::Error(CKKS_ELEVEL, "the head needs 5 Q limbs");
+  const double t_start = blk::now_s();
+  double* dx = dbuf(D);
+  CKKS_CUDA(cudaMemcpyAsync(dx, x_last, sizeof(double) * D, cudaMemcpyHostToDevice, C.stream));
+  double* dv = dbuf(SL);
+  blk::pack_kernel<<<dim3(nb, 1), blk::kThreads, 0, C.stream>>>(dx, dv, 1, D, B, SL);
+  const auto xin = client_encrypt(dv, 1, kHeadLimbs);
+  const std::vector<int> one{1};
+  const Ciphertext fl = layernorm(xin, one)[0];
+  const Ciphertext lin = bsgs(babies_of(fl), kHeadLinear);
+  // client: SiLU on lane 0 (12blocks_head..._t123_v3.cpp:740-755)
+  client_decrypt({lin}, dv);
+  blk::silu_kernel<<<nb, blk::kThreads, 0, C.stream>>>(dv, dv, B, D, SL);
+  CKKS_CUDA(cudaGetLastError());
+  const auto act = client_encrypt(dv, 1, kHeadLimbs);
+  count["client_round_trips"] += 1;
+  count["client_logical_instances"] += 1;
+  const Ciphertext hl = layernorm(act, one)[0];
+  const Ciphertext margin = feature_sum(mul_pt_rs(hl, feature_plain(2, readout, hl->limbs())));
+  client_decrypt({margin}, dv);
+  double m = 0.0;
+  CKKS_CUDA(cudaMemcpyAsync(&m, dv, sizeof(double), cudaMemcpyDeviceToHost, C.stream));
+  CKKS_CUDA(cudaStreamSynchronize(C.stream));
+  C.release(dv);
+  C.release(dx);
+  seconds["head_total"] = blk::now_s() - t_start;
+  return m;
+}
+
 void ckks::block_orphan(ckks_block* b) { b->release_device(); }
 
 namespace {
@@ -916,6 +1010,95 @@ int ckks_block_create(ckks_ctx* ctx, const double* ln1, const double* attn_qkv, 
   });
 }
 
+int ckks_head_create(ckks_ctx* ctx, const double* final_ln, const double* head_linear, const double* head_ln,
+                     const double* readout, int d_model, ckks_block** out) {
+  return bguard([&] {
+    if (!ctx || !ctx->c || !out) throw ckks::Error(CKKS_EARG, "null argument");
+    if (!final_ln || !head_linear || !head_ln || !readout) throw ckks::Error(CKKS_EARG, "null weight");
+    ckks::Context& C = *ctx->c;
+    blk::Shape s;
+    s.D = d_model;
+    s.H = 1;
+    s.HD = d_model;
+    s.MLP = d_model;
+    s.T = 1;
+    s.B = 32;
+    s.PW = C.N / 2 / s.B;
+    if (d_model <= 0 || s.PW < d_model) throw ckks::Error(CKKS_EARG, "shape does not fit the slot layout");
+    s.n1 = 32;
+    while (s.n1 * s.n1 > s.PW) s.n1 >>= 1;
+    s.n2 = s.PW / s.n1;
+    s.groups = 1;
+    auto* b = new ckks_block(ctx, s);
+    try {
+      b->nfc = 0;
+      const int D = d_model;
+      std::vector<double> w((size_t)D * D);
+      for (int r = 0; r < D; ++r)
+        for (int c = 0; c < D; ++c) w[(size_t)r * D + c] = head_linear[(size_t)r * D + c] * final_ln[c];
+      b->d_head = upload_matrix(w);
+      b->readout.assign(b->s.PW, 0.0);
+      for (int f = 0; f < D; ++f) b->readout[f] = readout[f] * head_ln[f];
+    } catch (...) {
+      delete b;
+      throw;
+    }
+    {
+      std::lock_guard<std::mutex> lk(ctx->mu);
+      ctx->blocks.insert(b);
+    }
+    *out = b;
+  });
+}
+
+int ckks_head_forward(ckks_block* h, const double* x_last, double* margin) {
+  return bguard([&] {
+    if (!h || !x_last || !margin) throw ckks::Error(CKKS_EARG, "null argument");
+    if (h->orphaned) throw ckks::Error(CKKS_ESTATE, "the head's context was destroyed");
+    if (!h->d_head) throw ckks::Error(CKKS_EARG, "not a head object");
+    *margin = h->head_forward(x_last);
+  });
+}
+
+int ckks_block_release_cache(ckks_block* b, size_t* released) {
+  return bguard([&] {
+    if (!b) throw ckks::Error(CKKS_EARG, "null argument");
+    const size_t r = b->orphaned ? 0 : b->release_cache();
+    if (released) *released = r;
+  });
+}
+
+int ckks_model_forward(ckks_block* const* blocks, int nblocks, ckks_block* head, const double* x, int tokens,
+                       int cached_blocks, double* hidden, double* margin) {
+  return bguard([&] {
+    if (!blocks || nblocks <= 0 || !x || !hidden) throw ckks::Error(CKKS_EARG, "null argument");
+    for (int i = 0; i < nblocks; ++i) {
+      if (!blocks[i] || blocks[i]->orphaned || blocks[i]->d_head) throw ckks::Error(CKKS_EARG, "bad block handle");
+      if (blocks[i]->s.T != tokens || blocks[i]->ctx != blocks[0]->ctx)
+        throw ckks::Error(CKKS_EARG, "blocks differ in token count or context");
+    }
+    if (head && (head->orphaned || !head->d_head || head->ctx != blocks[0]->ctx || head->s.D != blocks[0]->s.D))
+      throw ckks::Error(CKKS_EARG, "bad head handle");
+    if (head && !margin) throw ckks::Error(CKKS_EARG, "null margin");
+    const size_t n = (size_t)tokens * blocks[0]->s.D;
+    std::vector<double> cur(x, x + n), nxt(n);
+    // each block decrypts its output and the next re-encrypts it: the
+    // reference's full-hidden-state refresh between blocks
+    // (12blocks_head..._t123_v3.cpp:452-470)
+    for (int i = 0; i < nblocks; ++i) {
+      blocks[i]->forward(cur.data(), tokens, nxt.data());
+      for (size_t k = 0; k < n; ++k)
+        if (!std::isfinite(nxt[k])) throw ckks::Error(CKKS_ESTATE, "non-finite hidden state at a block boundary");
+      // blocks past the cache budget encode their diagonals again on each use
+      if (i >= cached_blocks) blocks[i]->release_cache();
+      cur.swap(nxt);
+    }
+    std::memcpy(hidden, cur.data(), sizeof(double) * n);
+    // last-token refresh into the head (:480-510)
+    if (head) *margin = head->head_forward(cur.data() + (size_t)(tokens - 1) * blocks[0]->s.D);
+  });
+}
+
 int ckks_block_destroy(ckks_block* b) {
   return bguard([&] {
     if (!b) return;
@@ -950,6 +1133,7 @@ int ckks_block_report(const ckks_block* b, char* buf, size_t size) {
     js += (first ? "\"" : ", \"") + kv.first + "\": " + std::to_string(kv.second);
     first = false;
   }
+  js += std::string(first ? "" : ", ") + "\"diagonal_cache_mib\": " + std::to_string(b->cache_bytes() >> 20);
   js += "}, \"seconds\": {";
   first = true;
   char tmp[64];

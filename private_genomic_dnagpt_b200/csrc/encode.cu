@@ -26,10 +26,12 @@ __device__ __forceinline__ double2 cmul_rn(double2 a, double2 b) {
   return make_double2(__dsub_rn(t1, t2), __dadd_rn(t3, t4));
 }
 
-// inverse butterfly at (i, j) of span len: u = a + b, v = (a - b) * ksi[idx]
-__device__ __forceinline__ void inv_bfly(double2& a, double2& b, const double2* ksi, uint32_t rg, int len, int M) {
-  const int lenq = len << 2, gap = M / lenq;
-  const int idx = (lenq - (int)(rg % (uint32_t)lenq)) * gap;
+// Spans, the cyclotomic order M and the twiddle stride are powers of two:
+// indices come from shifts and masks (lg = log2 span, lm = log2 M).
+// inverse butterfly at (i, j) of span 2^lg: u = a + b, v = (a - b) * ksi[idx]
+__device__ __forceinline__ void inv_bfly(double2& a, double2& b, const double2* ksi, uint32_t rg, int lg, int lm) {
+  const uint32_t lenq = 4u << lg;
+  const int idx = (int)((lenq - (rg & (lenq - 1u))) << (lm - lg - 2));
   const double2 u = make_double2(__dadd_rn(a.x, b.x), __dadd_rn(a.y, b.y));
   const double2 d = make_double2(__dsub_rn(a.x, b.x), __dsub_rn(a.y, b.y));
   a = u;
@@ -37,56 +39,57 @@ __device__ __forceinline__ void inv_bfly(double2& a, double2& b, const double2* 
 }
 
 // forward butterfly: t = b * ksi[idx]; a' = a + t; b' = a - t
-__device__ __forceinline__ void fwd_bfly(double2& a, double2& b, const double2* ksi, uint32_t rg, int len, int M) {
-  const int lenq = len << 2, gap = M / lenq;
-  const int idx = (int)(rg % (uint32_t)lenq) * gap;
+__device__ __forceinline__ void fwd_bfly(double2& a, double2& b, const double2* ksi, uint32_t rg, int lg, int lm) {
+  const uint32_t lenq = 4u << lg;
+  const int idx = (int)((rg & (lenq - 1u)) << (lm - lg - 2));
   const double2 t = cmul_rn(b, __ldg(ksi + idx));
   const double2 u = a;
   a = make_double2(__dadd_rn(u.x, t.x), __dadd_rn(u.y, t.y));
   b = make_double2(__dsub_rn(u.x, t.x), __dsub_rn(u.y, t.y));
 }
 
-__global__ void __launch_bounds__(kThreads) fft_stage_kernel(double2* __restrict__ v, int n, int len, bool inverse,
+__global__ void __launch_bounds__(kThreads) fft_stage_kernel(double2* __restrict__ v, int n, int lg, bool inverse,
                                                              const double2* __restrict__ ksi,
-                                                             const uint32_t* __restrict__ rot_group, int M) {
+                                                             const uint32_t* __restrict__ rot_group, int lm) {
   const int p = blockIdx.x * kThreads + threadIdx.x;
   if (p >= n / 2) return;
-  const int lenh = len >> 1;
-  const int i = (p / lenh) * len, j = p % lenh;
+  const int lenh = 1 << (lg - 1);
+  const int i = (p >> (lg - 1)) << lg, j = p & (lenh - 1);
   double2* vec = v + (size_t)blockIdx.y * n;
   double2 a = vec[i + j], b = vec[i + j + lenh];
   const uint32_t rg = __ldg(rot_group + j);
   if (inverse)
-    inv_bfly(a, b, ksi, rg, len, M);
+    inv_bfly(a, b, ksi, rg, lg, lm);
   else
-    fwd_bfly(a, b, ksi, rg, len, M);
+    fwd_bfly(a, b, ksi, rg, lg, lm);
   vec[i + j] = a;
   vec[i + j + lenh] = b;
 }
 
 // all stages with span <= blk inside one aligned block of blk entries
-__global__ void __launch_bounds__(kThreads) fft_smem_kernel(double2* __restrict__ v, int n, int blk, bool inverse,
+__global__ void __launch_bounds__(kThreads) fft_smem_kernel(double2* __restrict__ v, int n, int lb, bool inverse,
                                                             const double2* __restrict__ ksi,
-                                                            const uint32_t* __restrict__ rot_group, int M) {
+                                                            const uint32_t* __restrict__ rot_group, int lm) {
   __shared__ double2 s[kSmemLen];
+  const int blk = 1 << lb;
   double2* vec = v + (size_t)blockIdx.y * n + (size_t)blockIdx.x * blk;
   for (int e = threadIdx.x; e < blk; e += kThreads) s[e] = vec[e];
   __syncthreads();
   if (inverse) {
-    for (int len = blk; len >= 2; len >>= 1) {
-      const int lenh = len >> 1;
+    for (int lg = lb; lg >= 1; --lg) {
+      const int lenh = 1 << (lg - 1);
       for (int p = threadIdx.x; p < blk / 2; p += kThreads) {
-        const int i = (p / lenh) * len, j = p % lenh;
-        inv_bfly(s[i + j], s[i + j + lenh], ksi, __ldg(rot_group + j), len, M);
+        const int i = (p >> (lg - 1)) << lg, j = p & (lenh - 1);
+        inv_bfly(s[i + j], s[i + j + lenh], ksi, __ldg(rot_group + j), lg, lm);
       }
       __syncthreads();
     }
   } else {
-    for (int len = 2; len <= blk; len <<= 1) {
-      const int lenh = len >> 1;
+    for (int lg = 1; lg <= lb; ++lg) {
+      const int lenh = 1 << (lg - 1);
       for (int p = threadIdx.x; p < blk / 2; p += kThreads) {
-        const int i = (p / lenh) * len, j = p % lenh;
-        fwd_bfly(s[i + j], s[i + j + lenh], ksi, __ldg(rot_group + j), len, M);
+        const int i = (p >> (lg - 1)) << lg, j = p & (lenh - 1);
+        fwd_bfly(s[i + j], s[i + j + lenh], ksi, __ldg(rot_group + j), lg, lm);
       }
       __syncthreads();
     }
@@ -236,24 +239,26 @@ __global__ void __launch_bounds__(kThreads) take_real_kernel(const double2* __re
   out[j] = v[j].x;
 }
 
+constexpr int kSmemLog = 11;  // log2 kSmemLen
+
 void fft_inverse_batch(const Context& c, double2* v, int batch, cudaStream_t st) {
-  const int n = c.N / 2, M = 2 * c.N;
-  const int blk = n < kSmemLen ? n : kSmemLen;
-  for (int len = n; len > blk; len >>= 1) {
-    fft_stage_kernel<<<dim3((n / 2 + kThreads - 1) / kThreads, batch), kThreads, 0, st>>>(v, n, len, true, c.d_ksi,
-                                                                                          c.d_rot_group, M);
+  const int ln = c.logN - 1, n = 1 << ln, lm = c.logN + 1;
+  const int lb = ln < kSmemLog ? ln : kSmemLog;
+  for (int lg = ln; lg > lb; --lg) {
+    fft_stage_kernel<<<dim3((n / 2 + kThreads - 1) / kThreads, batch), kThreads, 0, st>>>(v, n, lg, true, c.d_ksi,
+                                                                                          c.d_rot_group, lm);
   }
-  fft_smem_kernel<<<dim3(n / blk, batch), kThreads, 0, st>>>(v, n, blk, true, c.d_ksi, c.d_rot_group, M);
+  fft_smem_kernel<<<dim3(n >> lb, batch), kThreads, 0, st>>>(v, n, lb, true, c.d_ksi, c.d_rot_group, lm);
   CKKS_CUDA(cudaGetLastError());
 }
 
 void fft_forward_batch(const Context& c, double2* v, int batch, cudaStream_t st) {
-  const int n = c.N / 2, M = 2 * c.N;
-  const int blk = n < kSmemLen ? n : kSmemLen;
-  fft_smem_kernel<<<dim3(n / blk, batch), kThreads, 0, st>>>(v, n, blk, false, c.d_ksi, c.d_rot_group, M);
-  for (int len = blk * 2; len <= n; len <<= 1) {
-    fft_stage_kernel<<<dim3((n / 2 + kThreads - 1) / kThreads, batch), kThreads, 0, st>>>(v, n, len, false, c.d_ksi,
-                                                                                          c.d_rot_group, M);
+  const int ln = c.logN - 1, n = 1 << ln, lm = c.logN + 1;
+  const int lb = ln < kSmemLog ? ln : kSmemLog;
+  fft_smem_kernel<<<dim3(n >> lb, batch), kThreads, 0, st>>>(v, n, lb, false, c.d_ksi, c.d_rot_group, lm);
+  for (int lg = lb + 1; lg <= ln; ++lg) {
+    fft_stage_kernel<<<dim3((n / 2 + kThreads - 1) / kThreads, batch), kThreads, 0, st>>>(v, n, lg, false, c.d_ksi,
+                                                                                          c.d_rot_group, lm);
   }
   CKKS_CUDA(cudaGetLastError());
 }
@@ -267,9 +272,15 @@ void encode_batch(const Context& c, const double* d_values, int batch, int limbs
   const int n = c.N / 2;
   double2* v = (double2*)c.alloc(sizeof(double2) * (size_t)batch * n);
   const dim3 g((n + kThreads - 1) / kThreads, batch);
-  load_real_kernel<<<g, kThreads, 0, st>>>(d_values, v, n);
-  fft_inverse_batch(c, v, batch, st);
-  round_kernel<<<g, kThreads, 0, st>>>(v, n, c.logN - 1, scale, out, out_stride, limbs, c.d_mods);
+  {
+    ProfScope ps(c, "encode_fft", 2.0 * 16.0 * n * batch, st);
+    load_real_kernel<<<g, kThreads, 0, st>>>(d_values, v, n);
+    fft_inverse_batch(c, v, batch, st);
+  }
+  {
+    ProfScope ps(c, "encode_round", (16.0 * n + 8.0 * 2 * n * limbs) * batch, st);
+    round_kernel<<<g, kThreads, 0, st>>>(v, n, c.logN - 1, scale, out, out_stride, limbs, c.d_mods);
+  }
   CKKS_CUDA(cudaGetLastError());
   c.release(v);
   if (out_stride == (size_t)limbs * c.N) {

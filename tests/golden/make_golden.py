@@ -4,6 +4,10 @@ Python modules (run in a container that has the reference tree at
 
   plain_block_t8.npz  fhe/realweights/manual.py block_reference on the seeded
                       synthetic block (seed 3, T = 8) -- pins oracle/plain_block.py
+  plain_head.npz      fhe/multiblock/manual.py classifier_head_reference on
+                      seeded synthetic head weights and hidden states (seed
+                      11 weights, seed 12 hidden, 4 tokens) with a two-row
+                      readout [N, A] -- pins oracle/plain_block.py head()
   simd_layout_b32.json + simd_layout_b32.npz
                       fhe/gpu_real_scheme_b/simd_layout.py at batch width 32,
                       one copy (the 32-tokens-per-ciphertext layout): slot map,
@@ -28,7 +32,7 @@ sys.path.insert(0, os.path.join(REF, "fhe", "realweights"))
 import manual  # noqa: E402  (reference: fhe/realweights/manual.py)
 import simd_layout as sl  # noqa: E402  (reference: fhe/gpu_real_scheme_b/simd_layout.py)
 
-from oracle.plain_block import synthetic_input, synthetic_weights  # noqa: E402
+from oracle.plain_block import synthetic_head_weights, synthetic_input, synthetic_weights  # noqa: E402
 from tests.golden.inputs import layout_inputs  # noqa: E402
 
 
@@ -40,6 +44,24 @@ def plain_block():
     np.savez_compressed(os.path.join(HERE, "plain_block_t8.npz"), seed_weights=3, seed_input=4,
                         block_output=ref["block_output"], ln1_output=ref["ln1_output"],
                         attention_scores=ref["attention_scores"], residual1=ref["residual1"])
+
+
+def plain_head():
+    import importlib.util
+    spec = importlib.util.spec_from_file_location("multiblock_manual",
+                                                  os.path.join(REF, "fhe", "multiblock", "manual.py"))
+    mb = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(mb)  # reference: fhe/multiblock/manual.py
+    hw = synthetic_head_weights(11)
+    rng = np.random.default_rng(13)
+    r_a = rng.normal(0.0, 0.02, hw["readout"].shape[0])
+    readout_rows = np.stack([hw["readout"] + r_a, r_a])  # rows N and A: N - A = readout
+    hidden = synthetic_input(12, 4)
+    ref = mb.classifier_head_reference(hidden, {"final_ln": hw["final_ln"], "head_linear": hw["head_linear"],
+                                                "head_ln": hw["head_ln"], "head_readout": readout_rows})
+    np.savez_compressed(os.path.join(HERE, "plain_head.npz"), seed_weights=11, seed_hidden=12, seed_readout_a=13,
+                        readout_rows=readout_rows, logits=ref["logits"], head_ln_output=ref["head_ln_output"],
+                        margin=ref["logits"][:, 0] - ref["logits"][:, 1])
 
 
 def layout():
@@ -75,5 +97,6 @@ def layout():
 
 if __name__ == "__main__":
     plain_block()
+    plain_head()
     layout()
     print("golden fixtures written")

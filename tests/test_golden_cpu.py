@@ -2,6 +2,9 @@
 
   plain_block_t8.npz    fhe/realweights/manual.py block_reference  -> pins
                         oracle/plain_block.py (the decrypted-output checker)
+  plain_head.npz        fhe/multiblock/manual.py classifier_head_reference
+                        (readout rows N, A) -> pins oracle/plain_block.py
+                        head() and its N - A margin
   simd_layout_b32.*     fhe/gpu_real_scheme_b/simd_layout.py at 32 tokens per
                         ciphertext, one copy -> pins the engine's host-side
                         block schedule (causal lane shifts, BSGS diagonals)
@@ -28,6 +31,22 @@ def test_plain_block_oracle_matches_reference_manual_py():
     for k in ("block_output", "ln1_output", "attention_scores", "residual1"):
         ref = g[k]
         assert np.abs(got[k] - ref).max() <= 1e-12 * max(1.0, np.abs(ref).max()), k
+
+
+def test_plain_head_oracle_matches_reference_manual_py():
+    g = np.load(os.path.join(GOLD, "plain_head.npz"))
+    hw = plain_block.synthetic_head_weights(int(g["seed_weights"]))
+    hidden = plain_block.synthetic_input(int(g["seed_hidden"]), 4)
+    assert np.abs(g["readout_rows"][0] - g["readout_rows"][1] - hw["readout"]).max() < 1e-15
+    for t in range(4):
+        m = plain_block.head(hidden[t], hw)
+        assert abs(m - g["margin"][t]) <= 1e-12 * max(1.0, abs(g["margin"][t])), t
+    # a two-block model ends in the same head on its last token
+    w = [plain_block.synthetic_weights(3), plain_block.synthetic_weights(4)]
+    x = plain_block.synthetic_input(4, 5)
+    h, m = plain_block.model(x, w, hw)
+    assert np.allclose(h, plain_block.block(plain_block.block(x, w[0]), w[1]), rtol=0, atol=0)
+    assert m == plain_block.head(h[-1], hw)
 
 
 def test_causal_lane_shifts_match_simd_layout():
