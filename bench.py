@@ -363,6 +363,80 @@ def run_engine(args):
         dist.destroy_process_group()
 
 
+def run_shard(args):
+    """One block sharded over the torchrun ranks (strong scaling): token
+    groups and (query, key) tiles split across ranks, Q/K/V broadcasts, a
+    score all-reduce, partial-context merges and an output all-reduce over
+    NCCL between the stages (private_genomic_dnagpt_b200/shard.py).  Every
+    rank holds the same keys (same seed).  value = device time of one block
+    from the first stage to the assembled output, max over ranks."""
+    import datetime
+
+    import torch
+    import torch.distributed as dist
+    import private_genomic_dnagpt_b200 as eng
+    from private_genomic_dnagpt_b200 import shard
+    from oracle import plain_block
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
+    os.environ.setdefault("MASTER_PORT", "29533")
+    torch.cuda.set_device(local)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=600),
+                            device_id=torch.device("cuda", local))
+    cc = eng.GenCryptoContext(eng.CCParams(ring_dim_log=LOG_N, limbs=LIMBS, dnum=DNUM, seed=1, device=local))
+    cc.KeyGen()
+    cc.EvalMultKeyGen()
+    w = plain_block.synthetic_weights(5)
+    x = plain_block.synthetic_input(6, args.tokens)
+    block = eng.EncryptedBlock(cc, w, args.tokens)
+    cc.EvalRotateKeyGen(block.rotation_indices())
+    io = shard.EngineIO(block)
+    sb = shard.ShardedBlock(io, args.tokens, 32, 12, plain_block.D, dist, "cuda")
+    stream = torch.cuda.ExternalStream(cc.stream_handle())
+    ref = plain_block.block(x, w)
+    for _ in range(args.warmup):
+        y = sb.forward(x)
+    err = plain_block.rel_inf(ref, y)
+    assert err < 1e-6, f"sharded block output error {err}"
+    cc.Synchronize()
+    dist.barrier()
+    steps = []
+    with ClockSampler(local) as clk:
+        for _ in range(args.steps):
+            e0 = torch.cuda.Event(enable_timing=True)
+            e1 = torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            y = sb.forward(x)
+            e1.record(stream)
+            e1.synchronize()
+            steps.append(e0.elapsed_time(e1) / 1e3)
+        cc.Synchronize()
+        dist.barrier()
+    t = torch.tensor([float(np.mean(steps))], device="cuda", dtype=torch.float64)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    value = float(t[0])
+    if rank == 0:
+        groups = -(-args.tokens // 32)
+        line = {
+            "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": value * 1e3, "higher_is_better": False, "scaling": "strong",
+            "vs_baseline": value / REF_A100_BLOCK_S, "dtype": "u64", "data": "synthetic",
+            "config": {"workload": WORKLOAD, "parallelism": f"shard{world} (token groups + attention tiles)",
+                       "flush": "inputs > L2 (keys, diagonals)", "rel_inf_vs_plaintext": err,
+                       "plan": [{"groups": rp.groups, "tiles": rp.tiles} for rp in sb.plan]},
+            "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": groups * cc.slots * 8,
+                    "d2h_bytes_per_step": groups * cc.slots * 8},
+            "per_step_s": [round(v, 4) for v in steps],
+            "clocks": clk.summary(),
+        }
+        print(json.dumps(line), flush=True)
+    dist.barrier()
+    dist.destroy_process_group()
+
+
 def run_model(args):
     """Chained blocks (the two-block and 12-block configurations) with the
     full-hidden-state client refresh between blocks and, with --head, the
@@ -546,6 +620,8 @@ def main():
     ap.add_argument("--blocks", type=int, default=1)
     ap.add_argument("--head", action="store_true")
     ap.add_argument("--cached-blocks", type=int, default=-1)
+    # one block sharded over the torchrun ranks instead of one replica per rank
+    ap.add_argument("--shard", action="store_true")
     args = ap.parse_args()
     if args.impl == "reference":
         run_reference(args)
@@ -553,6 +629,8 @@ def main():
         run_primitive(args)
     elif args.blocks > 1 or args.head:
         run_model(args)
+    elif args.shard:
+        run_shard(args)
     else:
         run_engine(args)
 

@@ -105,6 +105,25 @@ int ckks_ct_export(ckks_ctx* ctx, const ckks_ct* ct, uint64_t* host, size_t word
 int ckks_ct_import(ckks_ctx* ctx, ckks_ct* ct, const uint64_t* host, int limbs, double scale, int noise_deg);
 int ckks_pt_export(ckks_ctx* ctx, const ckks_pt* pt, uint64_t* host, size_t words);
 int ckks_pt_import(ckks_ctx* ctx, ckks_pt* pt, const uint64_t* host, int limbs, double scale);
+/* The same transfer between device buffers, enqueued on the context stream:
+ * the exchange of ciphertexts between ranks (an NCCL all-gather of these
+ * buffers on the same stream).  No counterpart in the reference, whose
+ * shards exchange serialized files (shard_layout.py, docs/hybrid/tasks.md). */
+int ckks_ct_export_device(ckks_ctx* ctx, const ckks_ct* ct, uint64_t* dev, size_t words);
+int ckks_ct_import_device(ckks_ctx* ctx, ckks_ct* ct, const uint64_t* dev, int limbs, double scale, int noise_deg);
+
+/* Binary wire format of ciphertexts and switching keys: a 48-byte header
+ * (magic "CKB2", version 1, kind, log2 N, Q limbs, special limbs, polynomials,
+ * noise degree, scale, rotation index, digits), the modulus of every limb,
+ * then the residues.  Readers check magic, version, ring degree and every
+ * modulus against their context.  Serialize returns the byte count (with
+ * buf == NULL: the size needed) or -1; the reference's serialize_writer /
+ * serialize_reader drivers use OpenFHE's own format instead. */
+long long ckks_ct_serialize(ckks_ctx* ctx, const ckks_ct* ct, uint8_t* buf, size_t cap);
+int ckks_ct_deserialize(ckks_ctx* ctx, ckks_ct* ct, const uint8_t* buf, size_t size);
+/* k = 0: relinearisation key; else the rotation key of index k */
+long long ckks_key_serialize(ckks_ctx* ctx, int k, uint8_t* buf, size_t cap);
+int ckks_key_deserialize(ckks_ctx* ctx, const uint8_t* buf, size_t size);
 int ckks_ct_copy(ckks_ctx* ctx, const ckks_ct* src, ckks_ct* dst);
 
 /* MakeCKKSPackedPlaintext(values, 1, level, nullptr, N/2) (T123.cpp:955-960,
@@ -205,6 +224,29 @@ int ckks_block_rotation_indices(const ckks_block* b, int* out, int cap);
 int ckks_block_forward(ckks_block* b, const double* x, int tokens, double* y);
 /* operation counts and stage seconds of the last forward, JSON text */
 int ckks_block_report(const ckks_block* b, char* buf, size_t size);
+/* Stages of one block evaluation over unit subsets, for sharding one block
+ * over several devices (one context per device, identical keys from the same
+ * seed).  A forward is inputs -> qkv(groups) -> scores(tiles) -> softmax ->
+ * context(tiles) -> output(groups); between stages the ranks exchange the
+ * Q/K/V ciphertexts of their groups, the score matrix (disjoint entries:
+ * a sum over ranks of zero-initialised buffers) and the partial contexts
+ * (summed with EvalAdd).  Tiles are (query group, key group) pairs as 2n
+ * ints.  d_scores: [tokens][heads][tokens] float64 on the device.  The units
+ * follow the independent work of T123.cpp:780-790 (groups), :798-833 (tiles)
+ * and shard_layout.py (exact EvalAdd merges of partial sums). */
+int ckks_block_shard_inputs(ckks_block* b, const double* x, int tokens);
+int ckks_block_shard_qkv(ckks_block* b, const int* groups, int n);
+int ckks_block_shard_scores(ckks_block* b, const int* pairs, int n, double* d_scores);
+int ckks_block_shard_softmax(ckks_block* b, const double* d_scores);
+int ckks_block_shard_context(ckks_block* b, const int* pairs, int n);
+/* writes the rows of the given groups into y [tokens, d_model] (host) */
+int ckks_block_shard_output(ckks_block* b, const int* groups, int n, double* y);
+/* state ciphertexts by kind (0 Q, 1 K, 2 V, 3 partial context, 4 encrypted
+ * input) and token group: get copies into `out`; set copies from `in` (a
+ * handle without data clears the entry) */
+int ckks_block_state_get(ckks_block* b, int kind, int group, ckks_ct* out);
+int ckks_block_state_set(ckks_block* b, int kind, int group, const ckks_ct* in);
+
 /* drop the block's encoded BSGS diagonals and masks (about 26 GB per block
  * at N = 2^16); the next forward encodes them again on the device */
 int ckks_block_release_cache(ckks_block* b, size_t* released_bytes);

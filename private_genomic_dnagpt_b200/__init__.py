@@ -130,6 +130,20 @@ _SIGS = [
     ("ckks_block_forward", ctypes.c_int, [_vp, _f64p, ctypes.c_int, _f64p]),
     ("ckks_block_report", ctypes.c_int, [_vp, ctypes.c_char_p, ctypes.c_size_t]),
     ("ckks_block_release_cache", ctypes.c_int, [_vp, ctypes.POINTER(ctypes.c_size_t)]),
+    ("ckks_block_shard_inputs", ctypes.c_int, [_vp, _f64p, ctypes.c_int]),
+    ("ckks_block_shard_qkv", ctypes.c_int, [_vp, ctypes.POINTER(ctypes.c_int), ctypes.c_int]),
+    ("ckks_block_shard_scores", ctypes.c_int, [_vp, ctypes.POINTER(ctypes.c_int), ctypes.c_int, _vp]),
+    ("ckks_block_shard_softmax", ctypes.c_int, [_vp, _vp]),
+    ("ckks_block_shard_context", ctypes.c_int, [_vp, ctypes.POINTER(ctypes.c_int), ctypes.c_int]),
+    ("ckks_block_shard_output", ctypes.c_int, [_vp, ctypes.POINTER(ctypes.c_int), ctypes.c_int, _f64p]),
+    ("ckks_block_state_get", ctypes.c_int, [_vp, ctypes.c_int, ctypes.c_int, _vp]),
+    ("ckks_block_state_set", ctypes.c_int, [_vp, ctypes.c_int, ctypes.c_int, _vp]),
+    ("ckks_ct_export_device", ctypes.c_int, [_vp, _vp, _vp, ctypes.c_size_t]),
+    ("ckks_ct_import_device", ctypes.c_int, [_vp, _vp, _vp, ctypes.c_int, ctypes.c_double, ctypes.c_int]),
+    ("ckks_ct_serialize", ctypes.c_longlong, [_vp, _vp, ctypes.c_char_p, ctypes.c_size_t]),
+    ("ckks_ct_deserialize", ctypes.c_int, [_vp, _vp, ctypes.c_char_p, ctypes.c_size_t]),
+    ("ckks_key_serialize", ctypes.c_longlong, [_vp, ctypes.c_int, ctypes.c_char_p, ctypes.c_size_t]),
+    ("ckks_key_deserialize", ctypes.c_int, [_vp, ctypes.c_char_p, ctypes.c_size_t]),
     ("ckks_head_create", ctypes.c_int, [_vp] + [_f64p] * 4 + [ctypes.c_int, ctypes.POINTER(_vp)]),
     ("ckks_head_forward", ctypes.c_int, [_vp, _f64p, _f64p]),
     ("ckks_model_forward", ctypes.c_int, [ctypes.POINTER(_vp), ctypes.c_int, _vp, _f64p, ctypes.c_int, ctypes.c_int,
@@ -386,6 +400,43 @@ class CryptoContext:
         return pt
 
     # -- raw ops (no scale management) ------------------------------------
+    def export_device(self, ct: Ciphertext, dev_ptr: int, words: int):
+        """Copy ct's limbs (c0 then c1) into a device buffer, on the engine stream."""
+        _check(lib().ckks_ct_export_device(self.h, ct.h, ctypes.c_void_p(dev_ptr), words))
+
+    def import_device(self, dev_ptr: int, limbs: int, scale: float, deg: int = 1) -> Ciphertext:
+        ct = self._new()
+        _check(lib().ckks_ct_import_device(self.h, ct.h, ctypes.c_void_p(dev_ptr), limbs, scale, deg))
+        return ct
+
+    def serialize(self, ct: Ciphertext) -> bytes:
+        """Binary wire format: header, moduli, residues (checked on load)."""
+        n = lib().ckks_ct_serialize(self.h, ct.h, None, 0)
+        if n < 0:
+            _check(2)
+        buf = ctypes.create_string_buffer(n)
+        if lib().ckks_ct_serialize(self.h, ct.h, buf, n) != n:
+            _check(1)
+        return buf.raw
+
+    def deserialize(self, data: bytes) -> Ciphertext:
+        ct = self._new()
+        _check(lib().ckks_ct_deserialize(self.h, ct.h, data, len(data)))
+        return ct
+
+    def serialize_key(self, k: int = 0) -> bytes:
+        """Switching key in the wire format: relinearisation (k = 0) or rotation k."""
+        n = lib().ckks_key_serialize(self.h, k, None, 0)
+        if n < 0:
+            _check(4)
+        buf = ctypes.create_string_buffer(n)
+        if lib().ckks_key_serialize(self.h, k, buf, n) != n:
+            _check(1)
+        return buf.raw
+
+    def deserialize_key(self, data: bytes):
+        _check(lib().ckks_key_deserialize(self.h, data, len(data)))
+
     def _new(self) -> Ciphertext:
         return Ciphertext(self)
 
@@ -568,6 +619,49 @@ class EncryptedBlock:
         lib().ckks_block_report(self.h, buf, n + 1)
         return json.loads(buf.value.decode())
 
+
+    # ---- stages over unit subsets (sharding one block over ranks) ----
+    def shard_inputs(self, x: np.ndarray):
+        x = np.ascontiguousarray(x, np.float64)
+        _check(lib().ckks_block_shard_inputs(self.h, _f64(x), x.shape[0]))
+
+    def shard_qkv(self, groups):
+        g = (ctypes.c_int * max(1, len(groups)))(*groups)
+        _check(lib().ckks_block_shard_qkv(self.h, g, len(groups)))
+
+    @staticmethod
+    def _pairs(pairs):
+        flat = [v for p in pairs for v in p]
+        return (ctypes.c_int * max(1, len(flat)))(*flat), len(pairs)
+
+    def shard_scores(self, pairs, d_scores_ptr: int):
+        p, n = self._pairs(pairs)
+        _check(lib().ckks_block_shard_scores(self.h, p, n, ctypes.c_void_p(d_scores_ptr)))
+
+    def shard_softmax(self, d_scores_ptr: int):
+        _check(lib().ckks_block_shard_softmax(self.h, ctypes.c_void_p(d_scores_ptr)))
+
+    def shard_context(self, pairs):
+        p, n = self._pairs(pairs)
+        _check(lib().ckks_block_shard_context(self.h, p, n))
+
+    def shard_output(self, groups, y: np.ndarray):
+        assert y.dtype == np.float64 and y.flags["C_CONTIGUOUS"]
+        g = (ctypes.c_int * max(1, len(groups)))(*groups)
+        _check(lib().ckks_block_shard_output(self.h, g, len(groups), _f64(y)))
+
+    def state_get(self, kind: int, group: int):
+        """Copy of a state ciphertext (0 Q, 1 K, 2 V, 3 partial context,
+        4 encrypted input) of a token group, or None if absent."""
+        out = self.cc._new()
+        rc = lib().ckks_block_state_get(self.h, kind, group, out.h)
+        if rc == 2:  # CKKS_ESTATE: not present
+            return None
+        _check(rc)
+        return out
+
+    def state_set(self, kind: int, group: int, ct):
+        _check(lib().ckks_block_state_set(self.h, kind, group, ct.h))
 
     def release_cache(self) -> int:
         """Drop the encoded diagonals (re-encoded on the next forward);

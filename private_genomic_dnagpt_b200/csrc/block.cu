@@ -203,12 +203,13 @@ __global__ void pack_kernel(const double* __restrict__ x, double* __restrict__ v
   vals[(size_t)g * slots + i] = (f < D && tok < T) ? x[(size_t)tok * D + f] : 0.0;
 }
 
+// token group g0 + blockIdx.y from slot vector blockIdx.y of vals
 __global__ void unpack_kernel(const double* __restrict__ vals, double* __restrict__ y, int T, int D, int B,
-                              int slots) {
+                              int slots, int g0) {
   const int i = blockIdx.x * kThreads + threadIdx.x;
   if (i >= slots) return;
-  const int g = blockIdx.y, f = i / B, t = i % B, tok = g * B + t;
-  if (f < D && tok < T) y[(size_t)tok * D + f] = vals[(size_t)g * slots + i];
+  const int g = g0 + blockIdx.y, f = i / B, t = i % B, tok = g * B + t;
+  if (f < D && tok < T) y[(size_t)tok * D + f] = vals[(size_t)blockIdx.y * slots + i];
 }
 
 struct TileTag {
@@ -310,6 +311,16 @@ struct ckks_block {
     cudaFree(d_proj2);
     cudaFree(d_head);
     d_qkv = d_proj = d_fc = d_proj2 = d_head = nullptr;
+    st_x.clear();
+    st_q.clear();
+    st_k.clear();
+    st_v.clear();
+    st_ctx.clear();
+    C.release(st_prob);
+    st_prob = nullptr;
+    if (ev_in) cudaEventDestroy(ev_in);
+    if (ev_out) cudaEventDestroy(ev_out);
+    ev_in = ev_out = nullptr;
     orphaned = true;
   }
   // drop the encoded diagonals and masks (rebuilt on the next use); returns
@@ -661,6 +672,25 @@ struct ckks_block {
   }
 
   static constexpr int kHeadLinear = 100;
+  // evaluation state between the stages of one forward
+  std::vector<Ciphertext> st_x, st_q, st_k, st_v, st_ctx;
+  double* st_prob = nullptr;
+  cudaEvent_t ev_in = nullptr, ev_out = nullptr;
+  double t_start = 0.0, t_stage = 0.0, alloc_s0 = 0.0;
+  long alloc_n0 = 0;
+  void stamp(const char* k) {
+    cc.Synchronize();
+    const double n = blk::now_s();
+    seconds[k] += n - t_stage;
+    t_stage = n;
+  }
+  std::vector<blk::TileTag> tags_of(int kg, const std::vector<std::pair<int, int>>& pairs) const;
+  void shard_inputs(const double* x, int T);
+  void shard_qkv(const std::vector<int>& groups);
+  void shard_scores(const std::vector<std::pair<int, int>>& pairs, double* d_scores);
+  void shard_softmax(const double* d_scores);
+  void shard_context(const std::vector<std::pair<int, int>>& pairs);
+  void shard_output(const std::vector<int>& groups, double* y);
   void forward(const double* x, int T, double* y);
   double head_forward(const double* x_last);
   std::vector<int> rotation_indices() const;
@@ -690,79 +720,97 @@ std::vector<int> ckks_block::rotation_indices() const {
   return v;
 }
 
-void ckks_block::forward(const double* x, int T, double* y) {
+// ---- stages of one block evaluation ---------------------------------------
+// A forward is shard_inputs, shard_qkv(groups), shard_scores(tiles),
+// shard_softmax, shard_context(tiles), shard_output(groups).  Run on every
+// unit they give one block on one device; run on a subset of the token
+// groups / (query group, key group) tiles by each rank, with the Q/K/V and
+// partial-context ciphertexts and the score matrix exchanged between the
+// stages, they shard one block over several devices.
+
+std::vector<blk::TileTag> ckks_block::tags_of(int kg, const std::vector<std::pair<int, int>>& pairs) const {
+  std::vector<blk::TileTag> t;
+  for (const auto& pr : pairs)
+    if (pr.second == kg)
+      for (int d : blk::active_shifts(s.T, s.B, pr.first, kg)) t.push_back({pr.first, kg, d});
+  return t;
+}
+
+void ckks_block::shard_inputs(const double* x, int T) {
   if (T != s.T) throw ckks::Error(CKKS_EARG, "token count differs from the block's");
-  const int G = s.groups, B = s.B, D = s.D, PW = s.PW, H = s.H, HD = s.HD;
-  const int SL = slots();
+  const int G = s.groups, D = s.D, SL = slots();
   const int nb = (SL + blk::kThreads - 1) / blk::kThreads;
   count.clear();
   seconds.clear();
   client_seconds = 0.0;
-  const double alloc_s0 = C.alloc_seconds;
-  const long alloc_n0 = C.alloc_calls;
-  const double t_start = blk::now_s();
-  auto stamp = [&](const char* k, double& t) {
-    cc.Synchronize();
-    const double n = blk::now_s();
-    seconds[k] += n - t;
-    t = n;
-  };
-  double t = t_start;
-  std::vector<int> active(G);
-  for (int g = 0; g < G; ++g) active[g] = s.count(g);
+  alloc_s0 = C.alloc_seconds;
+  alloc_n0 = C.alloc_calls;
+  t_start = t_stage = blk::now_s();
+  st_x.assign(G, Ciphertext());
+  st_q.assign(G, Ciphertext());
+  st_k.assign(G, Ciphertext());
+  st_v.assign(G, Ciphertext());
+  st_ctx.assign(G, Ciphertext());
   // client: pack and encrypt the embeddings (T123.cpp:1642-1661)
   double* dx = dbuf((size_t)T * D);
   CKKS_CUDA(cudaMemcpyAsync(dx, x, sizeof(double) * T * D, cudaMemcpyHostToDevice, C.stream));
   double* dvals = dbuf((size_t)G * SL);
-  blk::pack_kernel<<<dim3(nb, G), blk::kThreads, 0, C.stream>>>(dx, dvals, T, D, B, SL);
-  const std::vector<Ciphertext> xin = client_encrypt(dvals, G, LX);
+  blk::pack_kernel<<<dim3(nb, G), blk::kThreads, 0, C.stream>>>(dx, dvals, T, D, s.B, SL);
+  st_x = client_encrypt(dvals, G, LX);
   C.release(dvals);
   C.release(dx);
-  stamp("encrypt_inputs", t);
+  stamp("encrypt_inputs");
   // device-timed span from encrypted inputs resident to encrypted outputs
   // resident (client refreshes included: the stream waits on them)
-  cudaEvent_t ev0, ev1;
-  CKKS_CUDA(cudaEventCreate(&ev0));
-  CKKS_CUDA(cudaEventCreate(&ev1));
-  CKKS_CUDA(cudaEventRecord(ev0, C.stream));
+  if (!ev_in) CKKS_CUDA(cudaEventCreate(&ev_in));
+  if (!ev_out) CKKS_CUDA(cudaEventCreate(&ev_out));
+  CKKS_CUDA(cudaEventRecord(ev_in, C.stream));
+}
 
-  // LN1 + QKV
-  std::vector<Ciphertext> Q(G), K(G), V(G);
-  {
-    const auto nrm = layernorm(xin, active);
-    for (int g = 0; g < G; ++g) {
-      const auto baby = babies_of(nrm[g]);
-      Q[g] = bsgs(baby, 0);
-      K[g] = bsgs(baby, 1);
-      V[g] = bsgs(baby, 2);
-    }
+// LN1 + QKV of the given token groups
+void ckks_block::shard_qkv(const std::vector<int>& groups) {
+  if (groups.empty()) return;
+  std::vector<Ciphertext> xs;
+  std::vector<int> act;
+  for (int g : groups) {
+    if (g < 0 || g >= s.groups || !st_x[g]) throw ckks::Error(CKKS_ESTATE, "inputs not encrypted");
+    xs.push_back(st_x[g]);
+    act.push_back(s.count(g));
   }
-  stamp("ln1_qkv", t);
+  const auto nrm = layernorm(xs, act);
+  for (size_t i = 0; i < groups.size(); ++i) {
+    const int g = groups[i];
+    const auto baby = babies_of(nrm[i]);
+    st_q[g] = bsgs(baby, 0);
+    st_k[g] = bsgs(baby, 1);
+    st_v[g] = bsgs(baby, 2);
+  }
+  stamp("ln1_qkv");
+}
 
-  // scores: server products and head sums, client gathers them on the device
-  const int lk = Q[0]->limbs() - 1;  // shifted value level
-  // scores are only decrypted: keys shifted from 4 limbs, products of 3-limb
-  // operands, head sums and decryption at 2
-  const int lks = std::min(lk, 3);
-  std::vector<Ciphertext> Qr(G);
-  for (int g = 0; g < G; ++g) Qr[g] = reduce_to(Q[g], lks);
-  double* d_scores = dbuf((size_t)T * H * T);
-  double* d_prob = dbuf((size_t)T * H * T);
-  CKKS_CUDA(cudaMemsetAsync(d_scores, 0xFF, sizeof(double) * T * H * T, C.stream));  // NaN = missing
-  std::vector<std::vector<blk::TileTag>> tags(G);
-  for (int kg = 0; kg < G; ++kg)
-    for (int qg = kg; qg < G; ++qg)
-      for (int d : blk::active_shifts(T, B, qg, kg)) tags[kg].push_back({qg, kg, d});
+// scores of the given (query group, key group) tiles written into d_scores
+// ([q][head][k] doubles on the device): server products and head-window sums,
+// the client decrypts and gathers them on the device
+void ckks_block::shard_scores(const std::vector<std::pair<int, int>>& pairs, double* d_scores) {
+  const int T = s.T, H = s.H, HD = s.HD, B = s.B, SL = slots();
   const double inv_sqrt_hd = 1.0 / std::sqrt((double)HD);
-  for (int kg = 0; kg < G; ++kg) {
+  for (int kg = 0; kg < s.groups; ++kg) {
+    const auto tags = tags_of(kg, pairs);
+    if (tags.empty()) continue;
+    if (!st_k[kg]) throw ckks::Error(CKKS_ESTATE, "key group not evaluated");
     std::vector<int> need;
-    for (const auto& tg : tags[kg])
+    for (const auto& tg : tags) {
+      if (!st_q[tg.qg]) throw ckks::Error(CKKS_ESTATE, "query group not evaluated");
       if (std::find(need.begin(), need.end(), tg.d) == need.end()) need.push_back(tg.d);
-    auto ks = lane_shifts(lower(K[kg], lks + 1), need, lks);
+    }
+    // scores are only decrypted: keys shifted from 4 limbs, products of
+    // 3-limb operands, head sums and decryption at 2
+    const int lks = std::min(st_q[tags[0].qg]->limbs() - 1, 3);
+    auto ks = lane_shifts(lower(st_k[kg], lks + 1), need, lks);
     count["cached_key_lane_shifts"] += (long)ks.size() - (ks.count(0) ? 1 : 0);
     std::vector<Ciphertext> qa, kb;
-    for (const auto& tg : tags[kg]) {
-      qa.push_back(Qr[tg.qg]);
+    for (const auto& tg : tags) {
+      qa.push_back(reduce_to(st_q[tg.qg], lks));
       kb.push_back(ks[tg.d]);
     }
     const auto sums = head_window_sums(mul_ct_rs_batch(qa, kb));
@@ -770,7 +818,7 @@ void ckks_block::forward(const double* x, int T, double* y) {
     double* dv = dbuf((size_t)M * SL);
     client_decrypt(sums, dv);
     blk::TileTag* dt = (blk::TileTag*)C.alloc(sizeof(blk::TileTag) * M);
-    CKKS_CUDA(cudaMemcpyAsync(dt, tags[kg].data(), sizeof(blk::TileTag) * M, cudaMemcpyHostToDevice, C.stream));
+    CKKS_CUDA(cudaMemcpyAsync(dt, tags.data(), sizeof(blk::TileTag) * M, cudaMemcpyHostToDevice, C.stream));
     blk::score_gather_kernel<<<dim3(M, H), 32 * ((B + 31) / 32), 0, C.stream>>>(dv, dt, T, H, HD, B, SL, inv_sqrt_hd,
                                                                               d_scores);
     CKKS_CUDA(cudaGetLastError());
@@ -779,34 +827,46 @@ void ckks_block::forward(const double* x, int T, double* y) {
     count["score_tile_decryptions"] += M;
     count["client_round_trips"] += M;
   }
-  stamp("scores", t);
-  // client: exact causal softmax in float64 (T123.cpp:629-665)
-  {
-    int* bad = (int*)C.alloc(sizeof(int));
-    CKKS_CUDA(cudaMemsetAsync(bad, 0, sizeof(int), C.stream));
-    blk::softmax_kernel<<<(T * H + blk::kThreads - 1) / blk::kThreads, blk::kThreads, 0, C.stream>>>(d_scores, d_prob,
-                                                                                                       T, H, bad);
-    int hbad = 0;
-    CKKS_CUDA(cudaMemcpyAsync(&hbad, bad, sizeof(int), cudaMemcpyDeviceToHost, C.stream));
-    CKKS_CUDA(cudaStreamSynchronize(C.stream));
-    C.release(bad);
-    if (hbad) throw ckks::Error(CKKS_ESTATE, "missing/non-finite causal attention score");
-    count["client_logical_instances"] += (long)H * T * (T + 1) / 2;
-  }
+  stamp("scores");
+}
 
-  // context: client weight tiles x shifted values (T123.cpp:838-860)
-  std::vector<Ciphertext> ctx(G);
-  for (int kg = 0; kg < G; ++kg) {
+// client: exact causal softmax in float64 (T123.cpp:629-665)
+void ckks_block::shard_softmax(const double* d_scores) {
+  const int T = s.T, H = s.H;
+  if (!st_prob) st_prob = (double*)C.alloc(sizeof(double) * (size_t)T * H * T);
+  int* bad = (int*)C.alloc(sizeof(int));
+  CKKS_CUDA(cudaMemsetAsync(bad, 0, sizeof(int), C.stream));
+  blk::softmax_kernel<<<(T * H + blk::kThreads - 1) / blk::kThreads, blk::kThreads, 0, C.stream>>>(d_scores, st_prob,
+                                                                                                     T, H, bad);
+  int hbad = 0;
+  CKKS_CUDA(cudaMemcpyAsync(&hbad, bad, sizeof(int), cudaMemcpyDeviceToHost, C.stream));
+  CKKS_CUDA(cudaStreamSynchronize(C.stream));
+  C.release(bad);
+  if (hbad) throw ckks::Error(CKKS_ESTATE, "missing/non-finite causal attention score");
+  count["client_logical_instances"] += (long)H * T * (T + 1) / 2;
+}
+
+// context of the given tiles: client weight tiles x shifted values, summed
+// into per-query-group partial contexts (T123.cpp:838-860)
+void ckks_block::shard_context(const std::vector<std::pair<int, int>>& pairs) {
+  const int T = s.T, H = s.H, HD = s.HD, D = s.D, B = s.B, SL = slots();
+  const int nb = (SL + blk::kThreads - 1) / blk::kThreads;
+  if (!st_prob) throw ckks::Error(CKKS_ESTATE, "softmax not evaluated");
+  for (int kg = 0; kg < s.groups; ++kg) {
+    const auto tags = tags_of(kg, pairs);
+    if (tags.empty()) continue;
+    if (!st_v[kg]) throw ckks::Error(CKKS_ESTATE, "value group not evaluated");
     std::vector<int> need;
-    for (const auto& tg : tags[kg])
+    for (const auto& tg : tags)
       if (std::find(need.begin(), need.end(), tg.d) == need.end()) need.push_back(tg.d);
-    auto vs = lane_shifts(V[kg], need, lk);
+    const int lk = st_v[kg]->limbs() - 1;
+    auto vs = lane_shifts(st_v[kg], need, lk);
     count["cached_value_lane_shifts"] += (long)vs.size() - (vs.count(0) ? 1 : 0);
-    const int M = (int)tags[kg].size();
+    const int M = (int)tags.size();
     double* dv = dbuf((size_t)M * SL);
     blk::TileTag* dt = (blk::TileTag*)C.alloc(sizeof(blk::TileTag) * M);
-    CKKS_CUDA(cudaMemcpyAsync(dt, tags[kg].data(), sizeof(blk::TileTag) * M, cudaMemcpyHostToDevice, C.stream));
-    blk::weight_tile_kernel<<<dim3(nb, M), blk::kThreads, 0, C.stream>>>(d_prob, dt, T, H, HD, D, B, SL, dv);
+    CKKS_CUDA(cudaMemcpyAsync(dt, tags.data(), sizeof(blk::TileTag) * M, cudaMemcpyHostToDevice, C.stream));
+    blk::weight_tile_kernel<<<dim3(nb, M), blk::kThreads, 0, C.stream>>>(st_prob, dt, T, H, HD, D, B, SL, dv);
     CKKS_CUDA(cudaGetLastError());
     const auto wa = client_encrypt(dv, M, lk);
     C.release(dt);
@@ -814,31 +874,39 @@ void ckks_block::forward(const double* x, int T, double* y) {
     count["weight_tile_encryptions"] += M;
     count["client_round_trips"] += M;
     std::vector<Ciphertext> vb;
-    for (const auto& tg : tags[kg]) vb.push_back(vs[tg.d]);
+    for (const auto& tg : tags) vb.push_back(vs[tg.d]);
     const auto prods = mul_ct_rs_batch(wa, vb);
-    for (int qg = kg; qg < G; ++qg) {
+    for (int qg = kg; qg < s.groups; ++qg) {
       std::vector<Ciphertext> terms;
-      if (ctx[qg]) terms.push_back(ctx[qg]);
+      if (st_ctx[qg]) terms.push_back(st_ctx[qg]);
       for (int i = 0; i < M; ++i)
-        if (tags[kg][i].qg == qg) terms.push_back(prods[i]);
-      if (!terms.empty()) ctx[qg] = terms.size() == 1 ? terms[0] : cc.EvalAddMany(terms);
+        if (tags[i].qg == qg) terms.push_back(prods[i]);
+      if (!terms.empty()) st_ctx[qg] = terms.size() == 1 ? terms[0] : cc.EvalAddMany(terms);
     }
   }
-  C.release(d_scores);
-  C.release(d_prob);
-  stamp("context", t);
+  stamp("context");
+}
 
-  // O projection, residual, LN2, MLP
-  std::vector<Ciphertext> r1(G);
-  for (int g = 0; g < G; ++g) {
-    const Ciphertext o = bsgs(babies_of(ctx[g]), 3);
-    r1[g] = add(reduce_to(xin[g], o->limbs()), o);
+// O projection, residual, LN2, MLP of the given groups, then the client
+// decrypts them into their rows of y ([T, D] host)
+void ckks_block::shard_output(const std::vector<int>& groups, double* y) {
+  if (groups.empty()) return;
+  const int T = s.T, D = s.D, B = s.B, PW = s.PW, SL = slots();
+  const int nb = (SL + blk::kThreads - 1) / blk::kThreads;
+  std::vector<Ciphertext> r1;
+  std::vector<int> act;
+  for (int g : groups) {
+    if (!st_ctx[g] || !st_x[g]) throw ckks::Error(CKKS_ESTATE, "context of the group not complete");
+    const Ciphertext o = bsgs(babies_of(st_ctx[g]), 3);
+    r1.push_back(add(reduce_to(st_x[g], o->limbs()), o));
+    act.push_back(s.count(g));
   }
-  const auto n2 = layernorm(r1, active);
-  std::vector<Ciphertext> out(G);
+  const auto n2 = layernorm(r1, act);
+  std::vector<Ciphertext> out(groups.size());
   const int gelu_limbs = 3;
-  for (int g = 0; g < G; ++g) {
-    const auto fb = babies_of(n2[g]);
+  for (size_t i = 0; i < groups.size(); ++i) {
+    const int g = groups[i];
+    const auto fb = babies_of(n2[i]);
     std::vector<Ciphertext> hc;
     for (int c = 0; c < nfc; ++c) hc.push_back(bsgs(fb, 4 + c));
     // client: exact tanh-GELU on the active lanes (T123.cpp:540-568)
@@ -858,37 +926,55 @@ void ckks_block::forward(const double* x, int T, double* y) {
       const Ciphertext pc = bsgs(babies_of(ge[c]), 4 + nfc + c);
       mlp = c ? add(mlp, pc) : pc;
     }
-    out[g] = add(reduce_to(r1[g], mlp->limbs()), mlp);
+    out[i] = add(reduce_to(r1[i], mlp->limbs()), mlp);
   }
-  CKKS_CUDA(cudaEventRecord(ev1, C.stream));
-  stamp("oproj_ln2_mlp", t);
-  {
-    float ms = 0.f;
-    CKKS_CUDA(cudaEventElapsedTime(&ms, ev0, ev1));
-    seconds["evaluate_events"] = ms / 1e3;
-    cudaEventDestroy(ev0);
-    cudaEventDestroy(ev1);
-  }
-
+  CKKS_CUDA(cudaEventRecord(ev_out, C.stream));
+  stamp("oproj_ln2_mlp");
   // client: decrypt and unpack (T123.cpp:1675-1694)
   {
-    double* dv = dbuf((size_t)G * SL);
+    const int M = (int)groups.size();
+    double* dv = dbuf((size_t)M * SL);
     client_decrypt(out, dv);
     double* dy = dbuf((size_t)T * D);
-    blk::unpack_kernel<<<dim3(nb, G), blk::kThreads, 0, C.stream>>>(dv, dy, T, D, B, SL);
-    CKKS_CUDA(cudaMemcpyAsync(y, dy, sizeof(double) * T * D, cudaMemcpyDeviceToHost, C.stream));
+    for (int i = 0; i < M; ++i) {
+      const int g = groups[i];
+      blk::unpack_kernel<<<dim3(nb, 1), blk::kThreads, 0, C.stream>>>(dv + (size_t)i * SL, dy, T, D, B, SL, g);
+      const int r0 = g * B, r1_ = std::min(T, (g + 1) * B);
+      CKKS_CUDA(cudaMemcpyAsync(y + (size_t)r0 * D, dy + (size_t)r0 * D, sizeof(double) * (size_t)(r1_ - r0) * D,
+                                cudaMemcpyDeviceToHost, C.stream));
+    }
+    CKKS_CUDA(cudaGetLastError());
     CKKS_CUDA(cudaStreamSynchronize(C.stream));
     C.release(dv);
     C.release(dy);
+    count["output_limbs"] = out[0]->limbs();
   }
-  stamp("decrypt_outputs", t);
+  stamp("decrypt_outputs");
   seconds["total"] = blk::now_s() - t_start;
   seconds["client"] = client_seconds;
   seconds["alloc_host"] = C.alloc_seconds - alloc_s0;
   count["alloc_calls"] = C.alloc_calls - alloc_n0;
-
-  count["output_limbs"] = out[0]->limbs();
   count["input_limbs"] = LX;
+  float ms = 0.f;
+  CKKS_CUDA(cudaEventElapsedTime(&ms, ev_in, ev_out));
+  seconds["evaluate_events"] = ms / 1e3;
+}
+
+void ckks_block::forward(const double* x, int T, double* y) {
+  shard_inputs(x, T);
+  std::vector<int> groups(s.groups);
+  for (int g = 0; g < s.groups; ++g) groups[g] = g;
+  std::vector<std::pair<int, int>> pairs;
+  for (int kg = 0; kg < s.groups; ++kg)
+    for (int qg = kg; qg < s.groups; ++qg) pairs.push_back({qg, kg});
+  shard_qkv(groups);
+  double* d_scores = dbuf((size_t)T * s.H * T);
+  CKKS_CUDA(cudaMemsetAsync(d_scores, 0xFF, sizeof(double) * T * s.H * T, C.stream));  // NaN = missing
+  shard_scores(pairs, d_scores);
+  shard_softmax(d_scores);
+  C.release(d_scores);
+  shard_context(pairs);
+  shard_output(groups, y);
 }
 
 // Classifier head on the last token's hidden state
@@ -1096,6 +1182,125 @@ int ckks_model_forward(ckks_block* const* blocks, int nblocks, ckks_block* head,
     std::memcpy(hidden, cur.data(), sizeof(double) * n);
     // last-token refresh into the head (:480-510)
     if (head) *margin = head->head_forward(cur.data() + (size_t)(tokens - 1) * blocks[0]->s.D);
+  });
+}
+
+// ---- sharded evaluation of one block (stages over unit subsets) ----------
+namespace {
+std::vector<int> group_list(const ckks_block* b, const int* groups, int n) {
+  if (n < 0 || (n && !groups)) throw ckks::Error(CKKS_EARG, "bad group list");
+  std::vector<int> v(groups, groups + n);
+  for (int g : v)
+    if (g < 0 || g >= b->s.groups) throw ckks::Error(CKKS_EARG, "group index out of range");
+  return v;
+}
+std::vector<std::pair<int, int>> pair_list(const ckks_block* b, const int* pairs, int n) {
+  if (n < 0 || (n && !pairs)) throw ckks::Error(CKKS_EARG, "bad tile list");
+  std::vector<std::pair<int, int>> v;
+  for (int i = 0; i < n; ++i) {
+    const int qg = pairs[2 * i], kg = pairs[2 * i + 1];
+    if (kg < 0 || qg < kg || qg >= b->s.groups) throw ckks::Error(CKKS_EARG, "tile (qg, kg) out of range");
+    v.push_back({qg, kg});
+  }
+  return v;
+}
+ckks_block* live(ckks_block* b) {
+  if (!b) throw ckks::Error(CKKS_EARG, "null block");
+  if (b->orphaned) throw ckks::Error(CKKS_ESTATE, "the block's context was destroyed");
+  if (b->d_head) throw ckks::Error(CKKS_EARG, "not a block object");
+  return b;
+}
+}  // namespace
+
+int ckks_block_shard_inputs(ckks_block* b, const double* x, int tokens) {
+  return bguard([&] {
+    if (!x) throw ckks::Error(CKKS_EARG, "null input");
+    live(b)->shard_inputs(x, tokens);
+  });
+}
+
+int ckks_block_shard_qkv(ckks_block* b, const int* groups, int n) {
+  return bguard([&] { live(b)->shard_qkv(group_list(b, groups, n)); });
+}
+
+int ckks_block_shard_scores(ckks_block* b, const int* pairs, int n, double* d_scores) {
+  return bguard([&] {
+    if (!d_scores) throw ckks::Error(CKKS_EARG, "null score buffer");
+    live(b)->shard_scores(pair_list(b, pairs, n), d_scores);
+  });
+}
+
+int ckks_block_shard_softmax(ckks_block* b, const double* d_scores) {
+  return bguard([&] {
+    if (!d_scores) throw ckks::Error(CKKS_EARG, "null score buffer");
+    live(b)->shard_softmax(d_scores);
+  });
+}
+
+int ckks_block_shard_context(ckks_block* b, const int* pairs, int n) {
+  return bguard([&] { live(b)->shard_context(pair_list(b, pairs, n)); });
+}
+
+int ckks_block_shard_output(ckks_block* b, const int* groups, int n, double* y) {
+  return bguard([&] {
+    if (!y) throw ckks::Error(CKKS_EARG, "null output");
+    live(b)->shard_output(group_list(b, groups, n), y);
+  });
+}
+
+// kind: 0 Q, 1 K, 2 V, 3 context (partial sum), 4 encrypted input
+int ckks_block_state_get(ckks_block* b, int kind, int group, ckks_ct* out) {
+  return bguard([&] {
+    live(b);
+    if (!out || out->owner != b->ctx) throw ckks::Error(CKKS_EARG, "bad ciphertext handle");
+    if (group < 0 || group >= b->s.groups) throw ckks::Error(CKKS_EARG, "group index out of range");
+    std::vector<Ciphertext>* v[] = {&b->st_q, &b->st_k, &b->st_v, &b->st_ctx, &b->st_x};
+    if (kind < 0 || kind > 4) throw ckks::Error(CKKS_EARG, "bad state kind");
+    if ((int)v[kind]->size() <= group || !(*v[kind])[group]) throw ckks::Error(CKKS_ESTATE, "state not present");
+    const ckks::DevPoly& p = (*v[kind])[group]->handle()->p;
+    ckks::Context& C = b->C;
+    ckks::DevPoly tmp;
+    tmp.ensure(&C, 2, p.limbs);
+    for (int k = 0; k < 2; ++k)
+      CKKS_CUDA(cudaMemcpyAsync(tmp.poly(k), p.poly(k), sizeof(uint64_t) * (size_t)p.limbs * C.N,
+                                cudaMemcpyDeviceToDevice, C.stream));
+    tmp.limbs = p.limbs;
+    tmp.scale = p.scale;
+    tmp.deg = p.deg;
+    std::swap(out->p.data, tmp.data);
+    std::swap(out->p.npolys, tmp.npolys);
+    std::swap(out->p.cap, tmp.cap);
+    std::swap(out->p.limbs, tmp.limbs);
+    std::swap(out->p.scale, tmp.scale);
+    std::swap(out->p.deg, tmp.deg);
+    out->p.ctx = &C;
+  });
+}
+
+// an empty ciphertext handle (no limbs) clears the entry
+int ckks_block_state_set(ckks_block* b, int kind, int group, const ckks_ct* in) {
+  return bguard([&] {
+    live(b);
+    if (!in || in->owner != b->ctx) throw ckks::Error(CKKS_EARG, "bad ciphertext handle");
+    if (group < 0 || group >= b->s.groups) throw ckks::Error(CKKS_EARG, "group index out of range");
+    std::vector<Ciphertext>* v[] = {&b->st_q, &b->st_k, &b->st_v, &b->st_ctx, &b->st_x};
+    if (kind < 0 || kind > 4) throw ckks::Error(CKKS_EARG, "bad state kind");
+    if ((int)v[kind]->size() != b->s.groups) throw ckks::Error(CKKS_ESTATE, "inputs not encrypted");
+    if (!in->p.data || in->p.limbs <= 0) {
+      (*v[kind])[group] = Ciphertext();
+      return;
+    }
+    Ciphertext c = b->cc.fresh();
+    ckks::DevPoly& p = c->handle()->p;
+    ckks::Context& C = b->C;
+    p.ensure(&C, 2, in->p.limbs);
+    for (int k = 0; k < 2; ++k)
+      CKKS_CUDA(cudaMemcpyAsync(p.poly(k), in->p.poly(k), sizeof(uint64_t) * (size_t)in->p.limbs * C.N,
+                                cudaMemcpyDeviceToDevice, C.stream));
+    p.limbs = in->p.limbs;
+    p.scale = in->p.scale;
+    p.deg = in->p.deg;
+    (*v[kind])[group] = c;
   });
 }
 

@@ -1070,4 +1070,154 @@ int ckks_ntt_inverse_polys(ckks_ctx* ctx, uint64_t* data, int npolys, int limbs)
   });
 }
 
+// ---- device-to-device limb transfer (NCCL exchanges between ranks) -------
+int ckks_ct_export_device(ckks_ctx* ctx, const ckks_ct* ct, uint64_t* dev, size_t words) {
+  return guard([&] {
+    Context& c = C(ctx);
+    same_ctx(ctx, ct);
+    const size_t per = (size_t)ct->p.limbs * c.N;
+    need(dev && words >= 2 * per, CKKS_EARG, "device buffer too small");
+    for (int p = 0; p < 2; ++p)
+      CKKS_CUDA(cudaMemcpyAsync(dev + p * per, ct->p.poly(p), sizeof(uint64_t) * per, cudaMemcpyDeviceToDevice,
+                                c.stream));
+  });
+}
+
+int ckks_ct_import_device(ckks_ctx* ctx, ckks_ct* ct, const uint64_t* dev, int limbs, double scale, int noise_deg) {
+  return guard([&] {
+    Context& c = C(ctx);
+    need(ct && ct->owner == ctx && dev, CKKS_EARG, "bad argument");
+    need(limbs >= 1 && limbs <= c.L, CKKS_EARG, "limb count outside 1..L");
+    need(noise_deg == 1 || noise_deg == 2, CKKS_EARG, "noise degree must be 1 or 2");
+    DevPoly tmp;
+    tmp.ensure(&c, 2, limbs);
+    const size_t per = (size_t)limbs * c.N;
+    for (int p = 0; p < 2; ++p)
+      CKKS_CUDA(cudaMemcpyAsync(tmp.poly(p), dev + p * per, sizeof(uint64_t) * per, cudaMemcpyDeviceToDevice,
+                                c.stream));
+    tmp.limbs = limbs;
+    tmp.scale = scale;
+    tmp.deg = noise_deg;
+    take(ct->p, tmp);
+  });
+}
+
+// ---- binary wire format ----------------------------------------------------
+// Little-endian; header then the moduli of every limb, then the residues:
+//   u32 magic 'CKB2', u32 version 1, u32 kind (1 ciphertext, 2 switching key),
+//   u32 log2 N, u32 Q limbs, u32 special limbs, u32 polynomials, u32 noise
+//   degree, f64 scale, i32 rotation index (keys; 0 = relinearisation key),
+//   u32 digits (keys), then (Q limbs + special limbs) u64 moduli, then
+//   polynomials x limbs x N u64 residues (a key: digits x 2 x (L + K) limbs).
+// Readers check the magic, version, ring degree and every modulus against
+// the context, so limbs never land under the wrong primes.
+namespace {
+constexpr uint32_t kWireMagic = 0x32424B43u;  // "CKB2"
+struct WireHeader {
+  uint32_t magic, version, kind, log_n, q_limbs, special, polys, deg;
+  double scale;
+  int32_t rot;
+  uint32_t digits;
+};
+static_assert(sizeof(WireHeader) == 48, "wire header layout");
+
+size_t wire_size(const WireHeader& h, int N) {
+  return sizeof(WireHeader) + 8ull * (h.q_limbs + h.special) +
+         8ull * (size_t)N * (h.kind == 1 ? (size_t)h.polys * h.q_limbs : (size_t)h.digits * 2 * (h.q_limbs + h.special));
+}
+
+void check_header(const Context& c, const WireHeader& h, const uint8_t* buf, size_t size) {
+  need(h.magic == kWireMagic && h.version == 1, CKKS_EARG, "not a ckks_b200 wire buffer");
+  need((int)h.log_n == c.logN, CKKS_EARG, "ring degree differs from the context's");
+  need(size >= wire_size(h, c.N), CKKS_EARG, "wire buffer truncated");
+  const uint64_t* mod = (const uint64_t*)(buf + sizeof(WireHeader));
+  for (uint32_t i = 0; i < h.q_limbs; ++i) need(mod[i] == c.moduli[i], CKKS_EARG, "Q modulus differs from the context's");
+  for (uint32_t i = 0; i < h.special; ++i)
+    need(mod[h.q_limbs + i] == c.moduli[c.L + i], CKKS_EARG, "special modulus differs from the context's");
+}
+}  // namespace
+
+long long ckks_ct_serialize(ckks_ctx* ctx, const ckks_ct* ct, uint8_t* buf, size_t cap) {
+  long long out = -1;
+  const int rc = guard([&] {
+    Context& c = C(ctx);
+    same_ctx(ctx, ct);
+    WireHeader h{kWireMagic, 1, 1, (uint32_t)c.logN, (uint32_t)ct->p.limbs, 0, 2, (uint32_t)ct->p.deg, ct->p.scale, 0, 0};
+    const size_t n = wire_size(h, c.N);
+    out = (long long)n;
+    if (!buf) return;
+    need(cap >= n, CKKS_EARG, "wire buffer too small");
+    std::memcpy(buf, &h, sizeof h);
+    std::memcpy(buf + sizeof h, c.moduli.data(), 8ull * h.q_limbs);
+    uint64_t* data = (uint64_t*)(buf + sizeof h + 8ull * h.q_limbs);
+    const size_t per = (size_t)ct->p.limbs * c.N;
+    for (int p = 0; p < 2; ++p)
+      CKKS_CUDA(cudaMemcpyAsync(data + p * per, ct->p.poly(p), 8 * per, cudaMemcpyDeviceToHost, c.stream));
+    CKKS_CUDA(cudaStreamSynchronize(c.stream));
+  });
+  return rc == CKKS_OK ? out : -1;
+}
+
+int ckks_ct_deserialize(ckks_ctx* ctx, ckks_ct* ct, const uint8_t* buf, size_t size) {
+  return guard([&] {
+    Context& c = C(ctx);
+    need(ct && ct->owner == ctx && buf && size >= sizeof(WireHeader), CKKS_EARG, "bad argument");
+    WireHeader h;
+    std::memcpy(&h, buf, sizeof h);
+    need(h.kind == 1 && h.polys == 2 && h.special == 0, CKKS_EARG, "not a ciphertext");
+    need(h.q_limbs >= 1 && (int)h.q_limbs <= c.L, CKKS_EARG, "limb count outside 1..L");
+    need(h.deg == 1 || h.deg == 2, CKKS_EARG, "bad noise degree");
+    check_header(c, h, buf, size);
+    DevPoly tmp;
+    tmp.ensure(&c, 2, (int)h.q_limbs);
+    const uint64_t* data = (const uint64_t*)(buf + sizeof h + 8ull * h.q_limbs);
+    const size_t per = (size_t)h.q_limbs * c.N;
+    for (int p = 0; p < 2; ++p)
+      CKKS_CUDA(cudaMemcpyAsync(tmp.poly(p), data + p * per, 8 * per, cudaMemcpyHostToDevice, c.stream));
+    CKKS_CUDA(cudaStreamSynchronize(c.stream));
+    tmp.limbs = (int)h.q_limbs;
+    tmp.scale = h.scale;
+    tmp.deg = (int)h.deg;
+    take(ct->p, tmp);
+  });
+}
+
+long long ckks_key_serialize(ckks_ctx* ctx, int k, uint8_t* buf, size_t cap) {
+  long long out = -1;
+  const int rc = guard([&] {
+    Context& c = C(ctx);
+    const uint64_t* src = k == 0 ? c.d_rlk : c.rot_key(c.galois(k));
+    need(src != nullptr, CKKS_EKEY, "key not generated");
+    WireHeader h{kWireMagic, 1, 2, (uint32_t)c.logN, (uint32_t)c.L, (uint32_t)c.K, 0, 1, 1.0, k,
+                 (uint32_t)(c.key_words() / (2 * (size_t)c.P * c.N))};
+    const size_t n = wire_size(h, c.N);
+    out = (long long)n;
+    if (!buf) return;
+    need(cap >= n, CKKS_EARG, "wire buffer too small");
+    std::memcpy(buf, &h, sizeof h);
+    std::memcpy(buf + sizeof h, c.moduli.data(), 8ull * c.P);
+    CKKS_CUDA(cudaMemcpyAsync(buf + sizeof h + 8ull * c.P, src, 8 * c.key_words(), cudaMemcpyDeviceToHost, c.stream));
+    CKKS_CUDA(cudaStreamSynchronize(c.stream));
+  });
+  return rc == CKKS_OK ? out : -1;
+}
+
+int ckks_key_deserialize(ckks_ctx* ctx, const uint8_t* buf, size_t size) {
+  return guard([&] {
+    Context& c = C(ctx);
+    need(buf && size >= sizeof(WireHeader), CKKS_EARG, "bad argument");
+    WireHeader h;
+    std::memcpy(&h, buf, sizeof h);
+    need(h.kind == 2, CKKS_EARG, "not a switching key");
+    need((int)h.q_limbs == c.L && (int)h.special == c.K && (size_t)h.digits * 2 * c.P * c.N == c.key_words(),
+         CKKS_EARG, "key shape differs from the context's");
+    check_header(c, h, buf, size);
+    uint64_t* key = nullptr;
+    CKKS_CUDA(cudaMalloc(&key, 8 * c.key_words()));
+    CKKS_CUDA(cudaMemcpyAsync(key, buf + sizeof h + 8ull * c.P, 8 * c.key_words(), cudaMemcpyHostToDevice, c.stream));
+    CKKS_CUDA(cudaStreamSynchronize(c.stream));
+    c.install_key(h.rot, key);
+  });
+}
+
 }  // extern "C"

@@ -176,6 +176,9 @@ class Context {
   size_t key_words() const { return (size_t)beta_top * 2 * P * N; }
   uint32_t galois(int k) const;
   const uint64_t* rot_key(uint32_t g) const;
+  // takes ownership of a cudaMalloc'd switching key: relinearisation for
+  // k == 0, else rotation by k (replaces a key already present)
+  void install_key(int k, uint64_t* key);
 
   void* alloc(size_t bytes) const;
   void release(void* p) const;

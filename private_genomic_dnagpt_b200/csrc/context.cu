@@ -442,6 +442,18 @@ const uint64_t* Context::rot_key(uint32_t g) const {
   return it == rot_keys.end() ? nullptr : it->second;
 }
 
+void Context::install_key(int k, uint64_t* key) {
+  if (k == 0) {
+    if (d_rlk) cudaFree(d_rlk);
+    d_rlk = key;
+    return;
+  }
+  const uint32_t g = galois(k);
+  auto it = rot_keys.find(g);
+  if (it != rot_keys.end()) cudaFree(it->second);
+  rot_keys[g] = key;
+}
+
 namespace {
 // bucket: powers of two up to 1 MiB, then multiples of 256 KiB
 size_t bucket(size_t bytes) {

@@ -1,0 +1,163 @@
+"""Sharding one block over ranks: the unit plan and the exchange protocol on
+CPU ranks (gloo, world size 2) over a float64 stand-in engine.
+
+The stand-in evaluates each stage of the plaintext block (oracle/plain_block)
+on exactly the units it is given, and keeps its per-group state (Q, K, V
+rows, partial contexts) as tensors that the orchestration exchanges; so the
+sharded output equals the unsharded block only if every unit is evaluated
+once and every exchange (state broadcast, score all-reduce, partial-context
+merge, output all-reduce) moves the right data.
+"""
+
+import contextlib
+import math
+import os
+import socket
+
+import numpy as np
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+from oracle import plain_block
+from private_genomic_dnagpt_b200 import shard
+
+B = 32
+
+
+def test_plan_covers_every_unit_once():
+    for tokens in (1, 31, 40, 103, 256):
+        groups = -(-tokens // B)
+        pairs = {(qg, kg) for kg in range(groups) for qg in range(kg, groups)}
+        for world in range(1, 9):
+            plan = shard.shard_plan(tokens, B, world)
+            assert len(plan) == world
+            gs = [g for rp in plan for g in rp.groups]
+            assert sorted(gs) == list(range(groups))
+            ps = [p for rp in plan for p in rp.pairs]
+            assert len(ps) == len(pairs) and set(ps) == pairs
+            w = {p: len(shard.active_shifts(tokens, B, *p)) for p in pairs}
+            loads = [sum(w[p] for p in rp.pairs) for rp in plan]
+            assert max(loads) - min(loads) <= max(w.values())
+            assert [rp.tiles for rp in plan] == loads
+
+
+def test_plan_for_the_benchmark_shape():
+    plan = shard.shard_plan(103, B, 4)
+    assert [rp.groups for rp in plan] == [[0], [1], [2], [3]]
+    total = sum(rp.tiles for rp in plan)
+    assert total == sum(len(shard.active_shifts(103, B, qg, kg)) for kg in range(4) for qg in range(kg, 4))
+
+
+class PlainIO:
+    """Float64 stand-in engine: the plaintext block, stage by stage."""
+
+    def __init__(self, w, tokens, heads=12):
+        self.w, self.T, self.H = w, tokens, heads
+        self.D = w["ln1"].shape[0]
+        self.hd = self.D // heads
+        self.state = {}
+
+    def stream(self):
+        return contextlib.nullcontext()
+
+    def rows(self, g):
+        return slice(g * B, min(self.T, (g + 1) * B))
+
+    def inputs(self, x):
+        self.x = np.asarray(x, np.float64)
+        self.state = {}
+
+    def qkv(self, groups):
+        D = self.D
+        for g in groups:
+            h1 = plain_block.layer_norm(self.x[self.rows(g)], self.w["ln1"])
+            qkv = h1 @ self.w["attn_qkv"].T
+            for kind in range(3):
+                self.state[(kind, g)] = qkv[:, kind * D:(kind + 1) * D].copy()
+
+    def scores(self, pairs, t):
+        s = t.view(self.T, self.H, self.T)
+        for qg, kg in pairs:
+            q = self.state[(0, qg)].reshape(-1, self.H, self.hd)
+            k = self.state[(1, kg)].reshape(-1, self.H, self.hd)
+            for i in range(q.shape[0]):
+                for j in range(k.shape[0]):
+                    tq, tk = qg * B + i, kg * B + j
+                    if tk <= tq:
+                        s[tq, :, tk] = torch.from_numpy((q[i] * k[j]).sum(-1) / math.sqrt(self.hd))
+
+    def softmax(self, t):
+        s = t.view(self.T, self.H, self.T).numpy().transpose(1, 0, 2)
+        mask = np.tril(np.ones((self.T, self.T), bool))
+        s = np.where(mask[None], s, -np.inf)
+        p = np.exp(s - s.max(-1, keepdims=True))
+        self.p = p / p.sum(-1, keepdims=True)  # [H, T, T]
+
+    def context(self, pairs):
+        for qg, kg in pairs:
+            v = self.state[(2, kg)].reshape(-1, self.H, self.hd)
+            rq = self.rows(qg)
+            part = np.zeros((rq.stop - rq.start, self.H, self.hd))
+            for i in range(part.shape[0]):
+                for j in range(v.shape[0]):
+                    tq, tk = qg * B + i, kg * B + j
+                    if tk <= tq:
+                        part[i] += self.p[:, tq, tk][:, None] * v[j]
+            key = (3, qg)
+            self.state[key] = self.state.get(key, 0) + part.reshape(-1, self.D)
+
+    def output(self, groups, y):
+        for g in groups:
+            r1 = self.x[self.rows(g)] + self.state[(3, g)] @ self.w["attn_proj"].T
+            h2 = plain_block.layer_norm(r1, self.w["ln2"])
+            y[self.rows(g)] = r1 + plain_block.gelu_tanh(h2 @ self.w["mlp_fc"].T) @ self.w["mlp_proj"].T
+
+    def state_meta(self, kind, g):
+        a = self.state.get((kind, g))
+        return None if a is None else (float(a.shape[0]), 1.0, 1.0)
+
+    def state_buffer(self, meta):
+        return torch.zeros(int(meta[0]) * self.D, dtype=torch.float64)
+
+    def state_export(self, kind, g):
+        a = self.state[(kind, g)]
+        return torch.from_numpy(a.reshape(-1).copy()), (float(a.shape[0]), 1.0, 1.0)
+
+    def state_import(self, kind, g, buf, meta):
+        self.state[(kind, g)] = buf.numpy().reshape(int(meta[0]), self.D).copy()
+
+    def state_sum(self, kind, g, bufs, meta):
+        self.state[(kind, g)] = sum(b.numpy().reshape(int(meta[0]), self.D) for b in bufs)
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _rank_main(rank, world, port, tokens, out_path):
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        w = plain_block.synthetic_weights(3)
+        x = plain_block.synthetic_input(4, tokens)
+        sb = shard.ShardedBlock(PlainIO(w, tokens), tokens, B, 12, plain_block.D, dist, "cpu")
+        y = sb.forward(x)
+        if rank == 0:
+            np.save(out_path, y)
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("world,tokens", [(2, 40), (2, 70), (3, 70)])
+def test_sharded_block_over_gloo_ranks_equals_the_block(tmp_path, world, tokens):
+    out = str(tmp_path / "y.npy")
+    mp.start_processes(_rank_main, args=(world, _free_port(), tokens, out), nprocs=world, join=True,
+                       start_method="spawn")
+    y = np.load(out)
+    ref = plain_block.block(plain_block.synthetic_input(4, tokens), plain_block.synthetic_weights(3))
+    assert np.abs(y - ref).max() <= 1e-12 * np.abs(ref).max()
