@@ -23,7 +23,12 @@ N(0, 0.02) in [out, in] layout, unit LN gains, embeddings N(0,1) clipped to
              by the block's operation counts.
 `--impl reference` reports that CPU figure alone (the reference's own CPU
 path, OpenFHE, is not available; the oracle port stands in).
-Under torchrun every rank evaluates its own replica block (weak scaling).
+Under torchrun the block is sharded over the ranks (token groups and
+attention tiles split, NCCL exchanges between the stages; strong scaling,
+`value` = latency of the one block); `--replicas` instead gives every rank
+its own block (weak scaling).  `--blocks N [--head]` times chained blocks
+(two-block and 12-block + head configurations), `--primitive` the primitive
+operations of one (N, L, dnum) configuration.
 """
 
 from __future__ import annotations
@@ -466,7 +471,9 @@ def run_model(args):
     x = plain_block.synthetic_input(6 + rank, args.tokens)
     # diagonal caches: about 26 GB per block; keep what fits beside the keys
     free, _ = torch.cuda.mem_get_info(local)
-    cached = args.cached_blocks if args.cached_blocks >= 0 else max(1, int((free / 2**30 - 40) // 27))
+    # headroom: one block re-encoding its diagonals (26 GB), keys (~8 GB) and
+    # the evaluation's working set
+    cached = args.cached_blocks if args.cached_blocks >= 0 else max(1, int((free / 2**30 - 70) // 27))
     model = eng.EncryptedModel(cc, ws, hw, args.tokens, cached_blocks=min(cached, args.blocks))
     cc.EvalRotateKeyGen(model.rotation_indices())
     stream = torch.cuda.ExternalStream(cc.stream_handle())
@@ -620,8 +627,10 @@ def main():
     ap.add_argument("--blocks", type=int, default=1)
     ap.add_argument("--head", action="store_true")
     ap.add_argument("--cached-blocks", type=int, default=-1)
-    # one block sharded over the torchrun ranks instead of one replica per rank
+    # under torchrun (WORLD_SIZE > 1) one block is sharded over the ranks
+    # (strong scaling); --replicas runs one independent block per rank instead
     ap.add_argument("--shard", action="store_true")
+    ap.add_argument("--replicas", action="store_true")
     args = ap.parse_args()
     if args.impl == "reference":
         run_reference(args)
@@ -629,7 +638,7 @@ def main():
         run_primitive(args)
     elif args.blocks > 1 or args.head:
         run_model(args)
-    elif args.shard:
+    elif args.shard or (int(os.environ.get("WORLD_SIZE", "1")) > 1 and not args.replicas):
         run_shard(args)
     else:
         run_engine(args)

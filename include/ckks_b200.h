@@ -82,8 +82,17 @@ int ckks_keygen(ckks_ctx* ctx);
 int ckks_relin_keygen(ckks_ctx* ctx);
 /* EvalRotateKeyGen(sk, indices) (T123.cpp:1624; index set :455-481) */
 int ckks_rotkey_gen(ckks_ctx* ctx, const int* indices, int count);
+/* Both generate, besides the key over all K special primes, a one-digit key
+ * over the first K_low special primes when the parameters allow it
+ * (log2(p_0 ... p_{K_low-1}) >= log2(q_0 ... q_3) + 20 with K_low < K and
+ * alpha >= 4): key switches at <= 4 limbs then use it (fewer limbs to
+ * extend, transform and divide).  ckks_ctx_low_set reports (4, K_low) or
+ * (0, 0). */
+int ckks_ctx_low_set(const ckks_ctx* ctx, int* low_limbs, int* low_special);
 /* key material to host: which = 0 secret (P*N), 1 public (2*L*N),
- * 2 relinearisation key, 3 rotation key for index k (dnum*2*(L+K)*N words) */
+ * 2 relinearisation key, 3 rotation key for index k (dnum*2*(L+K)*N words),
+ * 4 / 5 the relinearisation / rotation key over the reduced special-prime
+ * set (2*(L+K)*N words, rows of unused primes zero) */
 int ckks_key_export(ckks_ctx* ctx, int which, int k, uint64_t* host, size_t words);
 
 int ckks_ct_create(ckks_ctx* ctx, ckks_ct** out);
@@ -178,6 +187,12 @@ int ckks_rotate_hoisted(ckks_ctx* ctx, const ckks_ct* a, const int* k, int count
  * of EvalRotate / EvalMult / Rescale calls over independent ciphertexts
  * (the reference issues them one at a time, T123.cpp:795-860). */
 int ckks_rotate_batch(ckks_ctx* ctx, const ckks_ct* const* in, const int* k, int count, ckks_ct* const* outs);
+/* out = sum_i EvalRotate(in[i], k[i]) (all inputs at one level and scale):
+ * the giant-step sum of a BSGS product (T123.cpp:1283-1291).  The key
+ * switches of up to 32 non-identity rotations are added in the extended
+ * basis Q_l P and divided by P once (one ModDown per 32 rotations, in input
+ * order, instead of one per rotation); identity rotations are added as is. */
+int ckks_rotate_sum(ckks_ctx* ctx, const ckks_ct* const* in, const int* k, int count, ckks_ct* out);
 int ckks_mul_ct_batch(ckks_ctx* ctx, const ckks_ct* const* a, const ckks_ct* const* b, int count,
                       ckks_ct* const* outs);
 int ckks_rescale_batch(ckks_ctx* ctx, const ckks_ct* const* in, int count, ckks_ct* const* outs);

@@ -233,6 +233,14 @@ class CryptoContextImpl {
     check(ckks_rotate_batch(h_, in.data(), k.data(), (int)a.size(), hs.data()));
     return outs;
   }
+  // sum_i rot(a[i], k[i]) with one ModDown per 32 rotations
+  Ciphertext EvalRotateSum(const std::vector<Ciphertext>& a, const std::vector<int>& k) {
+    Ciphertext out = fresh();
+    std::vector<const ckks_ct*> in;
+    for (const auto& x : a) in.push_back(x->handle());
+    check(ckks_rotate_sum(h_, in.data(), k.data(), (int)a.size(), out->handle()));
+    return out;
+  }
   std::vector<Ciphertext> EvalMultBatch(const std::vector<Ciphertext>& a, const std::vector<Ciphertext>& b) {
     std::vector<Ciphertext> outs;
     std::vector<const ckks_ct*> x, y;

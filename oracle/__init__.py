@@ -42,7 +42,7 @@ def lib():
         L.oc_create.restype = ctypes.c_void_p
         L.oc_create.argtypes = [ctypes.c_int] * 6 + [ctypes.c_uint64]
         L.oc_destroy.argtypes = [ctypes.c_void_p]
-        for name in ("oc_N", "oc_L", "oc_K", "oc_alpha"):
+        for name in ("oc_N", "oc_L", "oc_K", "oc_alpha", "oc_low_limbs", "oc_K_low"):
             getattr(L, name).argtypes = [ctypes.c_void_p]
             getattr(L, name).restype = ctypes.c_int
         L.oc_scale.argtypes = [ctypes.c_void_p, ctypes.c_int]
@@ -90,6 +90,10 @@ class Oracle:
         self.dnum = dnum
         self.beta = -(-self.L // self.alpha)
         self.seed = seed
+        # one-digit key switches at <= low_limbs limbs use keys over the first
+        # K_low special primes (0: no such set)
+        self.low_limbs = self.L_.oc_low_limbs(self.h)
+        self.K_low = self.L_.oc_K_low(self.h)
         q = np.zeros(self.L + self.K, np.uint64)
         self.L_.oc_moduli(ctypes.c_void_p(self.h), _p(q))
         self.moduli = q
@@ -169,6 +173,11 @@ class Oracle:
     def switch_key(self, k: int) -> np.ndarray:
         out = np.zeros((self.beta, 2, self.L + self.K, self.N), np.uint64)
         self._check(self.L_.oc_switch_key(self._c(), int(k), _p(out)))
+        return out
+
+    def switch_key_low(self, k: int) -> np.ndarray:
+        out = np.zeros((2, self.L + self.K, self.N), np.uint64)
+        self._check(self.L_.oc_switch_key_low(self._c(), int(k), _p(out)))
         return out
 
     # -- client ------------------------------------------------------------
@@ -280,6 +289,13 @@ class Oracle:
         kk = np.ascontiguousarray(ks, np.int32)
         out = np.zeros((len(kk),) + ct.shape, np.uint64)
         self._check(self.L_.oc_rotate_hoisted(self._c(), _p(ct), ct.shape[1], _p(kk), len(kk), _p(out)))
+        return out
+
+    def rotate_sum(self, cts, ks):
+        cts = np.ascontiguousarray(cts, np.uint64)  # n x 2 x limbs x N
+        kk = np.ascontiguousarray(ks, np.int32)
+        out = np.zeros(cts.shape[1:], np.uint64)
+        self._check(self.L_.oc_rotate_sum(self._c(), _p(cts), cts.shape[2], _p(kk), len(kk), _p(out)))
         return out
 
     def accumulate_sum(self, ct, count: int, stride: int):

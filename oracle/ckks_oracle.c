@@ -151,7 +151,15 @@ struct oc_ctx {
     int nrot;
     uint32_t rot_g[OC_MAXROT];
     uint64_t* rot_key[OC_MAXROT];
+    /* one-digit key switches at <= low_limbs limbs use keys over the first
+     * K_low special primes (log2 P' >= log2 Q_low + 20); 0 = none */
+    int low_limbs, K_low;
+    uint64_t* rlk_low;                 /* 2*(L+K)*N, unused primes zero */
+    uint64_t* rot_key_low[OC_MAXROT];  /* parallel to rot_key */
 };
+
+static inline int is_low(const oc_ctx* c, int limbs) { return c->low_limbs > 0 && limbs <= c->low_limbs; }
+static inline int kx(const oc_ctx* c, int limbs) { return is_low(c, limbs) ? c->K_low : c->K; }
 
 int oc_N(const oc_ctx* c) { return c->N; }
 int oc_L(const oc_ctx* c) { return c->L; }
@@ -285,6 +293,18 @@ oc_ctx* oc_create(int logN, int L, int dnum, int first_bits, int scale_bits,
      * scaling prime; each rescale by q_{l-1} maps s -> s*s/q_{l-1}. */
     c->scales[L] = (L >= 2) ? (double)c->q[L - 1] : ldexp(1.0, scale_bits);
     for (int l = L; l >= 2; l--) c->scales[l - 1] = c->scales[l] * c->scales[l] / (double)c->q[l - 1];
+    /* reduced special-prime set for one-digit key switches at <= 4 limbs */
+    {
+        const int lo = c->alpha < 4 ? c->alpha : 4;
+        double qbits = 0.0, pbits = 0.0;
+        for (int i = 0; i < lo; i++) qbits += log2((double)c->q[i]);
+        int k = 0;
+        while (k < c->K && pbits < qbits + 20.0) pbits += log2((double)c->q[L + k++]);
+        if (L >= lo && lo >= 1 && pbits >= qbits + 20.0 && k < c->K) {
+            c->low_limbs = lo;
+            c->K_low = k;
+        }
+    }
     /* canonical-embedding tables (HEAAN special FFT) */
     const int M = 2 * N;
     c->ksi = (cplx*)malloc(sizeof(cplx) * (size_t)(M + 1));
@@ -306,8 +326,8 @@ void oc_destroy(oc_ctx* c) {
     if (!c) return;
     free(c->w); free(c->wp); free(c->wi); free(c->wip);
     free(c->ksi); free(c->rot_group);
-    free(c->sk); free(c->pk); free(c->rlk);
-    for (int i = 0; i < c->nrot; i++) free(c->rot_key[i]);
+    free(c->sk); free(c->pk); free(c->rlk); free(c->rlk_low);
+    for (int i = 0; i < c->nrot; i++) { free(c->rot_key[i]); free(c->rot_key_low[i]); }
     free(c);
 }
 
@@ -436,6 +456,7 @@ void oc_chacha_words(uint64_t seed, uint64_t nonce, uint64_t counter, uint64_t o
 #define NONCE_PK_A 0x02ull
 #define NONCE_PK_E 0x03ull
 #define NONCE_KSK(id, j, part) ((0x10ull << 36) | ((uint64_t)(id) << 8) | ((uint64_t)(j) << 1) | (uint64_t)(part))
+#define NONCE_KSK_LOW(id, part) ((0x11ull << 36) | ((uint64_t)(id) << 8) | (uint64_t)(part))
 #define NONCE_ENC(cnt, sub) ((0x20ull << 56) | ((uint64_t)(cnt) << 2) | (uint64_t)(sub))
 #define KEYID_RELIN 1u
 #define KEYID_ROT(g) (0x100u + (uint32_t)(g))
@@ -704,6 +725,42 @@ static uint64_t* make_switch_key(const oc_ctx* c, const uint64_t* s_from, uint32
     return key;
 }
 
+/* the same key over the reduced special-prime set: one digit covering Q
+ * primes 0..low_limbs-1 with P' = p_0 ... p_{K_low-1}; rows of the other
+ * primes stay zero */
+static uint64_t* make_switch_key_low(const oc_ctx* c, const uint64_t* s_from, uint32_t key_id) {
+    const int N = c->N, P = c->L + c->K, lq = c->low_limbs, kp = c->K_low;
+    uint64_t* key = (uint64_t*)calloc((size_t)2 * P * N, sizeof(uint64_t));
+    int* e = (int*)malloc(sizeof(int) * (size_t)N);
+    for (int n = 0; n < N; n++) e[n] = sample_cbd(c->seed, NONCE_KSK_LOW(key_id, 1), (uint64_t)n);
+    uint64_t* b = key;
+    uint64_t* a = key + (size_t)P * N;
+    int rows[OC_MAXP], nr = 0;
+    for (int t = 0; t < lq; t++) rows[nr++] = t;
+    for (int k = 0; k < kp; k++) rows[nr++] = c->L + k;
+#pragma omp parallel for schedule(static)
+    for (int r = 0; r < nr; r++) {
+        const int t = rows[r];
+        const modulus_t* m = &c->mod[t];
+        uint64_t pmod = 1;
+        for (int k = 0; k < kp; k++) pmod = mulm(pmod, c->q[c->L + k] % m->q, m);
+        uint64_t* en = (uint64_t*)malloc(sizeof(uint64_t) * (size_t)N);
+        for (int n = 0; n < N; n++) en[n] = small_to_res(e[n], m->q);
+        oc_ntt_fwd(c, t, en);
+        for (int n = 0; n < N; n++) {
+            size_t o = (size_t)t * N + n;
+            uint64_t av = sample_uniform(c->seed, NONCE_KSK_LOW(key_id, 0), o, m);
+            a[o] = av;
+            uint64_t bv = subm(en[n], mulm(av, c->sk[o], m), m->q);
+            if (t < lq) bv = addm(bv, mulm(pmod, s_from[o], m), m->q);
+            b[o] = bv;
+        }
+        free(en);
+    }
+    free(e);
+    return key;
+}
+
 void oc_relin_keygen(oc_ctx* c) {
     const int N = c->N, P = c->L + c->K;
     uint64_t* s2 = (uint64_t*)malloc(sizeof(uint64_t) * (size_t)P * N);
@@ -714,6 +771,10 @@ void oc_relin_keygen(oc_ctx* c) {
         }
     free(c->rlk);
     c->rlk = make_switch_key(c, s2, KEYID_RELIN);
+    if (c->low_limbs) {
+        free(c->rlk_low);
+        c->rlk_low = make_switch_key_low(c, s2, KEYID_RELIN);
+    }
     free(s2);
 }
 
@@ -748,6 +809,16 @@ static uint64_t* find_rot_key(const oc_ctx* c, uint32_t g) {
     return NULL;
 }
 
+/* the switching key of a key switch at `limbs` limbs: rotation g, or the
+ * relinearisation key for g == 1 */
+static const uint64_t* key_for(const oc_ctx* c, uint32_t g, int limbs) {
+    const int low = is_low(c, limbs);
+    if (g == 1) return low ? c->rlk_low : c->rlk;
+    for (int i = 0; i < c->nrot; i++)
+        if (c->rot_g[i] == g) return low ? c->rot_key_low[i] : c->rot_key[i];
+    return NULL;
+}
+
 int oc_rot_keygen(oc_ctx* c, int k) {
     uint32_t g = oc_galois_element(c, k);
     if (g == 1 || find_rot_key(c, g)) return 0;
@@ -757,10 +828,22 @@ int oc_rot_keygen(oc_ctx* c, int k) {
     oc_automorphism(c, c->sk, 1, P, g, sg);
     c->rot_g[c->nrot] = g;
     c->rot_key[c->nrot] = make_switch_key(c, sg, KEYID_ROT(g));
+    c->rot_key_low[c->nrot] = c->low_limbs ? make_switch_key_low(c, sg, KEYID_ROT(g)) : NULL;
     c->nrot++;
     free(sg);
     return 0;
 }
+
+int oc_switch_key_low(const oc_ctx* c, int k, uint64_t* out) {
+    if (!c->low_limbs) { set_err("no reduced special-prime set"); return -1; }
+    const uint32_t g = (k == 0) ? 1u : oc_galois_element(c, k);
+    const uint64_t* key = key_for(c, g, 1);
+    if (!key) { set_err("switch key not generated"); return -1; }
+    memcpy(out, key, sizeof(uint64_t) * (size_t)2 * (c->L + c->K) * c->N);
+    return 0;
+}
+int oc_low_limbs(const oc_ctx* c) { return c->low_limbs; }
+int oc_K_low(const oc_ctx* c) { return c->K_low; }
 
 int oc_switch_key(const oc_ctx* c, int k, uint64_t* out) {
     const size_t sz = sizeof(uint64_t) * (size_t)c->beta * 2 * (c->L + c->K) * c->N;
@@ -907,7 +990,7 @@ static inline int ext_prime(const oc_ctx* c, int limbs, int t) { return t < limb
 /* ModUp of NTT-form d over `limbs` Q limbs: digit j keeps its own limbs
  * and receives the others by approximate basis conversion. */
 void oc_modup(const oc_ctx* c, const uint64_t* d, int limbs, uint64_t* ext) {
-    const int N = c->N, K = c->K, E = limbs + K;
+    const int N = c->N, K = kx(c, limbs), E = limbs + K;
     const int beta = (limbs + c->alpha - 1) / c->alpha;
     uint64_t* dc = (uint64_t*)malloc(sizeof(uint64_t) * (size_t)limbs * N);
     memcpy(dc, d, sizeof(uint64_t) * (size_t)limbs * N);
@@ -960,7 +1043,7 @@ void oc_modup(const oc_ctx* c, const uint64_t* d, int limbs, uint64_t* ext) {
 /* ModDown: x over limbs+K extended limbs (NTT form) -> limbs Q limbs of
  * (x - conv_{P->Q}(x mod P)) * P^{-1}. */
 void oc_moddown(const oc_ctx* c, const uint64_t* x, int limbs, uint64_t* out) {
-    const int N = c->N, K = c->K, L = c->L;
+    const int N = c->N, K = kx(c, limbs), L = c->L;
     uint64_t* xp = (uint64_t*)malloc(sizeof(uint64_t) * (size_t)K * N);
     memcpy(xp, x + (size_t)limbs * N, sizeof(uint64_t) * (size_t)K * N);
 #pragma omp parallel for schedule(static)
@@ -1004,7 +1087,7 @@ void oc_moddown(const oc_ctx* c, const uint64_t* x, int limbs, uint64_t* out) {
  * automorphism g) with a switching key; acc: 2 x (limbs+K) limbs */
 static void ks_inner(const oc_ctx* c, const uint64_t* ext, int limbs, const uint64_t* key, uint32_t g,
                      uint64_t* acc) {
-    const int N = c->N, K = c->K, E = limbs + K, P = c->L + K;
+    const int N = c->N, E = limbs + kx(c, limbs), P = c->L + c->K;
     const int beta = (limbs + c->alpha - 1) / c->alpha;
     uint32_t* idx = (uint32_t*)malloc(sizeof(uint32_t) * (size_t)N);
     for (int k = 0; k < N; k++) idx[k] = (g == 1) ? (uint32_t)k : auto_index((uint32_t)k, g, c->logN);
@@ -1029,7 +1112,7 @@ static void ks_inner(const oc_ctx* c, const uint64_t* ext, int limbs, const uint
 }
 
 void oc_keyswitch(const oc_ctx* c, const uint64_t* d, int limbs, const uint64_t* ksk, uint64_t* out) {
-    const int N = c->N, E = limbs + c->K;
+    const int N = c->N, E = limbs + kx(c, limbs);
     const int beta = (limbs + c->alpha - 1) / c->alpha;
     uint64_t* ext = (uint64_t*)malloc(sizeof(uint64_t) * (size_t)beta * E * N);
     uint64_t* acc = (uint64_t*)malloc(sizeof(uint64_t) * 2 * (size_t)E * N);
@@ -1043,13 +1126,14 @@ void oc_keyswitch(const oc_ctx* c, const uint64_t* d, int limbs, const uint64_t*
 
 /* EvalMult(ct, ct) = tensor + relinearisation of d2 (T123.cpp:1144-1147) */
 int oc_mul_ct(const oc_ctx* c, const uint64_t* a, const uint64_t* b, int limbs, uint64_t* out) {
-    if (!c->rlk) { set_err("relinearisation key not generated"); return -1; }
+    const uint64_t* rlk = key_for(c, 1, limbs);
+    if (!rlk) { set_err("relinearisation key not generated"); return -1; }
     const int N = c->N;
     const size_t S = (size_t)limbs * N;
     uint64_t* d = (uint64_t*)malloc(sizeof(uint64_t) * 3 * S);
     uint64_t* ks = (uint64_t*)malloc(sizeof(uint64_t) * 2 * S);
     oc_tensor(c, a, b, limbs, d);
-    oc_keyswitch(c, d + 2 * S, limbs, c->rlk, ks);
+    oc_keyswitch(c, d + 2 * S, limbs, rlk, ks);
     oc_add(c, d, ks, 2, limbs, out);
     free(d);
     free(ks);
@@ -1085,12 +1169,12 @@ void oc_rescale(const oc_ctx* c, const uint64_t* ct, int limbs, uint64_t* out) {
  * with its key, runs ModDown and adds the permuted c0.  EvalRotate is the
  * single-index case. */
 int oc_rotate_hoisted(const oc_ctx* c, const uint64_t* ct, int limbs, const int* ks, int n, uint64_t* out) {
-    const int N = c->N, E = limbs + c->K;
+    const int N = c->N, E = limbs + kx(c, limbs);
     const int beta = (limbs + c->alpha - 1) / c->alpha;
     const size_t S = (size_t)limbs * N;
     for (int r = 0; r < n; r++) {
         uint32_t g = oc_galois_element(c, ks[r]);
-        if (g != 1 && !find_rot_key(c, g)) { set_err("rotation key not generated"); return -1; }
+        if (g != 1 && !key_for(c, g, limbs)) { set_err("rotation key not generated"); return -1; }
     }
     uint64_t* ext = (uint64_t*)malloc(sizeof(uint64_t) * (size_t)beta * E * N);
     uint64_t* acc = (uint64_t*)malloc(sizeof(uint64_t) * 2 * (size_t)E * N);
@@ -1100,7 +1184,7 @@ int oc_rotate_hoisted(const oc_ctx* c, const uint64_t* ct, int limbs, const int*
         uint64_t* o = out + (size_t)r * 2 * S;
         uint32_t g = oc_galois_element(c, ks[r]);
         if (g == 1) { memcpy(o, ct, sizeof(uint64_t) * 2 * S); continue; }
-        ks_inner(c, ext, limbs, find_rot_key(c, g), g, acc);
+        ks_inner(c, ext, limbs, key_for(c, g, limbs), g, acc);
         oc_moddown(c, acc, limbs, tmp);
         oc_moddown(c, acc + (size_t)E * N, limbs, tmp + S);
         oc_automorphism(c, ct, 1, limbs, g, o);
@@ -1113,6 +1197,59 @@ int oc_rotate_hoisted(const oc_ctx* c, const uint64_t* ct, int limbs, const int*
 
 int oc_rotate(const oc_ctx* c, const uint64_t* ct, int limbs, int k, uint64_t* out) {
     return oc_rotate_hoisted(c, ct, limbs, &k, 1, out);
+}
+
+/* sum_r rot(ct_r, k_r), the giant-step sum of a BSGS product (T123.cpp:
+ * 1283-1291), with the key switches of each group of up to 32 non-identity
+ * rotations (in input order) added in the extended basis and one ModDown per
+ * group; identity rotations are added as is.  cts: n x 2 x limbs x N. */
+int oc_rotate_sum(const oc_ctx* c, const uint64_t* cts, int limbs, const int* ks, int n, uint64_t* out) {
+    const int N = c->N, E = limbs + kx(c, limbs);
+    const int beta = (limbs + c->alpha - 1) / c->alpha;
+    const size_t S = (size_t)limbs * N;
+    for (int r = 0; r < n; r++) {
+        uint32_t g = oc_galois_element(c, ks[r]);
+        if (g != 1 && !key_for(c, g, limbs)) { set_err("rotation key not generated"); return -1; }
+    }
+    uint64_t* ext = (uint64_t*)malloc(sizeof(uint64_t) * (size_t)beta * E * N);
+    uint64_t* acc = (uint64_t*)malloc(sizeof(uint64_t) * 2 * (size_t)E * N);
+    uint64_t* accsum = (uint64_t*)malloc(sizeof(uint64_t) * 2 * (size_t)E * N);
+    uint64_t* tmp = (uint64_t*)malloc(sizeof(uint64_t) * 2 * S);
+    memset(out, 0, sizeof(uint64_t) * 2 * S);
+    int in_group = 0;
+    for (int r = 0; r <= n; r++) {
+        const int last = (r == n);
+        uint32_t g = last ? 0 : oc_galois_element(c, ks[r]);
+        if (last || in_group == 32) {
+            if (in_group) {  /* close the group: one ModDown of the summed products */
+                oc_moddown(c, accsum, limbs, tmp);
+                oc_moddown(c, accsum + (size_t)E * N, limbs, tmp + S);
+                oc_add(c, out, tmp, 2, limbs, out);
+            }
+            in_group = 0;
+            if (last) break;
+        }
+        const uint64_t* ct = cts + (size_t)r * 2 * S;
+        if (g == 1) {
+            oc_add(c, out, ct, 2, limbs, out);
+            continue;
+        }
+        if (in_group == 0) memset(accsum, 0, sizeof(uint64_t) * 2 * (size_t)E * N);
+        oc_modup(c, ct + S, limbs, ext);
+        ks_inner(c, ext, limbs, key_for(c, g, limbs), g, acc);
+        for (int p = 0; p < 2; p++)
+            for (int t = 0; t < E; t++) {
+                const uint64_t q = c->q[ext_prime(c, limbs, t)];
+                uint64_t* a = accsum + ((size_t)p * E + t) * N;
+                const uint64_t* b = acc + ((size_t)p * E + t) * N;
+                for (int k = 0; k < N; k++) a[k] = addm(a[k], b[k], q);
+            }
+        oc_automorphism(c, ct, 1, limbs, g, tmp);
+        oc_add(c, out, tmp, 1, limbs, out);
+        in_group++;
+    }
+    free(ext); free(acc); free(accsum); free(tmp);
+    return 0;
 }
 
 /* AccumulateSum(ct, count, stride) (T123.cpp:1154-1159, keys :444-453):

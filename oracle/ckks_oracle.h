@@ -81,6 +81,12 @@ void oc_public_key(const oc_ctx* c, uint64_t* out);   /* 2*L*N */
 /* key-switch key of a rotation (k) or relinearisation (k == 0):
  * dnum digits x 2 polys x (L+K) limbs x N */
 int oc_switch_key(const oc_ctx* c, int k, uint64_t* out);
+/* key switches at <= oc_low_limbs() limbs use keys over the first oc_K_low()
+ * special primes (0: no such set); the key of index k (0 = relinearisation),
+ * 2 x (L+K) x N words with the unused primes zero */
+int oc_switch_key_low(const oc_ctx* c, int k, uint64_t* out);
+int oc_low_limbs(const oc_ctx* c);
+int oc_K_low(const oc_ctx* c);
 
 void oc_encrypt(const oc_ctx* c, const uint64_t* pt, int limbs, uint64_t counter, uint64_t* ct);
 void oc_decrypt(const oc_ctx* c, const uint64_t* ct, int limbs, uint64_t* pt);
@@ -108,6 +114,8 @@ void oc_automorphism(const oc_ctx* c, const uint64_t* a, int npolys, int limbs, 
 uint32_t oc_galois_element(const oc_ctx* c, int k);
 int oc_rotate(const oc_ctx* c, const uint64_t* ct, int limbs, int k, uint64_t* out);
 int oc_rotate_hoisted(const oc_ctx* c, const uint64_t* ct, int limbs, const int* ks, int n, uint64_t* out);
+/* sum_r rot(cts[r], ks[r]) with one ModDown per group of 32 non-identity rotations */
+int oc_rotate_sum(const oc_ctx* c, const uint64_t* cts, int limbs, const int* ks, int n, uint64_t* out);
 int oc_accumulate_sum(const oc_ctx* c, const uint64_t* ct, int limbs, int count, int stride, uint64_t* out);
 
 /* ModUp / ModDown exposed for limb-level parity of the key-switch stages.

@@ -65,6 +65,7 @@ _SIGS = [
     ("ckks_ctx_create", ctypes.c_int, [ctypes.POINTER(ckks_params), ctypes.POINTER(_vp)]),
     ("ckks_ctx_destroy", ctypes.c_int, [_vp]),
     ("ckks_ctx_info", ctypes.c_int, [_vp] + [ctypes.POINTER(ctypes.c_int)] * 4),
+    ("ckks_ctx_low_set", ctypes.c_int, [_vp, ctypes.POINTER(ctypes.c_int), ctypes.POINTER(ctypes.c_int)]),
     ("ckks_ctx_moduli", ctypes.c_int, [_vp, _u64p, ctypes.c_int]),
     ("ckks_ctx_scale", ctypes.c_double, [_vp, ctypes.c_int]),
     ("ckks_sync", ctypes.c_int, [_vp]),
@@ -115,6 +116,7 @@ _SIGS = [
                                            ctypes.POINTER(_vp)]),
     ("ckks_rotate_batch", ctypes.c_int, [_vp, ctypes.POINTER(_vp), ctypes.POINTER(ctypes.c_int), ctypes.c_int,
                                          ctypes.POINTER(_vp)]),
+    ("ckks_rotate_sum", ctypes.c_int, [_vp, ctypes.POINTER(_vp), ctypes.POINTER(ctypes.c_int), ctypes.c_int, _vp]),
     ("ckks_mul_ct_batch", ctypes.c_int, [_vp, ctypes.POINTER(_vp), ctypes.POINTER(_vp), ctypes.c_int,
                                          ctypes.POINTER(_vp)]),
     ("ckks_rescale_batch", ctypes.c_int, [_vp, ctypes.POINTER(_vp), ctypes.c_int, ctypes.POINTER(_vp)]),
@@ -286,6 +288,9 @@ class CryptoContext:
         _check(lib().ckks_ctx_info(h, ctypes.byref(n), ctypes.byref(L), ctypes.byref(K), ctypes.byref(a)))
         self.N, self.L, self.K, self.alpha = n.value, L.value, K.value, a.value
         self.slots = self.N // 2
+        lo, kl = ctypes.c_int(0), ctypes.c_int(0)
+        _check(lib().ckks_ctx_low_set(self.h, ctypes.byref(lo), ctypes.byref(kl)))
+        self.low_limbs, self.K_low = lo.value, kl.value
         m = np.zeros(self.L + self.K, np.uint64)
         _check(lib().ckks_ctx_moduli(h, _u64(m), m.size))
         self.moduli = m
@@ -342,7 +347,9 @@ class CryptoContext:
     def key_array(self, which: int, k: int = 0) -> np.ndarray:
         P = self.L + self.K
         beta = -(-self.L // self.alpha)
-        shapes = {0: (P, self.N), 1: (2, self.L, self.N), 2: (beta, 2, P, self.N), 3: (beta, 2, P, self.N)}
+        # 4, 5: relinearisation / rotation key over the reduced special-prime set
+        shapes = {0: (P, self.N), 1: (2, self.L, self.N), 2: (beta, 2, P, self.N), 3: (beta, 2, P, self.N),
+                  4: (2, P, self.N), 5: (2, P, self.N)}
         out = np.zeros(shapes[which], np.uint64)
         _check(lib().ckks_key_export(self.h, which, k, _u64(out), out.size))
         return out
@@ -546,6 +553,13 @@ class CryptoContext:
         _check(lib().ckks_rotate_batch(self.h, (_vp * n)(*[c.h for c in cts]), (ctypes.c_int * n)(*ks), n,
                                        (_vp * n)(*[o.h for o in outs])))
         return outs
+
+    def EvalRotateSum(self, cts, ks) -> Ciphertext:
+        """sum_i EvalRotate(cts[i], ks[i]) with one ModDown per 32 rotations."""
+        out = self._new()
+        n = len(cts)
+        _check(lib().ckks_rotate_sum(self.h, (_vp * n)(*[c.h for c in cts]), (ctypes.c_int * n)(*ks), n, out.h))
+        return out
 
     def mul_ct_batch(self, a, b) -> list[Ciphertext]:
         outs = [self._new() for _ in a]

@@ -660,14 +660,12 @@ struct ckks_block {
                                                                        C.d_mods);
     }
     CKKS_CUDA(cudaGetLastError());
-    // giant-step rotations of the n2 - 1 inner sums, batched
-    std::vector<Ciphertext> gin(inner.begin() + 1, inner.end());
-    std::vector<int> gk;
-    for (int g = 1; g < s.n2; ++g) gk.push_back(s.B * s.n1 * g);
-    count["rotations"] += (long)gk.size();
-    auto terms = cc.EvalRotateBatch(gin, gk);
-    terms.insert(terms.begin(), inner[0]);
-    const Ciphertext acc = cc.EvalAddMany(terms);
+    // giant steps: sum_g rot(inner_g, B n1 g), the key switches summed in the
+    // extended basis with one ModDown (g = 0 is the identity)
+    std::vector<int> gk(s.n2);
+    for (int g = 0; g < s.n2; ++g) gk[g] = s.B * s.n1 * g;
+    count["rotations"] += s.n2 - 1;
+    const Ciphertext acc = cc.EvalRotateSum(inner, gk);
     return rs(acc);
   }
 
@@ -794,6 +792,9 @@ void ckks_block::shard_qkv(const std::vector<int>& groups) {
 void ckks_block::shard_scores(const std::vector<std::pair<int, int>>& pairs, double* d_scores) {
   const int T = s.T, H = s.H, HD = s.HD, B = s.B, SL = slots();
   const double inv_sqrt_hd = 1.0 / std::sqrt((double)HD);
+  // queries brought to the score level once per query group (a FLEXIBLEAUTO
+  // level reduction is a scaled multiply and a rescale)
+  std::map<int, Ciphertext> qr;
   for (int kg = 0; kg < s.groups; ++kg) {
     const auto tags = tags_of(kg, pairs);
     if (tags.empty()) continue;
@@ -810,7 +811,9 @@ void ckks_block::shard_scores(const std::vector<std::pair<int, int>>& pairs, dou
     count["cached_key_lane_shifts"] += (long)ks.size() - (ks.count(0) ? 1 : 0);
     std::vector<Ciphertext> qa, kb;
     for (const auto& tg : tags) {
-      qa.push_back(reduce_to(st_q[tg.qg], lks));
+      auto it = qr.find(tg.qg);
+      if (it == qr.end()) it = qr.emplace(tg.qg, reduce_to(st_q[tg.qg], lks)).first;
+      qa.push_back(it->second);
       kb.push_back(ks[tg.d]);
     }
     const auto sums = head_window_sums(mul_ct_rs_batch(qa, kb));

@@ -4,7 +4,10 @@
 #include <cmath>
 #include <cstdio>
 #include <cstring>
+#include <memory>
+#include <string>
 #include <utility>
+#include <vector>
 
 #include "../../include/ckks_b200.h"
 #include "capi_types.hpp"
@@ -102,7 +105,7 @@ void rotate_many(Context& c, const ckks_ct* a, const int* ks, int n, ckks_ct* co
   std::vector<uint32_t> gs(n);
   for (int r = 0; r < n; ++r) {
     gs[r] = c.galois(ks[r]);
-    if (gs[r] != 1u && !c.rot_key(gs[r]))
+    if (gs[r] != 1u && !c.switch_key(gs[r], limbs))
       throw Error(CKKS_EKEY, "rotation key not generated for index " + std::to_string(ks[r]));
   }
   std::vector<DevPoly> res(n);
@@ -123,7 +126,7 @@ void rotate_many(Context& c, const ckks_ct* a, const int* ks, int n, ckks_ct* co
     }
     const int m = b.M++;
     b.d[m] = a->p.poly(1);
-    b.key[m] = c.rot_key(gs[r]);
+    b.key[m] = c.switch_key(gs[r], limbs);
     b.g[m] = gs[r];
     b.add0[m] = a->p.poly(0);
     b.add1[m] = nullptr;
@@ -161,10 +164,11 @@ void rotate_batch(Context& c, const ckks_ct* const* in, const int* ks, int n, ck
                       limbs, c.stream);
       continue;
     }
-    if (!c.rot_key(g)) throw Error(CKKS_EKEY, "rotation key not generated for index " + std::to_string(ks[r]));
+    if (!c.switch_key(g, limbs))
+      throw Error(CKKS_EKEY, "rotation key not generated for index " + std::to_string(ks[r]));
     const int m = b.M++;
     b.d[m] = a->p.poly(1);
-    b.key[m] = c.rot_key(g);
+    b.key[m] = c.switch_key(g, limbs);
     b.g[m] = g;
     b.add0[m] = a->p.poly(0);
     b.add1[m] = nullptr;
@@ -179,11 +183,84 @@ void rotate_batch(Context& c, const ckks_ct* const* in, const int* ks, int n, ck
   }
 }
 
+// sum of polynomial pairs (c0, c1) at one limb count into `out` (up to 64
+// addends per launch; later launches add onto the running sum)
+void sum_pairs(Context& c, const std::vector<std::pair<const uint64_t*, const uint64_t*>>& terms, int limbs,
+               DevPoly& out) {
+  size_t i = 0;
+  bool first = true;
+  while (i < terms.size()) {
+    ckks::SumPtrs sp{};
+    int k = 0;
+    if (!first) {
+      sp.in0[k] = out.poly(0);
+      sp.in1[k] = out.poly(1);
+      ++k;
+    }
+    for (; i < terms.size() && k < ckks::kSumMax; ++i, ++k) {
+      sp.in0[k] = terms[i].first;
+      sp.in1[k] = terms[i].second;
+    }
+    sp.out0 = out.poly(0);
+    sp.out1 = out.poly(1);
+    ckks::add_many(c, sp, k, limbs, c.stream);
+    first = false;
+  }
+}
+
+// sum_r rot(in[r], ks[r]): the key switches of up to 32 non-identity
+// rotations are summed in the extended basis with one ModDown per group of
+// 32 (in input order); identity rotations and the groups' results are added
+void rotate_sum(Context& c, const ckks_ct* const* in, const int* ks, int n, DevPoly& res) {
+  const int limbs = in[0]->p.limbs;
+  std::vector<std::unique_ptr<DevPoly>> parts;
+  std::vector<std::pair<const uint64_t*, const uint64_t*>> terms;
+  ckks::KsBatch b{};
+  auto flush = [&] {
+    if (!b.M) return;
+    parts.emplace_back(new DevPoly);
+    DevPoly& p = *parts.back();
+    p.ensure(&c, 2, limbs);
+    ckks::keyswitch_sum(c, limbs, b, p.poly(0), p.poly(1), c.stream);
+    terms.push_back({p.poly(0), p.poly(1)});
+    b.M = 0;
+  };
+  for (int r = 0; r < n; ++r) {
+    const ckks_ct* a = in[r];
+    const uint32_t g = c.galois(ks[r]);
+    if (g == 1u) {
+      terms.push_back({a->p.poly(0), a->p.poly(1)});
+      continue;
+    }
+    if (!c.switch_key(g, limbs))
+      throw Error(CKKS_EKEY, "rotation key not generated for index " + std::to_string(ks[r]));
+    const int m = b.M++;
+    b.d[m] = a->p.poly(1);
+    b.key[m] = c.switch_key(g, limbs);
+    b.g[m] = g;
+    b.add0[m] = a->p.poly(0);
+    b.add1[m] = nullptr;
+    if (b.M == ckks::kKsBatch) flush();
+  }
+  flush();
+  res.ensure(&c, 2, limbs);
+  if (terms.size() == 1 && !parts.empty()) {
+    std::swap(res.data, parts[0]->data);
+    std::swap(res.cap, parts[0]->cap);
+    std::swap(res.npolys, parts[0]->npolys);
+  } else {
+    sum_pairs(c, terms, limbs, res);
+  }
+  res.limbs = limbs;
+  res.scale = in[0]->p.scale;
+  res.deg = in[0]->p.deg;
+}
+
 // tensor + relinearisation of (a[i], b[i]) pairs at one limb count
 void mul_ct_batch(Context& c, const ckks_ct* const* a, const ckks_ct* const* bb, int n, ckks_ct* const* outs) {
   if (n <= 0) return;
-  if (!c.d_rlk) throw Error(CKKS_EKEY, "relinearisation key not generated");
   const int limbs = a[0]->p.limbs, N = c.N;
+  if (!c.switch_key(1u, limbs)) throw Error(CKKS_EKEY, "relinearisation key not generated");
   const size_t S = (size_t)limbs * N;
   std::vector<DevPoly> res(n);
   std::vector<uint64_t*> dbuf;
@@ -207,7 +284,7 @@ void mul_ct_batch(Context& c, const ckks_ct* const* a, const ckks_ct* const* bb,
     res[r].deg = a[r]->p.deg + bb[r]->p.deg;
     const int m = b.M++;
     b.d[m] = d + 2 * S;
-    b.key[m] = c.d_rlk;
+    b.key[m] = c.switch_key(1u, limbs);
     b.g[m] = 1u;
     b.add0[m] = d;
     b.add1[m] = d + S;
@@ -322,6 +399,14 @@ int ckks_ctx_info(const ckks_ctx* ctx, int* ring_dim, int* limbs, int* special, 
   });
 }
 
+int ckks_ctx_low_set(const ckks_ctx* ctx, int* low_limbs, int* low_special) {
+  return guard([&] {
+    need(ctx && ctx->c, CKKS_EARG, "null context");
+    if (low_limbs) *low_limbs = ctx->c->low_limbs;
+    if (low_special) *low_special = ctx->c->K_low;
+  });
+}
+
 int ckks_ctx_moduli(const ckks_ctx* ctx, uint64_t* out, int count) {
   return guard([&] {
     need(ctx && ctx->c && out, CKKS_EARG, "null argument");
@@ -356,10 +441,9 @@ int ckks_relin_keygen(ckks_ctx* ctx) {
     uint64_t* s2 = (uint64_t*)c.alloc(sizeof(uint64_t) * (size_t)c.P * c.N);
     // s^2 over every prime (NTT form)
     ckks::ew_binary(c, ckks::EwOp::Mul, c.d_sk, 0, c.d_sk, 0, s2, 0, 1, c.P, c.stream);
-    uint64_t* key = ckks::make_switch_key(c, s2, 1u);
+    c.install_key(0, ckks::make_switch_key(c, s2, 1u));
+    if (c.low_limbs) c.install_key(0, ckks::make_switch_key_low(c, s2, 1u), true);
     c.release(s2);
-    if (c.d_rlk) cudaFree(c.d_rlk);
-    c.d_rlk = key;
   });
 }
 
@@ -374,6 +458,11 @@ int ckks_rotkey_gen(ckks_ctx* ctx, const int* indices, int count) {
       if (g == 1u || c.rot_key(g)) continue;
       ckks::automorphism(c, c.d_sk, sg, c.P, g, c.stream);
       c.rot_keys[g] = ckks::make_switch_key(c, sg, 0x100u + g);
+      if (c.low_limbs) {
+        auto it = c.rot_keys_low.find(g);
+        if (it != c.rot_keys_low.end()) cudaFree(it->second);
+        c.rot_keys_low[g] = ckks::make_switch_key_low(c, sg, 0x100u + g);
+      }
     }
     c.release(sg);
     CKKS_CUDA(cudaStreamSynchronize(c.stream));
@@ -391,6 +480,13 @@ int ckks_key_export(ckks_ctx* ctx, int which, int k, uint64_t* host, size_t word
       case 1: src = c.d_pk; n = 2 * (size_t)c.L * c.N; break;
       case 2: src = c.d_rlk; n = c.key_words(); break;
       case 3: src = c.rot_key(c.galois(k)); n = c.key_words(); break;
+      case 4: src = c.d_rlk_low; n = c.low_key_words(); break;
+      case 5: {
+        auto it = c.rot_keys_low.find(c.galois(k));
+        src = it == c.rot_keys_low.end() ? nullptr : it->second;
+        n = c.low_key_words();
+        break;
+      }
       default: throw Error(CKKS_EARG, "unknown key kind");
     }
     need(src != nullptr, CKKS_EKEY, "key not generated");
@@ -874,7 +970,7 @@ int ckks_mul_ct(ckks_ctx* ctx, const ckks_ct* a, const ckks_ct* b, ckks_ct* out)
     same_ctx(ctx, a);
     same_ctx(ctx, b);
     need(out && out->owner == ctx, CKKS_EARG, "bad output handle");
-    need(c.d_rlk != nullptr, CKKS_EKEY, "relinearisation key not generated");
+    need(c.switch_key(1u, a->p.limbs) != nullptr, CKKS_EKEY, "relinearisation key not generated");
     need(a->p.limbs == b->p.limbs, CKKS_ELEVEL, "operands at different levels");
     const ckks_ct* as[1] = {a};
     const ckks_ct* bs[1] = {b};
@@ -906,6 +1002,23 @@ int ckks_rotate_batch(ckks_ctx* ctx, const ckks_ct* const* in, const int* k, int
       need(outs[i] && outs[i]->owner == ctx, CKKS_EARG, "bad output handle");
     }
     rotate_batch(c, in, k, count, outs);
+  });
+}
+
+int ckks_rotate_sum(ckks_ctx* ctx, const ckks_ct* const* in, const int* k, int count, ckks_ct* out) {
+  return guard([&] {
+    Context& c = C(ctx);
+    need(count >= 1 && in && k, CKKS_EARG, "empty rotation sum");
+    need(out && out->owner == ctx, CKKS_EARG, "bad output handle");
+    for (int i = 0; i < count; ++i) {
+      same_ctx(ctx, in[i]);
+      need(in[i]->p.limbs == in[0]->p.limbs, CKKS_ELEVEL, "operands at different levels");
+      need(in[i]->p.deg == in[0]->p.deg, CKKS_ESCALE, "operands with different noise degree");
+      check_scales(in[0]->p.scale, in[i]->p.scale);
+    }
+    DevPoly tmp;
+    rotate_sum(c, in, k, count, tmp);
+    take(out->p, tmp);
   });
 }
 
@@ -1122,8 +1235,10 @@ struct WireHeader {
 static_assert(sizeof(WireHeader) == 48, "wire header layout");
 
 size_t wire_size(const WireHeader& h, int N) {
-  return sizeof(WireHeader) + 8ull * (h.q_limbs + h.special) +
-         8ull * (size_t)N * (h.kind == 1 ? (size_t)h.polys * h.q_limbs : (size_t)h.digits * 2 * (h.q_limbs + h.special));
+  const size_t P = h.q_limbs + h.special;
+  const size_t words = h.kind == 1 ? (size_t)h.polys * h.q_limbs
+                                   : (size_t)h.digits * 2 * P + (h.polys == 2 ? 2 * P : 0);
+  return sizeof(WireHeader) + 8ull * P + 8ull * (size_t)N * words;
 }
 
 void check_header(const Context& c, const WireHeader& h, const uint8_t* buf, size_t size) {
@@ -1188,15 +1303,26 @@ long long ckks_key_serialize(ckks_ctx* ctx, int k, uint8_t* buf, size_t cap) {
     Context& c = C(ctx);
     const uint64_t* src = k == 0 ? c.d_rlk : c.rot_key(c.galois(k));
     need(src != nullptr, CKKS_EKEY, "key not generated");
-    WireHeader h{kWireMagic, 1, 2, (uint32_t)c.logN, (uint32_t)c.L, (uint32_t)c.K, 0, 1, 1.0, k,
-                 (uint32_t)(c.key_words() / (2 * (size_t)c.P * c.N))};
+    // the key over the reduced special-prime set, when the context has one,
+    // follows the standard key (polys = 2, deg = its special-prime count)
+    const uint64_t* low = nullptr;
+    if (c.low_limbs) {
+      low = k == 0 ? c.d_rlk_low : c.switch_key(c.galois(k), 1);
+      need(low != nullptr, CKKS_EKEY, "reduced-set key not generated");
+    }
+    WireHeader h{kWireMagic, 1, 2, (uint32_t)c.logN, (uint32_t)c.L, (uint32_t)c.K, low ? 2u : 1u,
+                 (uint32_t)(low ? c.K_low : 0), 1.0, k, (uint32_t)(c.key_words() / (2 * (size_t)c.P * c.N))};
     const size_t n = wire_size(h, c.N);
     out = (long long)n;
     if (!buf) return;
     need(cap >= n, CKKS_EARG, "wire buffer too small");
     std::memcpy(buf, &h, sizeof h);
     std::memcpy(buf + sizeof h, c.moduli.data(), 8ull * c.P);
-    CKKS_CUDA(cudaMemcpyAsync(buf + sizeof h + 8ull * c.P, src, 8 * c.key_words(), cudaMemcpyDeviceToHost, c.stream));
+    uint8_t* data = buf + sizeof h + 8ull * c.P;
+    CKKS_CUDA(cudaMemcpyAsync(data, src, 8 * c.key_words(), cudaMemcpyDeviceToHost, c.stream));
+    if (low)
+      CKKS_CUDA(cudaMemcpyAsync(data + 8 * c.key_words(), low, 8 * c.low_key_words(), cudaMemcpyDeviceToHost,
+                                c.stream));
     CKKS_CUDA(cudaStreamSynchronize(c.stream));
   });
   return rc == CKKS_OK ? out : -1;
@@ -1212,11 +1338,21 @@ int ckks_key_deserialize(ckks_ctx* ctx, const uint8_t* buf, size_t size) {
     need((int)h.q_limbs == c.L && (int)h.special == c.K && (size_t)h.digits * 2 * c.P * c.N == c.key_words(),
          CKKS_EARG, "key shape differs from the context's");
     check_header(c, h, buf, size);
+    need(h.polys == (c.low_limbs ? 2u : 1u) && h.deg == (uint32_t)(c.low_limbs ? c.K_low : 0), CKKS_EARG,
+         "key's reduced special-prime set differs from the context's");
+    const uint8_t* data = buf + sizeof h + 8ull * c.P;
     uint64_t* key = nullptr;
     CKKS_CUDA(cudaMalloc(&key, 8 * c.key_words()));
-    CKKS_CUDA(cudaMemcpyAsync(key, buf + sizeof h + 8ull * c.P, 8 * c.key_words(), cudaMemcpyHostToDevice, c.stream));
+    CKKS_CUDA(cudaMemcpyAsync(key, data, 8 * c.key_words(), cudaMemcpyHostToDevice, c.stream));
+    uint64_t* low = nullptr;
+    if (h.polys == 2) {
+      CKKS_CUDA(cudaMalloc(&low, 8 * c.low_key_words()));
+      CKKS_CUDA(cudaMemcpyAsync(low, data + 8 * c.key_words(), 8 * c.low_key_words(), cudaMemcpyHostToDevice,
+                                c.stream));
+    }
     CKKS_CUDA(cudaStreamSynchronize(c.stream));
     c.install_key(h.rot, key);
+    if (low) c.install_key(h.rot, low, true);
   });
 }
 

@@ -173,12 +173,37 @@ class Context {
   std::map<uint32_t, uint64_t*> rot_keys;  // galois element -> key
   uint64_t enc_counter = 0;
 
+  // Key switches at <= low_limbs limbs (one digit) use switching keys over
+  // the first K_low special primes only, P' = p_0 ... p_{K_low-1}, with
+  // log2 P' >= log2 Q_{low_limbs} + 20 so that the ModDown error stays below
+  // 2^-20 of the digit bound.  Disabled (0) when that needs all K primes or
+  // the digit is shorter than low_limbs.
+  int low_limbs = 0, K_low = 0;
+  ulonglong2* d_pmod_low = nullptr;          // [P] P' mod q_t, 0 for special primes
+  ulonglong2* d_down_scale_low_a = nullptr;  // [K] (first K_low) P'hat_k^-1 * n^-1
+  ulonglong2* d_down_scale_low_b = nullptr;  // [K] P'hat_k^-1 * Winv[1] * n^-1
+  std::vector<LevelTables> levels_low;       // index = limbs (1..low_limbs)
+  uint64_t* d_rlk_low = nullptr;             // [1][2][P][N], primes < low_limbs and the first K_low special
+  std::map<uint32_t, uint64_t*> rot_keys_low;
+
+  // the special-prime set of a key switch at `limbs` limbs
+  bool low(int limbs) const { return low_limbs > 0 && limbs <= low_limbs; }
+  int Kx(int limbs) const { return low(limbs) ? K_low : K; }
+  const LevelTables& lt(int limbs) const { return low(limbs) ? levels_low[limbs] : levels[limbs]; }
+  const ulonglong2* down_scale_a(int limbs) const { return low(limbs) ? d_down_scale_low_a : d_down_scale_a; }
+  const ulonglong2* down_scale_b(int limbs) const { return low(limbs) ? d_down_scale_low_b : d_down_scale_b; }
+  // switching key for a key switch at `limbs` limbs: rotation (g != 1) or,
+  // with g == 1, relinearisation; null when not generated
+  const uint64_t* switch_key(uint32_t g, int limbs) const;
+
   size_t key_words() const { return (size_t)beta_top * 2 * P * N; }
+  size_t low_key_words() const { return (size_t)2 * P * N; }
   uint32_t galois(int k) const;
   const uint64_t* rot_key(uint32_t g) const;
   // takes ownership of a cudaMalloc'd switching key: relinearisation for
-  // k == 0, else rotation by k (replaces a key already present)
-  void install_key(int k, uint64_t* key);
+  // k == 0, else rotation by k (replaces a key already present); `low`
+  // selects the reduced special-prime set
+  void install_key(int k, uint64_t* key, bool low = false);
 
   void* alloc(size_t bytes) const;
   void release(void* p) const;
@@ -290,6 +315,12 @@ struct KsBatch {
   int M;
 };
 void keyswitch_batch(const Context& c, int limbs, const KsBatch& b, bool shared_input, cudaStream_t st);
+// Sum of the M key switches of a batch with one ModDown: the key inner
+// products are added in the extended basis Q_l P and divided by P once;
+// out0 = ModDown(sum acc0) + sum_m auto_{g_m}(add0[m]), out1 = ModDown(sum
+// acc1) + sum_m add1[m] (null addends skipped).  The giant steps of a BSGS
+// product: sum_g rot(inner_g, k_g).
+void keyswitch_sum(const Context& c, int limbs, const KsBatch& b, uint64_t* out0, uint64_t* out1, cudaStream_t st);
 
 // Batched rescale of M ciphertexts (c0, c1 pointers per item, `limbs` limbs
 // each) into outputs of limbs-1 limbs.
@@ -314,6 +345,9 @@ void rescale(const Context& c, const uint64_t* x, size_t sx, int npolys, int lim
 // keys / sampling / client
 void keygen_secret_public(Context& c);
 uint64_t* make_switch_key(Context& c, const uint64_t* s_from, uint32_t key_id);
+// the same key over the reduced special-prime set (one digit covering the
+// first low_limbs Q primes)
+uint64_t* make_switch_key_low(Context& c, const uint64_t* s_from, uint32_t key_id);
 void encrypt(Context& c, const uint64_t* pt, int limbs, uint64_t counter, uint64_t* c0, uint64_t* c1);
 void decrypt(const Context& c, const uint64_t* c0, const uint64_t* c1, int limbs, uint64_t* pt);
 

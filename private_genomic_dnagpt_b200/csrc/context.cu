@@ -236,27 +236,55 @@ Context::Context(const Params& p) : params(p) {
   d_w1ninv = upload(w1ninv);
   d_pmod = upload(pmod);
 
-  // (P/p_k)^-1 mod p_k
+  // reduced special-prime set for one-digit key switches at <= 4 limbs: the
+  // fewest leading special primes whose product exceeds Q_{low} by 2^20
   {
-    std::vector<ulonglong2> phatinv(K);
-    for (int k = 0; k < K; ++k) {
+    const int lo = std::min(4, alpha);
+    double qbits = 0.0, pbits = 0.0;
+    for (int i = 0; i < lo; ++i) qbits += std::log2((double)moduli[i]);
+    int k = 0;
+    while (k < K && pbits < qbits + 20.0) pbits += std::log2((double)moduli[L + k++]);
+    if (L >= lo && lo >= 1 && pbits >= qbits + 20.0 && k < K) {
+      low_limbs = lo;
+      K_low = k;
+    }
+  }
+
+  // (P/p_k)^-1 mod p_k over the first Kx special primes, with the ModDown
+  // pre-scaling folded into the inverse NTT
+  auto down_scales = [&](int Kx, ulonglong2*& da, ulonglong2*& db, std::vector<ulonglong2>* phat_out) {
+    std::vector<ulonglong2> phatinv(K, make_ulonglong2(0, 0)), sa(K, make_ulonglong2(0, 0)),
+        sb(K, make_ulonglong2(0, 0));
+    for (int k = 0; k < Kx; ++k) {
       const uint64_t pk = moduli[L + k];
       uint64_t prod = 1;
-      for (int k2 = 0; k2 < K; ++k2)
+      for (int k2 = 0; k2 < Kx; ++k2)
         if (k2 != k) prod = mulm(prod, moduli[L + k2] % pk, pk);
       phatinv[k] = shoup_pair(invm(prod, pk), pk);
-    }
-    d_phatinv = upload(phatinv);
-    std::vector<ulonglong2> sa(K), sb(K);
-    for (int k = 0; k < K; ++k) {
-      const uint64_t pk = moduli[L + k];
       const uint64_t ni = invm((uint64_t)N, pk);
       const uint64_t w1 = mulm(ni, itw[(size_t)(L + k) * N + 1].x, pk);
       sa[k] = shoup_pair(mulm(phatinv[k].x, ni, pk), pk);
       sb[k] = shoup_pair(mulm(phatinv[k].x, w1, pk), pk);
     }
-    d_down_scale_a = upload(sa);
-    d_down_scale_b = upload(sb);
+    if (phat_out) *phat_out = phatinv;
+    da = upload(sa);
+    db = upload(sb);
+  };
+  {
+    std::vector<ulonglong2> phatinv;
+    down_scales(K, d_down_scale_a, d_down_scale_b, &phatinv);
+    d_phatinv = upload(phatinv);
+    if (low_limbs) {
+      down_scales(K_low, d_down_scale_low_a, d_down_scale_low_b, nullptr);
+      std::vector<ulonglong2> pl(P);
+      for (int i = 0; i < P; ++i) {
+        const uint64_t q = moduli[i];
+        uint64_t pm = 1;
+        for (int k = 0; k < K_low; ++k) pm = mulm(pm, moduli[L + k] % q, q);
+        pl[i] = shoup_pair(i < L ? pm : 0, q);
+      }
+      d_pmod_low = upload(pl);
+    }
   }
 
   // canonical embedding tables
@@ -277,13 +305,12 @@ Context::Context(const Params& p) : params(p) {
     d_rot_group = upload(rg);
   }
 
-  // per-level ModUp / ModDown / Rescale constants
-  levels.resize(L + 1);
-  for (int l = 1; l <= L; ++l) {
-    LevelTables& t = levels[l];
+  // per-level ModUp / ModDown / Rescale constants over the first Kx special primes
+  auto level_tables = [&](int l, int Kx) {
+    LevelTables t;
     t.limbs = l;
     t.beta = (l + alpha - 1) / alpha;
-    const int E = l + K;
+    const int E = l + Kx;
     std::vector<ulonglong2> hatinv((size_t)t.beta * alpha, make_ulonglong2(0, 0));
     std::vector<uint64_t> hat((size_t)t.beta * alpha * E, 0);
     for (int j = 0; j < t.beta; ++j) {
@@ -318,14 +345,14 @@ Context::Context(const Params& p) : params(p) {
       t.d_up_scale_b = upload(sb);
     }
     t.d_up_hat = upload(hat);
-    std::vector<uint64_t> phat((size_t)K * l);
+    std::vector<uint64_t> phat((size_t)Kx * l);
     std::vector<ulonglong2> pinv(l);
     for (int tt = 0; tt < l; ++tt) {
       const uint64_t qt = moduli[tt];
       uint64_t pp = 1;
-      for (int k = 0; k < K; ++k) {
+      for (int k = 0; k < Kx; ++k) {
         uint64_t h = 1;
-        for (int k2 = 0; k2 < K; ++k2)
+        for (int k2 = 0; k2 < Kx; ++k2)
           if (k2 != k) h = mulm(h, moduli[L + k2] % qt, qt);
         phat[(size_t)k * l + tt] = h;
         pp = mulm(pp, moduli[L + k] % qt, qt);
@@ -337,7 +364,12 @@ Context::Context(const Params& p) : params(p) {
     std::vector<ulonglong2> rinv(l > 1 ? l - 1 : 1, make_ulonglong2(0, 0));
     for (int i = 0; i + 1 < l; ++i) rinv[i] = shoup_pair(invm(moduli[l - 1] % moduli[i], moduli[i]), moduli[i]);
     t.d_rescale_inv = upload(rinv);
-  }
+    return t;
+  };
+  levels.resize(L + 1);
+  for (int l = 1; l <= L; ++l) levels[l] = level_tables(l, K);
+  levels_low.resize(low_limbs + 1);
+  for (int l = 1; l <= low_limbs; ++l) levels_low[l] = level_tables(l, K_low);
 
   CKKS_CUDA(cudaDeviceSynchronize());
 }
@@ -363,6 +395,20 @@ Context::~Context() {
   }
   cudaFree(d_down_scale_a);
   cudaFree(d_down_scale_b);
+  for (auto& t : levels_low) {
+    cudaFree(t.d_up_hatinv);
+    cudaFree(t.d_up_hat);
+    cudaFree(t.d_down_phat);
+    cudaFree(t.d_down_pinv);
+    cudaFree(t.d_rescale_inv);
+    cudaFree(t.d_up_scale_a);
+    cudaFree(t.d_up_scale_b);
+  }
+  cudaFree(d_down_scale_low_a);
+  cudaFree(d_down_scale_low_b);
+  cudaFree(d_pmod_low);
+  for (auto& kv : rot_keys_low) cudaFree(kv.second);
+  cudaFree(d_rlk_low);
   cudaFree(d_mods);
   cudaFree(d_tw);
   cudaFree(d_itw);
@@ -442,16 +488,28 @@ const uint64_t* Context::rot_key(uint32_t g) const {
   return it == rot_keys.end() ? nullptr : it->second;
 }
 
-void Context::install_key(int k, uint64_t* key) {
+void Context::install_key(int k, uint64_t* key, bool lowset) {
+  uint64_t*& rlk = lowset ? d_rlk_low : d_rlk;
+  auto& rot = lowset ? rot_keys_low : rot_keys;
   if (k == 0) {
-    if (d_rlk) cudaFree(d_rlk);
-    d_rlk = key;
+    if (rlk) cudaFree(rlk);
+    rlk = key;
     return;
   }
   const uint32_t g = galois(k);
-  auto it = rot_keys.find(g);
-  if (it != rot_keys.end()) cudaFree(it->second);
-  rot_keys[g] = key;
+  auto it = rot.find(g);
+  if (it != rot.end()) cudaFree(it->second);
+  rot[g] = key;
+}
+
+const uint64_t* Context::switch_key(uint32_t g, int limbs) const {
+  if (low(limbs)) {
+    if (g == 1u) return d_rlk_low;
+    auto it = rot_keys_low.find(g);
+    return it == rot_keys_low.end() ? nullptr : it->second;
+  }
+  if (g == 1u) return d_rlk;
+  return rot_key(g);
 }
 
 namespace {

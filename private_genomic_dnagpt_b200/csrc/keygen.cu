@@ -87,6 +87,10 @@ constexpr uint64_t kNoncePkE = 0x03ull;
 inline uint64_t nonce_ksk(uint32_t id, int j, int part) {
   return (0x10ull << 36) | ((uint64_t)id << 8) | ((uint64_t)j << 1) | (uint64_t)part;
 }
+// switching keys over the reduced special-prime set
+inline uint64_t nonce_ksk_low(uint32_t id, int part) {
+  return (0x11ull << 36) | ((uint64_t)id << 8) | (uint64_t)part;
+}
 inline uint64_t nonce_enc(uint64_t cnt, int sub) { return (0x20ull << 56) | (cnt << 2) | (uint64_t)sub; }
 
 // kind 0: uniform ternary from w0 mod 3; kind 1: centered binomial 21+21
@@ -136,11 +140,11 @@ __global__ void __launch_bounds__(kThreads) rlwe_combine_kernel(const uint64_t* 
                                                                 const uint64_t* __restrict__ s_from,
                                                                 const ulonglong2* __restrict__ pmod, int lo, int hi,
                                                                 uint64_t* __restrict__ b, int logN,
-                                                                const Mod* __restrict__ mods) {
+                                                                const Mod* __restrict__ mods, int first) {
   const int N = 1 << logN;
   const int n = blockIdx.x * kThreads + threadIdx.x;
   if (n >= N) return;
-  const int t = blockIdx.y;
+  const int t = first + blockIdx.y;
   const Mod m = mods[t];
   const size_t o = (size_t)t * N + n;
   uint64_t bv = sub_mod(e[o], mul_mod(a[o], s[o], m), m.q);
@@ -210,7 +214,7 @@ void keygen_secret_public(Context& c) {
   const ChachaKey key = key_from_seed(c.params.seed);
   uniform_kernel<<<grid_for(c, L), kThreads, 0, c.stream>>>(a, key, kNoncePkA, LimbMap::q(L, L), c.logN, c.d_mods);
   rlwe_combine_kernel<<<grid_for(c, L), kThreads, 0, c.stream>>>(e, a, c.d_sk, nullptr, nullptr, 0, 0, c.d_pk,
-                                                                 c.logN, c.d_mods);
+                                                                 c.logN, c.d_mods, 0);
   CKKS_CUDA(cudaGetLastError());
   c.release(e);
   c.release(scratch);
@@ -233,7 +237,39 @@ uint64_t* make_switch_key(Context& c, const uint64_t* s_from, uint32_t key_id) {
     uniform_kernel<<<grid_for(c, P), kThreads, 0, c.stream>>>(a, ck, nonce_ksk(key_id, j, 0), all, c.logN, c.d_mods);
     const int lo = j * c.alpha, hi = std::min(lo + c.alpha, L);
     rlwe_combine_kernel<<<grid_for(c, P), kThreads, 0, c.stream>>>(e, a, c.d_sk, s_from, c.d_pmod, lo, hi, b, c.logN,
-                                                                   c.d_mods);
+                                                                   c.d_mods, 0);
+    CKKS_CUDA(cudaGetLastError());
+  }
+  c.release(e);
+  c.release(scratch);
+  CKKS_CUDA(cudaStreamSynchronize(c.stream));
+  return key;
+}
+
+// One digit over Q primes 0..low_limbs-1 with P' = p_0 ... p_{K_low-1}:
+// b = e - a s + P' s_from on those Q primes, e - a s on the K_low special
+// primes; the other rows of the [2][P][N] layout stay zero.
+uint64_t* make_switch_key_low(Context& c, const uint64_t* s_from, uint32_t key_id) {
+  if (!c.d_sk) throw Error(kErrState, "secret key not generated");
+  if (!c.low_limbs) throw Error(kErrState, "no reduced special-prime set for these parameters");
+  const int N = c.N, P = c.P, L = c.L, lq = c.low_limbs, kp = c.K_low;
+  uint64_t* key = nullptr;
+  CKKS_CUDA(cudaMalloc(&key, sizeof(uint64_t) * c.low_key_words()));
+  CKKS_CUDA(cudaMemsetAsync(key, 0, sizeof(uint64_t) * c.low_key_words(), c.stream));
+  int* scratch = (int*)c.alloc(sizeof(int) * N);
+  uint64_t* e = (uint64_t*)c.alloc(sizeof(uint64_t) * (size_t)P * N);
+  const ChachaKey ck = key_from_seed(c.params.seed);
+  uint64_t* b = key;
+  uint64_t* a = key + (size_t)P * N;
+  for (int part = 0; part < 2; ++part) {
+    const LimbMap m = part == 0 ? LimbMap::q(lq, L) : LimbMap::ponly(kp, L);
+    const int rows = part == 0 ? lq : kp, first = part == 0 ? 0 : L;
+    const size_t off = (size_t)first * N;
+    small_ntt(c, nonce_ksk_low(key_id, 1), 1, m, rows, e + off, scratch);
+    uniform_kernel<<<grid_for(c, rows), kThreads, 0, c.stream>>>(a + off, ck, nonce_ksk_low(key_id, 0), m, c.logN,
+                                                                 c.d_mods);
+    rlwe_combine_kernel<<<grid_for(c, rows), kThreads, 0, c.stream>>>(e, a, c.d_sk, s_from, c.d_pmod_low, 0, lq, b,
+                                                                      c.logN, c.d_mods, first);
     CKKS_CUDA(cudaGetLastError());
   }
   c.release(e);

@@ -207,8 +207,8 @@ __global__ void __launch_bounds__(kThreads) rescale_combine_kernel(const uint64_
 
 void modup(const Context& c, const uint64_t* d_ntt, int limbs, uint64_t* ext, cudaStream_t st) {
   if (c.alpha > kMaxAlpha) throw Error(kErrArgument, "alpha above 16 is not supported");
-  const int N = c.N, E = limbs + c.K;
-  const LevelTables& lt = c.levels[limbs];
+  const int N = c.N, E = limbs + c.Kx(limbs);
+  const LevelTables& lt = c.lt(limbs);
   uint64_t* dc = (uint64_t*)c.alloc(sizeof(uint64_t) * (size_t)limbs * N);
   CKKS_CUDA(cudaMemcpyAsync(dc, d_ntt, sizeof(uint64_t) * (size_t)limbs * N, cudaMemcpyDeviceToDevice, st));
   ntt_inverse(c, dc, limbs, LimbMap::q(limbs, c.L), st, lt.d_up_scale_a, lt.d_up_scale_b);
@@ -224,11 +224,11 @@ void modup(const Context& c, const uint64_t* d_ntt, int limbs, uint64_t* ext, cu
                 : c.alpha <= 8 ? modup_conv_kernel<8>
                 : c.alpha <= 12 ? modup_conv_kernel<12>
                                 : modup_conv_kernel<16>;
-    kern<<<grid, kThreads, 0, st>>>(dc, d_ntt, ext, limbs, c.L, c.K, c.alpha, c.logN, nchunks, c.d_mods,
+    kern<<<grid, kThreads, 0, st>>>(dc, d_ntt, ext, limbs, c.L, c.Kx(limbs), c.alpha, c.logN, nchunks, c.d_mods,
                                     lt.d_up_hat);
   }
   CKKS_CUDA(cudaGetLastError());
-  LimbMap m = LimbMap::ext(limbs, c.K, c.L);
+  LimbMap m = LimbMap::ext(limbs, c.Kx(limbs), c.L);
   m.skip_alpha = c.alpha;
   ntt_forward(c, ext, lt.beta * E, m, st);
   c.release(dc);
@@ -236,33 +236,33 @@ void modup(const Context& c, const uint64_t* d_ntt, int limbs, uint64_t* ext, cu
 
 void ks_inner(const Context& c, const uint64_t* ext, int limbs, const uint64_t* key, uint32_t g, uint64_t* acc,
               cudaStream_t st) {
-  const LevelTables& lt = c.levels[limbs];
-  const dim3 grid((c.N + kThreads - 1) / kThreads, limbs + c.K);
-  const double E = limbs + c.K;
+  const LevelTables& lt = c.lt(limbs);
+  const dim3 grid((c.N + kThreads - 1) / kThreads, limbs + c.Kx(limbs));
+  const double E = limbs + c.Kx(limbs);
   ProfScope ps(c, "ks_inner", (3.0 * lt.beta * E + 2.0 * E) * c.limb_bytes(), st);
-  ks_inner_kernel<<<grid, kThreads, 0, st>>>(ext, key, acc, limbs, c.L, c.K, c.P, lt.beta, g, c.logN, c.d_mods);
+  ks_inner_kernel<<<grid, kThreads, 0, st>>>(ext, key, acc, limbs, c.L, c.Kx(limbs), c.P, lt.beta, g, c.logN, c.d_mods);
   CKKS_CUDA(cudaGetLastError());
 }
 
 void moddown2(const Context& c, uint64_t* acc, int limbs, const uint64_t* add0, uint32_t g_add0,
               const uint64_t* add1, uint64_t* out0, uint64_t* out1, cudaStream_t st) {
-  if (c.K > kMaxK) throw Error(kErrArgument, "more than 16 special primes is not supported");
-  const int N = c.N, E = limbs + c.K;
-  const LevelTables& lt = c.levels[limbs];
+  if (c.Kx(limbs) > kMaxK) throw Error(kErrArgument, "more than 16 special primes is not supported");
+  const int N = c.N, E = limbs + c.Kx(limbs);
+  const LevelTables& lt = c.lt(limbs);
   // both polynomials' special limbs in one launch (the Q limbs are skipped)
-  LimbMap pm = LimbMap::ext(limbs, c.K, c.L);
+  LimbMap pm = LimbMap::ext(limbs, c.Kx(limbs), c.L);
   pm.skip_q = 1;
-  ntt_inverse(c, acc, 2 * E, pm, st, c.d_down_scale_a, c.d_down_scale_b, c.L);
+  ntt_inverse(c, acc, 2 * E, pm, st, c.down_scale_a(limbs), c.down_scale_b(limbs), c.L);
   uint64_t* conv = (uint64_t*)c.alloc(sizeof(uint64_t) * 2 * (size_t)limbs * N);
   const int nchunks = (limbs + kTargets - 1) / kTargets;
   const dim3 g1((N / 2 + kThreads - 1) / kThreads, 2 * nchunks);
   {
-    ProfScope ps1(c, "moddown_conv", (2.0 * c.K + 2.0 * limbs) * c.limb_bytes(), st);
-    auto kern = c.K <= 4 ? moddown_conv_kernel<4>
-                : c.K <= 8 ? moddown_conv_kernel<8>
-                : c.K <= 12 ? moddown_conv_kernel<12>
+    ProfScope ps1(c, "moddown_conv", (2.0 * c.Kx(limbs) + 2.0 * limbs) * c.limb_bytes(), st);
+    auto kern = c.Kx(limbs) <= 4 ? moddown_conv_kernel<4>
+                : c.Kx(limbs) <= 8 ? moddown_conv_kernel<8>
+                : c.Kx(limbs) <= 12 ? moddown_conv_kernel<12>
                             : moddown_conv_kernel<16>;
-    kern<<<g1, kThreads, 0, st>>>(acc, conv, limbs, c.L, c.K, c.logN, nchunks, c.d_mods, lt.d_down_phat);
+    kern<<<g1, kThreads, 0, st>>>(acc, conv, limbs, c.L, c.Kx(limbs), c.logN, nchunks, c.d_mods, lt.d_down_phat);
   }
   CKKS_CUDA(cudaGetLastError());
   ntt_forward(c, conv, 2 * limbs, LimbMap::q(limbs, c.L), st);
@@ -270,7 +270,7 @@ void moddown2(const Context& c, uint64_t* acc, int limbs, const uint64_t* add0, 
   {
     ProfScope ps2(c, "moddown_combine", ((add0 ? 1.0 : 0.0) + (add1 ? 1.0 : 0.0) + 6.0) * limbs * c.limb_bytes(),
                   st);
-    moddown_combine_kernel<<<g2, kThreads, 0, st>>>(acc, conv, add0, g_add0, add1, out0, out1, limbs, c.K, c.logN,
+    moddown_combine_kernel<<<g2, kThreads, 0, st>>>(acc, conv, add0, g_add0, add1, out0, out1, limbs, c.Kx(limbs), c.logN,
                                                     c.d_mods, lt.d_down_pinv);
   }
   CKKS_CUDA(cudaGetLastError());
@@ -281,7 +281,7 @@ void rescale(const Context& c, const uint64_t* x, size_t sx, int npolys, int lim
              cudaStream_t st) {
   if (limbs < 2) throw Error(kErrLevel, "cannot rescale a single-limb ciphertext");
   const int N = c.N, lo = limbs - 1;
-  const LevelTables& lt = c.levels[limbs];
+  const LevelTables& lt = c.lt(limbs);
   uint64_t* last = (uint64_t*)c.alloc(sizeof(uint64_t) * (size_t)npolys * N);
   for (int p = 0; p < npolys; ++p)
     CKKS_CUDA(cudaMemcpyAsync(last + (size_t)p * N, x + p * sx + (size_t)lo * N, sizeof(uint64_t) * N,
@@ -310,8 +310,8 @@ void rescale(const Context& c, const uint64_t* x, size_t sx, int npolys, int lim
 // same kernels and order as modup() / moddown2(), no allocation.
 void modup_with(const Context& c, const uint64_t* d_ntt, int limbs, uint64_t* ext, uint64_t* dc, cudaStream_t st) {
   if (c.alpha > kMaxAlpha) throw Error(kErrArgument, "alpha above 16 is not supported");
-  const int N = c.N, E = limbs + c.K;
-  const LevelTables& lt = c.levels[limbs];
+  const int N = c.N, E = limbs + c.Kx(limbs);
+  const LevelTables& lt = c.lt(limbs);
   CKKS_CUDA(cudaMemcpyAsync(dc, d_ntt, sizeof(uint64_t) * (size_t)limbs * N, cudaMemcpyDeviceToDevice, st));
   ntt_inverse(c, dc, limbs, LimbMap::q(limbs, c.L), st, lt.d_up_scale_a, lt.d_up_scale_b);
   // the last digit may hold fewer than alpha limbs and so has the most targets
@@ -324,32 +324,32 @@ void modup_with(const Context& c, const uint64_t* d_ntt, int limbs, uint64_t* ex
                 : c.alpha <= 8 ? modup_conv_kernel<8>
                 : c.alpha <= 12 ? modup_conv_kernel<12>
                                 : modup_conv_kernel<16>;
-    kern<<<grid, kThreads, 0, st>>>(dc, d_ntt, ext, limbs, c.L, c.K, c.alpha, c.logN, nchunks, c.d_mods,
+    kern<<<grid, kThreads, 0, st>>>(dc, d_ntt, ext, limbs, c.L, c.Kx(limbs), c.alpha, c.logN, nchunks, c.d_mods,
                                     lt.d_up_hat);
   }
   CKKS_CUDA(cudaGetLastError());
-  LimbMap m = LimbMap::ext(limbs, c.K, c.L);
+  LimbMap m = LimbMap::ext(limbs, c.Kx(limbs), c.L);
   m.skip_alpha = c.alpha;
   ntt_forward(c, ext, lt.beta * E, m, st);
 }
 
 void moddown2_with(const Context& c, uint64_t* acc, int limbs, const uint64_t* add0, uint32_t g_add0,
                    const uint64_t* add1, uint64_t* out0, uint64_t* out1, uint64_t* conv, cudaStream_t st) {
-  if (c.K > kMaxK) throw Error(kErrArgument, "more than 16 special primes is not supported");
-  const int N = c.N, E = limbs + c.K;
-  const LevelTables& lt = c.levels[limbs];
-  LimbMap pm = LimbMap::ext(limbs, c.K, c.L);
+  if (c.Kx(limbs) > kMaxK) throw Error(kErrArgument, "more than 16 special primes is not supported");
+  const int N = c.N, E = limbs + c.Kx(limbs);
+  const LevelTables& lt = c.lt(limbs);
+  LimbMap pm = LimbMap::ext(limbs, c.Kx(limbs), c.L);
   pm.skip_q = 1;
-  ntt_inverse(c, acc, 2 * E, pm, st, c.d_down_scale_a, c.d_down_scale_b, c.L);
+  ntt_inverse(c, acc, 2 * E, pm, st, c.down_scale_a(limbs), c.down_scale_b(limbs), c.L);
   const int nchunks = (limbs + kTargets - 1) / kTargets;
   const dim3 g1((N / 2 + kThreads - 1) / kThreads, 2 * nchunks);
   {
-    ProfScope ps1(c, "moddown_conv", (2.0 * c.K + 2.0 * limbs) * c.limb_bytes(), st);
-    auto kern = c.K <= 4 ? moddown_conv_kernel<4>
-                : c.K <= 8 ? moddown_conv_kernel<8>
-                : c.K <= 12 ? moddown_conv_kernel<12>
+    ProfScope ps1(c, "moddown_conv", (2.0 * c.Kx(limbs) + 2.0 * limbs) * c.limb_bytes(), st);
+    auto kern = c.Kx(limbs) <= 4 ? moddown_conv_kernel<4>
+                : c.Kx(limbs) <= 8 ? moddown_conv_kernel<8>
+                : c.Kx(limbs) <= 12 ? moddown_conv_kernel<12>
                             : moddown_conv_kernel<16>;
-    kern<<<g1, kThreads, 0, st>>>(acc, conv, limbs, c.L, c.K, c.logN, nchunks, c.d_mods, lt.d_down_phat);
+    kern<<<g1, kThreads, 0, st>>>(acc, conv, limbs, c.L, c.Kx(limbs), c.logN, nchunks, c.d_mods, lt.d_down_phat);
   }
   CKKS_CUDA(cudaGetLastError());
   ntt_forward(c, conv, 2 * limbs, LimbMap::q(limbs, c.L), st);
@@ -357,7 +357,7 @@ void moddown2_with(const Context& c, uint64_t* acc, int limbs, const uint64_t* a
   {
     ProfScope ps2(c, "moddown_combine", ((add0 ? 1.0 : 0.0) + (add1 ? 1.0 : 0.0) + 6.0) * limbs * c.limb_bytes(),
                   st);
-    moddown_combine_kernel<<<g2, kThreads, 0, st>>>(acc, conv, add0, g_add0, add1, out0, out1, limbs, c.K, c.logN,
+    moddown_combine_kernel<<<g2, kThreads, 0, st>>>(acc, conv, add0, g_add0, add1, out0, out1, limbs, c.Kx(limbs), c.logN,
                                                     c.d_mods, lt.d_down_pinv);
   }
   CKKS_CUDA(cudaGetLastError());
@@ -451,6 +451,72 @@ __global__ void __launch_bounds__(kThreads) ks_inner_batch_kernel(KsBatch b, con
   uint64_t* acc = acc_all + (size_t)m * 2 * E * N;
   acc[(size_t)t * N + n] = reduce128(s0, md);
   acc[((size_t)E + t) * N + n] = reduce128(s1, md);
+}
+
+// inner products of every item summed: acc = sum_m sum_j ext_{m,j}[pi_m(n)] key_{m,j};
+// the 128-bit accumulators are folded to a residue every `fold` items so that
+// at most 63 products are ever summed unreduced
+__global__ void __launch_bounds__(kThreads) ks_inner_sum_kernel(KsBatch b, const uint64_t* __restrict__ ext_all,
+                                                                uint64_t* __restrict__ acc, int limbs, int L, int K,
+                                                                int P, int beta, int logN, int fold,
+                                                                const Mod* __restrict__ mods) {
+  const int N = 1 << logN;
+  const int n = blockIdx.x * kThreads + threadIdx.x;
+  if (n >= N) return;
+  const int t = blockIdx.y;
+  const int E = limbs + K;
+  const int pt = t < limbs ? t : L + (t - limbs);
+  const Mod md = mods[pt];
+  U128 s0{0, 0}, s1{0, 0};
+  for (int m = 0; m < b.M; ++m) {
+    const uint32_t g = b.g[m];
+    const uint32_t src = (g == 1u) ? (uint32_t)n : auto_index((uint32_t)n, g, logN);
+    const uint64_t* ext = ext_all + (size_t)m * beta * E * N;
+    const uint64_t* key = b.key[m];
+    for (int j = 0; j < beta; ++j) {
+      const uint64_t v = ext[((size_t)j * E + t) * N + src];
+      mac_wide(s0, v, key[((size_t)j * 2 * P + pt) * N + n]);
+      mac_wide(s1, v, key[((size_t)j * 2 * P + P + pt) * N + n]);
+    }
+    if ((m + 1) % fold == 0) {
+      s0 = U128{reduce128(s0, md), 0};
+      s1 = U128{reduce128(s1, md), 0};
+    }
+  }
+  acc[(size_t)t * N + n] = reduce128(s0, md);
+  acc[((size_t)E + t) * N + n] = reduce128(s1, md);
+}
+
+// (acc - conv) P^-1 plus every item's automorphism-permuted c0 (output 0)
+// or c1 addend (output 1)
+__global__ void __launch_bounds__(kThreads) moddown_combine_sum_kernel(KsBatch b, const uint64_t* __restrict__ acc,
+                                                                      const uint64_t* __restrict__ conv,
+                                                                      uint64_t* __restrict__ out0,
+                                                                      uint64_t* __restrict__ out1, int limbs, int K,
+                                                                      int logN, const Mod* __restrict__ mods,
+                                                                      const ulonglong2* __restrict__ pinv) {
+  const int N = 1 << logN;
+  const int n = blockIdx.x * kThreads + threadIdx.x;
+  if (n >= N) return;
+  const int t = blockIdx.y % limbs, p = blockIdx.y / limbs;
+  const int E = limbs + K;
+  const uint64_t q = mods[t].q;
+  const ulonglong2 pv = pinv[t];
+  uint64_t r = mul_shoup(sub_mod(acc[((size_t)p * E + t) * N + n], conv[((size_t)p * limbs + t) * N + n], q), pv.x,
+                         pv.y, q);
+  for (int m = 0; m < b.M; ++m) {
+    if (p == 0) {
+      const uint64_t* a0 = b.add0[m];
+      if (!a0) continue;
+      const uint32_t g = b.g[m];
+      const uint32_t src = (g == 1u) ? (uint32_t)n : auto_index((uint32_t)n, g, logN);
+      r = add_mod(r, a0[(size_t)t * N + src], q);
+    } else {
+      const uint64_t* a1 = b.add1[m];
+      if (a1) r = add_mod(r, a1[(size_t)t * N + n], q);
+    }
+  }
+  (p == 0 ? out0 : out1)[(size_t)t * N + n] = r;
 }
 
 template <int MAXK>
@@ -562,12 +628,12 @@ __global__ void __launch_bounds__(kThreads) rs_combine_batch_kernel(RsBatch b, c
 }  // namespace
 
 void keyswitch_batch(const Context& c, int limbs, const KsBatch& b, bool shared, cudaStream_t st) {
-  if (c.alpha > kMaxAlpha || c.K > kMaxK) throw Error(kErrArgument, "digit size above 16 is not supported");
+  if (c.alpha > kMaxAlpha || c.Kx(limbs) > kMaxK) throw Error(kErrArgument, "digit size above 16 is not supported");
   const int M = b.M;
   if (M <= 0) return;
   if (M > kKsBatch) throw Error(kErrArgument, "key-switch batch above 32");
-  const int N = c.N, E = limbs + c.K;
-  const LevelTables& lt = c.levels[limbs];
+  const int N = c.N, E = limbs + c.Kx(limbs);
+  const LevelTables& lt = c.lt(limbs);
   const int Mu = shared ? 1 : M;  // ModUp inputs
   const double lb = c.limb_bytes();
   uint64_t* dc = (uint64_t*)c.alloc(sizeof(uint64_t) * (size_t)Mu * limbs * N);
@@ -589,11 +655,11 @@ void keyswitch_batch(const Context& c, int limbs, const KsBatch& b, bool shared,
                 : c.alpha <= 12 ? modup_conv_batch_kernel<12>
                                 : modup_conv_batch_kernel<16>;
     kern<<<dim3((N / 2 + kThreads - 1) / kThreads, lt.beta * nch_up, Mu), kThreads, 0, st>>>(
-        b, dc, ext, limbs, c.L, c.K, c.alpha, lt.beta, c.logN, nch_up, c.d_mods, lt.d_up_hat);
+        b, dc, ext, limbs, c.L, c.Kx(limbs), c.alpha, lt.beta, c.logN, nch_up, c.d_mods, lt.d_up_hat);
   }
   CKKS_CUDA(cudaGetLastError());
   {
-    LimbMap m = LimbMap::ext(limbs, c.K, c.L);
+    LimbMap m = LimbMap::ext(limbs, c.Kx(limbs), c.L);
     m.skip_alpha = c.alpha;
     m.skip_beta = lt.beta;
     ntt_forward(c, ext, Mu * lt.beta * E, m, st);
@@ -602,31 +668,104 @@ void keyswitch_batch(const Context& c, int limbs, const KsBatch& b, bool shared,
   {
     ProfScope ps(c, "ks_inner", M * (2.0 * lt.beta * E + 2.0 * E) * lb + Mu * (double)lt.beta * E * lb, st);
     ks_inner_batch_kernel<<<dim3((N + kThreads - 1) / kThreads, E, M), kThreads, 0, st>>>(
-        b, ext, shared, acc, limbs, c.L, c.K, c.P, lt.beta, c.logN, c.d_mods);
+        b, ext, shared, acc, limbs, c.L, c.Kx(limbs), c.P, lt.beta, c.logN, c.d_mods);
   }
   CKKS_CUDA(cudaGetLastError());
   // ModDown
   {
-    LimbMap pm = LimbMap::ext(limbs, c.K, c.L);
+    LimbMap pm = LimbMap::ext(limbs, c.Kx(limbs), c.L);
     pm.skip_q = 1;
-    ntt_inverse(c, acc, M * 2 * E, pm, st, c.d_down_scale_a, c.d_down_scale_b, c.L);
+    ntt_inverse(c, acc, M * 2 * E, pm, st, c.down_scale_a(limbs), c.down_scale_b(limbs), c.L);
   }
   const int nch_dn = (limbs + kTargets - 1) / kTargets;
   {
-    ProfScope ps(c, "moddown_conv", M * (2.0 * c.K + 2.0 * limbs) * lb, st);
-    auto kern = c.K <= 4 ? moddown_conv_batch_kernel<4>
-                : c.K <= 8 ? moddown_conv_batch_kernel<8>
-                : c.K <= 12 ? moddown_conv_batch_kernel<12>
+    ProfScope ps(c, "moddown_conv", M * (2.0 * c.Kx(limbs) + 2.0 * limbs) * lb, st);
+    auto kern = c.Kx(limbs) <= 4 ? moddown_conv_batch_kernel<4>
+                : c.Kx(limbs) <= 8 ? moddown_conv_batch_kernel<8>
+                : c.Kx(limbs) <= 12 ? moddown_conv_batch_kernel<12>
                             : moddown_conv_batch_kernel<16>;
     kern<<<dim3((N / 2 + kThreads - 1) / kThreads, 2 * nch_dn, M), kThreads, 0, st>>>(
-        acc, conv, limbs, c.L, c.K, c.logN, nch_dn, c.d_mods, lt.d_down_phat);
+        acc, conv, limbs, c.L, c.Kx(limbs), c.logN, nch_dn, c.d_mods, lt.d_down_phat);
   }
   CKKS_CUDA(cudaGetLastError());
   ntt_forward(c, conv, M * 2 * limbs, LimbMap::q(limbs, c.L), st);
   {
     ProfScope ps(c, "moddown_combine", M * 8.0 * limbs * lb, st);
     moddown_combine_batch_kernel<<<dim3((N + kThreads - 1) / kThreads, 2 * limbs, M), kThreads, 0, st>>>(
-        b, acc, conv, limbs, c.K, c.logN, c.d_mods, lt.d_down_pinv);
+        b, acc, conv, limbs, c.Kx(limbs), c.logN, c.d_mods, lt.d_down_pinv);
+  }
+  CKKS_CUDA(cudaGetLastError());
+  c.release(dc);
+  c.release(ext);
+  c.release(acc);
+  c.release(conv);
+}
+
+void keyswitch_sum(const Context& c, int limbs, const KsBatch& b, uint64_t* out0, uint64_t* out1, cudaStream_t st) {
+  if (c.alpha > kMaxAlpha || c.Kx(limbs) > kMaxK) throw Error(kErrArgument, "digit size above 16 is not supported");
+  const int M = b.M;
+  if (M <= 0 || M > kKsBatch) throw Error(kErrArgument, "key-switch sum of 1..32 items");
+  const int N = c.N, E = limbs + c.Kx(limbs);
+  const LevelTables& lt = c.lt(limbs);
+  const double lb = c.limb_bytes();
+  uint64_t* dc = (uint64_t*)c.alloc(sizeof(uint64_t) * (size_t)M * limbs * N);
+  uint64_t* ext = (uint64_t*)c.alloc(sizeof(uint64_t) * (size_t)M * lt.beta * E * N);
+  uint64_t* acc = (uint64_t*)c.alloc(sizeof(uint64_t) * (size_t)2 * E * N);
+  uint64_t* conv = (uint64_t*)c.alloc(sizeof(uint64_t) * (size_t)2 * limbs * N);
+  // ModUp of every item
+  {
+    ProfScope ps(c, "ks_gather", 2.0 * M * limbs * lb, st);
+    gather_kernel<<<dim3((N / 2 + kThreads - 1) / kThreads, limbs, M), kThreads, 0, st>>>(b, limbs, c.logN, dc);
+  }
+  ntt_inverse(c, dc, M * limbs, LimbMap::q(limbs, c.L), st, lt.d_up_scale_a, lt.d_up_scale_b);
+  const int min_cnt = limbs - (lt.beta - 1) * c.alpha;
+  const int nch_up = (E - min_cnt + kTargets - 1) / kTargets;
+  {
+    ProfScope ps(c, "modup_conv", M * (2.0 * limbs + (double)lt.beta * E) * lb, st);
+    auto kern = c.alpha <= 4 ? modup_conv_batch_kernel<4>
+                : c.alpha <= 8 ? modup_conv_batch_kernel<8>
+                : c.alpha <= 12 ? modup_conv_batch_kernel<12>
+                                : modup_conv_batch_kernel<16>;
+    kern<<<dim3((N / 2 + kThreads - 1) / kThreads, lt.beta * nch_up, M), kThreads, 0, st>>>(
+        b, dc, ext, limbs, c.L, c.Kx(limbs), c.alpha, lt.beta, c.logN, nch_up, c.d_mods, lt.d_up_hat);
+  }
+  CKKS_CUDA(cudaGetLastError());
+  {
+    LimbMap m = LimbMap::ext(limbs, c.Kx(limbs), c.L);
+    m.skip_alpha = c.alpha;
+    m.skip_beta = lt.beta;
+    ntt_forward(c, ext, M * lt.beta * E, m, st);
+  }
+  // summed key inner products
+  {
+    const int fold = 63 / lt.beta;
+    ProfScope ps(c, "ks_inner_sum", (M * 3.0 * lt.beta * E + 2.0 * E) * lb, st);
+    ks_inner_sum_kernel<<<dim3((N + kThreads - 1) / kThreads, E), kThreads, 0, st>>>(
+        b, ext, acc, limbs, c.L, c.Kx(limbs), c.P, lt.beta, c.logN, fold, c.d_mods);
+  }
+  CKKS_CUDA(cudaGetLastError());
+  // one ModDown
+  {
+    LimbMap pm = LimbMap::ext(limbs, c.Kx(limbs), c.L);
+    pm.skip_q = 1;
+    ntt_inverse(c, acc, 2 * E, pm, st, c.down_scale_a(limbs), c.down_scale_b(limbs), c.L);
+  }
+  const int nch_dn = (limbs + kTargets - 1) / kTargets;
+  {
+    ProfScope ps(c, "moddown_conv", (2.0 * c.Kx(limbs) + 2.0 * limbs) * lb, st);
+    auto kern = c.Kx(limbs) <= 4 ? moddown_conv_batch_kernel<4>
+                : c.Kx(limbs) <= 8 ? moddown_conv_batch_kernel<8>
+                : c.Kx(limbs) <= 12 ? moddown_conv_batch_kernel<12>
+                            : moddown_conv_batch_kernel<16>;
+    kern<<<dim3((N / 2 + kThreads - 1) / kThreads, 2 * nch_dn, 1), kThreads, 0, st>>>(
+        acc, conv, limbs, c.L, c.Kx(limbs), c.logN, nch_dn, c.d_mods, lt.d_down_phat);
+  }
+  CKKS_CUDA(cudaGetLastError());
+  ntt_forward(c, conv, 2 * limbs, LimbMap::q(limbs, c.L), st);
+  {
+    ProfScope ps(c, "moddown_combine_sum", (6.0 + M) * limbs * lb, st);
+    moddown_combine_sum_kernel<<<dim3((N + kThreads - 1) / kThreads, 2 * limbs), kThreads, 0, st>>>(
+        b, acc, conv, out0, out1, limbs, c.Kx(limbs), c.logN, c.d_mods, lt.d_down_pinv);
   }
   CKKS_CUDA(cudaGetLastError());
   c.release(dc);
@@ -641,7 +780,7 @@ void rescale_batch(const Context& c, int limbs, const RsBatch& b, cudaStream_t s
   if (M <= 0) return;
   if (M > kKsBatch) throw Error(kErrArgument, "rescale batch above 32");
   const int N = c.N, lo = limbs - 1;
-  const LevelTables& lt = c.levels[limbs];
+  const LevelTables& lt = c.lt(limbs);
   const double lb = c.limb_bytes();
   uint64_t* last = (uint64_t*)c.alloc(sizeof(uint64_t) * (size_t)2 * M * N);
   uint64_t* tmp = (uint64_t*)c.alloc(sizeof(uint64_t) * (size_t)2 * M * lo * N);

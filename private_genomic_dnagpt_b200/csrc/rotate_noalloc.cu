@@ -64,8 +64,8 @@ extern "C" int ckks_rotate_noalloc(ckks_ctx* ctx, const uint64_t* in_dev, int li
     ckks::Context& c = *ctx->c;
     if (!in_dev || !out_dev) throw ckks::Error(CKKS_EARG, "null device buffer");
     if (limbs < 1 || limbs > c.L) throw ckks::Error(CKKS_EARG, "limb count outside 1..L");
-    const size_t N = (size_t)c.N, S = (size_t)limbs * N, E = (size_t)limbs + c.K;
-    const size_t beta = (size_t)c.levels[limbs].beta;
+    const size_t N = (size_t)c.N, S = (size_t)limbs * N, E = (size_t)limbs + c.Kx(limbs);
+    const size_t beta = (size_t)c.lt(limbs).beta;
     const size_t need = (beta * E + 2 * E + 2 * (size_t)limbs) * N;
     if (need > kScratchWords)
       throw ckks::Error(CKKS_ECAPACITY, "rotation needs " + std::to_string(need * 8 >> 20) +
@@ -75,7 +75,7 @@ extern "C" int ckks_rotate_noalloc(ckks_ctx* ctx, const uint64_t* in_dev, int li
     const uint64_t *lo_out = out_dev, *hi_out = out_dev + 2 * S;
     if (lo_in < hi_out && lo_out < hi_in) throw ckks::Error(CKKS_EARG, "output overlaps input");
     const uint32_t g = c.galois(k);
-    const uint64_t* key = g == 1u ? nullptr : c.rot_key(g);
+    const uint64_t* key = g == 1u ? nullptr : c.switch_key(g, limbs);
     if (g != 1u && !key) throw ckks::Error(CKKS_EKEY, "rotation key not generated for index " + std::to_string(k));
     uint64_t* scratch = scratch_on(c.params.device);
     if (g == 1u) {

@@ -201,6 +201,20 @@ def test_hoisted_and_inplace(pair10):
     assert np.array_equal(cx.limbs_array(), o.rotate(rx, 5))
 
 
+@pytest.mark.parametrize("ks", [[0, 1, 2, 5, -7], [1] * 3 + [2, 3, 5, 8, 64, 100, -1, -7] * 4 + [0]])
+def test_rotate_sum_bit_exact(pair10, ks):
+    """Giant-step sums: one ModDown per group of 32 non-identity rotations
+    (the second case spans two groups and an identity term)."""
+    o, cc = pair10
+    limbs = 5
+    fr = [_fresh(o, cc, 50 + i, limbs) for i in range(len(ks))]
+    got = cc.EvalRotateSum([f[2] for f in fr], ks)
+    ref = o.rotate_sum(np.stack([f[1] for f in fr]), ks)
+    assert np.array_equal(got.limbs_array(), ref)
+    dec = cc.Decrypt(got).GetRealPackedValue()
+    assert np.abs(dec - sum(np.roll(f[0], -k) for f, k in zip(fr, ks))).max() < 1e-7
+
+
 @pytest.mark.parametrize("count,stride", [(64, 4), (16, 32)])
 def test_accumulate_sum_bit_exact(pair10, count, stride):
     o, cc = pair10
@@ -357,3 +371,42 @@ def test_add_many_and_add_batch_bit_exact(pair10):
     outs = cc.add_batch([it[2] for it in items[:35]], [it[2] for it in items[35:70]])
     for i, out in enumerate(outs):
         assert np.array_equal(out.limbs_array(), o.add(items[i][1], items[35 + i][1]))
+
+
+# ---- key switches over the reduced special-prime set (alpha = K = 8) -------
+WIDE_ROT = [1, 3, 5, 32, -7] + ladder_keys(16, 4)
+
+
+@pytest.fixture(scope="module")
+def pair_wide():
+    return make_pair(12, 8, 1, 23, rot=sorted(set(WIDE_ROT)))
+
+
+def test_reduced_set_keys_bit_exact(pair_wide):
+    o, cc = pair_wide
+    assert (cc.low_limbs, cc.K_low) == (o.low_limbs, o.K_low) == (4, 4)
+    assert np.array_equal(cc.key_array(2), o.switch_key(0))
+    assert np.array_equal(cc.key_array(4), o.switch_key_low(0))
+    for k in (1, -7, 32):
+        assert np.array_equal(cc.key_array(3, k), o.switch_key(k))
+        assert np.array_equal(cc.key_array(5, k), o.switch_key_low(k))
+
+
+@pytest.mark.parametrize("limbs", [1, 2, 3, 4, 5, 8])
+def test_key_switches_across_the_reduced_set_boundary(pair_wide, limbs):
+    o, cc = pair_wide
+    x, rx, cx = _fresh(o, cc, 80 + limbs, limbs)
+    y, ry, cy = _fresh(o, cc, 90 + limbs, limbs)
+    for k in (1, -7, 32):
+        assert np.array_equal(cc.EvalRotate(cx, k).limbs_array(), o.rotate(rx, k))
+    outs = cc.EvalFastRotation(cx, [1, 3, 5])
+    ref = o.rotate_hoisted(rx, [1, 3, 5])
+    for i in range(3):
+        assert np.array_equal(outs[i].limbs_array(), ref[i])
+    assert np.array_equal(cc.mul_ct(cx, cy).limbs_array(), o.mul_ct(rx, ry))
+    got = cc.EvalRotateSum([cx, cy, cx], [0, 3, 5])
+    assert np.array_equal(got.limbs_array(), o.rotate_sum(np.stack([rx, ry, rx]), [0, 3, 5]))
+    rb = cc.rotate_batch([cx, cy], [5, -7])
+    assert np.array_equal(rb[0].limbs_array(), o.rotate(rx, 5))
+    assert np.array_equal(rb[1].limbs_array(), o.rotate(ry, -7))
+    assert np.array_equal(cc.AccumulateSum(cx, 16, 4).limbs_array(), o.accumulate_sum(rx, 16, 4))

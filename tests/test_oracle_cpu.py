@@ -180,6 +180,21 @@ def test_hoisted_equals_single_rotations(small):
     assert np.array_equal(h[3], ct)
 
 
+def test_rotate_sum_decrypts_to_the_sum_of_rotations(small):
+    o = small
+    rng = np.random.default_rng(41)
+    xs = [rng.uniform(-1, 1, o.N // 2) for _ in range(4)]
+    ks = [0, 1, 3, 7]
+    S = o.scale(4)
+    cts = np.stack([o.encrypt(o.encode(x, 4), 40 + i) for i, x in enumerate(xs)])
+    got = o.decode(o.decrypt(o.rotate_sum(cts, ks)), S)
+    ref = sum(np.roll(x, -k) for x, k in zip(xs, ks))
+    assert np.abs(got - ref).max() < 1e-8
+    # one ModDown for the group equals the separate rotations up to rounding
+    sep = sum(o.decode(o.decrypt(o.rotate(ct, k)), S) for ct, k in zip(cts, ks))
+    assert np.abs(got - sep).max() < 1e-9
+
+
 @pytest.mark.parametrize("count,stride", ACC_CASES)
 def test_accumulate_sum(small, count, stride):
     o = small
@@ -212,3 +227,44 @@ def test_keyswitch_matches_definition(small):
     centered = np.array([int(v) if int(v) <= q // 2 else int(v) - q for v in diff], dtype=np.float64)
     # ModDown leaves noise of a few hundred units, nowhere near q ~ 2^60
     assert np.abs(centered).max() < 2.0 ** 20
+
+
+@pytest.fixture(scope="module")
+def wide():
+    """alpha = K = 8: key switches at <= 4 limbs use the 4-prime set."""
+    o = Oracle(logN=10, L=8, dnum=1, seed=17)
+    o.keygen()
+    o.relin_keygen()
+    o.rot_keygen([1, 3, 5, 32])
+    return o
+
+
+def test_reduced_special_prime_set_is_chosen_by_bits(wide):
+    o = wide
+    assert (o.low_limbs, o.K_low) == (4, 4) and o.K == 8
+    q = o.moduli
+    assert sum(np.log2(float(p)) for p in q[o.L:o.L + 4]) >= sum(np.log2(float(p)) for p in q[:4]) + 20
+    key = o.switch_key_low(0)
+    used = list(range(4)) + list(range(o.L, o.L + 4))
+    unused = [t for t in range(o.L + o.K) if t not in used]
+    assert not key[:, unused].any() and key[:, used].all(axis=-1).any()
+
+
+@pytest.mark.parametrize("limbs", [1, 2, 3, 4, 5, 8])
+def test_key_switches_on_both_prime_sets_decrypt(wide, limbs):
+    o = wide
+    rng = np.random.default_rng(limbs)
+    x = rng.uniform(-1, 1, o.N // 2)
+    y = rng.uniform(-1, 1, o.N // 2)
+    S = o.scale(limbs)
+    cx = o.encrypt(o.encode(x, limbs), 60 + limbs)
+    cy = o.encrypt(o.encode(y, limbs), 70 + limbs)
+    for k in (1, 5, 32):
+        assert np.abs(o.decode(o.decrypt(o.rotate(cx, k)), S) - np.roll(x, -k)).max() < 1e-7
+    h = o.rotate_hoisted(cx, [1, 3])
+    assert np.abs(o.decode(o.decrypt(h[1]), S) - np.roll(x, -3)).max() < 1e-7
+    if limbs >= 2:  # a product at scale S^2 needs more than the 60-bit first prime
+        prod = o.decode(o.decrypt(o.mul_ct(cx, cy)), S * S)
+        assert np.abs(prod - x * y).max() < 1e-7
+    rs = o.decode(o.decrypt(o.rotate_sum(np.stack([cx, cy]), [1, 5])), S)
+    assert np.abs(rs - np.roll(x, -1) - np.roll(y, -5)).max() < 1e-7

@@ -24,14 +24,16 @@ def _device_copy(arr):
     return t
 
 
-def test_noalloc_rotation_matches_allocating_rotation_twice():
+@pytest.mark.parametrize("dnum,levels", [(3, (8, 5)), (1, (8, 3))])
+def test_noalloc_rotation_matches_allocating_rotation_twice(dnum, levels):
     import torch
-    cc = eng.GenCryptoContext(eng.CCParams(ring_dim_log=13, limbs=8, dnum=3, seed=29))
+    # dnum 1 (alpha = K = 8): the 3-limb case switches over the reduced set
+    cc = eng.GenCryptoContext(eng.CCParams(ring_dim_log=13, limbs=8, dnum=dnum, seed=29))
     cc.KeyGen()
     ks = (1, -3)
     cc.EvalRotateKeyGen(list(ks))
     x = np.random.default_rng(3).uniform(-1, 1, cc.slots)
-    for limbs in (8, 5):
+    for limbs in levels:
         ct = cc.drop_limbs(cc.Encrypt(cc.MakeCKKSPackedPlaintext(x)), limbs)
         src = ct.limbs_array()
         d_in = _device_copy(src)
