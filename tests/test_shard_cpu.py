@@ -153,7 +153,7 @@ def _rank_main(rank, world, port, tokens, out_path):
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("world,tokens", [(2, 40), (2, 70), (3, 70)])
+@pytest.mark.parametrize("world,tokens", [(2, 40), (2, 70), (3, 70), (5, 70)])
 def test_sharded_block_over_gloo_ranks_equals_the_block(tmp_path, world, tokens):
     out = str(tmp_path / "y.npy")
     mp.start_processes(_rank_main, args=(world, _free_port(), tokens, out), nprocs=world, join=True,
