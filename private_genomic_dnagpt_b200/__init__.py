@@ -744,6 +744,21 @@ class EncryptedModel:
         self.tokens = tokens
         self.cached_blocks = len(self.blocks) if cached_blocks is None else cached_blocks
 
+    @classmethod
+    def from_fixture(cls, cc: CryptoContext, directory, tokens: int | None = None, heads: int = 12,
+                     cached_blocks: int | None = None, verify: bool = True):
+        """Blocks and head from a fixture directory in the reference's float64
+        format (`fixture.load_fixture`); tokens default to the fixture's
+        `input.embeddings` rows."""
+        from . import fixture as fx_mod
+        fx = fx_mod.load_fixture(directory, verify)
+        if tokens is None:
+            tokens = fx.embeddings().shape[0]
+        model = cls(cc, [fx.block_weights(b) for b in range(fx.num_blocks)], fx.head_weights(), tokens, heads,
+                    cached_blocks)
+        model.fixture = fx
+        return model
+
     def rotation_indices(self) -> list[int]:
         s = set(self.blocks[0].rotation_indices())
         if self.head is not None:

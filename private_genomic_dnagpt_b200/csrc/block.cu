@@ -97,13 +97,15 @@ __global__ void __launch_bounds__(kThreads) diag_values_kernel(const double* __r
   vals[(size_t)blockIdx.y * slots + s] = diag_value(W, out_dim, in_dim, ld, PW, n1, d / n1, d % n1, s / B);
 }
 
+// token groups that share one pass over a product's diagonals
+constexpr int kMaxGroups = 4;
 struct BabyPtrs {
-  const uint64_t* c0[kMaxBaby];
-  const uint64_t* c1[kMaxBaby];
+  const uint64_t* c0[kMaxGroups][kMaxBaby];
+  const uint64_t* c1[kMaxGroups][kMaxBaby];
 };
 struct InnerPtrs {
-  uint64_t* c0[kMaxBaby];
-  uint64_t* c1[kMaxBaby];
+  uint64_t* c0[kMaxGroups][kMaxBaby];
+  uint64_t* c1[kMaxGroups][kMaxBaby];
 };
 
 // Encoded diagonals are stored tile-major, [limb][coefficient tile][diagonal]
@@ -128,7 +130,9 @@ __global__ void __launch_bounds__(kThreads) diag_tile_kernel(const uint64_t* __r
 // one contiguous 64 KiB span of the tile-major diagonal store.
 constexpr int kBsgsThreads = 128;
 
-__global__ void __launch_bounds__(kBsgsThreads) bsgs_inner_kernel(BabyPtrs babies, int n1,
+// inner sums of giant step g for `ng` token groups at once: every diagonal
+// residue is loaded once and multiplied into each group's baby steps
+__global__ void __launch_bounds__(kBsgsThreads) bsgs_inner_kernel(BabyPtrs babies, int ng, int n1,
                                                                   const uint64_t* __restrict__ diag, InnerPtrs out,
                                                                   int limbs, int logN, int n2,
                                                                   const ckks::Mod* __restrict__ mods) {
@@ -138,19 +142,35 @@ __global__ void __launch_bounds__(kBsgsThreads) bsgs_inner_kernel(BabyPtrs babie
   const size_t off = (size_t)l * N + (size_t)tile * kThreads + c;
   const int ndiag = n1 * n2;
   const uint64_t* dtile = diag + (((size_t)l * (N / kThreads) + tile) * ndiag + (size_t)g * n1) * kThreads + c;
-  ckks::U128 a00{0, 0}, a01{0, 0}, a10{0, 0}, a11{0, 0};
+  ckks::U128 acc[kMaxGroups][4];
+#pragma unroll
+  for (int q = 0; q < kMaxGroups; ++q)
+#pragma unroll
+    for (int k = 0; k < 4; ++k) acc[q][k] = ckks::U128{0, 0};
   for (int j = 0; j < n1; ++j) {
-    const ulonglong2 b0 = *reinterpret_cast<const ulonglong2*>(babies.c0[j] + off);
-    const ulonglong2 b1 = *reinterpret_cast<const ulonglong2*>(babies.c1[j] + off);
     const ulonglong2 dv = __ldg(reinterpret_cast<const ulonglong2*>(dtile + (size_t)j * kThreads));
-    ckks::mac_wide(a00, dv.x, b0.x);
-    ckks::mac_wide(a01, dv.y, b0.y);
-    ckks::mac_wide(a10, dv.x, b1.x);
-    ckks::mac_wide(a11, dv.y, b1.y);
+#pragma unroll
+    for (int q = 0; q < kMaxGroups; ++q) {
+      if (q < ng) {
+        const ulonglong2 b0 = *reinterpret_cast<const ulonglong2*>(babies.c0[q][j] + off);
+        const ulonglong2 b1 = *reinterpret_cast<const ulonglong2*>(babies.c1[q][j] + off);
+        ckks::mac_wide(acc[q][0], dv.x, b0.x);
+        ckks::mac_wide(acc[q][1], dv.y, b0.y);
+        ckks::mac_wide(acc[q][2], dv.x, b1.x);
+        ckks::mac_wide(acc[q][3], dv.y, b1.y);
+      }
+    }
   }
   const ckks::Mod m = mods[l];
-  *reinterpret_cast<ulonglong2*>(out.c0[g] + off) = make_ulonglong2(ckks::reduce128(a00, m), ckks::reduce128(a01, m));
-  *reinterpret_cast<ulonglong2*>(out.c1[g] + off) = make_ulonglong2(ckks::reduce128(a10, m), ckks::reduce128(a11, m));
+#pragma unroll
+  for (int q = 0; q < kMaxGroups; ++q) {
+    if (q < ng) {
+      *reinterpret_cast<ulonglong2*>(out.c0[q][g] + off) =
+          make_ulonglong2(ckks::reduce128(acc[q][0], m), ckks::reduce128(acc[q][1], m));
+      *reinterpret_cast<ulonglong2*>(out.c1[q][g] + off) =
+          make_ulonglong2(ckks::reduce128(acc[q][2], m), ckks::reduce128(acc[q][3], m));
+    }
+  }
 }
 
 // ---- client-side float64 transforms, on the device ------------------------
@@ -625,49 +645,64 @@ struct ckks_block {
     return b;
   }
 
-  // x W^T for weight `id` from the baby-step rotations of x (T123.cpp:1264-1295)
-  Ciphertext bsgs(const std::vector<Ciphertext>& baby, int id) {
-    ++count["matrix_products"];
-    count["ct_plain"] += (long)s.n1 * s.n2;
-    const int limbs = baby[0]->limbs();
+  // x_q W^T for weight `id` and every token group q from their baby-step
+  // rotations (T123.cpp:1264-1295): the inner sums of up to 4 groups share
+  // one pass over the diagonals; the giant steps of each group are one
+  // rotation sum (one ModDown)
+  std::vector<Ciphertext> bsgs_groups(const std::vector<std::vector<Ciphertext>>& babies, int id) {
+    const int G = (int)babies.size();
+    std::vector<Ciphertext> outs(G);
+    if (!G) return outs;
+    count["matrix_products"] += G;
+    count["ct_plain"] += (long)G * s.n1 * s.n2;
+    const int limbs = babies[0][0]->limbs();
     const Diag& dg = diagonals(id, limbs);
-    blk::BabyPtrs bp{};
-    for (int j = 0; j < s.n1; ++j) {
-      const ckks::DevPoly& p = baby[j]->handle()->p;
-      if (p.limbs != limbs) throw ckks::Error(CKKS_ELEVEL, "baby steps at different levels");
-      bp.c0[j] = p.data;
-      bp.c1[j] = p.data + (size_t)p.cap * C.N;
-    }
-    const double sc = baby[0]->scale() * dg.scale;
-    std::vector<Ciphertext> inner(s.n2);
-    blk::InnerPtrs ip{};
-    for (int g = 0; g < s.n2; ++g) {
-      inner[g] = cc.fresh();
-      ckks::DevPoly& p = inner[g]->handle()->p;
-      p.ensure(&C, 2, limbs);
-      p.limbs = limbs;
-      p.scale = sc;
-      p.deg = baby[0]->noise_deg() + 1;
-      ip.c0[g] = p.data;
-      ip.c1[g] = p.data + (size_t)p.cap * C.N;
-    }
-    {
-      ckks::ProfScope ps(C, "bsgs_inner",
-                         ((double)s.n1 * s.n2 * limbs + 2.0 * s.n1 * limbs + 2.0 * s.n2 * limbs) * C.limb_bytes(),
-                         C.stream);
-      const dim3 grid(s.n2, C.N / blk::kThreads, limbs);
-      blk::bsgs_inner_kernel<<<grid, blk::kBsgsThreads, 0, C.stream>>>(bp, s.n1, dg.data, ip, limbs, C.logN, s.n2,
-                                                                       C.d_mods);
-    }
-    CKKS_CUDA(cudaGetLastError());
-    // giant steps: sum_g rot(inner_g, B n1 g), the key switches summed in the
-    // extended basis with one ModDown (g = 0 is the identity)
     std::vector<int> gk(s.n2);
     for (int g = 0; g < s.n2; ++g) gk[g] = s.B * s.n1 * g;
-    count["rotations"] += s.n2 - 1;
-    const Ciphertext acc = cc.EvalRotateSum(inner, gk);
-    return rs(acc);
+    for (int q0 = 0; q0 < G; q0 += blk::kMaxGroups) {
+      const int ng = std::min(blk::kMaxGroups, G - q0);
+      blk::BabyPtrs bp{};
+      blk::InnerPtrs ip{};
+      std::vector<std::vector<Ciphertext>> inner(ng, std::vector<Ciphertext>(s.n2));
+      for (int q = 0; q < ng; ++q) {
+        const auto& baby = babies[q0 + q];
+        for (int j = 0; j < s.n1; ++j) {
+          const ckks::DevPoly& p = baby[j]->handle()->p;
+          if (p.limbs != limbs) throw ckks::Error(CKKS_ELEVEL, "baby steps at different levels");
+          bp.c0[q][j] = p.data;
+          bp.c1[q][j] = p.data + (size_t)p.cap * C.N;
+        }
+        const double sc = baby[0]->scale() * dg.scale;
+        for (int g = 0; g < s.n2; ++g) {
+          inner[q][g] = cc.fresh();
+          ckks::DevPoly& p = inner[q][g]->handle()->p;
+          p.ensure(&C, 2, limbs);
+          p.limbs = limbs;
+          p.scale = sc;
+          p.deg = baby[0]->noise_deg() + 1;
+          ip.c0[q][g] = p.data;
+          ip.c1[q][g] = p.data + (size_t)p.cap * C.N;
+        }
+      }
+      {
+        ckks::ProfScope ps(
+            C, "bsgs_inner",
+            ((double)s.n1 * s.n2 * limbs + ng * (2.0 * s.n1 * limbs + 2.0 * s.n2 * limbs)) * C.limb_bytes(), C.stream);
+        const dim3 grid(s.n2, C.N / blk::kThreads, limbs);
+        blk::bsgs_inner_kernel<<<grid, blk::kBsgsThreads, 0, C.stream>>>(bp, ng, s.n1, dg.data, ip, limbs, C.logN,
+                                                                         s.n2, C.d_mods);
+      }
+      CKKS_CUDA(cudaGetLastError());
+      // giant steps: sum_g rot(inner_g, B n1 g), the key switches summed in the
+      // extended basis with one ModDown (g = 0 is the identity)
+      for (int q = 0; q < ng; ++q) {
+        count["rotations"] += s.n2 - 1;
+        outs[q0 + q] = rs(cc.EvalRotateSum(inner[q], gk));
+      }
+    }
+    return outs;
   }
+  Ciphertext bsgs(const std::vector<Ciphertext>& baby, int id) { return bsgs_groups({baby}, id)[0]; }
 
   static constexpr int kHeadLinear = 100;
   // evaluation state between the stages of one forward
@@ -776,12 +811,13 @@ void ckks_block::shard_qkv(const std::vector<int>& groups) {
     act.push_back(s.count(g));
   }
   const auto nrm = layernorm(xs, act);
+  std::vector<std::vector<Ciphertext>> babies;
+  for (const auto& n : nrm) babies.push_back(babies_of(n));
+  const auto q = bsgs_groups(babies, 0), k = bsgs_groups(babies, 1), v = bsgs_groups(babies, 2);
   for (size_t i = 0; i < groups.size(); ++i) {
-    const int g = groups[i];
-    const auto baby = babies_of(nrm[i]);
-    st_q[g] = bsgs(baby, 0);
-    st_k[g] = bsgs(baby, 1);
-    st_v[g] = bsgs(baby, 2);
+    st_q[groups[i]] = q[i];
+    st_k[groups[i]] = k[i];
+    st_v[groups[i]] = v[i];
   }
   stamp("ln1_qkv");
 }
@@ -896,41 +932,53 @@ void ckks_block::shard_output(const std::vector<int>& groups, double* y) {
   if (groups.empty()) return;
   const int T = s.T, D = s.D, B = s.B, PW = s.PW, SL = slots();
   const int nb = (SL + blk::kThreads - 1) / blk::kThreads;
-  std::vector<Ciphertext> r1;
+  const int G = (int)groups.size();
+  std::vector<std::vector<Ciphertext>> ob;
   std::vector<int> act;
   for (int g : groups) {
     if (!st_ctx[g] || !st_x[g]) throw ckks::Error(CKKS_ESTATE, "context of the group not complete");
-    const Ciphertext o = bsgs(babies_of(st_ctx[g]), 3);
-    r1.push_back(add(reduce_to(st_x[g], o->limbs()), o));
+    ob.push_back(babies_of(st_ctx[g]));
     act.push_back(s.count(g));
   }
+  const auto o = bsgs_groups(ob, 3);
+  ob.clear();
+  std::vector<Ciphertext> r1;
+  for (int i = 0; i < G; ++i) r1.push_back(add(reduce_to(st_x[groups[i]], o[i]->limbs()), o[i]));
   const auto n2 = layernorm(r1, act);
-  std::vector<Ciphertext> out(groups.size());
+  std::vector<std::vector<Ciphertext>> fb;
+  for (const auto& n : n2) fb.push_back(babies_of(n));
+  std::vector<std::vector<Ciphertext>> hc(nfc);  // [chunk][group]
+  for (int c = 0; c < nfc; ++c) hc[c] = bsgs_groups(fb, 4 + c);
+  fb.clear();
+  // client: exact tanh-GELU on the active lanes of every group and chunk, one
+  // device batch (T123.cpp:540-568); item i * nfc + c
   const int gelu_limbs = 3;
-  for (size_t i = 0; i < groups.size(); ++i) {
-    const int g = groups[i];
-    const auto fb = babies_of(n2[i]);
-    std::vector<Ciphertext> hc;
-    for (int c = 0; c < nfc; ++c) hc.push_back(bsgs(fb, 4 + c));
-    // client: exact tanh-GELU on the active lanes (T123.cpp:540-568)
-    double* dv = dbuf((size_t)nfc * SL);
-    client_decrypt(hc, dv);
+  std::vector<Ciphertext> flat;
+  for (int i = 0; i < G; ++i)
+    for (int c = 0; c < nfc; ++c) flat.push_back(hc[c][i]);
+  hc.clear();
+  double* dv = dbuf((size_t)G * nfc * SL);
+  client_decrypt(flat, dv);
+  for (int i = 0; i < G; ++i)
     for (int c = 0; c < nfc; ++c) {
       const int odim = std::min(PW, s.MLP - c * PW);
-      blk::gelu_kernel<<<dim3(nb, 1), blk::kThreads, 0, C.stream>>>(dv + (size_t)c * SL, dv + (size_t)c * SL, B, odim,
-                                                                    s.count(g), SL);
-      count["client_logical_instances"] += (long)odim * s.count(g);
+      double* v = dv + ((size_t)i * nfc + c) * SL;
+      blk::gelu_kernel<<<dim3(nb, 1), blk::kThreads, 0, C.stream>>>(v, v, B, odim, act[i], SL);
+      count["client_logical_instances"] += (long)odim * act[i];
     }
-    const auto ge = client_encrypt(dv, nfc, gelu_limbs);
-    C.release(dv);
-    count["client_round_trips"] += nfc;
-    Ciphertext mlp;
-    for (int c = 0; c < nfc; ++c) {
-      const Ciphertext pc = bsgs(babies_of(ge[c]), 4 + nfc + c);
-      mlp = c ? add(mlp, pc) : pc;
-    }
-    out[i] = add(reduce_to(r1[i], mlp->limbs()), mlp);
+  CKKS_CUDA(cudaGetLastError());
+  const auto ge = client_encrypt(dv, G * nfc, gelu_limbs);
+  C.release(dv);
+  count["client_round_trips"] += (long)G * nfc;
+  std::vector<Ciphertext> mlp(G);
+  for (int c = 0; c < nfc; ++c) {
+    std::vector<std::vector<Ciphertext>> db;
+    for (int i = 0; i < G; ++i) db.push_back(babies_of(ge[(size_t)i * nfc + c]));
+    const auto pc = bsgs_groups(db, 4 + nfc + c);
+    for (int i = 0; i < G; ++i) mlp[i] = c ? add(mlp[i], pc[i]) : pc[i];
   }
+  std::vector<Ciphertext> out(G);
+  for (int i = 0; i < G; ++i) out[i] = add(reduce_to(r1[i], mlp[i]->limbs()), mlp[i]);
   CKKS_CUDA(cudaEventRecord(ev_out, C.stream));
   stamp("oproj_ln2_mlp");
   // client: decrypt and unpack (T123.cpp:1675-1694)

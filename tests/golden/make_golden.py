@@ -8,6 +8,10 @@ Python modules (run in a container that has the reference tree at
                       seeded synthetic head weights and hidden states (seed
                       11 weights, seed 12 hidden, 4 tokens) with a two-row
                       readout [N, A] -- pins oracle/plain_block.py head()
+  fixture_small/      a two-block + head fixture directory written by the
+                      reference's own array writer (fhe/multiblock/export_fixture.py
+                      _write_array, manifest "arrays" table) from seeded synthetic
+                      weights at D = 16, MLP = 64, T = 3 -- pins the fixture loader
   simd_layout_b32.json + simd_layout_b32.npz
                       fhe/gpu_real_scheme_b/simd_layout.py at batch width 32,
                       one copy (the 32-tokens-per-ciphertext layout): slot map,
@@ -64,6 +68,32 @@ def plain_head():
                         margin=ref["logits"][:, 0] - ref["logits"][:, 1])
 
 
+def fixture_small():
+    import shutil
+    from collections import OrderedDict
+
+    sys.path.insert(0, REF)
+    import fhe.multiblock.export_fixture as ef  # reference: fhe/multiblock/export_fixture.py
+    from pathlib import Path
+    out = Path(HERE) / "fixture_small"
+    shutil.rmtree(out, ignore_errors=True)
+    out.mkdir()
+    arrays = OrderedDict()
+    blocks = [synthetic_weights(60 + b, d=16, mlp=64) for b in range(2)]
+    head = synthetic_head_weights(62, d=16)
+    for b, w in enumerate(blocks):
+        for f in ("ln1", "attn_qkv", "attn_proj", "ln2", "mlp_fc", "mlp_proj"):
+            ef._write_array(out, f"weights.block{b}.{f}", w[f], "synthetic", arrays)
+    ef._write_array(out, "weights.final_ln", head["final_ln"], "synthetic", arrays)
+    ef._write_array(out, "weights.head_linear", head["head_linear"], "synthetic", arrays)
+    ef._write_array(out, "weights.head_ln", head["head_ln"], "synthetic", arrays)
+    ef._write_array(out, "weights.head_readout_margin_n_minus_a", head["readout"], "synthetic", arrays)
+    ef._write_array(out, "input.embeddings", synthetic_input(63, 3, d=16), "synthetic", arrays)
+    with (out / "manifest.json").open("x", encoding="utf-8") as f:
+        json.dump({"schema": "synthetic test fixture", "seeds": {"blocks": [60, 61], "head": 62, "input": 63},
+                   "arrays": arrays}, f, indent=2, allow_nan=False)
+
+
 def layout():
     B, T = 32, 103
     out = {"batch_width": B, "tokens": T, "copies": 1}
@@ -98,5 +128,6 @@ def layout():
 if __name__ == "__main__":
     plain_block()
     plain_head()
+    fixture_small()
     layout()
     print("golden fixtures written")
