@@ -193,6 +193,12 @@ int ckks_rotate_batch(ckks_ctx* ctx, const ckks_ct* const* in, const int* k, int
  * basis Q_l P and divided by P once (one ModDown per 32 rotations, in input
  * order, instead of one per rotation); identity rotations are added as is. */
 int ckks_rotate_sum(ckks_ctx* ctx, const ckks_ct* const* in, const int* k, int count, ckks_ct* out);
+/* out = sum_i EvalMult(a[i], b[i]) with one relinearisation: the tensor
+ * products are summed as degree-2 ciphertexts and d2 is key-switched once
+ * (the context accumulation of T123.cpp:838-860, where every weight tile x
+ * shifted value product is only ever summed).  All products at one level,
+ * scale and noise degree; the result is not rescaled. */
+int ckks_mul_ct_sum(ckks_ctx* ctx, const ckks_ct* const* a, const ckks_ct* const* b, int count, ckks_ct* out);
 int ckks_mul_ct_batch(ckks_ctx* ctx, const ckks_ct* const* a, const ckks_ct* const* b, int count,
                       ckks_ct* const* outs);
 int ckks_rescale_batch(ckks_ctx* ctx, const ckks_ct* const* in, int count, ckks_ct* const* outs);

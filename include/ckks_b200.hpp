@@ -233,6 +233,17 @@ class CryptoContextImpl {
     check(ckks_rotate_batch(h_, in.data(), k.data(), (int)a.size(), hs.data()));
     return outs;
   }
+  // sum_i a[i] * b[i] with one relinearisation (not rescaled)
+  Ciphertext EvalMultSum(const std::vector<Ciphertext>& a, const std::vector<Ciphertext>& b) {
+    Ciphertext out = fresh();
+    std::vector<const ckks_ct*> x, y;
+    for (size_t i = 0; i < a.size(); ++i) {
+      x.push_back(a[i]->handle());
+      y.push_back(b[i]->handle());
+    }
+    check(ckks_mul_ct_sum(h_, x.data(), y.data(), (int)a.size(), out->handle()));
+    return out;
+  }
   // sum_i rot(a[i], k[i]) with one ModDown per 32 rotations
   Ciphertext EvalRotateSum(const std::vector<Ciphertext>& a, const std::vector<int>& k) {
     Ciphertext out = fresh();

@@ -291,6 +291,13 @@ class Oracle:
         self._check(self.L_.oc_rotate_hoisted(self._c(), _p(ct), ct.shape[1], _p(kk), len(kk), _p(out)))
         return out
 
+    def mul_ct_sum(self, a, b):
+        a = np.ascontiguousarray(a, np.uint64)  # n x 2 x limbs x N
+        b = np.ascontiguousarray(b, np.uint64)
+        out = np.zeros(a.shape[1:], np.uint64)
+        self._check(self.L_.oc_mul_ct_sum(self._c(), _p(a), _p(b), a.shape[0], a.shape[2], _p(out)))
+        return out
+
     def rotate_sum(self, cts, ks):
         cts = np.ascontiguousarray(cts, np.uint64)  # n x 2 x limbs x N
         kk = np.ascontiguousarray(ks, np.int32)

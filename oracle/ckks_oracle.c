@@ -1140,6 +1140,27 @@ int oc_mul_ct(const oc_ctx* c, const uint64_t* a, const uint64_t* b, int limbs, 
     return 0;
 }
 
+/* sum_r EvalMult(a_r, b_r) with one relinearisation: the tensor products are
+ * summed as degree-2 ciphertexts and d2 is key-switched once (the context
+ * accumulation of T123.cpp:838-860).  a, b: n x 2 x limbs x N. */
+int oc_mul_ct_sum(const oc_ctx* c, const uint64_t* a, const uint64_t* b, int n, int limbs, uint64_t* out) {
+    const uint64_t* rlk = key_for(c, 1, limbs);
+    if (!rlk) { set_err("relinearisation key not generated"); return -1; }
+    const int N = c->N;
+    const size_t S = (size_t)limbs * N;
+    uint64_t* d = (uint64_t*)calloc(3 * S, sizeof(uint64_t));
+    uint64_t* t = (uint64_t*)malloc(sizeof(uint64_t) * 3 * S);
+    uint64_t* ks = (uint64_t*)malloc(sizeof(uint64_t) * 2 * S);
+    for (int r = 0; r < n; r++) {
+        oc_tensor(c, a + (size_t)r * 2 * S, b + (size_t)r * 2 * S, limbs, t);
+        oc_add(c, d, t, 3, limbs, d);
+    }
+    oc_keyswitch(c, d + 2 * S, limbs, rlk, ks);
+    oc_add(c, d, ks, 2, limbs, out);
+    free(d); free(t); free(ks);
+    return 0;
+}
+
 /* Rescale (FLEXIBLEAUTO, T123.cpp:1608): x -> (x - [x]_{q_last}) / q_last */
 void oc_rescale(const oc_ctx* c, const uint64_t* ct, int limbs, uint64_t* out) {
     const int N = c->N, lo = limbs - 1;

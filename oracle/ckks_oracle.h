@@ -107,6 +107,8 @@ void oc_tensor(const oc_ctx* c, const uint64_t* a, const uint64_t* b, int limbs,
 /* hybrid key switch of d (limbs, NTT form) with key `ksk` (layout as oc_switch_key);
  * out: 2*limbs*N (delta c0, delta c1) */
 void oc_keyswitch(const oc_ctx* c, const uint64_t* d, int limbs, const uint64_t* ksk, uint64_t* out);
+/* sum_r a_r * b_r (n pairs, each 2*limbs*N) with one relinearisation */
+int oc_mul_ct_sum(const oc_ctx* c, const uint64_t* a, const uint64_t* b, int n, int limbs, uint64_t* out);
 /* drop the last limb with division by it; out 2*(limbs-1)*N */
 void oc_rescale(const oc_ctx* c, const uint64_t* ct, int limbs, uint64_t* out);
 /* automorphism X -> X^g in NTT form on npolys polys */

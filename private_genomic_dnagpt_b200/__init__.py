@@ -117,6 +117,7 @@ _SIGS = [
     ("ckks_rotate_batch", ctypes.c_int, [_vp, ctypes.POINTER(_vp), ctypes.POINTER(ctypes.c_int), ctypes.c_int,
                                          ctypes.POINTER(_vp)]),
     ("ckks_rotate_sum", ctypes.c_int, [_vp, ctypes.POINTER(_vp), ctypes.POINTER(ctypes.c_int), ctypes.c_int, _vp]),
+    ("ckks_mul_ct_sum", ctypes.c_int, [_vp, ctypes.POINTER(_vp), ctypes.POINTER(_vp), ctypes.c_int, _vp]),
     ("ckks_mul_ct_batch", ctypes.c_int, [_vp, ctypes.POINTER(_vp), ctypes.POINTER(_vp), ctypes.c_int,
                                          ctypes.POINTER(_vp)]),
     ("ckks_rescale_batch", ctypes.c_int, [_vp, ctypes.POINTER(_vp), ctypes.c_int, ctypes.POINTER(_vp)]),
@@ -553,6 +554,13 @@ class CryptoContext:
         _check(lib().ckks_rotate_batch(self.h, (_vp * n)(*[c.h for c in cts]), (ctypes.c_int * n)(*ks), n,
                                        (_vp * n)(*[o.h for o in outs])))
         return outs
+
+    def EvalMultSum(self, a, b) -> Ciphertext:
+        """sum_i a[i] * b[i] with one relinearisation (not rescaled)."""
+        out = self._new()
+        n = len(a)
+        _check(lib().ckks_mul_ct_sum(self.h, (_vp * n)(*[c.h for c in a]), (_vp * n)(*[c.h for c in b]), n, out.h))
+        return out
 
     def EvalRotateSum(self, cts, ks) -> Ciphertext:
         """sum_i EvalRotate(cts[i], ks[i]) with one ModDown per 32 rotations."""

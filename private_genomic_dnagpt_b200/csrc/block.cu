@@ -97,8 +97,11 @@ __global__ void __launch_bounds__(kThreads) diag_values_kernel(const double* __r
   vals[(size_t)blockIdx.y * slots + s] = diag_value(W, out_dim, in_dim, ld, PW, n1, d / n1, d % n1, s / B);
 }
 
-// token groups that share one pass over a product's diagonals
-constexpr int kMaxGroups = 4;
+// token groups per BSGS launch.  Sharing one pass over a product's diagonals
+// between groups (thread rows) did not pay: the kernel is bound by issue and
+// load latency of its 128-bit multiply-accumulates, not by the diagonal
+// traffic, so one group per launch keeps the most warps resident.
+constexpr int kMaxGroups = 1;
 struct BabyPtrs {
   const uint64_t* c0[kMaxGroups][kMaxBaby];
   const uint64_t* c1[kMaxGroups][kMaxBaby];
@@ -130,47 +133,34 @@ __global__ void __launch_bounds__(kThreads) diag_tile_kernel(const uint64_t* __r
 // one contiguous 64 KiB span of the tile-major diagonal store.
 constexpr int kBsgsThreads = 128;
 
-// inner sums of giant step g for `ng` token groups at once: every diagonal
-// residue is loaded once and multiplied into each group's baby steps
-__global__ void __launch_bounds__(kBsgsThreads) bsgs_inner_kernel(BabyPtrs babies, int ng, int n1,
-                                                                  const uint64_t* __restrict__ diag, InnerPtrs out,
-                                                                  int limbs, int logN, int n2,
-                                                                  const ckks::Mod* __restrict__ mods) {
+// inner sums of giant step g for `ng` token groups in one CTA of
+// kBsgsThreads x ng threads: thread row q computes group q
+__global__ void __launch_bounds__(kBsgsThreads * kMaxGroups) bsgs_inner_kernel(BabyPtrs babies, int ng, int n1,
+                                                                               const uint64_t* __restrict__ diag,
+                                                                               InnerPtrs out, int limbs, int logN,
+                                                                               int n2,
+                                                                               const ckks::Mod* __restrict__ mods) {
   const int N = 1 << logN;
   const int g = blockIdx.x, tile = blockIdx.y, l = blockIdx.z;
+  const int q = threadIdx.y;
+  if (q >= ng) return;
   const int c = 2 * threadIdx.x;  // coefficient within the tile
   const size_t off = (size_t)l * N + (size_t)tile * kThreads + c;
   const int ndiag = n1 * n2;
   const uint64_t* dtile = diag + (((size_t)l * (N / kThreads) + tile) * ndiag + (size_t)g * n1) * kThreads + c;
-  ckks::U128 acc[kMaxGroups][4];
-#pragma unroll
-  for (int q = 0; q < kMaxGroups; ++q)
-#pragma unroll
-    for (int k = 0; k < 4; ++k) acc[q][k] = ckks::U128{0, 0};
+  ckks::U128 a00{0, 0}, a01{0, 0}, a10{0, 0}, a11{0, 0};
   for (int j = 0; j < n1; ++j) {
+    const ulonglong2 b0 = *reinterpret_cast<const ulonglong2*>(babies.c0[q][j] + off);
+    const ulonglong2 b1 = *reinterpret_cast<const ulonglong2*>(babies.c1[q][j] + off);
     const ulonglong2 dv = __ldg(reinterpret_cast<const ulonglong2*>(dtile + (size_t)j * kThreads));
-#pragma unroll
-    for (int q = 0; q < kMaxGroups; ++q) {
-      if (q < ng) {
-        const ulonglong2 b0 = *reinterpret_cast<const ulonglong2*>(babies.c0[q][j] + off);
-        const ulonglong2 b1 = *reinterpret_cast<const ulonglong2*>(babies.c1[q][j] + off);
-        ckks::mac_wide(acc[q][0], dv.x, b0.x);
-        ckks::mac_wide(acc[q][1], dv.y, b0.y);
-        ckks::mac_wide(acc[q][2], dv.x, b1.x);
-        ckks::mac_wide(acc[q][3], dv.y, b1.y);
-      }
-    }
+    ckks::mac_wide(a00, dv.x, b0.x);
+    ckks::mac_wide(a01, dv.y, b0.y);
+    ckks::mac_wide(a10, dv.x, b1.x);
+    ckks::mac_wide(a11, dv.y, b1.y);
   }
   const ckks::Mod m = mods[l];
-#pragma unroll
-  for (int q = 0; q < kMaxGroups; ++q) {
-    if (q < ng) {
-      *reinterpret_cast<ulonglong2*>(out.c0[q][g] + off) =
-          make_ulonglong2(ckks::reduce128(acc[q][0], m), ckks::reduce128(acc[q][1], m));
-      *reinterpret_cast<ulonglong2*>(out.c1[q][g] + off) =
-          make_ulonglong2(ckks::reduce128(acc[q][2], m), ckks::reduce128(acc[q][3], m));
-    }
-  }
+  *reinterpret_cast<ulonglong2*>(out.c0[q][g] + off) = make_ulonglong2(ckks::reduce128(a00, m), ckks::reduce128(a01, m));
+  *reinterpret_cast<ulonglong2*>(out.c1[q][g] + off) = make_ulonglong2(ckks::reduce128(a10, m), ckks::reduce128(a11, m));
 }
 
 // ---- client-side float64 transforms, on the device ------------------------
@@ -646,9 +636,8 @@ struct ckks_block {
   }
 
   // x_q W^T for weight `id` and every token group q from their baby-step
-  // rotations (T123.cpp:1264-1295): the inner sums of up to 4 groups share
-  // one pass over the diagonals; the giant steps of each group are one
-  // rotation sum (one ModDown)
+  // rotations (T123.cpp:1264-1295): fused diagonal x baby-step inner sums,
+  // then the giant steps of each group as one rotation sum (one ModDown)
   std::vector<Ciphertext> bsgs_groups(const std::vector<std::vector<Ciphertext>>& babies, int id) {
     const int G = (int)babies.size();
     std::vector<Ciphertext> outs(G);
@@ -689,8 +678,8 @@ struct ckks_block {
             C, "bsgs_inner",
             ((double)s.n1 * s.n2 * limbs + ng * (2.0 * s.n1 * limbs + 2.0 * s.n2 * limbs)) * C.limb_bytes(), C.stream);
         const dim3 grid(s.n2, C.N / blk::kThreads, limbs);
-        blk::bsgs_inner_kernel<<<grid, blk::kBsgsThreads, 0, C.stream>>>(bp, ng, s.n1, dg.data, ip, limbs, C.logN,
-                                                                         s.n2, C.d_mods);
+        blk::bsgs_inner_kernel<<<grid, dim3(blk::kBsgsThreads, ng), 0, C.stream>>>(bp, ng, s.n1, dg.data, ip, limbs,
+                                                                                   C.logN, s.n2, C.d_mods);
       }
       CKKS_CUDA(cudaGetLastError());
       // giant steps: sum_g rot(inner_g, B n1 g), the key switches summed in the
@@ -886,11 +875,14 @@ void ckks_block::shard_softmax(const double* d_scores) {
 }
 
 // context of the given tiles: client weight tiles x shifted values, summed
-// into per-query-group partial contexts (T123.cpp:838-860)
+// into per-query-group partial contexts (T123.cpp:838-860).  The products of
+// a query group are only ever summed, so they are added as degree-2
+// ciphertexts and relinearised once (EvalMultSum), then rescaled.
 void ckks_block::shard_context(const std::vector<std::pair<int, int>>& pairs) {
   const int T = s.T, H = s.H, HD = s.HD, D = s.D, B = s.B, SL = slots();
   const int nb = (SL + blk::kThreads - 1) / blk::kThreads;
   if (!st_prob) throw ckks::Error(CKKS_ESTATE, "softmax not evaluated");
+  std::vector<std::vector<Ciphertext>> lhs(s.groups), rhs(s.groups);  // per query group
   for (int kg = 0; kg < s.groups; ++kg) {
     const auto tags = tags_of(kg, pairs);
     if (tags.empty()) continue;
@@ -912,16 +904,16 @@ void ckks_block::shard_context(const std::vector<std::pair<int, int>>& pairs) {
     C.release(dv);
     count["weight_tile_encryptions"] += M;
     count["client_round_trips"] += M;
-    std::vector<Ciphertext> vb;
-    for (const auto& tg : tags) vb.push_back(vs[tg.d]);
-    const auto prods = mul_ct_rs_batch(wa, vb);
-    for (int qg = kg; qg < s.groups; ++qg) {
-      std::vector<Ciphertext> terms;
-      if (st_ctx[qg]) terms.push_back(st_ctx[qg]);
-      for (int i = 0; i < M; ++i)
-        if (tags[i].qg == qg) terms.push_back(prods[i]);
-      if (!terms.empty()) st_ctx[qg] = terms.size() == 1 ? terms[0] : cc.EvalAddMany(terms);
+    for (int i = 0; i < M; ++i) {
+      lhs[tags[i].qg].push_back(wa[i]);
+      rhs[tags[i].qg].push_back(vs[tags[i].d]);
     }
+  }
+  for (int qg = 0; qg < s.groups; ++qg) {
+    if (lhs[qg].empty()) continue;
+    count["ct_ct"] += (long)lhs[qg].size();
+    const Ciphertext part = rs(cc.EvalMultSum(lhs[qg], rhs[qg]));
+    st_ctx[qg] = st_ctx[qg] ? add(st_ctx[qg], part) : part;
   }
   stamp("context");
 }

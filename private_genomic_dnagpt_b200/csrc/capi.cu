@@ -299,6 +299,49 @@ void mul_ct_batch(Context& c, const ckks_ct* const* a, const ckks_ct* const* bb,
   }
 }
 
+// sum_r a[r] * b[r] with one relinearisation: the tensor products are
+// summed as degree-2 ciphertexts (31 pairs per launch), then d2 is switched
+// once
+void mul_ct_sum(Context& c, const ckks_ct* const* a, const ckks_ct* const* bb, int n, DevPoly& res) {
+  const int limbs = a[0]->p.limbs, N = c.N;
+  if (!c.switch_key(1u, limbs)) throw Error(CKKS_EKEY, "relinearisation key not generated");
+  const size_t S = (size_t)limbs * N;
+  const double sc = a[0]->p.scale * bb[0]->p.scale;
+  const int deg = a[0]->p.deg + bb[0]->p.deg;
+  for (int r = 0; r < n; ++r) {
+    if (a[r]->p.limbs != limbs || bb[r]->p.limbs != limbs) throw Error(CKKS_ELEVEL, "operands at different levels");
+    if (a[r]->p.deg + bb[r]->p.deg != deg) throw Error(CKKS_ESCALE, "products of different noise degree");
+    check_scales(sc, a[r]->p.scale * bb[r]->p.scale);
+  }
+  uint64_t* d = (uint64_t*)c.alloc(sizeof(uint64_t) * 3 * S);
+  for (int r0 = 0; r0 < n; r0 += ckks::kTensorSum) {
+    const int k = std::min(ckks::kTensorSum, n - r0);
+    ckks::TensorPtrs tp{};
+    for (int i = 0; i < k; ++i) {
+      tp.a0[i] = a[r0 + i]->p.poly(0);
+      tp.a1[i] = a[r0 + i]->p.poly(1);
+      tp.b0[i] = bb[r0 + i]->p.poly(0);
+      tp.b1[i] = bb[r0 + i]->p.poly(1);
+    }
+    ckks::tensor_sum(c, tp, k, r0 > 0, d, d + S, d + 2 * S, limbs, c.stream);
+  }
+  res.ensure(&c, 2, limbs);
+  ckks::KsBatch b{};
+  b.M = 1;
+  b.d[0] = d + 2 * S;
+  b.key[0] = c.switch_key(1u, limbs);
+  b.g[0] = 1u;
+  b.add0[0] = d;
+  b.add1[0] = d + S;
+  b.out0[0] = res.poly(0);
+  b.out1[0] = res.poly(1);
+  ckks::keyswitch_batch(c, limbs, b, false, c.stream);
+  c.release(d);
+  res.limbs = limbs;
+  res.scale = sc;
+  res.deg = deg;
+}
+
 void rescale_many(Context& c, const ckks_ct* const* in, int n, ckks_ct* const* outs) {
   if (n <= 0) return;
   const int limbs = in[0]->p.limbs;
@@ -1002,6 +1045,21 @@ int ckks_rotate_batch(ckks_ctx* ctx, const ckks_ct* const* in, const int* k, int
       need(outs[i] && outs[i]->owner == ctx, CKKS_EARG, "bad output handle");
     }
     rotate_batch(c, in, k, count, outs);
+  });
+}
+
+int ckks_mul_ct_sum(ckks_ctx* ctx, const ckks_ct* const* a, const ckks_ct* const* b, int count, ckks_ct* out) {
+  return guard([&] {
+    Context& c = C(ctx);
+    need(count >= 1 && a && b, CKKS_EARG, "empty product sum");
+    need(out && out->owner == ctx, CKKS_EARG, "bad output handle");
+    for (int i = 0; i < count; ++i) {
+      same_ctx(ctx, a[i]);
+      same_ctx(ctx, b[i]);
+    }
+    DevPoly tmp;
+    mul_ct_sum(c, a, b, count, tmp);
+    take(out->p, tmp);
   });
 }
 

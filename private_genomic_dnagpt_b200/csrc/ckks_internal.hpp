@@ -287,6 +287,17 @@ void add_many(const Context& c, const SumPtrs& p, int k, int limbs, cudaStream_t
 void add_pairs(const Context& c, const PairPtrs& p, int M, int limbs, cudaStream_t st);
 void tensor(const Context& c, const uint64_t* a0, const uint64_t* a1, const uint64_t* b0, const uint64_t* b1,
             uint64_t* d0, uint64_t* d1, uint64_t* d2, int limbs, cudaStream_t st);
+// sum_i a_i (x) b_i of n <= kTensorSum ciphertext pairs (degree-2 result)
+constexpr int kTensorSum = 31;
+struct TensorPtrs {
+  const uint64_t* a0[kTensorSum];
+  const uint64_t* a1[kTensorSum];
+  const uint64_t* b0[kTensorSum];
+  const uint64_t* b1[kTensorSum];
+};
+// accumulate: add onto the sums already in d0, d1, d2
+void tensor_sum(const Context& c, const TensorPtrs& p, int n, bool accumulate, uint64_t* d0, uint64_t* d1,
+                uint64_t* d2, int limbs, cudaStream_t st);
 
 // key switching
 void modup(const Context& c, const uint64_t* d_ntt, int limbs, uint64_t* ext, cudaStream_t st);

@@ -109,6 +109,33 @@ __global__ void __launch_bounds__(kEwThreads) tensor_kernel(const uint64_t* __re
   d2[off] = mul_mod(x1, y1, m);
 }
 
+// sum_i a_i (x) b_i over up to kTensorSum pairs: d0 = sum a0 b0, d1 = sum
+// (a0 b1 + a1 b0), d2 = sum a1 b1, 128-bit accumulation (at most 62 products
+// of residues below 2^61 per accumulator)
+__global__ void __launch_bounds__(kEwThreads) tensor_sum_kernel(TensorPtrs p, int n, bool accumulate,
+                                                                uint64_t* __restrict__ d0, uint64_t* __restrict__ d1,
+                                                                uint64_t* __restrict__ d2, int logN,
+                                                                const Mod* __restrict__ mods) {
+  const int N = 1 << logN;
+  const int limb = blockIdx.y;
+  const Mod m = mods[limb];
+  const size_t i = (size_t)blockIdx.x * kEwThreads + threadIdx.x;
+  if (i >= (size_t)N) return;
+  const size_t off = (size_t)limb * N + i;
+  // accumulate: continue the sums already in d0, d1, d2 (residues)
+  U128 s0{accumulate ? d0[off] : 0, 0}, s1{accumulate ? d1[off] : 0, 0}, s2{accumulate ? d2[off] : 0, 0};
+  for (int k = 0; k < n; ++k) {
+    const uint64_t x0 = p.a0[k][off], x1 = p.a1[k][off], y0 = p.b0[k][off], y1 = p.b1[k][off];
+    mac_wide(s0, x0, y0);
+    mac_wide(s1, x0, y1);
+    mac_wide(s1, x1, y0);
+    mac_wide(s2, x1, y1);
+  }
+  d0[off] = reduce128(s0, m);
+  d1[off] = reduce128(s1, m);
+  d2[off] = reduce128(s2, m);
+}
+
 // out[k] = in[auto_index(k)]: each warp reads one aligned 32-residue span
 __global__ void __launch_bounds__(kEwThreads) automorphism_kernel(const uint64_t* __restrict__ a,
                                                                   uint64_t* __restrict__ o, uint32_t g, int logN) {
@@ -214,6 +241,15 @@ void tensor(const Context& c, const uint64_t* a0, const uint64_t* a1, const uint
   const dim3 grid((c.N + kEwThreads - 1) / kEwThreads, limbs);
   ProfScope ps(c, "tensor", 7.0 * limbs * c.limb_bytes(), st);
   tensor_kernel<<<grid, kEwThreads, 0, st>>>(a0, a1, b0, b1, d0, d1, d2, c.logN, c.d_mods);
+  CKKS_CUDA(cudaGetLastError());
+}
+
+void tensor_sum(const Context& c, const TensorPtrs& p, int n, bool accumulate, uint64_t* d0, uint64_t* d1,
+                uint64_t* d2, int limbs, cudaStream_t st) {
+  if (n < 1 || n > kTensorSum) throw Error(kErrArgument, "tensor sum of 1..31 pairs");
+  const dim3 grid((c.N + kEwThreads - 1) / kEwThreads, limbs);
+  ProfScope ps(c, "tensor_sum", (4.0 * n + 3.0) * limbs * c.limb_bytes(), st);
+  tensor_sum_kernel<<<grid, kEwThreads, 0, st>>>(p, n, accumulate, d0, d1, d2, c.logN, c.d_mods);
   CKKS_CUDA(cudaGetLastError());
 }
 

@@ -215,6 +215,18 @@ def test_rotate_sum_bit_exact(pair10, ks):
     assert np.abs(dec - sum(np.roll(f[0], -k) for f, k in zip(fr, ks))).max() < 1e-7
 
 
+@pytest.mark.parametrize("n,limbs", [(3, 6), (3, 2), (40, 4)])
+def test_mul_ct_sum_bit_exact(pair10, n, limbs):
+    """Products summed as degree-2 ciphertexts, one relinearisation (40
+    pairs span two tensor-sum launches)."""
+    o, cc = pair10
+    fa = [_fresh(o, cc, 300 + i, limbs) for i in range(n)]
+    fb = [_fresh(o, cc, 400 + i, limbs) for i in range(n)]
+    got = cc.EvalMultSum([f[2] for f in fa], [f[2] for f in fb])
+    ref = o.mul_ct_sum(np.stack([f[1] for f in fa]), np.stack([f[1] for f in fb]))
+    assert np.array_equal(got.limbs_array(), ref)
+
+
 @pytest.mark.parametrize("count,stride", [(64, 4), (16, 32)])
 def test_accumulate_sum_bit_exact(pair10, count, stride):
     o, cc = pair10
@@ -406,6 +418,8 @@ def test_key_switches_across_the_reduced_set_boundary(pair_wide, limbs):
     assert np.array_equal(cc.mul_ct(cx, cy).limbs_array(), o.mul_ct(rx, ry))
     got = cc.EvalRotateSum([cx, cy, cx], [0, 3, 5])
     assert np.array_equal(got.limbs_array(), o.rotate_sum(np.stack([rx, ry, rx]), [0, 3, 5]))
+    got = cc.EvalMultSum([cx, cy], [cy, cx])
+    assert np.array_equal(got.limbs_array(), o.mul_ct_sum(np.stack([rx, ry]), np.stack([ry, rx])))
     rb = cc.rotate_batch([cx, cy], [5, -7])
     assert np.array_equal(rb[0].limbs_array(), o.rotate(rx, 5))
     assert np.array_equal(rb[1].limbs_array(), o.rotate(ry, -7))

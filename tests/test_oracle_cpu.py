@@ -195,6 +195,16 @@ def test_rotate_sum_decrypts_to_the_sum_of_rotations(small):
     assert np.abs(got - sep).max() < 1e-9
 
 
+def test_mul_ct_sum_decrypts_to_the_sum_of_products(small):
+    o = small
+    rng = np.random.default_rng(43)
+    xs = [rng.uniform(-1, 1, o.N // 2) for _ in range(6)]
+    S = o.scale(4)
+    cts = np.stack([o.encrypt(o.encode(x, 4), 80 + i) for i, x in enumerate(xs)])
+    got = o.decode(o.decrypt(o.mul_ct_sum(cts[:3], cts[3:])), S * S)
+    assert np.abs(got - sum(xs[i] * xs[3 + i] for i in range(3))).max() < 1e-9
+
+
 @pytest.mark.parametrize("count,stride", ACC_CASES)
 def test_accumulate_sum(small, count, stride):
     o = small
