@@ -260,6 +260,11 @@ int ckks_block_shard_qkv(ckks_block* b, const int* groups, int n);
 int ckks_block_shard_scores(ckks_block* b, const int* pairs, int n, double* d_scores);
 int ckks_block_shard_softmax(ckks_block* b, const double* d_scores);
 int ckks_block_shard_context(ckks_block* b, const int* pairs, int n);
+/* the same two stages over explicit causal alignments (query group, key
+ * group, lane shift d) as 3n ints: the finer units that balance many ranks
+ * (each alignment is one score tile and one weight tile, T123.cpp:798-860) */
+int ckks_block_shard_scores_tiles(ckks_block* b, const int* tiles, int n, double* d_scores);
+int ckks_block_shard_context_tiles(ckks_block* b, const int* tiles, int n);
 /* writes the rows of the given groups into y [tokens, d_model] (host) */
 int ckks_block_shard_output(ckks_block* b, const int* groups, int n, double* y);
 /* state ciphertexts by kind (0 Q, 1 K, 2 V, 3 partial context, 4 encrypted

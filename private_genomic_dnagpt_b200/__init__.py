@@ -138,6 +138,8 @@ _SIGS = [
     ("ckks_block_shard_scores", ctypes.c_int, [_vp, ctypes.POINTER(ctypes.c_int), ctypes.c_int, _vp]),
     ("ckks_block_shard_softmax", ctypes.c_int, [_vp, _vp]),
     ("ckks_block_shard_context", ctypes.c_int, [_vp, ctypes.POINTER(ctypes.c_int), ctypes.c_int]),
+    ("ckks_block_shard_scores_tiles", ctypes.c_int, [_vp, ctypes.POINTER(ctypes.c_int), ctypes.c_int, _vp]),
+    ("ckks_block_shard_context_tiles", ctypes.c_int, [_vp, ctypes.POINTER(ctypes.c_int), ctypes.c_int]),
     ("ckks_block_shard_output", ctypes.c_int, [_vp, ctypes.POINTER(ctypes.c_int), ctypes.c_int, _f64p]),
     ("ckks_block_state_get", ctypes.c_int, [_vp, ctypes.c_int, ctypes.c_int, _vp]),
     ("ckks_block_state_set", ctypes.c_int, [_vp, ctypes.c_int, ctypes.c_int, _vp]),
@@ -666,6 +668,15 @@ class EncryptedBlock:
     def shard_context(self, pairs):
         p, n = self._pairs(pairs)
         _check(lib().ckks_block_shard_context(self.h, p, n))
+
+    def shard_scores_tiles(self, tiles, d_scores_ptr: int):
+        """Scores of explicit alignments (qg, kg, d)."""
+        p, n = self._pairs(tiles)
+        _check(lib().ckks_block_shard_scores_tiles(self.h, p, n, ctypes.c_void_p(d_scores_ptr)))
+
+    def shard_context_tiles(self, tiles):
+        p, n = self._pairs(tiles)
+        _check(lib().ckks_block_shard_context_tiles(self.h, p, n))
 
     def shard_output(self, groups, y: np.ndarray):
         assert y.dtype == np.float64 and y.flags["C_CONTIGUOUS"]

@@ -706,12 +706,14 @@ struct ckks_block {
     seconds[k] += n - t_stage;
     t_stage = n;
   }
-  std::vector<blk::TileTag> tags_of(int kg, const std::vector<std::pair<int, int>>& pairs) const;
+  // every causal alignment (qg, kg, d) of the given (qg, kg) tiles
+  std::vector<blk::TileTag> alignments(const std::vector<std::pair<int, int>>& pairs) const;
+  static std::vector<blk::TileTag> tags_of(int kg, const std::vector<blk::TileTag>& tiles);
   void shard_inputs(const double* x, int T);
   void shard_qkv(const std::vector<int>& groups);
-  void shard_scores(const std::vector<std::pair<int, int>>& pairs, double* d_scores);
+  void shard_scores(const std::vector<blk::TileTag>& tiles, double* d_scores);
   void shard_softmax(const double* d_scores);
-  void shard_context(const std::vector<std::pair<int, int>>& pairs);
+  void shard_context(const std::vector<blk::TileTag>& tiles);
   void shard_output(const std::vector<int>& groups, double* y);
   void forward(const double* x, int T, double* y);
   double head_forward(const double* x_last);
@@ -750,11 +752,17 @@ std::vector<int> ckks_block::rotation_indices() const {
 // partial-context ciphertexts and the score matrix exchanged between the
 // stages, they shard one block over several devices.
 
-std::vector<blk::TileTag> ckks_block::tags_of(int kg, const std::vector<std::pair<int, int>>& pairs) const {
+std::vector<blk::TileTag> ckks_block::alignments(const std::vector<std::pair<int, int>>& pairs) const {
   std::vector<blk::TileTag> t;
   for (const auto& pr : pairs)
-    if (pr.second == kg)
-      for (int d : blk::active_shifts(s.T, s.B, pr.first, kg)) t.push_back({pr.first, kg, d});
+    for (int d : blk::active_shifts(s.T, s.B, pr.first, pr.second)) t.push_back({pr.first, pr.second, d});
+  return t;
+}
+
+std::vector<blk::TileTag> ckks_block::tags_of(int kg, const std::vector<blk::TileTag>& tiles) {
+  std::vector<blk::TileTag> t;
+  for (const auto& tg : tiles)
+    if (tg.kg == kg) t.push_back(tg);
   return t;
 }
 
@@ -814,14 +822,14 @@ void ckks_block::shard_qkv(const std::vector<int>& groups) {
 // scores of the given (query group, key group) tiles written into d_scores
 // ([q][head][k] doubles on the device): server products and head-window sums,
 // the client decrypts and gathers them on the device
-void ckks_block::shard_scores(const std::vector<std::pair<int, int>>& pairs, double* d_scores) {
+void ckks_block::shard_scores(const std::vector<blk::TileTag>& tiles, double* d_scores) {
   const int T = s.T, H = s.H, HD = s.HD, B = s.B, SL = slots();
   const double inv_sqrt_hd = 1.0 / std::sqrt((double)HD);
   // queries brought to the score level once per query group (a FLEXIBLEAUTO
   // level reduction is a scaled multiply and a rescale)
   std::map<int, Ciphertext> qr;
   for (int kg = 0; kg < s.groups; ++kg) {
-    const auto tags = tags_of(kg, pairs);
+    const auto tags = tags_of(kg, tiles);
     if (tags.empty()) continue;
     if (!st_k[kg]) throw ckks::Error(CKKS_ESTATE, "key group not evaluated");
     std::vector<int> need;
@@ -878,13 +886,13 @@ void ckks_block::shard_softmax(const double* d_scores) {
 // into per-query-group partial contexts (T123.cpp:838-860).  The products of
 // a query group are only ever summed, so they are added as degree-2
 // ciphertexts and relinearised once (EvalMultSum), then rescaled.
-void ckks_block::shard_context(const std::vector<std::pair<int, int>>& pairs) {
+void ckks_block::shard_context(const std::vector<blk::TileTag>& tiles) {
   const int T = s.T, H = s.H, HD = s.HD, D = s.D, B = s.B, SL = slots();
   const int nb = (SL + blk::kThreads - 1) / blk::kThreads;
   if (!st_prob) throw ckks::Error(CKKS_ESTATE, "softmax not evaluated");
   std::vector<std::vector<Ciphertext>> lhs(s.groups), rhs(s.groups);  // per query group
   for (int kg = 0; kg < s.groups; ++kg) {
-    const auto tags = tags_of(kg, pairs);
+    const auto tags = tags_of(kg, tiles);
     if (tags.empty()) continue;
     if (!st_v[kg]) throw ckks::Error(CKKS_ESTATE, "value group not evaluated");
     std::vector<int> need;
@@ -1011,12 +1019,13 @@ void ckks_block::forward(const double* x, int T, double* y) {
   for (int kg = 0; kg < s.groups; ++kg)
     for (int qg = kg; qg < s.groups; ++qg) pairs.push_back({qg, kg});
   shard_qkv(groups);
+  const auto tiles = alignments(pairs);
   double* d_scores = dbuf((size_t)T * s.H * T);
   CKKS_CUDA(cudaMemsetAsync(d_scores, 0xFF, sizeof(double) * T * s.H * T, C.stream));  // NaN = missing
-  shard_scores(pairs, d_scores);
+  shard_scores(tiles, d_scores);
   shard_softmax(d_scores);
   C.release(d_scores);
-  shard_context(pairs);
+  shard_context(tiles);
   shard_output(groups, y);
 }
 
@@ -1247,6 +1256,21 @@ std::vector<std::pair<int, int>> pair_list(const ckks_block* b, const int* pairs
   }
   return v;
 }
+// (qg, kg, d) alignment triples; each must be a causal alignment of its tile
+std::vector<blk::TileTag> tile_list(const ckks_block* b, const int* t, int n) {
+  if (n < 0 || (n && !t)) throw ckks::Error(CKKS_EARG, "bad alignment list");
+  std::vector<blk::TileTag> v;
+  for (int i = 0; i < n; ++i) {
+    const int qg = t[3 * i], kg = t[3 * i + 1], d = t[3 * i + 2];
+    if (kg < 0 || qg < kg || qg >= b->s.groups) throw ckks::Error(CKKS_EARG, "tile (qg, kg) out of range");
+    const auto act = blk::active_shifts(b->s.T, b->s.B, qg, kg);
+    if (std::find(act.begin(), act.end(), d) == act.end())
+      throw ckks::Error(CKKS_EARG, "lane shift is not an alignment of the tile");
+    v.push_back({qg, kg, d});
+  }
+  return v;
+}
+
 ckks_block* live(ckks_block* b) {
   if (!b) throw ckks::Error(CKKS_EARG, "null block");
   if (b->orphaned) throw ckks::Error(CKKS_ESTATE, "the block's context was destroyed");
@@ -1269,7 +1293,14 @@ int ckks_block_shard_qkv(ckks_block* b, const int* groups, int n) {
 int ckks_block_shard_scores(ckks_block* b, const int* pairs, int n, double* d_scores) {
   return bguard([&] {
     if (!d_scores) throw ckks::Error(CKKS_EARG, "null score buffer");
-    live(b)->shard_scores(pair_list(b, pairs, n), d_scores);
+    live(b)->shard_scores(b->alignments(pair_list(b, pairs, n)), d_scores);
+  });
+}
+
+int ckks_block_shard_scores_tiles(ckks_block* b, const int* tiles, int n, double* d_scores) {
+  return bguard([&] {
+    if (!d_scores) throw ckks::Error(CKKS_EARG, "null score buffer");
+    live(b)->shard_scores(tile_list(b, tiles, n), d_scores);
   });
 }
 
@@ -1281,7 +1312,11 @@ int ckks_block_shard_softmax(ckks_block* b, const double* d_scores) {
 }
 
 int ckks_block_shard_context(ckks_block* b, const int* pairs, int n) {
-  return bguard([&] { live(b)->shard_context(pair_list(b, pairs, n)); });
+  return bguard([&] { live(b)->shard_context(b->alignments(pair_list(b, pairs, n))); });
+}
+
+int ckks_block_shard_context_tiles(ckks_block* b, const int* tiles, int n) {
+  return bguard([&] { live(b)->shard_context(tile_list(b, tiles, n)); });
 }
 
 int ckks_block_shard_output(ckks_block* b, const int* groups, int n, double* y) {

@@ -4,8 +4,9 @@ The reference evaluates a block on one GPU and models multi-GPU splits as
 independent, exactly merged units (fhe/gpu_real_scheme_b/shard_layout.py:
 Q/K/V per group, MLP partial sums merged by EvalAdd).  Here one block is
 split into its independent units -- token groups (LN1 + QKV, and O + LN2 +
-MLP, T123.cpp:780-790, 862-927) and (query group, key group) tiles (scores
-and context, T123.cpp:798-860) -- with one process per GPU, identical keys
+MLP, T123.cpp:780-790, 862-927) and the causal alignments (query group, key
+group, lane shift) of the score and context tiles (T123.cpp:798-860) -- with
+one process per GPU, identical keys
 on every rank (same seed) and these exchanges between the stages:
 
   after QKV      each group's Q, K, V ciphertexts, broadcast by the rank that
@@ -44,28 +45,36 @@ def active_shifts(tokens: int, batch: int, qg: int, kg: int) -> list[int]:
 @dataclass
 class RankPlan:
     groups: list[int] = field(default_factory=list)
-    pairs: list[tuple[int, int]] = field(default_factory=list)
-    tiles: int = 0
+    # causal alignments (query group, key group, lane shift) of this rank
+    tiles: list[tuple[int, int, int]] = field(default_factory=list)
+    # alignments per key-group unit assigned (the load balanced)
+    load: int = 0
 
 
 def shard_plan(tokens: int, batch: int, world: int) -> list[RankPlan]:
-    """Units of one block for each rank: token groups round-robin, tiles by
-    longest-processing-time-first over their alignment counts (ties to the
-    lowest rank), so every unit is evaluated exactly once."""
+    """Units of one block for each rank.  Token groups go round-robin.  The
+    attention work is split into (key group, lane shift d) units -- every
+    query group's alignment with that shift, which share one lane shift of
+    the key and value ciphertexts -- assigned longest-processing-time-first by
+    their alignment counts (ties to the lowest rank), so every alignment is
+    evaluated exactly once and every lane shift on one rank only."""
     if world < 1:
         raise ValueError("world size must be positive")
     groups = -(-tokens // batch)
     plan = [RankPlan() for _ in range(world)]
     for g in range(groups):
         plan[g % world].groups.append(g)
-    pairs = [(qg, kg) for kg in range(groups) for qg in range(kg, groups)]
-    weight = {p: len(active_shifts(tokens, batch, *p)) for p in pairs}
-    for p in sorted(pairs, key=lambda p: (-weight[p], p)):
-        r = min(range(world), key=lambda i: (plan[i].tiles, i))
-        plan[r].pairs.append(p)
-        plan[r].tiles += weight[p]
+    units: dict[tuple[int, int], list[tuple[int, int, int]]] = {}
+    for kg in range(groups):
+        for qg in range(kg, groups):
+            for d in active_shifts(tokens, batch, qg, kg):
+                units.setdefault((kg, d), []).append((qg, kg, d))
+    for u in sorted(units, key=lambda u: (-len(units[u]), u)):
+        r = min(range(world), key=lambda i: (plan[i].load, i))
+        plan[r].tiles.extend(units[u])
+        plan[r].load += len(units[u])
     for rp in plan:
-        rp.pairs.sort(key=lambda p: (p[1], p[0]))
+        rp.tiles.sort(key=lambda t: (t[1], t[0], t[2]))
     return plan
 
 
@@ -146,10 +155,10 @@ class ShardedBlock:
             for kind in (KIND_Q, KIND_K, KIND_V):
                 self._broadcast_state(kind, g, src)
         scores = torch.zeros(self.tokens * self.heads * self.tokens, dtype=torch.float64, device=self.device)
-        io.scores(mine.pairs, scores)
+        io.scores(mine.tiles, scores)
         dist.all_reduce(scores)
         io.softmax(scores)
-        io.context(mine.pairs)
+        io.context(mine.tiles)
         for qg in range(self.groups):
             self._merge_contexts(qg, group_owner(self.plan, qg))
         y = np.zeros((self.tokens, self.d_model), np.float64)
@@ -178,14 +187,14 @@ class EngineIO:
     def qkv(self, groups):
         self.b.shard_qkv(groups)
 
-    def scores(self, pairs, t):
-        self.b.shard_scores(pairs, t.data_ptr())
+    def scores(self, tiles, t):
+        self.b.shard_scores_tiles(tiles, t.data_ptr())
 
     def softmax(self, t):
         self.b.shard_softmax(t.data_ptr())
 
-    def context(self, pairs):
-        self.b.shard_context(pairs)
+    def context(self, tiles):
+        self.b.shard_context_tiles(tiles)
 
     def output(self, groups, y):
         self.b.shard_output(groups, y)

@@ -29,25 +29,31 @@ B = 32
 def test_plan_covers_every_unit_once():
     for tokens in (1, 31, 40, 103, 256):
         groups = -(-tokens // B)
-        pairs = {(qg, kg) for kg in range(groups) for qg in range(kg, groups)}
+        want = {(qg, kg, d) for kg in range(groups) for qg in range(kg, groups)
+                for d in shard.active_shifts(tokens, B, qg, kg)}
         for world in range(1, 9):
             plan = shard.shard_plan(tokens, B, world)
             assert len(plan) == world
             gs = [g for rp in plan for g in rp.groups]
             assert sorted(gs) == list(range(groups))
-            ps = [p for rp in plan for p in rp.pairs]
-            assert len(ps) == len(pairs) and set(ps) == pairs
-            w = {p: len(shard.active_shifts(tokens, B, *p)) for p in pairs}
-            loads = [sum(w[p] for p in rp.pairs) for rp in plan]
-            assert max(loads) - min(loads) <= max(w.values())
-            assert [rp.tiles for rp in plan] == loads
+            ts = [t for rp in plan for t in rp.tiles]
+            assert len(ts) == len(want) and set(ts) == want
+            # a lane shift of a key group lives on one rank only
+            owner = {}
+            for r, rp in enumerate(plan):
+                for qg, kg, d in rp.tiles:
+                    assert owner.setdefault((kg, d), r) == r
+            loads = [len(rp.tiles) for rp in plan]
+            assert loads == [rp.load for rp in plan]
+            assert max(loads) - min(loads) <= groups
 
 
 def test_plan_for_the_benchmark_shape():
-    plan = shard.shard_plan(103, B, 4)
-    assert [rp.groups for rp in plan] == [[0], [1], [2], [3]]
-    total = sum(rp.tiles for rp in plan)
-    assert total == sum(len(shard.active_shifts(103, B, qg, kg)) for kg in range(4) for qg in range(kg, 4))
+    plan = shard.shard_plan(103, B, 8)
+    assert [rp.groups for rp in plan] == [[0], [1], [2], [3], [], [], [], []]
+    total = sum(len(shard.active_shifts(103, B, qg, kg)) for kg in range(4) for qg in range(kg, 4))
+    assert sum(rp.load for rp in plan) == total == 295
+    assert max(rp.load for rp in plan) - min(rp.load for rp in plan) <= 4
 
 
 class PlainIO:
@@ -77,16 +83,22 @@ class PlainIO:
             for kind in range(3):
                 self.state[(kind, g)] = qkv[:, kind * D:(kind + 1) * D].copy()
 
-    def scores(self, pairs, t):
+    def _entries(self, qg, kg, d):
+        """(query row in group, key row in group) of alignment (qg, kg, d):
+        query lane ql meets key lane (ql + d) mod B, kept when causal."""
+        for ql in range(B):
+            kl = (ql + d) % B
+            tq, tk = qg * B + ql, kg * B + kl
+            if tq < self.T and tk < self.T and tk <= tq:
+                yield ql, kl, tq, tk
+
+    def scores(self, tiles, t):
         s = t.view(self.T, self.H, self.T)
-        for qg, kg in pairs:
+        for qg, kg, d in tiles:
             q = self.state[(0, qg)].reshape(-1, self.H, self.hd)
             k = self.state[(1, kg)].reshape(-1, self.H, self.hd)
-            for i in range(q.shape[0]):
-                for j in range(k.shape[0]):
-                    tq, tk = qg * B + i, kg * B + j
-                    if tk <= tq:
-                        s[tq, :, tk] = torch.from_numpy((q[i] * k[j]).sum(-1) / math.sqrt(self.hd))
+            for ql, kl, tq, tk in self._entries(qg, kg, d):
+                s[tq, :, tk] = torch.from_numpy((q[ql] * k[kl]).sum(-1) / math.sqrt(self.hd))
 
     def softmax(self, t):
         s = t.view(self.T, self.H, self.T).numpy().transpose(1, 0, 2)
@@ -95,16 +107,13 @@ class PlainIO:
         p = np.exp(s - s.max(-1, keepdims=True))
         self.p = p / p.sum(-1, keepdims=True)  # [H, T, T]
 
-    def context(self, pairs):
-        for qg, kg in pairs:
+    def context(self, tiles):
+        for qg, kg, d in tiles:
             v = self.state[(2, kg)].reshape(-1, self.H, self.hd)
             rq = self.rows(qg)
             part = np.zeros((rq.stop - rq.start, self.H, self.hd))
-            for i in range(part.shape[0]):
-                for j in range(v.shape[0]):
-                    tq, tk = qg * B + i, kg * B + j
-                    if tk <= tq:
-                        part[i] += self.p[:, tq, tk][:, None] * v[j]
+            for ql, kl, tq, tk in self._entries(qg, kg, d):
+                part[ql] += self.p[:, tq, tk][:, None] * v[kl]
             key = (3, qg)
             self.state[key] = self.state.get(key, 0) + part.reshape(-1, self.D)
 
@@ -153,7 +162,7 @@ def _rank_main(rank, world, port, tokens, out_path):
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("world,tokens", [(2, 40), (2, 70), (3, 70), (5, 70)])
+@pytest.mark.parametrize("world,tokens", [(2, 40), (2, 70), (3, 70), (5, 70), (8, 103)])
 def test_sharded_block_over_gloo_ranks_equals_the_block(tmp_path, world, tokens):
     out = str(tmp_path / "y.npy")
     mp.start_processes(_rank_main, args=(world, _free_port(), tokens, out), nprocs=world, join=True,
