@@ -227,16 +227,25 @@ struct TileTag {
 };
 
 // score(q, k, head) from the head-window sums: feature head*HD, lane q - qg*B
-__global__ void score_gather_kernel(const double* __restrict__ vals, const TileTag* __restrict__ tags, int T, int H,
-                                    int HD, int B, int slots, double inv_sqrt_hd, double* __restrict__ scores) {
+// alignment (qg, kg, d) of a packed score tile (decrypted slot vector v)
+struct ScoreTag {
+  int qg, kg, d, v;
+};
+
+// score(q, k, head) from a packed tile: alignment d of head h sits at
+// feature (h*HD - d) mod PW, lane q - qg*B (the isolation mask already applied
+// the 1/sqrt(HD) scale)
+__global__ void score_gather_kernel(const double* __restrict__ vals, const ScoreTag* __restrict__ tags, int T, int H,
+                                    int HD, int B, int PW, int slots, double* __restrict__ scores) {
   const int ql = threadIdx.x;  // one lane per thread, B <= blockDim
   const int m = blockIdx.x, h = blockIdx.y;
   if (ql >= B) return;
-  const TileTag tg = tags[m];
+  const ScoreTag tg = tags[m];
   const int kl = (ql + tg.d) % B;
   const int q = tg.qg * B + ql, k = tg.kg * B + kl;
   if (q >= T || k >= T || k > q) return;
-  scores[((size_t)q * H + h) * T + k] = vals[(size_t)m * slots + (size_t)(h * HD) * B + ql] * inv_sqrt_hd;
+  const int f = (h * HD - tg.d + PW) % PW;
+  scores[((size_t)q * H + h) * T + k] = vals[(size_t)tg.v * slots + (size_t)f * B + ql];
 }
 
 // stable causal softmax of row (q, h) over k <= q; a missing score poisons the row
@@ -442,6 +451,24 @@ struct ckks_block {
     for (int f = 0; f < s.PW; ++f)
       for (int t = 0; t < s.B; ++t) v[(size_t)f * s.B + t] = ((t < s.B - delta) == lower) ? 1.0 : 0.0;
     (void)id;
+    auto p = cc.MakePlaintextAt(v, limbs, S(limbs));
+    masks[key] = p;
+    return p;
+  }
+
+  // isolation mask of alignment tg: `value` at feature h*HD (every head h)
+  // of the lanes whose (query, key) pair is causal and inside the sequence
+  Plaintext score_plain(const blk::TileTag& tg, int limbs, double value) {
+    auto key = std::make_pair(100000 + (tg.qg * s.groups + tg.kg) * s.B + tg.d, limbs);
+    auto it = masks.find(key);
+    if (it != masks.end()) return it->second;
+    std::vector<double> v((size_t)s.PW * s.B, 0.0);
+    for (int ql = 0; ql < s.B; ++ql) {
+      const int kl = (ql + tg.d) % s.B;
+      const int q = tg.qg * s.B + ql, k = tg.kg * s.B + kl;
+      if (q >= s.T || k >= s.T || k > q) continue;
+      for (int h = 0; h < s.H; ++h) v[(size_t)(h * s.HD) * s.B + ql] = value;
+    }
     auto p = cc.MakePlaintextAt(v, limbs, S(limbs));
     masks[key] = p;
     return p;
@@ -850,18 +877,45 @@ void ckks_block::shard_scores(const std::vector<blk::TileTag>& tiles, double* d_
       kb.push_back(ks[tg.d]);
     }
     const auto sums = head_window_sums(mul_ct_rs_batch(qa, kb));
+    // isolate each head's score at its causal lanes (scaled by 1/sqrt(HD)),
+    // move alignment d to feature h*HD - d (a rotation by d*B: the baby-step
+    // keys) and pack every alignment of a (query group, key group) tile into
+    // one ciphertext: one rotation sum, one client decryption per tile
+    // (T123.cpp:803-833); distinct d < B <= HD never share a feature
     const int M = (int)sums.size();
-    double* dv = dbuf((size_t)M * SL);
-    client_decrypt(sums, dv);
-    blk::TileTag* dt = (blk::TileTag*)C.alloc(sizeof(blk::TileTag) * M);
-    CKKS_CUDA(cudaMemcpyAsync(dt, tags.data(), sizeof(blk::TileTag) * M, cudaMemcpyHostToDevice, C.stream));
-    blk::score_gather_kernel<<<dim3(M, H), 32 * ((B + 31) / 32), 0, C.stream>>>(dv, dt, T, H, HD, B, SL, inv_sqrt_hd,
-                                                                              d_scores);
+    std::vector<Ciphertext> iso(M);
+    for (int i = 0; i < M; ++i) iso[i] = cc.EvalMult(sums[i], score_plain(tags[i], sums[i]->limbs(), inv_sqrt_hd));
+    count["ct_plain"] += M;
+    iso = cc.RescaleBatch(iso);
+    std::vector<int> qgs;
+    for (const auto& tg : tags)
+      if (std::find(qgs.begin(), qgs.end(), tg.qg) == qgs.end()) qgs.push_back(tg.qg);
+    std::vector<Ciphertext> packed;
+    std::vector<blk::ScoreTag> st;
+    for (size_t v = 0; v < qgs.size(); ++v) {
+      std::vector<Ciphertext> parts;
+      std::vector<int> rot;
+      for (int i = 0; i < M; ++i)
+        if (tags[i].qg == qgs[v]) {
+          parts.push_back(iso[i]);
+          rot.push_back(tags[i].d * B);
+          st.push_back({tags[i].qg, kg, tags[i].d, (int)v});
+        }
+      count["rotations"] += (long)parts.size();
+      packed.push_back(cc.EvalRotateSum(parts, rot));
+    }
+    const int P = (int)packed.size();
+    double* dv = dbuf((size_t)P * SL);
+    client_decrypt(packed, dv);
+    blk::ScoreTag* dt = (blk::ScoreTag*)C.alloc(sizeof(blk::ScoreTag) * st.size());
+    CKKS_CUDA(cudaMemcpyAsync(dt, st.data(), sizeof(blk::ScoreTag) * st.size(), cudaMemcpyHostToDevice, C.stream));
+    blk::score_gather_kernel<<<dim3((unsigned)st.size(), H), 32 * ((B + 31) / 32), 0, C.stream>>>(
+        dv, dt, T, H, HD, B, s.PW, SL, d_scores);
     CKKS_CUDA(cudaGetLastError());
     C.release(dt);
     C.release(dv);
-    count["score_tile_decryptions"] += M;
-    count["client_round_trips"] += M;
+    count["score_tile_decryptions"] += P;
+    count["client_round_trips"] += P;
   }
   stamp("scores");
 }
@@ -1116,7 +1170,8 @@ int ckks_block_create(ckks_ctx* ctx, const double* ln1, const double* attn_qkv, 
     s.HD = d_model / heads;
     s.B = 32;
     s.PW = C.N / 2 / s.B;
-    if (s.PW < d_model || (s.HD & (s.HD - 1))) throw ckks::Error(CKKS_EARG, "shape does not fit the slot layout");
+    if (s.PW < d_model || (s.HD & (s.HD - 1)) || s.B > s.HD)
+      throw ckks::Error(CKKS_EARG, "shape does not fit the slot layout");
     s.n1 = 32;
     while (s.n1 * s.n1 > s.PW) s.n1 >>= 1;
     s.n2 = s.PW / s.n1;
