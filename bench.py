@@ -180,8 +180,8 @@ def cpu_block_estimate(counts: dict, threads: int, budget_s: float = 12.0):
 
 
 # counts of one T=103 block (32 tokens/ciphertext), as reported by the engine
-BLOCK_COUNTS_T103 = {"rotations": 4150, "accumulate_sum": 16, "ct_ct": 606, "ct_plain": 41372,
-                     "matrix_products": 40, "client_round_trips": 610}
+BLOCK_COUNTS_T103 = {"rotations": 4445, "accumulate_sum": 16, "ct_ct": 606, "ct_plain": 41667,
+                     "matrix_products": 40, "client_round_trips": 325}
 
 
 def run_reference(args):
