@@ -370,9 +370,10 @@ def run_engine(args):
 
 def run_shard(args):
     """One block sharded over the torchrun ranks (strong scaling): token
-    groups and (query, key) tiles split across ranks, Q/K/V broadcasts, a
-    score all-reduce, partial-context merges and an output all-reduce over
-    NCCL between the stages (private_genomic_dnagpt_b200/shard.py).  Every
+    groups (with more ranks than groups, their Q/K/V projections and MLP
+    chunks) and attention alignments split across ranks, Q/K/V broadcasts, a
+    score all-reduce, partial-context and MLP merges and an output all-reduce
+    over NCCL between the stages (private_genomic_dnagpt_b200/shard.py).  Every
     rank holds the same keys (same seed).  value = device time of one block
     from the first stage to the assembled output, max over ranks."""
     import datetime
@@ -425,13 +426,17 @@ def run_shard(args):
     value = float(t[0])
     if rank == 0:
         groups = -(-args.tokens // 32)
+        metric = METRIC.replace(f"@{TOKENS} tok", f"@{args.tokens} tok")
         line = {
-            "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+            "metric": metric, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": value * 1e3, "higher_is_better": False, "scaling": "strong",
             "vs_baseline": value / REF_A100_BLOCK_S, "dtype": "u64", "data": "synthetic",
-            "config": {"workload": WORKLOAD, "parallelism": f"shard{world} (token groups + attention tiles)",
+            "config": {"workload": WORKLOAD.replace(f"{TOKENS} tokens", f"{args.tokens} tokens"),
+                       "parallelism": f"shard{world} (token groups, Q/K/V and MLP chunks, attention tiles)",
                        "flush": "inputs > L2 (keys, diagonals)", "rel_inf_vs_plaintext": err,
-                       "plan": [{"groups": rp.groups, "tiles": rp.tiles} for rp in sb.plan]},
+                       "plan": [{"groups": rp.groups, "qkv": rp.qkv, "mlp": rp.mlp, "tiles": rp.tiles}
+                                for rp in sb.plan],
+                       "rank0_stage_s": {k: round(v, 4) for k, v in block.report().get("seconds", {}).items()}},
             "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": groups * cc.slots * 8,
                     "d2h_bytes_per_step": groups * cc.slots * 8},
             "per_step_s": [round(v, 4) for v in steps],

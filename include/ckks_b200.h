@@ -267,9 +267,20 @@ int ckks_block_shard_scores_tiles(ckks_block* b, const int* tiles, int n, double
 int ckks_block_shard_context_tiles(ckks_block* b, const int* tiles, int n);
 /* writes the rows of the given groups into y [tokens, d_model] (host) */
 int ckks_block_shard_output(ckks_block* b, const int* groups, int n, double* y);
+/* finer units for more ranks than token groups (shard_layout.py: Q/K/V
+ * projections of a group on different devices, MLP partial sums merged by
+ * EvalAdd).  qkv_parts: bit 0 Q, bit 1 K, bit 2 V.  shard_mlp: O projection,
+ * residual (state 6), LN2 and the MLP chunks [chunk_begin, chunk_end) of the
+ * groups, their sum kept as state 5 (the output stage = shard_mlp over all
+ * chunks + shard_finish).  shard_finish: residual + MLP sum (states 6 and 5)
+ * decrypted into the groups' rows of y.  mlp_chunks: the chunk count. */
+int ckks_block_shard_qkv_parts(ckks_block* b, const int* groups, int n, int parts);
+int ckks_block_shard_mlp(ckks_block* b, const int* groups, int n, int chunk_begin, int chunk_end);
+int ckks_block_shard_finish(ckks_block* b, const int* groups, int n, double* y);
+int ckks_block_mlp_chunks(const ckks_block* b);
 /* state ciphertexts by kind (0 Q, 1 K, 2 V, 3 partial context, 4 encrypted
- * input) and token group: get copies into `out`; set copies from `in` (a
- * handle without data clears the entry) */
+ * input, 5 MLP sum, 6 attention residual) and token group: get copies into
+ * `out`; set copies from `in` (a handle without data clears the entry) */
 int ckks_block_state_get(ckks_block* b, int kind, int group, ckks_ct* out);
 int ckks_block_state_set(ckks_block* b, int kind, int group, const ckks_ct* in);
 

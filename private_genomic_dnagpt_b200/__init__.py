@@ -141,6 +141,11 @@ _SIGS = [
     ("ckks_block_shard_scores_tiles", ctypes.c_int, [_vp, ctypes.POINTER(ctypes.c_int), ctypes.c_int, _vp]),
     ("ckks_block_shard_context_tiles", ctypes.c_int, [_vp, ctypes.POINTER(ctypes.c_int), ctypes.c_int]),
     ("ckks_block_shard_output", ctypes.c_int, [_vp, ctypes.POINTER(ctypes.c_int), ctypes.c_int, _f64p]),
+    ("ckks_block_shard_qkv_parts", ctypes.c_int, [_vp, ctypes.POINTER(ctypes.c_int), ctypes.c_int, ctypes.c_int]),
+    ("ckks_block_shard_mlp", ctypes.c_int, [_vp, ctypes.POINTER(ctypes.c_int), ctypes.c_int, ctypes.c_int,
+                                            ctypes.c_int]),
+    ("ckks_block_shard_finish", ctypes.c_int, [_vp, ctypes.POINTER(ctypes.c_int), ctypes.c_int, _f64p]),
+    ("ckks_block_mlp_chunks", ctypes.c_int, [_vp]),
     ("ckks_block_state_get", ctypes.c_int, [_vp, ctypes.c_int, ctypes.c_int, _vp]),
     ("ckks_block_state_set", ctypes.c_int, [_vp, ctypes.c_int, ctypes.c_int, _vp]),
     ("ckks_ct_export_device", ctypes.c_int, [_vp, _vp, _vp, ctypes.c_size_t]),
@@ -649,9 +654,25 @@ class EncryptedBlock:
         x = np.ascontiguousarray(x, np.float64)
         _check(lib().ckks_block_shard_inputs(self.h, _f64(x), x.shape[0]))
 
-    def shard_qkv(self, groups):
+    def shard_qkv(self, groups, parts: int = 7):
+        """LN1 and the projections of `parts` (bit 0 Q, bit 1 K, bit 2 V)."""
         g = (ctypes.c_int * max(1, len(groups)))(*groups)
-        _check(lib().ckks_block_shard_qkv(self.h, g, len(groups)))
+        _check(lib().ckks_block_shard_qkv_parts(self.h, g, len(groups), parts))
+
+    @property
+    def mlp_chunks(self) -> int:
+        return lib().ckks_block_mlp_chunks(self.h)
+
+    def shard_mlp(self, groups, chunk_begin: int, chunk_end: int):
+        """O projection, residual, LN2 and MLP chunks [begin, end) of the
+        groups; the chunks' sum is state 5, the residual state 6."""
+        g = (ctypes.c_int * max(1, len(groups)))(*groups)
+        _check(lib().ckks_block_shard_mlp(self.h, g, len(groups), chunk_begin, chunk_end))
+
+    def shard_finish(self, groups, y: np.ndarray):
+        assert y.dtype == np.float64 and y.flags["C_CONTIGUOUS"]
+        g = (ctypes.c_int * max(1, len(groups)))(*groups)
+        _check(lib().ckks_block_shard_finish(self.h, g, len(groups), _f64(y)))
 
     @staticmethod
     def _pairs(pairs):
@@ -685,7 +706,8 @@ class EncryptedBlock:
 
     def state_get(self, kind: int, group: int):
         """Copy of a state ciphertext (0 Q, 1 K, 2 V, 3 partial context,
-        4 encrypted input) of a token group, or None if absent."""
+        4 encrypted input, 5 MLP sum, 6 attention residual) of a token group,
+        or None if absent."""
         out = self.cc._new()
         rc = lib().ckks_block_state_get(self.h, kind, group, out.h)
         if rc == 2:  # CKKS_ESTATE: not present

@@ -335,6 +335,8 @@ struct ckks_block {
     st_k.clear();
     st_v.clear();
     st_ctx.clear();
+    st_r1.clear();
+    st_mlp.clear();
     C.release(st_prob);
     st_prob = nullptr;
     if (ev_in) cudaEventDestroy(ev_in);
@@ -722,7 +724,7 @@ struct ckks_block {
 
   static constexpr int kHeadLinear = 100;
   // evaluation state between the stages of one forward
-  std::vector<Ciphertext> st_x, st_q, st_k, st_v, st_ctx;
+  std::vector<Ciphertext> st_x, st_q, st_k, st_v, st_ctx, st_r1, st_mlp;
   double* st_prob = nullptr;
   cudaEvent_t ev_in = nullptr, ev_out = nullptr;
   double t_start = 0.0, t_stage = 0.0, alloc_s0 = 0.0;
@@ -737,10 +739,13 @@ struct ckks_block {
   std::vector<blk::TileTag> alignments(const std::vector<std::pair<int, int>>& pairs) const;
   static std::vector<blk::TileTag> tags_of(int kg, const std::vector<blk::TileTag>& tiles);
   void shard_inputs(const double* x, int T);
-  void shard_qkv(const std::vector<int>& groups);
+  // parts: bit 0 Q, bit 1 K, bit 2 V
+  void shard_qkv(const std::vector<int>& groups, int parts);
   void shard_scores(const std::vector<blk::TileTag>& tiles, double* d_scores);
   void shard_softmax(const double* d_scores);
   void shard_context(const std::vector<blk::TileTag>& tiles);
+  void shard_mlp(const std::vector<int>& groups, int c0, int c1);
+  void shard_finish(const std::vector<int>& groups, double* y);
   void shard_output(const std::vector<int>& groups, double* y);
   void forward(const double* x, int T, double* y);
   double head_forward(const double* x_last);
@@ -808,6 +813,8 @@ void ckks_block::shard_inputs(const double* x, int T) {
   st_k.assign(G, Ciphertext());
   st_v.assign(G, Ciphertext());
   st_ctx.assign(G, Ciphertext());
+  st_r1.assign(G, Ciphertext());
+  st_mlp.assign(G, Ciphertext());
   // client: pack and encrypt the embeddings (T123.cpp:1642-1661)
   double* dx = dbuf((size_t)T * D);
   CKKS_CUDA(cudaMemcpyAsync(dx, x, sizeof(double) * T * D, cudaMemcpyHostToDevice, C.stream));
@@ -825,8 +832,8 @@ void ckks_block::shard_inputs(const double* x, int T) {
 }
 
 // LN1 + QKV of the given token groups
-void ckks_block::shard_qkv(const std::vector<int>& groups) {
-  if (groups.empty()) return;
+void ckks_block::shard_qkv(const std::vector<int>& groups, int parts) {
+  if (groups.empty() || !(parts & 7)) return;
   std::vector<Ciphertext> xs;
   std::vector<int> act;
   for (int g : groups) {
@@ -837,11 +844,11 @@ void ckks_block::shard_qkv(const std::vector<int>& groups) {
   const auto nrm = layernorm(xs, act);
   std::vector<std::vector<Ciphertext>> babies;
   for (const auto& n : nrm) babies.push_back(babies_of(n));
-  const auto q = bsgs_groups(babies, 0), k = bsgs_groups(babies, 1), v = bsgs_groups(babies, 2);
-  for (size_t i = 0; i < groups.size(); ++i) {
-    st_q[groups[i]] = q[i];
-    st_k[groups[i]] = k[i];
-    st_v[groups[i]] = v[i];
+  std::vector<Ciphertext>* dst[3] = {&st_q, &st_k, &st_v};
+  for (int w = 0; w < 3; ++w) {
+    if (!(parts & (1 << w))) continue;
+    const auto r = bsgs_groups(babies, w);
+    for (size_t i = 0; i < groups.size(); ++i) (*dst[w])[groups[i]] = r[i];
   }
   stamp("ln1_qkv");
 }
@@ -982,9 +989,15 @@ void ckks_block::shard_context(const std::vector<blk::TileTag>& tiles) {
 
 // O projection, residual, LN2, MLP of the given groups, then the client
 // decrypts them into their rows of y ([T, D] host)
-void ckks_block::shard_output(const std::vector<int>& groups, double* y) {
+// O projection, residual, LN2 and the MLP chunks [c0, c1) of the given
+// groups: the residual is kept in st_r1, the chunks' sum in st_mlp (the MLP
+// of a group may be split over ranks and its partial sums added with EvalAdd,
+// shard_layout.py stage 2)
+void ckks_block::shard_mlp(const std::vector<int>& groups, int c0, int c1) {
   if (groups.empty()) return;
-  const int T = s.T, D = s.D, B = s.B, PW = s.PW, SL = slots();
+  c0 = std::max(0, c0);
+  c1 = std::min(nfc, c1);
+  const int B = s.B, PW = s.PW, SL = slots();
   const int nb = (SL + blk::kThreads - 1) / blk::kThreads;
   const int G = (int)groups.size();
   std::vector<std::vector<Ciphertext>> ob;
@@ -998,50 +1011,70 @@ void ckks_block::shard_output(const std::vector<int>& groups, double* y) {
   ob.clear();
   std::vector<Ciphertext> r1;
   for (int i = 0; i < G; ++i) r1.push_back(add(reduce_to(st_x[groups[i]], o[i]->limbs()), o[i]));
+  for (int i = 0; i < G; ++i) st_r1[groups[i]] = r1[i];
+  if (c0 >= c1) {
+    for (int g : groups) st_mlp[g] = Ciphertext();
+    stamp("oproj_ln2_mlp");
+    return;
+  }
+  const int nc = c1 - c0;
   const auto n2 = layernorm(r1, act);
   std::vector<std::vector<Ciphertext>> fb;
   for (const auto& n : n2) fb.push_back(babies_of(n));
-  std::vector<std::vector<Ciphertext>> hc(nfc);  // [chunk][group]
-  for (int c = 0; c < nfc; ++c) hc[c] = bsgs_groups(fb, 4 + c);
+  std::vector<std::vector<Ciphertext>> hc(nc);  // [chunk][group]
+  for (int c = 0; c < nc; ++c) hc[c] = bsgs_groups(fb, 4 + c0 + c);
   fb.clear();
   // client: exact tanh-GELU on the active lanes of every group and chunk, one
-  // device batch (T123.cpp:540-568); item i * nfc + c
+  // device batch (T123.cpp:540-568); item i * nc + c
   const int gelu_limbs = 3;
   std::vector<Ciphertext> flat;
   for (int i = 0; i < G; ++i)
-    for (int c = 0; c < nfc; ++c) flat.push_back(hc[c][i]);
+    for (int c = 0; c < nc; ++c) flat.push_back(hc[c][i]);
   hc.clear();
-  double* dv = dbuf((size_t)G * nfc * SL);
+  double* dv = dbuf((size_t)G * nc * SL);
   client_decrypt(flat, dv);
   for (int i = 0; i < G; ++i)
-    for (int c = 0; c < nfc; ++c) {
-      const int odim = std::min(PW, s.MLP - c * PW);
-      double* v = dv + ((size_t)i * nfc + c) * SL;
+    for (int c = 0; c < nc; ++c) {
+      const int odim = std::min(PW, s.MLP - (c0 + c) * PW);
+      double* v = dv + ((size_t)i * nc + c) * SL;
       blk::gelu_kernel<<<dim3(nb, 1), blk::kThreads, 0, C.stream>>>(v, v, B, odim, act[i], SL);
       count["client_logical_instances"] += (long)odim * act[i];
     }
   CKKS_CUDA(cudaGetLastError());
-  const auto ge = client_encrypt(dv, G * nfc, gelu_limbs);
+  const auto ge = client_encrypt(dv, G * nc, gelu_limbs);
   C.release(dv);
-  count["client_round_trips"] += (long)G * nfc;
+  count["client_round_trips"] += (long)G * nc;
   std::vector<Ciphertext> mlp(G);
-  for (int c = 0; c < nfc; ++c) {
+  for (int c = 0; c < nc; ++c) {
     std::vector<std::vector<Ciphertext>> db;
-    for (int i = 0; i < G; ++i) db.push_back(babies_of(ge[(size_t)i * nfc + c]));
-    const auto pc = bsgs_groups(db, 4 + nfc + c);
+    for (int i = 0; i < G; ++i) db.push_back(babies_of(ge[(size_t)i * nc + c]));
+    const auto pc = bsgs_groups(db, 4 + nfc + c0 + c);
     for (int i = 0; i < G; ++i) mlp[i] = c ? add(mlp[i], pc[i]) : pc[i];
   }
-  std::vector<Ciphertext> out(G);
-  for (int i = 0; i < G; ++i) out[i] = add(reduce_to(r1[i], mlp[i]->limbs()), mlp[i]);
-  CKKS_CUDA(cudaEventRecord(ev_out, C.stream));
+  for (int i = 0; i < G; ++i) st_mlp[groups[i]] = mlp[i];
   stamp("oproj_ln2_mlp");
+}
+
+// block output r1 + MLP of the given groups, decrypted by the client into
+// their rows of y ([T, D] host)
+void ckks_block::shard_finish(const std::vector<int>& groups, double* y) {
+  if (groups.empty()) return;
+  const int T = s.T, D = s.D, B = s.B, SL = slots();
+  const int nb = (SL + blk::kThreads - 1) / blk::kThreads;
+  const int G = (int)groups.size();
+  std::vector<Ciphertext> out(G);
+  for (int i = 0; i < G; ++i) {
+    const int g = groups[i];
+    if (!st_r1[g] || !st_mlp[g]) throw ckks::Error(CKKS_ESTATE, "MLP of the group not complete");
+    out[i] = add(reduce_to(st_r1[g], st_mlp[g]->limbs()), st_mlp[g]);
+  }
+  CKKS_CUDA(cudaEventRecord(ev_out, C.stream));
   // client: decrypt and unpack (T123.cpp:1675-1694)
   {
-    const int M = (int)groups.size();
-    double* dv = dbuf((size_t)M * SL);
+    double* dv = dbuf((size_t)G * SL);
     client_decrypt(out, dv);
     double* dy = dbuf((size_t)T * D);
-    for (int i = 0; i < M; ++i) {
+    for (int i = 0; i < G; ++i) {
       const int g = groups[i];
       blk::unpack_kernel<<<dim3(nb, 1), blk::kThreads, 0, C.stream>>>(dv + (size_t)i * SL, dy, T, D, B, SL, g);
       const int r0 = g * B, r1_ = std::min(T, (g + 1) * B);
@@ -1065,6 +1098,11 @@ void ckks_block::shard_output(const std::vector<int>& groups, double* y) {
   seconds["evaluate_events"] = ms / 1e3;
 }
 
+void ckks_block::shard_output(const std::vector<int>& groups, double* y) {
+  shard_mlp(groups, 0, nfc);
+  shard_finish(groups, y);
+}
+
 void ckks_block::forward(const double* x, int T, double* y) {
   shard_inputs(x, T);
   std::vector<int> groups(s.groups);
@@ -1072,7 +1110,7 @@ void ckks_block::forward(const double* x, int T, double* y) {
   std::vector<std::pair<int, int>> pairs;
   for (int kg = 0; kg < s.groups; ++kg)
     for (int qg = kg; qg < s.groups; ++qg) pairs.push_back({qg, kg});
-  shard_qkv(groups);
+  shard_qkv(groups, 7);
   const auto tiles = alignments(pairs);
   double* d_scores = dbuf((size_t)T * s.H * T);
   CKKS_CUDA(cudaMemsetAsync(d_scores, 0xFF, sizeof(double) * T * s.H * T, C.stream));  // NaN = missing
@@ -1342,8 +1380,28 @@ int ckks_block_shard_inputs(ckks_block* b, const double* x, int tokens) {
 }
 
 int ckks_block_shard_qkv(ckks_block* b, const int* groups, int n) {
-  return bguard([&] { live(b)->shard_qkv(group_list(b, groups, n)); });
+  return bguard([&] { live(b)->shard_qkv(group_list(b, groups, n), 7); });
 }
+
+int ckks_block_shard_qkv_parts(ckks_block* b, const int* groups, int n, int parts) {
+  return bguard([&] {
+    if (parts < 0 || parts > 7) throw ckks::Error(CKKS_EARG, "parts: bit 0 Q, bit 1 K, bit 2 V");
+    live(b)->shard_qkv(group_list(b, groups, n), parts);
+  });
+}
+
+int ckks_block_shard_mlp(ckks_block* b, const int* groups, int n, int chunk_begin, int chunk_end) {
+  return bguard([&] { live(b)->shard_mlp(group_list(b, groups, n), chunk_begin, chunk_end); });
+}
+
+int ckks_block_shard_finish(ckks_block* b, const int* groups, int n, double* y) {
+  return bguard([&] {
+    if (!y) throw ckks::Error(CKKS_EARG, "null output");
+    live(b)->shard_finish(group_list(b, groups, n), y);
+  });
+}
+
+int ckks_block_mlp_chunks(const ckks_block* b) { return b ? b->nfc : -1; }
 
 int ckks_block_shard_scores(ckks_block* b, const int* pairs, int n, double* d_scores) {
   return bguard([&] {
@@ -1387,8 +1445,8 @@ int ckks_block_state_get(ckks_block* b, int kind, int group, ckks_ct* out) {
     live(b);
     if (!out || out->owner != b->ctx) throw ckks::Error(CKKS_EARG, "bad ciphertext handle");
     if (group < 0 || group >= b->s.groups) throw ckks::Error(CKKS_EARG, "group index out of range");
-    std::vector<Ciphertext>* v[] = {&b->st_q, &b->st_k, &b->st_v, &b->st_ctx, &b->st_x};
-    if (kind < 0 || kind > 4) throw ckks::Error(CKKS_EARG, "bad state kind");
+    std::vector<Ciphertext>* v[] = {&b->st_q, &b->st_k, &b->st_v, &b->st_ctx, &b->st_x, &b->st_mlp, &b->st_r1};
+    if (kind < 0 || kind > 6) throw ckks::Error(CKKS_EARG, "bad state kind");
     if ((int)v[kind]->size() <= group || !(*v[kind])[group]) throw ckks::Error(CKKS_ESTATE, "state not present");
     const ckks::DevPoly& p = (*v[kind])[group]->handle()->p;
     ckks::Context& C = b->C;
@@ -1416,8 +1474,8 @@ int ckks_block_state_set(ckks_block* b, int kind, int group, const ckks_ct* in) 
     live(b);
     if (!in || in->owner != b->ctx) throw ckks::Error(CKKS_EARG, "bad ciphertext handle");
     if (group < 0 || group >= b->s.groups) throw ckks::Error(CKKS_EARG, "group index out of range");
-    std::vector<Ciphertext>* v[] = {&b->st_q, &b->st_k, &b->st_v, &b->st_ctx, &b->st_x};
-    if (kind < 0 || kind > 4) throw ckks::Error(CKKS_EARG, "bad state kind");
+    std::vector<Ciphertext>* v[] = {&b->st_q, &b->st_k, &b->st_v, &b->st_ctx, &b->st_x, &b->st_mlp, &b->st_r1};
+    if (kind < 0 || kind > 6) throw ckks::Error(CKKS_EARG, "bad state kind");
     if ((int)v[kind]->size() != b->s.groups) throw ckks::Error(CKKS_ESTATE, "inputs not encrypted");
     if (!in->p.data || in->p.limbs <= 0) {
       (*v[kind])[group] = Ciphertext();

@@ -10,16 +10,24 @@ one process per GPU, identical keys
 on every rank (same seed) and these exchanges between the stages:
 
   after QKV      each group's Q, K, V ciphertexts, broadcast by the rank that
-                 evaluated the group (every tile needs K/V of its key group
-                 and Q of its query group);
+                 evaluated them (every tile needs K/V of its key group and
+                 Q of its query group);
   after scores   the score matrix: every rank fills the entries of its
                  tiles into a zero-initialised buffer, an all-reduce sum
                  assembles it (entries are disjoint, so the sum is exact);
   after context  per query group, the partial context sums of all ranks,
                  all-gathered and added with EvalAdd (exact modular adds) by
-                 the rank that owns the group;
+                 the ranks that evaluate the group's MLP;
+  after the MLP  a helper's partial MLP sum, broadcast and added with
+                 EvalAdd by the group's owner;
   at the end     the output rows of every group (disjoint rows, all-reduce
                  sum).
+
+With more ranks than token groups, group g also gets a helper rank
+(groups + g): the owner evaluates the Q and K projections and the first MLP
+chunks, the helper the V projection and the remaining chunks (both evaluate
+the O projection and LN2 the chunks need), as in shard_layout.py's split of
+the projections and of the MLP into exactly merged partial sums.
 
 ``shard_plan`` is pure host logic; ``ShardedBlock`` drives a block through
 an engine adapter, so the same orchestration runs on CPU ranks (gloo) over
@@ -32,7 +40,8 @@ from dataclasses import dataclass, field
 
 import numpy as np
 
-KIND_Q, KIND_K, KIND_V, KIND_CTX = 0, 1, 2, 3
+KIND_Q, KIND_K, KIND_V, KIND_CTX, KIND_X, KIND_MLP, KIND_RES = 0, 1, 2, 3, 4, 5, 6
+PART_Q, PART_K, PART_V = 1, 2, 4
 
 
 def active_shifts(tokens: int, batch: int, qg: int, kg: int) -> list[int]:
@@ -44,26 +53,48 @@ def active_shifts(tokens: int, batch: int, qg: int, kg: int) -> list[int]:
 
 @dataclass
 class RankPlan:
+    # token groups this rank owns: their output rows are decrypted here
     groups: list[int] = field(default_factory=list)
     # causal alignments (query group, key group, lane shift) of this rank
     tiles: list[tuple[int, int, int]] = field(default_factory=list)
     # alignments per key-group unit assigned (the load balanced)
     load: int = 0
+    # group -> projections evaluated here (PART_Q | PART_K | PART_V)
+    qkv: dict[int, int] = field(default_factory=dict)
+    # group -> MLP chunks [begin, end) evaluated here
+    mlp: dict[int, tuple[int, int]] = field(default_factory=dict)
 
 
-def shard_plan(tokens: int, batch: int, world: int) -> list[RankPlan]:
-    """Units of one block for each rank.  Token groups go round-robin.  The
-    attention work is split into (key group, lane shift d) units -- every
-    query group's alignment with that shift, which share one lane shift of
-    the key and value ciphertexts -- assigned longest-processing-time-first by
-    their alignment counts (ties to the lowest rank), so every alignment is
-    evaluated exactly once and every lane shift on one rank only."""
+def shard_plan(tokens: int, batch: int, world: int, mlp_chunks: int = 3) -> list[RankPlan]:
+    """Units of one block for each rank.  Token groups go round-robin to
+    owners; with more ranks than groups, rank groups + g helps group g (V and
+    the last floor(chunks / 2) MLP chunks; the owner keeps Q, K and the first
+    chunks).  The attention work is split into (key group, lane shift d)
+    units -- every query group's alignment with that shift, which share one
+    lane shift of the key and value ciphertexts -- assigned
+    longest-processing-time-first by their alignment counts (ties to the
+    lowest rank), so every alignment is evaluated exactly once and every lane
+    shift on one rank only."""
     if world < 1:
         raise ValueError("world size must be positive")
+    if mlp_chunks < 1:
+        raise ValueError("the MLP has at least one chunk")
     groups = -(-tokens // batch)
     plan = [RankPlan() for _ in range(world)]
     for g in range(groups):
-        plan[g % world].groups.append(g)
+        owner = plan[g % world]
+        owner.groups.append(g)
+        h = groups + g
+        if h < world:
+            split = mlp_chunks - mlp_chunks // 2
+            owner.qkv[g] = PART_Q | PART_K
+            owner.mlp[g] = (0, split)
+            plan[h].qkv[g] = PART_V
+            if split < mlp_chunks:
+                plan[h].mlp[g] = (split, mlp_chunks)
+        else:
+            owner.qkv[g] = PART_Q | PART_K | PART_V
+            owner.mlp[g] = (0, mlp_chunks)
     units: dict[tuple[int, int], list[tuple[int, int, int]]] = {}
     for kg in range(groups):
         for qg in range(kg, groups):
@@ -85,6 +116,20 @@ def group_owner(plan: list[RankPlan], g: int) -> int:
     raise ValueError(f"group {g} has no owner")
 
 
+def part_source(plan: list[RankPlan], g: int, part: int) -> int:
+    """The rank that evaluates projection `part` of group g."""
+    for r, rp in enumerate(plan):
+        if rp.qkv.get(g, 0) & part:
+            return r
+    raise ValueError(f"projection {part} of group {g} is not assigned")
+
+
+def mlp_ranks(plan: list[RankPlan], g: int) -> list[int]:
+    """Ranks that evaluate MLP chunks of group g, the owner first."""
+    owner = group_owner(plan, g)
+    return [owner] + [r for r, rp in enumerate(plan) if g in rp.mlp and r != owner]
+
+
 class ShardedBlock:
     """Drives one block through its stages on this rank's units and does the
     exchanges.  ``io`` is the engine adapter (``EngineIO`` for the CKKS
@@ -94,7 +139,7 @@ class ShardedBlock:
         self.io, self.dist, self.device = io, dist, device
         self.tokens, self.batch, self.heads, self.d_model = tokens, batch, heads, d_model
         self.rank, self.world = dist.get_rank(), dist.get_world_size()
-        self.plan = shard_plan(tokens, batch, self.world)
+        self.plan = shard_plan(tokens, batch, self.world, io.mlp_chunks)
         self.groups = -(-tokens // batch)
 
     def _broadcast_state(self, kind: int, g: int, src: int):
@@ -113,9 +158,20 @@ class ShardedBlock:
         if self.rank != src:
             io.state_import(kind, g, buf, meta)
 
-    def _merge_contexts(self, qg: int, owner: int):
+    @staticmethod
+    def _check_meta(present):
+        ref = present[0]
+        for m in present:
+            # same limbs and degree; scales equal to the engine's tolerance
+            # (a FLEXIBLEAUTO level reduction and a rescaled shift differ in
+            # the last bits)
+            if m[0] != ref[0] or m[2] != ref[2] or abs(m[1] - ref[1]) > 1e-9 * abs(ref[1]):
+                raise RuntimeError("partial sums at different levels or scales")
+        return ref
+
+    def _merge_contexts(self, qg: int, sinks: list[int]):
         """All-gather every rank's partial context of query group qg (a flag
-        and the limbs); the owner sums the present ones."""
+        and the limbs); the ranks in `sinks` sum the present ones."""
         import torch
         io, dist = self.io, self.dist
         meta = io.state_meta(KIND_CTX, qg)  # (limbs, scale, deg) or None
@@ -124,24 +180,42 @@ class ShardedBlock:
         metas = [torch.zeros_like(mt) for _ in range(self.world)]
         dist.all_gather(metas, mt)
         metas = [tuple(m.cpu().tolist()) for m in metas]
-        present = [m for m in metas if m[0] > 0]
+        present = [m[1:] for m in metas if m[0] > 0]
         if not present:
             raise RuntimeError(f"no rank evaluated a context tile of query group {qg}")
-        ref = present[0][1:]
-        for m in present:
-            # same limbs and degree; scales equal to the engine's tolerance
-            # (a FLEXIBLEAUTO level reduction and a rescaled shift differ in
-            # the last bits)
-            if m[1] != ref[0] or m[3] != ref[2] or abs(m[2] - ref[1]) > 1e-9 * abs(ref[1]):
-                raise RuntimeError("partial contexts at different levels or scales")
+        ref = self._check_meta(present)
         buf = io.state_export(KIND_CTX, qg)[0] if meta is not None else io.state_buffer(ref)
         if meta is None:
             buf.zero_()
         bufs = [torch.empty_like(buf) for _ in range(self.world)]
         dist.all_gather(bufs, buf)
-        if self.rank == owner:
+        if self.rank in sinks:
             parts = [bufs[r] for r in range(self.world) if metas[r][0] > 0]
             io.state_sum(KIND_CTX, qg, parts, ref)
+
+    def _merge_mlp(self, g: int, ranks: list[int]):
+        """Every helper in `ranks[1:]` broadcasts its partial MLP sum of
+        group g; the owner ranks[0] adds them to its own with EvalAdd."""
+        import torch
+        io, dist = self.io, self.dist
+        owner = ranks[0]
+        parts = [io.state_export(KIND_MLP, g)] if self.rank == owner else []
+        for src in ranks[1:]:
+            if self.rank == src:
+                buf, meta = io.state_export(KIND_MLP, g)
+                meta_t = torch.tensor(meta, dtype=torch.float64, device=self.device)
+            else:
+                meta_t = torch.zeros(3, dtype=torch.float64, device=self.device)
+            dist.broadcast(meta_t, src=src)
+            meta = tuple(float(v) for v in meta_t.cpu().tolist())
+            if self.rank != src:
+                buf = io.state_buffer(meta)
+            dist.broadcast(buf, src=src)
+            if self.rank == owner:
+                parts.append((buf, meta))
+        if self.rank == owner:
+            ref = self._check_meta([m for _, m in parts])
+            io.state_sum(KIND_MLP, g, [b for b, _ in parts], ref)
 
     def forward(self, x: np.ndarray) -> np.ndarray:
         with self.io.stream():
@@ -152,20 +226,32 @@ class ShardedBlock:
         io, dist = self.io, self.dist
         mine = self.plan[self.rank]
         io.inputs(x)
-        io.qkv(mine.groups)
+        by_parts: dict[int, list[int]] = {}
+        for g, parts in sorted(mine.qkv.items()):
+            by_parts.setdefault(parts, []).append(g)
+        for parts, gs in sorted(by_parts.items()):
+            io.qkv(gs, parts)
         for g in range(self.groups):
-            src = group_owner(self.plan, g)
-            for kind in (KIND_Q, KIND_K, KIND_V):
-                self._broadcast_state(kind, g, src)
+            for kind, part in ((KIND_Q, PART_Q), (KIND_K, PART_K), (KIND_V, PART_V)):
+                self._broadcast_state(kind, g, part_source(self.plan, g, part))
         scores = torch.zeros(self.tokens * self.heads * self.tokens, dtype=torch.float64, device=self.device)
         io.scores(mine.tiles, scores)
         dist.all_reduce(scores)
         io.softmax(scores)
         io.context(mine.tiles)
         for qg in range(self.groups):
-            self._merge_contexts(qg, group_owner(self.plan, qg))
+            self._merge_contexts(qg, mlp_ranks(self.plan, qg))
+        by_chunks: dict[tuple[int, int], list[int]] = {}
+        for g, chunks in sorted(mine.mlp.items()):
+            by_chunks.setdefault(chunks, []).append(g)
+        for (c0, c1), gs in sorted(by_chunks.items()):
+            io.mlp(gs, c0, c1)
+        for g in range(self.groups):
+            ranks = mlp_ranks(self.plan, g)
+            if len(ranks) > 1:
+                self._merge_mlp(g, ranks)
         y = np.zeros((self.tokens, self.d_model), np.float64)
-        io.output(mine.groups, y)
+        io.finish(mine.groups, y)
         yt = torch.from_numpy(y).to(self.device)
         dist.all_reduce(yt)
         return yt.cpu().numpy()
@@ -187,8 +273,12 @@ class EngineIO:
     def inputs(self, x):
         self.b.shard_inputs(x)
 
-    def qkv(self, groups):
-        self.b.shard_qkv(groups)
+    @property
+    def mlp_chunks(self) -> int:
+        return self.b.mlp_chunks
+
+    def qkv(self, groups, parts):
+        self.b.shard_qkv(groups, parts)
 
     def scores(self, tiles, t):
         self.b.shard_scores_tiles(tiles, t.data_ptr())
@@ -199,8 +289,11 @@ class EngineIO:
     def context(self, tiles):
         self.b.shard_context_tiles(tiles)
 
-    def output(self, groups, y):
-        self.b.shard_output(groups, y)
+    def mlp(self, groups, chunk_begin, chunk_end):
+        self.b.shard_mlp(groups, chunk_begin, chunk_end)
+
+    def finish(self, groups, y):
+        self.b.shard_finish(groups, y)
 
     def state_meta(self, kind, g):
         ct = self.b.state_get(kind, g)

@@ -3,10 +3,11 @@ CPU ranks (gloo, world size 2) over a float64 stand-in engine.
 
 The stand-in evaluates each stage of the plaintext block (oracle/plain_block)
 on exactly the units it is given, and keeps its per-group state (Q, K, V
-rows, partial contexts) as tensors that the orchestration exchanges; so the
-sharded output equals the unsharded block only if every unit is evaluated
-once and every exchange (state broadcast, score all-reduce, partial-context
-merge, output all-reduce) moves the right data.
+rows, partial contexts, MLP partial sums) as tensors that the orchestration
+exchanges; so the sharded output equals the unsharded block only if every
+unit is evaluated once and every exchange (state broadcast, score
+all-reduce, partial-context merge, MLP merge, output all-reduce) moves the
+right data.
 """
 
 import contextlib
@@ -48,9 +49,33 @@ def test_plan_covers_every_unit_once():
             assert max(loads) - min(loads) <= groups
 
 
+def test_plan_splits_projections_and_mlp_chunks():
+    for tokens in (1, 40, 103, 256):
+        groups = -(-tokens // B)
+        for world in range(1, 12):
+            for chunks in (1, 2, 3, 4):
+                plan = shard.shard_plan(tokens, B, world, chunks)
+                for g in range(groups):
+                    # each projection of each group on exactly one rank
+                    for part in (shard.PART_Q, shard.PART_K, shard.PART_V):
+                        assert sum(bool(rp.qkv.get(g, 0) & part) for rp in plan) == 1
+                    # the chunk ranges tile [0, chunks), the owner's first
+                    ranks = shard.mlp_ranks(plan, g)
+                    assert ranks[0] == shard.group_owner(plan, g)
+                    spans = sorted(plan[r].mlp[g] for r in ranks)
+                    assert spans[0][0] == 0 and spans[-1][1] == chunks
+                    assert all(a[1] == b[0] and a[0] < a[1] for a, b in zip(spans, spans[1:]))
+                    assert plan[ranks[0]].mlp[g][0] == 0
+                    helped = groups + g < world
+                    assert len([rp for rp in plan if g in rp.qkv]) == (2 if helped else 1)
+
+
 def test_plan_for_the_benchmark_shape():
     plan = shard.shard_plan(103, B, 8)
     assert [rp.groups for rp in plan] == [[0], [1], [2], [3], [], [], [], []]
+    assert [rp.qkv for rp in plan] == [{0: 3}, {1: 3}, {2: 3}, {3: 3}, {0: 4}, {1: 4}, {2: 4}, {3: 4}]
+    assert [rp.mlp for rp in plan] == [{0: (0, 2)}, {1: (0, 2)}, {2: (0, 2)}, {3: (0, 2)},
+                                       {0: (2, 3)}, {1: (2, 3)}, {2: (2, 3)}, {3: (2, 3)}]
     total = sum(len(shard.active_shifts(103, B, qg, kg)) for kg in range(4) for qg in range(kg, 4))
     assert sum(rp.load for rp in plan) == total == 295
     assert max(rp.load for rp in plan) - min(rp.load for rp in plan) <= 4
@@ -75,13 +100,21 @@ class PlainIO:
         self.x = np.asarray(x, np.float64)
         self.state = {}
 
-    def qkv(self, groups):
+    # MLP hidden units per chunk (one plaintext width of the engine)
+    CHUNK = 1024
+
+    @property
+    def mlp_chunks(self):
+        return -(-self.w["mlp_fc"].shape[0] // self.CHUNK)
+
+    def qkv(self, groups, parts):
         D = self.D
         for g in groups:
             h1 = plain_block.layer_norm(self.x[self.rows(g)], self.w["ln1"])
             qkv = h1 @ self.w["attn_qkv"].T
             for kind in range(3):
-                self.state[(kind, g)] = qkv[:, kind * D:(kind + 1) * D].copy()
+                if parts & (1 << kind):
+                    self.state[(kind, g)] = qkv[:, kind * D:(kind + 1) * D].copy()
 
     def _entries(self, qg, kg, d):
         """(query row in group, key row in group) of alignment (qg, kg, d):
@@ -117,11 +150,18 @@ class PlainIO:
             key = (3, qg)
             self.state[key] = self.state.get(key, 0) + part.reshape(-1, self.D)
 
-    def output(self, groups, y):
+    def mlp(self, groups, c0, c1):
         for g in groups:
             r1 = self.x[self.rows(g)] + self.state[(3, g)] @ self.w["attn_proj"].T
             h2 = plain_block.layer_norm(r1, self.w["ln2"])
-            y[self.rows(g)] = r1 + plain_block.gelu_tanh(h2 @ self.w["mlp_fc"].T) @ self.w["mlp_proj"].T
+            cols = slice(c0 * self.CHUNK, c1 * self.CHUNK)
+            hid = plain_block.gelu_tanh(h2 @ self.w["mlp_fc"][cols].T)
+            self.state[(6, g)] = r1
+            self.state[(5, g)] = hid @ self.w["mlp_proj"][:, cols].T
+
+    def finish(self, groups, y):
+        for g in groups:
+            y[self.rows(g)] = self.state[(6, g)] + self.state[(5, g)]
 
     def state_meta(self, kind, g):
         a = self.state.get((kind, g))
@@ -162,7 +202,7 @@ def _rank_main(rank, world, port, tokens, out_path):
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("world,tokens", [(2, 40), (2, 70), (3, 70), (5, 70), (8, 103)])
+@pytest.mark.parametrize("world,tokens", [(2, 40), (2, 70), (3, 70), (5, 70), (6, 103), (8, 103)])
 def test_sharded_block_over_gloo_ranks_equals_the_block(tmp_path, world, tokens):
     out = str(tmp_path / "y.npy")
     mp.start_processes(_rank_main, args=(world, _free_port(), tokens, out), nprocs=world, join=True,

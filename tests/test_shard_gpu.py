@@ -91,7 +91,28 @@ def test_block_state_get_set_round_trip():
     assert np.array_equal(blk.state_get(0, 1).limbs_array(), q0.limbs_array())
     # a full staged forward equals the plaintext block
     y = blk.forward(x)
-    assert plain_block.rel_inf(plain_block.block(x, w), y) < 1e-6
+    ref = plain_block.block(x, w)
+    assert plain_block.rel_inf(ref, y) < 1e-6
+    # the output stage split as an owner and a helper would: MLP chunks
+    # [2, 3) and [0, 2) evaluated apart, their sums added with EvalAdd
+    assert blk.mlp_chunks == 3
+    blk.shard_mlp([0, 1], 2, 3)
+    tail = [blk.state_get(5, g) for g in (0, 1)]
+    blk.shard_mlp([0, 1], 0, 2)
+    for g in (0, 1):
+        blk.state_set(5, g, cc.EvalAdd(blk.state_get(5, g), tail[g]))
+    y2 = np.zeros_like(y)
+    blk.shard_finish([0, 1], y2)
+    assert plain_block.rel_inf(ref, y2) < 1e-6
+    # a projection evaluated alone equals the batched one (LN1 encrypts
+    # fresh refreshes, so the ciphertexts differ in their noise)
+    v_all = cc.DecryptDecodeBatch([blk.state_get(2, 1)])[0]
+    blk.state_set(2, 1, cc._new())
+    assert blk.state_get(2, 1) is None
+    blk.shard_qkv([1], 4)
+    assert blk.state_get(1, 1) is not None
+    v_one = cc.DecryptDecodeBatch([blk.state_get(2, 1)])[0]
+    assert np.abs(v_one - v_all).max() <= 1e-6 * np.abs(v_all).max()
 
 
 def _free_port():
@@ -129,13 +150,15 @@ def _rank(rank, world, port, tokens, out):
 
 @pytest.mark.skipif(not __import__("torch").cuda.is_available() or __import__("torch").cuda.device_count() < 2,
                     reason="needs two GPUs")
-def test_block_sharded_over_two_gpus(tmp_path):
+@pytest.mark.parametrize("tokens", [103, 32])
+def test_block_sharded_over_two_gpus(tmp_path, tokens):
+    """103 tokens: two owners of token groups; 32 tokens: one group, its
+    owner (Q, K, MLP chunks 0-1) and a helper (V, MLP chunk 2)."""
     import torch.multiprocessing as mp
-    tokens = 103
     out = str(tmp_path / "y.npy")
     mp.start_processes(_rank, args=(2, _free_port(), tokens, out), nprocs=2, join=True, start_method="spawn")
     y = np.load(out)
     ref = plain_block.block(plain_block.synthetic_input(6, tokens), plain_block.synthetic_weights(5))
     err = plain_block.rel_inf(ref, y)
-    print(f"sharded over 2 GPUs: rel_inf {err:.3e}")
+    print(f"{tokens} tokens sharded over 2 GPUs: rel_inf {err:.3e}")
     assert err < 1e-6
