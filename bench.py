@@ -270,6 +270,7 @@ def run_engine(args):
             prof = cc.profile_report()  # folds this step's kernel events (the GPU is idle here)
         barrier()
         torch.cuda.cudart().cudaProfilerStop()
+    sections = cc.profile_sections()
     e2e_ms = float(np.mean(e2e_ms_steps))
     cc.profile(False)
     rep = block.report()
@@ -358,6 +359,12 @@ def run_engine(args):
                       "e2e_s_per_step": [round(v / 1e3, 4) for v in e2e_ms_steps],
                       "host_per_step": diag_steps},
             "kernels": {k: {"launches": v["launches"], "ms": round(v["ms"], 3)} for k, v in prof.items()},
+            # per block stage: device ms per step of its kernels, the largest first
+            "stage_kernels_ms": {
+                sec: dict(sorted(((k, round(v["ms"] / args.steps, 2)) for k, v in ks.items()),
+                                 key=lambda kv: -kv[1])[:8]) | {
+                    "_total": round(sum(v["ms"] for v in ks.values()) / args.steps, 2)}
+                for sec, ks in sections.items()},
             "gpu_launches": launches,
             "clocks": clk.summary(),
             "cpu_baseline": cpu,

@@ -204,6 +204,20 @@ int ckks_mul_ct_batch(ckks_ctx* ctx, const ckks_ct* const* a, const ckks_ct* con
 int ckks_rescale_batch(ckks_ctx* ctx, const ckks_ct* const* in, int count, ckks_ct* const* outs);
 /* AccumulateSum(ct, count, stride) (T123.cpp:1154-1159; key ladder :444-453) */
 int ckks_accumulate_sum(ckks_ctx* ctx, const ckks_ct* a, int count, int stride, ckks_ct* out);
+/* outs[i] = sum_r EvalRotate(in[i], k[r]) for every input (k distinct; an
+ * index 0 adds in[i] itself): the rotations of one input share its ModUp
+ * (as EvalFastRotation) and their key switches are added in Q_l P and
+ * divided by P once per input; up to 32 inputs per launch sequence, all at
+ * one limb count.  Equal to ckks_rotate_sum over (in[i], k[r]) pairs. */
+int ckks_rotate_sum_hoisted(ckks_ctx* ctx, const ckks_ct* const* in, int count, const int* k, int nk,
+                            ckks_ct* const* outs);
+/* outs[i] = sum_{j < window} EvalRotate(in[i], j * stride): the sums of the
+ * AccumulateSum ladder (base 4, keys stride * 4^s * {1, 2, 3}) with every
+ * step one hoisted rotation sum (one ModUp and one ModDown per step and
+ * input, where AccumulateSum takes one ModDown per rotation) -- the same
+ * slot values as AccumulateSum, different rounding noise. */
+int ckks_window_sum_batch(ckks_ctx* ctx, const ckks_ct* const* in, int count, int window, int stride,
+                          ckks_ct* const* outs);
 
 /* Kernel timer (the reference's per-call-site Profiler buckets,
  * fhe/gpu_real_scheme_b/src/real_dnagpt_fides_scheme_b_lintransform.cpp:627-629,
@@ -214,6 +228,9 @@ int ckks_accumulate_sum(ckks_ctx* ctx, const ckks_ct* a, int count, int stride, 
 int ckks_profile_enable(ckks_ctx* ctx, int on);
 int ckks_profile_reset(ckks_ctx* ctx);
 int ckks_profile_report(ckks_ctx* ctx, char* buf, size_t size);
+/* the same totals split by section (the block evaluation names its stages:
+ * {"section": {"kernel": {"launches": n, "ms": t}}}), JSON text */
+int ckks_profile_sections(ckks_ctx* ctx, char* buf, size_t size);
 
 /* Limb-level kernels on caller-owned DEVICE buffers (uint64 residues,
  * limb-major, N words per limb), for parity checks and kernel benchmarks.

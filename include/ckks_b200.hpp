@@ -282,6 +282,33 @@ class CryptoContextImpl {
     check(ckks_accumulate_sum(h_, a->handle(), count, stride, o->handle()));
     return o;
   }
+  // [sum_r rot(x, k[r]) for x in a]: one ModUp and one ModDown per input
+  std::vector<Ciphertext> EvalRotateSumHoisted(const std::vector<Ciphertext>& a, const std::vector<int>& k) {
+    std::vector<Ciphertext> outs;
+    std::vector<const ckks_ct*> in;
+    std::vector<ckks_ct*> hs;
+    for (const auto& x : a) {
+      outs.push_back(fresh());
+      in.push_back(x->handle());
+      hs.push_back(outs.back()->handle());
+    }
+    check(ckks_rotate_sum_hoisted(h_, in.data(), (int)a.size(), k.data(), (int)k.size(), hs.data()));
+    return outs;
+  }
+  // [sum_{j < window} rot(x, j * stride) for x in a]: the AccumulateSum
+  // ladder with one ModDown per step
+  std::vector<Ciphertext> WindowSumBatch(const std::vector<Ciphertext>& a, int window, int stride) {
+    std::vector<Ciphertext> outs;
+    std::vector<const ckks_ct*> in;
+    std::vector<ckks_ct*> hs;
+    for (const auto& x : a) {
+      outs.push_back(fresh());
+      in.push_back(x->handle());
+      hs.push_back(outs.back()->handle());
+    }
+    check(ckks_window_sum_batch(h_, in.data(), (int)a.size(), window, stride, hs.data()));
+    return outs;
+  }
   // degree-1 ciphertext at `limbs` limbs with that level's FLEXIBLEAUTO scale
   Ciphertext LevelReduce(const Ciphertext& a, int limbs) {
     Ciphertext x = deg1(a);

@@ -1273,6 +1273,24 @@ int oc_rotate_sum(const oc_ctx* c, const uint64_t* cts, int limbs, const int* ks
     return 0;
 }
 
+/* sum_{j < window} rot(ct, j * stride) by the AccumulateSum ladder with each
+ * step's rotations {0, s, 2s, 3s} * stride summed as one rotation sum (the
+ * key switches added in the extended basis, one ModDown per step) -- the
+ * engine's hoisted window sums. */
+int oc_window_sum(const oc_ctx* c, const uint64_t* ct, int limbs, int window, int stride, uint64_t* out) {
+    const size_t S2 = 2 * (size_t)limbs * c->N;
+    memcpy(out, ct, sizeof(uint64_t) * S2);
+    uint64_t* rep = (uint64_t*)malloc(sizeof(uint64_t) * 4 * S2);
+    for (long step = 1; step < window; step *= 4) {
+        int ks[4] = {0, 0, 0, 0}, n = 1;
+        for (int m = 1; m < 4 && step * m < window; m++) ks[n++] = (int)(stride * step * m);
+        for (int r = 0; r < n; r++) memcpy(rep + (size_t)r * S2, out, sizeof(uint64_t) * S2);
+        if (oc_rotate_sum(c, rep, limbs, ks, n, out)) { free(rep); return -1; }
+    }
+    free(rep);
+    return 0;
+}
+
 /* AccumulateSum(ct, count, stride) (T123.cpp:1154-1159, keys :444-453):
  * base-4 ladder; at step s the hoisted rotations by stride*s*{1,2,3}
  * (those with s*m < count) are added to the running sum. */

@@ -122,9 +122,13 @@ _SIGS = [
                                          ctypes.POINTER(_vp)]),
     ("ckks_rescale_batch", ctypes.c_int, [_vp, ctypes.POINTER(_vp), ctypes.c_int, ctypes.POINTER(_vp)]),
     ("ckks_accumulate_sum", ctypes.c_int, [_vp, _vp, ctypes.c_int, ctypes.c_int, _vp]),
+    ("ckks_rotate_sum_hoisted", ctypes.c_int, [_vp, _vp, ctypes.c_int, ctypes.POINTER(ctypes.c_int), ctypes.c_int,
+                                               _vp]),
+    ("ckks_window_sum_batch", ctypes.c_int, [_vp, _vp, ctypes.c_int, ctypes.c_int, ctypes.c_int, _vp]),
     ("ckks_profile_enable", ctypes.c_int, [_vp, ctypes.c_int]),
     ("ckks_profile_reset", ctypes.c_int, [_vp]),
     ("ckks_profile_report", ctypes.c_int, [_vp, ctypes.c_char_p, ctypes.c_size_t]),
+    ("ckks_profile_sections", ctypes.c_int, [_vp, ctypes.c_char_p, ctypes.c_size_t]),
     ("ckks_ntt_forward_device", ctypes.c_int, [_vp, _vp, ctypes.c_int, ctypes.c_int]),
     ("ckks_rotate_noalloc", ctypes.c_int, [_vp, _vp, ctypes.c_int, ctypes.c_int, _vp]),
     ("ckks_block_create", ctypes.c_int, [_vp] + [_f64p] * 6 + [ctypes.c_int] * 4 + [ctypes.POINTER(_vp)]),
@@ -347,6 +351,16 @@ class CryptoContext:
             raise CKKSError(-1, lib().ckks_last_error().decode())
         buf = ctypes.create_string_buffer(n + 1)
         lib().ckks_profile_report(self.h, buf, n + 1)
+        return json.loads(buf.value.decode())
+
+    def profile_sections(self) -> dict:
+        """Kernel totals per section (block stages) since the last reset."""
+        import json
+        n = lib().ckks_profile_sections(self.h, None, 0)
+        if n < 0:
+            raise CKKSError(-1, lib().ckks_last_error().decode())
+        buf = ctypes.create_string_buffer(n + 1)
+        lib().ckks_profile_sections(self.h, buf, n + 1)
         return json.loads(buf.value.decode())
 
     def stream_handle(self) -> int:
@@ -591,6 +605,24 @@ class CryptoContext:
 
     def AccumulateSum(self, ct: Ciphertext, count: int, stride: int) -> Ciphertext:
         o = self._new(); _check(lib().ckks_accumulate_sum(self.h, ct.h, count, stride, o.h)); return o
+
+    def EvalRotateSumHoisted(self, cts, ks) -> list[Ciphertext]:
+        """[sum_r EvalRotate(ct, ks[r]) for ct in cts]: one ModUp and one
+        ModDown per ciphertext."""
+        n, nk = len(cts), len(ks)
+        outs = [self._new() for _ in cts]
+        _check(lib().ckks_rotate_sum_hoisted(self.h, (_vp * max(1, n))(*[c.h for c in cts]), n,
+                                             (ctypes.c_int * nk)(*ks), nk, (_vp * max(1, n))(*[o.h for o in outs])))
+        return outs
+
+    def WindowSumBatch(self, cts, window: int, stride: int) -> list[Ciphertext]:
+        """[sum_{j < window} EvalRotate(ct, j * stride) for ct in cts]: the
+        AccumulateSum ladder with one ModDown per step."""
+        n = len(cts)
+        outs = [self._new() for _ in cts]
+        _check(lib().ckks_window_sum_batch(self.h, (_vp * max(1, n))(*[c.h for c in cts]), n, window, stride,
+                                           (_vp * max(1, n))(*[o.h for o in outs])))
+        return outs
 
 
 def GenCryptoContext(params: CCParams) -> CryptoContext:

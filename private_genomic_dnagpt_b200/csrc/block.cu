@@ -18,9 +18,9 @@
 //   QKV      one hoisted baby-step set, three fused BSGS products (n1 = n2 = 32).
 //   scores   for every causal (query group, key group, lane shift delta):
 //            Q * lane_shift(K, delta), then a window sum over each head's 64
-//            features (rotations by B*2^i); the client reads score(q, k, head)
-//            at feature 64*head and runs the exact float64 softmax
-//            (T123.cpp:629-665).
+//            features (the AccumulateSum ladder, each step one hoisted
+//            rotation sum); the client reads score(q, k, head) at feature
+//            64*head and runs the exact float64 softmax (T123.cpp:629-665).
 //   context  the client encrypts the weight tile of every alignment; the
 //            server accumulates tile * lane_shift(V, delta).
 //   O proj   BSGS; residual1 = x + O.
@@ -476,10 +476,16 @@ struct ckks_block {
     return p;
   }
 
-  Ciphertext feature_sum(const Ciphertext& x) {
-    ++count["accumulate_sum"];
-    return cc.AccumulateSum(x, s.PW, s.B);
+  // sum over the PW features of every lane (the AccumulateSum ladder of
+  // T123.cpp:1154-1159, each base-4 step one hoisted rotation sum), for a
+  // batch of ciphertexts at one level
+  std::vector<Ciphertext> feature_sums(const std::vector<Ciphertext>& xs) {
+    count["accumulate_sum"] += (long)xs.size();
+    for (long step = 1; step < s.PW; step *= 4)
+      for (int m = 1; m < 4 && step * m < s.PW; ++m) count["rotations"] += (long)xs.size();
+    return cc.WindowSumBatch(xs, s.PW, s.B);
   }
+  Ciphertext feature_sum(const Ciphertext& x) { return feature_sums({x})[0]; }
 
   // LayerNorm without the gain (folded into the next product), for a batch of
   // token groups: the server computes centered and var + eps; the client
@@ -490,9 +496,10 @@ struct ckks_block {
     std::vector<double> invd(s.PW, 0.0);
     for (int f = 0; f < s.D; ++f) invd[f] = 1.0 / s.D;
     std::vector<Ciphertext> centered, sqs;
-    for (const auto& x : xs) {
-      const Ciphertext mean = mul_pt_rs(feature_sum(x), feature_plain(1, invd, lx));
-      centered.push_back(cc.EvalSub(reduce_to(x, lx - 1), mean));
+    const auto sums = feature_sums(xs);
+    for (size_t i = 0; i < xs.size(); ++i) {
+      const Ciphertext mean = mul_pt_rs(sums[i], feature_plain(1, invd, lx));
+      centered.push_back(cc.EvalSub(reduce_to(xs[i], lx - 1), mean));
     }
     // the variance is only decrypted: square at 4 limbs, sum and scale at 3,
     // decrypt at 2
@@ -501,8 +508,8 @@ struct ckks_block {
     count["ct_ct"] += (long)xs.size();
     sqs = cc.RescaleBatch(cc.EvalMultBatch(low, low));
     std::vector<Ciphertext> var;
-    for (const auto& sq : sqs)
-      var.push_back(cc.EvalAdd(mul_pt_rs(feature_sum(sq), feature_plain(1, invd, sq->limbs())), 1e-5));
+    for (const auto& sq : feature_sums(sqs))
+      var.push_back(cc.EvalAdd(mul_pt_rs(sq, feature_plain(1, invd, sq->limbs())), 1e-5));
     const int M = (int)xs.size();
     double* dv = dbuf((size_t)M * slots());
     client_decrypt(var, dv);
@@ -565,15 +572,12 @@ struct ckks_block {
     return cc.RescaleBatch(cc.EvalMultBatch(a, b));
   }
 
-  // sum of the hd features of every head, left at the head's first feature,
-  // for a batch of ciphertexts (rotations by B*2^i, batched per step)
-  std::vector<Ciphertext> head_window_sums(std::vector<Ciphertext> h) {
-    for (int w = 1; w < s.HD; w <<= 1) {
-      count["rotations"] += (long)h.size();
-      const auto r = cc.EvalRotateBatch(h, std::vector<int>(h.size(), s.B * w));
-      h = cc.EvalAddBatch(h, r);
-    }
-    return h;
+  // per head, the sum of its HD features at the head's first feature (and
+  // window sums elsewhere): a base-4 ladder of hoisted rotation sums
+  std::vector<Ciphertext> head_window_sums(const std::vector<Ciphertext>& h) {
+    for (long step = 1; step < s.HD; step *= 4)
+      for (int m = 1; m < 4 && step * m < s.HD; ++m) count["rotations"] += (long)h.size();
+    return cc.WindowSumBatch(h, s.HD, s.B);
   }
 
   // weight id -> (device matrix, out_dim, in_dim, leading dimension)
@@ -769,7 +773,8 @@ std::vector<int> ckks_block::rotation_indices() const {
     v.push_back(canon(d));
     v.push_back(canon(d - s.B));
   }
-  for (int w = 1; w < s.HD; w <<= 1) v.push_back(canon((long)s.B * w));
+  for (long step = 1; step < s.HD; step *= 4)  // head window sums: the same ladder over HD features
+    for (int m = 1; m < 4 && step * m < s.HD; ++m) v.push_back(canon((long)s.B * step * m));
   std::sort(v.begin(), v.end());
   v.erase(std::unique(v.begin(), v.end()), v.end());
   v.erase(std::remove(v.begin(), v.end(), 0), v.end());
@@ -799,6 +804,7 @@ std::vector<blk::TileTag> ckks_block::tags_of(int kg, const std::vector<blk::Til
 }
 
 void ckks_block::shard_inputs(const double* x, int T) {
+  C.prof.section = "encrypt_inputs";
   if (T != s.T) throw ckks::Error(CKKS_EARG, "token count differs from the block's");
   const int G = s.groups, D = s.D, SL = slots();
   const int nb = (SL + blk::kThreads - 1) / blk::kThreads;
@@ -833,6 +839,7 @@ void ckks_block::shard_inputs(const double* x, int T) {
 
 // LN1 + QKV of the given token groups
 void ckks_block::shard_qkv(const std::vector<int>& groups, int parts) {
+  C.prof.section = "ln1_qkv";
   if (groups.empty() || !(parts & 7)) return;
   std::vector<Ciphertext> xs;
   std::vector<int> act;
@@ -857,6 +864,7 @@ void ckks_block::shard_qkv(const std::vector<int>& groups, int parts) {
 // ([q][head][k] doubles on the device): server products and head-window sums,
 // the client decrypts and gathers them on the device
 void ckks_block::shard_scores(const std::vector<blk::TileTag>& tiles, double* d_scores) {
+  C.prof.section = "scores";
   const int T = s.T, H = s.H, HD = s.HD, B = s.B, SL = slots();
   const double inv_sqrt_hd = 1.0 / std::sqrt((double)HD);
   // queries brought to the score level once per query group (a FLEXIBLEAUTO
@@ -929,6 +937,7 @@ void ckks_block::shard_scores(const std::vector<blk::TileTag>& tiles, double* d_
 
 // client: exact causal softmax in float64 (T123.cpp:629-665)
 void ckks_block::shard_softmax(const double* d_scores) {
+  C.prof.section = "softmax";
   const int T = s.T, H = s.H;
   if (!st_prob) st_prob = (double*)C.alloc(sizeof(double) * (size_t)T * H * T);
   int* bad = (int*)C.alloc(sizeof(int));
@@ -948,6 +957,7 @@ void ckks_block::shard_softmax(const double* d_scores) {
 // a query group are only ever summed, so they are added as degree-2
 // ciphertexts and relinearised once (EvalMultSum), then rescaled.
 void ckks_block::shard_context(const std::vector<blk::TileTag>& tiles) {
+  C.prof.section = "context";
   const int T = s.T, H = s.H, HD = s.HD, D = s.D, B = s.B, SL = slots();
   const int nb = (SL + blk::kThreads - 1) / blk::kThreads;
   if (!st_prob) throw ckks::Error(CKKS_ESTATE, "softmax not evaluated");
@@ -994,6 +1004,7 @@ void ckks_block::shard_context(const std::vector<blk::TileTag>& tiles) {
 // of a group may be split over ranks and its partial sums added with EvalAdd,
 // shard_layout.py stage 2)
 void ckks_block::shard_mlp(const std::vector<int>& groups, int c0, int c1) {
+  C.prof.section = "oproj_ln2_mlp";
   if (groups.empty()) return;
   c0 = std::max(0, c0);
   c1 = std::min(nfc, c1);
@@ -1058,6 +1069,7 @@ void ckks_block::shard_mlp(const std::vector<int>& groups, int c0, int c1) {
 // block output r1 + MLP of the given groups, decrypted by the client into
 // their rows of y ([T, D] host)
 void ckks_block::shard_finish(const std::vector<int>& groups, double* y) {
+  C.prof.section = "decrypt_outputs";
   if (groups.empty()) return;
   const int T = s.T, D = s.D, B = s.B, SL = slots();
   const int nb = (SL + blk::kThreads - 1) / blk::kThreads;
@@ -1129,6 +1141,7 @@ void ckks_block::forward(const double* x, int T, double* y) {
 // encrypted at 5 limbs (LN 2, linear 1, decryption at 2), the SiLU output
 // at 5 (LN 2, readout 1, decryption at 2).
 double ckks_block::head_forward(const double* x_last) {
+  C.prof.section = "head";
   const int D = s.D, B = s.B, SL = slots();
   const int nb = (SL + blk::kThreads - 1) / blk::kThreads;
   constexpr int kHeadLimbs = 5;

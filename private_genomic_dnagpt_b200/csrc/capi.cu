@@ -1,6 +1,7 @@
 // capi.cu -- the extern "C" boundary declared in include/ckks_b200.h.
 // Each entry point validates its arguments, runs the device pipeline on the
 // context's stream and converts C++ exceptions into status codes.
+#include <algorithm>
 #include <cmath>
 #include <cstdio>
 #include <cstring>
@@ -180,6 +181,61 @@ void rotate_batch(Context& c, const ckks_ct* const* in, const int* ks, int n, ck
   for (int r = 0; r < n; ++r) {
     outs[r]->owner = in[r]->owner;
     take(outs[r]->p, res[r]);
+  }
+}
+
+// out[i] = sum_r rot(in[i], ks[r]) for every i (index 0 adds in[i] itself):
+// the rotations of one input share its ModUp and one ModDown, and up to 32
+// inputs go through each launch (all at one limb count; distinct indices)
+void hoisted_sum_batch(Context& c, const ckks_ct* const* in, int n, const int* ks, int R, std::vector<DevPoly>& res) {
+  res.assign(n, DevPoly());
+  if (n <= 0) return;
+  const int limbs = in[0]->p.limbs;
+  ckks::HoistKeys h{};
+  bool identity = false;
+  std::vector<uint32_t> seen;
+  for (int r = 0; r < R; ++r) {
+    const uint32_t g = c.galois(ks[r]);
+    if (std::find(seen.begin(), seen.end(), g) != seen.end())
+      throw Error(CKKS_EARG, "rotation indices of a hoisted sum must be distinct");
+    seen.push_back(g);
+    if (g == 1u) {
+      identity = true;
+      continue;
+    }
+    if (!c.switch_key(g, limbs))
+      throw Error(CKKS_EKEY, "rotation key not generated for index " + std::to_string(ks[r]));
+    if (h.R == ckks::kKsBatch) throw Error(CKKS_EARG, "hoisted sum of more than 32 rotations");
+    h.key[h.R] = c.switch_key(g, limbs);
+    h.g[h.R] = g;
+    ++h.R;
+  }
+  for (int i = 0; i < n; ++i) {
+    if (in[i]->p.limbs != limbs) throw Error(CKKS_ELEVEL, "batched rotation sums need one limb count");
+    res[i].ensure(&c, 2, limbs);
+    res[i].limbs = limbs;
+    res[i].scale = in[i]->p.scale;
+    res[i].deg = in[i]->p.deg;
+    if (!h.R) {
+      if (identity)
+        ckks::ew_binary(c, ckks::EwOp::Copy, in[i]->p.data, stride(in[i]->p), nullptr, 0, res[i].data,
+                        stride(res[i]), 2, limbs, c.stream);
+      else
+        CKKS_CUDA(cudaMemsetAsync(res[i].data, 0, sizeof(uint64_t) * stride(res[i]) * 2, c.stream));
+    }
+  }
+  if (!h.R) return;
+  for (int i0 = 0; i0 < n; i0 += ckks::kKsBatch) {
+    ckks::KsBatch b{};
+    b.M = std::min(ckks::kKsBatch, n - i0);
+    for (int m = 0; m < b.M; ++m) {
+      const ckks_ct* a = in[i0 + m];
+      b.d[m] = a->p.poly(1);
+      b.add0[m] = a->p.poly(0);
+      b.out0[m] = res[i0 + m].poly(0);
+      b.out1[m] = res[i0 + m].poly(1);
+    }
+    ckks::keyswitch_hoisted_sum(c, limbs, b, h, identity, c.stream);
   }
 }
 
@@ -1141,6 +1197,65 @@ int ckks_rotate_hoisted(ckks_ctx* ctx, const ckks_ct* a, const int* k, int count
   });
 }
 
+int ckks_rotate_sum_hoisted(ckks_ctx* ctx, const ckks_ct* const* in, int count, const int* k, int nk,
+                            ckks_ct* const* outs) {
+  return guard([&] {
+    Context& c = C(ctx);
+    need(count >= 0 && (count == 0 || (in && outs)), CKKS_EARG, "bad batch");
+    need(nk >= 1 && k, CKKS_EARG, "empty rotation list");
+    for (int i = 0; i < count; ++i) {
+      same_ctx(ctx, in[i]);
+      need(outs[i] && outs[i]->owner == ctx, CKKS_EARG, "bad output handle");
+    }
+    std::vector<DevPoly> res;
+    hoisted_sum_batch(c, in, count, k, nk, res);
+    for (int i = 0; i < count; ++i) take(outs[i]->p, res[i]);
+  });
+}
+
+int ckks_window_sum_batch(ckks_ctx* ctx, const ckks_ct* const* in, int count, int window, int stride_,
+                          ckks_ct* const* outs) {
+  return guard([&] {
+    Context& c = C(ctx);
+    need(count >= 0 && (count == 0 || (in && outs)), CKKS_EARG, "bad batch");
+    need(window >= 1, CKKS_EARG, "window must be positive");
+    for (int i = 0; i < count; ++i) {
+      same_ctx(ctx, in[i]);
+      need(outs[i] && outs[i]->owner == ctx, CKKS_EARG, "bad output handle");
+    }
+    if (!count) return;
+    // base-4 ladder: step s adds the rotations by stride * s * {1, 2, 3}
+    // (those below the window) to the running sums, hoisted per ciphertext
+    std::vector<ckks_ct> acc(count);
+    std::vector<const ckks_ct*> cur(in, in + count);
+    for (long step = 1; step < window; step *= 4) {
+      int ks[4] = {0, 0, 0, 0}, nk = 1;
+      for (int m = 1; m < 4 && step * m < window; ++m) ks[nk++] = (int)(stride_ * step * m);
+      std::vector<DevPoly> res;
+      hoisted_sum_batch(c, cur.data(), count, ks, nk, res);
+      for (int i = 0; i < count; ++i) {
+        acc[i].owner = ctx;
+        take(acc[i].p, res[i]);
+        cur[i] = &acc[i];
+      }
+    }
+    for (int i = 0; i < count; ++i) {
+      if (cur[i] == in[i]) {  // window 1: a copy
+        DevPoly cp;
+        cp.ensure(&c, 2, in[i]->p.limbs);
+        ckks::ew_binary(c, ckks::EwOp::Copy, in[i]->p.data, stride(in[i]->p), nullptr, 0, cp.data, stride(cp), 2,
+                        in[i]->p.limbs, c.stream);
+        cp.limbs = in[i]->p.limbs;
+        cp.scale = in[i]->p.scale;
+        cp.deg = in[i]->p.deg;
+        take(outs[i]->p, cp);
+      } else {
+        take(outs[i]->p, acc[i].p);
+      }
+    }
+  });
+}
+
 int ckks_accumulate_sum(ckks_ctx* ctx, const ckks_ct* a, int count, int stride_, ckks_ct* out) {
   return guard([&] {
     Context& c = C(ctx);
@@ -1177,6 +1292,37 @@ int ckks_profile_enable(ckks_ctx* ctx, int on) {
 
 int ckks_profile_reset(ckks_ctx* ctx) {
   return guard([&] { C(ctx).prof.reset(); });
+}
+
+int ckks_profile_sections(ckks_ctx* ctx, char* buf, size_t size) {
+  std::string js;
+  const int rc = guard([&] {
+    ckks::Profiler& p = C(ctx).prof;
+    p.report();
+    js = "{";
+    char tmp[256];
+    bool fs = true;
+    for (auto& sec : p.sections()) {
+      js += (fs ? "\"" : ", \"") + sec.first + "\": {";
+      fs = false;
+      bool first = true;
+      for (auto& kv : sec.second) {
+        std::snprintf(tmp, sizeof tmp, "%s\"%s\": {\"launches\": %ld, \"ms\": %.6f}", first ? "" : ", ",
+                      kv.first.c_str(), kv.second.launches, kv.second.ms);
+        js += tmp;
+        first = false;
+      }
+      js += "}";
+    }
+    js += "}";
+  });
+  if (rc != CKKS_OK) return -1;
+  if (buf && size) {
+    const size_t n = js.size() < size - 1 ? js.size() : size - 1;
+    std::memcpy(buf, js.data(), n);
+    buf[n] = 0;
+  }
+  return (int)js.size();
 }
 
 int ckks_profile_report(ckks_ctx* ctx, char* buf, size_t size) {

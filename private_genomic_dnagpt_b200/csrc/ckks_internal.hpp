@@ -110,9 +110,14 @@ class Profiler {
     double ms = 0.0;
     double bytes = 0.0;
   };
+  // launches are also totalled per section (a caller-named phase, e.g. a
+  // stage of a block evaluation)
+  std::string section;
   size_t begin(const char* name, double bytes, cudaStream_t st);
   void end(size_t idx, cudaStream_t st);
   std::map<std::string, Totals> report();  // synchronises pending events
+  // per section and kernel name; call after report()
+  const std::map<std::string, std::map<std::string, Totals>>& sections() const { return by_section_; }
   void reset();
   ~Profiler();
 
@@ -121,10 +126,12 @@ class Profiler {
     const char* name;
     double bytes;
     cudaEvent_t a, b;
+    std::string section;
   };
   std::vector<Rec> pending_;
   std::vector<cudaEvent_t> pool_;
   std::map<std::string, Totals> totals_;
+  std::map<std::string, std::map<std::string, Totals>> by_section_;
   cudaEvent_t get();
 };
 
@@ -332,6 +339,19 @@ void keyswitch_batch(const Context& c, int limbs, const KsBatch& b, bool shared_
 // acc1) + sum_m add1[m] (null addends skipped).  The giant steps of a BSGS
 // product: sum_g rot(inner_g, k_g).
 void keyswitch_sum(const Context& c, int limbs, const KsBatch& b, uint64_t* out0, uint64_t* out1, cudaStream_t st);
+// Rotation keys of a hoisted sum (R non-identity Galois elements)
+struct HoistKeys {
+  const uint64_t* key[kKsBatch];
+  uint32_t g[kKsBatch];
+  int R;
+};
+// For each of the M items (d = c1, add0 = c0, out0/out1): the sum of its R
+// rotations by h (plus the item itself when `identity`), with one ModUp per
+// item, the R key inner products added in the extended basis Q_l P and one
+// ModDown per item -- a rotation sum of one ciphertext, evaluated once for
+// a batch of ciphertexts.
+void keyswitch_hoisted_sum(const Context& c, int limbs, const KsBatch& b, const HoistKeys& h, bool identity,
+                           cudaStream_t st);
 
 // Batched rescale of M ciphertexts (c0, c1 pointers per item, `limbs` limbs
 // each) into outputs of limbs-1 limbs.

@@ -433,7 +433,7 @@ cudaEvent_t Profiler::get() {
 }
 
 size_t Profiler::begin(const char* name, double bytes, cudaStream_t st) {
-  Rec r{name, bytes, get(), get()};
+  Rec r{name, bytes, get(), get(), section};
   CKKS_CUDA(cudaEventRecord(r.a, st));
   pending_.push_back(r);
   return pending_.size() - 1;
@@ -452,10 +452,11 @@ std::map<std::string, Profiler::Totals> Profiler::report() {
       pool_.push_back(r.b);
       continue;
     }
-    Totals& t = totals_[r.name];
-    t.launches += 1;
-    t.ms += ms;
-    t.bytes += r.bytes;
+    for (Totals* t : {&totals_[r.name], &by_section_[r.section.empty() ? "-" : r.section][r.name]}) {
+      t->launches += 1;
+      t->ms += ms;
+      t->bytes += r.bytes;
+    }
     pool_.push_back(r.a);
     pool_.push_back(r.b);
   }
@@ -466,6 +467,7 @@ std::map<std::string, Profiler::Totals> Profiler::report() {
 void Profiler::reset() {
   report();
   totals_.clear();
+  by_section_.clear();
 }
 
 Profiler::~Profiler() {

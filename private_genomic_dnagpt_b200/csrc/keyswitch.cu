@@ -625,6 +625,92 @@ __global__ void __launch_bounds__(kThreads) rs_combine_batch_kernel(RsBatch b, c
   o[(size_t)i * N + n] = mul_shoup(sub_mod(a, t, q), iv.x, iv.y, q);
 }
 
+// hoisted sums: acc_m = sum_r sum_j ext_{m,j}[pi_r(n)] key_{r,j} -- the R
+// rotations of item m share its ModUp.  A thread owns one residue (n, t) of
+// kHoistItems items, so each key residue and automorphism index is loaded
+// once for them; 128-bit accumulators folded every `fold` products as in
+// ks_inner_sum_kernel.
+constexpr int kHoistItems = 4;
+__global__ void __launch_bounds__(kThreads) ks_inner_hoist_kernel(HoistKeys h, const uint64_t* __restrict__ ext_all,
+                                                                  uint64_t* __restrict__ acc_all, int M, int limbs,
+                                                                  int L, int K, int P, int beta, int logN, int fold,
+                                                                  const Mod* __restrict__ mods) {
+  const int N = 1 << logN;
+  const int n = blockIdx.x * kThreads + threadIdx.x;
+  if (n >= N) return;
+  const int t = blockIdx.y, m0 = blockIdx.z * kHoistItems;
+  const int E = limbs + K;
+  const int pt = t < limbs ? t : L + (t - limbs);
+  const Mod md = mods[pt];
+  const int cnt = min(kHoistItems, M - m0);
+  const size_t item = (size_t)beta * E * N;
+  const uint64_t* ext = ext_all + (size_t)m0 * item + (size_t)t * N;
+  U128 s0[kHoistItems], s1[kHoistItems];
+#pragma unroll
+  for (int i = 0; i < kHoistItems; ++i) s0[i] = s1[i] = U128{0, 0};
+  for (int r = 0; r < h.R; ++r) {
+    const uint32_t src = auto_index((uint32_t)n, h.g[r], logN);
+    const uint64_t* key = h.key[r];
+    for (int j = 0; j < beta; ++j) {
+      const uint64_t k0 = key[((size_t)j * 2 * P + pt) * N + n];
+      const uint64_t k1 = key[((size_t)j * 2 * P + P + pt) * N + n];
+      const uint64_t* ej = ext + (size_t)j * E * N + src;
+#pragma unroll
+      for (int i = 0; i < kHoistItems; ++i) {
+        if (i < cnt) {
+          const uint64_t v = ej[(size_t)i * item];
+          mac_wide(s0[i], v, k0);
+          mac_wide(s1[i], v, k1);
+        }
+      }
+    }
+    if ((r + 1) % fold == 0) {
+#pragma unroll
+      for (int i = 0; i < kHoistItems; ++i) {
+        s0[i] = U128{reduce128(s0[i], md), 0};
+        s1[i] = U128{reduce128(s1[i], md), 0};
+      }
+    }
+  }
+#pragma unroll
+  for (int i = 0; i < kHoistItems; ++i) {
+    if (i < cnt) {
+      uint64_t* acc = acc_all + (size_t)(m0 + i) * 2 * E * N;
+      acc[(size_t)t * N + n] = reduce128(s0[i], md);
+      acc[((size_t)E + t) * N + n] = reduce128(s1[i], md);
+    }
+  }
+}
+
+// (acc_m - conv_m) P^-1 plus sum_r pi_r(c0_m) (output 0), and the input
+// itself when the identity is part of the sum
+__global__ void __launch_bounds__(kThreads) moddown_combine_hoist_kernel(KsBatch b, HoistKeys h, bool identity,
+                                                                        const uint64_t* __restrict__ acc_all,
+                                                                        const uint64_t* __restrict__ conv_all,
+                                                                        int limbs, int K, int logN,
+                                                                        const Mod* __restrict__ mods,
+                                                                        const ulonglong2* __restrict__ pinv) {
+  const int N = 1 << logN;
+  const int n = blockIdx.x * kThreads + threadIdx.x;
+  if (n >= N) return;
+  const int t = blockIdx.y % limbs, p = blockIdx.y / limbs, m = blockIdx.z;
+  const int E = limbs + K;
+  const uint64_t q = mods[t].q;
+  const ulonglong2 pv = pinv[t];
+  const uint64_t a = acc_all[((size_t)(2 * m + p) * E + t) * N + n];
+  const uint64_t cv = conv_all[((size_t)(2 * m + p) * limbs + t) * N + n];
+  uint64_t r = mul_shoup(sub_mod(a, cv, q), pv.x, pv.y, q);
+  if (p == 0) {
+    const uint64_t* c0 = b.add0[m] + (size_t)t * N;
+    if (identity) r = add_mod(r, c0[n], q);
+    for (int k = 0; k < h.R; ++k) r = add_mod(r, c0[auto_index((uint32_t)n, h.g[k], logN)], q);
+    b.out0[m][(size_t)t * N + n] = r;
+  } else {
+    if (identity) r = add_mod(r, b.d[m][(size_t)t * N + n], q);
+    b.out1[m][(size_t)t * N + n] = r;
+  }
+}
+
 }  // namespace
 
 void keyswitch_batch(const Context& c, int limbs, const KsBatch& b, bool shared, cudaStream_t st) {
@@ -766,6 +852,83 @@ void keyswitch_sum(const Context& c, int limbs, const KsBatch& b, uint64_t* out0
     ProfScope ps(c, "moddown_combine_sum", (6.0 + M) * limbs * lb, st);
     moddown_combine_sum_kernel<<<dim3((N + kThreads - 1) / kThreads, 2 * limbs), kThreads, 0, st>>>(
         b, acc, conv, out0, out1, limbs, c.Kx(limbs), c.logN, c.d_mods, lt.d_down_pinv);
+  }
+  CKKS_CUDA(cudaGetLastError());
+  c.release(dc);
+  c.release(ext);
+  c.release(acc);
+  c.release(conv);
+}
+
+void keyswitch_hoisted_sum(const Context& c, int limbs, const KsBatch& b, const HoistKeys& h, bool identity,
+                           cudaStream_t st) {
+  if (c.alpha > kMaxAlpha || c.Kx(limbs) > kMaxK) throw Error(kErrArgument, "digit size above 16 is not supported");
+  const int M = b.M;
+  if (M <= 0) return;
+  if (M > kKsBatch) throw Error(kErrArgument, "hoisted-sum batch above 32");
+  if (h.R < 1 || h.R > kKsBatch) throw Error(kErrArgument, "hoisted sum of 1..32 rotations");
+  const int N = c.N, E = limbs + c.Kx(limbs);
+  const LevelTables& lt = c.lt(limbs);
+  const double lb = c.limb_bytes();
+  uint64_t* dc = (uint64_t*)c.alloc(sizeof(uint64_t) * (size_t)M * limbs * N);
+  uint64_t* ext = (uint64_t*)c.alloc(sizeof(uint64_t) * (size_t)M * lt.beta * E * N);
+  uint64_t* acc = (uint64_t*)c.alloc(sizeof(uint64_t) * (size_t)M * 2 * E * N);
+  uint64_t* conv = (uint64_t*)c.alloc(sizeof(uint64_t) * (size_t)M * 2 * limbs * N);
+  // one ModUp per item
+  {
+    ProfScope ps(c, "ks_gather", 2.0 * M * limbs * lb, st);
+    gather_kernel<<<dim3((N / 2 + kThreads - 1) / kThreads, limbs, M), kThreads, 0, st>>>(b, limbs, c.logN, dc);
+  }
+  ntt_inverse(c, dc, M * limbs, LimbMap::q(limbs, c.L), st, lt.d_up_scale_a, lt.d_up_scale_b);
+  const int min_cnt = limbs - (lt.beta - 1) * c.alpha;
+  const int nch_up = (E - min_cnt + kTargets - 1) / kTargets;
+  {
+    ProfScope ps(c, "modup_conv", M * (2.0 * limbs + (double)lt.beta * E) * lb, st);
+    auto kern = c.alpha <= 4 ? modup_conv_batch_kernel<4>
+                : c.alpha <= 8 ? modup_conv_batch_kernel<8>
+                : c.alpha <= 12 ? modup_conv_batch_kernel<12>
+                                : modup_conv_batch_kernel<16>;
+    kern<<<dim3((N / 2 + kThreads - 1) / kThreads, lt.beta * nch_up, M), kThreads, 0, st>>>(
+        b, dc, ext, limbs, c.L, c.Kx(limbs), c.alpha, lt.beta, c.logN, nch_up, c.d_mods, lt.d_up_hat);
+  }
+  CKKS_CUDA(cudaGetLastError());
+  {
+    LimbMap m = LimbMap::ext(limbs, c.Kx(limbs), c.L);
+    m.skip_alpha = c.alpha;
+    m.skip_beta = lt.beta;
+    ntt_forward(c, ext, M * lt.beta * E, m, st);
+  }
+  // the R key inner products of each item, summed
+  {
+    const int fold = 63 / lt.beta;
+    ProfScope ps(c, "ks_inner_hoist", (M * (lt.beta * (1.0 + 2.0 * h.R) + 2.0) * E + 2.0 * h.R * lt.beta * E) * lb,
+                 st);
+    ks_inner_hoist_kernel<<<dim3((N + kThreads - 1) / kThreads, E, (M + kHoistItems - 1) / kHoistItems), kThreads,
+                            0, st>>>(h, ext, acc, M, limbs, c.L, c.Kx(limbs), c.P, lt.beta, c.logN, fold, c.d_mods);
+  }
+  CKKS_CUDA(cudaGetLastError());
+  // one ModDown per item
+  {
+    LimbMap pm = LimbMap::ext(limbs, c.Kx(limbs), c.L);
+    pm.skip_q = 1;
+    ntt_inverse(c, acc, M * 2 * E, pm, st, c.down_scale_a(limbs), c.down_scale_b(limbs), c.L);
+  }
+  const int nch_dn = (limbs + kTargets - 1) / kTargets;
+  {
+    ProfScope ps(c, "moddown_conv", M * (2.0 * c.Kx(limbs) + 2.0 * limbs) * lb, st);
+    auto kern = c.Kx(limbs) <= 4 ? moddown_conv_batch_kernel<4>
+                : c.Kx(limbs) <= 8 ? moddown_conv_batch_kernel<8>
+                : c.Kx(limbs) <= 12 ? moddown_conv_batch_kernel<12>
+                            : moddown_conv_batch_kernel<16>;
+    kern<<<dim3((N / 2 + kThreads - 1) / kThreads, 2 * nch_dn, M), kThreads, 0, st>>>(
+        acc, conv, limbs, c.L, c.Kx(limbs), c.logN, nch_dn, c.d_mods, lt.d_down_phat);
+  }
+  CKKS_CUDA(cudaGetLastError());
+  ntt_forward(c, conv, M * 2 * limbs, LimbMap::q(limbs, c.L), st);
+  {
+    ProfScope ps(c, "moddown_combine_hoist", M * (6.0 + h.R + (identity ? 2.0 : 0.0)) * limbs * lb, st);
+    moddown_combine_hoist_kernel<<<dim3((N + kThreads - 1) / kThreads, 2 * limbs, M), kThreads, 0, st>>>(
+        b, h, identity, acc, conv, limbs, c.Kx(limbs), c.logN, c.d_mods, lt.d_down_pinv);
   }
   CKKS_CUDA(cudaGetLastError());
   c.release(dc);

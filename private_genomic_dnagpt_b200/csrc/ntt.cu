@@ -63,20 +63,49 @@ __device__ __forceinline__ void gs_bfly(uint64_t& x, uint64_t& y, ulonglong2 w, 
   y = mul_shoup_lazy(d, w.x, w.y, q);
 }
 
-template <int S_LOG, bool INV, bool STRIDED>
-__global__ void __launch_bounds__(kThreads) ntt_pass_kernel(uint64_t* __restrict__ data, PassArgs a) {
+// Lazy butterflies for primes below 2^kLazyBits: no correction inside a
+// pass.  Forward: the Shoup product is in [0, 2q) for any 64-bit input, so
+// every stage adds at most 2q to the bound (inputs < 4q: < 38q after 17
+// stages).  Inverse: the sum doubles the bound each stage and the difference
+// is offset by bq, a multiple of q at or above the current bound (inputs
+// < 2q: < 2^10 q after 9 stages); each pass ends with one Shoup reduction by
+// w = 1 (w' = floor(2^64/q), the high word of floor(2^128/q)) to [0, 2q).
+// The results are the canonical residues of the exact transform, as with
+// the corrected butterflies.
+constexpr int kLazyBits = 52;
+
+__device__ __forceinline__ void ct_bfly_lazy(uint64_t& x, uint64_t& y, ulonglong2 w, uint64_t q, uint64_t q2) {
+  const uint64_t t = mul_shoup_lazy(y, w.x, w.y, q);
+  const uint64_t a = x;
+  x = a + t;
+  y = a + q2 - t;
+}
+
+__device__ __forceinline__ void gs_bfly_lazy(uint64_t& x, uint64_t& y, ulonglong2 w, uint64_t q, uint64_t bq) {
+  const uint64_t s = x + y;
+  const uint64_t d = x + bq - y;
+  x = s;
+  y = mul_shoup_lazy(d, w.x, w.y, q);
+}
+
+// x mod q into [0, 2q) for any 64-bit x (Shoup product by 1)
+__device__ __forceinline__ uint64_t reduce_2q(uint64_t x, uint64_t q, uint64_t w1) {
+  return x - __umul64hi(x, w1) * q;
+}
+
+template <int S_LOG, bool INV, bool STRIDED, bool LAZY>
+__device__ __forceinline__ void ntt_pass_body(uint64_t* __restrict__ data, const PassArgs& a, uint64_t* sm) {
   constexpr int S = 1 << S_LOG;
   constexpr int T = S >= 8 ? S / 8 : 1;  // threads per sub-transform
   constexpr int NG = (S_LOG + 2) / 3;     // register stage groups
-  extern __shared__ uint64_t sm[];
 
   const int limb = blockIdx.y;
   const int prime = a.map.prime(limb);
-  if (a.map.skipped(limb)) return;
   const int N = 1 << a.logN;
   uint64_t* poly = data + (size_t)limb * N;
   const uint64_t q = a.mods[prime].q;
   const uint64_t q2 = 2 * q;
+  const uint64_t w1 = LAZY ? a.mods[prime].r1 : 0;  // floor(2^64 / q)
   const ulonglong2* tw = a.tw + (size_t)prime * N;
 
   const int tid = threadIdx.x;
@@ -106,6 +135,7 @@ __global__ void __launch_bounds__(kThreads) ntt_pass_kernel(uint64_t* __restrict
   };
 
   uint64_t x[8];
+  int done = 0;  // stages of this pass already applied (inverse lazy bound)
 
 #pragma unroll
   for (int step = 0; step < NG; ++step) {
@@ -134,11 +164,13 @@ __global__ void __launch_bounds__(kThreads) ntt_pass_kernel(uint64_t* __restrict
       uint64_t* xu = x + uj * usz;
 #pragma unroll
       for (int it = 0; it < 3; ++it) {
+        if (it >= G) break;
         const int rr = INV ? (G - 1 - it) : it;
-        if (rr < 0 || it >= G) break;
         const int st = st0 + rr;
         const int h = 1 << (G - 1 - rr);
         const bool final_stage = INV && STRIDED && st == 0;
+        // inverse lazy bound: inputs of this stage < 2^(done+it+1) q
+        const uint64_t bq = q2 << (done + it);
         const uint32_t idx0 = (1u << (gs0 + st)) + (prefix << st) + (B << rr);
         ulonglong2 w[4];
         if (!final_stage) {
@@ -151,21 +183,29 @@ __global__ void __launch_bounds__(kThreads) ntt_pass_kernel(uint64_t* __restrict
           if (k >= usz) break;
           if (k & h) continue;
           if (!INV) {
-            ct_bfly(xu[k], xu[k + h], w[k >> (G - rr)], q, q2);
+            if (LAZY)
+              ct_bfly_lazy(xu[k], xu[k + h], w[k >> (G - rr)], q, q2);
+            else
+              ct_bfly(xu[k], xu[k + h], w[k >> (G - rr)], q, q2);
           } else if (!final_stage) {
-            gs_bfly(xu[k], xu[k + h], w[k >> (G - rr)], q, q2);
+            if (LAZY)
+              gs_bfly_lazy(xu[k], xu[k + h], w[k >> (G - rr)], q, bq);
+            else
+              gs_bfly(xu[k], xu[k + h], w[k >> (G - rr)], q, q2);
           } else {
             const ulonglong2 c0 = a.scale_a ? __ldg(a.scale_a + (prime - a.scale_base)) : __ldg(a.ninv_last + prime);
             const ulonglong2 c1 = a.scale_b ? __ldg(a.scale_b + (prime - a.scale_base)) : __ldg(a.w1_ninv + prime);
             const uint64_t u0 = xu[k], v0 = xu[k + h];
+            const uint64_t off = LAZY ? bq : q2;
             const uint64_t s0 = mul_shoup_lazy(u0 + v0, c0.x, c0.y, q);
-            const uint64_t d0 = mul_shoup_lazy(u0 + q2 - v0, c1.x, c1.y, q);
+            const uint64_t d0 = mul_shoup_lazy(u0 + off - v0, c1.x, c1.y, q);
             xu[k] = s0 >= q ? s0 - q : s0;
             xu[k + h] = d0 >= q ? d0 - q : d0;
           }
         }
       }
     }
+    done += G;
     // store
     if (step + 1 < NG) {
       if (step > 0) __syncthreads();  // everyone has read the previous layout
@@ -184,15 +224,31 @@ __global__ void __launch_bounds__(kThreads) ntt_pass_kernel(uint64_t* __restrict
         const int uj = j / usz, k = j % usz;
         const int u = sub_t + uj * T;
         uint64_t v = x[j];
-        if (last_pass && !INV) {  // forward output: [0, 4q) -> [0, q)
-          v = v >= q2 ? v - q2 : v;
+        if (last_pass && !INV) {  // forward output -> [0, q)
+          if (LAZY) v = reduce_2q(v, q, w1);
+          else v = v >= q2 ? v - q2 : v;
           v = v >= q ? v - q : v;
+        } else if (LAZY && INV && !last_pass) {  // first inverse pass -> [0, 2q)
+          v = reduce_2q(v, q, w1);
         }
-        // inverse output of the final stage is already canonical
+        // inverse output of the final stage is already canonical; a forward
+        // first pass hands values < 4q + 2q S_LOG to the second
         poly[gaddr((u / D) * (D << G) + (u % D) + k * D)] = v;
       }
     }
   }
+}
+
+template <int S_LOG, bool INV, bool STRIDED>
+__global__ void __launch_bounds__(kThreads, 2) ntt_pass_kernel(uint64_t* __restrict__ data, PassArgs a) {
+  extern __shared__ uint64_t sm[];
+  const int limb = blockIdx.y;
+  if (a.map.skipped(limb)) return;
+  const uint64_t q = a.mods[a.map.prime(limb)].q;
+  if (q < (1ull << kLazyBits))
+    ntt_pass_body<S_LOG, INV, STRIDED, true>(data, a, sm);
+  else
+    ntt_pass_body<S_LOG, INV, STRIDED, false>(data, a, sm);
 }
 
 template <int S_LOG, bool INV, bool STRIDED>

@@ -235,6 +235,33 @@ def test_accumulate_sum_bit_exact(pair10, count, stride):
     assert np.array_equal(got.limbs_array(), o.accumulate_sum(rx, count, stride))
 
 
+@pytest.mark.parametrize("window,stride,limbs", [(64, 4, None), (16, 32, None), (64, 4, 2), (1, 4, 3)])
+def test_window_sums_bit_exact(pair10, window, stride, limbs):
+    """Batched hoisted window sums (three inputs per launch) against the
+    oracle's ladder of rotation sums."""
+    o, cc = pair10
+    lv = o.L if limbs is None else limbs
+    fs = [_fresh(o, cc, 40 + i, lv) for i in range(3)]
+    got = cc.WindowSumBatch([f[2] for f in fs], window, stride)
+    for f, g in zip(fs, got):
+        assert g.limbs == lv
+        assert np.array_equal(g.limbs_array(), o.window_sum(f[1], window, stride))
+
+
+def test_hoisted_rotation_sum_equals_the_rotation_sum(pair10):
+    o, cc = pair10
+    x, rx, cx = _fresh(o, cc, 44, o.L)
+    ks = [0, 4, 8, 12]
+    h = cc.EvalRotateSumHoisted([cx], ks)[0]
+    assert np.array_equal(h.limbs_array(), cc.EvalRotateSum([cx] * 4, ks).limbs_array())
+    assert np.array_equal(h.limbs_array(), o.rotate_sum(np.stack([rx] * 4), ks))
+    # without the identity
+    h2 = cc.EvalRotateSumHoisted([cx], [4, 8])[0]
+    assert np.array_equal(h2.limbs_array(), o.rotate_sum(np.stack([rx] * 2), [4, 8]))
+    with pytest.raises(eng.CKKSError):
+        cc.EvalRotateSumHoisted([cx], [4, 4])
+
+
 def test_errors_are_reported(pair10):
     o, cc = pair10
     x, rx, cx = _fresh(o, cc, 8, 3)

@@ -206,6 +206,26 @@ def test_mul_ct_sum_decrypts_to_the_sum_of_products(small):
 
 
 @pytest.mark.parametrize("count,stride", ACC_CASES)
+def test_window_sum_equals_the_ladder_of_rotation_sums(small, count, stride):
+    """The engine's window sums: the AccumulateSum slot values, each ladder
+    step one rotation sum over (acc, acc, acc, acc) with one ModDown."""
+    o = small
+    x = np.random.default_rng(6).uniform(-1, 1, o.N // 2)
+    S = o.scale(o.L)
+    ct = o.encrypt(o.encode(x, o.L), 9)
+    got = o.window_sum(ct, count, stride)
+    ref = sum(np.roll(x, -stride * k) for k in range(count))
+    assert np.abs(o.decode(o.decrypt(got), S) - ref).max() < 1e-7
+    acc = ct
+    step = 1
+    while step < count:
+        ks = [0] + [stride * step * m for m in range(1, 4) if step * m < count]
+        acc = o.rotate_sum(np.stack([acc] * len(ks)), ks)
+        step *= 4
+    assert np.array_equal(got, acc)
+
+
+@pytest.mark.parametrize("count,stride", ACC_CASES)
 def test_accumulate_sum(small, count, stride):
     o = small
     x = np.random.default_rng(5).uniform(-1, 1, o.N // 2)
