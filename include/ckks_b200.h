@@ -227,6 +227,8 @@ int ckks_window_sum_batch(ckks_ctx* ctx, const ckks_ct* const* in, int count, in
  * returns the length written (truncated to `size`) or -1. */
 int ckks_profile_enable(ckks_ctx* ctx, int on);
 int ckks_profile_reset(ckks_ctx* ctx);
+/* time only the launches of one kernel name (NULL or "" = every kernel) */
+int ckks_profile_only(ckks_ctx* ctx, const char* kernel);
 int ckks_profile_report(ckks_ctx* ctx, char* buf, size_t size);
 /* the same totals split by section (the block evaluation names its stages:
  * {"section": {"kernel": {"launches": n, "ms": t}}}), JSON text */

@@ -129,6 +129,7 @@ _SIGS = [
     ("ckks_profile_reset", ctypes.c_int, [_vp]),
     ("ckks_profile_report", ctypes.c_int, [_vp, ctypes.c_char_p, ctypes.c_size_t]),
     ("ckks_profile_sections", ctypes.c_int, [_vp, ctypes.c_char_p, ctypes.c_size_t]),
+    ("ckks_profile_only", ctypes.c_int, [_vp, ctypes.c_char_p]),
     ("ckks_ntt_forward_device", ctypes.c_int, [_vp, _vp, ctypes.c_int, ctypes.c_int]),
     ("ckks_rotate_noalloc", ctypes.c_int, [_vp, _vp, ctypes.c_int, ctypes.c_int, _vp]),
     ("ckks_block_create", ctypes.c_int, [_vp] + [_f64p] * 6 + [ctypes.c_int] * 4 + [ctypes.POINTER(_vp)]),
@@ -352,6 +353,10 @@ class CryptoContext:
         buf = ctypes.create_string_buffer(n + 1)
         lib().ckks_profile_report(self.h, buf, n + 1)
         return json.loads(buf.value.decode())
+
+    def profile_only(self, kernel: str | None):
+        """Time only launches of `kernel` (None: every kernel)."""
+        _check(lib().ckks_profile_only(self.h, (kernel or "").encode()))
 
     def profile_sections(self) -> dict:
         """Kernel totals per section (block stages) since the last reset."""

@@ -101,7 +101,7 @@ __global__ void __launch_bounds__(kThreads) diag_values_kernel(const double* __r
 // between groups (thread rows) did not pay: the kernel is bound by issue and
 // load latency of its 128-bit multiply-accumulates, not by the diagonal
 // traffic, so one group per launch keeps the most warps resident.
-constexpr int kMaxGroups = 1;
+constexpr int kMaxGroups = 4;
 struct BabyPtrs {
   const uint64_t* c0[kMaxGroups][kMaxBaby];
   const uint64_t* c1[kMaxGroups][kMaxBaby];
@@ -111,17 +111,53 @@ struct InnerPtrs {
   uint64_t* c1[kMaxGroups][kMaxBaby];
 };
 
+// Products of residues below kFpPrime are formed exactly in float64 (the
+// FP64 pipe sustains about twice the 64-bit integer multiply-add rate):
+// with d, b < q < 2^50.6 both exact doubles,
+//   hi = d*b (rounded), lo = fma(d, b, -hi)      d*b = hi + lo exactly, |lo| < 2^49
+//   k  = rint(hi / q) via fma(hi, 1/q, 1.5*2^52)  |k - d*b/q| < 1.05
+//   r  = fma(-k, q, hi) + lo                       exact, r = d*b mod q, |r| < 1.05 q
+// and sums of four such r (|sum| < 4.75 q < 2^53) are exact; each four
+// products the running sum is brought back to |acc| < 0.51 q the same way.
+constexpr uint64_t kFpPrime = (1ull << 50) + (1ull << 49);
+constexpr double kRoundMagic = 6755399441055744.0;  // 1.5 * 2^52
+
+__device__ __forceinline__ double fp_mod_product(double d, double b, double q, double qinv) {
+  const double hi = __dmul_rn(d, b);
+  const double lo = __fma_rn(d, b, -hi);
+  const double k = __dsub_rn(__fma_rn(hi, qinv, kRoundMagic), kRoundMagic);
+  return __dadd_rn(__fma_rn(-k, q, hi), lo);
+}
+
+__device__ __forceinline__ double fp_center(double acc, double q, double qinv) {
+  const double k = __dsub_rn(__fma_rn(acc, qinv, kRoundMagic), kRoundMagic);
+  return __fma_rn(-k, q, acc);
+}
+
+// |acc| < 0.51 q -> canonical residue
+__device__ __forceinline__ uint64_t fp_canonical(double acc, double q) {
+  return __double2ull_rn(acc < 0.0 ? __dadd_rn(acc, q) : acc);
+}
+
+// residue (< 2^52) -> the same integer as a double
+__device__ __forceinline__ double u2d(uint64_t v) {
+  return __dsub_rn(__longlong_as_double((long long)(v | 0x4330000000000000ull)), 4503599627370496.0);
+}
+
 // Encoded diagonals are stored tile-major, [limb][coefficient tile][diagonal]
 // [kThreads residues], so that one CTA of the product streams one contiguous
 // span: this transposes a chunk of plaintext-major encodings into place.
+// Limbs whose prime is below kFpPrime hold their residues as doubles.
 __global__ void __launch_bounds__(kThreads) diag_tile_kernel(const uint64_t* __restrict__ src, int cnt, int d0,
                                                              int ndiag, int limbs, int logN,
+                                                             const ckks::Mod* __restrict__ mods,
                                                              uint64_t* __restrict__ dst) {
   const int N = 1 << logN;
   const int ntiles = N / kThreads;
   const int tile = blockIdx.x, l = blockIdx.y, dd = blockIdx.z;
   if (dd >= cnt) return;
-  const uint64_t v = src[((size_t)dd * limbs + l) * N + (size_t)tile * kThreads + threadIdx.x];
+  uint64_t v = src[((size_t)dd * limbs + l) * N + (size_t)tile * kThreads + threadIdx.x];
+  if (mods[l].q < kFpPrime) v = (uint64_t)__double_as_longlong((double)v);
   dst[(((size_t)l * ntiles + tile) * ndiag + (d0 + dd)) * kThreads + threadIdx.x] = v;
 }
 
@@ -138,10 +174,10 @@ constexpr int kBsgsThreads = 128;
 __global__ void __launch_bounds__(kBsgsThreads * kMaxGroups) bsgs_inner_kernel(BabyPtrs babies, int ng, int n1,
                                                                                const uint64_t* __restrict__ diag,
                                                                                InnerPtrs out, int limbs, int logN,
-                                                                               int n2,
+                                                                               int n2, int l0,
                                                                                const ckks::Mod* __restrict__ mods) {
   const int N = 1 << logN;
-  const int g = blockIdx.x, tile = blockIdx.y, l = blockIdx.z;
+  const int g = blockIdx.x, tile = blockIdx.y, l = l0 + blockIdx.z;
   const int q = threadIdx.y;
   if (q >= ng) return;
   const int c = 2 * threadIdx.x;  // coefficient within the tile
@@ -161,6 +197,106 @@ __global__ void __launch_bounds__(kBsgsThreads * kMaxGroups) bsgs_inner_kernel(B
   const ckks::Mod m = mods[l];
   *reinterpret_cast<ulonglong2*>(out.c0[q][g] + off) = make_ulonglong2(ckks::reduce128(a00, m), ckks::reduce128(a01, m));
   *reinterpret_cast<ulonglong2*>(out.c1[q][g] + off) = make_ulonglong2(ckks::reduce128(a10, m), ckks::reduce128(a11, m));
+}
+
+// the same inner sums for a limb whose prime is below kFpPrime: diagonals
+// stored as doubles, babies converted on load, float64 products
+__global__ void __launch_bounds__(kBsgsThreads * kMaxGroups) bsgs_inner_fp_kernel(BabyPtrs babies, int ng, int n1,
+                                                                                  const uint64_t* __restrict__ diag,
+                                                                                  InnerPtrs out, int limbs, int logN,
+                                                                                  int n2, int l0,
+                                                                                  const ckks::Mod* __restrict__ mods) {
+  const int N = 1 << logN;
+  const int g = blockIdx.x, tile = blockIdx.y, l = l0 + blockIdx.z;
+  const int q = threadIdx.y;
+  if (q >= ng) return;
+  const int c = 2 * threadIdx.x;
+  const size_t off = (size_t)l * N + (size_t)tile * kThreads + c;
+  const int ndiag = n1 * n2;
+  const double* dtile = reinterpret_cast<const double*>(diag) +
+                        (((size_t)l * (N / kThreads) + tile) * ndiag + (size_t)g * n1) * kThreads + c;
+  const double qd = (double)mods[l].q, qinv = 1.0 / qd;
+  double a00 = 0.0, a01 = 0.0, a10 = 0.0, a11 = 0.0;
+  for (int j = 0; j < n1; ++j) {
+    const ulonglong2 b0 = *reinterpret_cast<const ulonglong2*>(babies.c0[q][j] + off);
+    const ulonglong2 b1 = *reinterpret_cast<const ulonglong2*>(babies.c1[q][j] + off);
+    const double2 dv = __ldg(reinterpret_cast<const double2*>(dtile + (size_t)j * kThreads));
+    a00 = __dadd_rn(a00, fp_mod_product(dv.x, u2d(b0.x), qd, qinv));
+    a01 = __dadd_rn(a01, fp_mod_product(dv.y, u2d(b0.y), qd, qinv));
+    a10 = __dadd_rn(a10, fp_mod_product(dv.x, u2d(b1.x), qd, qinv));
+    a11 = __dadd_rn(a11, fp_mod_product(dv.y, u2d(b1.y), qd, qinv));
+    if ((j & 3) == 3) {
+      a00 = fp_center(a00, qd, qinv);
+      a01 = fp_center(a01, qd, qinv);
+      a10 = fp_center(a10, qd, qinv);
+      a11 = fp_center(a11, qd, qinv);
+    }
+  }
+  a00 = fp_center(a00, qd, qinv);
+  a01 = fp_center(a01, qd, qinv);
+  a10 = fp_center(a10, qd, qinv);
+  a11 = fp_center(a11, qd, qinv);
+  *reinterpret_cast<ulonglong2*>(out.c0[q][g] + off) = make_ulonglong2(fp_canonical(a00, qd), fp_canonical(a01, qd));
+  *reinterpret_cast<ulonglong2*>(out.c1[q][g] + off) = make_ulonglong2(fp_canonical(a10, qd), fp_canonical(a11, qd));
+}
+
+// Float64 inner sums with the baby residues held in registers (as doubles):
+// kBsgsSplit lanes share one coefficient of one token group and one limb,
+// each holding n1 / kBsgsSplit of the babies, looping over the n2 giant steps
+// and streaming their diagonals (8-byte loads over the tile-major store); the
+// lanes' sums meet by shuffles once per giant step.  The CTAs of the token
+// groups of one tile are adjacent in the grid, so each diagonal tile comes
+// from HBM once and from L2 for the other groups, and no baby residue is
+// read twice.
+constexpr int kBsgsRegThreads = 128;
+constexpr int kBsgsSplit = 2;                                   // lanes per coefficient
+constexpr int kBsgsRegCoeffs = kBsgsRegThreads / kBsgsSplit;  // coefficients per CTA
+template <int NB>
+__global__ void __launch_bounds__(kBsgsRegThreads, 4) bsgs_inner_reg_kernel(BabyPtrs babies, int ng,
+                                                                              const uint64_t* __restrict__ diag,
+                                                                              InnerPtrs out, int logN, int n2, int l0,
+                                                                              const ckks::Mod* __restrict__ mods) {
+  constexpr int H = NB / kBsgsSplit;  // babies per lane
+  const int N = 1 << logN;
+  const int q = blockIdx.x % ng, part = blockIdx.x / ng;
+  const int tile = blockIdx.y, l = l0 + blockIdx.z;
+  const int half = threadIdx.x % kBsgsSplit;
+  const int c = part * kBsgsRegCoeffs + threadIdx.x / kBsgsSplit;  // coefficient within the tile
+  const size_t off = (size_t)l * N + (size_t)tile * kThreads + c;
+  double b0[H], b1[H];
+#pragma unroll
+  for (int j = 0; j < H; ++j) {
+    b0[j] = u2d(babies.c0[q][half * H + j][off]);
+    b1[j] = u2d(babies.c1[q][half * H + j][off]);
+  }
+  const double* dt = reinterpret_cast<const double*>(diag) +
+                     ((size_t)l * (N / kThreads) + tile) * (size_t)(NB * n2) * kThreads + (size_t)half * H * kThreads +
+                     c;
+  const double qd = (double)mods[l].q, qinv = 1.0 / qd;
+  for (int g = 0; g < n2; ++g) {
+    const double* dg = dt + (size_t)g * NB * kThreads;
+    double a0 = 0.0, a1 = 0.0;
+#pragma unroll
+    for (int j = 0; j < H; ++j) {
+      const double d = __ldg(dg + (size_t)j * kThreads);
+      a0 = __dadd_rn(a0, fp_mod_product(d, b0[j], qd, qinv));
+      a1 = __dadd_rn(a1, fp_mod_product(d, b1[j], qd, qinv));
+      if ((j & 3) == 3) {
+        a0 = fp_center(a0, qd, qinv);
+        a1 = fp_center(a1, qd, qinv);
+      }
+    }
+    // |a| < 0.51 q per lane: sums of up to eight lanes stay exact (< 4.1 q)
+#pragma unroll
+    for (int m = 1; m < kBsgsSplit; m <<= 1) {
+      a0 = __dadd_rn(a0, __shfl_xor_sync(0xffffffffu, a0, m));
+      a1 = __dadd_rn(a1, __shfl_xor_sync(0xffffffffu, a1, m));
+    }
+    if (half == 0)
+      out.c0[q][g][off] = fp_canonical(fp_center(a0, qd, qinv), qd);
+    else if (half == 1)
+      out.c1[q][g][off] = fp_canonical(fp_center(a1, qd, qinv), qd);
+  }
 }
 
 // ---- client-side float64 transforms, on the device ------------------------
@@ -648,7 +784,7 @@ struct ckks_block {
       {
         ckks::ProfScope ps(C, "diag_tile", 2.0 * cnt * stride * 8.0, C.stream);
         blk::diag_tile_kernel<<<dim3(C.N / blk::kThreads, limbs, cnt), blk::kThreads, 0, C.stream>>>(
-            enc, cnt, d0, nd, limbs, C.logN, dg.data);
+            enc, cnt, d0, nd, limbs, C.logN, C.d_mods, dg.data);
       }
       CKKS_CUDA(cudaGetLastError());
     }
@@ -710,9 +846,28 @@ struct ckks_block {
         ckks::ProfScope ps(
             C, "bsgs_inner",
             ((double)s.n1 * s.n2 * limbs + ng * (2.0 * s.n1 * limbs + 2.0 * s.n2 * limbs)) * C.limb_bytes(), C.stream);
-        const dim3 grid(s.n2, C.N / blk::kThreads, limbs);
-        blk::bsgs_inner_kernel<<<grid, dim3(blk::kBsgsThreads, ng), 0, C.stream>>>(bp, ng, s.n1, dg.data, ip, limbs,
-                                                                                   C.logN, s.n2, C.d_mods);
+        // runs of limbs with primes below kFpPrime take the float64
+        // products, the others (the 60-bit first prime) the integer ones
+        for (int l0 = 0; l0 < limbs;) {
+          const bool fp = C.moduli[l0] < blk::kFpPrime;
+          int l1 = l0 + 1;
+          while (l1 < limbs && (C.moduli[l1] < blk::kFpPrime) == fp) ++l1;
+          const dim3 grid(s.n2, C.N / blk::kThreads, l1 - l0);
+          if (fp && (s.n1 == 32 || s.n1 == 16 || s.n1 == 8)) {
+            static_assert(blk::kThreads % blk::kBsgsRegCoeffs == 0, "a tile of whole CTAs");
+            const dim3 rgrid(ng * (blk::kThreads / blk::kBsgsRegCoeffs), C.N / blk::kThreads, l1 - l0);
+            auto kern = s.n1 == 32   ? blk::bsgs_inner_reg_kernel<32>
+                        : s.n1 == 16 ? blk::bsgs_inner_reg_kernel<16>
+                                     : blk::bsgs_inner_reg_kernel<8>;
+            kern<<<rgrid, blk::kBsgsRegThreads, 0, C.stream>>>(bp, ng, dg.data, ip, C.logN, s.n2, l0, C.d_mods);
+          } else if (fp)
+            blk::bsgs_inner_fp_kernel<<<grid, dim3(blk::kBsgsThreads, ng), 0, C.stream>>>(
+                bp, ng, s.n1, dg.data, ip, limbs, C.logN, s.n2, l0, C.d_mods);
+          else
+            blk::bsgs_inner_kernel<<<grid, dim3(blk::kBsgsThreads, ng), 0, C.stream>>>(
+                bp, ng, s.n1, dg.data, ip, limbs, C.logN, s.n2, l0, C.d_mods);
+          l0 = l1;
+        }
       }
       CKKS_CUDA(cudaGetLastError());
       // giant steps: sum_g rot(inner_g, B n1 g), the key switches summed in the
@@ -772,6 +927,7 @@ std::vector<int> ckks_block::rotation_indices() const {
   for (int d = 1; d < s.B; ++d) {
     v.push_back(canon(d));
     v.push_back(canon(d - s.B));
+    v.push_back(canon((long)d * s.B));  // packing alignment d to feature h*HD - d (baby keys when n1 >= B)
   }
   for (long step = 1; step < s.HD; step *= 4)  // head window sums: the same ladder over HD features
     for (int m = 1; m < 4 && step * m < s.HD; ++m) v.push_back(canon((long)s.B * step * m));

@@ -1290,6 +1290,10 @@ int ckks_profile_enable(ckks_ctx* ctx, int on) {
   return guard([&] { C(ctx).prof.on = on != 0; });
 }
 
+int ckks_profile_only(ckks_ctx* ctx, const char* kernel) {
+  return guard([&] { C(ctx).prof.only = kernel ? kernel : ""; });
+}
+
 int ckks_profile_reset(ckks_ctx* ctx) {
   return guard([&] { C(ctx).prof.reset(); });
 }

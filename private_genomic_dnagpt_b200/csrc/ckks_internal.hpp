@@ -113,6 +113,10 @@ class Profiler {
   // launches are also totalled per section (a caller-named phase, e.g. a
   // stage of a block evaluation)
   std::string section;
+  // when set, only launches of this kernel name are timed (two events per
+  // launch cost host time; a filtered profile leaves the rest untouched)
+  std::string only;
+  bool wants(const char* name) const { return only.empty() || only == name; }
   size_t begin(const char* name, double bytes, cudaStream_t st);
   void end(size_t idx, cudaStream_t st);
   std::map<std::string, Totals> report();  // synchronises pending events
@@ -233,7 +237,7 @@ class Context {
 };
 
 inline ProfScope::ProfScope(const Context& c, const char* name, double bytes, cudaStream_t s)
-    : p(c.prof), st(s), on(c.prof.on) {
+    : p(c.prof), st(s), on(c.prof.on && c.prof.wants(name)) {
   if (on) idx = p.begin(name, bytes, s);
 }
 inline ProfScope::~ProfScope() {

@@ -51,3 +51,21 @@ def test_block_matches_plaintext_oracle(ctx, tokens):
     assert c["weight_tile_encryptions"] == alignments
     if tokens == 103:
         assert (c["score_tile_decryptions"], c["weight_tile_encryptions"]) == (10, 295)
+
+
+@pytest.mark.parametrize("log_n,d,heads,mlp", [(13, 128, 2, 256), (14, 256, 4, 512)])
+def test_block_on_smaller_rings(log_n, d, heads, mlp):
+    """Fewer slots per ciphertext: 8 (N = 2^13) and 16 (N = 2^14) baby steps
+    per product instead of 32."""
+    cc = eng.GenCryptoContext(eng.CCParams(ring_dim_log=log_n, limbs=24, dnum=3, seed=43))
+    cc.KeyGen()
+    cc.EvalMultKeyGen()
+    tokens = 40
+    w = plain_block.synthetic_weights(7, d=d, mlp=mlp)
+    x = plain_block.synthetic_input(8, tokens, d=d)
+    blk = eng.EncryptedBlock(cc, w, tokens, heads=heads)
+    cc.EvalRotateKeyGen(blk.rotation_indices())
+    y = blk.forward(x)
+    err = plain_block.rel_inf(plain_block.block(x, w, heads=heads), y)
+    print(f"N=2^{log_n} D={d}: rel_inf {err:.3e}")
+    assert np.isfinite(y).all() and err < 1e-6
