@@ -167,6 +167,8 @@ class Context {
   Mod* d_mods = nullptr;            // [P]
   ulonglong2* d_tw = nullptr;       // [P][N] forward (w, w')
   ulonglong2* d_itw = nullptr;      // [P][N] inverse (w, w')
+  double2* d_twd = nullptr;         // [P][N] forward (w, fl(w/q)) as doubles (primes below 2^50.3)
+  double2* d_itwd = nullptr;        // [P][N] inverse, the same
   ulonglong2* d_ninv = nullptr;     // [P]
   ulonglong2* d_w1ninv = nullptr;   // [P]
   ulonglong2* d_pmod = nullptr;     // [P] P mod q_t (Shoup pair), 0 for special primes

@@ -201,6 +201,7 @@ Context::Context(const Params& p) : params(p) {
 
   std::vector<Mod> mods(P);
   std::vector<ulonglong2> tw((size_t)P * N), itw((size_t)P * N), ninv(P), w1ninv(P), pmod(P);
+  std::vector<double2> twd((size_t)P * N), itwd((size_t)P * N);
   psi.resize(P);
   for (int i = 0; i < P; ++i) {
     const uint64_t q = moduli[i];
@@ -221,6 +222,9 @@ Context::Context(const Params& p) : params(p) {
     for (int j = 0; j < N; ++j) {
       tw[(size_t)i * N + j] = shoup_pair(w[j], q);
       itw[(size_t)i * N + j] = shoup_pair(wi[j], q);
+      // float64 twiddles (exact for the primes below 2^53 that use them)
+      twd[(size_t)i * N + j] = make_double2((double)w[j], (double)w[j] / (double)q);
+      itwd[(size_t)i * N + j] = make_double2((double)wi[j], (double)wi[j] / (double)q);
     }
     const uint64_t ni = invm((uint64_t)N, q);
     ninv[i] = shoup_pair(ni, q);
@@ -232,6 +236,8 @@ Context::Context(const Params& p) : params(p) {
   d_mods = upload(mods);
   d_tw = upload(tw);
   d_itw = upload(itw);
+  d_twd = upload(twd);
+  d_itwd = upload(itwd);
   d_ninv = upload(ninv);
   d_w1ninv = upload(w1ninv);
   d_pmod = upload(pmod);
@@ -412,6 +418,8 @@ Context::~Context() {
   cudaFree(d_mods);
   cudaFree(d_tw);
   cudaFree(d_itw);
+  cudaFree(d_twd);
+  cudaFree(d_itwd);
   cudaFree(d_ninv);
   cudaFree(d_w1ninv);
   cudaFree(d_pmod);

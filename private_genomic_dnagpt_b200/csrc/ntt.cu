@@ -27,6 +27,7 @@ constexpr int kThreads = 512;
 
 struct PassArgs {
   const ulonglong2* tw;  // [P][N] (w, w'), forward or inverse table
+  const double2* twd;    // [P][N] (w, fl(w / q)) as doubles, the same twiddles
   const Mod* mods;
   const ulonglong2* ninv_last;  // [P] (n^-1, shoup) ; inverse only
   const ulonglong2* w1_ninv;    // [P] (Winv[1] * n^-1, shoup) ; inverse only
@@ -39,6 +40,15 @@ struct PassArgs {
   int logN;
   int per_cta;  // columns (strided) or blocks (contiguous) per CTA
 };
+
+// Shared-memory slot of residue r in a contiguous block: the low four bits
+// are XORed with a function of bits 4-6, so that each half-warp's 64-bit
+// accesses of all three register-group layouts of a 256-point block fall in
+// 16 distinct bank pairs (a bijection on every aligned 16 residues).
+__device__ __forceinline__ int swizzle(int r) {
+  const int h = r >> 4;
+  return (h & 1) ^ (((h >> 1) & 1) * 6) ^ (((h >> 2) & 1) * 8);
+}
 
 __device__ __forceinline__ int group_size(int s_log, int gi) {
   const int rem = s_log - 3 * gi;
@@ -63,37 +73,7 @@ __device__ __forceinline__ void gs_bfly(uint64_t& x, uint64_t& y, ulonglong2 w, 
   y = mul_shoup_lazy(d, w.x, w.y, q);
 }
 
-// Lazy butterflies for primes below 2^kLazyBits: no correction inside a
-// pass.  Forward: the Shoup product is in [0, 2q) for any 64-bit input, so
-// every stage adds at most 2q to the bound (inputs < 4q: < 38q after 17
-// stages).  Inverse: the sum doubles the bound each stage and the difference
-// is offset by bq, a multiple of q at or above the current bound (inputs
-// < 2q: < 2^10 q after 9 stages); each pass ends with one Shoup reduction by
-// w = 1 (w' = floor(2^64/q), the high word of floor(2^128/q)) to [0, 2q).
-// The results are the canonical residues of the exact transform, as with
-// the corrected butterflies.
-constexpr int kLazyBits = 52;
-
-__device__ __forceinline__ void ct_bfly_lazy(uint64_t& x, uint64_t& y, ulonglong2 w, uint64_t q, uint64_t q2) {
-  const uint64_t t = mul_shoup_lazy(y, w.x, w.y, q);
-  const uint64_t a = x;
-  x = a + t;
-  y = a + q2 - t;
-}
-
-__device__ __forceinline__ void gs_bfly_lazy(uint64_t& x, uint64_t& y, ulonglong2 w, uint64_t q, uint64_t bq) {
-  const uint64_t s = x + y;
-  const uint64_t d = x + bq - y;
-  x = s;
-  y = mul_shoup_lazy(d, w.x, w.y, q);
-}
-
-// x mod q into [0, 2q) for any 64-bit x (Shoup product by 1)
-__device__ __forceinline__ uint64_t reduce_2q(uint64_t x, uint64_t q, uint64_t w1) {
-  return x - __umul64hi(x, w1) * q;
-}
-
-template <int S_LOG, bool INV, bool STRIDED, bool LAZY>
+template <int S_LOG, bool INV, bool STRIDED>
 __device__ __forceinline__ void ntt_pass_body(uint64_t* __restrict__ data, const PassArgs& a, uint64_t* sm) {
   constexpr int S = 1 << S_LOG;
   constexpr int T = S >= 8 ? S / 8 : 1;  // threads per sub-transform
@@ -105,7 +85,6 @@ __device__ __forceinline__ void ntt_pass_body(uint64_t* __restrict__ data, const
   uint64_t* poly = data + (size_t)limb * N;
   const uint64_t q = a.mods[prime].q;
   const uint64_t q2 = 2 * q;
-  const uint64_t w1 = LAZY ? a.mods[prime].r1 : 0;  // floor(2^64 / q)
   const ulonglong2* tw = a.tw + (size_t)prime * N;
 
   const int tid = threadIdx.x;
@@ -131,11 +110,10 @@ __device__ __forceinline__ void ntt_pass_body(uint64_t* __restrict__ data, const
     return STRIDED ? (size_t)r * stride + sub_global : (size_t)sub_global * S + r;
   };
   auto saddr = [&](int r) -> int {
-    return STRIDED ? r * per + lane_idx : lane_idx * (S + S / 16) + r + (r >> 4);
+    return STRIDED ? r * per + lane_idx : lane_idx * S + (r ^ swizzle(r));
   };
 
   uint64_t x[8];
-  int done = 0;  // stages of this pass already applied (inverse lazy bound)
 
 #pragma unroll
   for (int step = 0; step < NG; ++step) {
@@ -169,8 +147,6 @@ __device__ __forceinline__ void ntt_pass_body(uint64_t* __restrict__ data, const
         const int st = st0 + rr;
         const int h = 1 << (G - 1 - rr);
         const bool final_stage = INV && STRIDED && st == 0;
-        // inverse lazy bound: inputs of this stage < 2^(done+it+1) q
-        const uint64_t bq = q2 << (done + it);
         const uint32_t idx0 = (1u << (gs0 + st)) + (prefix << st) + (B << rr);
         ulonglong2 w[4];
         if (!final_stage) {
@@ -183,29 +159,21 @@ __device__ __forceinline__ void ntt_pass_body(uint64_t* __restrict__ data, const
           if (k >= usz) break;
           if (k & h) continue;
           if (!INV) {
-            if (LAZY)
-              ct_bfly_lazy(xu[k], xu[k + h], w[k >> (G - rr)], q, q2);
-            else
-              ct_bfly(xu[k], xu[k + h], w[k >> (G - rr)], q, q2);
+            ct_bfly(xu[k], xu[k + h], w[k >> (G - rr)], q, q2);
           } else if (!final_stage) {
-            if (LAZY)
-              gs_bfly_lazy(xu[k], xu[k + h], w[k >> (G - rr)], q, bq);
-            else
-              gs_bfly(xu[k], xu[k + h], w[k >> (G - rr)], q, q2);
+            gs_bfly(xu[k], xu[k + h], w[k >> (G - rr)], q, q2);
           } else {
             const ulonglong2 c0 = a.scale_a ? __ldg(a.scale_a + (prime - a.scale_base)) : __ldg(a.ninv_last + prime);
             const ulonglong2 c1 = a.scale_b ? __ldg(a.scale_b + (prime - a.scale_base)) : __ldg(a.w1_ninv + prime);
             const uint64_t u0 = xu[k], v0 = xu[k + h];
-            const uint64_t off = LAZY ? bq : q2;
             const uint64_t s0 = mul_shoup_lazy(u0 + v0, c0.x, c0.y, q);
-            const uint64_t d0 = mul_shoup_lazy(u0 + off - v0, c1.x, c1.y, q);
+            const uint64_t d0 = mul_shoup_lazy(u0 + q2 - v0, c1.x, c1.y, q);
             xu[k] = s0 >= q ? s0 - q : s0;
             xu[k + h] = d0 >= q ? d0 - q : d0;
           }
         }
       }
     }
-    done += G;
     // store
     if (step + 1 < NG) {
       if (step > 0) __syncthreads();  // everyone has read the previous layout
@@ -224,15 +192,190 @@ __device__ __forceinline__ void ntt_pass_body(uint64_t* __restrict__ data, const
         const int uj = j / usz, k = j % usz;
         const int u = sub_t + uj * T;
         uint64_t v = x[j];
-        if (last_pass && !INV) {  // forward output -> [0, q)
-          if (LAZY) v = reduce_2q(v, q, w1);
-          else v = v >= q2 ? v - q2 : v;
+        if (last_pass && !INV) {  // forward output: [0, 4q) -> [0, q)
+          v = v >= q2 ? v - q2 : v;
           v = v >= q ? v - q : v;
-        } else if (LAZY && INV && !last_pass) {  // first inverse pass -> [0, 2q)
-          v = reduce_2q(v, q, w1);
         }
-        // inverse output of the final stage is already canonical; a forward
-        // first pass hands values < 4q + 2q S_LOG to the second
+        // inverse output of the final stage is already canonical
+        poly[gaddr((u / D) * (D << G) + (u % D) + k * D)] = v;
+      }
+    }
+  }
+}
+
+// Float64 butterflies for primes below kFpNttPrime.  Residues are signed
+// doubles; the twiddle product of y by (w, wq = fl(w/q)) is exact:
+//   k = rint(y wq) (the 1.5 * 2^52 rounding, valid while |y wq| < 2^51),
+//   r = fma(-k, q, y*w) + fma(y, w, -y*w)  = y w - k q,  |r| < 0.52 q,
+// with |y| < 1.6 q; the bounds per stage within a register group of three
+// stages, from inputs centred to |x| <= 0.51 q:
+//   forward  x' = x + r, y' = x - r: the multiplied input of stages 1-3 is
+//            below 0.51, 1.03, 1.55 q; all values stay below 2.1 q;
+//   inverse  x' = x + y, y' = (x - y) w: the difference is re-centred before
+//            the product from the group's second stage on; values stay below
+//            2.1 q.
+// Every group ends by re-centring all values (k = rint(x / q), x - k q), so
+// each pass hands on |x| <= 0.51 q; the transform's output is the canonical
+// residue, as on the integer path.
+constexpr uint64_t kFpNttPrime = (1ull << 50) + (1ull << 48);
+constexpr double kFpMagic = 6755399441055744.0;  // 1.5 * 2^52
+
+__device__ __forceinline__ double fp_center(double x, double q, double qinv) {
+  const double k = __dsub_rn(__fma_rn(x, qinv, kFpMagic), kFpMagic);
+  return __fma_rn(-k, q, x);
+}
+
+__device__ __forceinline__ double fp_mulw(double y, double2 w, double q) {
+  const double k = __dsub_rn(__fma_rn(y, w.y, kFpMagic), kFpMagic);
+  const double hi = __dmul_rn(y, w.x);
+  const double lo = __fma_rn(y, w.x, -hi);
+  return __dadd_rn(__fma_rn(-k, q, hi), lo);
+}
+
+// |x| <= 0.51 q -> canonical residue
+__device__ __forceinline__ uint64_t fp_to_residue(double x, double q) {
+  return __double2ull_rn(x < 0.0 ? __dadd_rn(x, q) : x);
+}
+
+template <int S_LOG, bool INV, bool STRIDED>
+__device__ __forceinline__ void ntt_pass_body_fp(uint64_t* __restrict__ data, const PassArgs& a, uint64_t* sm) {
+  constexpr int S = 1 << S_LOG;
+  constexpr int T = S >= 8 ? S / 8 : 1;
+  constexpr int NG = (S_LOG + 2) / 3;
+
+  const int limb = blockIdx.y;
+  const int prime = a.map.prime(limb);
+  const int N = 1 << a.logN;
+  uint64_t* poly = data + (size_t)limb * N;
+  const uint64_t qi = a.mods[prime].q;
+  const double q = (double)qi, qinv = 1.0 / q;
+  const double2* tw = a.twd + (size_t)prime * N;
+
+  const int tid = threadIdx.x;
+  const int per = a.per_cta;
+  int sub_t, lane_idx;
+  if (STRIDED) {
+    lane_idx = tid % per;
+    sub_t = tid / per;
+  } else {
+    lane_idx = tid / T;
+    sub_t = tid % T;
+  }
+  const int sub_global = blockIdx.x * per + lane_idx;
+  const int stride = N >> S_LOG;
+  const int gs0 = STRIDED ? 0 : (a.logN - S_LOG);
+  const uint32_t prefix = STRIDED ? 0u : (uint32_t)sub_global;
+  const bool first_pass = (STRIDED != INV);
+
+  auto gaddr = [&](int r) -> size_t {
+    return STRIDED ? (size_t)r * stride + sub_global : (size_t)sub_global * S + r;
+  };
+  auto saddr = [&](int r) -> int {
+    return STRIDED ? r * per + lane_idx : lane_idx * S + (r ^ swizzle(r));
+  };
+
+  double x[8];
+
+#pragma unroll
+  for (int step = 0; step < NG; ++step) {
+    const int gi = INV ? (NG - 1 - step) : step;
+    const int G = group_size(S_LOG, gi);
+    const int st0 = 3 * gi;
+    const int D = S >> (st0 + G);
+    const int units_per_thread = 8 >> G;
+    const int usz = 1 << G;
+    // load: the transform's input as residues, the first pass's output and
+    // the exchanges as centred doubles
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      if (j >= units_per_thread * usz) break;
+      const int uj = j / usz, k = j % usz;
+      const int u = sub_t + uj * T;
+      const int r = (u / D) * (D << G) + (u % D) + k * D;
+      if (step > 0) {
+        x[j] = __longlong_as_double((long long)sm[saddr(r)]);
+      } else if (first_pass) {
+        x[j] = fp_center(__ull2double_rn(poly[gaddr(r)]), q, qinv);
+      } else {
+        x[j] = __longlong_as_double((long long)poly[gaddr(r)]);
+      }
+    }
+    bool final_done = false;
+#pragma unroll
+    for (int uj = 0; uj < 8; ++uj) {
+      if (uj >= units_per_thread) break;
+      const int u = sub_t + uj * T;
+      const uint32_t B = (uint32_t)(u / D);
+      double* xu = x + uj * usz;
+#pragma unroll
+      for (int it = 0; it < 3; ++it) {
+        if (it >= G) break;
+        const int rr = INV ? (G - 1 - it) : it;
+        const int st = st0 + rr;
+        const int h = 1 << (G - 1 - rr);
+        const bool final_stage = INV && STRIDED && st == 0;
+        const uint32_t idx0 = (1u << (gs0 + st)) + (prefix << st) + (B << rr);
+        double2 w[4];
+        if (!final_stage) {
+#pragma unroll
+          for (int j = 0; j < 4; ++j)
+            if (j < (1 << rr)) w[j] = __ldg(tw + idx0 + j);
+        }
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+          if (k >= usz) break;
+          if (k & h) continue;
+          if (!INV) {
+            const double t = fp_mulw(xu[k + h], w[k >> (G - rr)], q);
+            const double x0 = xu[k];
+            xu[k] = __dadd_rn(x0, t);
+            xu[k + h] = __dsub_rn(x0, t);
+          } else if (!final_stage) {
+            const double x0 = xu[k], y0 = xu[k + h];
+            double d = __dsub_rn(x0, y0);
+            if (it > 0) d = fp_center(d, q, qinv);
+            xu[k] = __dadd_rn(x0, y0);
+            xu[k + h] = fp_mulw(d, w[k >> (G - rr)], q);
+          } else {
+            // last inverse stage on canonical residues with the integer
+            // Shoup constants (n^-1 or the caller's scale folded in)
+            const ulonglong2 c0 = a.scale_a ? __ldg(a.scale_a + (prime - a.scale_base)) : __ldg(a.ninv_last + prime);
+            const ulonglong2 c1 = a.scale_b ? __ldg(a.scale_b + (prime - a.scale_base)) : __ldg(a.w1_ninv + prime);
+            const uint64_t u0 = fp_to_residue(fp_center(xu[k], q, qinv), q);
+            const uint64_t v0 = fp_to_residue(fp_center(xu[k + h], q, qinv), q);
+            const uint64_t s0 = mul_shoup_lazy(u0 + v0, c0.x, c0.y, qi);
+            const uint64_t d0 = mul_shoup_lazy(u0 + 2 * qi - v0, c1.x, c1.y, qi);
+            xu[k] = __longlong_as_double((long long)(s0 >= qi ? s0 - qi : s0));
+            xu[k + h] = __longlong_as_double((long long)(d0 >= qi ? d0 - qi : d0));
+            final_done = true;
+          }
+        }
+      }
+    }
+    // store
+    if (step + 1 < NG) {
+      if (step > 0) __syncthreads();
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        if (j >= units_per_thread * usz) break;
+        const int uj = j / usz, k = j % usz;
+        const int u = sub_t + uj * T;
+        sm[saddr((u / D) * (D << G) + (u % D) + k * D)] = (uint64_t)__double_as_longlong(fp_center(x[j], q, qinv));
+      }
+      __syncthreads();
+    } else {
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        if (j >= units_per_thread * usz) break;
+        const int uj = j / usz, k = j % usz;
+        const int u = sub_t + uj * T;
+        uint64_t v;
+        if (final_done) {  // inverse: canonical residues already
+          v = (uint64_t)__double_as_longlong(x[j]);
+        } else {
+          const double c = fp_center(x[j], q, qinv);
+          v = first_pass ? (uint64_t)__double_as_longlong(c) : fp_to_residue(c, q);
+        }
         poly[gaddr((u / D) * (D << G) + (u % D) + k * D)] = v;
       }
     }
@@ -245,10 +388,10 @@ __global__ void __launch_bounds__(kThreads, 2) ntt_pass_kernel(uint64_t* __restr
   const int limb = blockIdx.y;
   if (a.map.skipped(limb)) return;
   const uint64_t q = a.mods[a.map.prime(limb)].q;
-  if (q < (1ull << kLazyBits))
-    ntt_pass_body<S_LOG, INV, STRIDED, true>(data, a, sm);
+  if (q < kFpNttPrime)
+    ntt_pass_body_fp<S_LOG, INV, STRIDED>(data, a, sm);
   else
-    ntt_pass_body<S_LOG, INV, STRIDED, false>(data, a, sm);
+    ntt_pass_body<S_LOG, INV, STRIDED>(data, a, sm);
 }
 
 template <int S_LOG, bool INV, bool STRIDED>
@@ -263,8 +406,7 @@ void launch_pass(uint64_t* data, int nlimbs, const PassArgs& a0, cudaStream_t st
   a.per_cta = per;
   const dim3 grid(subs / per, nlimbs);
   const int threads = per * T;
-  const size_t smem = STRIDED ? (size_t)S * per * sizeof(uint64_t)
-                              : (size_t)per * (S + S / 16) * sizeof(uint64_t);
+  const size_t smem = (size_t)S * per * sizeof(uint64_t);
   auto k = ntt_pass_kernel<S_LOG, INV, STRIDED>;
   if (smem > 48 * 1024) cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   k<<<grid, threads, smem, st>>>(data, a);
@@ -300,6 +442,7 @@ void ntt_forward(const Context& c, uint64_t* data, int nlimbs, LimbMap map, cuda
   const double bytes = live_limbs(map, nlimbs) * c.limb_bytes();
   PassArgs a{};
   a.tw = c.d_tw;
+  a.twd = c.d_twd;
   a.mods = c.d_mods;
   a.map = map;
   a.logN = c.logN;
@@ -321,6 +464,7 @@ void ntt_inverse(const Context& c, uint64_t* data, int nlimbs, LimbMap map, cuda
   const double bytes = live_limbs(map, nlimbs) * c.limb_bytes();
   PassArgs a{};
   a.tw = c.d_itw;
+  a.twd = c.d_itwd;
   a.mods = c.d_mods;
   a.ninv_last = c.d_ninv;
   a.w1_ninv = c.d_w1ninv;
