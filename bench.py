@@ -220,13 +220,19 @@ def run_engine(args):
         import torch.distributed as dist
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600))
 
-    cc = eng.GenCryptoContext(eng.CCParams(ring_dim_log=LOG_N, limbs=LIMBS, dnum=DNUM, seed=1 + rank,
+    # a smaller ring only for profiler captures: the block shrunk to fit its
+    # slots (D = N / 64 up to 768, 64-feature heads, MLP 4 D)
+    d_model, heads, mlp = plain_block.D, plain_block.HEADS, plain_block.MLP
+    if args.logn != LOG_N:
+        d_model = min(plain_block.D, (1 << args.logn) // 64)
+        heads, mlp = d_model // 64, 4 * d_model
+    cc = eng.GenCryptoContext(eng.CCParams(ring_dim_log=args.logn, limbs=LIMBS, dnum=DNUM, seed=1 + rank,
                                            device=local))
     cc.KeyGen()
     cc.EvalMultKeyGen()
-    w = plain_block.synthetic_weights(5)
-    x = plain_block.synthetic_input(6, args.tokens)
-    block = eng.EncryptedBlock(cc, w, args.tokens)
+    w = plain_block.synthetic_weights(5, d=d_model, mlp=mlp)
+    x = plain_block.synthetic_input(6, args.tokens, d=d_model)
+    block = eng.EncryptedBlock(cc, w, args.tokens, heads=heads)
     cc.EvalRotateKeyGen(sorted(set(block.rotation_indices()) | set(ROT_INDICES)))
     stream = torch.cuda.ExternalStream(cc.stream_handle())
 
@@ -242,7 +248,7 @@ def run_engine(args):
     # steps time only the dominant kernel's launches, for the roofline, so
     # that the per-launch event records of the others stay out of the
     # headline number.
-    ref = plain_block.block(x, w)
+    ref = plain_block.block(x, w, heads=heads)
     for i in range(args.warmup):
         if i == args.warmup - 1:
             barrier()
@@ -327,7 +333,7 @@ def run_engine(args):
         achieved = (d["bytes"] / d["launches"]) / (per_launch_ms / 1e3) / 1e9
         traffic = None
         if name in NCU_TRAFFIC_PER_LIMB:  # limbs per launch x measured bytes per limb
-            limbs_per_launch = d["bytes"] / d["launches"] / (8.0 * (1 << LOG_N))
+            limbs_per_launch = d["bytes"] / d["launches"] / (8.0 * (1 << args.logn))
             traffic = NCU_TRAFFIC_PER_LIMB[name] * limbs_per_launch
         roof = {"kernel": name, "bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                 "frac": achieved / peak, "traffic": traffic, "peak_kind": peak_kind,
@@ -354,6 +360,10 @@ def run_engine(args):
         if args.tokens != TOKENS:  # profiler captures on a smaller case
             metric = METRIC.replace(f"@{TOKENS} tok", f"@{args.tokens} tok")
             workload = WORKLOAD.replace(f"{TOKENS} tokens", f"{args.tokens} tokens")
+        if args.logn != LOG_N:
+            metric = metric.replace(f"N=2^{LOG_N}", f"N=2^{args.logn}")
+            workload = (workload.replace(f"N=2^{LOG_N}", f"N=2^{args.logn}")
+                        .replace("D=768, 12 heads, MLP 3072", f"D={d_model}, {heads} heads, MLP {mlp}"))
         line = {
             "metric": metric, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": e2e_ms, "higher_is_better": False,
@@ -370,7 +380,9 @@ def run_engine(args):
                       "e2e_s_per_step": [round(v / 1e3, 4) for v in e2e_ms_steps],
                       "host_per_step": diag_steps},
             # one block, every launch timed (the last warm-up step)
-            "kernels": {k: {"launches": v["launches"], "ms": round(v["ms"], 3)} for k, v in prof_all.items()},
+            "kernels": {k: {"launches": v["launches"], "ms": round(v["ms"], 3),
+                            "GBps": round(v["bytes"] / v["ms"] / 1e6, 1) if v["ms"] > 0 else None}
+                        for k, v in prof_all.items()},
             # per block stage: device ms of its kernels, the largest first
             "stage_kernels_ms": {
                 sec: dict(sorted(((k, round(v["ms"], 2)) for k, v in ks.items()), key=lambda kv: -kv[1])[:8]) | {

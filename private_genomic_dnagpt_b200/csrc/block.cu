@@ -252,7 +252,7 @@ constexpr int kBsgsRegThreads = 128;
 constexpr int kBsgsSplit = 2;                                   // lanes per coefficient
 constexpr int kBsgsRegCoeffs = kBsgsRegThreads / kBsgsSplit;  // coefficients per CTA
 template <int NB>
-__global__ void __launch_bounds__(kBsgsRegThreads, 4) bsgs_inner_reg_kernel(BabyPtrs babies, int ng,
+__global__ void __launch_bounds__(kBsgsRegThreads, NB >= 32 ? 3 : 4) bsgs_inner_reg_kernel(BabyPtrs babies, int ng,
                                                                               const uint64_t* __restrict__ diag,
                                                                               InnerPtrs out, int logN, int n2, int l0,
                                                                               const ckks::Mod* __restrict__ mods) {
@@ -272,13 +272,33 @@ __global__ void __launch_bounds__(kBsgsRegThreads, 4) bsgs_inner_reg_kernel(Baby
   const double* dt = reinterpret_cast<const double*>(diag) +
                      ((size_t)l * (N / kThreads) + tile) * (size_t)(NB * n2) * kThreads + (size_t)half * H * kThreads +
                      c;
-  const double qd = (double)mods[l].q, qinv = 1.0 / qd;
-  for (int g = 0; g < n2; ++g) {
+  // the next giant step's diagonals stream into this thread's own
+  // shared-memory slots while the current one is computed (cp.async, two
+  // buffers; each thread reads only what it copied, so no barrier)
+  __shared__ double sd[2][H][kBsgsRegThreads];
+  auto prefetch = [&](int g, int buf) {
     const double* dg = dt + (size_t)g * NB * kThreads;
+#pragma unroll
+    for (int j = 0; j < H; ++j) {
+      const uint32_t dst = (uint32_t)__cvta_generic_to_shared(&sd[buf][j][threadIdx.x]);
+      asm volatile("cp.async.ca.shared.global [%0], [%1], 8;\n" ::"r"(dst), "l"(dg + (size_t)j * kThreads));
+    }
+    asm volatile("cp.async.commit_group;\n" ::);
+  };
+  const double qd = (double)mods[l].q, qinv = 1.0 / qd;
+  prefetch(0, 0);
+  for (int g = 0; g < n2; ++g) {
+    if (g + 1 < n2) {
+      prefetch(g + 1, (g + 1) & 1);
+      asm volatile("cp.async.wait_group 1;\n" ::);
+    } else {
+      asm volatile("cp.async.wait_group 0;\n" ::);
+    }
+    const int buf = g & 1;
     double a0 = 0.0, a1 = 0.0;
 #pragma unroll
     for (int j = 0; j < H; ++j) {
-      const double d = __ldg(dg + (size_t)j * kThreads);
+      const double d = sd[buf][j][threadIdx.x];
       a0 = __dadd_rn(a0, fp_mod_product(d, b0[j], qd, qinv));
       a1 = __dadd_rn(a1, fp_mod_product(d, b1[j], qd, qinv));
       if ((j & 3) == 3) {
