@@ -65,11 +65,13 @@ def measured_peaks():
     return 6650.0, "fallback"
 
 
-# DRAM bytes (read + write) per limb of one NTT pass, from the ncu capture of
-# a 1536-limb forward transform (profiles/ntt_pass_n65536_1536limbs.md); the
-# pass traffic grows in proportion to the limbs it transforms
-NCU_TRAFFIC_PER_LIMB = {"ntt_fwd_rows": (877.050368 + 751.248640) * 1e6 / 1536,
-                        "ntt_fwd_cols": (805.437952 + 745.955328) * 1e6 / 1536}
+# DRAM bytes (read + write) per limb of one NTT pass, from an ncu capture of a
+# 1536-limb forward transform (64 polynomials x 24 limbs, float64 butterflies
+# on 23 of the 24 primes): ntt_fwd_rows is the strided pass, ntt_fwd_cols the
+# contiguous one; the pass traffic grows in proportion to the limbs it
+# transforms
+NCU_TRAFFIC_PER_LIMB = {"ntt_fwd_rows": (805.442304 + 760.096512) * 1e6 / 1536,
+                        "ntt_fwd_cols": (891.555840 + 753.208576) * 1e6 / 1536}
 
 
 def keyswitch_bytes(limbs: int, K: int, alpha: int, N: int) -> float:

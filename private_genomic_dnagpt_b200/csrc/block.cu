@@ -319,6 +319,68 @@ __global__ void __launch_bounds__(kBsgsRegThreads, NB >= 32 ? 3 : 4) bsgs_inner_
   }
 }
 
+// The same structure for a limb whose prime is too large for the float64
+// products (the 60-bit first prime): 64-bit baby residues in registers,
+// 128-bit multiply-accumulate chains, the lane pair's sums added as 128-bit
+// values (each below 2^124) and reduced once.
+template <int NB>
+__global__ void __launch_bounds__(kBsgsRegThreads, NB >= 32 ? 3 : 4) bsgs_inner_reg_int_kernel(
+    BabyPtrs babies, int ng, const uint64_t* __restrict__ diag, InnerPtrs out, int logN, int n2, int l0,
+    const ckks::Mod* __restrict__ mods) {
+  constexpr int H = NB / kBsgsSplit;
+  const int N = 1 << logN;
+  const int q = blockIdx.x % ng, part = blockIdx.x / ng;
+  const int tile = blockIdx.y, l = l0 + blockIdx.z;
+  const int half = threadIdx.x % kBsgsSplit;
+  const int c = part * kBsgsRegCoeffs + threadIdx.x / kBsgsSplit;
+  const size_t off = (size_t)l * N + (size_t)tile * kThreads + c;
+  uint64_t b0[H], b1[H];
+#pragma unroll
+  for (int j = 0; j < H; ++j) {
+    b0[j] = babies.c0[q][half * H + j][off];
+    b1[j] = babies.c1[q][half * H + j][off];
+  }
+  const uint64_t* dt =
+      diag + ((size_t)l * (N / kThreads) + tile) * (size_t)(NB * n2) * kThreads + (size_t)half * H * kThreads + c;
+  __shared__ uint64_t sd[2][H][kBsgsRegThreads];
+  auto prefetch = [&](int g, int buf) {
+    const uint64_t* dg = dt + (size_t)g * NB * kThreads;
+#pragma unroll
+    for (int j = 0; j < H; ++j) {
+      const uint32_t dst = (uint32_t)__cvta_generic_to_shared(&sd[buf][j][threadIdx.x]);
+      asm volatile("cp.async.ca.shared.global [%0], [%1], 8;\n" ::"r"(dst), "l"(dg + (size_t)j * kThreads));
+    }
+    asm volatile("cp.async.commit_group;\n" ::);
+  };
+  const ckks::Mod m = mods[l];
+  prefetch(0, 0);
+  for (int g = 0; g < n2; ++g) {
+    if (g + 1 < n2) {
+      prefetch(g + 1, (g + 1) & 1);
+      asm volatile("cp.async.wait_group 1;\n" ::);
+    } else {
+      asm volatile("cp.async.wait_group 0;\n" ::);
+    }
+    const int buf = g & 1;
+    ckks::U128 a0{0, 0}, a1{0, 0};
+#pragma unroll
+    for (int j = 0; j < H; ++j) {
+      const uint64_t d = sd[buf][j][threadIdx.x];
+      ckks::mac_wide(a0, d, b0[j]);
+      ckks::mac_wide(a1, d, b1[j]);
+    }
+#pragma unroll
+    for (int s = 1; s < kBsgsSplit; s <<= 1) {
+      ckks::add_wide(a0, ckks::U128{__shfl_xor_sync(0xffffffffu, a0.lo, s), __shfl_xor_sync(0xffffffffu, a0.hi, s)});
+      ckks::add_wide(a1, ckks::U128{__shfl_xor_sync(0xffffffffu, a1.lo, s), __shfl_xor_sync(0xffffffffu, a1.hi, s)});
+    }
+    if (half == 0)
+      out.c0[q][g][off] = ckks::reduce128(a0, m);
+    else if (half == 1)
+      out.c1[q][g][off] = ckks::reduce128(a1, m);
+  }
+}
+
 // ---- client-side float64 transforms, on the device ------------------------
 // (the reference computes these exactly in float64 on the host:
 //  1/sqrt T123.cpp:514-538, tanh-GELU :190-194/:540-568, softmax :629-665)
@@ -873,12 +935,15 @@ struct ckks_block {
           int l1 = l0 + 1;
           while (l1 < limbs && (C.moduli[l1] < blk::kFpPrime) == fp) ++l1;
           const dim3 grid(s.n2, C.N / blk::kThreads, l1 - l0);
-          if (fp && (s.n1 == 32 || s.n1 == 16 || s.n1 == 8)) {
+          if (s.n1 == 32 || s.n1 == 16 || s.n1 == 8) {
             static_assert(blk::kThreads % blk::kBsgsRegCoeffs == 0, "a tile of whole CTAs");
             const dim3 rgrid(ng * (blk::kThreads / blk::kBsgsRegCoeffs), C.N / blk::kThreads, l1 - l0);
-            auto kern = s.n1 == 32   ? blk::bsgs_inner_reg_kernel<32>
-                        : s.n1 == 16 ? blk::bsgs_inner_reg_kernel<16>
-                                     : blk::bsgs_inner_reg_kernel<8>;
+            auto kern = fp ? (s.n1 == 32   ? blk::bsgs_inner_reg_kernel<32>
+                              : s.n1 == 16 ? blk::bsgs_inner_reg_kernel<16>
+                                           : blk::bsgs_inner_reg_kernel<8>)
+                           : (s.n1 == 32   ? blk::bsgs_inner_reg_int_kernel<32>
+                              : s.n1 == 16 ? blk::bsgs_inner_reg_int_kernel<16>
+                                           : blk::bsgs_inner_reg_int_kernel<8>);
             kern<<<rgrid, blk::kBsgsRegThreads, 0, C.stream>>>(bp, ng, dg.data, ip, C.logN, s.n2, l0, C.d_mods);
           } else if (fp)
             blk::bsgs_inner_fp_kernel<<<grid, dim3(blk::kBsgsThreads, ng), 0, C.stream>>>(
