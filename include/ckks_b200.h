@@ -202,6 +202,10 @@ int ckks_mul_ct_sum(ckks_ctx* ctx, const ckks_ct* const* a, const ckks_ct* const
 int ckks_mul_ct_batch(ckks_ctx* ctx, const ckks_ct* const* a, const ckks_ct* const* b, int count,
                       ckks_ct* const* outs);
 int ckks_rescale_batch(ckks_ctx* ctx, const ckks_ct* const* in, int count, ckks_ct* const* outs);
+/* outs[i] = EvalMult(a[i], p[i]) (ciphertext x plaintext, T123.cpp:1149-1152) for ciphertexts at one
+ * limb count, up to 32 products per launch */
+int ckks_mul_pt_batch(ckks_ctx* ctx, const ckks_ct* const* a, const ckks_pt* const* p, int count,
+                      ckks_ct* const* outs);
 /* AccumulateSum(ct, count, stride) (T123.cpp:1154-1159; key ladder :444-453) */
 int ckks_accumulate_sum(ckks_ctx* ctx, const ckks_ct* a, int count, int stride, ckks_ct* out);
 /* outs[i] = sum_r EvalRotate(in[i], k[r]) for every input (k distinct; an

@@ -265,6 +265,22 @@ class CryptoContextImpl {
     check(ckks_mul_ct_batch(h_, x.data(), y.data(), (int)a.size(), hs.data()));
     return outs;
   }
+  // [EvalMult(a[i], p[i])] for ciphertexts at one level, batched launches
+  std::vector<Ciphertext> EvalMultPlainBatch(const std::vector<Ciphertext>& a, const std::vector<Plaintext>& p) {
+    std::vector<Ciphertext> outs, in;
+    std::vector<const ckks_ct*> x;
+    std::vector<const ckks_pt*> y;
+    std::vector<ckks_ct*> hs;
+    for (size_t i = 0; i < a.size(); ++i) {
+      outs.push_back(fresh());
+      in.push_back(deg1(a[i]));
+      x.push_back(in.back()->handle());
+      y.push_back(p[i]->handle());
+      hs.push_back(outs.back()->handle());
+    }
+    check(ckks_mul_pt_batch(h_, x.data(), y.data(), (int)a.size(), hs.data()));
+    return outs;
+  }
   std::vector<Ciphertext> RescaleBatch(const std::vector<Ciphertext>& a) {
     std::vector<Ciphertext> outs;
     std::vector<const ckks_ct*> in;

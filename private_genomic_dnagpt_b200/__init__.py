@@ -107,6 +107,7 @@ _SIGS = [
                                       ctypes.POINTER(_vp)]),
     ("ckks_add_scalar", ctypes.c_int, [_vp, _vp, ctypes.c_double, _vp]),
     ("ckks_mul_pt", ctypes.c_int, [_vp, _vp, _vp, _vp]),
+    ("ckks_mul_pt_batch", ctypes.c_int, [_vp, _vp, _vp, ctypes.c_int, _vp]),
     ("ckks_mul_ct", ctypes.c_int, [_vp, _vp, _vp, _vp]),
     ("ckks_mul_int", ctypes.c_int, [_vp, _vp, ctypes.c_int64, _vp]),
     ("ckks_rescale", ctypes.c_int, [_vp, _vp, _vp]),
@@ -482,6 +483,15 @@ class CryptoContext:
 
     def mul_pt(self, a, p):
         o = self._new(); _check(lib().ckks_mul_pt(self.h, a.h, p.h, o.h)); return o
+
+    def mul_pt_batch(self, cts, pts):
+        """[mul_pt(a, p) for a, p in zip(cts, pts)], ciphertexts at one level."""
+        n = len(cts)
+        outs = [self._new() for _ in cts]
+        _check(lib().ckks_mul_pt_batch(self.h, (_vp * max(1, n))(*[c.h for c in cts]),
+                                       (_vp * max(1, n))(*[p.h for p in pts]), n,
+                                       (_vp * max(1, n))(*[o.h for o in outs])))
+        return outs
 
     def mul_ct(self, a, b):
         o = self._new(); _check(lib().ckks_mul_ct(self.h, a.h, b.h, o.h)); return o

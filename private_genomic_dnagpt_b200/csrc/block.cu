@@ -772,14 +772,19 @@ struct ckks_block {
     count["rotations"] += (long)idx.size();
     const auto r = cc.EvalFastRotation(x, idx);
     const int l = x->limbs();
-    std::vector<Ciphertext> sums;
+    std::vector<Plaintext> masks;
     for (size_t i = 0; i < ds.size(); ++i) {
-      const Ciphertext a = cc.EvalMult(r[2 * i], lane_plain(0, ds[i], true, l));
-      const Ciphertext b = cc.EvalMult(r[2 * i + 1], lane_plain(0, ds[i], false, l));
-      count["ct_plain"] += 2;
-      sums.push_back(cc.EvalAdd(a, b));
+      masks.push_back(lane_plain(0, ds[i], true, l));
+      masks.push_back(lane_plain(0, ds[i], false, l));
     }
-    const auto rs_ = cc.RescaleBatch(sums);
+    count["ct_plain"] += (long)r.size();
+    const auto prod = cc.EvalMultPlainBatch(r, masks);
+    std::vector<Ciphertext> lo, hi;
+    for (size_t i = 0; i < ds.size(); ++i) {
+      lo.push_back(prod[2 * i]);
+      hi.push_back(prod[2 * i + 1]);
+    }
+    const auto rs_ = cc.RescaleBatch(cc.EvalAddBatch(lo, hi));
     for (size_t i = 0; i < ds.size(); ++i) out[ds[i]] = rs_[i];
     return out;
   }
@@ -1140,7 +1145,11 @@ void ckks_block::shard_scores(const std::vector<blk::TileTag>& tiles, double* d_
     // (T123.cpp:803-833); distinct d < B <= HD never share a feature
     const int M = (int)sums.size();
     std::vector<Ciphertext> iso(M);
-    for (int i = 0; i < M; ++i) iso[i] = cc.EvalMult(sums[i], score_plain(tags[i], sums[i]->limbs(), inv_sqrt_hd));
+    {
+      std::vector<Plaintext> pl;
+      for (int i = 0; i < M; ++i) pl.push_back(score_plain(tags[i], sums[i]->limbs(), inv_sqrt_hd));
+      iso = cc.EvalMultPlainBatch(sums, pl);
+    }
     count["ct_plain"] += M;
     iso = cc.RescaleBatch(iso);
     std::vector<int> qgs;

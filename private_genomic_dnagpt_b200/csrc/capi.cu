@@ -321,9 +321,13 @@ void mul_ct_batch(Context& c, const ckks_ct* const* a, const ckks_ct* const* bb,
   std::vector<DevPoly> res(n);
   std::vector<uint64_t*> dbuf;
   ckks::KsBatch b{};
+  ckks::TensorBatch tb{};
+  tb.S = S;
   auto flush = [&] {
+    ckks::tensor_batch(c, tb, limbs, c.stream);  // the batch's tensors in one launch
     if (b.M) ckks::keyswitch_batch(c, limbs, b, false, c.stream);
     b.M = 0;
+    tb.M = 0;
     for (uint64_t* p : dbuf) c.release(p);
     dbuf.clear();
   };
@@ -332,8 +336,12 @@ void mul_ct_batch(Context& c, const ckks_ct* const* a, const ckks_ct* const* bb,
       throw Error(CKKS_ELEVEL, "operands at different levels");
     uint64_t* d = (uint64_t*)c.alloc(sizeof(uint64_t) * 3 * S);
     dbuf.push_back(d);
-    ckks::tensor(c, a[r]->p.poly(0), a[r]->p.poly(1), bb[r]->p.poly(0), bb[r]->p.poly(1), d, d + S, d + 2 * S,
-                 limbs, c.stream);
+    tb.a0[tb.M] = a[r]->p.poly(0);
+    tb.a1[tb.M] = a[r]->p.poly(1);
+    tb.b0[tb.M] = bb[r]->p.poly(0);
+    tb.b1[tb.M] = bb[r]->p.poly(1);
+    tb.d[tb.M] = d;
+    ++tb.M;
     res[r].ensure(&c, 2, limbs);
     res[r].limbs = limbs;
     res[r].scale = a[r]->p.scale * bb[r]->p.scale;
@@ -1042,6 +1050,42 @@ int ckks_mul_pt(ckks_ctx* ctx, const ckks_ct* a, const ckks_pt* p, ckks_ct* out)
     dst->scale = a->p.scale * p->p.scale;
     dst->deg = a->p.deg + 1;
     if (dst == &tmp) take(out->p, tmp);
+  });
+}
+
+int ckks_mul_pt_batch(ckks_ctx* ctx, const ckks_ct* const* a, const ckks_pt* const* p, int count,
+                      ckks_ct* const* outs) {
+  return guard([&] {
+    Context& c = C(ctx);
+    need(count >= 0 && (count == 0 || (a && p && outs)), CKKS_EARG, "bad batch");
+    if (!count) return;
+    const int limbs = a[0]->p.limbs;
+    for (int i = 0; i < count; ++i) {
+      same_ctx(ctx, a[i]);
+      same_ctx(ctx, p[i]);
+      need(outs[i] && outs[i]->owner == ctx, CKKS_EARG, "bad output handle");
+      need(a[i]->p.limbs == limbs, CKKS_ELEVEL, "batched products need one limb count");
+      need(p[i]->p.limbs >= limbs, CKKS_ELEVEL, "plaintext has fewer limbs than the ciphertext");
+    }
+    std::vector<DevPoly> res(count);
+    for (int i0 = 0; i0 < count; i0 += ckks::kKsBatch) {
+      ckks::MulPtBatch b{};
+      b.M = std::min(ckks::kKsBatch, count - i0);
+      for (int m = 0; m < b.M; ++m) {
+        const int i = i0 + m;
+        res[i].ensure(&c, 2, limbs);
+        res[i].limbs = limbs;
+        res[i].scale = a[i]->p.scale * p[i]->p.scale;
+        res[i].deg = a[i]->p.deg + 1;
+        b.a0[m] = a[i]->p.poly(0);
+        b.a1[m] = a[i]->p.poly(1);
+        b.pt[m] = p[i]->p.data;
+        b.o0[m] = res[i].poly(0);
+        b.o1[m] = res[i].poly(1);
+      }
+      ckks::ew_mul_pt_batch(c, b, limbs, c.stream);
+    }
+    for (int i = 0; i < count; ++i) take(outs[i]->p, res[i]);
   });
 }
 

@@ -300,8 +300,32 @@ void add_many(const Context& c, const SumPtrs& p, int k, int limbs, cudaStream_t
 void add_pairs(const Context& c, const PairPtrs& p, int M, int limbs, cudaStream_t st);
 void tensor(const Context& c, const uint64_t* a0, const uint64_t* a1, const uint64_t* b0, const uint64_t* b1,
             uint64_t* d0, uint64_t* d1, uint64_t* d2, int limbs, cudaStream_t st);
+// items per batched launch sequence (key switches, rescales, products)
+constexpr int kKsBatch = 32;
 // sum_i a_i (x) b_i of n <= kTensorSum ciphertext pairs (degree-2 result)
 constexpr int kTensorSum = 31;
+// batched plaintext products: item m is (a0[m], a1[m]) * pt[m] -> (o0[m], o1[m])
+struct MulPtBatch {
+  const uint64_t* a0[kKsBatch];
+  const uint64_t* a1[kKsBatch];
+  const uint64_t* pt[kKsBatch];
+  uint64_t* o0[kKsBatch];
+  uint64_t* o1[kKsBatch];
+  int M;
+};
+void ew_mul_pt_batch(const Context& c, const MulPtBatch& b, int limbs, cudaStream_t st);
+// batched tensors: item m writes d0, d1, d2 at d[m], d[m] + S, d[m] + 2 S
+struct TensorBatch {
+  const uint64_t* a0[kKsBatch];
+  const uint64_t* a1[kKsBatch];
+  const uint64_t* b0[kKsBatch];
+  const uint64_t* b1[kKsBatch];
+  uint64_t* d[kKsBatch];
+  size_t S;
+  int M;
+};
+void tensor_batch(const Context& c, const TensorBatch& b, int limbs, cudaStream_t st);
+
 struct TensorPtrs {
   const uint64_t* a0[kTensorSum];
   const uint64_t* a1[kTensorSum];
@@ -327,7 +351,6 @@ void moddown2(const Context& c, uint64_t* acc, int limbs, const uint64_t* add0, 
 // add0[m][pi_g(n)], out1[m] = ModDown(acc1) + add1[m] (addends optional).
 // With shared_input every item switches d[0] and one ModUp serves all
 // (hoisted rotations).
-constexpr int kKsBatch = 32;
 struct KsBatch {
   const uint64_t* d[kKsBatch];
   const uint64_t* key[kKsBatch];

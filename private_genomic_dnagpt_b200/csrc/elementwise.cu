@@ -60,6 +60,21 @@ __global__ void __launch_bounds__(kEwThreads) mul_pt_kernel(const uint64_t* __re
   *reinterpret_cast<ulonglong2*>(o + p * so + off) = make_ulonglong2(mul_mod(x.x, y.x, m), mul_mod(x.y, y.y, m));
 }
 
+// item m = blockIdx.z: (c0, c1) of ciphertext m times plaintext m
+__global__ void __launch_bounds__(kEwThreads) mul_pt_batch_kernel(MulPtBatch b, int limbs, int logN,
+                                                                  const Mod* __restrict__ mods) {
+  const int N = 1 << logN;
+  const int limb = blockIdx.y % limbs, p = blockIdx.y / limbs, mi = blockIdx.z;
+  const Mod m = mods[limb];
+  const size_t i = ((size_t)blockIdx.x * kEwThreads + threadIdx.x) * 2;
+  if (i >= (size_t)N) return;
+  const size_t off = (size_t)limb * N + i;
+  const ulonglong2 x = *reinterpret_cast<const ulonglong2*>((p ? b.a1[mi] : b.a0[mi]) + off);
+  const ulonglong2 y = *reinterpret_cast<const ulonglong2*>(b.pt[mi] + off);
+  *reinterpret_cast<ulonglong2*>((p ? b.o1[mi] : b.o0[mi]) + off) =
+      make_ulonglong2(mul_mod(x.x, y.x, m), mul_mod(x.y, y.y, m));
+}
+
 __global__ void __launch_bounds__(kEwThreads) mul_const_kernel(const uint64_t* __restrict__ a, size_t sa,
                                                                uint64_t* __restrict__ o, size_t so, int limbs,
                                                                int logN, const Mod* __restrict__ mods, ConstRes k) {
@@ -107,6 +122,24 @@ __global__ void __launch_bounds__(kEwThreads) tensor_kernel(const uint64_t* __re
   d0[off] = mul_mod(x0, y0, m);
   d1[off] = reduce128(mid, m);
   d2[off] = mul_mod(x1, y1, m);
+}
+
+// tensors of up to kKsBatch pairs, item m = blockIdx.z: d_m = (a0 b0, a0 b1 + a1 b0, a1 b1)
+__global__ void __launch_bounds__(kEwThreads) tensor_batch_kernel(TensorBatch b, int logN,
+                                                                  const Mod* __restrict__ mods) {
+  const int N = 1 << logN;
+  const int limb = blockIdx.y, mi = blockIdx.z;
+  const Mod m = mods[limb];
+  const size_t i = (size_t)blockIdx.x * kEwThreads + threadIdx.x;
+  if (i >= (size_t)N) return;
+  const size_t off = (size_t)limb * N + i;
+  const uint64_t x0 = b.a0[mi][off], x1 = b.a1[mi][off], y0 = b.b0[mi][off], y1 = b.b1[mi][off];
+  U128 mid = mul_wide(x0, y1);
+  mac_wide(mid, x1, y0);
+  uint64_t* d = b.d[mi];
+  d[off] = mul_mod(x0, y0, m);
+  d[b.S + off] = reduce128(mid, m);
+  d[2 * b.S + off] = mul_mod(x1, y1, m);
 }
 
 // sum_i a_i (x) b_i over up to kTensorSum pairs: d0 = sum a0 b0, d1 = sum
@@ -221,6 +254,15 @@ void ew_mul_pt(const Context& c, const uint64_t* a, size_t sa, const uint64_t* p
   CKKS_CUDA(cudaGetLastError());
 }
 
+void ew_mul_pt_batch(const Context& c, const MulPtBatch& b, int limbs, cudaStream_t st) {
+  if (b.M <= 0) return;
+  if (b.M > kKsBatch) throw Error(kErrArgument, "plaintext-product batch above 32");
+  const dim3 grid((c.N / 2 + kEwThreads - 1) / kEwThreads, 2 * limbs, b.M);
+  ProfScope ps(c, "mul_pt", 5.0 * b.M * limbs * c.limb_bytes(), st);
+  mul_pt_batch_kernel<<<grid, kEwThreads, 0, st>>>(b, limbs, c.logN, c.d_mods);
+  CKKS_CUDA(cudaGetLastError());
+}
+
 void ew_mul_const(const Context& c, const uint64_t* a, size_t sa, uint64_t* o, size_t so, int npolys, int limbs,
                   const std::vector<uint64_t>& k_res, cudaStream_t st) {
   const dim3 grid((c.N / 2 + kEwThreads - 1) / kEwThreads, npolys * limbs);
@@ -241,6 +283,15 @@ void tensor(const Context& c, const uint64_t* a0, const uint64_t* a1, const uint
   const dim3 grid((c.N + kEwThreads - 1) / kEwThreads, limbs);
   ProfScope ps(c, "tensor", 7.0 * limbs * c.limb_bytes(), st);
   tensor_kernel<<<grid, kEwThreads, 0, st>>>(a0, a1, b0, b1, d0, d1, d2, c.logN, c.d_mods);
+  CKKS_CUDA(cudaGetLastError());
+}
+
+void tensor_batch(const Context& c, const TensorBatch& b, int limbs, cudaStream_t st) {
+  if (b.M <= 0) return;
+  if (b.M > kKsBatch) throw Error(kErrArgument, "tensor batch above 32");
+  const dim3 grid((c.N + kEwThreads - 1) / kEwThreads, limbs, b.M);
+  ProfScope ps(c, "tensor", 7.0 * b.M * limbs * c.limb_bytes(), st);
+  tensor_batch_kernel<<<grid, kEwThreads, 0, st>>>(b, c.logN, c.d_mods);
   CKKS_CUDA(cudaGetLastError());
 }
 

@@ -262,6 +262,16 @@ def test_hoisted_rotation_sum_equals_the_rotation_sum(pair10):
         cc.EvalRotateSumHoisted([cx], [4, 4])
 
 
+def test_batched_plaintext_products_bit_exact(pair10):
+    """40 products (two launches) against the oracle's single products."""
+    o, cc = pair10
+    fs = [_fresh(o, cc, 60 + i, 4) for i in range(40)]
+    pts = [o.encode(np.random.default_rng(90 + i).uniform(-1, 1, o.N // 2), 4) for i in range(40)]
+    got = cc.mul_pt_batch([f[2] for f in fs], [cc.import_pt(p, o.scale(4)) for p in pts])
+    for f, p, g in zip(fs, pts, got):
+        assert np.array_equal(g.limbs_array(), o.mul_pt(f[1], p))
+
+
 def test_errors_are_reported(pair10):
     o, cc = pair10
     x, rx, cx = _fresh(o, cc, 8, 3)
