@@ -461,16 +461,37 @@ void oc_chacha_words(uint64_t seed, uint64_t nonce, uint64_t counter, uint64_t o
 #define KEYID_RELIN 1u
 #define KEYID_ROT(g) (0x100u + (uint32_t)(g))
 
+/* ternary in {-1, 0, 1} and the centred binomial of 21 + 21 bits */
+static int ternary_of(uint64_t w) {
+    uint64_t t = w % 3;
+    return t == 0 ? 0 : (t == 1 ? 1 : -1);
+}
+static int cbd_of(uint64_t w) {
+    return __builtin_popcountll(w & 0x1FFFFFull) - __builtin_popcountll((w >> 21) & 0x1FFFFFull);
+}
 static int sample_ternary(uint64_t seed, uint64_t nonce, uint64_t n) {
     uint64_t w[2];
     chacha_words(seed, nonce, n, w);
-    uint64_t t = w[0] % 3;
-    return t == 0 ? 0 : (t == 1 ? 1 : -1);
+    return ternary_of(w[0]);
 }
 static int sample_cbd(uint64_t seed, uint64_t nonce, uint64_t n) {
     uint64_t w[2];
     chacha_words(seed, nonce, n, w);
-    return __builtin_popcountll(w[0] & 0x1FFFFFull) - __builtin_popcountll((w[0] >> 21) & 0x1FFFFFull);
+    return cbd_of(w[0]);
+}
+/* all 16 output words of block `counter` as eight 64-bit words: the
+ * encryption sampler takes coefficient n from word n % 8 of block n / 8 */
+static void chacha_words8(uint64_t seed, uint64_t nonce, uint64_t counter, uint64_t out[8]) {
+    uint32_t key[8];
+    uint64_t s = seed;
+    for (int i = 0; i < 4; i++) {
+        uint64_t k = splitmix(&s);
+        key[2 * i] = (uint32_t)k;
+        key[2 * i + 1] = (uint32_t)(k >> 32);
+    }
+    uint32_t w[16];
+    oc_chacha_block(key, counter, nonce, w);
+    for (int i = 0; i < 8; i++) out[i] = (uint64_t)w[2 * i] | ((uint64_t)w[2 * i + 1] << 32);
 }
 static uint64_t sample_uniform(uint64_t seed, uint64_t nonce, uint64_t counter, const modulus_t* m) {
     uint64_t w[2];
@@ -861,10 +882,16 @@ void oc_encrypt(const oc_ctx* c, const uint64_t* pt, int limbs, uint64_t counter
     int* u = (int*)malloc(sizeof(int) * (size_t)N);
     int* e0 = (int*)malloc(sizeof(int) * (size_t)N);
     int* e1 = (int*)malloc(sizeof(int) * (size_t)N);
-    for (int n = 0; n < N; n++) {
-        u[n] = sample_ternary(c->seed, NONCE_ENC(counter, 0), (uint64_t)n);
-        e0[n] = sample_cbd(c->seed, NONCE_ENC(counter, 1), (uint64_t)n);
-        e1[n] = sample_cbd(c->seed, NONCE_ENC(counter, 2), (uint64_t)n);
+    for (int b = 0; b < N / 8; b++) {
+        uint64_t wu[8], w0[8], w1[8];
+        chacha_words8(c->seed, NONCE_ENC(counter, 0), (uint64_t)b, wu);
+        chacha_words8(c->seed, NONCE_ENC(counter, 1), (uint64_t)b, w0);
+        chacha_words8(c->seed, NONCE_ENC(counter, 2), (uint64_t)b, w1);
+        for (int k = 0; k < 8; k++) {
+            u[8 * b + k] = ternary_of(wu[k]);
+            e0[8 * b + k] = cbd_of(w0[k]);
+            e1[8 * b + k] = cbd_of(w1[k]);
+        }
     }
     int* pr = all_primes(c);
     uint64_t* un = (uint64_t*)malloc(sizeof(uint64_t) * (size_t)limbs * N);

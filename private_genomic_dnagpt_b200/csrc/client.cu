@@ -42,7 +42,9 @@ Key8 key_from_seed(uint64_t seed) {
 
 __device__ __forceinline__ uint32_t rotl(uint32_t v, int n) { return (v << n) | (v >> (32 - n)); }
 
-__device__ uint64_t chacha_w0(const Key8& key, uint64_t nonce, uint64_t counter) {
+// the ChaCha20 block (RFC 7539 rounds, 64-bit counter in words 12-13 and
+// 64-bit nonce in words 14-15) as eight 64-bit output words
+__device__ void chacha_words8(const Key8& key, uint64_t nonce, uint64_t counter, uint64_t out[8]) {
   uint32_t st[16] = {0x61707865u, 0x3320646eu, 0x79622d32u, 0x6b206574u, key.k[0], key.k[1], key.k[2], key.k[3],
                      key.k[4],    key.k[5],    key.k[6],    key.k[7],    (uint32_t)counter, (uint32_t)(counter >> 32),
                      (uint32_t)nonce, (uint32_t)(nonce >> 32)};
@@ -74,26 +76,35 @@ __device__ uint64_t chacha_w0(const Key8& key, uint64_t nonce, uint64_t counter)
     QR(x[3], x[4], x[9], x[14]);
   }
 #undef QR
-  return (uint64_t)(x[0] + st[0]) | ((uint64_t)(x[1] + st[1]) << 32);
+#pragma unroll
+  for (int i = 0; i < 8; ++i) out[i] = (uint64_t)(x[2 * i] + st[2 * i]) | ((uint64_t)(x[2 * i + 1] + st[2 * i + 1]) << 32);
 }
 
 // encryption randomness of item m: sub 0 ternary u, subs 1/2 centered
-// binomial e0/e1 (nonce (0x20 << 56) | counter << 2 | sub, as single encryptions)
+// binomial e0/e1 (nonce (0x20 << 56) | counter << 2 | sub, as single
+// encryptions); coefficient n takes 64-bit word n % 8 of ChaCha block n / 8,
+// so a thread computes one block for eight coefficients
 __global__ void __launch_bounds__(kThreads) enc_sample_kernel(Key8 key, uint64_t counter0, int N,
                                                               int* __restrict__ out) {
-  const int n = blockIdx.x * kThreads + threadIdx.x;
-  if (n >= N) return;
+  const int b = blockIdx.x * kThreads + threadIdx.x;
+  if (b >= N / 8) return;
   const int m = blockIdx.y, sub = blockIdx.z;
   const uint64_t nonce = (0x20ull << 56) | ((counter0 + (uint64_t)m) << 2) | (uint64_t)sub;
-  const uint64_t w0 = chacha_w0(key, nonce, (uint64_t)n);
-  int v;
-  if (sub == 0) {
-    const uint64_t t = w0 % 3ull;
-    v = t == 0 ? 0 : (t == 1 ? 1 : -1);
-  } else {
-    v = __popcll(w0 & 0x1FFFFFull) - __popcll((w0 >> 21) & 0x1FFFFFull);
+  uint64_t w[8];
+  chacha_words8(key, nonce, (uint64_t)b, w);
+  int v[8];
+#pragma unroll
+  for (int k = 0; k < 8; ++k) {
+    if (sub == 0) {
+      const uint64_t t = w[k] % 3ull;
+      v[k] = t == 0 ? 0 : (t == 1 ? 1 : -1);
+    } else {
+      v[k] = __popcll(w[k] & 0x1FFFFFull) - __popcll((w[k] >> 21) & 0x1FFFFFull);
+    }
   }
-  out[((size_t)m * 3 + sub) * N + n] = v;
+  int4* o = reinterpret_cast<int4*>(out + ((size_t)m * 3 + sub) * N + (size_t)8 * b);
+  o[0] = make_int4(v[0], v[1], v[2], v[3]);
+  o[1] = make_int4(v[4], v[5], v[6], v[7]);
 }
 
 __global__ void __launch_bounds__(kThreads) enc_spread_kernel(const int* __restrict__ v, uint64_t* __restrict__ out,
@@ -175,8 +186,8 @@ void encrypt_batch(Context& c, const uint64_t* pts, int limbs, int M, uint64_t* 
   c.enc_counter += (uint64_t)M;
   {
     ProfScope ps(c, "enc_sample", 12.0 * M * N, st);
-    enc_sample_kernel<<<dim3((N + kThreads - 1) / kThreads, M, 3), kThreads, 0, st>>>(key_from_seed(c.params.seed),
-                                                                                       counter0, N, small);
+    enc_sample_kernel<<<dim3((N / 8 + kThreads - 1) / kThreads, M, 3), kThreads, 0, st>>>(
+        key_from_seed(c.params.seed), counter0, N, small);
     enc_spread_kernel<<<dim3((N + kThreads - 1) / kThreads, 3 * M * limbs), kThreads, 0, st>>>(small, r, limbs,
                                                                                                c.logN, c.d_mods);
   }

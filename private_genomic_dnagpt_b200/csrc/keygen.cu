@@ -81,6 +81,29 @@ __device__ void chacha_words(const ChachaKey& key, uint64_t nonce, uint64_t coun
   w1 = (uint64_t)(x[2] + st[2]) | ((uint64_t)(x[3] + st[3]) << 32);
 }
 
+// the whole block as eight 64-bit words (the encryption sampler's layout)
+__device__ void chacha_words8(const ChachaKey& key, uint64_t nonce, uint64_t counter, uint64_t w[8]) {
+  uint32_t st[16] = {0x61707865u, 0x3320646eu, 0x79622d32u, 0x6b206574u, key.k[0], key.k[1], key.k[2], key.k[3],
+                     key.k[4],    key.k[5],    key.k[6],    key.k[7],    (uint32_t)counter, (uint32_t)(counter >> 32),
+                     (uint32_t)nonce, (uint32_t)(nonce >> 32)};
+  uint32_t x[16];
+#pragma unroll
+  for (int i = 0; i < 16; ++i) x[i] = st[i];
+#pragma unroll 1
+  for (int r = 0; r < 10; ++r) {
+    CKKS_QR(x[0], x[4], x[8], x[12]);
+    CKKS_QR(x[1], x[5], x[9], x[13]);
+    CKKS_QR(x[2], x[6], x[10], x[14]);
+    CKKS_QR(x[3], x[7], x[11], x[15]);
+    CKKS_QR(x[0], x[5], x[10], x[15]);
+    CKKS_QR(x[1], x[6], x[11], x[12]);
+    CKKS_QR(x[2], x[7], x[8], x[13]);
+    CKKS_QR(x[3], x[4], x[9], x[14]);
+  }
+#pragma unroll
+  for (int i = 0; i < 8; ++i) w[i] = (uint64_t)(x[2 * i] + st[2 * i]) | ((uint64_t)(x[2 * i + 1] + st[2 * i + 1]) << 32);
+}
+
 constexpr uint64_t kNonceSk = 0x01ull;
 constexpr uint64_t kNoncePkA = 0x02ull;
 constexpr uint64_t kNoncePkE = 0x03ull;
@@ -108,6 +131,27 @@ __global__ void __launch_bounds__(kThreads) sample_small_kernel(int* __restrict_
     v = __popcll(w0 & 0x1FFFFFull) - __popcll((w0 >> 21) & 0x1FFFFFull);
   }
   out[n] = v;
+}
+
+// encryption randomness: coefficient n from 64-bit word n % 8 of block n / 8
+// (the same sampling as the batched encryption, one thread per block)
+__global__ void __launch_bounds__(kThreads) sample_small_wide_kernel(int* __restrict__ out, ChachaKey key,
+                                                                     uint64_t nonce, int N, int kind) {
+  const int b = blockIdx.x * kThreads + threadIdx.x;
+  if (b >= N / 8) return;
+  uint64_t w[8];
+  chacha_words8(key, nonce, (uint64_t)b, w);
+#pragma unroll
+  for (int k = 0; k < 8; ++k) {
+    int v;
+    if (kind == 0) {
+      const uint64_t t = w[k] % 3ull;
+      v = t == 0 ? 0 : (t == 1 ? 1 : -1);
+    } else {
+      v = __popcll(w[k] & 0x1FFFFFull) - __popcll((w[k] >> 21) & 0x1FFFFFull);
+    }
+    out[8 * b + k] = v;
+  }
 }
 
 __global__ void __launch_bounds__(kThreads) small_to_limbs_kernel(const int* __restrict__ v, uint64_t* __restrict__ out,
@@ -191,9 +235,14 @@ dim3 grid_for(const Context& c, int limbs) { return dim3((c.N + kThreads - 1) / 
 
 // small polynomial sampled with (nonce, kind), spread over `limbs` primes
 // (map) and transformed to NTT form
-void small_ntt(const Context& c, uint64_t nonce, int kind, LimbMap map, int limbs, uint64_t* out, int* scratch) {
+void small_ntt(const Context& c, uint64_t nonce, int kind, LimbMap map, int limbs, uint64_t* out, int* scratch,
+               bool wide = false) {
   const ChachaKey key = key_from_seed(c.params.seed);
-  sample_small_kernel<<<(c.N + kThreads - 1) / kThreads, kThreads, 0, c.stream>>>(scratch, key, nonce, c.N, kind);
+  if (wide)
+    sample_small_wide_kernel<<<(c.N / 8 + kThreads - 1) / kThreads, kThreads, 0, c.stream>>>(scratch, key, nonce,
+                                                                                             c.N, kind);
+  else
+    sample_small_kernel<<<(c.N + kThreads - 1) / kThreads, kThreads, 0, c.stream>>>(scratch, key, nonce, c.N, kind);
   small_to_limbs_kernel<<<grid_for(c, limbs), kThreads, 0, c.stream>>>(scratch, out, map, c.logN, c.d_mods);
   CKKS_CUDA(cudaGetLastError());
   ntt_forward(c, out, limbs, map, c.stream);
@@ -285,9 +334,9 @@ void encrypt(Context& c, const uint64_t* pt, int limbs, uint64_t counter, uint64
   uint64_t* buf = (uint64_t*)c.alloc(sizeof(uint64_t) * 3 * (size_t)limbs * N);
   uint64_t *u = buf, *e0 = buf + (size_t)limbs * N, *e1 = buf + 2 * (size_t)limbs * N;
   const LimbMap m = LimbMap::q(limbs, L);
-  small_ntt(c, nonce_enc(counter, 0), 0, m, limbs, u, scratch);
-  small_ntt(c, nonce_enc(counter, 1), 1, m, limbs, e0, scratch);
-  small_ntt(c, nonce_enc(counter, 2), 1, m, limbs, e1, scratch);
+  small_ntt(c, nonce_enc(counter, 0), 0, m, limbs, u, scratch, true);
+  small_ntt(c, nonce_enc(counter, 1), 1, m, limbs, e0, scratch, true);
+  small_ntt(c, nonce_enc(counter, 2), 1, m, limbs, e1, scratch, true);
   enc_combine_kernel<<<grid_for(c, limbs), kThreads, 0, c.stream>>>(c.d_pk, c.d_pk + (size_t)L * N, u, e0, e1, pt, c0,
                                                                     c1, c.logN, c.d_mods);
   CKKS_CUDA(cudaGetLastError());
