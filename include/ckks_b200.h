@@ -182,6 +182,12 @@ int ckks_rotate(ckks_ctx* ctx, const ckks_ct* a, int k, ckks_ct* out);
 /* EvalFastRotation(ct, k[], M, nullptr): one ModUp shared by `count`
  * rotations (T123.cpp:1183-1203, 1343-1362) */
 int ckks_rotate_hoisted(ckks_ctx* ctx, const ckks_ct* a, const int* k, int count, ckks_ct* const* outs);
+/* EvalFastRotation of `count` ciphertexts at one limb count by the same nk
+ * indices: outs[i * nk + r] = rotation k[r] of in[i]; one ModUp per input and
+ * each rotation key read from HBM once for all inputs (the baby steps of all
+ * token groups of a BSGS product) */
+int ckks_rotate_hoisted_batch(ckks_ctx* ctx, const ckks_ct* const* in, int count, const int* k, int nk,
+                              ckks_ct* const* outs);
 /* Batched forms: `count` independent operations at one limb count, run as
  * one launch sequence per stage (up to 32 per sequence).  They replace loops
  * of EvalRotate / EvalMult / Rescale calls over independent ciphertexts

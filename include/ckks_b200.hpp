@@ -189,6 +189,22 @@ class CryptoContextImpl {
     check(ckks_rotate(h_, a->handle(), k, o->handle()));
     return o;
   }
+  // [[EvalFastRotation(x, k)] for x in a]: each key read once for all inputs
+  std::vector<std::vector<Ciphertext>> EvalFastRotationBatch(const std::vector<Ciphertext>& a,
+                                                             const std::vector<int>& k) {
+    std::vector<std::vector<Ciphertext>> outs(a.size());
+    std::vector<const ckks_ct*> in;
+    std::vector<ckks_ct*> hs;
+    for (size_t i = 0; i < a.size(); ++i) {
+      in.push_back(a[i]->handle());
+      for (size_t r = 0; r < k.size(); ++r) {
+        outs[i].push_back(fresh());
+        hs.push_back(outs[i].back()->handle());
+      }
+    }
+    check(ckks_rotate_hoisted_batch(h_, in.data(), (int)a.size(), k.data(), (int)k.size(), hs.data()));
+    return outs;
+  }
   std::vector<Ciphertext> EvalFastRotation(const Ciphertext& a, const std::vector<int>& k) {
     std::vector<Ciphertext> outs;
     std::vector<ckks_ct*> hs;

@@ -108,6 +108,8 @@ _SIGS = [
     ("ckks_add_scalar", ctypes.c_int, [_vp, _vp, ctypes.c_double, _vp]),
     ("ckks_mul_pt", ctypes.c_int, [_vp, _vp, _vp, _vp]),
     ("ckks_mul_pt_batch", ctypes.c_int, [_vp, _vp, _vp, ctypes.c_int, _vp]),
+    ("ckks_rotate_hoisted_batch", ctypes.c_int, [_vp, _vp, ctypes.c_int, ctypes.POINTER(ctypes.c_int), ctypes.c_int,
+                                                 _vp]),
     ("ckks_mul_ct", ctypes.c_int, [_vp, _vp, _vp, _vp]),
     ("ckks_mul_int", ctypes.c_int, [_vp, _vp, ctypes.c_int64, _vp]),
     ("ckks_rescale", ctypes.c_int, [_vp, _vp, _vp]),
@@ -620,6 +622,16 @@ class CryptoContext:
 
     def AccumulateSum(self, ct: Ciphertext, count: int, stride: int) -> Ciphertext:
         o = self._new(); _check(lib().ckks_accumulate_sum(self.h, ct.h, count, stride, o.h)); return o
+
+    def EvalFastRotationBatch(self, cts, ks) -> list[list[Ciphertext]]:
+        """[[EvalFastRotation(ct, ks)] for ct in cts], each key read once."""
+        n, nk = len(cts), len(ks)
+        outs = [[self._new() for _ in ks] for _ in cts]
+        flat = [o for row in outs for o in row]
+        _check(lib().ckks_rotate_hoisted_batch(self.h, (_vp * max(1, n))(*[c.h for c in cts]), n,
+                                               (ctypes.c_int * max(1, nk))(*ks), nk,
+                                               (_vp * max(1, len(flat)))(*[o.h for o in flat])))
+        return outs
 
     def EvalRotateSumHoisted(self, cts, ks) -> list[Ciphertext]:
         """[sum_r EvalRotate(ct, ks[r]) for ct in cts]: one ModUp and one

@@ -881,14 +881,20 @@ struct ckks_block {
     return diags.emplace(key, dg).first->second;
   }
 
-  std::vector<Ciphertext> babies_of(const Ciphertext& x) {
+  std::vector<Ciphertext> babies_of(const Ciphertext& x) { return babies_of_batch({x})[0]; }
+  // baby steps x, rot(x, B j) for j < n1 of every input, one hoisted batch
+  // (each rotation key read once for all inputs)
+  std::vector<std::vector<Ciphertext>> babies_of_batch(const std::vector<Ciphertext>& xs) {
     std::vector<int> idx;
     for (int j = 1; j < s.n1; ++j) idx.push_back(s.B * j);
-    auto r = cc.EvalFastRotation(x, idx);
-    count["rotations"] += (long)idx.size();
-    std::vector<Ciphertext> b{x};
-    b.insert(b.end(), r.begin(), r.end());
-    return b;
+    auto r = cc.EvalFastRotationBatch(xs, idx);
+    count["rotations"] += (long)idx.size() * (long)xs.size();
+    std::vector<std::vector<Ciphertext>> out(xs.size());
+    for (size_t i = 0; i < xs.size(); ++i) {
+      out[i].push_back(xs[i]);
+      out[i].insert(out[i].end(), r[i].begin(), r[i].end());
+    }
+    return out;
   }
 
   // x_q W^T for weight `id` and every token group q from their baby-step
@@ -1095,8 +1101,7 @@ void ckks_block::shard_qkv(const std::vector<int>& groups, int parts) {
     act.push_back(s.count(g));
   }
   const auto nrm = layernorm(xs, act);
-  std::vector<std::vector<Ciphertext>> babies;
-  for (const auto& n : nrm) babies.push_back(babies_of(n));
+  const auto babies = babies_of_batch(nrm);
   std::vector<Ciphertext>* dst[3] = {&st_q, &st_k, &st_v};
   for (int w = 0; w < 3; ++w) {
     if (!(parts & (1 << w))) continue;
@@ -1261,13 +1266,14 @@ void ckks_block::shard_mlp(const std::vector<int>& groups, int c0, int c1) {
   const int B = s.B, PW = s.PW, SL = slots();
   const int nb = (SL + blk::kThreads - 1) / blk::kThreads;
   const int G = (int)groups.size();
-  std::vector<std::vector<Ciphertext>> ob;
+  std::vector<Ciphertext> ctxs;
   std::vector<int> act;
   for (int g : groups) {
     if (!st_ctx[g] || !st_x[g]) throw ckks::Error(CKKS_ESTATE, "context of the group not complete");
-    ob.push_back(babies_of(st_ctx[g]));
+    ctxs.push_back(st_ctx[g]);
     act.push_back(s.count(g));
   }
+  auto ob = babies_of_batch(ctxs);
   const auto o = bsgs_groups(ob, 3);
   ob.clear();
   std::vector<Ciphertext> r1;
@@ -1280,8 +1286,7 @@ void ckks_block::shard_mlp(const std::vector<int>& groups, int c0, int c1) {
   }
   const int nc = c1 - c0;
   const auto n2 = layernorm(r1, act);
-  std::vector<std::vector<Ciphertext>> fb;
-  for (const auto& n : n2) fb.push_back(babies_of(n));
+  auto fb = babies_of_batch(n2);
   std::vector<std::vector<Ciphertext>> hc(nc);  // [chunk][group]
   for (int c = 0; c < nc; ++c) hc[c] = bsgs_groups(fb, 4 + c0 + c);
   fb.clear();
@@ -1306,9 +1311,10 @@ void ckks_block::shard_mlp(const std::vector<int>& groups, int c0, int c1) {
   C.release(dv);
   count["client_round_trips"] += (long)G * nc;
   std::vector<Ciphertext> mlp(G);
+  auto gb = babies_of_batch(ge);  // item i * nc + c
   for (int c = 0; c < nc; ++c) {
     std::vector<std::vector<Ciphertext>> db;
-    for (int i = 0; i < G; ++i) db.push_back(babies_of(ge[(size_t)i * nc + c]));
+    for (int i = 0; i < G; ++i) db.push_back(std::move(gb[(size_t)i * nc + c]));
     const auto pc = bsgs_groups(db, 4 + nfc + c0 + c);
     for (int i = 0; i < G; ++i) mlp[i] = c ? add(mlp[i], pc[i]) : pc[i];
   }

@@ -142,6 +142,66 @@ void rotate_many(Context& c, const ckks_ct* a, const int* ks, int n, ckks_ct* co
   }
 }
 
+// rotations of every input in[g] by ks[0..nk) into outs[g * nk + r]: one
+// ModUp per input; each key is read once for all inputs
+void rotate_hoisted_batch(Context& c, const ckks_ct* const* in, int G, const int* ks, int nk,
+                          ckks_ct* const* outs) {
+  if (G <= 0 || nk <= 0) return;
+  const int limbs = in[0]->p.limbs;
+  std::vector<uint32_t> gs(nk);
+  std::vector<int> live;  // non-identity rotations
+  for (int r = 0; r < nk; ++r) {
+    gs[r] = c.galois(ks[r]);
+    if (gs[r] == 1u) continue;
+    if (!c.switch_key(gs[r], limbs))
+      throw Error(CKKS_EKEY, "rotation key not generated for index " + std::to_string(ks[r]));
+    live.push_back(r);
+  }
+  std::vector<DevPoly> res((size_t)G * nk);
+  for (int g = 0; g < G; ++g) {
+    const ckks_ct* a = in[g];
+    if (a->p.limbs != limbs) throw Error(CKKS_ELEVEL, "batched rotations need one limb count");
+    for (int r = 0; r < nk; ++r) {
+      DevPoly& o = res[(size_t)g * nk + r];
+      o.ensure(&c, 2, limbs);
+      o.limbs = limbs;
+      o.scale = a->p.scale;
+      o.deg = a->p.deg;
+      if (gs[r] == 1u)
+        ckks::ew_binary(c, ckks::EwOp::Copy, a->p.data, stride(a->p), nullptr, 0, o.data, stride(o), 2, limbs,
+                        c.stream);
+    }
+  }
+  for (int g0 = 0; g0 < G; g0 += ckks::kKsBatch) {
+    const int gn = std::min(ckks::kKsBatch, G - g0);
+    for (size_t r0 = 0; r0 < live.size(); r0 += ckks::kKsBatch) {
+      const int rn = (int)std::min<size_t>(ckks::kKsBatch, live.size() - r0);
+      ckks::HoistKeys h{};
+      h.R = rn;
+      for (int i = 0; i < rn; ++i) {
+        h.key[i] = c.switch_key(gs[live[r0 + i]], limbs);
+        h.g[i] = gs[live[r0 + i]];
+      }
+      std::vector<const uint64_t*> d(gn), c0(gn);
+      std::vector<uint64_t*> o0((size_t)gn * rn), o1((size_t)gn * rn);
+      for (int g = 0; g < gn; ++g) {
+        d[g] = in[g0 + g]->p.poly(1);
+        c0[g] = in[g0 + g]->p.poly(0);
+        for (int i = 0; i < rn; ++i) {
+          DevPoly& o = res[(size_t)(g0 + g) * nk + live[r0 + i]];
+          o0[(size_t)g * rn + i] = o.poly(0);
+          o1[(size_t)g * rn + i] = o.poly(1);
+        }
+      }
+      ckks::keyswitch_hoisted_multi(c, limbs, d.data(), c0.data(), gn, h, o0.data(), o1.data(), c.stream);
+    }
+  }
+  for (size_t i = 0; i < res.size(); ++i) {
+    outs[i]->owner = in[i / nk]->owner;
+    take(outs[i]->p, res[i]);
+  }
+}
+
 // independent rotations in[i] by ks[i] (all at one limb count)
 void rotate_batch(Context& c, const ckks_ct* const* in, const int* ks, int n, ckks_ct* const* outs) {
   if (n <= 0) return;
@@ -1297,6 +1357,17 @@ int ckks_window_sum_batch(ckks_ctx* ctx, const ckks_ct* const* in, int count, in
         take(outs[i]->p, acc[i].p);
       }
     }
+  });
+}
+
+int ckks_rotate_hoisted_batch(ckks_ctx* ctx, const ckks_ct* const* in, int count, const int* k, int nk,
+                              ckks_ct* const* outs) {
+  return guard([&] {
+    Context& c = C(ctx);
+    need(count >= 0 && nk >= 0 && (count == 0 || nk == 0 || (in && k && outs)), CKKS_EARG, "bad batch");
+    for (int i = 0; i < count; ++i) same_ctx(ctx, in[i]);
+    for (long i = 0; i < (long)count * nk; ++i) need(outs[i] && outs[i]->owner == ctx, CKKS_EARG, "bad output handle");
+    rotate_hoisted_batch(c, in, count, k, nk, outs);
   });
 }
 

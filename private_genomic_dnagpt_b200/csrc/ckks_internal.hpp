@@ -344,6 +344,13 @@ void ks_inner(const Context& c, const uint64_t* ext, int limbs, const uint64_t* 
 // when given; acc holds 2 polys of limbs+K limbs and is consumed
 void moddown2(const Context& c, uint64_t* acc, int limbs, const uint64_t* add0, uint32_t g_add0,
               const uint64_t* add1, uint64_t* out0, uint64_t* out1, cudaStream_t st);
+// Rotation keys of a hoisted sum (R non-identity Galois elements)
+struct HoistKeys {
+  const uint64_t* key[kKsBatch];
+  uint32_t g[kKsBatch];
+  int R;
+};
+
 // Batched key switching: up to kKsBatch independent switches at one limb
 // count in one launch sequence (ModUp, inner product, ModDown each a single
 // launch over the batch).  Item m switches d[m] with key[m]; the ModUp digits
@@ -359,21 +366,24 @@ struct KsBatch {
   uint64_t* out0[kKsBatch];
   uint64_t* out1[kKsBatch];
   uint32_t g[kKsBatch];
+  uint8_t src[kKsBatch];  // keyswitch_hoisted_multi: the ModUp input of each item
   int M;
 };
 void keyswitch_batch(const Context& c, int limbs, const KsBatch& b, bool shared_input, cudaStream_t st);
+// Hoisted rotations of G inputs (d = c1 pointers, c0 = their c0) by the same
+// R rotations (h): one ModUp per input, then the key products and ModDowns of
+// up to 32 (input, rotation) items per launch sequence, the items of one key
+// adjacent in the grid so that its residues come from HBM once for all
+// inputs.  out0/out1[g * R + r] = rotation r of input g.
+void keyswitch_hoisted_multi(const Context& c, int limbs, const uint64_t* const* d, const uint64_t* const* c0,
+                             int G, const HoistKeys& h, uint64_t* const* out0, uint64_t* const* out1,
+                             cudaStream_t st);
 // Sum of the M key switches of a batch with one ModDown: the key inner
 // products are added in the extended basis Q_l P and divided by P once;
 // out0 = ModDown(sum acc0) + sum_m auto_{g_m}(add0[m]), out1 = ModDown(sum
 // acc1) + sum_m add1[m] (null addends skipped).  The giant steps of a BSGS
 // product: sum_g rot(inner_g, k_g).
 void keyswitch_sum(const Context& c, int limbs, const KsBatch& b, uint64_t* out0, uint64_t* out1, cudaStream_t st);
-// Rotation keys of a hoisted sum (R non-identity Galois elements)
-struct HoistKeys {
-  const uint64_t* key[kKsBatch];
-  uint32_t g[kKsBatch];
-  int R;
-};
 // For each of the M items (d = c1, add0 = c0, out0/out1): the sum of its R
 // rotations by h (plus the item itself when `identity`), with one ModUp per
 // item, the R key inner products added in the extended basis Q_l P and one

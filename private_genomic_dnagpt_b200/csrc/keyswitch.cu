@@ -711,6 +711,36 @@ __global__ void __launch_bounds__(kThreads) moddown_combine_hoist_kernel(KsBatch
   }
 }
 
+// key products of (input, rotation) items, item m = blockIdx.x (fastest), so
+// the CTAs of the items sharing one key and one residue range run together
+// and its residues come from HBM once
+__global__ void __launch_bounds__(kThreads) ks_inner_multi_kernel(KsBatch b, const uint64_t* __restrict__ ext_all,
+                                                                  uint64_t* __restrict__ acc_all, int limbs, int L,
+                                                                  int K, int P, int beta, int logN,
+                                                                  const Mod* __restrict__ mods) {
+  const int N = 1 << logN;
+  const int m = blockIdx.x;
+  const int n = blockIdx.y * kThreads + threadIdx.x;
+  if (n >= N) return;
+  const int t = blockIdx.z;
+  const int E = limbs + K;
+  const int pt = t < limbs ? t : L + (t - limbs);
+  const Mod md = mods[pt];
+  const uint32_t g = b.g[m];
+  const uint64_t* ext = ext_all + (size_t)b.src[m] * beta * E * N;
+  const uint64_t* key = b.key[m];
+  const uint32_t src = auto_index((uint32_t)n, g, logN);
+  U128 s0{0, 0}, s1{0, 0};
+  for (int j = 0; j < beta; ++j) {
+    const uint64_t v = ext[((size_t)j * E + t) * N + src];
+    mac_wide(s0, v, key[((size_t)j * 2 * P + pt) * N + n]);
+    mac_wide(s1, v, key[((size_t)j * 2 * P + P + pt) * N + n]);
+  }
+  uint64_t* acc = acc_all + (size_t)m * 2 * E * N;
+  acc[(size_t)t * N + n] = reduce128(s0, md);
+  acc[((size_t)E + t) * N + n] = reduce128(s1, md);
+}
+
 }  // namespace
 
 void keyswitch_batch(const Context& c, int limbs, const KsBatch& b, bool shared, cudaStream_t st) {
@@ -782,6 +812,101 @@ void keyswitch_batch(const Context& c, int limbs, const KsBatch& b, bool shared,
   }
   CKKS_CUDA(cudaGetLastError());
   c.release(dc);
+  c.release(ext);
+  c.release(acc);
+  c.release(conv);
+}
+
+void keyswitch_hoisted_multi(const Context& c, int limbs, const uint64_t* const* d, const uint64_t* const* c0,
+                             int G, const HoistKeys& h, uint64_t* const* out0, uint64_t* const* out1,
+                             cudaStream_t st) {
+  if (c.alpha > kMaxAlpha || c.Kx(limbs) > kMaxK) throw Error(kErrArgument, "digit size above 16 is not supported");
+  if (G <= 0 || h.R <= 0) return;
+  if (G > kKsBatch) throw Error(kErrArgument, "hoisted rotations of more than 32 inputs");
+  const int N = c.N, E = limbs + c.Kx(limbs);
+  const LevelTables& lt = c.lt(limbs);
+  const double lb = c.limb_bytes();
+  // one ModUp per input
+  KsBatch bu{};
+  bu.M = G;
+  for (int g = 0; g < G; ++g) bu.d[g] = d[g];
+  uint64_t* dc = (uint64_t*)c.alloc(sizeof(uint64_t) * (size_t)G * limbs * N);
+  uint64_t* ext = (uint64_t*)c.alloc(sizeof(uint64_t) * (size_t)G * lt.beta * E * N);
+  {
+    ProfScope ps(c, "ks_gather", 2.0 * G * limbs * lb, st);
+    gather_kernel<<<dim3((N / 2 + kThreads - 1) / kThreads, limbs, G), kThreads, 0, st>>>(bu, limbs, c.logN, dc);
+  }
+  ntt_inverse(c, dc, G * limbs, LimbMap::q(limbs, c.L), st, lt.d_up_scale_a, lt.d_up_scale_b);
+  const int min_cnt = limbs - (lt.beta - 1) * c.alpha;
+  const int nch_up = (E - min_cnt + kTargets - 1) / kTargets;
+  {
+    ProfScope ps(c, "modup_conv", G * (2.0 * limbs + (double)lt.beta * E) * lb, st);
+    auto kern = c.alpha <= 4 ? modup_conv_batch_kernel<4>
+                : c.alpha <= 8 ? modup_conv_batch_kernel<8>
+                : c.alpha <= 12 ? modup_conv_batch_kernel<12>
+                                : modup_conv_batch_kernel<16>;
+    kern<<<dim3((N / 2 + kThreads - 1) / kThreads, lt.beta * nch_up, G), kThreads, 0, st>>>(
+        bu, dc, ext, limbs, c.L, c.Kx(limbs), c.alpha, lt.beta, c.logN, nch_up, c.d_mods, lt.d_up_hat);
+  }
+  CKKS_CUDA(cudaGetLastError());
+  {
+    LimbMap m = LimbMap::ext(limbs, c.Kx(limbs), c.L);
+    m.skip_alpha = c.alpha;
+    m.skip_beta = lt.beta;
+    ntt_forward(c, ext, G * lt.beta * E, m, st);
+  }
+  c.release(dc);
+  // items (input g, rotation r), r-major so that a key's items are adjacent;
+  // up to kKsBatch items per launch sequence
+  const int per = std::max(1, kKsBatch / G);  // rotations per chunk
+  uint64_t* acc = (uint64_t*)c.alloc(sizeof(uint64_t) * (size_t)kKsBatch * 2 * E * N);
+  uint64_t* conv = (uint64_t*)c.alloc(sizeof(uint64_t) * (size_t)kKsBatch * 2 * limbs * N);
+  for (int r0 = 0; r0 < h.R; r0 += per) {
+    const int r1 = std::min(h.R, r0 + per);
+    KsBatch b{};
+    for (int r = r0; r < r1; ++r)
+      for (int g = 0; g < G; ++g) {
+        const int m = b.M++;
+        b.key[m] = h.key[r];
+        b.g[m] = h.g[r];
+        b.src[m] = (uint8_t)g;
+        b.add0[m] = c0[g];
+        b.add1[m] = nullptr;
+        b.out0[m] = out0[(size_t)g * h.R + r];
+        b.out1[m] = out1[(size_t)g * h.R + r];
+      }
+    const int M = b.M;
+    {
+      // acc writes, each key once, the gathered ext residues
+      ProfScope ps(c, "ks_inner", (M * (2.0 * E + (double)lt.beta * E) + (r1 - r0) * 2.0 * lt.beta * E) * lb, st);
+      ks_inner_multi_kernel<<<dim3(M, (N + kThreads - 1) / kThreads, E), kThreads, 0, st>>>(
+          b, ext, acc, limbs, c.L, c.Kx(limbs), c.P, lt.beta, c.logN, c.d_mods);
+    }
+    CKKS_CUDA(cudaGetLastError());
+    {
+      LimbMap pm = LimbMap::ext(limbs, c.Kx(limbs), c.L);
+      pm.skip_q = 1;
+      ntt_inverse(c, acc, M * 2 * E, pm, st, c.down_scale_a(limbs), c.down_scale_b(limbs), c.L);
+    }
+    const int nch_dn = (limbs + kTargets - 1) / kTargets;
+    {
+      ProfScope ps(c, "moddown_conv", M * (2.0 * c.Kx(limbs) + 2.0 * limbs) * lb, st);
+      auto kern = c.Kx(limbs) <= 4 ? moddown_conv_batch_kernel<4>
+                  : c.Kx(limbs) <= 8 ? moddown_conv_batch_kernel<8>
+                  : c.Kx(limbs) <= 12 ? moddown_conv_batch_kernel<12>
+                              : moddown_conv_batch_kernel<16>;
+      kern<<<dim3((N / 2 + kThreads - 1) / kThreads, 2 * nch_dn, M), kThreads, 0, st>>>(
+          acc, conv, limbs, c.L, c.Kx(limbs), c.logN, nch_dn, c.d_mods, lt.d_down_phat);
+    }
+    CKKS_CUDA(cudaGetLastError());
+    ntt_forward(c, conv, M * 2 * limbs, LimbMap::q(limbs, c.L), st);
+    {
+      ProfScope ps(c, "moddown_combine", M * 8.0 * limbs * lb, st);
+      moddown_combine_batch_kernel<<<dim3((N + kThreads - 1) / kThreads, 2 * limbs, M), kThreads, 0, st>>>(
+          b, acc, conv, limbs, c.Kx(limbs), c.logN, c.d_mods, lt.d_down_pinv);
+    }
+    CKKS_CUDA(cudaGetLastError());
+  }
   c.release(ext);
   c.release(acc);
   c.release(conv);

@@ -262,6 +262,21 @@ def test_hoisted_rotation_sum_equals_the_rotation_sum(pair10):
         cc.EvalRotateSumHoisted([cx], [4, 4])
 
 
+@pytest.mark.parametrize("limbs", [None, 2])
+def test_batched_hoisted_rotations_bit_exact(pair10, limbs):
+    """Five inputs by the same indices (an identity among them), against
+    the oracle's hoisted rotations of each input."""
+    o, cc = pair10
+    lv = o.L if limbs is None else limbs
+    fs = [_fresh(o, cc, 70 + i, lv) for i in range(5)]
+    ks = [1, 0, 3, -1, 8, 64]
+    got = cc.EvalFastRotationBatch([f[2] for f in fs], ks)
+    for f, row in zip(fs, got):
+        ref = o.rotate_hoisted(f[1], ks)
+        for r, g in enumerate(row):
+            assert np.array_equal(g.limbs_array(), ref[r])
+
+
 def test_batched_plaintext_products_bit_exact(pair10):
     """40 products (two launches) against the oracle's single products."""
     o, cc = pair10
