@@ -263,11 +263,24 @@ struct DevPoly {
 };
 
 // ---- kernel launchers ----------------------------------------------------
-void ntt_forward(const Context& c, uint64_t* data, int nlimbs, LimbMap map, cudaStream_t st);
+// Where a transform reads its input when that is not `data` itself (the
+// result is still written to `data`): batch limb i reads item[i / per_item]
+// + (i % per_item) * limb_stride words; with `reduce` each value is first
+// reduced modulo the limb's prime (a residue of another prime spread over a
+// set of primes).  Up to 64 items.
+struct NttSource {
+  const uint64_t* item[64];
+  int per_item;
+  int limb_stride;
+  bool reduce;
+};
+void ntt_forward(const Context& c, uint64_t* data, int nlimbs, LimbMap map, cudaStream_t st,
+                 const NttSource* src = nullptr);
 // inverse transform; with scale_a/scale_b (indexed by prime - scale_base:
 // c*n^-1 and c*Winv[1]*n^-1 as Shoup pairs) it returns the coefficients times c
 void ntt_inverse(const Context& c, uint64_t* data, int nlimbs, LimbMap map, cudaStream_t st,
-                 const ulonglong2* scale_a = nullptr, const ulonglong2* scale_b = nullptr, int scale_base = 0);
+                 const ulonglong2* scale_a = nullptr, const ulonglong2* scale_b = nullptr, int scale_base = 0,
+                 const NttSource* src = nullptr);
 
 // element-wise over `limbs` Q limbs of `npolys` polynomials with strides
 enum class EwOp : int { Add = 0, Sub = 1, Mul = 2, Neg = 3, Copy = 4 };

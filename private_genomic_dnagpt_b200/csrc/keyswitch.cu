@@ -368,16 +368,6 @@ void moddown2_with(const Context& c, uint64_t* acc, int limbs, const uint64_t* a
 // ---------------------------------------------------------------------------
 namespace {
 
-// dc[m] = d[m] (limbs limbs), ulonglong2 per thread
-__global__ void __launch_bounds__(kThreads) gather_kernel(KsBatch b, int limbs, int logN, uint64_t* __restrict__ dc) {
-  const int N = 1 << logN;
-  const int n = 2 * (blockIdx.x * kThreads + threadIdx.x);
-  if (n >= N) return;
-  const int l = blockIdx.y, m = blockIdx.z;
-  *reinterpret_cast<ulonglong2*>(dc + ((size_t)m * limbs + l) * N + n) =
-      *reinterpret_cast<const ulonglong2*>(b.d[m] + (size_t)l * N + n);
-}
-
 template <int MAXA>
 __global__ void __launch_bounds__(kThreads) modup_conv_batch_kernel(KsBatch b, const uint64_t* __restrict__ y_all,
                                                                     uint64_t* __restrict__ ext_all, int limbs, int L,
@@ -586,28 +576,6 @@ __global__ void __launch_bounds__(kThreads) moddown_combine_batch_kernel(KsBatch
   }
 }
 
-__global__ void __launch_bounds__(kThreads) rs_gather_last_kernel(RsBatch b, int limbs, int logN,
-                                                                  uint64_t* __restrict__ last) {
-  const int N = 1 << logN;
-  const int n = blockIdx.x * kThreads + threadIdx.x;
-  if (n >= N) return;
-  const int p = blockIdx.y, m = blockIdx.z;
-  const uint64_t* src = p ? b.in1[m] : b.in0[m];
-  last[(size_t)(2 * m + p) * N + n] = src[(size_t)(limbs - 1) * N + n];
-}
-
-__global__ void __launch_bounds__(kThreads) rs_spread_batch_kernel(const uint64_t* __restrict__ last,
-                                                                   uint64_t* __restrict__ tmp, int limbs, int logN,
-                                                                   const Mod* __restrict__ mods) {
-  const int N = 1 << logN;
-  const int n = blockIdx.x * kThreads + threadIdx.x;
-  if (n >= N) return;
-  const int lo = limbs - 1;
-  const int i = blockIdx.y % lo, p = blockIdx.y / lo, m = blockIdx.z;
-  const uint64_t v = last[(size_t)(2 * m + p) * N + n];
-  tmp[((size_t)(2 * m + p) * lo + i) * N + n] = reduce128(U128{v, 0}, mods[i]);
-}
-
 __global__ void __launch_bounds__(kThreads) rs_combine_batch_kernel(RsBatch b, const uint64_t* __restrict__ tmp,
                                                                     int limbs, int logN, const Mod* __restrict__ mods,
                                                                     const ulonglong2* __restrict__ inv) {
@@ -757,11 +725,13 @@ void keyswitch_batch(const Context& c, int limbs, const KsBatch& b, bool shared,
   uint64_t* acc = (uint64_t*)c.alloc(sizeof(uint64_t) * (size_t)M * 2 * E * N);
   uint64_t* conv = (uint64_t*)c.alloc(sizeof(uint64_t) * (size_t)M * 2 * limbs * N);
   // ModUp
-  {
-    ProfScope ps(c, "ks_gather", 2.0 * Mu * limbs * lb, st);
-    gather_kernel<<<dim3((N / 2 + kThreads - 1) / kThreads, limbs, Mu), kThreads, 0, st>>>(b, limbs, c.logN, dc);
+  {  // the inverse transform reads the inputs in place (no gather copy)
+    NttSource src{};
+    src.per_item = limbs;
+    src.limb_stride = N;
+    for (int m = 0; m < Mu; ++m) src.item[m] = b.d[m];
+    ntt_inverse(c, dc, Mu * limbs, LimbMap::q(limbs, c.L), st, lt.d_up_scale_a, lt.d_up_scale_b, 0, &src);
   }
-  ntt_inverse(c, dc, Mu * limbs, LimbMap::q(limbs, c.L), st, lt.d_up_scale_a, lt.d_up_scale_b);
   const int min_cnt = limbs - (lt.beta - 1) * c.alpha;
   const int nch_up = (E - min_cnt + kTargets - 1) / kTargets;
   {
@@ -832,11 +802,13 @@ void keyswitch_hoisted_multi(const Context& c, int limbs, const uint64_t* const*
   for (int g = 0; g < G; ++g) bu.d[g] = d[g];
   uint64_t* dc = (uint64_t*)c.alloc(sizeof(uint64_t) * (size_t)G * limbs * N);
   uint64_t* ext = (uint64_t*)c.alloc(sizeof(uint64_t) * (size_t)G * lt.beta * E * N);
-  {
-    ProfScope ps(c, "ks_gather", 2.0 * G * limbs * lb, st);
-    gather_kernel<<<dim3((N / 2 + kThreads - 1) / kThreads, limbs, G), kThreads, 0, st>>>(bu, limbs, c.logN, dc);
+  {  // the inverse transform reads the inputs in place (no gather copy)
+    NttSource src{};
+    src.per_item = limbs;
+    src.limb_stride = N;
+    for (int m = 0; m < G; ++m) src.item[m] = bu.d[m];
+    ntt_inverse(c, dc, G * limbs, LimbMap::q(limbs, c.L), st, lt.d_up_scale_a, lt.d_up_scale_b, 0, &src);
   }
-  ntt_inverse(c, dc, G * limbs, LimbMap::q(limbs, c.L), st, lt.d_up_scale_a, lt.d_up_scale_b);
   const int min_cnt = limbs - (lt.beta - 1) * c.alpha;
   const int nch_up = (E - min_cnt + kTargets - 1) / kTargets;
   {
@@ -924,11 +896,13 @@ void keyswitch_sum(const Context& c, int limbs, const KsBatch& b, uint64_t* out0
   uint64_t* acc = (uint64_t*)c.alloc(sizeof(uint64_t) * (size_t)2 * E * N);
   uint64_t* conv = (uint64_t*)c.alloc(sizeof(uint64_t) * (size_t)2 * limbs * N);
   // ModUp of every item
-  {
-    ProfScope ps(c, "ks_gather", 2.0 * M * limbs * lb, st);
-    gather_kernel<<<dim3((N / 2 + kThreads - 1) / kThreads, limbs, M), kThreads, 0, st>>>(b, limbs, c.logN, dc);
+  {  // the inverse transform reads the inputs in place (no gather copy)
+    NttSource src{};
+    src.per_item = limbs;
+    src.limb_stride = N;
+    for (int m = 0; m < M; ++m) src.item[m] = b.d[m];
+    ntt_inverse(c, dc, M * limbs, LimbMap::q(limbs, c.L), st, lt.d_up_scale_a, lt.d_up_scale_b, 0, &src);
   }
-  ntt_inverse(c, dc, M * limbs, LimbMap::q(limbs, c.L), st, lt.d_up_scale_a, lt.d_up_scale_b);
   const int min_cnt = limbs - (lt.beta - 1) * c.alpha;
   const int nch_up = (E - min_cnt + kTargets - 1) / kTargets;
   {
@@ -1000,11 +974,13 @@ void keyswitch_hoisted_sum(const Context& c, int limbs, const KsBatch& b, const 
   uint64_t* acc = (uint64_t*)c.alloc(sizeof(uint64_t) * (size_t)M * 2 * E * N);
   uint64_t* conv = (uint64_t*)c.alloc(sizeof(uint64_t) * (size_t)M * 2 * limbs * N);
   // one ModUp per item
-  {
-    ProfScope ps(c, "ks_gather", 2.0 * M * limbs * lb, st);
-    gather_kernel<<<dim3((N / 2 + kThreads - 1) / kThreads, limbs, M), kThreads, 0, st>>>(b, limbs, c.logN, dc);
+  {  // the inverse transform reads the inputs in place (no gather copy)
+    NttSource src{};
+    src.per_item = limbs;
+    src.limb_stride = N;
+    for (int m = 0; m < M; ++m) src.item[m] = b.d[m];
+    ntt_inverse(c, dc, M * limbs, LimbMap::q(limbs, c.L), st, lt.d_up_scale_a, lt.d_up_scale_b, 0, &src);
   }
-  ntt_inverse(c, dc, M * limbs, LimbMap::q(limbs, c.L), st, lt.d_up_scale_a, lt.d_up_scale_b);
   const int min_cnt = limbs - (lt.beta - 1) * c.alpha;
   const int nch_up = (E - min_cnt + kTargets - 1) / kTargets;
   {
@@ -1072,17 +1048,24 @@ void rescale_batch(const Context& c, int limbs, const RsBatch& b, cudaStream_t s
   const double lb = c.limb_bytes();
   uint64_t* last = (uint64_t*)c.alloc(sizeof(uint64_t) * (size_t)2 * M * N);
   uint64_t* tmp = (uint64_t*)c.alloc(sizeof(uint64_t) * (size_t)2 * M * lo * N);
-  {
-    ProfScope ps(c, "rescale_gather", 4.0 * M * lb, st);
-    rs_gather_last_kernel<<<dim3((N + kThreads - 1) / kThreads, 2, M), kThreads, 0, st>>>(b, limbs, c.logN, last);
+  {  // last limb of every polynomial (2m + p), read in place by the inverse transform
+    NttSource src{};
+    src.per_item = 1;
+    src.limb_stride = 0;
+    for (int m = 0; m < M; ++m) {
+      src.item[2 * m] = b.in0[m] + (size_t)lo * N;
+      src.item[2 * m + 1] = b.in1[m] + (size_t)lo * N;
+    }
+    ntt_inverse(c, last, 2 * M, LimbMap::single(lo), st, nullptr, nullptr, 0, &src);
   }
-  ntt_inverse(c, last, 2 * M, LimbMap::single(lo), st);
-  {
-    ProfScope ps(c, "rescale_spread", 2.0 * M * (1.0 + lo) * lb, st);
-    rs_spread_batch_kernel<<<dim3((N + kThreads - 1) / kThreads, 2 * lo, M), kThreads, 0, st>>>(last, tmp, limbs,
-                                                                                                 c.logN, c.d_mods);
+  {  // its coefficients reduced modulo every remaining prime as the forward transform reads them
+    NttSource src{};
+    src.per_item = lo;
+    src.limb_stride = 0;
+    src.reduce = true;
+    for (int i = 0; i < 2 * M; ++i) src.item[i] = last + (size_t)i * N;
+    ntt_forward(c, tmp, 2 * M * lo, LimbMap::q(lo, c.L), st, &src);
   }
-  ntt_forward(c, tmp, 2 * M * lo, LimbMap::q(lo, c.L), st);
   {
     ProfScope ps(c, "rescale_combine", 6.0 * M * lo * lb, st);
     rs_combine_batch_kernel<<<dim3((N + kThreads - 1) / kThreads, 2 * lo, M), kThreads, 0, st>>>(

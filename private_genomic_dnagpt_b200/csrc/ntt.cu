@@ -39,7 +39,15 @@ struct PassArgs {
   LimbMap map;
   int logN;
   int per_cta;  // columns (strided) or blocks (contiguous) per CTA
+  bool has_src;  // the first pass reads `src` instead of the data array
+  NttSource src;
 };
+
+// the array the first pass of limb `limb` reads
+__device__ __forceinline__ const uint64_t* pass_input(const PassArgs& a, uint64_t* poly, int limb, bool first_pass) {
+  if (!a.has_src || !first_pass) return poly;
+  return a.src.item[limb / a.src.per_item] + (size_t)(limb % a.src.per_item) * a.src.limb_stride;
+}
 
 // Shared-memory slot of residue r in a contiguous block: the low four bits
 // are XORed with a function of bits 4-6, so that each half-warp's 64-bit
@@ -105,6 +113,7 @@ __device__ __forceinline__ void ntt_pass_body(uint64_t* __restrict__ data, const
   // (inverse); the contiguous pass the others
   const bool first_pass = (STRIDED != INV);
   const bool last_pass = !first_pass;
+  const uint64_t* in = pass_input(a, poly, limb, first_pass);
 
   auto gaddr = [&](int r) -> size_t {
     return STRIDED ? (size_t)r * stride + sub_global : (size_t)sub_global * S + r;
@@ -130,7 +139,12 @@ __device__ __forceinline__ void ntt_pass_body(uint64_t* __restrict__ data, const
       const int uj = j / usz, k = j % usz;
       const int u = sub_t + uj * T;
       const int r = (u / D) * (D << G) + (u % D) + k * D;
-      x[j] = (step == 0) ? poly[gaddr(r)] : sm[saddr(r)];
+      if (step > 0) {
+        x[j] = sm[saddr(r)];
+      } else {
+        x[j] = in[gaddr(r)];
+        if (first_pass && a.has_src && a.src.reduce) x[j] = reduce128(U128{x[j], 0}, a.mods[prime]);
+      }
     }
     // butterflies; the twiddle of pair (k, k+h) at stage st0+rr is
     // tw[2^(gs0+st) + prefix*2^st + B*2^rr + (k >> (G-rr))], B = u / D
@@ -266,6 +280,7 @@ __device__ __forceinline__ void ntt_pass_body_fp(uint64_t* __restrict__ data, co
   const int gs0 = STRIDED ? 0 : (a.logN - S_LOG);
   const uint32_t prefix = STRIDED ? 0u : (uint32_t)sub_global;
   const bool first_pass = (STRIDED != INV);
+  const uint64_t* in = pass_input(a, poly, limb, first_pass);
 
   auto gaddr = [&](int r) -> size_t {
     return STRIDED ? (size_t)r * stride + sub_global : (size_t)sub_global * S + r;
@@ -295,7 +310,9 @@ __device__ __forceinline__ void ntt_pass_body_fp(uint64_t* __restrict__ data, co
       if (step > 0) {
         x[j] = __longlong_as_double((long long)sm[saddr(r)]);
       } else if (first_pass) {
-        x[j] = fp_center(__ull2double_rn(poly[gaddr(r)]), q, qinv);
+        uint64_t v = in[gaddr(r)];
+        if (a.has_src && a.src.reduce) v = reduce128(U128{v, 0}, a.mods[prime]);
+        x[j] = fp_center(__ull2double_rn(v), q, qinv);
       } else {
         x[j] = __longlong_as_double((long long)poly[gaddr(r)]);
       }
@@ -435,7 +452,7 @@ int live_limbs(const LimbMap& m, int nlimbs) {
   return n;
 }
 
-void ntt_forward(const Context& c, uint64_t* data, int nlimbs, LimbMap map, cudaStream_t st) {
+void ntt_forward(const Context& c, uint64_t* data, int nlimbs, LimbMap map, cudaStream_t st, const NttSource* src) {
   if (nlimbs <= 0) return;
   // algorithmic traffic of a transform is one read + one write per limb;
   // each of the two passes is credited with half of it
@@ -449,7 +466,12 @@ void ntt_forward(const Context& c, uint64_t* data, int nlimbs, LimbMap map, cuda
   const int s1 = c.logN / 2, s2 = c.logN - s1;
   {
     ProfScope ps(c, "ntt_fwd_rows", bytes, st);
-    dispatch_pass<false, true>(s1, data, nlimbs, a, st);
+    PassArgs a1 = a;
+    if (src) {
+      a1.has_src = true;
+      a1.src = *src;
+    }
+    dispatch_pass<false, true>(s1, data, nlimbs, a1, st);
   }
   {
     ProfScope ps(c, "ntt_fwd_cols", bytes, st);
@@ -459,7 +481,7 @@ void ntt_forward(const Context& c, uint64_t* data, int nlimbs, LimbMap map, cuda
 }
 
 void ntt_inverse(const Context& c, uint64_t* data, int nlimbs, LimbMap map, cudaStream_t st,
-                 const ulonglong2* scale_a, const ulonglong2* scale_b, int scale_base) {
+                 const ulonglong2* scale_a, const ulonglong2* scale_b, int scale_base, const NttSource* src) {
   if (nlimbs <= 0) return;
   const double bytes = live_limbs(map, nlimbs) * c.limb_bytes();
   PassArgs a{};
@@ -476,7 +498,12 @@ void ntt_inverse(const Context& c, uint64_t* data, int nlimbs, LimbMap map, cuda
   const int s1 = c.logN / 2, s2 = c.logN - s1;
   {
     ProfScope ps(c, "ntt_inv_cols", bytes, st);
-    dispatch_pass<true, false>(s2, data, nlimbs, a, st);
+    PassArgs a1 = a;
+    if (src) {
+      a1.has_src = true;
+      a1.src = *src;
+    }
+    dispatch_pass<true, false>(s2, data, nlimbs, a1, st);
   }
   {
     ProfScope ps(c, "ntt_inv_rows", bytes, st);
