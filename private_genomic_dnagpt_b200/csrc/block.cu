@@ -174,7 +174,7 @@ constexpr int kBsgsThreads = 128;
 __global__ void __launch_bounds__(kBsgsThreads * kMaxGroups) bsgs_inner_kernel(BabyPtrs babies, int ng, int n1,
                                                                                const uint64_t* __restrict__ diag,
                                                                                InnerPtrs out, int limbs, int logN,
-                                                                               int n2, int l0,
+                                                                               int n2, int l0, bool accumulate,
                                                                                const ckks::Mod* __restrict__ mods) {
   const int N = 1 << logN;
   const int g = blockIdx.x, tile = blockIdx.y, l = l0 + blockIdx.z;
@@ -195,8 +195,16 @@ __global__ void __launch_bounds__(kBsgsThreads * kMaxGroups) bsgs_inner_kernel(B
     ckks::mac_wide(a11, dv.y, b1.y);
   }
   const ckks::Mod m = mods[l];
-  *reinterpret_cast<ulonglong2*>(out.c0[q][g] + off) = make_ulonglong2(ckks::reduce128(a00, m), ckks::reduce128(a01, m));
-  *reinterpret_cast<ulonglong2*>(out.c1[q][g] + off) = make_ulonglong2(ckks::reduce128(a10, m), ckks::reduce128(a11, m));
+  ulonglong2 r0 = make_ulonglong2(ckks::reduce128(a00, m), ckks::reduce128(a01, m));
+  ulonglong2 r1 = make_ulonglong2(ckks::reduce128(a10, m), ckks::reduce128(a11, m));
+  if (accumulate) {
+    const ulonglong2 p0 = *reinterpret_cast<const ulonglong2*>(out.c0[q][g] + off);
+    const ulonglong2 p1 = *reinterpret_cast<const ulonglong2*>(out.c1[q][g] + off);
+    r0 = make_ulonglong2(ckks::add_mod(r0.x, p0.x, m.q), ckks::add_mod(r0.y, p0.y, m.q));
+    r1 = make_ulonglong2(ckks::add_mod(r1.x, p1.x, m.q), ckks::add_mod(r1.y, p1.y, m.q));
+  }
+  *reinterpret_cast<ulonglong2*>(out.c0[q][g] + off) = r0;
+  *reinterpret_cast<ulonglong2*>(out.c1[q][g] + off) = r1;
 }
 
 // the same inner sums for a limb whose prime is below kFpPrime: diagonals
@@ -204,7 +212,7 @@ __global__ void __launch_bounds__(kBsgsThreads * kMaxGroups) bsgs_inner_kernel(B
 __global__ void __launch_bounds__(kBsgsThreads * kMaxGroups) bsgs_inner_fp_kernel(BabyPtrs babies, int ng, int n1,
                                                                                   const uint64_t* __restrict__ diag,
                                                                                   InnerPtrs out, int limbs, int logN,
-                                                                                  int n2, int l0,
+                                                                                  int n2, int l0, bool accumulate,
                                                                                   const ckks::Mod* __restrict__ mods) {
   const int N = 1 << logN;
   const int g = blockIdx.x, tile = blockIdx.y, l = l0 + blockIdx.z;
@@ -236,8 +244,17 @@ __global__ void __launch_bounds__(kBsgsThreads * kMaxGroups) bsgs_inner_fp_kerne
   a01 = fp_center(a01, qd, qinv);
   a10 = fp_center(a10, qd, qinv);
   a11 = fp_center(a11, qd, qinv);
-  *reinterpret_cast<ulonglong2*>(out.c0[q][g] + off) = make_ulonglong2(fp_canonical(a00, qd), fp_canonical(a01, qd));
-  *reinterpret_cast<ulonglong2*>(out.c1[q][g] + off) = make_ulonglong2(fp_canonical(a10, qd), fp_canonical(a11, qd));
+  ulonglong2 r0 = make_ulonglong2(fp_canonical(a00, qd), fp_canonical(a01, qd));
+  ulonglong2 r1 = make_ulonglong2(fp_canonical(a10, qd), fp_canonical(a11, qd));
+  if (accumulate) {
+    const uint64_t qi = mods[l].q;
+    const ulonglong2 p0 = *reinterpret_cast<const ulonglong2*>(out.c0[q][g] + off);
+    const ulonglong2 p1 = *reinterpret_cast<const ulonglong2*>(out.c1[q][g] + off);
+    r0 = make_ulonglong2(ckks::add_mod(r0.x, p0.x, qi), ckks::add_mod(r0.y, p0.y, qi));
+    r1 = make_ulonglong2(ckks::add_mod(r1.x, p1.x, qi), ckks::add_mod(r1.y, p1.y, qi));
+  }
+  *reinterpret_cast<ulonglong2*>(out.c0[q][g] + off) = r0;
+  *reinterpret_cast<ulonglong2*>(out.c1[q][g] + off) = r1;
 }
 
 // Float64 inner sums with the baby residues held in registers (as doubles):
@@ -255,6 +272,7 @@ template <int NB>
 __global__ void __launch_bounds__(kBsgsRegThreads, NB >= 32 ? 3 : 4) bsgs_inner_reg_kernel(BabyPtrs babies, int ng,
                                                                               const uint64_t* __restrict__ diag,
                                                                               InnerPtrs out, int logN, int n2, int l0,
+                                                                              bool accumulate,
                                                                               const ckks::Mod* __restrict__ mods) {
   constexpr int H = NB / kBsgsSplit;  // babies per lane
   const int N = 1 << logN;
@@ -312,10 +330,12 @@ __global__ void __launch_bounds__(kBsgsRegThreads, NB >= 32 ? 3 : 4) bsgs_inner_
       a0 = __dadd_rn(a0, __shfl_xor_sync(0xffffffffu, a0, m));
       a1 = __dadd_rn(a1, __shfl_xor_sync(0xffffffffu, a1, m));
     }
-    if (half == 0)
-      out.c0[q][g][off] = fp_canonical(fp_center(a0, qd, qinv), qd);
-    else if (half == 1)
-      out.c1[q][g][off] = fp_canonical(fp_center(a1, qd, qinv), qd);
+    if (half < 2) {
+      uint64_t* dst = half == 0 ? out.c0[q][g] : out.c1[q][g];
+      uint64_t r = fp_canonical(fp_center(half == 0 ? a0 : a1, qd, qinv), qd);
+      if (accumulate) r = ckks::add_mod(r, dst[off], mods[l].q);
+      dst[off] = r;
+    }
   }
 }
 
@@ -326,7 +346,7 @@ __global__ void __launch_bounds__(kBsgsRegThreads, NB >= 32 ? 3 : 4) bsgs_inner_
 template <int NB>
 __global__ void __launch_bounds__(kBsgsRegThreads, NB >= 32 ? 3 : 4) bsgs_inner_reg_int_kernel(
     BabyPtrs babies, int ng, const uint64_t* __restrict__ diag, InnerPtrs out, int logN, int n2, int l0,
-    const ckks::Mod* __restrict__ mods) {
+    bool accumulate, const ckks::Mod* __restrict__ mods) {
   constexpr int H = NB / kBsgsSplit;
   const int N = 1 << logN;
   const int q = blockIdx.x % ng, part = blockIdx.x / ng;
@@ -374,10 +394,12 @@ __global__ void __launch_bounds__(kBsgsRegThreads, NB >= 32 ? 3 : 4) bsgs_inner_
       ckks::add_wide(a0, ckks::U128{__shfl_xor_sync(0xffffffffu, a0.lo, s), __shfl_xor_sync(0xffffffffu, a0.hi, s)});
       ckks::add_wide(a1, ckks::U128{__shfl_xor_sync(0xffffffffu, a1.lo, s), __shfl_xor_sync(0xffffffffu, a1.hi, s)});
     }
-    if (half == 0)
-      out.c0[q][g][off] = ckks::reduce128(a0, m);
-    else if (half == 1)
-      out.c1[q][g][off] = ckks::reduce128(a1, m);
+    if (half < 2) {
+      uint64_t* dst = half == 0 ? out.c0[q][g] : out.c1[q][g];
+      uint64_t r = ckks::reduce128(half == 0 ? a0 : a1, m);
+      if (accumulate) r = ckks::add_mod(r, dst[off], m.q);
+      dst[off] = r;
+    }
   }
 }
 
@@ -901,44 +923,67 @@ struct ckks_block {
   // rotations (T123.cpp:1264-1295): fused diagonal x baby-step inner sums,
   // then the giant steps of each group as one rotation sum (one ModDown)
   std::vector<Ciphertext> bsgs_groups(const std::vector<std::vector<Ciphertext>>& babies, int id) {
-    const int G = (int)babies.size();
+    return bsgs_sum_groups({babies}, {id});
+  }
+  // sum_t x_{t,q} W_t^T for every token group q: the inner sums of all terms
+  // t (weights ids[t] on baby steps babies[t][q]) accumulate into one set of
+  // giant-step inputs, so the giant-step rotations run once per group for
+  // the whole sum (rotation is linear)
+  std::vector<Ciphertext> bsgs_sum_groups(const std::vector<std::vector<std::vector<Ciphertext>>>& babies,
+                                          const std::vector<int>& ids) {
+    const int nt = (int)babies.size();
+    const int G = nt ? (int)babies[0].size() : 0;
     std::vector<Ciphertext> outs(G);
     if (!G) return outs;
-    count["matrix_products"] += G;
-    count["ct_plain"] += (long)G * s.n1 * s.n2;
-    const int limbs = babies[0][0]->limbs();
-    const Diag& dg = diagonals(id, limbs);
+    const int limbs = babies[0][0][0]->limbs();
+    std::vector<const Diag*> dgs;
+    for (int t = 0; t < nt; ++t) {
+      if ((int)babies[t].size() != G) throw ckks::Error(CKKS_EARG, "terms over different groups");
+      dgs.push_back(&diagonals(ids[t], limbs));
+      count["matrix_products"] += G;
+      count["ct_plain"] += (long)G * s.n1 * s.n2;
+    }
     std::vector<int> gk(s.n2);
     for (int g = 0; g < s.n2; ++g) gk[g] = s.B * s.n1 * g;
     for (int q0 = 0; q0 < G; q0 += blk::kMaxGroups) {
       const int ng = std::min(blk::kMaxGroups, G - q0);
-      blk::BabyPtrs bp{};
       blk::InnerPtrs ip{};
       std::vector<std::vector<Ciphertext>> inner(ng, std::vector<Ciphertext>(s.n2));
       for (int q = 0; q < ng; ++q) {
-        const auto& baby = babies[q0 + q];
-        for (int j = 0; j < s.n1; ++j) {
-          const ckks::DevPoly& p = baby[j]->handle()->p;
-          if (p.limbs != limbs) throw ckks::Error(CKKS_ELEVEL, "baby steps at different levels");
-          bp.c0[q][j] = p.data;
-          bp.c1[q][j] = p.data + (size_t)p.cap * C.N;
+        const double sc = babies[0][q0 + q][0]->scale() * dgs[0]->scale;
+        for (int t = 1; t < nt; ++t) {
+          const double st_ = babies[t][q0 + q][0]->scale() * dgs[t]->scale;
+          if (std::fabs(st_ - sc) > 1e-9 * sc) throw ckks::Error(CKKS_ESCALE, "product terms at different scales");
         }
-        const double sc = baby[0]->scale() * dg.scale;
         for (int g = 0; g < s.n2; ++g) {
           inner[q][g] = cc.fresh();
           ckks::DevPoly& p = inner[q][g]->handle()->p;
           p.ensure(&C, 2, limbs);
           p.limbs = limbs;
           p.scale = sc;
-          p.deg = baby[0]->noise_deg() + 1;
+          p.deg = babies[0][q0 + q][0]->noise_deg() + 1;
           ip.c0[q][g] = p.data;
           ip.c1[q][g] = p.data + (size_t)p.cap * C.N;
         }
       }
-      {
+      for (int t = 0; t < nt; ++t) {
+        blk::BabyPtrs bp{};
+        for (int q = 0; q < ng; ++q) {
+          const auto& baby = babies[t][q0 + q];
+          for (int j = 0; j < s.n1; ++j) {
+            const ckks::DevPoly& p = baby[j]->handle()->p;
+            if (p.limbs != limbs) throw ckks::Error(CKKS_ELEVEL, "baby steps at different levels");
+            bp.c0[q][j] = p.data;
+            bp.c1[q][j] = p.data + (size_t)p.cap * C.N;
+          }
+        }
+        const Diag& dg = *dgs[t];
+        const bool acc = t > 0;
         ckks::ProfScope ps(
             C, "bsgs_inner",
-            ((double)s.n1 * s.n2 * limbs + ng * (2.0 * s.n1 * limbs + 2.0 * s.n2 * limbs)) * C.limb_bytes(), C.stream);
+            ((double)s.n1 * s.n2 * limbs + ng * (2.0 * s.n1 * limbs + (acc ? 4.0 : 2.0) * s.n2 * limbs)) *
+                C.limb_bytes(),
+            C.stream);
         // runs of limbs with primes below kFpPrime take the float64
         // products, the others (the 60-bit first prime) the integer ones
         for (int l0 = 0; l0 < limbs;) {
@@ -955,17 +1000,19 @@ struct ckks_block {
                            : (s.n1 == 32   ? blk::bsgs_inner_reg_int_kernel<32>
                               : s.n1 == 16 ? blk::bsgs_inner_reg_int_kernel<16>
                                            : blk::bsgs_inner_reg_int_kernel<8>);
-            kern<<<rgrid, blk::kBsgsRegThreads, 0, C.stream>>>(bp, ng, dg.data, ip, C.logN, s.n2, l0, C.d_mods);
-          } else if (fp)
+            kern<<<rgrid, blk::kBsgsRegThreads, 0, C.stream>>>(bp, ng, dg.data, ip, C.logN, s.n2, l0, acc,
+                                                               C.d_mods);
+          } else if (fp) {
             blk::bsgs_inner_fp_kernel<<<grid, dim3(blk::kBsgsThreads, ng), 0, C.stream>>>(
-                bp, ng, s.n1, dg.data, ip, limbs, C.logN, s.n2, l0, C.d_mods);
-          else
+                bp, ng, s.n1, dg.data, ip, limbs, C.logN, s.n2, l0, acc, C.d_mods);
+          } else {
             blk::bsgs_inner_kernel<<<grid, dim3(blk::kBsgsThreads, ng), 0, C.stream>>>(
-                bp, ng, s.n1, dg.data, ip, limbs, C.logN, s.n2, l0, C.d_mods);
+                bp, ng, s.n1, dg.data, ip, limbs, C.logN, s.n2, l0, acc, C.d_mods);
+          }
           l0 = l1;
         }
+        CKKS_CUDA(cudaGetLastError());
       }
-      CKKS_CUDA(cudaGetLastError());
       // giant steps: sum_g rot(inner_g, B n1 g), the key switches summed in the
       // extended basis with one ModDown (g = 0 is the identity)
       for (int q = 0; q < ng; ++q) {
@@ -1310,14 +1357,16 @@ void ckks_block::shard_mlp(const std::vector<int>& groups, int c0, int c1) {
   const auto ge = client_encrypt(dv, G * nc, gelu_limbs);
   C.release(dv);
   count["client_round_trips"] += (long)G * nc;
-  std::vector<Ciphertext> mlp(G);
+  // down projection: the chunks' products summed before one set of giant
+  // steps per group
   auto gb = babies_of_batch(ge);  // item i * nc + c
+  std::vector<std::vector<std::vector<Ciphertext>>> db(nc);
+  std::vector<int> dids;
   for (int c = 0; c < nc; ++c) {
-    std::vector<std::vector<Ciphertext>> db;
-    for (int i = 0; i < G; ++i) db.push_back(std::move(gb[(size_t)i * nc + c]));
-    const auto pc = bsgs_groups(db, 4 + nfc + c0 + c);
-    for (int i = 0; i < G; ++i) mlp[i] = c ? add(mlp[i], pc[i]) : pc[i];
+    for (int i = 0; i < G; ++i) db[c].push_back(std::move(gb[(size_t)i * nc + c]));
+    dids.push_back(4 + nfc + c0 + c);
   }
+  const std::vector<Ciphertext> mlp = bsgs_sum_groups(db, dids);
   for (int i = 0; i < G; ++i) st_mlp[groups[i]] = mlp[i];
   stamp("oproj_ln2_mlp");
 }
