@@ -228,6 +228,10 @@ int ckks_rotate_sum_hoisted(ckks_ctx* ctx, const ckks_ct* const* in, int count, 
  * slot values as AccumulateSum, different rounding noise. */
 int ckks_window_sum_batch(ckks_ctx* ctx, const ckks_ct* const* in, int count, int window, int stride,
                           ckks_ct* const* outs);
+/* the same with a base-r ladder (2 <= r <= 33; keys stride * r^s * {1 .. r-1}):
+ * fewer ModUp/ModDown pairs (ceil(log_r window) per input) for more key products */
+int ckks_window_sum_batch_radix(ckks_ctx* ctx, const ckks_ct* const* in, int count, int window, int stride,
+                                int radix, ckks_ct* const* outs);
 
 /* Kernel timer (the reference's per-call-site Profiler buckets,
  * fhe/gpu_real_scheme_b/src/real_dnagpt_fides_scheme_b_lintransform.cpp:627-629,

@@ -329,7 +329,7 @@ class CryptoContextImpl {
   }
   // [sum_{j < window} rot(x, j * stride) for x in a]: the AccumulateSum
   // ladder with one ModDown per step
-  std::vector<Ciphertext> WindowSumBatch(const std::vector<Ciphertext>& a, int window, int stride) {
+  std::vector<Ciphertext> WindowSumBatch(const std::vector<Ciphertext>& a, int window, int stride, int radix = 4) {
     std::vector<Ciphertext> outs;
     std::vector<const ckks_ct*> in;
     std::vector<ckks_ct*> hs;
@@ -338,7 +338,7 @@ class CryptoContextImpl {
       in.push_back(x->handle());
       hs.push_back(outs.back()->handle());
     }
-    check(ckks_window_sum_batch(h_, in.data(), (int)a.size(), window, stride, hs.data()));
+    check(ckks_window_sum_batch_radix(h_, in.data(), (int)a.size(), window, stride, radix, hs.data()));
     return outs;
   }
   // degree-1 ciphertext at `limbs` limbs with that level's FLEXIBLEAUTO scale

@@ -305,10 +305,10 @@ class Oracle:
         self._check(self.L_.oc_rotate_sum(self._c(), _p(cts), cts.shape[2], _p(kk), len(kk), _p(out)))
         return out
 
-    def window_sum(self, ct, window: int, stride: int):
+    def window_sum(self, ct, window: int, stride: int, radix: int = 4):
         ct = np.ascontiguousarray(ct, np.uint64)
         out = np.empty_like(ct)
-        self._check(self.L_.oc_window_sum(self._c(), _p(ct), ct.shape[1], window, stride, _p(out)))
+        self._check(self.L_.oc_window_sum_radix(self._c(), _p(ct), ct.shape[1], window, stride, radix, _p(out)))
         return out
 
     def accumulate_sum(self, ct, count: int, stride: int):

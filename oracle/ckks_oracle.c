@@ -1305,16 +1305,27 @@ int oc_rotate_sum(const oc_ctx* c, const uint64_t* cts, int limbs, const int* ks
  * key switches added in the extended basis, one ModDown per step) -- the
  * engine's hoisted window sums. */
 int oc_window_sum(const oc_ctx* c, const uint64_t* ct, int limbs, int window, int stride, uint64_t* out) {
+    return oc_window_sum_radix(c, ct, limbs, window, stride, 4, out);
+}
+
+/* the same with a base-r ladder: step s sums the rotations by
+ * stride * s * {0 .. r-1} below the window as one rotation sum */
+int oc_window_sum_radix(const oc_ctx* c, const uint64_t* ct, int limbs, int window, int stride, int radix,
+                        uint64_t* out) {
+    if (radix < 2 || radix > 33) { set_err("radix must be 2..33"); return -1; }
     const size_t S2 = 2 * (size_t)limbs * c->N;
     memcpy(out, ct, sizeof(uint64_t) * S2);
-    uint64_t* rep = (uint64_t*)malloc(sizeof(uint64_t) * 4 * S2);
-    for (long step = 1; step < window; step *= 4) {
-        int ks[4] = {0, 0, 0, 0}, n = 1;
-        for (int m = 1; m < 4 && step * m < window; m++) ks[n++] = (int)(stride * step * m);
+    uint64_t* rep = (uint64_t*)malloc(sizeof(uint64_t) * (size_t)radix * S2);
+    int* ks = (int*)malloc(sizeof(int) * (size_t)radix);
+    for (long step = 1; step < window; step *= radix) {
+        int n = 1;
+        ks[0] = 0;
+        for (int m = 1; m < radix && step * m < window; m++) ks[n++] = (int)(stride * step * m);
         for (int r = 0; r < n; r++) memcpy(rep + (size_t)r * S2, out, sizeof(uint64_t) * S2);
-        if (oc_rotate_sum(c, rep, limbs, ks, n, out)) { free(rep); return -1; }
+        if (oc_rotate_sum(c, rep, limbs, ks, n, out)) { free(rep); free(ks); return -1; }
     }
     free(rep);
+    free(ks);
     return 0;
 }
 

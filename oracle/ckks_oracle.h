@@ -121,6 +121,8 @@ int oc_rotate_sum(const oc_ctx* c, const uint64_t* cts, int limbs, const int* ks
 int oc_accumulate_sum(const oc_ctx* c, const uint64_t* ct, int limbs, int count, int stride, uint64_t* out);
 /* the engine's window sums: the same ladder, one ModDown per step */
 int oc_window_sum(const oc_ctx* c, const uint64_t* ct, int limbs, int window, int stride, uint64_t* out);
+int oc_window_sum_radix(const oc_ctx* c, const uint64_t* ct, int limbs, int window, int stride, int radix,
+                        uint64_t* out);
 
 /* ModUp / ModDown exposed for limb-level parity of the key-switch stages.
  * modup: d in coefficient form (limbs) -> digits x (limbs+K) NTT form.

@@ -128,6 +128,8 @@ _SIGS = [
     ("ckks_rotate_sum_hoisted", ctypes.c_int, [_vp, _vp, ctypes.c_int, ctypes.POINTER(ctypes.c_int), ctypes.c_int,
                                                _vp]),
     ("ckks_window_sum_batch", ctypes.c_int, [_vp, _vp, ctypes.c_int, ctypes.c_int, ctypes.c_int, _vp]),
+    ("ckks_window_sum_batch_radix", ctypes.c_int, [_vp, _vp, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int,
+                                                   _vp]),
     ("ckks_profile_enable", ctypes.c_int, [_vp, ctypes.c_int]),
     ("ckks_profile_reset", ctypes.c_int, [_vp]),
     ("ckks_profile_report", ctypes.c_int, [_vp, ctypes.c_char_p, ctypes.c_size_t]),
@@ -642,13 +644,14 @@ class CryptoContext:
                                              (ctypes.c_int * nk)(*ks), nk, (_vp * max(1, n))(*[o.h for o in outs])))
         return outs
 
-    def WindowSumBatch(self, cts, window: int, stride: int) -> list[Ciphertext]:
-        """[sum_{j < window} EvalRotate(ct, j * stride) for ct in cts]: the
-        AccumulateSum ladder with one ModDown per step."""
+    def WindowSumBatch(self, cts, window: int, stride: int, radix: int = 4) -> list[Ciphertext]:
+        """[sum_{j < window} EvalRotate(ct, j * stride) for ct in cts]: a
+        base-radix ladder (the AccumulateSum ladder for radix 4) with one
+        ModDown per step."""
         n = len(cts)
         outs = [self._new() for _ in cts]
-        _check(lib().ckks_window_sum_batch(self.h, (_vp * max(1, n))(*[c.h for c in cts]), n, window, stride,
-                                           (_vp * max(1, n))(*[o.h for o in outs])))
+        _check(lib().ckks_window_sum_batch_radix(self.h, (_vp * max(1, n))(*[c.h for c in cts]), n, window, stride,
+                                                 radix, (_vp * max(1, n))(*[o.h for o in outs])))
         return outs
 
 

@@ -818,11 +818,14 @@ struct ckks_block {
   }
 
   // per head, the sum of its HD features at the head's first feature (and
-  // window sums elsewhere): a base-4 ladder of hoisted rotation sums
+  // window sums elsewhere): a base-8 ladder of hoisted rotation sums (two
+  // steps for 64 features; at 2 limbs a step's ModUp and ModDown cost more
+  // than its seven key products)
+  static constexpr int kHeadRadix = 8;
   std::vector<Ciphertext> head_window_sums(const std::vector<Ciphertext>& h) {
-    for (long step = 1; step < s.HD; step *= 4)
-      for (int m = 1; m < 4 && step * m < s.HD; ++m) count["rotations"] += (long)h.size();
-    return cc.WindowSumBatch(h, s.HD, s.B);
+    for (long step = 1; step < s.HD; step *= kHeadRadix)
+      for (int m = 1; m < kHeadRadix && step * m < s.HD; ++m) count["rotations"] += (long)h.size();
+    return cc.WindowSumBatch(h, s.HD, s.B, kHeadRadix);
   }
 
   // weight id -> (device matrix, out_dim, in_dim, leading dimension)
@@ -1072,8 +1075,8 @@ std::vector<int> ckks_block::rotation_indices() const {
     v.push_back(canon(d - s.B));
     v.push_back(canon((long)d * s.B));  // packing alignment d to feature h*HD - d (baby keys when n1 >= B)
   }
-  for (long step = 1; step < s.HD; step *= 4)  // head window sums: the same ladder over HD features
-    for (int m = 1; m < 4 && step * m < s.HD; ++m) v.push_back(canon((long)s.B * step * m));
+  for (long step = 1; step < s.HD; step *= kHeadRadix)  // head window sums: base-8 ladder over HD features
+    for (int m = 1; m < kHeadRadix && step * m < s.HD; ++m) v.push_back(canon((long)s.B * step * m));
   std::sort(v.begin(), v.end());
   v.erase(std::unique(v.begin(), v.end()), v.end());
   v.erase(std::remove(v.begin(), v.end(), 0), v.end());

@@ -1319,24 +1319,31 @@ int ckks_rotate_sum_hoisted(ckks_ctx* ctx, const ckks_ct* const* in, int count, 
 
 int ckks_window_sum_batch(ckks_ctx* ctx, const ckks_ct* const* in, int count, int window, int stride_,
                           ckks_ct* const* outs) {
+  return ckks_window_sum_batch_radix(ctx, in, count, window, stride_, 4, outs);
+}
+
+int ckks_window_sum_batch_radix(ckks_ctx* ctx, const ckks_ct* const* in, int count, int window, int stride_,
+                                int radix, ckks_ct* const* outs) {
   return guard([&] {
     Context& c = C(ctx);
     need(count >= 0 && (count == 0 || (in && outs)), CKKS_EARG, "bad batch");
     need(window >= 1, CKKS_EARG, "window must be positive");
+    need(radix >= 2 && radix <= ckks::kKsBatch + 1, CKKS_EARG, "radix must be 2..33");
     for (int i = 0; i < count; ++i) {
       same_ctx(ctx, in[i]);
       need(outs[i] && outs[i]->owner == ctx, CKKS_EARG, "bad output handle");
     }
     if (!count) return;
-    // base-4 ladder: step s adds the rotations by stride * s * {1, 2, 3}
+    // base-r ladder: step s adds the rotations by stride * s * {1 .. r-1}
     // (those below the window) to the running sums, hoisted per ciphertext
     std::vector<ckks_ct> acc(count);
     std::vector<const ckks_ct*> cur(in, in + count);
-    for (long step = 1; step < window; step *= 4) {
-      int ks[4] = {0, 0, 0, 0}, nk = 1;
-      for (int m = 1; m < 4 && step * m < window; ++m) ks[nk++] = (int)(stride_ * step * m);
+    for (long step = 1; step < window; step *= radix) {
+      std::vector<int> ks{0};
+      for (int m = 1; m < radix && step * m < window; ++m) ks.push_back((int)(stride_ * step * m));
+      const int nk = (int)ks.size();
       std::vector<DevPoly> res;
-      hoisted_sum_batch(c, cur.data(), count, ks, nk, res);
+      hoisted_sum_batch(c, cur.data(), count, ks.data(), nk, res);
       for (int i = 0; i < count; ++i) {
         acc[i].owner = ctx;
         take(acc[i].p, res[i]);

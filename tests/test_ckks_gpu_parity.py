@@ -37,7 +37,8 @@ def make_pair(logN, L, dnum, seed, rot=(), relin=True):
     return o, cc
 
 
-ROT = [1, 2, 3, 5, -1, -7, 8, 64, 100] + ladder_keys(64, 4) + ladder_keys(16, 32)
+ROT = ([1, 2, 3, 5, -1, -7, 8, 64, 100] + ladder_keys(64, 4) + ladder_keys(16, 32)
+       + [4 * m for m in range(1, 8)] + [32 * m for m in range(1, 8)])  # base-8 ladder of 64 at stride 4
 
 
 @pytest.fixture(scope="module")
@@ -235,17 +236,18 @@ def test_accumulate_sum_bit_exact(pair10, count, stride):
     assert np.array_equal(got.limbs_array(), o.accumulate_sum(rx, count, stride))
 
 
-@pytest.mark.parametrize("window,stride,limbs", [(64, 4, None), (16, 32, None), (64, 4, 2), (1, 4, 3)])
-def test_window_sums_bit_exact(pair10, window, stride, limbs):
+@pytest.mark.parametrize("window,stride,limbs,radix", [(64, 4, None, 4), (16, 32, None, 4), (64, 4, 2, 4),
+                                                        (1, 4, 3, 4), (64, 4, 2, 8), (64, 4, None, 8)])
+def test_window_sums_bit_exact(pair10, window, stride, limbs, radix):
     """Batched hoisted window sums (three inputs per launch) against the
-    oracle's ladder of rotation sums."""
+    oracle's ladder of rotation sums (base 4 and base 8)."""
     o, cc = pair10
     lv = o.L if limbs is None else limbs
     fs = [_fresh(o, cc, 40 + i, lv) for i in range(3)]
-    got = cc.WindowSumBatch([f[2] for f in fs], window, stride)
+    got = cc.WindowSumBatch([f[2] for f in fs], window, stride, radix)
     for f, g in zip(fs, got):
         assert g.limbs == lv
-        assert np.array_equal(g.limbs_array(), o.window_sum(f[1], window, stride))
+        assert np.array_equal(g.limbs_array(), o.window_sum(f[1], window, stride, radix))
 
 
 def test_hoisted_rotation_sum_equals_the_rotation_sum(pair10):

@@ -41,7 +41,7 @@ def small():
     o = Oracle(logN=10, L=6, dnum=3, seed=11)
     o.keygen()
     o.relin_keygen()
-    keys = [1, 2, 3, -1, 7, 8, 256]
+    keys = [1, 2, 3, -1, 7, 8, 256] + [32 * m for m in range(1, 8)]  # + the base-8 ladder of 8 at stride 32
     for c, st in ACC_CASES:
         keys += ladder_keys(c, st)
     o.rot_keygen(sorted(set(keys)))
@@ -223,6 +223,11 @@ def test_window_sum_equals_the_ladder_of_rotation_sums(small, count, stride):
         acc = o.rotate_sum(np.stack([acc] * len(ks)), ks)
         step *= 4
     assert np.array_equal(got, acc)
+    if count == 8:  # base 8: one step, the rotations by stride * {0 .. 7}
+        got8 = o.window_sum(ct, count, stride, 8)
+        ks = [stride * m for m in range(8)]
+        assert np.array_equal(got8, o.rotate_sum(np.stack([ct] * 8), ks))
+        assert np.abs(o.decode(o.decrypt(got8), S) - ref).max() < 1e-7
 
 
 @pytest.mark.parametrize("count,stride", ACC_CASES)
