@@ -490,8 +490,10 @@ def run_model(args):
     full-hidden-state client refresh between blocks and, with --head, the
     last-token refresh into the classifier head (N - A margin).  One step is
     one sequence through the whole model; under torchrun every rank runs its
-    own sequence (replicas, weak scaling).  Blocks beyond the diagonal-cache
-    budget of the device encode their diagonals again on every step."""
+    own sequence (replicas, weak scaling), or with --shard the ranks share one
+    sequence, every block sharded over them (strong scaling, shard.py
+    ShardedModel).  Blocks beyond the diagonal-cache budget of the device
+    encode their diagonals again on every step."""
     import torch
     import private_genomic_dnagpt_b200 as eng
     from oracle import plain_block
@@ -505,13 +507,15 @@ def run_model(args):
         import datetime
         import torch.distributed as dist
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=900))
-    cc = eng.GenCryptoContext(eng.CCParams(ring_dim_log=LOG_N, limbs=LIMBS, dnum=DNUM, seed=1 + rank,
-                                           device=local))
+    sharded = dist is not None and args.shard
+    # sharded: identical keys (same seed) and one sequence on every rank
+    cc = eng.GenCryptoContext(eng.CCParams(ring_dim_log=LOG_N, limbs=LIMBS, dnum=DNUM,
+                                           seed=1 if sharded else 1 + rank, device=local))
     cc.KeyGen()
     cc.EvalMultKeyGen()
     ws = [plain_block.synthetic_weights(100 + b) for b in range(args.blocks)]
     hw = plain_block.synthetic_head_weights(99) if args.head else None
-    x = plain_block.synthetic_input(6 + rank, args.tokens)
+    x = plain_block.synthetic_input(6 if sharded else 6 + rank, args.tokens)
     # diagonal caches: about 26 GB per block; keep what fits beside the keys
     free, _ = torch.cuda.mem_get_info(local)
     # headroom: one block re-encoding its diagonals (26 GB), keys (~8 GB) and
@@ -521,6 +525,12 @@ def run_model(args):
     cc.EvalRotateKeyGen(model.rotation_indices())
     stream = torch.cuda.ExternalStream(cc.stream_handle())
     h_ref, m_ref = plain_block.model(x, ws, hw)
+    forward = model.forward
+    if sharded:
+        from private_genomic_dnagpt_b200 import shard
+        sm = shard.ShardedModel([shard.EngineIO(b) for b in model.blocks], model.head, args.tokens, 32,
+                                plain_block.HEADS, plain_block.D, dist, "cuda", cached_blocks=model.cached_blocks)
+        forward = sm.forward
 
     def barrier():
         cc.Synchronize()
@@ -529,7 +539,7 @@ def run_model(args):
             dist.barrier()
 
     for _ in range(args.warmup):
-        h, m = model.forward(x)
+        h, m = forward(x)
     err = plain_block.rel_inf(h_ref, h)
     assert err < 1e-6, f"model hidden-state error {err}"
     barrier()
@@ -539,10 +549,13 @@ def run_model(args):
             e0 = torch.cuda.Event(enable_timing=True)
             e1 = torch.cuda.Event(enable_timing=True)
             e0.record(stream)
-            h, m = model.forward(x)
+            h, m = forward(x)
             e1.record(stream)
             e1.synchronize()
             steps_s.append(e0.elapsed_time(e1) / 1e3)
+            if sharded:  # device time of the whole sharded sequence, exchanges included
+                eval_s.append(steps_s[-1])
+                continue
             ev = sum(b.report()["seconds"].get("evaluate_events", 0.0) for b in model.blocks)
             if model.head is not None:
                 ev += model.head.report()["seconds"].get("head_total", 0.0)
@@ -560,11 +573,15 @@ def run_model(args):
         line = {
             "metric": f"encrypted {name} latency (s) @{args.tokens} tok, N=2^16", "value": value, "unit": "s",
             "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": e2e * 1e3,
-            "higher_is_better": False, "scaling": "weak", "vs_baseline": None, "dtype": "u64", "data": "synthetic",
-            "config": {"workload": f"{name}, one sequence per GPU, {args.tokens} tokens, D=768, 12 heads, "
-                                   f"MLP 3072, N=2^16, 24 limbs, dnum=3; full-hidden-state client refresh between "
-                                   f"blocks", "cached_blocks": model.cached_blocks,
-                       "parallelism": f"replicas{world}", "flush": "inputs > L2 (keys, diagonals)",
+            "higher_is_better": False, "scaling": "strong" if sharded else "weak", "vs_baseline": None,
+            "dtype": "u64", "data": "synthetic",
+            "config": {"workload": f"{name}, " + ("one sequence sharded over the GPUs" if sharded else
+                                                  "one sequence per GPU") +
+                                   f", {args.tokens} tokens, D=768, 12 heads, MLP 3072, N=2^16, 24 limbs, dnum=3; "
+                                   f"full-hidden-state client refresh between blocks",
+                       "cached_blocks": model.cached_blocks,
+                       "parallelism": f"shard{world}" if sharded else f"replicas{world}",
+                       "flush": "inputs > L2 (keys, diagonals)",
                        "rel_inf_vs_plaintext": err,
                        "margin": m, "margin_plaintext": m_ref},
             "e2e": {"value": e2e, "unit": "s", "h2d_bytes_per_step": args.blocks * groups * ct_bytes,

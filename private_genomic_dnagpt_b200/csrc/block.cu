@@ -611,7 +611,7 @@ struct ckks_block {
     const double t0 = blk::now_s();
     const size_t stride = (size_t)limbs * C.N;
     uint64_t* pt = (uint64_t*)C.alloc(sizeof(uint64_t) * (size_t)M * stride);
-    ckks::encode_batch(C, dvals, M, limbs, S(limbs), pt, stride, C.stream);
+    ckks::encode_batch(C, dvals, M, limbs, S(limbs), pt, stride, C.stream, /*ntt=*/false);
     std::vector<Ciphertext> out(M);
     std::vector<uint64_t*> c0(M), c1(M);
     for (int m = 0; m < M; ++m) {
@@ -624,7 +624,7 @@ struct ckks_block {
       c0[m] = p.data;
       c1[m] = p.data + (size_t)p.cap * C.N;
     }
-    ckks::encrypt_batch(C, pt, limbs, M, c0.data(), c1.data(), C.stream);
+    ckks::encrypt_batch_coef(C, pt, limbs, M, c0.data(), c1.data(), C.stream);
     C.release(pt);
     client_seconds += blk::now_s() - t0;
     return out;
@@ -1125,7 +1125,7 @@ void ckks_block::shard_inputs(const double* x, int T) {
   st_mlp.assign(G, Ciphertext());
   // client: pack and encrypt the embeddings (T123.cpp:1642-1661)
   double* dx = dbuf((size_t)T * D);
-  CKKS_CUDA(cudaMemcpyAsync(dx, x, sizeof(double) * T * D, cudaMemcpyHostToDevice, C.stream));
+  C.stage_upload(dx, x, sizeof(double) * T * D, C.stream);
   double* dvals = dbuf((size_t)G * SL);
   blk::pack_kernel<<<dim3(nb, G), blk::kThreads, 0, C.stream>>>(dx, dvals, T, D, s.B, SL);
   st_x = client_encrypt(dvals, G, LX);
@@ -1228,7 +1228,7 @@ void ckks_block::shard_scores(const std::vector<blk::TileTag>& tiles, double* d_
     double* dv = dbuf((size_t)P * SL);
     client_decrypt(packed, dv);
     blk::ScoreTag* dt = (blk::ScoreTag*)C.alloc(sizeof(blk::ScoreTag) * st.size());
-    CKKS_CUDA(cudaMemcpyAsync(dt, st.data(), sizeof(blk::ScoreTag) * st.size(), cudaMemcpyHostToDevice, C.stream));
+    C.stage_upload(dt, st.data(), sizeof(blk::ScoreTag) * st.size(), C.stream);
     blk::score_gather_kernel<<<dim3((unsigned)st.size(), H), 32 * ((B + 31) / 32), 0, C.stream>>>(
         dv, dt, T, H, HD, B, s.PW, SL, d_scores);
     CKKS_CUDA(cudaGetLastError());
@@ -1280,7 +1280,7 @@ void ckks_block::shard_context(const std::vector<blk::TileTag>& tiles) {
     const int M = (int)tags.size();
     double* dv = dbuf((size_t)M * SL);
     blk::TileTag* dt = (blk::TileTag*)C.alloc(sizeof(blk::TileTag) * M);
-    CKKS_CUDA(cudaMemcpyAsync(dt, tags.data(), sizeof(blk::TileTag) * M, cudaMemcpyHostToDevice, C.stream));
+    C.stage_upload(dt, tags.data(), sizeof(blk::TileTag) * M, C.stream);
     blk::weight_tile_kernel<<<dim3(nb, M), blk::kThreads, 0, C.stream>>>(st_prob, dt, T, H, HD, D, B, SL, dv);
     CKKS_CUDA(cudaGetLastError());
     const auto wa = client_encrypt(dv, M, lk);
@@ -1456,7 +1456,7 @@ double ckks_block::head_forward(const double* x_last) {
   if (C.L < kHeadLimbs) throw ckks::Error(CKKS_ELEVEL, "the head needs 5 Q limbs");
   const double t_start = blk::now_s();
   double* dx = dbuf(D);
-  CKKS_CUDA(cudaMemcpyAsync(dx, x_last, sizeof(double) * D, cudaMemcpyHostToDevice, C.stream));
+  C.stage_upload(dx, x_last, sizeof(double) * D, C.stream);
   double* dv = dbuf(SL);
   blk::pack_kernel<<<dim3(nb, 1), blk::kThreads, 0, C.stream>>>(dx, dv, 1, D, B, SL);
   const auto xin = client_encrypt(dv, 1, kHeadLimbs);

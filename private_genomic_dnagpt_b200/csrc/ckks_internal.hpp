@@ -220,6 +220,11 @@ class Context {
 
   void* alloc(size_t bytes) const;
   void release(void* p) const;
+  // host -> device copy of a small host array on stream `st` through a
+  // pinned staging ring, so that it does not synchronise the stream (a copy
+  // from pageable memory would); the ring waits for the stream only when it
+  // wraps.  Larger arrays are copied directly.
+  void stage_upload(void* dst, const void* src, size_t bytes, cudaStream_t st) const;
 
   mutable Profiler prof;
   double limb_bytes() const { return 8.0 * N; }
@@ -236,6 +241,9 @@ class Context {
   mutable std::unordered_map<size_t, std::vector<void*>> free_;
   mutable std::unordered_map<void*, size_t> size_of_;
   void drop_cache() const;
+  static constexpr size_t kStageBytes = 8u << 20;
+  mutable char* stage_ = nullptr;  // pinned host ring
+  mutable size_t stage_off_ = 0;
 };
 
 inline ProfScope::ProfScope(const Context& c, const char* name, double bytes, cudaStream_t s)
@@ -443,11 +451,17 @@ void decrypt_decode_batch(const Context& c, const uint64_t* const* c0, const uin
                           const double* scales_host, double* out, cudaStream_t st);
 void encrypt_batch(Context& c, const uint64_t* pts, int limbs, int M, uint64_t* const* c0, uint64_t* const* c1,
                    cudaStream_t st);
+// the same for plaintexts still in coefficient form ([M][limbs][N], consumed):
+// e0 is added to them before their forward transform (NTT(m + e0) = NTT(m) +
+// NTT(e0) exactly), so an encryption transforms three polynomials, not four;
+// the ciphertexts equal encrypt_batch's on the transformed plaintexts
+void encrypt_batch_coef(Context& c, uint64_t* pts_coef, int limbs, int M, uint64_t* const* c0, uint64_t* const* c1,
+                        cudaStream_t st);
 void decode_contiguous_batch(const Context& c, uint64_t* pts, int use, int M, const double* scales, double* out,
                              cudaStream_t st);
 // batch x (N/2) device values -> batch plaintexts of `limbs` limbs, out_stride words apart
 void encode_batch(const Context& c, const double* d_values, int batch, int limbs, double scale, uint64_t* out,
-                  size_t out_stride, cudaStream_t st);
+                  size_t out_stride, cudaStream_t st, bool ntt = true);
 void decode(const Context& c, const uint64_t* pt, int limbs, double scale, double* d_values, cudaStream_t st);
 
 // integer / double residues on the host

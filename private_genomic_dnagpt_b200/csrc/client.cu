@@ -118,6 +118,46 @@ __global__ void __launch_bounds__(kThreads) enc_spread_kernel(const int* __restr
   out[((size_t)ms * limbs + l) * N + n] = x >= 0 ? (uint64_t)x : q - (uint64_t)(-x);
 }
 
+// u and e1 of item m into r ([m][2][limbs]); e0 added onto the item's
+// coefficient-form plaintext
+__global__ void __launch_bounds__(kThreads) enc_spread_coef_kernel(const int* __restrict__ v, uint64_t* __restrict__ r,
+                                                                   uint64_t* __restrict__ pts, int limbs, int logN,
+                                                                   const Mod* __restrict__ mods) {
+  const int N = 1 << logN;
+  const int n = blockIdx.x * kThreads + threadIdx.x;
+  if (n >= N) return;
+  const int l = blockIdx.y % limbs, ms = blockIdx.y / limbs;  // ms = m * 3 + sub
+  const int m = ms / 3, sub = ms % 3;
+  const uint64_t q = mods[l].q;
+  const int x = v[(size_t)ms * N + n];
+  const uint64_t res = x >= 0 ? (uint64_t)x : q - (uint64_t)(-x);
+  if (sub == 1) {
+    uint64_t* p = pts + ((size_t)m * limbs + l) * N + n;
+    *p = add_mod(*p, res, q);
+  } else {
+    r[((size_t)(2 * m + (sub >> 1)) * limbs + l) * N + n] = res;
+  }
+}
+
+__global__ void __launch_bounds__(kThreads) enc_combine_coef_kernel(const uint64_t* __restrict__ pb,
+                                                                    const uint64_t* __restrict__ pa,
+                                                                    const uint64_t* __restrict__ r,
+                                                                    const uint64_t* __restrict__ pts,
+                                                                    uint64_t** c0s, uint64_t** c1s, int limbs,
+                                                                    int logN, const Mod* __restrict__ mods) {
+  const int N = 1 << logN;
+  const int n = blockIdx.x * kThreads + threadIdx.x;
+  if (n >= N) return;
+  const int l = blockIdx.y, m = blockIdx.z;
+  const Mod md = mods[l];
+  const size_t o_l = (size_t)l * N + n;
+  const size_t S = (size_t)limbs * N;
+  const uint64_t* rm = r + (size_t)m * 2 * S;  // u, e1
+  const uint64_t uv = rm[o_l];
+  c0s[m][o_l] = add_mod(mul_mod(pb[o_l], uv, md), pts[(size_t)m * S + o_l], md.q);
+  c1s[m][o_l] = add_mod(mul_mod(pa[o_l], uv, md), rm[S + o_l], md.q);
+}
+
 struct OutPtrs {
   uint64_t** c0;
   uint64_t** c1;
@@ -163,7 +203,7 @@ __global__ void __launch_bounds__(kThreads) dec_batch_kernel(InPtrs in, const ui
 template <typename T>
 T* upload_async(const Context& c, const std::vector<T>& v, cudaStream_t st) {
   T* d = (T*)c.alloc(sizeof(T) * v.size());
-  CKKS_CUDA(cudaMemcpyAsync(d, v.data(), sizeof(T) * v.size(), cudaMemcpyHostToDevice, st));
+  c.stage_upload(d, v.data(), sizeof(T) * v.size(), st);
   return d;
 }
 
@@ -200,6 +240,41 @@ void encrypt_batch(Context& c, const uint64_t* pts, int limbs, int M, uint64_t* 
     ProfScope ps(c, "enc_combine", 7.0 * M * limbs * c.limb_bytes(), st);
     enc_combine_batch_kernel<<<dim3((N + kThreads - 1) / kThreads, limbs, M), kThreads, 0, st>>>(
         c.d_pk, c.d_pk + (size_t)c.L * N, r, pts, OutPtrs{d0, d1}, limbs, c.logN, c.d_mods);
+  }
+  CKKS_CUDA(cudaGetLastError());
+  c.release(small);
+  c.release(r);
+  c.release(d0);
+  c.release(d1);
+}
+
+void encrypt_batch_coef(Context& c, uint64_t* pts, int limbs, int M, uint64_t* const* c0, uint64_t* const* c1,
+                        cudaStream_t st) {
+  if (!c.d_pk) throw Error(kErrState, "public key not generated");
+  if (M <= 0) return;
+  const int N = c.N;
+  const size_t S = (size_t)limbs * N;
+  int* small = (int*)c.alloc(sizeof(int) * (size_t)M * 3 * N);
+  uint64_t* r = (uint64_t*)c.alloc(sizeof(uint64_t) * (size_t)M * 2 * S);
+  const uint64_t counter0 = c.enc_counter;
+  c.enc_counter += (uint64_t)M;
+  {
+    ProfScope ps(c, "enc_sample", 12.0 * M * N, st);
+    enc_sample_kernel<<<dim3((N / 8 + kThreads - 1) / kThreads, M, 3), kThreads, 0, st>>>(
+        key_from_seed(c.params.seed), counter0, N, small);
+    enc_spread_coef_kernel<<<dim3((N + kThreads - 1) / kThreads, 3 * M * limbs), kThreads, 0, st>>>(
+        small, r, pts, limbs, c.logN, c.d_mods);
+  }
+  CKKS_CUDA(cudaGetLastError());
+  ntt_forward(c, r, M * 2 * limbs, LimbMap::q(limbs, c.L), st);
+  ntt_forward(c, pts, M * limbs, LimbMap::q(limbs, c.L), st);
+  std::vector<uint64_t*> h0(c0, c0 + M), h1(c1, c1 + M);
+  uint64_t** d0 = upload_async(c, h0, st);
+  uint64_t** d1 = upload_async(c, h1, st);
+  {
+    ProfScope ps(c, "enc_combine", 6.0 * M * limbs * c.limb_bytes(), st);
+    enc_combine_coef_kernel<<<dim3((N + kThreads - 1) / kThreads, limbs, M), kThreads, 0, st>>>(
+        c.d_pk, c.d_pk + (size_t)c.L * N, r, pts, d0, d1, limbs, c.logN, c.d_mods);
   }
   CKKS_CUDA(cudaGetLastError());
   c.release(small);

@@ -383,6 +383,7 @@ Context::Context(const Params& p) : params(p) {
 Context::~Context() {
   cudaSetDevice(params.device);
   cudaStreamSynchronize(stream);
+  if (stage_) cudaFreeHost(stage_);
   drop_cache();
   for (auto& kv : size_of_) cudaFree(kv.first);  // blocks still held by live objects
   size_of_.clear();
@@ -563,6 +564,24 @@ void* Context::alloc(size_t bytes) const {
   alloc_seconds += std::chrono::duration<double>(std::chrono::steady_clock::now() - t0).count();
   ++alloc_calls;
   return p;
+}
+
+void Context::stage_upload(void* dst, const void* src, size_t bytes, cudaStream_t st) const {
+  if (!bytes) return;
+  const size_t span = (bytes + 255) & ~(size_t)255;
+  if (span > kStageBytes) {
+    CKKS_CUDA(cudaMemcpyAsync(dst, src, bytes, cudaMemcpyHostToDevice, st));
+    return;
+  }
+  if (!stage_) CKKS_CUDA(cudaHostAlloc((void**)&stage_, kStageBytes, cudaHostAllocDefault));
+  if (stage_off_ + span > kStageBytes) {
+    // every copy out of the ring so far was issued on the context's stream
+    CKKS_CUDA(cudaStreamSynchronize(st));
+    stage_off_ = 0;
+  }
+  std::memcpy(stage_ + stage_off_, src, bytes);
+  CKKS_CUDA(cudaMemcpyAsync(dst, stage_ + stage_off_, bytes, cudaMemcpyHostToDevice, st));
+  stage_off_ += span;
 }
 
 void Context::release(void* p) const {

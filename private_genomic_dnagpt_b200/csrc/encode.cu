@@ -268,7 +268,7 @@ void fft_forward_batch(const Context& c, double2* v, int batch, cudaStream_t st)
 // values: batch x n doubles (device); out: batch polys of `limbs` limbs at
 // out_stride words apart, NTT form
 void encode_batch(const Context& c, const double* d_values, int batch, int limbs, double scale, uint64_t* out,
-                  size_t out_stride, cudaStream_t st) {
+                  size_t out_stride, cudaStream_t st, bool ntt) {
   const int n = c.N / 2;
   double2* v = (double2*)c.alloc(sizeof(double2) * (size_t)batch * n);
   const dim3 g((n + kThreads - 1) / kThreads, batch);
@@ -283,6 +283,7 @@ void encode_batch(const Context& c, const double* d_values, int batch, int limbs
   }
   CKKS_CUDA(cudaGetLastError());
   c.release(v);
+  if (!ntt) return;  // coefficient form, for encrypt_batch_coef
   if (out_stride == (size_t)limbs * c.N) {
     ntt_forward(c, out, batch * limbs, LimbMap::q(limbs, c.L), st);  // one launch pair for the batch
   } else {

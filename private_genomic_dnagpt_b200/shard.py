@@ -257,6 +257,41 @@ class ShardedBlock:
         return yt.cpu().numpy()
 
 
+class ShardedModel:
+    """Chained blocks, each sharded over the ranks (``ShardedBlock``), with
+    the client's full-hidden-state refresh between blocks -- the decrypted
+    output of one block is the next block's input (the 12-block driver's
+    refresh, 12blocks_head_cpudiagcache_t123_v3.cpp:452-470) -- and the
+    classifier head on the last token, evaluated by rank 0 and broadcast
+    (V3:480-510).  ``ios`` holds one engine adapter per block; blocks with
+    index >= ``cached_blocks`` drop their encoded diagonals after each use
+    (``io.release_cache()``)."""
+
+    def __init__(self, ios, head, tokens: int, batch: int, heads: int, d_model: int, dist, device,
+                 cached_blocks: int | None = None):
+        self.blocks = [ShardedBlock(io, tokens, batch, heads, d_model, dist, device) for io in ios]
+        self.head, self.dist, self.device = head, dist, device
+        self.rank = dist.get_rank()
+        self.cached_blocks = len(ios) if cached_blocks is None else cached_blocks
+
+    def forward(self, x: np.ndarray):
+        """Returns (hidden [tokens, D] of the last block, head margin or None)
+        on every rank."""
+        import torch
+        h = np.asarray(x, np.float64)
+        for i, sb in enumerate(self.blocks):
+            h = sb.forward(h)
+            if i >= self.cached_blocks:
+                sb.io.release_cache()
+        if self.head is None:
+            return h, None
+        m = torch.zeros(1, dtype=torch.float64, device=self.device)
+        if self.rank == 0:
+            m[0] = self.head.forward(h[-1])
+        self.dist.broadcast(m, src=0)
+        return h, float(m.cpu()[0])
+
+
 class EngineIO:
     """Adapter from ShardedBlock to an EncryptedBlock on this rank's GPU: all
     device work on the engine stream, collectives on the same stream."""
@@ -291,6 +326,9 @@ class EngineIO:
 
     def mlp(self, groups, chunk_begin, chunk_end):
         self.b.shard_mlp(groups, chunk_begin, chunk_end)
+
+    def release_cache(self):
+        self.b.release_cache()
 
     def finish(self, groups, y):
         self.b.shard_finish(groups, y)

@@ -163,6 +163,9 @@ class PlainIO:
         for g in groups:
             y[self.rows(g)] = self.state[(6, g)] + self.state[(5, g)]
 
+    def release_cache(self):
+        pass
+
     def state_meta(self, kind, g):
         a = self.state.get((kind, g))
         return None if a is None else (float(a.shape[0]), 1.0, 1.0)
@@ -210,3 +213,44 @@ def test_sharded_block_over_gloo_ranks_equals_the_block(tmp_path, world, tokens)
     y = np.load(out)
     ref = plain_block.block(plain_block.synthetic_input(4, tokens), plain_block.synthetic_weights(3))
     assert np.abs(y - ref).max() <= 1e-12 * np.abs(ref).max()
+
+
+class PlainHead:
+    def __init__(self, hw):
+        self.hw = hw
+
+    def forward(self, x_last):
+        return plain_block.head(x_last, self.hw)
+
+
+def _model_rank(rank, world, port, tokens, out_path):
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        ws = [plain_block.synthetic_weights(20 + b) for b in range(2)]
+        hw = plain_block.synthetic_head_weights(29)
+        x = plain_block.synthetic_input(4, tokens)
+        m = shard.ShardedModel([PlainIO(w, tokens) for w in ws], PlainHead(hw), tokens, B, 12, plain_block.D,
+                               dist, "cpu", cached_blocks=1)
+        h, margin = m.forward(x)
+        np.save(out_path + f".{rank}.npy", np.concatenate([h.ravel(), [margin]]))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("world", [2, 5])
+def test_sharded_two_block_model_with_head(tmp_path, world):
+    """Two chained blocks sharded over the ranks with the refresh between
+    them, and the head on rank 0: every rank ends with the plaintext
+    model's hidden state and margin."""
+    tokens = 70
+    out = str(tmp_path / "m")
+    mp.start_processes(_model_rank, args=(world, _free_port(), tokens, out), nprocs=world, join=True,
+                       start_method="spawn")
+    ws = [plain_block.synthetic_weights(20 + b) for b in range(2)]
+    h_ref, m_ref = plain_block.model(plain_block.synthetic_input(4, tokens), ws, plain_block.synthetic_head_weights(29))
+    for r in range(world):
+        got = np.load(out + f".{r}.npy")
+        assert np.abs(got[:-1] - h_ref.ravel()).max() <= 1e-12 * np.abs(h_ref).max()
+        assert abs(got[-1] - m_ref) <= 1e-12 * max(1.0, abs(m_ref))

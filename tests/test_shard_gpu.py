@@ -162,3 +162,49 @@ def test_block_sharded_over_two_gpus(tmp_path, tokens):
     err = plain_block.rel_inf(ref, y)
     print(f"{tokens} tokens sharded over 2 GPUs: rel_inf {err:.3e}")
     assert err < 1e-6
+
+
+def _model_rank(rank, world, port, tokens, out):
+    import datetime
+
+    import torch
+    import torch.distributed as dist
+    from private_genomic_dnagpt_b200 import shard
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=300),
+                            device_id=torch.device("cuda", rank))
+    try:
+        cc = eng.GenCryptoContext(eng.CCParams(ring_dim_log=16, limbs=24, dnum=3, seed=62, device=rank))
+        cc.KeyGen()
+        cc.EvalMultKeyGen()
+        ws = [plain_block.synthetic_weights(30 + b) for b in range(2)]
+        hw = plain_block.synthetic_head_weights(39)
+        x = plain_block.synthetic_input(6, tokens)
+        model = eng.EncryptedModel(cc, ws, hw, tokens, cached_blocks=1)
+        cc.EvalRotateKeyGen(model.rotation_indices())
+        sm = shard.ShardedModel([shard.EngineIO(b) for b in model.blocks], model.head, tokens, 32, 12, plain_block.D,
+                                dist, "cuda", cached_blocks=1)
+        h, m = sm.forward(x)
+        np.save(out + f".{rank}.npy", np.concatenate([h.ravel(), [m]]))
+        dist.barrier()
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.skipif(not __import__("torch").cuda.is_available() or __import__("torch").cuda.device_count() < 2,
+                    reason="needs two GPUs")
+def test_two_block_model_sharded_over_two_gpus(tmp_path):
+    """Two chained blocks (the second releasing its diagonals after use) and
+    the head, sharded over two GPUs with NCCL."""
+    import torch.multiprocessing as mp
+    tokens = 70
+    out = str(tmp_path / "m")
+    mp.start_processes(_model_rank, args=(2, _free_port(), tokens, out), nprocs=2, join=True, start_method="spawn")
+    ws = [plain_block.synthetic_weights(30 + b) for b in range(2)]
+    h_ref, m_ref = plain_block.model(plain_block.synthetic_input(6, tokens), ws, plain_block.synthetic_head_weights(39))
+    for r in range(2):
+        got = np.load(out + f".{r}.npy")
+        err = plain_block.rel_inf(h_ref, got[:-1].reshape(h_ref.shape))
+        print(f"rank {r}: hidden rel_inf {err:.3e}, margin {got[-1]:.6f} vs {m_ref:.6f}")
+        assert err < 1e-6 and abs(got[-1] - m_ref) < 1e-6
