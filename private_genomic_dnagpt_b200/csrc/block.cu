@@ -775,41 +775,63 @@ struct ckks_block {
     return rs(cc.EvalAdd(a, b));
   }
 
-  // lane shifts of x for every delta in `deltas` (0 -> x brought to the
-  // shifted level): one hoisted ModUp for all 2 |deltas| rotations, batched
-  // masks, one batched rescale
-  std::map<int, Ciphertext> lane_shifts(const Ciphertext& x, const std::vector<int>& deltas, int target_limbs) {
-    std::map<int, Ciphertext> out;
-    std::vector<int> idx, ds;
-    for (int d : deltas) {
-      if (d == 0) {
-        out[0] = reduce_to(x, target_limbs);
-        continue;
+  // lane shifts of several inputs (xs[i] for every delta in needs[i], 0 ->
+  // xs[i] brought to targets[i] limbs): inputs with the same deltas and level
+  // share one hoisted batch (each rotation key read once for all of them),
+  // then batched masks, adds and rescales
+  std::vector<std::map<int, Ciphertext>> lane_shifts_batch(const std::vector<Ciphertext>& xs,
+                                                           const std::vector<std::vector<int>>& needs,
+                                                           const std::vector<int>& targets) {
+    std::vector<std::map<int, Ciphertext>> out(xs.size());
+    std::map<std::pair<std::vector<int>, int>, std::vector<size_t>> bins;  // (deltas, limbs) -> inputs
+    for (size_t i = 0; i < xs.size(); ++i) {
+      std::vector<int> ds;
+      for (int d : needs[i]) {
+        if (d == 0)
+          out[i][0] = reduce_to(xs[i], targets[i]);
+        else
+          ds.push_back(d);
       }
-      ds.push_back(d);
-      idx.push_back(d);
-      idx.push_back(d - s.B);
+      std::sort(ds.begin(), ds.end());
+      ds.erase(std::unique(ds.begin(), ds.end()), ds.end());
+      if (!ds.empty()) bins[{ds, xs[i]->limbs()}].push_back(i);
     }
-    if (ds.empty()) return out;
-    count["rotations"] += (long)idx.size();
-    const auto r = cc.EvalFastRotation(x, idx);
-    const int l = x->limbs();
-    std::vector<Plaintext> masks;
-    for (size_t i = 0; i < ds.size(); ++i) {
-      masks.push_back(lane_plain(0, ds[i], true, l));
-      masks.push_back(lane_plain(0, ds[i], false, l));
+    for (const auto& bin : bins) {
+      const std::vector<int>& ds = bin.first.first;
+      const int l = bin.first.second;
+      const std::vector<size_t>& mem = bin.second;
+      std::vector<int> idx;
+      for (int d : ds) {
+        idx.push_back(d);
+        idx.push_back(d - s.B);
+      }
+      std::vector<Ciphertext> in;
+      for (size_t i : mem) in.push_back(xs[i]);
+      count["rotations"] += (long)idx.size() * (long)mem.size();
+      const auto r = cc.EvalFastRotationBatch(in, idx);
+      std::vector<Ciphertext> rot;
+      std::vector<Plaintext> masks;
+      for (size_t g = 0; g < mem.size(); ++g)
+        for (size_t k = 0; k < ds.size(); ++k) {
+          rot.push_back(r[g][2 * k]);
+          rot.push_back(r[g][2 * k + 1]);
+          masks.push_back(lane_plain(0, ds[k], true, l));
+          masks.push_back(lane_plain(0, ds[k], false, l));
+        }
+      count["ct_plain"] += (long)rot.size();
+      const auto prod = cc.EvalMultPlainBatch(rot, masks);
+      std::vector<Ciphertext> lo, hi;
+      for (size_t j = 0; j < prod.size(); j += 2) {
+        lo.push_back(prod[j]);
+        hi.push_back(prod[j + 1]);
+      }
+      const auto rs_ = cc.RescaleBatch(cc.EvalAddBatch(lo, hi));
+      for (size_t g = 0; g < mem.size(); ++g)
+        for (size_t k = 0; k < ds.size(); ++k) out[mem[g]][ds[k]] = rs_[g * ds.size() + k];
     }
-    count["ct_plain"] += (long)r.size();
-    const auto prod = cc.EvalMultPlainBatch(r, masks);
-    std::vector<Ciphertext> lo, hi;
-    for (size_t i = 0; i < ds.size(); ++i) {
-      lo.push_back(prod[2 * i]);
-      hi.push_back(prod[2 * i + 1]);
-    }
-    const auto rs_ = cc.RescaleBatch(cc.EvalAddBatch(lo, hi));
-    for (size_t i = 0; i < ds.size(); ++i) out[ds[i]] = rs_[i];
     return out;
   }
+
 
   // products a[i] * b[i], rescaled, batched
   std::vector<Ciphertext> mul_ct_rs_batch(const std::vector<Ciphertext>& a, const std::vector<Ciphertext>& b) {
@@ -1171,6 +1193,13 @@ void ckks_block::shard_scores(const std::vector<blk::TileTag>& tiles, double* d_
   // queries brought to the score level once per query group (a FLEXIBLEAUTO
   // level reduction is a scaled multiply and a rescale)
   std::map<int, Ciphertext> qr;
+  // scores are only decrypted: keys shifted from 4 limbs, products of 3-limb
+  // operands, head sums and decryption at 2; the key lane shifts of all key
+  // groups in one batch
+  std::vector<int> kgs, lks_of(s.groups, 0);
+  std::vector<Ciphertext> kx;
+  std::vector<std::vector<int>> kneed;
+  std::vector<int> ktarget;
   for (int kg = 0; kg < s.groups; ++kg) {
     const auto tags = tags_of(kg, tiles);
     if (tags.empty()) continue;
@@ -1180,10 +1209,19 @@ void ckks_block::shard_scores(const std::vector<blk::TileTag>& tiles, double* d_
       if (!st_q[tg.qg]) throw ckks::Error(CKKS_ESTATE, "query group not evaluated");
       if (std::find(need.begin(), need.end(), tg.d) == need.end()) need.push_back(tg.d);
     }
-    // scores are only decrypted: keys shifted from 4 limbs, products of
-    // 3-limb operands, head sums and decryption at 2
-    const int lks = std::min(st_q[tags[0].qg]->limbs() - 1, 3);
-    auto ks = lane_shifts(lower(st_k[kg], lks + 1), need, lks);
+    lks_of[kg] = std::min(st_q[tags[0].qg]->limbs() - 1, 3);
+    kgs.push_back(kg);
+    kx.push_back(lower(st_k[kg], lks_of[kg] + 1));
+    kneed.push_back(need);
+    ktarget.push_back(lks_of[kg]);
+  }
+  auto kshift = lane_shifts_batch(kx, kneed, ktarget);
+  kx.clear();
+  for (size_t ki = 0; ki < kgs.size(); ++ki) {
+    const int kg = kgs[ki];
+    const auto tags = tags_of(kg, tiles);
+    const int lks = lks_of[kg];
+    auto ks = std::move(kshift[ki]);
     count["cached_key_lane_shifts"] += (long)ks.size() - (ks.count(0) ? 1 : 0);
     std::vector<Ciphertext> qa, kb;
     for (const auto& tg : tags) {
@@ -1267,6 +1305,11 @@ void ckks_block::shard_context(const std::vector<blk::TileTag>& tiles) {
   const int nb = (SL + blk::kThreads - 1) / blk::kThreads;
   if (!st_prob) throw ckks::Error(CKKS_ESTATE, "softmax not evaluated");
   std::vector<std::vector<Ciphertext>> lhs(s.groups), rhs(s.groups);  // per query group
+  // the value lane shifts of all key groups in one batch
+  std::vector<int> kgs;
+  std::vector<Ciphertext> vx;
+  std::vector<std::vector<int>> vneed;
+  std::vector<int> vtarget;
   for (int kg = 0; kg < s.groups; ++kg) {
     const auto tags = tags_of(kg, tiles);
     if (tags.empty()) continue;
@@ -1274,8 +1317,18 @@ void ckks_block::shard_context(const std::vector<blk::TileTag>& tiles) {
     std::vector<int> need;
     for (const auto& tg : tags)
       if (std::find(need.begin(), need.end(), tg.d) == need.end()) need.push_back(tg.d);
+    kgs.push_back(kg);
+    vx.push_back(st_v[kg]);
+    vneed.push_back(need);
+    vtarget.push_back(st_v[kg]->limbs() - 1);
+  }
+  auto vshift = lane_shifts_batch(vx, vneed, vtarget);
+  vx.clear();
+  for (size_t ki = 0; ki < kgs.size(); ++ki) {
+    const int kg = kgs[ki];
+    const auto tags = tags_of(kg, tiles);
     const int lk = st_v[kg]->limbs() - 1;
-    auto vs = lane_shifts(st_v[kg], need, lk);
+    auto vs = std::move(vshift[ki]);
     count["cached_value_lane_shifts"] += (long)vs.size() - (vs.count(0) ? 1 : 0);
     const int M = (int)tags.size();
     double* dv = dbuf((size_t)M * SL);
