@@ -421,8 +421,9 @@ __global__ void __launch_bounds__(kThreads) ks_inner_batch_kernel(KsBatch b, con
                                                                   bool shared, uint64_t* __restrict__ acc_all,
                                                                   int limbs, int L, int K, int P, int beta, int logN,
                                                                   const Mod* __restrict__ mods) {
+  // two adjacent residues per thread (src(n + 1) = src(n) ^ 1)
   const int N = 1 << logN;
-  const int n = blockIdx.x * kThreads + threadIdx.x;
+  const int n = 2 * (blockIdx.x * kThreads + threadIdx.x);
   if (n >= N) return;
   const int t = blockIdx.y, m = blockIdx.z;
   const int E = limbs + K;
@@ -432,15 +433,22 @@ __global__ void __launch_bounds__(kThreads) ks_inner_batch_kernel(KsBatch b, con
   const uint64_t* ext = ext_all + (shared ? 0 : (size_t)m * beta * E * N);
   const uint64_t* key = b.key[m];
   const uint32_t src = (g == 1u) ? (uint32_t)n : auto_index((uint32_t)n, g, logN);
-  U128 s0{0, 0}, s1{0, 0};
+  const bool swap = src & 1u;
+  U128 a0{0, 0}, a1{0, 0}, b0{0, 0}, b1{0, 0};
   for (int j = 0; j < beta; ++j) {
-    const uint64_t v = ext[((size_t)j * E + t) * N + src];
-    mac_wide(s0, v, key[((size_t)j * 2 * P + pt) * N + n]);
-    mac_wide(s1, v, key[((size_t)j * 2 * P + P + pt) * N + n]);
+    const ulonglong2 v = *reinterpret_cast<const ulonglong2*>(ext + ((size_t)j * E + t) * N + (src & ~1u));
+    const uint64_t v0 = swap ? v.y : v.x, v1 = swap ? v.x : v.y;
+    const ulonglong2 k0 = *reinterpret_cast<const ulonglong2*>(key + ((size_t)j * 2 * P + pt) * N + n);
+    const ulonglong2 k1 = *reinterpret_cast<const ulonglong2*>(key + ((size_t)j * 2 * P + P + pt) * N + n);
+    mac_wide(a0, v0, k0.x);
+    mac_wide(a1, v1, k0.y);
+    mac_wide(b0, v0, k1.x);
+    mac_wide(b1, v1, k1.y);
   }
   uint64_t* acc = acc_all + (size_t)m * 2 * E * N;
-  acc[(size_t)t * N + n] = reduce128(s0, md);
-  acc[((size_t)E + t) * N + n] = reduce128(s1, md);
+  *reinterpret_cast<ulonglong2*>(acc + (size_t)t * N + n) = make_ulonglong2(reduce128(a0, md), reduce128(a1, md));
+  *reinterpret_cast<ulonglong2*>(acc + ((size_t)E + t) * N + n) =
+      make_ulonglong2(reduce128(b0, md), reduce128(b1, md));
 }
 
 // inner products of every item summed: acc = sum_m sum_j ext_{m,j}[pi_m(n)] key_{m,j};
@@ -450,31 +458,42 @@ __global__ void __launch_bounds__(kThreads) ks_inner_sum_kernel(KsBatch b, const
                                                                 uint64_t* __restrict__ acc, int limbs, int L, int K,
                                                                 int P, int beta, int logN, int fold,
                                                                 const Mod* __restrict__ mods) {
+  // two adjacent residues per thread (src(n + 1) = src(n) ^ 1): 16-byte
+  // loads and stores
   const int N = 1 << logN;
-  const int n = blockIdx.x * kThreads + threadIdx.x;
+  const int n = 2 * (blockIdx.x * kThreads + threadIdx.x);
   if (n >= N) return;
   const int t = blockIdx.y;
   const int E = limbs + K;
   const int pt = t < limbs ? t : L + (t - limbs);
   const Mod md = mods[pt];
-  U128 s0{0, 0}, s1{0, 0};
+  U128 a0{0, 0}, a1{0, 0}, b0{0, 0}, b1{0, 0};
   for (int m = 0; m < b.M; ++m) {
     const uint32_t g = b.g[m];
     const uint32_t src = (g == 1u) ? (uint32_t)n : auto_index((uint32_t)n, g, logN);
+    const bool swap = src & 1u;
     const uint64_t* ext = ext_all + (size_t)m * beta * E * N;
     const uint64_t* key = b.key[m];
     for (int j = 0; j < beta; ++j) {
-      const uint64_t v = ext[((size_t)j * E + t) * N + src];
-      mac_wide(s0, v, key[((size_t)j * 2 * P + pt) * N + n]);
-      mac_wide(s1, v, key[((size_t)j * 2 * P + P + pt) * N + n]);
+      const ulonglong2 v = *reinterpret_cast<const ulonglong2*>(ext + ((size_t)j * E + t) * N + (src & ~1u));
+      const uint64_t v0 = swap ? v.y : v.x, v1 = swap ? v.x : v.y;
+      const ulonglong2 k0 = *reinterpret_cast<const ulonglong2*>(key + ((size_t)j * 2 * P + pt) * N + n);
+      const ulonglong2 k1 = *reinterpret_cast<const ulonglong2*>(key + ((size_t)j * 2 * P + P + pt) * N + n);
+      mac_wide(a0, v0, k0.x);
+      mac_wide(a1, v1, k0.y);
+      mac_wide(b0, v0, k1.x);
+      mac_wide(b1, v1, k1.y);
     }
     if ((m + 1) % fold == 0) {
-      s0 = U128{reduce128(s0, md), 0};
-      s1 = U128{reduce128(s1, md), 0};
+      a0 = U128{reduce128(a0, md), 0};
+      a1 = U128{reduce128(a1, md), 0};
+      b0 = U128{reduce128(b0, md), 0};
+      b1 = U128{reduce128(b1, md), 0};
     }
   }
-  acc[(size_t)t * N + n] = reduce128(s0, md);
-  acc[((size_t)E + t) * N + n] = reduce128(s1, md);
+  *reinterpret_cast<ulonglong2*>(acc + (size_t)t * N + n) = make_ulonglong2(reduce128(a0, md), reduce128(a1, md));
+  *reinterpret_cast<ulonglong2*>(acc + ((size_t)E + t) * N + n) =
+      make_ulonglong2(reduce128(b0, md), reduce128(b1, md));
 }
 
 // (acc - conv) P^-1 plus every item's automorphism-permuted c0 (output 0)
@@ -686,9 +705,12 @@ __global__ void __launch_bounds__(kThreads) ks_inner_multi_kernel(KsBatch b, con
                                                                   uint64_t* __restrict__ acc_all, int limbs, int L,
                                                                   int K, int P, int beta, int logN,
                                                                   const Mod* __restrict__ mods) {
+  // two adjacent residues n, n + 1 per thread: the automorphism maps the
+  // aligned pair onto an aligned pair (src(n + 1) = src(n) ^ 1), so every
+  // load and store is 16 bytes
   const int N = 1 << logN;
   const int m = blockIdx.x;
-  const int n = blockIdx.y * kThreads + threadIdx.x;
+  const int n = 2 * (blockIdx.y * kThreads + threadIdx.x);
   if (n >= N) return;
   const int t = blockIdx.z;
   const int E = limbs + K;
@@ -698,15 +720,22 @@ __global__ void __launch_bounds__(kThreads) ks_inner_multi_kernel(KsBatch b, con
   const uint64_t* ext = ext_all + (size_t)b.src[m] * beta * E * N;
   const uint64_t* key = b.key[m];
   const uint32_t src = auto_index((uint32_t)n, g, logN);
-  U128 s0{0, 0}, s1{0, 0};
+  const bool swap = src & 1u;
+  U128 a0{0, 0}, a1{0, 0}, b0{0, 0}, b1{0, 0};
   for (int j = 0; j < beta; ++j) {
-    const uint64_t v = ext[((size_t)j * E + t) * N + src];
-    mac_wide(s0, v, key[((size_t)j * 2 * P + pt) * N + n]);
-    mac_wide(s1, v, key[((size_t)j * 2 * P + P + pt) * N + n]);
+    const ulonglong2 v = *reinterpret_cast<const ulonglong2*>(ext + ((size_t)j * E + t) * N + (src & ~1u));
+    const uint64_t v0 = swap ? v.y : v.x, v1 = swap ? v.x : v.y;
+    const ulonglong2 k0 = *reinterpret_cast<const ulonglong2*>(key + ((size_t)j * 2 * P + pt) * N + n);
+    const ulonglong2 k1 = *reinterpret_cast<const ulonglong2*>(key + ((size_t)j * 2 * P + P + pt) * N + n);
+    mac_wide(a0, v0, k0.x);
+    mac_wide(a1, v1, k0.y);
+    mac_wide(b0, v0, k1.x);
+    mac_wide(b1, v1, k1.y);
   }
   uint64_t* acc = acc_all + (size_t)m * 2 * E * N;
-  acc[(size_t)t * N + n] = reduce128(s0, md);
-  acc[((size_t)E + t) * N + n] = reduce128(s1, md);
+  *reinterpret_cast<ulonglong2*>(acc + (size_t)t * N + n) = make_ulonglong2(reduce128(a0, md), reduce128(a1, md));
+  *reinterpret_cast<ulonglong2*>(acc + ((size_t)E + t) * N + n) =
+      make_ulonglong2(reduce128(b0, md), reduce128(b1, md));
 }
 
 }  // namespace
@@ -753,7 +782,7 @@ void keyswitch_batch(const Context& c, int limbs, const KsBatch& b, bool shared,
   // key inner products
   {
     ProfScope ps(c, "ks_inner", M * (2.0 * lt.beta * E + 2.0 * E) * lb + Mu * (double)lt.beta * E * lb, st);
-    ks_inner_batch_kernel<<<dim3((N + kThreads - 1) / kThreads, E, M), kThreads, 0, st>>>(
+    ks_inner_batch_kernel<<<dim3((N / 2 + kThreads - 1) / kThreads, E, M), kThreads, 0, st>>>(
         b, ext, shared, acc, limbs, c.L, c.Kx(limbs), c.P, lt.beta, c.logN, c.d_mods);
   }
   CKKS_CUDA(cudaGetLastError());
@@ -851,7 +880,7 @@ void keyswitch_hoisted_multi(const Context& c, int limbs, const uint64_t* const*
     {
       // acc writes, each key once, the gathered ext residues
       ProfScope ps(c, "ks_inner", (M * (2.0 * E + (double)lt.beta * E) + (r1 - r0) * 2.0 * lt.beta * E) * lb, st);
-      ks_inner_multi_kernel<<<dim3(M, (N + kThreads - 1) / kThreads, E), kThreads, 0, st>>>(
+      ks_inner_multi_kernel<<<dim3(M, (N / 2 + kThreads - 1) / kThreads, E), kThreads, 0, st>>>(
           b, ext, acc, limbs, c.L, c.Kx(limbs), c.P, lt.beta, c.logN, c.d_mods);
     }
     CKKS_CUDA(cudaGetLastError());
@@ -925,7 +954,7 @@ void keyswitch_sum(const Context& c, int limbs, const KsBatch& b, uint64_t* out0
   {
     const int fold = 63 / lt.beta;
     ProfScope ps(c, "ks_inner_sum", (M * 3.0 * lt.beta * E + 2.0 * E) * lb, st);
-    ks_inner_sum_kernel<<<dim3((N + kThreads - 1) / kThreads, E), kThreads, 0, st>>>(
+    ks_inner_sum_kernel<<<dim3((N / 2 + kThreads - 1) / kThreads, E), kThreads, 0, st>>>(
         b, ext, acc, limbs, c.L, c.Kx(limbs), c.P, lt.beta, c.logN, fold, c.d_mods);
   }
   CKKS_CUDA(cudaGetLastError());
