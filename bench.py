@@ -209,6 +209,20 @@ def run_reference(args):
     print(json.dumps(line), flush=True)
 
 
+def ntt_launch_sizes(prof: dict, logn: int) -> dict:
+    """The NTT passes' launches and milliseconds by limbs per launch (the
+    profiler's size buckets are log2 of algorithmic bytes, 2^(logn+3) per limb)."""
+    out = {}
+    for name, v in prof.items():
+        if not name.startswith("ntt_"):
+            continue
+        for e, (n, ms) in v.get("by_size", {}).items():
+            cur = out.setdefault(max(int(e) - (logn + 3), 0), [0, 0.0])
+            cur[0] += n
+            cur[1] = round(cur[1] + ms, 3)
+    return {f"2^{k}": out[k] for k in sorted(out)}
+
+
 def run_engine(args):
     import torch
     import private_genomic_dnagpt_b200 as eng
@@ -391,6 +405,8 @@ def run_engine(args):
             "kernels": {k: {"launches": v["launches"], "ms": round(v["ms"], 3),
                             "GBps": round(v["bytes"] / v["ms"] / 1e6, 1) if v["ms"] > 0 else None}
                         for k, v in prof_all.items()},
+            # NTT passes by launch size: "2^k" = launches of 2^k to 2^(k+1) limbs: [launches, ms]
+            "ntt_launch_sizes": ntt_launch_sizes(prof_all, args.logn),
             # per block stage: device ms of its kernels, the largest first
             "stage_kernels_ms": {
                 sec: dict(sorted(((k, round(v["ms"], 2)) for k, v in ks.items()), key=lambda kv: -kv[1])[:8]) | {

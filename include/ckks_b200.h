@@ -237,7 +237,9 @@ int ckks_window_sum_batch_radix(ckks_ctx* ctx, const ckks_ct* const* in, int cou
  * fhe/gpu_real_scheme_b/src/real_dnagpt_fides_scheme_b_lintransform.cpp:627-629,
  * 797-824): when on, every kernel launch is bracketed by CUDA events on the
  * context stream.  The report is JSON text
- * {"<kernel>": {"launches": n, "ms": t, "bytes": algorithmic bytes}, ...};
+ * {"<kernel>": {"launches": n, "ms": t, "bytes": algorithmic bytes,
+ *               "by_size": {"<e>": [n_e, t_e], ...}}, ...}, where n_e and t_e
+ * count the launches of 2^e to 2^(e+1) algorithmic bytes;
  * returns the length written (truncated to `size`) or -1. */
 int ckks_profile_enable(ckks_ctx* ctx, int on);
 int ckks_profile_reset(ckks_ctx* ctx);

@@ -1459,9 +1459,16 @@ int ckks_profile_report(ckks_ctx* ctx, char* buf, size_t size) {
     bool first = true;
     char tmp[256];
     for (auto& kv : t) {
-      std::snprintf(tmp, sizeof tmp, "%s\"%s\": {\"launches\": %ld, \"ms\": %.6f, \"bytes\": %.1f}",
+      std::snprintf(tmp, sizeof tmp, "%s\"%s\": {\"launches\": %ld, \"ms\": %.6f, \"bytes\": %.1f, \"by_size\": {",
                     first ? "" : ", ", kv.first.c_str(), kv.second.launches, kv.second.ms, kv.second.bytes);
       js += tmp;
+      bool fh = true;
+      for (auto& h : kv.second.by_size) {
+        std::snprintf(tmp, sizeof tmp, "%s\"%d\": [%ld, %.6f]", fh ? "" : ", ", h.first, h.second.first, h.second.second);
+        js += tmp;
+        fh = false;
+      }
+      js += "}}";
       first = false;
     }
     js += "}";

@@ -109,6 +109,8 @@ class Profiler {
     long launches = 0;
     double ms = 0.0;
     double bytes = 0.0;
+    // launches and milliseconds by launch size: key e = floor(log2(bytes))
+    std::map<int, std::pair<long, double>> by_size;
   };
   // launches are also totalled per section (a caller-named phase, e.g. a
   // stage of a block evaluation)

@@ -466,6 +466,9 @@ std::map<std::string, Profiler::Totals> Profiler::report() {
       t->ms += ms;
       t->bytes += r.bytes;
     }
+    auto& h = totals_[r.name].by_size[r.bytes >= 1.0 ? std::ilogb(r.bytes) : 0];
+    h.first += 1;
+    h.second += ms;
     pool_.push_back(r.a);
     pool_.push_back(r.b);
   }
