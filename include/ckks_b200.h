@@ -199,6 +199,15 @@ int ckks_rotate_batch(ckks_ctx* ctx, const ckks_ct* const* in, const int* k, int
  * basis Q_l P and divided by P once (one ModDown per 32 rotations, in input
  * order, instead of one per rotation); identity rotations are added as is. */
 int ckks_rotate_sum(ckks_ctx* ctx, const ckks_ct* const* in, const int* k, int count, ckks_ct* out);
+/* outs[g] = sum_i EvalRotate(in[g * count + i], k[i]) for `groups` groups of
+ * inputs (all at one level and scale): ckks_rotate_sum of every group, the
+ * giant steps of one BSGS product for several token groups.  When k holds at
+ * most one identity and at most 32 other indices, up to 4 groups share one
+ * launch sequence: one ModUp per input, the key products of all groups in one
+ * launch (each rotation key read once for them), one batched ModDown.  Equal
+ * to ckks_rotate_sum per group, bit for bit. */
+int ckks_rotate_sum_groups(ckks_ctx* ctx, const ckks_ct* const* in, int groups, const int* k, int count,
+                           ckks_ct* const* outs);
 /* out = sum_i EvalMult(a[i], b[i]) with one relinearisation: the tensor
  * products are summed as degree-2 ciphertexts and d2 is key-switched once
  * (the context accumulation of T123.cpp:838-860, where every weight tile x

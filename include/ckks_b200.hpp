@@ -268,6 +268,21 @@ class CryptoContextImpl {
     check(ckks_rotate_sum(h_, in.data(), k.data(), (int)a.size(), out->handle()));
     return out;
   }
+  // EvalRotateSum(a[g], k) for every group g (all groups of k.size() inputs)
+  std::vector<Ciphertext> EvalRotateSumGroups(const std::vector<std::vector<Ciphertext>>& a,
+                                              const std::vector<int>& k) {
+    std::vector<Ciphertext> outs;
+    std::vector<const ckks_ct*> in;
+    std::vector<ckks_ct*> hs;
+    for (const auto& grp : a) {
+      if (grp.size() != k.size()) throw std::invalid_argument("EvalRotateSumGroups: group length differs from k");
+      for (const auto& x : grp) in.push_back(x->handle());
+      outs.push_back(fresh());
+      hs.push_back(outs.back()->handle());
+    }
+    check(ckks_rotate_sum_groups(h_, in.data(), (int)a.size(), k.data(), (int)k.size(), hs.data()));
+    return outs;
+  }
   std::vector<Ciphertext> EvalMultBatch(const std::vector<Ciphertext>& a, const std::vector<Ciphertext>& b) {
     std::vector<Ciphertext> outs;
     std::vector<const ckks_ct*> x, y;
@@ -360,6 +375,49 @@ class CryptoContextImpl {
       return d;
     }
     return r;
+  }
+  // LevelReduce(a[i], limbs[i]) for every input; the rescales of the scaled
+  // inputs at one limb count run as one batch
+  std::vector<Ciphertext> LevelReduceBatch(const std::vector<Ciphertext>& a, const std::vector<int>& limbs) {
+    if (a.size() != limbs.size()) throw std::invalid_argument("LevelReduceBatch: one limb count per input");
+    std::vector<Ciphertext> out(a.size()), scaled(a.size());
+    std::vector<uint64_t> q(limbs_);
+    check(ckks_ctx_moduli(h_, q.data(), limbs_));
+    std::vector<std::pair<int, std::vector<size_t>>> bins;  // limb count -> inputs, first-seen order
+    for (size_t i = 0; i < a.size(); ++i) {
+      Ciphertext x = deg1(a[i]);
+      if (x->limbs() == limbs[i]) {
+        out[i] = x;
+        continue;
+      }
+      const double target = ScaleAt(limbs_ - limbs[i]);
+      const double ql = (double)q[x->limbs() - 1];
+      const int64_t c = (int64_t)std::llround(target * ql / x->scale());
+      auto t = fresh();
+      check(ckks_mul_int(h_, x->handle(), c, t->handle()));
+      check(ckks_ct_set_scale(t->handle(), x->scale() * (double)c, 2));
+      scaled[i] = t;
+      size_t k = 0;
+      while (k < bins.size() && bins[k].first != t->limbs()) ++k;
+      if (k == bins.size()) bins.push_back({t->limbs(), {}});
+      bins[k].second.push_back(i);
+    }
+    for (const auto& bin : bins) {
+      std::vector<Ciphertext> xs;
+      for (size_t i : bin.second) xs.push_back(scaled[i]);
+      const auto r = RescaleBatch(xs);
+      for (size_t k = 0; k < bin.second.size(); ++k) {
+        const size_t i = bin.second[k];
+        if (r[k]->limbs() > limbs[i]) {
+          auto d = fresh();
+          check(ckks_drop_limbs(h_, r[k]->handle(), limbs[i], d->handle()));
+          out[i] = d;
+        } else {
+          out[i] = r[k];
+        }
+      }
+    }
+    return out;
   }
 
  private:

@@ -130,6 +130,7 @@ _SIGS = [
     ("ckks_window_sum_batch", ctypes.c_int, [_vp, _vp, ctypes.c_int, ctypes.c_int, ctypes.c_int, _vp]),
     ("ckks_window_sum_batch_radix", ctypes.c_int, [_vp, _vp, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int,
                                                    _vp]),
+    ("ckks_rotate_sum_groups", ctypes.c_int, [_vp, _vp, ctypes.c_int, _vp, ctypes.c_int, _vp]),
     ("ckks_profile_enable", ctypes.c_int, [_vp, ctypes.c_int]),
     ("ckks_profile_reset", ctypes.c_int, [_vp]),
     ("ckks_profile_report", ctypes.c_int, [_vp, ctypes.c_char_p, ctypes.c_size_t]),
@@ -608,6 +609,18 @@ class CryptoContext:
         n = len(cts)
         _check(lib().ckks_rotate_sum(self.h, (_vp * n)(*[c.h for c in cts]), (ctypes.c_int * n)(*ks), n, out.h))
         return out
+
+    def EvalRotateSumGroups(self, groups, ks) -> list[Ciphertext]:
+        """[EvalRotateSum(g, ks) for g in groups]: the groups' giant-step sums
+        share launches (each rotation key read once for all groups)."""
+        G, n = len(groups), len(ks)
+        flat = [c.h for g in groups for c in g]
+        if any(len(g) != n for g in groups):
+            raise ValueError("every group needs one input per rotation index")
+        outs = [self._new() for _ in range(G)]
+        _check(lib().ckks_rotate_sum_groups(self.h, (_vp * len(flat))(*flat), G, (ctypes.c_int * n)(*ks), n,
+                                            (_vp * G)(*[o.h for o in outs])))
+        return outs
 
     def mul_ct_batch(self, a, b) -> list[Ciphertext]:
         outs = [self._new() for _ in a]

@@ -667,6 +667,44 @@ struct ckks_block {
   // a at no more than `limbs` limbs: work whose result is next decrypted
   // runs at the fewest limbs that leave two at the decryption
   Ciphertext lower(const Ciphertext& a, int limbs) { return a->limbs() > limbs ? reduce_to(a, limbs) : a; }
+  // reduce_to / lower of several ciphertexts, the rescales batched
+  std::vector<Ciphertext> reduce_many(const std::vector<Ciphertext>& a, const std::vector<int>& limbs,
+                                      bool only_lower = false) {
+    std::vector<Ciphertext> out(a);
+    std::vector<Ciphertext> xs;
+    std::vector<int> ls;
+    std::vector<size_t> idx;
+    for (size_t i = 0; i < a.size(); ++i) {
+      if (a[i]->limbs() == limbs[i] || (only_lower && a[i]->limbs() < limbs[i])) continue;
+      ++count["level_reduce"];
+      xs.push_back(a[i]);
+      ls.push_back(limbs[i]);
+      idx.push_back(i);
+    }
+    if (!xs.empty()) {
+      const auto r = cc.LevelReduceBatch(xs, ls);
+      for (size_t k = 0; k < idx.size(); ++k) out[idx[k]] = r[k];
+    }
+    return out;
+  }
+  // rescales of several ciphertexts, one batch per limb count
+  std::vector<Ciphertext> rs_many(const std::vector<Ciphertext>& a) {
+    std::vector<Ciphertext> out(a.size());
+    std::vector<std::pair<int, std::vector<size_t>>> bins;
+    for (size_t i = 0; i < a.size(); ++i) {
+      size_t k = 0;
+      while (k < bins.size() && bins[k].first != a[i]->limbs()) ++k;
+      if (k == bins.size()) bins.push_back({a[i]->limbs(), {}});
+      bins[k].second.push_back(i);
+    }
+    for (const auto& bin : bins) {
+      std::vector<Ciphertext> xs;
+      for (size_t i : bin.second) xs.push_back(a[i]);
+      const auto r = cc.RescaleBatch(xs);
+      for (size_t k = 0; k < bin.second.size(); ++k) out[bin.second[k]] = r[k];
+    }
+    return out;
+  }
   Ciphertext rot(const Ciphertext& a, int k) {
     ++count["rotations"];
     return cc.EvalRotate(a, k);
@@ -737,19 +775,26 @@ struct ckks_block {
     for (int f = 0; f < s.D; ++f) invd[f] = 1.0 / s.D;
     std::vector<Ciphertext> centered, sqs;
     const auto sums = feature_sums(xs);
+    std::vector<Ciphertext> prods;
     for (size_t i = 0; i < xs.size(); ++i) {
-      const Ciphertext mean = mul_pt_rs(sums[i], feature_plain(1, invd, lx));
-      centered.push_back(cc.EvalSub(reduce_to(xs[i], lx - 1), mean));
+      ++count["ct_plain"];
+      prods.push_back(cc.EvalMult(sums[i], feature_plain(1, invd, lx)));
     }
+    const auto means = rs_many(prods);
+    const auto xr = reduce_many(xs, std::vector<int>(xs.size(), lx - 1));
+    for (size_t i = 0; i < xs.size(); ++i) centered.push_back(cc.EvalSub(xr[i], means[i]));
     // the variance is only decrypted: square at 4 limbs, sum and scale at 3,
     // decrypt at 2
-    std::vector<Ciphertext> low;
-    for (const auto& c : centered) low.push_back(lower(c, 4));
+    const auto low = reduce_many(centered, std::vector<int>(centered.size(), 4), true);
     count["ct_ct"] += (long)xs.size();
     sqs = cc.RescaleBatch(cc.EvalMultBatch(low, low));
+    prods.clear();
+    for (const auto& sq : feature_sums(sqs)) {
+      ++count["ct_plain"];
+      prods.push_back(cc.EvalMult(sq, feature_plain(1, invd, sq->limbs())));
+    }
     std::vector<Ciphertext> var;
-    for (const auto& sq : feature_sums(sqs))
-      var.push_back(cc.EvalAdd(mul_pt_rs(sq, feature_plain(1, invd, sq->limbs())), 1e-5));
+    for (const auto& v : rs_many(prods)) var.push_back(cc.EvalAdd(v, 1e-5));
     const int M = (int)xs.size();
     double* dv = dbuf((size_t)M * slots());
     client_decrypt(var, dv);
@@ -1039,11 +1084,11 @@ struct ckks_block {
         CKKS_CUDA(cudaGetLastError());
       }
       // giant steps: sum_g rot(inner_g, B n1 g), the key switches summed in the
-      // extended basis with one ModDown (g = 0 is the identity)
-      for (int q = 0; q < ng; ++q) {
-        count["rotations"] += s.n2 - 1;
-        outs[q0 + q] = rs(cc.EvalRotateSum(inner[q], gk));
-      }
+      // extended basis with one ModDown (g = 0 is the identity); the groups'
+      // sums share launches and each giant-step key is read once for them
+      count["rotations"] += (long)ng * (s.n2 - 1);
+      const auto sums = cc.RescaleBatch(cc.EvalRotateSumGroups(inner, gk));
+      for (int q = 0; q < ng; ++q) outs[q0 + q] = sums[q];
     }
     return outs;
   }
@@ -1346,11 +1391,18 @@ void ckks_block::shard_context(const std::vector<blk::TileTag>& tiles) {
       rhs[tags[i].qg].push_back(vs[tags[i].d]);
     }
   }
+  std::vector<Ciphertext> sums;
+  std::vector<int> qgs;
   for (int qg = 0; qg < s.groups; ++qg) {
     if (lhs[qg].empty()) continue;
     count["ct_ct"] += (long)lhs[qg].size();
-    const Ciphertext part = rs(cc.EvalMultSum(lhs[qg], rhs[qg]));
-    st_ctx[qg] = st_ctx[qg] ? add(st_ctx[qg], part) : part;
+    sums.push_back(cc.EvalMultSum(lhs[qg], rhs[qg]));
+    qgs.push_back(qg);
+  }
+  sums = rs_many(sums);
+  for (size_t i = 0; i < qgs.size(); ++i) {
+    const int qg = qgs[i];
+    st_ctx[qg] = st_ctx[qg] ? add(st_ctx[qg], sums[i]) : sums[i];
   }
   stamp("context");
 }
@@ -1379,8 +1431,14 @@ void ckks_block::shard_mlp(const std::vector<int>& groups, int c0, int c1) {
   auto ob = babies_of_batch(ctxs);
   const auto o = bsgs_groups(ob, 3);
   ob.clear();
-  std::vector<Ciphertext> r1;
-  for (int i = 0; i < G; ++i) r1.push_back(add(reduce_to(st_x[groups[i]], o[i]->limbs()), o[i]));
+  std::vector<Ciphertext> r1, xg;
+  std::vector<int> lg;
+  for (int i = 0; i < G; ++i) {
+    xg.push_back(st_x[groups[i]]);
+    lg.push_back(o[i]->limbs());
+  }
+  xg = reduce_many(xg, lg);
+  for (int i = 0; i < G; ++i) r1.push_back(add(xg[i], o[i]));
   for (int i = 0; i < G; ++i) st_r1[groups[i]] = r1[i];
   if (c0 >= c1) {
     for (int g : groups) st_mlp[g] = Ciphertext();
@@ -1435,12 +1493,16 @@ void ckks_block::shard_finish(const std::vector<int>& groups, double* y) {
   const int T = s.T, D = s.D, B = s.B, SL = slots();
   const int nb = (SL + blk::kThreads - 1) / blk::kThreads;
   const int G = (int)groups.size();
-  std::vector<Ciphertext> out(G);
+  std::vector<Ciphertext> out(G), rg;
+  std::vector<int> lg;
   for (int i = 0; i < G; ++i) {
     const int g = groups[i];
     if (!st_r1[g] || !st_mlp[g]) throw ckks::Error(CKKS_ESTATE, "MLP of the group not complete");
-    out[i] = add(reduce_to(st_r1[g], st_mlp[g]->limbs()), st_mlp[g]);
+    rg.push_back(st_r1[g]);
+    lg.push_back(st_mlp[g]->limbs());
   }
+  rg = reduce_many(rg, lg);
+  for (int i = 0; i < G; ++i) out[i] = add(rg[i], st_mlp[groups[i]]);
   CKKS_CUDA(cudaEventRecord(ev_out, C.stream));
   // client: decrypt and unpack (T123.cpp:1675-1694)
   {

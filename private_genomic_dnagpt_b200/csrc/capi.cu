@@ -372,6 +372,63 @@ void rotate_sum(Context& c, const ckks_ct* const* in, const int* ks, int n, DevP
   res.deg = in[0]->p.deg;
 }
 
+// outs[g] = sum_r rot(in[g * n + r], ks[r]) for G groups: when the groups'
+// rotations hold at most one identity and 32 others, the groups' giant-step
+// sums run together, up to 4 groups per launch sequence
+// (keyswitch_sum_groups); otherwise one rotate_sum per group
+void rotate_sum_groups(Context& c, const ckks_ct* const* in, int G, const int* ks, int n, DevPoly* outs) {
+  const int limbs = in[0]->p.limbs;
+  int ident = -1, others = 0;
+  bool shared = true;
+  std::vector<uint32_t> gs(n);
+  for (int r = 0; r < n; ++r) {
+    gs[r] = c.galois(ks[r]);
+    if (gs[r] == 1u) {
+      if (ident >= 0) shared = false;
+      ident = r;
+    } else {
+      ++others;
+      if (!c.switch_key(gs[r], limbs))
+        throw Error(CKKS_EKEY, "rotation key not generated for index " + std::to_string(ks[r]));
+    }
+  }
+  if (others == 0 || others > ckks::kKsBatch) shared = false;
+  if (!shared) {
+    for (int gi = 0; gi < G; ++gi) rotate_sum(c, in + (size_t)gi * n, ks, n, outs[gi]);
+    return;
+  }
+  for (int g0 = 0; g0 < G; g0 += ckks::kSumGroups) {
+    const int k = std::min(ckks::kSumGroups, G - g0);
+    std::vector<ckks::KsBatch> bs(k);
+    ckks::SumGroups sg{};
+    for (int i = 0; i < k; ++i) {
+      const ckks_ct* const* gin = in + (size_t)(g0 + i) * n;
+      ckks::KsBatch& b = bs[i];
+      b = ckks::KsBatch{};
+      for (int r = 0; r < n; ++r) {
+        if (r == ident) continue;
+        const int m = b.M++;
+        b.d[m] = gin[r]->p.poly(1);
+        b.key[m] = c.switch_key(gs[r], limbs);
+        b.g[m] = gs[r];
+        b.add0[m] = gin[r]->p.poly(0);
+      }
+      DevPoly& o = outs[g0 + i];
+      o.ensure(&c, 2, limbs);
+      o.limbs = limbs;
+      o.scale = gin[0]->p.scale;
+      o.deg = gin[0]->p.deg;
+      sg.out0[i] = o.poly(0);
+      sg.out1[i] = o.poly(1);
+      if (ident >= 0) {
+        sg.id0[i] = gin[ident]->p.poly(0);
+        sg.id1[i] = gin[ident]->p.poly(1);
+      }
+    }
+    ckks::keyswitch_sum_groups(c, limbs, bs.data(), sg, k, c.stream);
+  }
+}
+
 // tensor + relinearisation of (a[i], b[i]) pairs at one limb count
 void mul_ct_batch(Context& c, const ckks_ct* const* a, const ckks_ct* const* bb, int n, ckks_ct* const* outs) {
   if (n <= 0) return;
@@ -1220,6 +1277,24 @@ int ckks_mul_ct_sum(ckks_ctx* ctx, const ckks_ct* const* a, const ckks_ct* const
     DevPoly tmp;
     mul_ct_sum(c, a, b, count, tmp);
     take(out->p, tmp);
+  });
+}
+
+int ckks_rotate_sum_groups(ckks_ctx* ctx, const ckks_ct* const* in, int groups, const int* k, int count,
+                           ckks_ct* const* outs) {
+  return guard([&] {
+    Context& c = C(ctx);
+    need(groups >= 1 && count >= 1 && in && k && outs, CKKS_EARG, "empty rotation sum");
+    for (int i = 0; i < groups * count; ++i) {
+      same_ctx(ctx, in[i]);
+      need(in[i]->p.limbs == in[0]->p.limbs, CKKS_ELEVEL, "operands at different levels");
+      need(in[i]->p.deg == in[0]->p.deg, CKKS_ESCALE, "operands with different noise degree");
+      check_scales(in[0]->p.scale, in[i]->p.scale);
+    }
+    for (int g = 0; g < groups; ++g) need(outs[g] && outs[g]->owner == ctx, CKKS_EARG, "bad output handle");
+    std::vector<DevPoly> tmp(groups);
+    rotate_sum_groups(c, in, groups, k, count, tmp.data());
+    for (int g = 0; g < groups; ++g) take(outs[g]->p, tmp[g]);
   });
 }
 

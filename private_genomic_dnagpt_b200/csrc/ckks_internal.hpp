@@ -407,6 +407,24 @@ void keyswitch_hoisted_multi(const Context& c, int limbs, const uint64_t* const*
 // acc1) + sum_m add1[m] (null addends skipped).  The giant steps of a BSGS
 // product: sum_g rot(inner_g, k_g).
 void keyswitch_sum(const Context& c, int limbs, const KsBatch& b, uint64_t* out0, uint64_t* out1, cudaStream_t st);
+// keyswitch_sum of G <= 4 groups that rotate by the same keys (bs[g].key and
+// .g equal across groups; bs[g].d/add0 the group's inputs): one ModUp per
+// input, the key inner products of all groups in one launch (a key residue is
+// loaded once for the groups), one batched ModDown.  out0_g = ModDown(sum
+// acc0) + sum_m auto_{g_m}(add0[g][m]) + id0_g, out1_g = ModDown(sum acc1) +
+// id1_g, the identity terms id0/id1 optional (null).  The caller fills s.id0,
+// s.id1, s.out0, s.out1; add0, g and M are taken from bs.
+constexpr int kSumGroups = 4;
+struct SumGroups {
+  const uint64_t* add0[kSumGroups][kKsBatch];
+  const uint64_t* id0[kSumGroups];
+  const uint64_t* id1[kSumGroups];
+  uint64_t* out0[kSumGroups];
+  uint64_t* out1[kSumGroups];
+  uint32_t g[kKsBatch];
+  int M;
+};
+void keyswitch_sum_groups(const Context& c, int limbs, const KsBatch* bs, SumGroups& s, int G, cudaStream_t st);
 // For each of the M items (d = c1, add0 = c0, out0/out1): the sum of its R
 // rotations by h (plus the item itself when `identity`), with one ModUp per
 // item, the R key inner products added in the extended basis Q_l P and one

@@ -528,6 +528,38 @@ __global__ void __launch_bounds__(kThreads) moddown_combine_sum_kernel(KsBatch b
   (p == 0 ? out0 : out1)[(size_t)t * N + n] = r;
 }
 
+// giant-step sums of several groups: out0_g = ModDown(acc0_g) + sum_m
+// pi_m(add0[g][m]) (+ id0_g), out1_g = ModDown(acc1_g) (+ id1_g)
+__global__ void __launch_bounds__(kThreads) moddown_combine_groups_kernel(SumGroups s,
+                                                                         const uint64_t* __restrict__ acc_all,
+                                                                         const uint64_t* __restrict__ conv_all,
+                                                                         int limbs, int K, int logN,
+                                                                         const Mod* __restrict__ mods,
+                                                                         const ulonglong2* __restrict__ pinv) {
+  const int N = 1 << logN;
+  const int n = blockIdx.x * kThreads + threadIdx.x;
+  if (n >= N) return;
+  const int t = blockIdx.y % limbs, p = blockIdx.y / limbs, gi = blockIdx.z;
+  const int E = limbs + K;
+  const uint64_t q = mods[t].q;
+  const ulonglong2 pv = pinv[t];
+  const uint64_t a = acc_all[((size_t)(2 * gi + p) * E + t) * N + n];
+  const uint64_t cv = conv_all[((size_t)(2 * gi + p) * limbs + t) * N + n];
+  uint64_t r = mul_shoup(sub_mod(a, cv, q), pv.x, pv.y, q);
+  if (p == 0) {
+    for (int m = 0; m < s.M; ++m) {
+      const uint32_t g = s.g[m];
+      const uint32_t src = (g == 1u) ? (uint32_t)n : auto_index((uint32_t)n, g, logN);
+      r = add_mod(r, s.add0[gi][m][(size_t)t * N + src], q);
+    }
+    if (s.id0[gi]) r = add_mod(r, s.id0[gi][(size_t)t * N + n], q);
+    s.out0[gi][(size_t)t * N + n] = r;
+  } else {
+    if (s.id1[gi]) r = add_mod(r, s.id1[gi][(size_t)t * N + n], q);
+    s.out1[gi][(size_t)t * N + n] = r;
+  }
+}
+
 template <int MAXK>
 __global__ void __launch_bounds__(kThreads) moddown_conv_batch_kernel(const uint64_t* __restrict__ acc_all,
                                                                       uint64_t* __restrict__ conv_all, int limbs,
@@ -618,10 +650,15 @@ __global__ void __launch_bounds__(kThreads) rs_combine_batch_kernel(RsBatch b, c
 // once for them; 128-bit accumulators folded every `fold` products as in
 // ks_inner_sum_kernel.
 constexpr int kHoistItems = 4;
+// Item i of rotation r reads its extended digits at ext_all + i * istride +
+// r * rstride: rstride = 0 for the rotations of one ModUp (hoisted sums),
+// one digit set for the giant steps of several groups (one ModUp per
+// rotated input).
 __global__ void __launch_bounds__(kThreads) ks_inner_hoist_kernel(HoistKeys h, const uint64_t* __restrict__ ext_all,
                                                                   uint64_t* __restrict__ acc_all, int M, int limbs,
                                                                   int L, int K, int P, int beta, int logN, int fold,
-                                                                  const Mod* __restrict__ mods) {
+                                                                  const Mod* __restrict__ mods, size_t istride,
+                                                                  size_t rstride) {
   const int N = 1 << logN;
   const int n = blockIdx.x * kThreads + threadIdx.x;
   if (n >= N) return;
@@ -630,8 +667,7 @@ __global__ void __launch_bounds__(kThreads) ks_inner_hoist_kernel(HoistKeys h, c
   const int pt = t < limbs ? t : L + (t - limbs);
   const Mod md = mods[pt];
   const int cnt = min(kHoistItems, M - m0);
-  const size_t item = (size_t)beta * E * N;
-  const uint64_t* ext = ext_all + (size_t)m0 * item + (size_t)t * N;
+  const uint64_t* ext = ext_all + (size_t)m0 * istride + (size_t)t * N;
   U128 s0[kHoistItems], s1[kHoistItems];
 #pragma unroll
   for (int i = 0; i < kHoistItems; ++i) s0[i] = s1[i] = U128{0, 0};
@@ -641,11 +677,11 @@ __global__ void __launch_bounds__(kThreads) ks_inner_hoist_kernel(HoistKeys h, c
     for (int j = 0; j < beta; ++j) {
       const uint64_t k0 = key[((size_t)j * 2 * P + pt) * N + n];
       const uint64_t k1 = key[((size_t)j * 2 * P + P + pt) * N + n];
-      const uint64_t* ej = ext + (size_t)j * E * N + src;
+      const uint64_t* ej = ext + (size_t)r * rstride + (size_t)j * E * N + src;
 #pragma unroll
       for (int i = 0; i < kHoistItems; ++i) {
         if (i < cnt) {
-          const uint64_t v = ej[(size_t)i * item];
+          const uint64_t v = ej[(size_t)i * istride];
           mac_wide(s0[i], v, k0);
           mac_wide(s1[i], v, k1);
         }
@@ -988,6 +1024,105 @@ void keyswitch_sum(const Context& c, int limbs, const KsBatch& b, uint64_t* out0
   c.release(conv);
 }
 
+void keyswitch_sum_groups(const Context& c, int limbs, const KsBatch* bs, SumGroups& s, int G, cudaStream_t st) {
+  if (c.alpha > kMaxAlpha || c.Kx(limbs) > kMaxK) throw Error(kErrArgument, "digit size above 16 is not supported");
+  if (G <= 0) return;
+  if (G > kSumGroups) throw Error(kErrArgument, "key-switch sums of 1..4 groups");
+  const int M = bs[0].M;
+  if (M <= 0 || M > kKsBatch) throw Error(kErrArgument, "key-switch sum of 1..32 items");
+  for (int gi = 1; gi < G; ++gi) {
+    if (bs[gi].M != M) throw Error(kErrArgument, "groups of a key-switch sum differ in length");
+    for (int m = 0; m < M; ++m)
+      if (bs[gi].g[m] != bs[0].g[m] || bs[gi].key[m] != bs[0].key[m])
+        throw Error(kErrArgument, "groups of a key-switch sum differ in their rotations");
+  }
+  const int N = c.N, E = limbs + c.Kx(limbs);
+  const LevelTables& lt = c.lt(limbs);
+  const double lb = c.limb_bytes();
+  const size_t item = (size_t)lt.beta * E * N;
+  uint64_t* dc = (uint64_t*)c.alloc(sizeof(uint64_t) * (size_t)M * limbs * N);
+  uint64_t* ext = (uint64_t*)c.alloc(sizeof(uint64_t) * (size_t)G * M * item);
+  uint64_t* acc = (uint64_t*)c.alloc(sizeof(uint64_t) * (size_t)G * 2 * E * N);
+  uint64_t* conv = (uint64_t*)c.alloc(sizeof(uint64_t) * (size_t)G * 2 * limbs * N);
+  // ModUp of every item of every group (one launch sequence per group)
+  const int min_cnt = limbs - (lt.beta - 1) * c.alpha;
+  const int nch_up = (E - min_cnt + kTargets - 1) / kTargets;
+  for (int gi = 0; gi < G; ++gi) {
+    const KsBatch& b = bs[gi];
+    uint64_t* eg = ext + (size_t)gi * M * item;
+    {
+      NttSource src{};
+      src.per_item = limbs;
+      src.limb_stride = N;
+      for (int m = 0; m < M; ++m) src.item[m] = b.d[m];
+      ntt_inverse(c, dc, M * limbs, LimbMap::q(limbs, c.L), st, lt.d_up_scale_a, lt.d_up_scale_b, 0, &src);
+    }
+    {
+      ProfScope ps(c, "modup_conv", M * (2.0 * limbs + (double)lt.beta * E) * lb, st);
+      auto kern = c.alpha <= 4 ? modup_conv_batch_kernel<4>
+                  : c.alpha <= 8 ? modup_conv_batch_kernel<8>
+                  : c.alpha <= 12 ? modup_conv_batch_kernel<12>
+                                  : modup_conv_batch_kernel<16>;
+      kern<<<dim3((N / 2 + kThreads - 1) / kThreads, lt.beta * nch_up, M), kThreads, 0, st>>>(
+          b, dc, eg, limbs, c.L, c.Kx(limbs), c.alpha, lt.beta, c.logN, nch_up, c.d_mods, lt.d_up_hat);
+    }
+    CKKS_CUDA(cudaGetLastError());
+    LimbMap m = LimbMap::ext(limbs, c.Kx(limbs), c.L);
+    m.skip_alpha = c.alpha;
+    m.skip_beta = lt.beta;
+    ntt_forward(c, eg, M * lt.beta * E, m, st);
+  }
+  // summed key inner products, each key residue loaded once for all groups
+  {
+    HoistKeys h{};
+    h.R = M;
+    for (int m = 0; m < M; ++m) {
+      h.key[m] = bs[0].key[m];
+      h.g[m] = bs[0].g[m];
+    }
+    const int fold = 63 / lt.beta;
+    ProfScope ps(c, "ks_inner_sum", ((double)G * M * lt.beta * E + 2.0 * M * lt.beta * E + 2.0 * G * E) * lb, st);
+    ks_inner_hoist_kernel<<<dim3((N + kThreads - 1) / kThreads, E, (G + kHoistItems - 1) / kHoistItems), kThreads, 0,
+                            st>>>(h, ext, acc, G, limbs, c.L, c.Kx(limbs), c.P, lt.beta, c.logN, fold, c.d_mods,
+                                  (size_t)M * item, item);
+  }
+  CKKS_CUDA(cudaGetLastError());
+  // one ModDown per group
+  {
+    LimbMap pm = LimbMap::ext(limbs, c.Kx(limbs), c.L);
+    pm.skip_q = 1;
+    ntt_inverse(c, acc, G * 2 * E, pm, st, c.down_scale_a(limbs), c.down_scale_b(limbs), c.L);
+  }
+  const int nch_dn = (limbs + kTargets - 1) / kTargets;
+  {
+    ProfScope ps(c, "moddown_conv", G * (2.0 * c.Kx(limbs) + 2.0 * limbs) * lb, st);
+    auto kern = c.Kx(limbs) <= 4 ? moddown_conv_batch_kernel<4>
+                : c.Kx(limbs) <= 8 ? moddown_conv_batch_kernel<8>
+                : c.Kx(limbs) <= 12 ? moddown_conv_batch_kernel<12>
+                            : moddown_conv_batch_kernel<16>;
+    kern<<<dim3((N / 2 + kThreads - 1) / kThreads, 2 * nch_dn, G), kThreads, 0, st>>>(
+        acc, conv, limbs, c.L, c.Kx(limbs), c.logN, nch_dn, c.d_mods, lt.d_down_phat);
+  }
+  CKKS_CUDA(cudaGetLastError());
+  ntt_forward(c, conv, G * 2 * limbs, LimbMap::q(limbs, c.L), st);
+  {
+    s.M = M;
+    for (int m = 0; m < M; ++m) s.g[m] = bs[0].g[m];
+    for (int gi = 0; gi < G; ++gi)
+      for (int m = 0; m < M; ++m) s.add0[gi][m] = bs[gi].add0[m];
+    double extra = 0.0;
+    for (int gi = 0; gi < G; ++gi) extra += (s.id0[gi] ? 1.0 : 0.0) + (s.id1[gi] ? 1.0 : 0.0);
+    ProfScope ps(c, "moddown_combine_sum", (G * (6.0 + M) + extra) * limbs * lb, st);
+    moddown_combine_groups_kernel<<<dim3((N + kThreads - 1) / kThreads, 2 * limbs, G), kThreads, 0, st>>>(
+        s, acc, conv, limbs, c.Kx(limbs), c.logN, c.d_mods, lt.d_down_pinv);
+  }
+  CKKS_CUDA(cudaGetLastError());
+  c.release(dc);
+  c.release(ext);
+  c.release(acc);
+  c.release(conv);
+}
+
 void keyswitch_hoisted_sum(const Context& c, int limbs, const KsBatch& b, const HoistKeys& h, bool identity,
                            cudaStream_t st) {
   if (c.alpha > kMaxAlpha || c.Kx(limbs) > kMaxK) throw Error(kErrArgument, "digit size above 16 is not supported");
@@ -1034,7 +1169,8 @@ void keyswitch_hoisted_sum(const Context& c, int limbs, const KsBatch& b, const 
     ProfScope ps(c, "ks_inner_hoist", (M * (lt.beta * (1.0 + 2.0 * h.R) + 2.0) * E + 2.0 * h.R * lt.beta * E) * lb,
                  st);
     ks_inner_hoist_kernel<<<dim3((N + kThreads - 1) / kThreads, E, (M + kHoistItems - 1) / kHoistItems), kThreads,
-                            0, st>>>(h, ext, acc, M, limbs, c.L, c.Kx(limbs), c.P, lt.beta, c.logN, fold, c.d_mods);
+                            0, st>>>(h, ext, acc, M, limbs, c.L, c.Kx(limbs), c.P, lt.beta, c.logN, fold, c.d_mods,
+                                     (size_t)lt.beta * E * N, 0);
   }
   CKKS_CUDA(cudaGetLastError());
   // one ModDown per item

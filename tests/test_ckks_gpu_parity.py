@@ -216,6 +216,24 @@ def test_rotate_sum_bit_exact(pair10, ks):
     assert np.abs(dec - sum(np.roll(f[0], -k) for f, k in zip(fr, ks))).max() < 1e-7
 
 
+@pytest.mark.parametrize("groups,ks,limbs", [
+    (3, [0, 8, 16, 24], 5),             # identity + 3 giant steps, one launch sequence
+    (5, [4, 8, -1], 4),                 # no identity; 4 + 1 groups
+    (2, [0, 1, 0, 2], 3),               # two identities: one rotation sum per group
+    (2, [0] + [1, 2, 3, 5, 8, 64, 100, -1, -7] * 4, 2),  # 36 others: per group
+])
+def test_rotate_sum_groups_bit_exact(pair10, groups, ks, limbs):
+    """Giant-step sums of several groups sharing launches equal the oracle's
+    rotation sum of each group."""
+    o, cc = pair10
+    fr = [[_fresh(o, cc, 500 + 40 * g + i, limbs) for i in range(len(ks))] for g in range(groups)]
+    got = cc.EvalRotateSumGroups([[f[2] for f in grp] for grp in fr], ks)
+    assert len(got) == groups
+    for grp, out in zip(fr, got):
+        assert out.limbs == limbs
+        assert np.array_equal(out.limbs_array(), o.rotate_sum(np.stack([f[1] for f in grp]), ks))
+
+
 @pytest.mark.parametrize("n,limbs", [(3, 6), (3, 2), (40, 4)])
 def test_mul_ct_sum_bit_exact(pair10, n, limbs):
     """Products summed as degree-2 ciphertexts, one relinearisation (40
