@@ -8,9 +8,12 @@
 //             (stages s1..logN-1);
 //   inverse:  pass B' (stages logN-1..s1) then pass A' (stages s1-1..0), with
 //             N^-1 folded into the last stage's twiddles.
-// Inside a pass each thread keeps 8 residues in registers and applies up to
-// three radix-2 stages to them before exchanging through shared memory, so a
-// 256-point sub-transform costs 2 shared-memory exchanges for 8 stages.
+// Inside a pass each thread keeps 8 or 16 residues in registers and applies
+// up to three or four radix-2 stages to them before exchanging through shared
+// memory: a 256-point sub-transform costs two exchanges in the contiguous
+// pass (8 residues, 1024 resident threads per SM) and one in the strided pass
+// (16 residues, 768 resident threads, whose column loads gain most from more
+// loads in flight per thread).
 // Twiddles are psi^bitrev in the Longa-Naehrig order, stored with their
 // Shoup companions as (w, w') pairs; output order is bit-reversed (forward)
 // and natural (inverse), identical to the CPU restatement.
@@ -22,8 +25,12 @@ namespace ckks {
 
 namespace {
 
-// threads per CTA in both passes
-constexpr int kThreads = 512;
+// threads per CTA and resident CTAs per SM, by residues per thread (2^R_LOG)
+template <int R_LOG>
+struct PassShape {
+  static constexpr int kThreads = R_LOG >= 4 ? 256 : 512;
+  static constexpr int kMinBlocks = R_LOG >= 4 ? 3 : 2;
+};
 
 struct PassArgs {
   const ulonglong2* tw;  // [P][N] (w, w'), forward or inverse table
@@ -50,17 +57,23 @@ __device__ __forceinline__ const uint64_t* pass_input(const PassArgs& a, uint64_
 }
 
 // Shared-memory slot of residue r in a contiguous block: the low four bits
-// are XORed with a function of bits 4-6, so that each half-warp's 64-bit
-// accesses of all three register-group layouts of a 256-point block fall in
-// 16 distinct bank pairs (a bijection on every aligned 16 residues).
+// are XORed with a function of the next bits, so that each half-warp's
+// 64-bit accesses of every register-group layout of a 256-point block fall in
+// 16 distinct bank pairs (a bijection on every aligned 16 residues).  With 8
+// residues per thread the function of bits 4-6 covers the three layouts;
+// with 16 residues per thread the two layouts (r = u + 16 k and r = 16 u + k
+// for thread u) are covered by XORing bits 4-7 themselves.
+template <int R_LOG>
 __device__ __forceinline__ int swizzle(int r) {
   const int h = r >> 4;
+  if (R_LOG >= 4) return h & 15;
   return (h & 1) ^ (((h >> 1) & 1) * 6) ^ (((h >> 2) & 1) * 8);
 }
 
+template <int R_LOG>
 __device__ __forceinline__ int group_size(int s_log, int gi) {
-  const int rem = s_log - 3 * gi;
-  return rem < 3 ? rem : 3;
+  const int rem = s_log - R_LOG * gi;
+  return rem < R_LOG ? rem : R_LOG;
 }
 
 // Harvey butterflies.  Forward (Cooley-Tukey): values in [0, 4q);
@@ -81,11 +94,12 @@ __device__ __forceinline__ void gs_bfly(uint64_t& x, uint64_t& y, ulonglong2 w, 
   y = mul_shoup_lazy(d, w.x, w.y, q);
 }
 
-template <int S_LOG, bool INV, bool STRIDED>
+template <int S_LOG, bool INV, bool STRIDED, int R_LOG>
 __device__ __forceinline__ void ntt_pass_body(uint64_t* __restrict__ data, const PassArgs& a, uint64_t* sm) {
   constexpr int S = 1 << S_LOG;
-  constexpr int T = S >= 8 ? S / 8 : 1;  // threads per sub-transform
-  constexpr int NG = (S_LOG + 2) / 3;     // register stage groups
+  constexpr int R = 1 << R_LOG;                // residues per thread
+  constexpr int T = S >= R ? S / R : 1;        // threads per sub-transform
+  constexpr int NG = (S_LOG + R_LOG - 1) / R_LOG;  // register stage groups
 
   const int limb = blockIdx.y;
   const int prime = a.map.prime(limb);
@@ -119,22 +133,22 @@ __device__ __forceinline__ void ntt_pass_body(uint64_t* __restrict__ data, const
     return STRIDED ? (size_t)r * stride + sub_global : (size_t)sub_global * S + r;
   };
   auto saddr = [&](int r) -> int {
-    return STRIDED ? r * per + lane_idx : lane_idx * S + (r ^ swizzle(r));
+    return STRIDED ? r * per + lane_idx : lane_idx * S + (r ^ swizzle<R_LOG>(r));
   };
 
-  uint64_t x[8];
+  uint64_t x[R];
 
 #pragma unroll
   for (int step = 0; step < NG; ++step) {
     const int gi = INV ? (NG - 1 - step) : step;
-    const int G = group_size(S_LOG, gi);
-    const int st0 = 3 * gi;
+    const int G = group_size<R_LOG>(S_LOG, gi);
+    const int st0 = R_LOG * gi;
     const int D = S >> (st0 + G);  // smallest distance inside a unit
-    const int units_per_thread = 8 >> G;
+    const int units_per_thread = R >> G;
     const int usz = 1 << G;
     // load
 #pragma unroll
-    for (int j = 0; j < 8; ++j) {
+    for (int j = 0; j < R; ++j) {
       if (j >= units_per_thread * usz) break;
       const int uj = j / usz, k = j % usz;
       const int u = sub_t + uj * T;
@@ -149,41 +163,43 @@ __device__ __forceinline__ void ntt_pass_body(uint64_t* __restrict__ data, const
     // butterflies; the twiddle of pair (k, k+h) at stage st0+rr is
     // tw[2^(gs0+st) + prefix*2^st + B*2^rr + (k >> (G-rr))], B = u / D
 #pragma unroll
-    for (int uj = 0; uj < 8; ++uj) {
+    for (int uj = 0; uj < R; ++uj) {
       if (uj >= units_per_thread) break;
       const int u = sub_t + uj * T;
       const uint32_t B = (uint32_t)(u / D);
       uint64_t* xu = x + uj * usz;
 #pragma unroll
-      for (int it = 0; it < 3; ++it) {
+      for (int it = 0; it < R_LOG; ++it) {
         if (it >= G) break;
         const int rr = INV ? (G - 1 - it) : it;
         const int st = st0 + rr;
         const int h = 1 << (G - 1 - rr);
         const bool final_stage = INV && STRIDED && st == 0;
         const uint32_t idx0 = (1u << (gs0 + st)) + (prefix << st) + (B << rr);
-        ulonglong2 w[4];
-        if (!final_stage) {
+        // pairs (k, k + h) with k >> (G - rr) == jw share twiddle jw
 #pragma unroll
-          for (int j = 0; j < 4; ++j)
-            if (j < (1 << rr)) w[j] = __ldg(tw + idx0 + j);
-        }
+        for (int jw = 0; jw < R / 2; ++jw) {
+          if (jw >= (1 << rr)) break;
+          ulonglong2 w{0, 0};
+          if (!final_stage) w = __ldg(tw + idx0 + jw);
 #pragma unroll
-        for (int k = 0; k < 8; ++k) {
-          if (k >= usz) break;
-          if (k & h) continue;
-          if (!INV) {
-            ct_bfly(xu[k], xu[k + h], w[k >> (G - rr)], q, q2);
-          } else if (!final_stage) {
-            gs_bfly(xu[k], xu[k + h], w[k >> (G - rr)], q, q2);
-          } else {
-            const ulonglong2 c0 = a.scale_a ? __ldg(a.scale_a + (prime - a.scale_base)) : __ldg(a.ninv_last + prime);
-            const ulonglong2 c1 = a.scale_b ? __ldg(a.scale_b + (prime - a.scale_base)) : __ldg(a.w1_ninv + prime);
-            const uint64_t u0 = xu[k], v0 = xu[k + h];
-            const uint64_t s0 = mul_shoup_lazy(u0 + v0, c0.x, c0.y, q);
-            const uint64_t d0 = mul_shoup_lazy(u0 + q2 - v0, c1.x, c1.y, q);
-            xu[k] = s0 >= q ? s0 - q : s0;
-            xu[k + h] = d0 >= q ? d0 - q : d0;
+          for (int kk = 0; kk < R; ++kk) {
+            if (kk >= (1 << (G - rr))) break;
+            const int k = (jw << (G - rr)) + kk;
+            if (k & h) continue;
+            if (!INV) {
+              ct_bfly(xu[k], xu[k + h], w, q, q2);
+            } else if (!final_stage) {
+              gs_bfly(xu[k], xu[k + h], w, q, q2);
+            } else {
+              const ulonglong2 c0 = a.scale_a ? __ldg(a.scale_a + (prime - a.scale_base)) : __ldg(a.ninv_last + prime);
+              const ulonglong2 c1 = a.scale_b ? __ldg(a.scale_b + (prime - a.scale_base)) : __ldg(a.w1_ninv + prime);
+              const uint64_t u0 = xu[k], v0 = xu[k + h];
+              const uint64_t s0 = mul_shoup_lazy(u0 + v0, c0.x, c0.y, q);
+              const uint64_t d0 = mul_shoup_lazy(u0 + q2 - v0, c1.x, c1.y, q);
+              xu[k] = s0 >= q ? s0 - q : s0;
+              xu[k + h] = d0 >= q ? d0 - q : d0;
+            }
           }
         }
       }
@@ -192,7 +208,7 @@ __device__ __forceinline__ void ntt_pass_body(uint64_t* __restrict__ data, const
     if (step + 1 < NG) {
       if (step > 0) __syncthreads();  // everyone has read the previous layout
 #pragma unroll
-      for (int j = 0; j < 8; ++j) {
+      for (int j = 0; j < R; ++j) {
         if (j >= units_per_thread * usz) break;
         const int uj = j / usz, k = j % usz;
         const int u = sub_t + uj * T;
@@ -201,7 +217,7 @@ __device__ __forceinline__ void ntt_pass_body(uint64_t* __restrict__ data, const
       __syncthreads();
     } else {
 #pragma unroll
-      for (int j = 0; j < 8; ++j) {
+      for (int j = 0; j < R; ++j) {
         if (j >= units_per_thread * usz) break;
         const int uj = j / usz, k = j % usz;
         const int u = sub_t + uj * T;
@@ -221,13 +237,16 @@ __device__ __forceinline__ void ntt_pass_body(uint64_t* __restrict__ data, const
 // doubles; the twiddle product of y by (w, wq = fl(w/q)) is exact:
 //   k = rint(y wq) (the 1.5 * 2^52 rounding, valid while |y wq| < 2^51),
 //   r = fma(-k, q, y*w) + fma(y, w, -y*w)  = y w - k q,  |r| < 0.52 q,
-// with |y| < 1.6 q; the bounds per stage within a register group of three
-// stages, from inputs centred to |x| <= 0.51 q:
+// with |y| < 1.6 q; the bounds per stage within a register group of up to
+// four stages, from inputs centred to |x| <= 0.51 q:
 //   forward  x' = x + r, y' = x - r: the multiplied input of stages 1-3 is
-//            below 0.51, 1.03, 1.55 q; all values stay below 2.1 q;
+//            below 0.51, 1.03, 1.55 q, and the fourth stage re-centres it
+//            first; all values stay below 2.6 q;
 //   inverse  x' = x + y, y' = (x - y) w: the difference is re-centred before
-//            the product from the group's second stage on; values stay below
-//            2.1 q.
+//            the product from the group's second stage on; the sums stay
+//            below 4.1 q through three stages, and the fourth stage
+//            re-centres both of its inputs first.
+// All of these are below 2^53 for q < 1.25 * 2^50, so every sum is exact.
 // Every group ends by re-centring all values (k = rint(x / q), x - k q), so
 // each pass hands on |x| <= 0.51 q; the transform's output is the canonical
 // residue, as on the integer path.
@@ -251,11 +270,12 @@ __device__ __forceinline__ uint64_t fp_to_residue(double x, double q) {
   return __double2ull_rn(x < 0.0 ? __dadd_rn(x, q) : x);
 }
 
-template <int S_LOG, bool INV, bool STRIDED>
+template <int S_LOG, bool INV, bool STRIDED, int R_LOG>
 __device__ __forceinline__ void ntt_pass_body_fp(uint64_t* __restrict__ data, const PassArgs& a, uint64_t* sm) {
   constexpr int S = 1 << S_LOG;
-  constexpr int T = S >= 8 ? S / 8 : 1;
-  constexpr int NG = (S_LOG + 2) / 3;
+  constexpr int R = 1 << R_LOG;
+  constexpr int T = S >= R ? S / R : 1;
+  constexpr int NG = (S_LOG + R_LOG - 1) / R_LOG;
 
   const int limb = blockIdx.y;
   const int prime = a.map.prime(limb);
@@ -286,23 +306,23 @@ __device__ __forceinline__ void ntt_pass_body_fp(uint64_t* __restrict__ data, co
     return STRIDED ? (size_t)r * stride + sub_global : (size_t)sub_global * S + r;
   };
   auto saddr = [&](int r) -> int {
-    return STRIDED ? r * per + lane_idx : lane_idx * S + (r ^ swizzle(r));
+    return STRIDED ? r * per + lane_idx : lane_idx * S + (r ^ swizzle<R_LOG>(r));
   };
 
-  double x[8];
+  double x[R];
 
 #pragma unroll
   for (int step = 0; step < NG; ++step) {
     const int gi = INV ? (NG - 1 - step) : step;
-    const int G = group_size(S_LOG, gi);
-    const int st0 = 3 * gi;
+    const int G = group_size<R_LOG>(S_LOG, gi);
+    const int st0 = R_LOG * gi;
     const int D = S >> (st0 + G);
-    const int units_per_thread = 8 >> G;
+    const int units_per_thread = R >> G;
     const int usz = 1 << G;
     // load: the transform's input as residues, the first pass's output and
     // the exchanges as centred doubles
 #pragma unroll
-    for (int j = 0; j < 8; ++j) {
+    for (int j = 0; j < R; ++j) {
       if (j >= units_per_thread * usz) break;
       const int uj = j / usz, k = j % usz;
       const int u = sub_t + uj * T;
@@ -319,40 +339,48 @@ __device__ __forceinline__ void ntt_pass_body_fp(uint64_t* __restrict__ data, co
     }
     bool final_done = false;
 #pragma unroll
-    for (int uj = 0; uj < 8; ++uj) {
+    for (int uj = 0; uj < R; ++uj) {
       if (uj >= units_per_thread) break;
       const int u = sub_t + uj * T;
       const uint32_t B = (uint32_t)(u / D);
       double* xu = x + uj * usz;
 #pragma unroll
-      for (int it = 0; it < 3; ++it) {
+      for (int it = 0; it < R_LOG; ++it) {
         if (it >= G) break;
         const int rr = INV ? (G - 1 - it) : it;
         const int st = st0 + rr;
         const int h = 1 << (G - 1 - rr);
         const bool final_stage = INV && STRIDED && st == 0;
         const uint32_t idx0 = (1u << (gs0 + st)) + (prefix << st) + (B << rr);
-        double2 w[4];
-        if (!final_stage) {
+        // pairs (k, k + h) with k >> (G - rr) == jw share twiddle jw
 #pragma unroll
-          for (int j = 0; j < 4; ++j)
-            if (j < (1 << rr)) w[j] = __ldg(tw + idx0 + j);
-        }
+        for (int jw = 0; jw < R / 2; ++jw) {
+          if (jw >= (1 << rr)) break;
+          double2 w{0.0, 0.0};
+          if (!final_stage) w = __ldg(tw + idx0 + jw);
 #pragma unroll
-        for (int k = 0; k < 8; ++k) {
-          if (k >= usz) break;
+          for (int kk = 0; kk < R; ++kk) {
+          if (kk >= (1 << (G - rr))) break;
+          const int k = (jw << (G - rr)) + kk;
           if (k & h) continue;
           if (!INV) {
-            const double t = fp_mulw(xu[k + h], w[k >> (G - rr)], q);
+            const double y0 = it >= 3 ? fp_center(xu[k + h], q, qinv) : xu[k + h];
+            const double t = fp_mulw(y0, w, q);
             const double x0 = xu[k];
             xu[k] = __dadd_rn(x0, t);
             xu[k + h] = __dsub_rn(x0, t);
           } else if (!final_stage) {
-            const double x0 = xu[k], y0 = xu[k + h];
-            double d = __dsub_rn(x0, y0);
-            if (it > 0) d = fp_center(d, q, qinv);
+            double x0 = xu[k], y0 = xu[k + h], d;
+            if (it >= 3) {
+              x0 = fp_center(x0, q, qinv);
+              y0 = fp_center(y0, q, qinv);
+              d = __dsub_rn(x0, y0);
+            } else {
+              d = __dsub_rn(x0, y0);
+              if (it > 0) d = fp_center(d, q, qinv);
+            }
             xu[k] = __dadd_rn(x0, y0);
-            xu[k + h] = fp_mulw(d, w[k >> (G - rr)], q);
+            xu[k + h] = fp_mulw(d, w, q);
           } else {
             // last inverse stage on canonical residues with the integer
             // Shoup constants (n^-1 or the caller's scale folded in)
@@ -366,6 +394,7 @@ __device__ __forceinline__ void ntt_pass_body_fp(uint64_t* __restrict__ data, co
             xu[k + h] = __longlong_as_double((long long)(d0 >= qi ? d0 - qi : d0));
             final_done = true;
           }
+          }
         }
       }
     }
@@ -373,7 +402,7 @@ __device__ __forceinline__ void ntt_pass_body_fp(uint64_t* __restrict__ data, co
     if (step + 1 < NG) {
       if (step > 0) __syncthreads();
 #pragma unroll
-      for (int j = 0; j < 8; ++j) {
+      for (int j = 0; j < R; ++j) {
         if (j >= units_per_thread * usz) break;
         const int uj = j / usz, k = j % usz;
         const int u = sub_t + uj * T;
@@ -382,7 +411,7 @@ __device__ __forceinline__ void ntt_pass_body_fp(uint64_t* __restrict__ data, co
       __syncthreads();
     } else {
 #pragma unroll
-      for (int j = 0; j < 8; ++j) {
+      for (int j = 0; j < R; ++j) {
         if (j >= units_per_thread * usz) break;
         const int uj = j / usz, k = j % usz;
         const int u = sub_t + uj * T;
@@ -399,32 +428,37 @@ __device__ __forceinline__ void ntt_pass_body_fp(uint64_t* __restrict__ data, co
   }
 }
 
-template <int S_LOG, bool INV, bool STRIDED>
-__global__ void __launch_bounds__(kThreads, 2) ntt_pass_kernel(uint64_t* __restrict__ data, PassArgs a) {
+template <int S_LOG, bool INV, bool STRIDED, int R_LOG>
+__global__ void __launch_bounds__(PassShape<R_LOG>::kThreads, PassShape<R_LOG>::kMinBlocks)
+    ntt_pass_kernel(uint64_t* __restrict__ data, PassArgs a) {
   extern __shared__ uint64_t sm[];
   const int limb = blockIdx.y;
   if (a.map.skipped(limb)) return;
   const uint64_t q = a.mods[a.map.prime(limb)].q;
   if (q < kFpNttPrime)
-    ntt_pass_body_fp<S_LOG, INV, STRIDED>(data, a, sm);
+    ntt_pass_body_fp<S_LOG, INV, STRIDED, R_LOG>(data, a, sm);
   else
-    ntt_pass_body<S_LOG, INV, STRIDED>(data, a, sm);
+    ntt_pass_body<S_LOG, INV, STRIDED, R_LOG>(data, a, sm);
 }
 
 template <int S_LOG, bool INV, bool STRIDED>
 void launch_pass(uint64_t* data, int nlimbs, const PassArgs& a0, cudaStream_t st) {
+  // strided passes: 16 residues per thread (four stages per register group,
+  // twice the loads in flight per thread); contiguous passes, whose
+  // shared-memory exchanges favour more resident warps: 8
+  constexpr int R_LOG = (STRIDED && S_LOG >= 4) ? 4 : 3;
   constexpr int S = 1 << S_LOG;
-  constexpr int T = S >= 8 ? S / 8 : 1;
+  constexpr int T = S >= (1 << R_LOG) ? S / (1 << R_LOG) : 1;
   const int N = 1 << a0.logN;
   const int subs = N / S;  // sub-transforms per limb
-  int per = kThreads / T;
+  int per = PassShape<R_LOG>::kThreads / T;
   if (per > subs) per = subs;
   PassArgs a = a0;
   a.per_cta = per;
   const dim3 grid(subs / per, nlimbs);
   const int threads = per * T;
   const size_t smem = (size_t)S * per * sizeof(uint64_t);
-  auto k = ntt_pass_kernel<S_LOG, INV, STRIDED>;
+  auto k = ntt_pass_kernel<S_LOG, INV, STRIDED, R_LOG>;
   if (smem > 48 * 1024) cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   k<<<grid, threads, smem, st>>>(data, a);
 }
