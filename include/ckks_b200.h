@@ -348,6 +348,40 @@ int ckks_head_forward(ckks_block* head, const double* x_last, double* margin);
 int ckks_model_forward(ckks_block* const* blocks, int nblocks, ckks_block* head, const double* x, int tokens,
                        int cached_blocks, double* hidden, double* margin);
 
+/* ---- the block driver's fused matrix product and lane shift --------------
+ * Slot layout slot(feature f, lane t) = f * batch + t with pack width
+ * PW = N / (2 batch) features (T123.cpp:419-426 with one copy). */
+typedef struct ckks_diag ckks_diag;
+/* cached_diagonal_plains(W, level) (T123.cpp:1005-1059): the PW = n1 * n2
+ * diagonals of the Halevi-Shoup product with W ([out_dim, in_dim] float64,
+ * row stride ld, host; out_dim, in_dim <= PW), diagonal g * n1 + j holding
+ * W[(f - n1 g) mod PW][(f + j) mod PW] at feature f of every lane (zero
+ * outside the matrix, T123.cpp:1018-1046), encoded at `limbs` limbs with
+ * that level's FLEXIBLEAUTO scale and kept on the device until destroyed
+ * (n1, n2 <= 32). */
+int ckks_bsgs_diagonals_create(ckks_ctx* ctx, const double* W, int out_dim, int in_dim, int ld, int batch, int n1,
+                               int limbs, ckks_diag** out);
+int ckks_bsgs_diagonals_destroy(ckks_diag* d);
+/* matmul(BabyRotations, W) (T123.cpp:1264-1295) for `groups` token groups
+ * and a sum of `terms` matrices: outs[q] = Rescale(sum_t sum_g rot(sum_j
+ * diag_t[g n1 + j] * baby[(t * groups + q) * n1 + j], batch * n1 * g)),
+ * where baby[... + j] = EvalRotate(x_{t,q}, batch * j) (j = 0: x itself) at
+ * the diagonals' limbs and noise degree 1.  The inner sums of all groups of
+ * a coefficient tile run in one fused kernel that reads each diagonal tile
+ * from HBM once; the giant steps of a group are one rotation sum (one ModDown).
+ * With terms > 1 the inner sums accumulate before the giant steps (the
+ * summed MLP down projection).  Needs the rotation keys batch * n1 * g. */
+int ckks_bsgs_matmul(ckks_ctx* ctx, const ckks_diag* const* diags, int terms, const ckks_ct* const* baby, int groups,
+                     ckks_ct* const* outs);
+/* lane_shift(x, d) (T123.cpp:1297-1314): out[f, t] = x[f, (t + d) mod batch]
+ * = Rescale(rot(x, d) * [t < batch - d] + rot(x, d - batch) * [t >= batch - d])
+ * for every input (one limb count, noise degree 1) and every d in
+ * deltas (0 < d < batch): outs[i * nd + k] = lane_shift(in[i], deltas[k]).
+ * The rotations of all inputs are one hoisted batch.  Needs the rotation
+ * keys d and d - batch. */
+int ckks_lane_shift(ckks_ctx* ctx, const ckks_ct* const* in, int count, const int* deltas, int nd, int batch,
+                    ckks_ct* const* outs);
+
 /* host-only schedule helpers: causal lane shifts of a (query group, key
  * group) tile (simd_layout.py:386-406) and one BSGS diagonal as slot values
  * (T123.cpp:1018-1046) */

@@ -67,7 +67,11 @@ class PlaintextImpl {
 class CiphertextImpl {
  public:
   explicit CiphertextImpl(ckks_ctx* c) : ctx_(c) { check(ckks_ct_create(c, &h_)); }
-  ~CiphertextImpl() { ckks_ct_destroy(h_); }
+  // non-owning view of a handle the caller keeps (not destroyed with the view)
+  CiphertextImpl(ckks_ctx* c, ckks_ct* existing) : ctx_(c), h_(existing), owns_(false) {}
+  ~CiphertextImpl() {
+    if (owns_) ckks_ct_destroy(h_);
+  }
   CiphertextImpl(const CiphertextImpl&) = delete;
   CiphertextImpl& operator=(const CiphertextImpl&) = delete;
   ckks_ct* handle() const { return h_; }
@@ -79,6 +83,7 @@ class CiphertextImpl {
  private:
   ckks_ctx* ctx_;
   ckks_ct* h_ = nullptr;
+  bool owns_ = true;
 };
 
 using Plaintext = std::shared_ptr<PlaintextImpl>;

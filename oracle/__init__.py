@@ -70,6 +70,30 @@ class OracleError(RuntimeError):
     pass
 
 
+def diagonal_slots(W: np.ndarray, batch: int, pack_width: int, n1: int, g: int, j: int) -> np.ndarray:
+    """Slot values of BSGS diagonal g * n1 + j of W ([out, in]) on the layout
+    slot(feature f, lane t) = f * batch + t: the diagonal pre-rotated by the
+    giant step, W[rolled][(rolled + n1 g + j) mod PW] at feature f with
+    rolled = (f - n1 g) mod PW, zero outside W, the same on every lane
+    (cached_diagonal_plains, T123.cpp:1018-1046)."""
+    out_dim, in_dim = W.shape
+    f = np.arange(pack_width)
+    rolled = (f - n1 * g) % pack_width
+    col = (rolled + n1 * g + j) % pack_width
+    inside = (rolled < out_dim) & (col < in_dim)
+    v = np.where(inside, W[np.minimum(rolled, out_dim - 1), np.minimum(col, in_dim - 1)], 0.0)
+    return np.repeat(v, batch)
+
+
+def lane_mask_slots(batch: int, pack_width: int, delta: int, no_wrap: bool) -> np.ndarray:
+    """lane_mask_plain(delta, no_wrap) (T123.cpp:1076-1093): 1 on the lanes
+    t < batch - delta (no_wrap) or t >= batch - delta (not no_wrap) of every
+    feature."""
+    t = np.arange(batch)
+    lane = ((t < batch - delta) == no_wrap).astype(np.float64)
+    return np.tile(lane, pack_width)
+
+
 class Oracle:
     """One CPU CKKS context: parameters, tables and (after keygen) keys."""
 
@@ -141,6 +165,17 @@ class Oracle:
         out = np.zeros((limbs, self.N), np.uint64)
         sc = self.scale(limbs) if scale is None else scale
         self._check(self.L_.oc_encode(self._c(), _p(v), limbs, ctypes.c_double(sc), _p(out)))
+        return out
+
+    def encode_batch(self, values: np.ndarray, limbs: int, scale: float, out: np.ndarray | None = None):
+        """Encodings of the rows of `values` (count x N/2) at `limbs` limbs,
+        computed in parallel; writes into `out` (count x limbs x N) if given."""
+        v = np.ascontiguousarray(values, np.float64)
+        count = v.shape[0]
+        if out is None:
+            out = np.zeros((count, limbs, self.N), np.uint64)
+        assert out.flags["C_CONTIGUOUS"] and out.shape == (count, limbs, self.N)
+        self._check(self.L_.oc_encode_batch(self._c(), _p(v), count, limbs, ctypes.c_double(scale), _p(out)))
         return out
 
     def decode(self, pt: np.ndarray, scale: float) -> np.ndarray:
@@ -316,6 +351,61 @@ class Oracle:
         out = np.empty_like(ct)
         self._check(self.L_.oc_accumulate_sum(self._c(), _p(ct), ct.shape[1], count, stride, _p(out)))
         return out
+
+    # -- block-driver compositions (T123.cpp:1005-1059, 1264-1314) ---------
+    def bsgs_diagonals(self, W: np.ndarray, batch: int, n1: int, limbs: int) -> np.ndarray:
+        """cached_diagonal_plains(W, level): every diagonal of the n1 x n2
+        BSGS split encoded at `limbs` limbs and that level's scale,
+        (n1 * n2, limbs, N)."""
+        pw = self.N // 2 // batch
+        nd = pw
+        out = np.zeros((nd, limbs, self.N), np.uint64)
+        for d0 in range(0, nd, 64):
+            vals = np.stack([diagonal_slots(W, batch, pw, n1, d // n1, d % n1) for d in range(d0, min(nd, d0 + 64))])
+            self.encode_batch(vals, limbs, self.scale(limbs), out[d0:d0 + len(vals)])
+        return out
+
+    def bsgs_inner(self, babies: np.ndarray, diags: np.ndarray, n1: int, out: np.ndarray | None = None):
+        """out[g] (+)= sum_j diags[g n1 + j] * babies[j] (adds to `out` when
+        given); babies (n1, 2, limbs, N), diags (n1 n2, limbs, N)."""
+        babies = np.ascontiguousarray(babies, np.uint64)
+        diags = np.ascontiguousarray(diags, np.uint64)
+        n2 = diags.shape[0] // n1
+        limbs = babies.shape[2]
+        acc = out is not None
+        if out is None:
+            out = np.zeros((n2, 2, limbs, self.N), np.uint64)
+        assert out.flags["C_CONTIGUOUS"] and out.dtype == np.uint64
+        self._check(self.L_.oc_bsgs_inner(self._c(), _p(babies), n1, _p(diags), n2, limbs, int(acc), _p(out)))
+        return out
+
+    def bsgs_matmul(self, diags_terms, babies_terms, n1: int, batch: int):
+        """matmul(BabyRotations, W) (T123.cpp:1264-1295) summed over matrix
+        terms: for each group q, Rescale(sum_g rot(sum_t sum_j
+        diag_t[g n1 + j] * babies_t[q][j], batch n1 g)), the giant steps as
+        one rotation sum (one ModDown per 32 rotations, oc_rotate_sum)."""
+        G = len(babies_terms[0])
+        n2 = diags_terms[0].shape[0] // n1
+        ks = [batch * n1 * g for g in range(n2)]
+        outs = []
+        for q in range(G):
+            inner = None
+            for t, diags in enumerate(diags_terms):
+                inner = self.bsgs_inner(np.stack(babies_terms[t][q]), diags, n1, inner)
+            outs.append(self.rescale(self.rotate_sum(inner, ks)))
+        return outs
+
+    def lane_shift(self, ct, delta: int, batch: int):
+        """lane_shift(x, delta) (T123.cpp:1297-1314): rot(x, d) masked to
+        the lanes t < batch - d plus rot(x, d - batch) masked to the others,
+        rescaled; the two rotations share one ModUp (EvalFastRotation)."""
+        limbs = ct.shape[1]
+        pw = self.N // 2 // batch
+        r = self.rotate_hoisted(ct, [delta, delta - batch])
+        sc = self.scale(limbs)
+        lo = self.mul_pt(r[0], self.encode(lane_mask_slots(batch, pw, delta, True), limbs, sc))
+        hi = self.mul_pt(r[1], self.encode(lane_mask_slots(batch, pw, delta, False), limbs, sc))
+        return self.rescale(self.add(lo, hi))
 
     @staticmethod
     def chacha(seed: int, nonce: int, counter: int):

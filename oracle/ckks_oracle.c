@@ -627,6 +627,19 @@ int oc_encode(const oc_ctx* c, const double* values, int limbs, double scale, ui
     return 0;
 }
 
+/* `count` independent encodings (values: count x N/2, out: count x limbs x
+ * N), spread over the threads: the reference encodes a product's diagonals
+ * this way, one MakeCKKSPackedPlaintext per diagonal in an OpenMP loop
+ * (T123.cpp:1048-1056). */
+int oc_encode_batch(const oc_ctx* c, const double* values, int count, int limbs, double scale, uint64_t* out) {
+    if (limbs > c->L) { set_err("encode: more limbs than the Q chain"); return -1; }
+    int bad = 0;
+#pragma omp parallel for schedule(dynamic) reduction(| : bad)
+    for (int i = 0; i < count; i++)
+        bad |= oc_encode(c, values + (size_t)i * (c->N / 2), limbs, scale, out + (size_t)i * limbs * c->N) != 0;
+    return bad ? -1 : 0;
+}
+
 /* centered CRT over the first two limbs -> double, then /scale and FFT
  * (Decrypt + GetRealPackedValue, T123.cpp:523-531). */
 void oc_decode(const oc_ctx* c, const uint64_t* pt, int limbs, double scale, double* values) {
@@ -1343,5 +1356,38 @@ int oc_accumulate_sum(const oc_ctx* c, const uint64_t* ct, int limbs, int count,
         for (int r = 0; r < n; r++) oc_add(c, out, rot + (size_t)r * S2, 2, limbs, out);
     }
     free(rot);
+    return 0;
+}
+
+/* Inner sums of the Halevi-Shoup product matmul(BabyRotations, W)
+ * (T123.cpp:1264-1295, the loop over `small`): for every giant step g < n2,
+ * out[g] (+)= sum_{j < n1} diag[g * n1 + j] * baby[j], both polynomials.
+ * babies: n1 x 2 x limbs x N; diags: (n1 * n2) x limbs x N plaintexts;
+ * out: n2 x 2 x limbs x N, added to when `accumulate` (a sum of products
+ * whose giant steps run once).  Each output residue is the exact sum
+ * reduced once (products below 2^120, at most 32 of them). */
+int oc_bsgs_inner(const oc_ctx* c, const uint64_t* babies, int n1, const uint64_t* diags, int n2, int limbs,
+                  int accumulate, uint64_t* out) {
+    if (n1 <= 0 || n1 > 64 || n2 <= 0) { set_err("bsgs: n1 in 1..64, n2 > 0"); return -1; }
+    const int N = c->N;
+    const size_t S = (size_t)limbs * N;
+#pragma omp parallel for collapse(2) schedule(dynamic)
+    for (int g = 0; g < n2; g++)
+        for (int l = 0; l < limbs; l++) {
+            const modulus_t* m = &c->mod[l];
+            for (int p = 0; p < 2; p++) {
+                uint64_t* o = out + (size_t)g * 2 * S + (size_t)p * S + (size_t)l * N;
+                for (int n = 0; n < N; n++) {
+                    u128 acc = 0;
+                    for (int j = 0; j < n1; j++) {
+                        const uint64_t b = babies[(size_t)j * 2 * S + (size_t)p * S + (size_t)l * N + n];
+                        const uint64_t d = diags[((size_t)g * n1 + j) * S + (size_t)l * N + n];
+                        acc += (u128)b * d;
+                    }
+                    const uint64_t r = reduce128(acc, m);
+                    o[n] = accumulate ? addm(o[n], r, m->q) : r;
+                }
+            }
+        }
     return 0;
 }

@@ -68,6 +68,8 @@ void oc_chacha_words(uint64_t seed, uint64_t nonce, uint64_t counter, uint64_t o
 
 /* values: N/2 real slots; out: limbs*N, NTT form.  Returns 0. */
 int oc_encode(const oc_ctx* c, const double* values, int limbs, double scale, uint64_t* out);
+/* count encodings at once (values count x N/2, out count x limbs x N), in parallel */
+int oc_encode_batch(const oc_ctx* c, const double* values, int count, int limbs, double scale, uint64_t* out);
 /* coefficient-form rounding only (no NTT); out: limbs*N */
 int oc_encode_coeffs(const oc_ctx* c, const double* values, int limbs, double scale, uint64_t* out);
 void oc_decode(const oc_ctx* c, const uint64_t* pt, int limbs, double scale, double* values);
@@ -129,6 +131,12 @@ int oc_window_sum_radix(const oc_ctx* c, const uint64_t* ct, int limbs, int wind
  * (takes NTT-form d, like the engine does) */
 void oc_modup(const oc_ctx* c, const uint64_t* d_ntt, int limbs, uint64_t* ext);
 void oc_moddown(const oc_ctx* c, const uint64_t* x_ntt, int limbs, uint64_t* out);
+
+/* inner sums of the BSGS product (T123.cpp:1264-1295): out[g] (+)= sum_{j<n1}
+ * diag[g*n1 + j] * baby[j] for g < n2; babies n1 x 2 x limbs x N, diags
+ * (n1*n2) x limbs x N, out n2 x 2 x limbs x N */
+int oc_bsgs_inner(const oc_ctx* c, const uint64_t* babies, int n1, const uint64_t* diags, int n2, int limbs,
+                  int accumulate, uint64_t* out);
 
 const char* oc_last_error(void);
 

@@ -174,6 +174,12 @@ _SIGS = [
     ("ckks_ntt_inverse_device", ctypes.c_int, [_vp, _vp, ctypes.c_int, ctypes.c_int]),
     ("ckks_ntt_forward_polys", ctypes.c_int, [_vp, _vp, ctypes.c_int, ctypes.c_int]),
     ("ckks_ntt_inverse_polys", ctypes.c_int, [_vp, _vp, ctypes.c_int, ctypes.c_int]),
+    ("ckks_bsgs_diagonals_create", ctypes.c_int, [_vp, _f64p] + [ctypes.c_int] * 6 + [ctypes.POINTER(_vp)]),
+    ("ckks_bsgs_diagonals_destroy", ctypes.c_int, [_vp]),
+    ("ckks_bsgs_matmul", ctypes.c_int, [_vp, ctypes.POINTER(_vp), ctypes.c_int, ctypes.POINTER(_vp), ctypes.c_int,
+                                        ctypes.POINTER(_vp)]),
+    ("ckks_lane_shift", ctypes.c_int, [_vp, ctypes.POINTER(_vp), ctypes.c_int, ctypes.POINTER(ctypes.c_int),
+                                       ctypes.c_int, ctypes.c_int, ctypes.POINTER(_vp)]),
 ]
 
 _lib = None
@@ -291,6 +297,30 @@ class Ciphertext:
         out = np.zeros((2, self.limbs, self.cc.N), np.uint64)
         _check(lib().ckks_ct_export(self.cc.h, self.h, _u64(out), out.size))
         return out
+
+
+class Diagonals:
+    """cached_diagonal_plains of one matrix at one level (T123.cpp:1005-1059):
+    the n1 * n2 encoded BSGS diagonals, kept on the device."""
+
+    def __init__(self, cc: "CryptoContext", W: np.ndarray, batch: int, n1: int, limbs: int):
+        self.cc = cc
+        W = np.ascontiguousarray(W, np.float64)
+        out_dim, in_dim = W.shape
+        h = _vp()
+        _check(lib().ckks_bsgs_diagonals_create(cc.h, W.ctypes.data_as(_f64p), out_dim, in_dim, in_dim, batch, n1,
+                                                limbs, ctypes.byref(h)))
+        self.h = h
+        self.batch, self.n1, self.limbs = batch, n1, limbs
+        self.n2 = cc.N // 2 // batch // n1
+
+    def __del__(self):
+        try:
+            if self.h:
+                lib().ckks_bsgs_diagonals_destroy(self.h)
+                self.h = None
+        except Exception:
+            pass
 
 
 class CryptoContext:
@@ -655,6 +685,37 @@ class CryptoContext:
         outs = [self._new() for _ in cts]
         _check(lib().ckks_rotate_sum_hoisted(self.h, (_vp * max(1, n))(*[c.h for c in cts]), n,
                                              (ctypes.c_int * nk)(*ks), nk, (_vp * max(1, n))(*[o.h for o in outs])))
+        return outs
+
+    def bsgs_diagonals(self, W: np.ndarray, batch: int, n1: int, limbs: int) -> Diagonals:
+        """The encoded BSGS diagonals of W ([out, in]) at `limbs` limbs."""
+        return Diagonals(self, W, batch, n1, limbs)
+
+    def bsgs_babies(self, cts, batch: int, n1: int) -> list[list[Ciphertext]]:
+        """Baby steps [x, rot(x, batch), ..., rot(x, batch (n1 - 1))] of every
+        input, one hoisted batch (EvalFastRotation, T123.cpp:1190-1191)."""
+        r = self.EvalFastRotationBatch(cts, [batch * j for j in range(1, n1)])
+        return [[c] + row for c, row in zip(cts, r)]
+
+    def bsgs_matmul(self, diags, babies) -> list[Ciphertext]:
+        """matmul(BabyRotations, W) (T123.cpp:1264-1295): babies[t][q] are the
+        n1 baby steps of token group q for matrix term t (diags[t]); returns
+        one rescaled product per group, summed over the terms."""
+        T, G = len(diags), len(babies[0])
+        flat = [c.h for t in range(T) for q in range(G) for c in babies[t][q]]
+        outs = [self._new() for _ in range(G)]
+        _check(lib().ckks_bsgs_matmul(self.h, (_vp * T)(*[d.h for d in diags]), T, (_vp * len(flat))(*flat), G,
+                                      (_vp * G)(*[o.h for o in outs])))
+        return outs
+
+    def lane_shift(self, cts, deltas, batch: int) -> list[list[Ciphertext]]:
+        """lane_shift (T123.cpp:1297-1314) of every input by every delta:
+        out[i][k][f, t] = cts[i][f, (t + deltas[k]) mod batch], rescaled."""
+        n, nd = len(cts), len(deltas)
+        outs = [[self._new() for _ in deltas] for _ in cts]
+        flat = [o.h for row in outs for o in row]
+        _check(lib().ckks_lane_shift(self.h, (_vp * n)(*[c.h for c in cts]), n, (ctypes.c_int * nd)(*deltas), nd,
+                                     batch, (_vp * len(flat))(*flat)))
         return outs
 
     def WindowSumBatch(self, cts, window: int, stride: int, radix: int = 4) -> list[Ciphertext]:

@@ -36,6 +36,7 @@
 #include <cmath>
 #include <cstdio>
 #include <cstring>
+#include <functional>
 #include <map>
 #include <string>
 #include <vector>
@@ -525,6 +526,200 @@ double now_s() {
   return std::chrono::duration<double>(std::chrono::steady_clock::now().time_since_epoch()).count();
 }
 
+// All n1 * n2 BSGS diagonals of W ([out, in] float64 on the device, row
+// stride ld) as plaintexts of `limbs` limbs at `scale`, in the tile-major
+// layout the inner-sum kernels stream (the reference encodes them on the
+// host, cached_diagonal_plains, T123.cpp:1005-1059).  Returns a buffer of
+// n1 * n2 * limbs * N words from C.alloc.
+uint64_t* encode_diagonals(ckks::Context& C, const double* W, int od, int idim, int ld, int PW, int B, int n1,
+                           int n2, int limbs, double scale) {
+  const int nd = n1 * n2, slots = PW * B;
+  const size_t stride = (size_t)limbs * C.N;
+  uint64_t* data = (uint64_t*)C.alloc(sizeof(uint64_t) * nd * stride);
+  const int chunk = 128;
+  double* vals = (double*)C.alloc(sizeof(double) * (size_t)chunk * slots);
+  uint64_t* enc = (uint64_t*)C.alloc(sizeof(uint64_t) * (size_t)chunk * stride);
+  for (int d0 = 0; d0 < nd; d0 += chunk) {
+    const int cnt = std::min(chunk, nd - d0);
+    {
+      ckks::ProfScope ps(C, "diag_values", 8.0 * slots * cnt, C.stream);
+      diag_values_kernel<<<dim3((slots + kThreads - 1) / kThreads, cnt), kThreads, 0, C.stream>>>(
+          W, od, idim, ld, PW, B, n1, d0, vals);
+    }
+    CKKS_CUDA(cudaGetLastError());
+    ckks::encode_batch(C, vals, cnt, limbs, scale, enc, stride, C.stream);
+    {
+      ckks::ProfScope ps(C, "diag_tile", 2.0 * cnt * stride * 8.0, C.stream);
+      diag_tile_kernel<<<dim3(C.N / kThreads, limbs, cnt), kThreads, 0, C.stream>>>(enc, cnt, d0, nd, limbs, C.logN,
+                                                                                     C.d_mods, data);
+    }
+    CKKS_CUDA(cudaGetLastError());
+  }
+  C.release(vals);
+  C.release(enc);
+  return data;
+}
+
+// encoded diagonals of one matrix term of a product
+struct DiagRef {
+  const uint64_t* data;
+  int limbs;
+  double scale;
+};
+
+// outs[q] = Rescale(sum_g rot(sum_t sum_j diag_t[g n1 + j] * babies[t][q][j],
+// B n1 g)) for every token group q: the Halevi-Shoup product of
+// matmul(BabyRotations, W) (T123.cpp:1264-1295) summed over the terms t (a
+// sum of products x_t W_t^T whose giant-step rotations run once for the
+// whole sum, rotation being linear).  babies[t][q] holds the n1 baby steps
+// rot(x_{t,q}, B j); every term's diagonals are encoded at the babies'
+// limbs.  The inner sums are fused kernels over all groups of a tile (up to
+// kMaxGroups per launch); the giant steps of the groups are one rotation sum
+// each, their key products sharing launches, then one batched rescale.
+std::vector<Ciphertext> bsgs_products(ckks_b200::CryptoContextImpl& cc, ckks::Context& C,
+                                      const std::vector<std::vector<std::vector<Ciphertext>>>& babies,
+                                      const std::vector<DiagRef>& dgs, int n1, int n2, int B) {
+  const int nt = (int)babies.size();
+  const int G = nt ? (int)babies[0].size() : 0;
+  std::vector<Ciphertext> outs(G);
+  if (!G) return outs;
+  if ((int)dgs.size() != nt) throw ckks::Error(CKKS_EARG, "one diagonal set per term");
+  const int limbs = babies[0][0][0]->limbs();
+  for (int t = 0; t < nt; ++t) {
+    if ((int)babies[t].size() != G) throw ckks::Error(CKKS_EARG, "terms over different groups");
+    if (dgs[t].limbs != limbs) throw ckks::Error(CKKS_ELEVEL, "diagonals at another level than the baby steps");
+  }
+  std::vector<int> gk(n2);
+  for (int g = 0; g < n2; ++g) gk[g] = B * n1 * g;
+  for (int q0 = 0; q0 < G; q0 += kMaxGroups) {
+    const int ng = std::min(kMaxGroups, G - q0);
+    InnerPtrs ip{};
+    std::vector<std::vector<Ciphertext>> inner(ng, std::vector<Ciphertext>(n2));
+    for (int q = 0; q < ng; ++q) {
+      const double sc = babies[0][q0 + q][0]->scale() * dgs[0].scale;
+      for (int t = 1; t < nt; ++t) {
+        const double st_ = babies[t][q0 + q][0]->scale() * dgs[t].scale;
+        if (std::fabs(st_ - sc) > 1e-9 * sc) throw ckks::Error(CKKS_ESCALE, "product terms at different scales");
+      }
+      for (int g = 0; g < n2; ++g) {
+        inner[q][g] = cc.fresh();
+        ckks::DevPoly& p = inner[q][g]->handle()->p;
+        p.ensure(&C, 2, limbs);
+        p.limbs = limbs;
+        p.scale = sc;
+        p.deg = babies[0][q0 + q][0]->noise_deg() + 1;
+        ip.c0[q][g] = p.data;
+        ip.c1[q][g] = p.data + (size_t)p.cap * C.N;
+      }
+    }
+    for (int t = 0; t < nt; ++t) {
+      BabyPtrs bp{};
+      for (int q = 0; q < ng; ++q) {
+        const auto& baby = babies[t][q0 + q];
+        if ((int)baby.size() != n1) throw ckks::Error(CKKS_EARG, "baby-step count differs from n1");
+        for (int j = 0; j < n1; ++j) {
+          const ckks::DevPoly& p = baby[j]->handle()->p;
+          if (p.limbs != limbs) throw ckks::Error(CKKS_ELEVEL, "baby steps at different levels");
+          bp.c0[q][j] = p.data;
+          bp.c1[q][j] = p.data + (size_t)p.cap * C.N;
+        }
+      }
+      const uint64_t* dg = dgs[t].data;
+      const bool acc = t > 0;
+      ckks::ProfScope ps(
+          C, "bsgs_inner",
+          ((double)n1 * n2 * limbs + ng * (2.0 * n1 * limbs + (acc ? 4.0 : 2.0) * n2 * limbs)) * C.limb_bytes(),
+          C.stream);
+      // runs of limbs with primes below kFpPrime take the float64 products,
+      // the others (the 60-bit first prime) the integer ones
+      for (int l0 = 0; l0 < limbs;) {
+        const bool fp = C.moduli[l0] < kFpPrime;
+        int l1 = l0 + 1;
+        while (l1 < limbs && (C.moduli[l1] < kFpPrime) == fp) ++l1;
+        const dim3 grid(n2, C.N / kThreads, l1 - l0);
+        if (n1 == 32 || n1 == 16 || n1 == 8) {
+          static_assert(kThreads % kBsgsRegCoeffs == 0, "a tile of whole CTAs");
+          const dim3 rgrid(ng * (kThreads / kBsgsRegCoeffs), C.N / kThreads, l1 - l0);
+          auto kern = fp ? (n1 == 32   ? bsgs_inner_reg_kernel<32>
+                            : n1 == 16 ? bsgs_inner_reg_kernel<16>
+                                       : bsgs_inner_reg_kernel<8>)
+                         : (n1 == 32   ? bsgs_inner_reg_int_kernel<32>
+                            : n1 == 16 ? bsgs_inner_reg_int_kernel<16>
+                                       : bsgs_inner_reg_int_kernel<8>);
+          kern<<<rgrid, kBsgsRegThreads, 0, C.stream>>>(bp, ng, dg, ip, C.logN, n2, l0, acc, C.d_mods);
+        } else if (fp) {
+          bsgs_inner_fp_kernel<<<grid, dim3(kBsgsThreads, ng), 0, C.stream>>>(bp, ng, n1, dg, ip, limbs, C.logN, n2,
+                                                                               l0, acc, C.d_mods);
+        } else {
+          bsgs_inner_kernel<<<grid, dim3(kBsgsThreads, ng), 0, C.stream>>>(bp, ng, n1, dg, ip, limbs, C.logN, n2, l0,
+                                                                            acc, C.d_mods);
+        }
+        l0 = l1;
+      }
+      CKKS_CUDA(cudaGetLastError());
+    }
+    // giant steps: sum_g rot(inner_g, B n1 g), the key switches summed in the
+    // extended basis with one ModDown (g = 0 is the identity); the groups'
+    // sums share launches and each giant-step key is read once for them
+    const auto sums = cc.RescaleBatch(cc.EvalRotateSumGroups(inner, gk));
+    for (int q = 0; q < ng; ++q) outs[q0 + q] = sums[q];
+  }
+  return outs;
+}
+
+// mask plaintext of lane_shift by d: 1 on lanes t < B - d (lower) or t >=
+// B - d (upper) of every feature, at `limbs` limbs
+using LaneMask = std::function<Plaintext(int d, bool lower, int limbs)>;
+
+// out[i][k] = lane_shift(in[i], ds[k]) for inputs at one limb count, with
+// lane_shift(x, d)[f, t] = x[f, (t + d) mod B] = rot(x, d) * lower_d +
+// rot(x, d - B) * upper_d, rescaled (simd_layout.py:142-158,
+// T123.cpp:1297-1314).  The rotations of every input are one hoisted batch
+// (each rotation key read once for all inputs), then batched masks, adds and
+// rescales.
+std::vector<std::vector<Ciphertext>> lane_shift_set(ckks_b200::CryptoContextImpl& cc, const std::vector<Ciphertext>& in,
+                                                    const std::vector<int>& ds, int B, const LaneMask& mask) {
+  std::vector<std::vector<Ciphertext>> out(in.size());
+  if (in.empty() || ds.empty()) return out;
+  const int l = in[0]->limbs();
+  std::vector<int> idx;
+  for (int d : ds) {
+    if (d <= 0 || d >= B) throw ckks::Error(CKKS_EARG, "lane shift outside (0, batch)");
+    idx.push_back(d);
+    idx.push_back(d - B);
+  }
+  for (const auto& x : in)
+    if (x->limbs() != l) throw ckks::Error(CKKS_ELEVEL, "lane shift inputs at different levels");
+  const auto r = cc.EvalFastRotationBatch(in, idx);
+  std::vector<Ciphertext> rot;
+  std::vector<Plaintext> masks;
+  for (size_t g = 0; g < in.size(); ++g)
+    for (size_t k = 0; k < ds.size(); ++k) {
+      rot.push_back(r[g][2 * k]);
+      rot.push_back(r[g][2 * k + 1]);
+      masks.push_back(mask(ds[k], true, l));
+      masks.push_back(mask(ds[k], false, l));
+    }
+  const auto prod = cc.EvalMultPlainBatch(rot, masks);
+  std::vector<Ciphertext> lo, hi;
+  for (size_t j = 0; j < prod.size(); j += 2) {
+    lo.push_back(prod[j]);
+    hi.push_back(prod[j + 1]);
+  }
+  const auto rs_ = cc.RescaleBatch(cc.EvalAddBatch(lo, hi));
+  for (size_t g = 0; g < in.size(); ++g)
+    for (size_t k = 0; k < ds.size(); ++k) out[g].push_back(rs_[g * ds.size() + k]);
+  return out;
+}
+
+// the slot values of lane_shift's mask: 1 where (t < B - d) == lower
+std::vector<double> lane_mask_values(int PW, int B, int d, bool lower) {
+  std::vector<double> v((size_t)PW * B, 0.0);
+  for (int f = 0; f < PW; ++f)
+    for (int t = 0; t < B; ++t) v[(size_t)f * B + t] = ((t < B - d) == lower) ? 1.0 : 0.0;
+  return v;
+}
+
 }  // namespace blk
 
 struct ckks_block {
@@ -723,15 +918,11 @@ struct ckks_block {
     masks[key] = p;
     return p;
   }
-  Plaintext lane_plain(int id, int delta, bool lower, int limbs) {
+  Plaintext lane_plain(int delta, bool lower, int limbs) {
     auto key = std::make_pair(1000 + 2 * delta + (lower ? 1 : 0), limbs);
     auto it = masks.find(key);
     if (it != masks.end()) return it->second;
-    std::vector<double> v((size_t)s.PW * s.B, 0.0);
-    for (int f = 0; f < s.PW; ++f)
-      for (int t = 0; t < s.B; ++t) v[(size_t)f * s.B + t] = ((t < s.B - delta) == lower) ? 1.0 : 0.0;
-    (void)id;
-    auto p = cc.MakePlaintextAt(v, limbs, S(limbs));
+    auto p = cc.MakePlaintextAt(blk::lane_mask_values(s.PW, s.B, delta, lower), limbs, S(limbs));
     masks[key] = p;
     return p;
   }
@@ -807,23 +998,10 @@ struct ckks_block {
     return mul_ct_rs_batch(centered, inv);
   }
 
-  // output[f, t] = input[f, (t + delta) mod B]: two rotations, two masks, one
-  // add (simd_layout.py:142-158, T123.cpp:1297-1314)
-  Ciphertext lane_shift(const Ciphertext& x, int delta) {
-    const int l = x->limbs();
-    ++count["rotations"];
-    ++count["rotations"];
-    auto r = cc.EvalFastRotation(x, {delta, delta - s.B});
-    const Ciphertext a = cc.EvalMult(r[0], lane_plain(0, delta, true, l));
-    const Ciphertext b = cc.EvalMult(r[1], lane_plain(0, delta, false, l));
-    count["ct_plain"] += 2;
-    return rs(cc.EvalAdd(a, b));
-  }
-
   // lane shifts of several inputs (xs[i] for every delta in needs[i], 0 ->
   // xs[i] brought to targets[i] limbs): inputs with the same deltas and level
   // share one hoisted batch (each rotation key read once for all of them),
-  // then batched masks, adds and rescales
+  // then batched masks, adds and rescales (blk::lane_shift_set)
   std::vector<std::map<int, Ciphertext>> lane_shifts_batch(const std::vector<Ciphertext>& xs,
                                                            const std::vector<std::vector<int>>& needs,
                                                            const std::vector<int>& targets) {
@@ -841,38 +1019,17 @@ struct ckks_block {
       ds.erase(std::unique(ds.begin(), ds.end()), ds.end());
       if (!ds.empty()) bins[{ds, xs[i]->limbs()}].push_back(i);
     }
+    const blk::LaneMask mask = [this](int d, bool lower, int limbs) { return lane_plain(d, lower, limbs); };
     for (const auto& bin : bins) {
       const std::vector<int>& ds = bin.first.first;
-      const int l = bin.first.second;
       const std::vector<size_t>& mem = bin.second;
-      std::vector<int> idx;
-      for (int d : ds) {
-        idx.push_back(d);
-        idx.push_back(d - s.B);
-      }
       std::vector<Ciphertext> in;
       for (size_t i : mem) in.push_back(xs[i]);
-      count["rotations"] += (long)idx.size() * (long)mem.size();
-      const auto r = cc.EvalFastRotationBatch(in, idx);
-      std::vector<Ciphertext> rot;
-      std::vector<Plaintext> masks;
+      count["rotations"] += 2 * (long)ds.size() * (long)mem.size();
+      count["ct_plain"] += 2 * (long)ds.size() * (long)mem.size();
+      const auto sh = blk::lane_shift_set(cc, in, ds, s.B, mask);
       for (size_t g = 0; g < mem.size(); ++g)
-        for (size_t k = 0; k < ds.size(); ++k) {
-          rot.push_back(r[g][2 * k]);
-          rot.push_back(r[g][2 * k + 1]);
-          masks.push_back(lane_plain(0, ds[k], true, l));
-          masks.push_back(lane_plain(0, ds[k], false, l));
-        }
-      count["ct_plain"] += (long)rot.size();
-      const auto prod = cc.EvalMultPlainBatch(rot, masks);
-      std::vector<Ciphertext> lo, hi;
-      for (size_t j = 0; j < prod.size(); j += 2) {
-        lo.push_back(prod[j]);
-        hi.push_back(prod[j + 1]);
-      }
-      const auto rs_ = cc.RescaleBatch(cc.EvalAddBatch(lo, hi));
-      for (size_t g = 0; g < mem.size(); ++g)
-        for (size_t k = 0; k < ds.size(); ++k) out[mem[g]][ds[k]] = rs_[g * ds.size() + k];
+        for (size_t k = 0; k < ds.size(); ++k) out[mem[g]][ds[k]] = sh[g][k];
     }
     return out;
   }
@@ -942,33 +1099,10 @@ struct ckks_block {
     const double* W;
     int od, id_, ld;
     weight_view(id, W, od, id_, ld);
-    const int nd = s.n1 * s.n2, slots = s.PW * s.B;
-    const size_t stride = (size_t)limbs * C.N;
     Diag dg;
     dg.limbs = limbs;
     dg.scale = S(limbs);
-    dg.data = (uint64_t*)C.alloc(sizeof(uint64_t) * nd * stride);
-    const int chunk = 128;
-    double* vals = (double*)C.alloc(sizeof(double) * (size_t)chunk * slots);
-    uint64_t* enc = (uint64_t*)C.alloc(sizeof(uint64_t) * (size_t)chunk * stride);
-    for (int d0 = 0; d0 < nd; d0 += chunk) {
-      const int cnt = std::min(chunk, nd - d0);
-      {
-        ckks::ProfScope ps(C, "diag_values", 8.0 * slots * cnt, C.stream);
-        blk::diag_values_kernel<<<dim3((slots + blk::kThreads - 1) / blk::kThreads, cnt), blk::kThreads, 0,
-                                    C.stream>>>(W, od, id_, ld, s.PW, s.B, s.n1, d0, vals);
-      }
-      CKKS_CUDA(cudaGetLastError());
-      ckks::encode_batch(C, vals, cnt, limbs, dg.scale, enc, stride, C.stream);
-      {
-        ckks::ProfScope ps(C, "diag_tile", 2.0 * cnt * stride * 8.0, C.stream);
-        blk::diag_tile_kernel<<<dim3(C.N / blk::kThreads, limbs, cnt), blk::kThreads, 0, C.stream>>>(
-            enc, cnt, d0, nd, limbs, C.logN, C.d_mods, dg.data);
-      }
-      CKKS_CUDA(cudaGetLastError());
-    }
-    C.release(vals);
-    C.release(enc);
+    dg.data = blk::encode_diagonals(C, W, od, id_, ld, s.PW, s.B, s.n1, s.n2, limbs, dg.scale);
     seconds["diagonal_encode"] += blk::now_s() - t0;
     return diags.emplace(key, dg).first->second;
   }
@@ -1003,94 +1137,17 @@ struct ckks_block {
                                           const std::vector<int>& ids) {
     const int nt = (int)babies.size();
     const int G = nt ? (int)babies[0].size() : 0;
-    std::vector<Ciphertext> outs(G);
-    if (!G) return outs;
+    if (!G) return std::vector<Ciphertext>(G);
     const int limbs = babies[0][0][0]->limbs();
-    std::vector<const Diag*> dgs;
+    std::vector<blk::DiagRef> dgs;
     for (int t = 0; t < nt; ++t) {
-      if ((int)babies[t].size() != G) throw ckks::Error(CKKS_EARG, "terms over different groups");
-      dgs.push_back(&diagonals(ids[t], limbs));
+      const Diag& dg = diagonals(ids[t], limbs);
+      dgs.push_back({dg.data, dg.limbs, dg.scale});
       count["matrix_products"] += G;
       count["ct_plain"] += (long)G * s.n1 * s.n2;
     }
-    std::vector<int> gk(s.n2);
-    for (int g = 0; g < s.n2; ++g) gk[g] = s.B * s.n1 * g;
-    for (int q0 = 0; q0 < G; q0 += blk::kMaxGroups) {
-      const int ng = std::min(blk::kMaxGroups, G - q0);
-      blk::InnerPtrs ip{};
-      std::vector<std::vector<Ciphertext>> inner(ng, std::vector<Ciphertext>(s.n2));
-      for (int q = 0; q < ng; ++q) {
-        const double sc = babies[0][q0 + q][0]->scale() * dgs[0]->scale;
-        for (int t = 1; t < nt; ++t) {
-          const double st_ = babies[t][q0 + q][0]->scale() * dgs[t]->scale;
-          if (std::fabs(st_ - sc) > 1e-9 * sc) throw ckks::Error(CKKS_ESCALE, "product terms at different scales");
-        }
-        for (int g = 0; g < s.n2; ++g) {
-          inner[q][g] = cc.fresh();
-          ckks::DevPoly& p = inner[q][g]->handle()->p;
-          p.ensure(&C, 2, limbs);
-          p.limbs = limbs;
-          p.scale = sc;
-          p.deg = babies[0][q0 + q][0]->noise_deg() + 1;
-          ip.c0[q][g] = p.data;
-          ip.c1[q][g] = p.data + (size_t)p.cap * C.N;
-        }
-      }
-      for (int t = 0; t < nt; ++t) {
-        blk::BabyPtrs bp{};
-        for (int q = 0; q < ng; ++q) {
-          const auto& baby = babies[t][q0 + q];
-          for (int j = 0; j < s.n1; ++j) {
-            const ckks::DevPoly& p = baby[j]->handle()->p;
-            if (p.limbs != limbs) throw ckks::Error(CKKS_ELEVEL, "baby steps at different levels");
-            bp.c0[q][j] = p.data;
-            bp.c1[q][j] = p.data + (size_t)p.cap * C.N;
-          }
-        }
-        const Diag& dg = *dgs[t];
-        const bool acc = t > 0;
-        ckks::ProfScope ps(
-            C, "bsgs_inner",
-            ((double)s.n1 * s.n2 * limbs + ng * (2.0 * s.n1 * limbs + (acc ? 4.0 : 2.0) * s.n2 * limbs)) *
-                C.limb_bytes(),
-            C.stream);
-        // runs of limbs with primes below kFpPrime take the float64
-        // products, the others (the 60-bit first prime) the integer ones
-        for (int l0 = 0; l0 < limbs;) {
-          const bool fp = C.moduli[l0] < blk::kFpPrime;
-          int l1 = l0 + 1;
-          while (l1 < limbs && (C.moduli[l1] < blk::kFpPrime) == fp) ++l1;
-          const dim3 grid(s.n2, C.N / blk::kThreads, l1 - l0);
-          if (s.n1 == 32 || s.n1 == 16 || s.n1 == 8) {
-            static_assert(blk::kThreads % blk::kBsgsRegCoeffs == 0, "a tile of whole CTAs");
-            const dim3 rgrid(ng * (blk::kThreads / blk::kBsgsRegCoeffs), C.N / blk::kThreads, l1 - l0);
-            auto kern = fp ? (s.n1 == 32   ? blk::bsgs_inner_reg_kernel<32>
-                              : s.n1 == 16 ? blk::bsgs_inner_reg_kernel<16>
-                                           : blk::bsgs_inner_reg_kernel<8>)
-                           : (s.n1 == 32   ? blk::bsgs_inner_reg_int_kernel<32>
-                              : s.n1 == 16 ? blk::bsgs_inner_reg_int_kernel<16>
-                                           : blk::bsgs_inner_reg_int_kernel<8>);
-            kern<<<rgrid, blk::kBsgsRegThreads, 0, C.stream>>>(bp, ng, dg.data, ip, C.logN, s.n2, l0, acc,
-                                                               C.d_mods);
-          } else if (fp) {
-            blk::bsgs_inner_fp_kernel<<<grid, dim3(blk::kBsgsThreads, ng), 0, C.stream>>>(
-                bp, ng, s.n1, dg.data, ip, limbs, C.logN, s.n2, l0, acc, C.d_mods);
-          } else {
-            blk::bsgs_inner_kernel<<<grid, dim3(blk::kBsgsThreads, ng), 0, C.stream>>>(
-                bp, ng, s.n1, dg.data, ip, limbs, C.logN, s.n2, l0, acc, C.d_mods);
-          }
-          l0 = l1;
-        }
-        CKKS_CUDA(cudaGetLastError());
-      }
-      // giant steps: sum_g rot(inner_g, B n1 g), the key switches summed in the
-      // extended basis with one ModDown (g = 0 is the identity); the groups'
-      // sums share launches and each giant-step key is read once for them
-      count["rotations"] += (long)ng * (s.n2 - 1);
-      const auto sums = cc.RescaleBatch(cc.EvalRotateSumGroups(inner, gk));
-      for (int q = 0; q < ng; ++q) outs[q0 + q] = sums[q];
-    }
-    return outs;
+    count["rotations"] += (long)G * (s.n2 - 1);
+    return blk::bsgs_products(cc, C, babies, dgs, s.n1, s.n2, s.B);
   }
   Ciphertext bsgs(const std::vector<Ciphertext>& baby, int id) { return bsgs_groups({baby}, id)[0]; }
 
@@ -1998,6 +2055,153 @@ int ckks_schedule_diagonal(const double* W, int out_dim, int in_dim, int ld, int
     for (int t = 0; t < batch; ++t) out_slots[(size_t)f * batch + t] = v;
   }
   return CKKS_OK;
+}
+
+}  // extern "C"
+
+// ---- fused BSGS product and lane shift as entry points ---------------------
+namespace {
+// the caller's handle, viewed without taking ownership
+Ciphertext view(ckks_ctx* ctx, const ckks_ct* h) {
+  if (!h) throw ckks::Error(CKKS_EARG, "null ciphertext");
+  if (h->owner != ctx) throw ckks::Error(CKKS_EARG, "ciphertext belongs to another context");
+  if (!h->p.data || h->p.limbs <= 0) throw ckks::Error(CKKS_ESTATE, "ciphertext holds no data");
+  return std::make_shared<ckks_b200::CiphertextImpl>(ctx, const_cast<ckks_ct*>(h));
+}
+// moves a computed ciphertext into the caller's output handle
+void move_into(ckks_ctx* ctx, ckks_ct* dst, const Ciphertext& src) {
+  if (!dst || dst->owner != ctx) throw ckks::Error(CKKS_EARG, "bad output handle");
+  ckks::DevPoly& a = dst->p;
+  ckks::DevPoly& b = src->handle()->p;
+  std::swap(a.ctx, b.ctx);
+  std::swap(a.data, b.data);
+  std::swap(a.npolys, b.npolys);
+  std::swap(a.cap, b.cap);
+  std::swap(a.limbs, b.limbs);
+  std::swap(a.scale, b.scale);
+  std::swap(a.deg, b.deg);
+}
+}  // namespace
+
+extern "C" {
+
+int ckks_bsgs_diagonals_create(ckks_ctx* ctx, const double* W, int out_dim, int in_dim, int ld, int batch, int n1,
+                               int limbs, ckks_diag** out) {
+  return bguard([&] {
+    if (!ctx || !ctx->c || !W || !out) throw ckks::Error(CKKS_EARG, "null argument");
+    ckks::Context& C = *ctx->c;
+    if (batch <= 0 || (batch & (batch - 1)) || 2 * batch > C.N)
+      throw ckks::Error(CKKS_EARG, "batch must be a power of two dividing N/2");
+    const int PW = C.N / 2 / batch;
+    if (n1 <= 0 || n1 > blk::kMaxBaby || PW % n1 || PW / n1 > blk::kMaxBaby)
+      throw ckks::Error(CKKS_EARG, "n1 must divide the pack width with n1, n2 <= 32");
+    if (C.N < blk::kThreads) throw ckks::Error(CKKS_EARG, "ring too small for the tiled diagonal store");
+    if (out_dim <= 0 || in_dim <= 0 || out_dim > PW || in_dim > PW || ld < in_dim)
+      throw ckks::Error(CKKS_EARG, "matrix does not fit the pack width");
+    if (limbs <= 0 || limbs > C.L) throw ckks::Error(CKKS_ELEVEL, "limb count outside the chain");
+    const size_t words = (size_t)(out_dim - 1) * ld + in_dim;
+    double* dW = (double*)C.alloc(sizeof(double) * words);
+    CKKS_CUDA(cudaMemcpyAsync(dW, W, sizeof(double) * words, cudaMemcpyHostToDevice, C.stream));
+    auto* d = new ckks_diag;
+    d->owner = ctx;
+    d->limbs = limbs;
+    d->n1 = n1;
+    d->n2 = PW / n1;
+    d->batch = batch;
+    d->scale = C.scales[limbs];
+    try {
+      d->data = blk::encode_diagonals(C, dW, out_dim, in_dim, ld, PW, batch, n1, d->n2, limbs, d->scale);
+    } catch (...) {
+      C.release(dW);
+      delete d;
+      throw;
+    }
+    C.release(dW);
+    {
+      std::lock_guard<std::mutex> lk(ctx->mu);
+      ctx->diags.insert(d);
+    }
+    *out = d;
+  });
+}
+
+int ckks_bsgs_diagonals_destroy(ckks_diag* d) {
+  return bguard([&] {
+    if (!d) return;
+    if (d->owner) {
+      std::lock_guard<std::mutex> lk(d->owner->mu);
+      d->owner->diags.erase(d);
+      if (d->data) d->owner->c->release(d->data);
+    }
+    delete d;
+  });
+}
+
+int ckks_bsgs_matmul(ckks_ctx* ctx, const ckks_diag* const* diags, int terms, const ckks_ct* const* baby, int groups,
+                     ckks_ct* const* outs) {
+  return bguard([&] {
+    if (!ctx || !ctx->c || !diags || !baby || !outs) throw ckks::Error(CKKS_EARG, "null argument");
+    if (terms <= 0 || groups <= 0) throw ckks::Error(CKKS_EARG, "terms and groups must be positive");
+    ckks::Context& C = *ctx->c;
+    const ckks_diag* d0 = diags[0];
+    std::vector<blk::DiagRef> dgs;
+    for (int t = 0; t < terms; ++t) {
+      const ckks_diag* d = diags[t];
+      if (!d || d->owner != ctx || !d->data) throw ckks::Error(CKKS_EARG, "diagonals of another context or released");
+      if (d->n1 != d0->n1 || d->batch != d0->batch || d->limbs != d0->limbs)
+        throw ckks::Error(CKKS_EARG, "diagonal sets differ in shape or level");
+      dgs.push_back({d->data, d->limbs, d->scale});
+    }
+    const int n1 = d0->n1;
+    std::vector<std::vector<std::vector<Ciphertext>>> bb(terms, std::vector<std::vector<Ciphertext>>(groups));
+    for (int t = 0; t < terms; ++t)
+      for (int q = 0; q < groups; ++q)
+        for (int j = 0; j < n1; ++j) {
+          const ckks_ct* h = baby[((size_t)t * groups + q) * n1 + j];
+          Ciphertext x = view(ctx, h);
+          if (h->p.limbs != d0->limbs) throw ckks::Error(CKKS_ELEVEL, "baby step not at the diagonals' level");
+          if (h->p.deg != 1) throw ckks::Error(CKKS_ESTATE, "baby steps must be rescaled (noise degree 1)");
+          bb[t][q].push_back(std::move(x));
+        }
+    for (int q = 0; q < groups; ++q)
+      if (!outs[q] || outs[q]->owner != ctx) throw ckks::Error(CKKS_EARG, "bad output handle");
+    ckks_b200::CryptoContextImpl cc(ctx);
+    const auto r = blk::bsgs_products(cc, C, bb, dgs, n1, d0->n2, d0->batch);
+    for (int q = 0; q < groups; ++q) move_into(ctx, outs[q], r[q]);
+  });
+}
+
+int ckks_lane_shift(ckks_ctx* ctx, const ckks_ct* const* in, int count, const int* deltas, int nd, int batch,
+                    ckks_ct* const* outs) {
+  return bguard([&] {
+    if (!ctx || !ctx->c || !in || !deltas || !outs) throw ckks::Error(CKKS_EARG, "null argument");
+    if (count <= 0 || nd <= 0) throw ckks::Error(CKKS_EARG, "count and nd must be positive");
+    ckks::Context& C = *ctx->c;
+    if (batch <= 1 || (batch & (batch - 1)) || 2 * batch > C.N)
+      throw ckks::Error(CKKS_EARG, "batch must be a power of two dividing N/2");
+    std::vector<int> ds(deltas, deltas + nd);
+    std::vector<Ciphertext> xs;
+    for (int i = 0; i < count; ++i) {
+      Ciphertext x = view(ctx, in[i]);
+      if (x->noise_deg() != 1) throw ckks::Error(CKKS_ESTATE, "lane shift input must be rescaled (noise degree 1)");
+      if (x->limbs() < 2) throw ckks::Error(CKKS_ELEVEL, "lane shift needs two limbs (it rescales)");
+      xs.push_back(std::move(x));
+    }
+    for (int i = 0; i < count * nd; ++i)
+      if (!outs[i] || outs[i]->owner != ctx) throw ckks::Error(CKKS_EARG, "bad output handle");
+    ckks_b200::CryptoContextImpl cc(ctx);
+    const int PW = C.N / 2 / batch;
+    std::map<std::pair<int, bool>, Plaintext> cache;
+    const blk::LaneMask mask = [&](int d, bool lower, int limbs) {
+      auto key = std::make_pair(d, lower);
+      auto it = cache.find(key);
+      if (it != cache.end()) return it->second;
+      return cache[key] = cc.MakePlaintextAt(blk::lane_mask_values(PW, batch, d, lower), limbs, C.scales[limbs]);
+    };
+    const auto r = blk::lane_shift_set(cc, xs, ds, batch, mask);
+    for (int i = 0; i < count; ++i)
+      for (int k = 0; k < nd; ++k) move_into(ctx, outs[(size_t)i * nd + k], r[i][k]);
+  });
 }
 
 }  // extern "C"

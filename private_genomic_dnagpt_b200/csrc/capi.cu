@@ -603,8 +603,14 @@ int ckks_ctx_destroy(ckks_ctx* ctx) {
         t->p.ctx = nullptr;
         t->owner = nullptr;
       }
+      for (ckks_diag* d : ctx->diags) {
+        if (d->data) ctx->c->release(d->data);
+        d->data = nullptr;
+        d->owner = nullptr;
+      }
       ctx->cts.clear();
       ctx->pts.clear();
+      ctx->diags.clear();
       for (ckks_block* b : ctx->blocks) ckks::block_orphan(b);
       ctx->blocks.clear();
     }

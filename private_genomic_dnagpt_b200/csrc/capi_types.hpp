@@ -16,6 +16,7 @@ void set_last_error(const std::string& msg);
 struct ckks_ct;
 struct ckks_pt;
 struct ckks_block;
+struct ckks_diag;
 
 // Objects register with their context.  Destroying a context first frees the
 // device memory of every object still alive and marks it orphaned, so that
@@ -27,6 +28,7 @@ struct ckks_ctx {
   std::unordered_set<ckks_ct*> cts;
   std::unordered_set<ckks_pt*> pts;
   std::unordered_set<ckks_block*> blocks;
+  std::unordered_set<ckks_diag*> diags;
 };
 struct ckks_ct {
   ckks_ctx* owner = nullptr;
@@ -35,6 +37,16 @@ struct ckks_ct {
 struct ckks_pt {
   ckks_ctx* owner = nullptr;
   ckks::DevPoly p;
+};
+// the encoded BSGS diagonals of one matrix at one level (the reference's
+// cached_diagonal_plains): n1 * n2 plaintexts of `limbs` limbs in the
+// tile-major layout the inner-sum kernels stream, from the context's
+// allocator
+struct ckks_diag {
+  ckks_ctx* owner = nullptr;
+  uint64_t* data = nullptr;
+  int limbs = 0, n1 = 0, n2 = 0, batch = 0;
+  double scale = 0.0;
 };
 
 namespace ckks {

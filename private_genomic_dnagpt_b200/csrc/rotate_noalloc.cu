@@ -64,24 +64,32 @@ extern "C" int ckks_rotate_noalloc(ckks_ctx* ctx, const uint64_t* in_dev, int li
     ckks::Context& c = *ctx->c;
     if (!in_dev || !out_dev) throw ckks::Error(CKKS_EARG, "null device buffer");
     if (limbs < 1 || limbs > c.L) throw ckks::Error(CKKS_EARG, "limb count outside 1..L");
+    // the scratch address and the context's stream belong to the context's
+    // device: launching from another current device would hand its kernels
+    // the wrong GPU's array
+    int cur = -1;
+    CKKS_CUDA(cudaGetDevice(&cur));
+    if (cur != c.params.device)
+      throw ckks::Error(CKKS_EARG, "current device " + std::to_string(cur) + " is not the context's device " +
+                                       std::to_string(c.params.device));
     const size_t N = (size_t)c.N, S = (size_t)limbs * N, E = (size_t)limbs + c.Kx(limbs);
+    const uint64_t *lo_in = in_dev, *hi_in = in_dev + 2 * S;
+    const uint64_t *lo_out = out_dev, *hi_out = out_dev + 2 * S;
+    if (lo_in < hi_out && lo_out < hi_in) throw ckks::Error(CKKS_EARG, "output overlaps input");
+    const uint32_t g = c.galois(k);
+    if (g == 1u) {  // the identity is a copy and needs no scratch
+      CKKS_CUDA(cudaMemcpyAsync(out_dev, in_dev, sizeof(uint64_t) * 2 * S, cudaMemcpyDeviceToDevice, c.stream));
+      return CKKS_OK;
+    }
     const size_t beta = (size_t)c.lt(limbs).beta;
     const size_t need = (beta * E + 2 * E + 2 * (size_t)limbs) * N;
     if (need > kScratchWords)
       throw ckks::Error(CKKS_ECAPACITY, "rotation needs " + std::to_string(need * 8 >> 20) +
                                             " MiB of scratch; the fixed no-allocation array holds " +
                                             std::to_string(kScratchBytes >> 20) + " MiB");
-    const uint64_t *lo_in = in_dev, *hi_in = in_dev + 2 * S;
-    const uint64_t *lo_out = out_dev, *hi_out = out_dev + 2 * S;
-    if (lo_in < hi_out && lo_out < hi_in) throw ckks::Error(CKKS_EARG, "output overlaps input");
-    const uint32_t g = c.galois(k);
-    const uint64_t* key = g == 1u ? nullptr : c.switch_key(g, limbs);
-    if (g != 1u && !key) throw ckks::Error(CKKS_EKEY, "rotation key not generated for index " + std::to_string(k));
+    const uint64_t* key = c.switch_key(g, limbs);
+    if (!key) throw ckks::Error(CKKS_EKEY, "rotation key not generated for index " + std::to_string(k));
     uint64_t* scratch = scratch_on(c.params.device);
-    if (g == 1u) {
-      CKKS_CUDA(cudaMemcpyAsync(out_dev, in_dev, sizeof(uint64_t) * 2 * S, cudaMemcpyDeviceToDevice, c.stream));
-      return CKKS_OK;
-    }
     uint64_t* ext = scratch;                // beta * E limbs
     uint64_t* acc = ext + beta * E * N;     // 2 E limbs
     uint64_t* tmp = acc + 2 * E * N;        // limbs (ModUp copy), then 2 limbs (ModDown conversion)

@@ -37,11 +37,14 @@ def test_noalloc_rotation_matches_allocating_rotation_twice(dnum, levels):
         ct = cc.drop_limbs(cc.Encrypt(cc.MakeCKKSPackedPlaintext(x)), limbs)
         src = ct.limbs_array()
         d_in = _device_copy(src)
-        for k in ks:  # two calls in a row through the shared array
+        for i, k in enumerate(ks):  # two calls in a row through the shared array
             d_out = torch.zeros_like(d_in)
             torch.cuda.synchronize()
+            free0 = torch.cuda.mem_get_info()[0]
             eng._check(eng.lib().ckks_rotate_noalloc(cc.h, d_in.data_ptr(), limbs, k, d_out.data_ptr()))
             cc.Synchronize()
+            if i > 0:  # after the first call's address lookup, no device memory is taken
+                assert torch.cuda.mem_get_info()[0] == free0
             got = d_out.cpu().numpy().view(np.uint64).reshape(src.shape)
             ref = cc.EvalRotate(ct, k).limbs_array()
             assert np.array_equal(got, ref)
@@ -64,6 +67,11 @@ def test_noalloc_refuses_oversized_and_overlapping_requests():
         out = torch.zeros_like(d)
         eng._check(eng.lib().ckks_rotate_noalloc(cc.h, d.data_ptr(), 8, 5, out.data_ptr()))
     assert e.value.code == 4
+    # the identity is a copy: it needs no key and no scratch
+    out = torch.zeros_like(d)
+    eng._check(eng.lib().ckks_rotate_noalloc(cc.h, d.data_ptr(), 8, 0, out.data_ptr()))
+    cc.Synchronize()
+    assert torch.equal(out, d)
     # N = 2^17 with 24 limbs needs ~208 MiB of temporaries: above the fixed array
     big = eng.GenCryptoContext(eng.CCParams(ring_dim_log=17, limbs=24, dnum=3, seed=31))
     buf = torch.zeros(2 * 24 * (1 << 17), dtype=torch.int64, device="cuda")
