@@ -1,6 +1,6 @@
 """Generates the golden fixtures in this directory from the reference's own
-Python modules (run in a container that has the reference tree at
-/root/reference; the fixtures are committed, the tree is not needed later).
+Python modules: run with DNAGPT_REFERENCE_TREE naming the reference tree
+(the fixtures are committed; the tree is not needed later).
 
   plain_block_t8.npz  fhe/realweights/manual.py block_reference on the seeded
                       synthetic block (seed 3, T = 8) -- pins oracle/plain_block.py
@@ -28,7 +28,9 @@ import numpy as np
 
 HERE = os.path.dirname(os.path.abspath(__file__))
 ROOT = os.path.dirname(os.path.dirname(HERE))
-REF = "/root/reference"
+REF = os.environ.get("DNAGPT_REFERENCE_TREE", "")
+if not REF or not os.path.isdir(REF):
+    sys.exit("set DNAGPT_REFERENCE_TREE to the reference tree (fhe/ lies under it)")
 sys.path.insert(0, ROOT)
 sys.path.insert(0, os.path.join(REF, "fhe", "gpu_real_scheme_b"))
 sys.path.insert(0, os.path.join(REF, "fhe", "realweights"))

@@ -61,3 +61,30 @@ def test_two_chained_blocks_and_head(ctx):
         assert abs(m - m_ref) <= _margin_tol(hw, m_ref)
     assert model.blocks[0].report()["counts"]["diagonal_cache_mib"] > 0
     assert model.blocks[1].report()["counts"]["diagonal_cache_mib"] == 0
+
+
+def test_four_chained_blocks_past_the_cache_budget(ctx):
+    """Three of four blocks lie past the diagonal-cache budget: they encode
+    their diagonals inside every forward and release them after it (the
+    12-block model's path for the blocks that do not fit beside the keys)."""
+    tokens = 40
+    ws = [plain_block.synthetic_weights(41 + b) for b in range(4)]
+    hw = plain_block.synthetic_head_weights(45)
+    x = plain_block.synthetic_input(46, tokens)
+    model = eng.EncryptedModel(ctx, ws, hw, tokens, cached_blocks=1)
+    ctx.EvalRotateKeyGen(model.rotation_indices())
+    h_ref, m_ref = plain_block.model(x, ws, hw)
+    for step in range(2):
+        h, m = model.forward(x)
+        err = plain_block.rel_inf(h_ref, h)
+        print(f"four blocks, pass {step}: hidden rel_inf {err:.3e} margin {m:.9f} plaintext {m_ref:.9f}")
+        assert np.isfinite(h).all() and err < 1e-6
+        assert abs(m - m_ref) <= _margin_tol(hw, m_ref)
+        for b, blk in enumerate(model.blocks):
+            c = blk.report()["counts"]
+            if b == 0:
+                assert c["diagonal_cache_mib"] > 0
+                assert c.get("diagonal_cache_misses", 0) == (10 if step == 0 else 0)
+            else:  # re-encoded on every pass, released after it
+                assert c["diagonal_cache_mib"] == 0
+                assert c["diagonal_cache_misses"] == 10
