@@ -94,17 +94,34 @@ __device__ __forceinline__ void gs_bfly(uint64_t& x, uint64_t& y, ulonglong2 w, 
   y = mul_shoup_lazy(d, w.x, w.y, q);
 }
 
-template <int S_LOG, bool INV, bool STRIDED, int R_LOG>
-__device__ __forceinline__ void ntt_pass_body(uint64_t* __restrict__ data, const PassArgs& a, uint64_t* sm) {
+// Position of residue r of sub-transform `sub` inside a limb: strided
+// sub-transforms are columns (r at stride N / S), contiguous ones blocks.
+template <int S_LOG, bool STRIDED>
+__device__ __forceinline__ size_t pass_gaddr(int logN, int sub, int r) {
+  return STRIDED ? ((size_t)r << (logN - S_LOG)) + sub : ((size_t)sub << S_LOG) + r;
+}
+// Shared-memory slot of residue r of local sub-transform `lane` (the layout
+// of the exchanges inside a pass and of the contiguous pass's staged side)
+template <int S_LOG, bool STRIDED, int R_LOG>
+__device__ __forceinline__ int pass_saddr(int per, int lane, int r) {
+  return STRIDED ? r * per + lane : (lane << S_LOG) + (r ^ swizzle<R_LOG>(r));
+}
+
+// One pass: S-point sub-transforms of one limb, `per` of them per CTA
+// starting at sub-transform sub_base.  load0(sub, lane, r) returns residue r
+// of sub-transform sub (local index lane) as the pass starts;
+// store_last(sub, lane, r, v) takes it as the pass ends, after every thread
+// has called pre_store() once.
+template <int S_LOG, bool INV, bool STRIDED, int R_LOG, class Load0, class StoreLast, class PreStore>
+__device__ __forceinline__ void ntt_pass_body(const PassArgs& a, uint64_t* sm, int limb, int sub_base, Load0 load0,
+                                              StoreLast store_last, PreStore pre_store) {
   constexpr int S = 1 << S_LOG;
   constexpr int R = 1 << R_LOG;                // residues per thread
   constexpr int T = S >= R ? S / R : 1;        // threads per sub-transform
   constexpr int NG = (S_LOG + R_LOG - 1) / R_LOG;  // register stage groups
 
-  const int limb = blockIdx.y;
   const int prime = a.map.prime(limb);
   const int N = 1 << a.logN;
-  uint64_t* poly = data + (size_t)limb * N;
   const uint64_t q = a.mods[prime].q;
   const uint64_t q2 = 2 * q;
   const ulonglong2* tw = a.tw + (size_t)prime * N;
@@ -119,22 +136,16 @@ __device__ __forceinline__ void ntt_pass_body(uint64_t* __restrict__ data, const
     lane_idx = tid / T;
     sub_t = tid % T;
   }
-  const int sub_global = blockIdx.x * per + lane_idx;  // column or block index
-  const int stride = N >> S_LOG;                         // strided: distance between rows
+  const int sub_global = sub_base + lane_idx;  // column or block index
   const int gs0 = STRIDED ? 0 : (a.logN - S_LOG);
   const uint32_t prefix = STRIDED ? 0u : (uint32_t)sub_global;
   // the strided pass holds the first stages (forward) / the last stages
   // (inverse); the contiguous pass the others
   const bool first_pass = (STRIDED != INV);
   const bool last_pass = !first_pass;
-  const uint64_t* in = pass_input(a, poly, limb, first_pass);
+  (void)N;
 
-  auto gaddr = [&](int r) -> size_t {
-    return STRIDED ? (size_t)r * stride + sub_global : (size_t)sub_global * S + r;
-  };
-  auto saddr = [&](int r) -> int {
-    return STRIDED ? r * per + lane_idx : lane_idx * S + (r ^ swizzle<R_LOG>(r));
-  };
+  auto saddr = [&](int r) -> int { return pass_saddr<S_LOG, STRIDED, R_LOG>(per, lane_idx, r); };
 
   uint64_t x[R];
 
@@ -153,12 +164,7 @@ __device__ __forceinline__ void ntt_pass_body(uint64_t* __restrict__ data, const
       const int uj = j / usz, k = j % usz;
       const int u = sub_t + uj * T;
       const int r = (u / D) * (D << G) + (u % D) + k * D;
-      if (step > 0) {
-        x[j] = sm[saddr(r)];
-      } else {
-        x[j] = in[gaddr(r)];
-        if (first_pass && a.has_src && a.src.reduce) x[j] = reduce128(U128{x[j], 0}, a.mods[prime]);
-      }
+      x[j] = step > 0 ? sm[saddr(r)] : load0(sub_global, lane_idx, r);
     }
     // butterflies; the twiddle of pair (k, k+h) at stage st0+rr is
     // tw[2^(gs0+st) + prefix*2^st + B*2^rr + (k >> (G-rr))], B = u / D
@@ -216,6 +222,7 @@ __device__ __forceinline__ void ntt_pass_body(uint64_t* __restrict__ data, const
       }
       __syncthreads();
     } else {
+      pre_store();
 #pragma unroll
       for (int j = 0; j < R; ++j) {
         if (j >= units_per_thread * usz) break;
@@ -227,7 +234,7 @@ __device__ __forceinline__ void ntt_pass_body(uint64_t* __restrict__ data, const
           v = v >= q ? v - q : v;
         }
         // inverse output of the final stage is already canonical
-        poly[gaddr((u / D) * (D << G) + (u % D) + k * D)] = v;
+        store_last(sub_global, lane_idx, (u / D) * (D << G) + (u % D) + k * D, v);
       }
     }
   }
@@ -270,17 +277,16 @@ __device__ __forceinline__ uint64_t fp_to_residue(double x, double q) {
   return __double2ull_rn(x < 0.0 ? __dadd_rn(x, q) : x);
 }
 
-template <int S_LOG, bool INV, bool STRIDED, int R_LOG>
-__device__ __forceinline__ void ntt_pass_body_fp(uint64_t* __restrict__ data, const PassArgs& a, uint64_t* sm) {
+template <int S_LOG, bool INV, bool STRIDED, int R_LOG, class Load0, class StoreLast, class PreStore>
+__device__ __forceinline__ void ntt_pass_body_fp(const PassArgs& a, uint64_t* sm, int limb, int sub_base,
+                                                 Load0 load0, StoreLast store_last, PreStore pre_store) {
   constexpr int S = 1 << S_LOG;
   constexpr int R = 1 << R_LOG;
   constexpr int T = S >= R ? S / R : 1;
   constexpr int NG = (S_LOG + R_LOG - 1) / R_LOG;
 
-  const int limb = blockIdx.y;
   const int prime = a.map.prime(limb);
   const int N = 1 << a.logN;
-  uint64_t* poly = data + (size_t)limb * N;
   const uint64_t qi = a.mods[prime].q;
   const double q = (double)qi, qinv = 1.0 / q;
   const double2* tw = a.twd + (size_t)prime * N;
@@ -295,19 +301,12 @@ __device__ __forceinline__ void ntt_pass_body_fp(uint64_t* __restrict__ data, co
     lane_idx = tid / T;
     sub_t = tid % T;
   }
-  const int sub_global = blockIdx.x * per + lane_idx;
-  const int stride = N >> S_LOG;
+  const int sub_global = sub_base + lane_idx;
   const int gs0 = STRIDED ? 0 : (a.logN - S_LOG);
   const uint32_t prefix = STRIDED ? 0u : (uint32_t)sub_global;
   const bool first_pass = (STRIDED != INV);
-  const uint64_t* in = pass_input(a, poly, limb, first_pass);
 
-  auto gaddr = [&](int r) -> size_t {
-    return STRIDED ? (size_t)r * stride + sub_global : (size_t)sub_global * S + r;
-  };
-  auto saddr = [&](int r) -> int {
-    return STRIDED ? r * per + lane_idx : lane_idx * S + (r ^ swizzle<R_LOG>(r));
-  };
+  auto saddr = [&](int r) -> int { return pass_saddr<S_LOG, STRIDED, R_LOG>(per, lane_idx, r); };
 
   double x[R];
 
@@ -330,11 +329,9 @@ __device__ __forceinline__ void ntt_pass_body_fp(uint64_t* __restrict__ data, co
       if (step > 0) {
         x[j] = __longlong_as_double((long long)sm[saddr(r)]);
       } else if (first_pass) {
-        uint64_t v = in[gaddr(r)];
-        if (a.has_src && a.src.reduce) v = reduce128(U128{v, 0}, a.mods[prime]);
-        x[j] = fp_center(__ull2double_rn(v), q, qinv);
+        x[j] = fp_center(__ull2double_rn(load0(sub_global, lane_idx, r)), q, qinv);
       } else {
-        x[j] = __longlong_as_double((long long)poly[gaddr(r)]);
+        x[j] = __longlong_as_double((long long)load0(sub_global, lane_idx, r));
       }
     }
     bool final_done = false;
@@ -410,6 +407,7 @@ __device__ __forceinline__ void ntt_pass_body_fp(uint64_t* __restrict__ data, co
       }
       __syncthreads();
     } else {
+      pre_store();
 #pragma unroll
       for (int j = 0; j < R; ++j) {
         if (j >= units_per_thread * usz) break;
@@ -422,7 +420,7 @@ __device__ __forceinline__ void ntt_pass_body_fp(uint64_t* __restrict__ data, co
           const double c = fp_center(x[j], q, qinv);
           v = first_pass ? (uint64_t)__double_as_longlong(c) : fp_to_residue(c, q);
         }
-        poly[gaddr((u / D) * (D << G) + (u % D) + k * D)] = v;
+        store_last(sub_global, lane_idx, (u / D) * (D << G) + (u % D) + k * D, v);
       }
     }
   }
@@ -434,11 +432,50 @@ __global__ void __launch_bounds__(PassShape<R_LOG>::kThreads, PassShape<R_LOG>::
   extern __shared__ uint64_t sm[];
   const int limb = blockIdx.y;
   if (a.map.skipped(limb)) return;
-  const uint64_t q = a.mods[a.map.prime(limb)].q;
-  if (q < kFpNttPrime)
-    ntt_pass_body_fp<S_LOG, INV, STRIDED, R_LOG>(data, a, sm);
+  const int prime = a.map.prime(limb);
+  const Mod m = a.mods[prime];
+  const int logN = a.logN;
+  uint64_t* poly = data + ((size_t)limb << logN);
+  const bool first_pass = (STRIDED != INV);
+  const uint64_t* in = pass_input(a, poly, limb, first_pass);
+  const bool reduce = first_pass && a.has_src && a.src.reduce;
+  const int per = a.per_cta;
+  const int sub_base = blockIdx.x * per;
+  // A contiguous pass's CTA owns per * S consecutive words.  The forward's
+  // output would leave a thread's registers at a 4-residue stride: it is
+  // re-laid in shared memory and written in coalesced 16-byte stores.  (The
+  // inverse's input, read at the same stride, gained nothing from staging:
+  // the sectors of one load serve the next three from L1.)
+  constexpr bool kStageOut = !STRIDED && !INV;
+  const int W = per << S_LOG;
+  const int nt = (int)blockDim.x;
+  auto load0 = [&](int sub, int, int r) -> uint64_t {
+    const uint64_t v = in[pass_gaddr<S_LOG, STRIDED>(logN, sub, r)];
+    return reduce ? reduce128(U128{v, 0}, m) : v;
+  };
+  auto store_last = [&](int sub, int lane, int r, uint64_t v) {
+    if (kStageOut)
+      sm[pass_saddr<S_LOG, false, R_LOG>(per, lane, r)] = v;
+    else
+      poly[pass_gaddr<S_LOG, STRIDED>(logN, sub, r)] = v;
+  };
+  // the last step read shared memory: wait before overwriting it
+  auto pre_store = [] {
+    if (kStageOut) __syncthreads();
+  };
+  if (m.q < kFpNttPrime)
+    ntt_pass_body_fp<S_LOG, INV, STRIDED, R_LOG>(a, sm, limb, sub_base, load0, store_last, pre_store);
   else
-    ntt_pass_body<S_LOG, INV, STRIDED, R_LOG>(data, a, sm);
+    ntt_pass_body<S_LOG, INV, STRIDED, R_LOG>(a, sm, limb, sub_base, load0, store_last, pre_store);
+  if (kStageOut) {
+    __syncthreads();
+    uint64_t* dst = poly + ((size_t)sub_base << S_LOG);
+    for (int i = 2 * (int)threadIdx.x; i < W; i += 2 * nt) {
+      const uint64_t x0 = sm[pass_saddr<S_LOG, false, R_LOG>(per, i >> S_LOG, i & ((1 << S_LOG) - 1))];
+      const uint64_t x1 = sm[pass_saddr<S_LOG, false, R_LOG>(per, (i + 1) >> S_LOG, (i + 1) & ((1 << S_LOG) - 1))];
+      *reinterpret_cast<ulonglong2*>(dst + i) = make_ulonglong2(x0, x1);
+    }
+  }
 }
 
 template <int S_LOG, bool INV, bool STRIDED>
