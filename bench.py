@@ -78,8 +78,8 @@ def measured_peaks():
 # on 23 of the 24 primes): ntt_fwd_rows is the strided pass, ntt_fwd_cols the
 # contiguous one; the pass traffic grows in proportion to the limbs it
 # transforms
-NCU_TRAFFIC_PER_LIMB = {"ntt_fwd_rows": (805.831680 + 761.594112) * 1e6 / 1536,
-                        "ntt_fwd_cols": (888.829696 + 753.165824) * 1e6 / 1536}
+NCU_TRAFFIC_PER_LIMB = {"ntt_fwd_rows": (805.841920 + 762.777088) * 1e6 / 1536,
+                        "ntt_fwd_cols": (918.904576 + 755.164160) * 1e6 / 1536}
 
 
 def keyswitch_bytes(limbs: int, K: int, alpha: int, N: int) -> float:
