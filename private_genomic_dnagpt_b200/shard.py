@@ -213,8 +213,23 @@ class ShardedBlock:
             dist.broadcast(buf, src=src)
             if self.rank == owner:
                 parts.append((buf, meta))
+        # the owner checks that the parts add up and tells every rank, so
+        # that a mismatch ends all ranks together instead of leaving the
+        # others in their next collective until the timeout
+        ok = torch.ones(1, dtype=torch.float64, device=self.device)
+        err = None
         if self.rank == owner:
-            ref = self._check_meta([m for _, m in parts])
+            try:
+                ref = self._check_meta([m for _, m in parts])
+            except RuntimeError as e:
+                err = e
+                ok.zero_()
+        dist.broadcast(ok, src=owner)
+        if err is not None:
+            raise err
+        if float(ok.cpu()[0]) == 0.0:
+            raise RuntimeError(f"partial MLP sums of group {g} do not match on rank {owner}")
+        if self.rank == owner:
             io.state_sum(KIND_MLP, g, [b for b, _ in parts], ref)
 
     def forward(self, x: np.ndarray) -> np.ndarray:

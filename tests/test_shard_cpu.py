@@ -254,3 +254,47 @@ def test_sharded_two_block_model_with_head(tmp_path, world):
         got = np.load(out + f".{r}.npy")
         assert np.abs(got[:-1] - h_ref.ravel()).max() <= 1e-12 * np.abs(h_ref).max()
         assert abs(got[-1] - m_ref) <= 1e-12 * max(1.0, abs(m_ref))
+
+
+class MismatchedIO(PlainIO):
+    """A helper whose partial MLP sum claims another scale than the owner's."""
+
+    def state_export(self, kind, g):
+        buf, meta = super().state_export(kind, g)
+        return buf, (meta[0], 2.0 if kind == shard.KIND_MLP else meta[1], meta[2])
+
+
+def _mismatch_rank(rank, world, port, tokens, out_path):
+    import datetime
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60))
+    try:
+        w = plain_block.synthetic_weights(3)
+        x = plain_block.synthetic_input(4, tokens)
+        plan = shard.shard_plan(tokens, B, world)
+        helper = any(len(shard.mlp_ranks(plan, g)) > 1 and rank in shard.mlp_ranks(plan, g)[1:]
+                     for g in range(-(-tokens // B)))
+        io = MismatchedIO(w, tokens) if helper else PlainIO(w, tokens)
+        sb = shard.ShardedBlock(io, tokens, B, 12, plain_block.D, dist, "cpu")
+        try:
+            sb.forward(x)
+            outcome = "finished"
+        except RuntimeError as e:
+            outcome = "raised" if "partial" in str(e) else f"other: {e}"
+        with open(out_path + f".{rank}", "w") as f:
+            f.write(outcome)
+    finally:
+        dist.destroy_process_group()
+
+
+def test_mismatched_partial_sums_end_every_rank(tmp_path):
+    """A partial MLP sum at another scale is found on its owner; every rank
+    raises at the same collective step (none waits for the timeout)."""
+    world, tokens = 5, 70
+    out = str(tmp_path / "o")
+    mp.start_processes(_mismatch_rank, args=(world, _free_port(), tokens, out), nprocs=world, join=True,
+                       start_method="spawn")
+    for r in range(world):
+        with open(out + f".{r}") as f:
+            assert f.read() == "raised", r
