@@ -236,14 +236,15 @@ def run_reference(args):
     world = int(os.environ.get("WORLD_SIZE", "1"))
     if rank != 0:
         return
+    sharded = world > 1 and not args.replicas
     threads = os.cpu_count() or 1
     total, times, err, ops, cores, workers = run_cpu_block(args.tokens, args.logn, threads, args.steps, args.warmup)
     sample = cpu_sample_text(args.tokens, args.logn, len(times), times, cores, workers)
     line = {
         "impl": "reference", "metric": arm_metric(args.tokens, args.logn), "value": total, "unit": UNIT,
         "n_gpus": world, "steps": len(times), "warmup": args.warmup, "ms_per_step": total / len(times) * 1e3,
-        "higher_is_better": False, "scaling": "weak", "vs_baseline": total / REF_A100_BLOCK_S, "dtype": "u64",
-        "data": "synthetic", "config": arm_config(world, args.tokens, args.logn, world > 1 and not args.replicas),
+        "higher_is_better": False, "scaling": "strong" if sharded else "weak", "vs_baseline": total / REF_A100_BLOCK_S,
+        "dtype": "u64", "data": "synthetic", "config": arm_config(world, args.tokens, args.logn, sharded),
         "cpu_baseline": {"value": total, "unit": UNIT, "cores": cores, "kind": "port", "sample": sample},
         "e2e": {"value": total, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
         "accuracy": {"rel_inf_vs_plaintext": err}, "slice_s": [round(t, 3) for t in times], "ops": ops,
@@ -263,6 +264,45 @@ def ntt_launch_sizes(prof: dict, logn: int) -> dict:
             cur[0] += n
             cur[1] = round(cur[1] + ms, 3)
     return {f"2^{k}": out[k] for k in sorted(out)}
+
+
+# (log N, limbs, dnum) points of the primitive sweep recorded beside the
+# block: the ring sizes at 24 limbs, the limb counts at N = 2^16, the digit
+# counts at 24 limbs
+SWEEP = [(15, 24, 3), (17, 24, 3), (16, 8, 3), (16, 16, 3), (16, 32, 3), (16, 24, 2), (16, 24, 4)]
+
+
+def keyswitch_point(eng, torch, logn: int, limbs: int, dnum: int, device: int, R: int = 32, steps: int = 3):
+    """EvalRotate over R ciphertexts at one (N, limbs, dnum): one ckks_rotate
+    call each (indices 1..512), event-timed on the engine stream."""
+    cc = eng.GenCryptoContext(eng.CCParams(ring_dim_log=logn, limbs=limbs, dnum=dnum, seed=3, device=device))
+    cc.KeyGen()
+    cc.EvalRotateKeyGen(ROT_INDICES)
+    stream = torch.cuda.ExternalStream(cc.stream_handle())
+    rng = np.random.default_rng(logn * 100 + limbs)
+    cts = [cc.Encrypt(cc.MakeCKKSPackedPlaintext(rng.uniform(-1, 1, cc.slots))) for _ in range(R)]
+    outs = [eng.Ciphertext(cc) for _ in range(R)]
+    lib = eng.lib()
+
+    def step():
+        for r in range(R):
+            eng._check(lib.ckks_rotate(cc.h, cts[r].h, ROT_INDICES[r % len(ROT_INDICES)], outs[r].h))
+
+    step()
+    cc.Synchronize()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(steps):
+        step()
+    e1.record(stream)
+    e1.synchronize()
+    per = e0.elapsed_time(e1) / 1e3 / (R * steps)
+    ks_b = keyswitch_bytes(limbs, cc.K, cc.alpha, cc.N)
+    peak, _ = measured_peaks()
+    return {"logN": logn, "limbs": limbs, "dnum": dnum, "us_per_rotation": round(per * 1e6, 2),
+            "EvalRotate/s": round(1.0 / per, 1), "GBps": round(ks_b / per / 1e9, 1),
+            "frac": round(ks_b / per / 1e9 / peak, 4)}
 
 
 def run_engine(args):
@@ -417,6 +457,9 @@ def run_engine(args):
     if roof is not None:
         # the metric's key-switch part (ks bytes = (l + 2 beta (l + K) + 2 l) limbs)
         roof["keyswitch"] = keyswitch
+        if rank == 0 and not args.no_sweep:
+            block.release_cache()  # room for the sweep's contexts
+            roof["keyswitch_sweep"] = [keyswitch_point(eng, torch, *pt, device=local) for pt in SWEEP]
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
@@ -513,7 +556,7 @@ def run_shard(args):
     assert err < 1e-6, f"sharded block output error {err}"
     cc.Synchronize()
     dist.barrier()
-    steps = []
+    steps, evals = [], []
     with ClockSampler(local) as clk:
         for _ in range(args.steps):
             e0 = torch.cuda.Event(enable_timing=True)
@@ -523,23 +566,27 @@ def run_shard(args):
             e1.record(stream)
             e1.synchronize()
             steps.append(e0.elapsed_time(e1) / 1e3)
+            # this rank's span from encrypted inputs resident to encrypted
+            # outputs resident (exchanges included)
+            evals.append(block.report()["seconds"]["evaluate_events"])
         cc.Synchronize()
         dist.barrier()
-    t = torch.tensor([float(np.mean(steps))], device="cuda", dtype=torch.float64)
+    t = torch.tensor([float(np.mean(evals)), float(np.mean(steps))], device="cuda", dtype=torch.float64)
     dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    value = float(t[0])
+    value, e2e = float(t[0]), float(t[1])
     if rank == 0:
         groups = -(-args.tokens // 32)
         line = {
             "metric": arm_metric(args.tokens, LOG_N), "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
-            "warmup": args.warmup, "ms_per_step": value * 1e3, "higher_is_better": False, "scaling": "strong",
+            "warmup": args.warmup, "ms_per_step": e2e * 1e3, "higher_is_better": False, "scaling": "strong",
             "vs_baseline": value / REF_A100_BLOCK_S, "dtype": "u64", "data": "synthetic",
             "config": arm_config(world, args.tokens, LOG_N, True),
             "accuracy": {"rel_inf_vs_plaintext": err},
             "shard": {"plan": [{"groups": rp.groups, "qkv": rp.qkv, "mlp": rp.mlp, "tiles": rp.tiles}
                                for rp in sb.plan],
                       "rank0_stage_s": {k: round(v, 4) for k, v in block.report().get("seconds", {}).items()}},
-            "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": groups * cc.slots * 8,
+            # the whole sharded call: host embeddings in, host outputs out
+            "e2e": {"value": e2e, "unit": UNIT, "h2d_bytes_per_step": groups * cc.slots * 8,
                     "d2h_bytes_per_step": groups * cc.slots * 8},
             "per_step_s": [round(v, 4) for v in steps],
             "clocks": clk.summary(),
@@ -739,6 +786,7 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--no-sweep", action="store_true")
     # a smaller token count only for profiler captures (the benchmark is 103)
     ap.add_argument("--tokens", type=int, default=TOKENS)
     # primitive-operation sweep instead of the block (one configuration per run)

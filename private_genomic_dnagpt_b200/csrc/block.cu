@@ -270,15 +270,14 @@ constexpr int kBsgsRegThreads = 128;
 constexpr int kBsgsSplit = 2;                                   // lanes per coefficient
 constexpr int kBsgsRegCoeffs = kBsgsRegThreads / kBsgsSplit;  // coefficients per CTA
 template <int NB>
-__global__ void __launch_bounds__(kBsgsRegThreads, NB >= 32 ? 3 : 4) bsgs_inner_reg_kernel(BabyPtrs babies, int ng,
-                                                                              const uint64_t* __restrict__ diag,
-                                                                              InnerPtrs out, int logN, int n2, int l0,
-                                                                              bool accumulate,
-                                                                              const ckks::Mod* __restrict__ mods) {
+__device__ __forceinline__ void bsgs_inner_reg_fp(const BabyPtrs& babies, int ng, const uint64_t* __restrict__ diag,
+                                                  const InnerPtrs& out, int logN, int n2, int l, bool accumulate,
+                                                  const ckks::Mod* __restrict__ mods,
+                                                  double (*sd)[NB / kBsgsSplit][kBsgsRegThreads]) {
   constexpr int H = NB / kBsgsSplit;  // babies per lane
   const int N = 1 << logN;
   const int q = blockIdx.x % ng, part = blockIdx.x / ng;
-  const int tile = blockIdx.y, l = l0 + blockIdx.z;
+  const int tile = blockIdx.y;
   const int half = threadIdx.x % kBsgsSplit;
   const int c = part * kBsgsRegCoeffs + threadIdx.x / kBsgsSplit;  // coefficient within the tile
   const size_t off = (size_t)l * N + (size_t)tile * kThreads + c;
@@ -294,7 +293,6 @@ __global__ void __launch_bounds__(kBsgsRegThreads, NB >= 32 ? 3 : 4) bsgs_inner_
   // the next giant step's diagonals stream into this thread's own
   // shared-memory slots while the current one is computed (cp.async, two
   // buffers; each thread reads only what it copied, so no barrier)
-  __shared__ double sd[2][H][kBsgsRegThreads];
   auto prefetch = [&](int g, int buf) {
     const double* dg = dt + (size_t)g * NB * kThreads;
 #pragma unroll
@@ -345,13 +343,14 @@ __global__ void __launch_bounds__(kBsgsRegThreads, NB >= 32 ? 3 : 4) bsgs_inner_
 // 128-bit multiply-accumulate chains, the lane pair's sums added as 128-bit
 // values (each below 2^124) and reduced once.
 template <int NB>
-__global__ void __launch_bounds__(kBsgsRegThreads, NB >= 32 ? 3 : 4) bsgs_inner_reg_int_kernel(
-    BabyPtrs babies, int ng, const uint64_t* __restrict__ diag, InnerPtrs out, int logN, int n2, int l0,
-    bool accumulate, const ckks::Mod* __restrict__ mods) {
+__device__ __forceinline__ void bsgs_inner_reg_int(const BabyPtrs& babies, int ng, const uint64_t* __restrict__ diag,
+                                                   const InnerPtrs& out, int logN, int n2, int l, bool accumulate,
+                                                   const ckks::Mod* __restrict__ mods,
+                                                   uint64_t (*sd)[NB / kBsgsSplit][kBsgsRegThreads]) {
   constexpr int H = NB / kBsgsSplit;
   const int N = 1 << logN;
   const int q = blockIdx.x % ng, part = blockIdx.x / ng;
-  const int tile = blockIdx.y, l = l0 + blockIdx.z;
+  const int tile = blockIdx.y;
   const int half = threadIdx.x % kBsgsSplit;
   const int c = part * kBsgsRegCoeffs + threadIdx.x / kBsgsSplit;
   const size_t off = (size_t)l * N + (size_t)tile * kThreads + c;
@@ -363,7 +362,6 @@ __global__ void __launch_bounds__(kBsgsRegThreads, NB >= 32 ? 3 : 4) bsgs_inner_
   }
   const uint64_t* dt =
       diag + ((size_t)l * (N / kThreads) + tile) * (size_t)(NB * n2) * kThreads + (size_t)half * H * kThreads + c;
-  __shared__ uint64_t sd[2][H][kBsgsRegThreads];
   auto prefetch = [&](int g, int buf) {
     const uint64_t* dg = dt + (size_t)g * NB * kThreads;
 #pragma unroll
@@ -402,6 +400,27 @@ __global__ void __launch_bounds__(kBsgsRegThreads, NB >= 32 ? 3 : 4) bsgs_inner_
       dst[off] = r;
     }
   }
+}
+
+// Inner sums over limbs l0 .. l0 + gridDim.z - 1 in one grid: each CTA takes
+// the float64 products when its limb's prime allows them and the 128-bit
+// integer chains otherwise, so the 60-bit first limb's CTAs (launched first,
+// about 2.7x the work of a float64 limb) run beside the others instead of in
+// a launch of their own, on the integer pipe while the others use FP64.
+template <int NB>
+__global__ void __launch_bounds__(kBsgsRegThreads, NB >= 32 ? 3 : 4) bsgs_inner_reg_kernel(BabyPtrs babies, int ng,
+                                                                              const uint64_t* __restrict__ diag,
+                                                                              InnerPtrs out, int logN, int n2, int l0,
+                                                                              bool accumulate,
+                                                                              const ckks::Mod* __restrict__ mods) {
+  constexpr int H = NB / kBsgsSplit;
+  __shared__ uint64_t sd[2][H][kBsgsRegThreads];
+  const int l = l0 + blockIdx.z;
+  if (mods[l].q < kFpPrime)
+    bsgs_inner_reg_fp<NB>(babies, ng, diag, out, logN, n2, l, accumulate, mods,
+                          reinterpret_cast<double (*)[H][kBsgsRegThreads]>(sd));
+  else
+    bsgs_inner_reg_int<NB>(babies, ng, diag, out, logN, n2, l, accumulate, mods, sd);
 }
 
 // ---- client-side float64 transforms, on the device ------------------------
@@ -630,24 +649,22 @@ std::vector<Ciphertext> bsgs_products(ckks_b200::CryptoContextImpl& cc, ckks::Co
           C, "bsgs_inner",
           ((double)n1 * n2 * limbs + ng * (2.0 * n1 * limbs + (acc ? 4.0 : 2.0) * n2 * limbs)) * C.limb_bytes(),
           C.stream);
-      // runs of limbs with primes below kFpPrime take the float64 products,
-      // the others (the 60-bit first prime) the integer ones
-      for (int l0 = 0; l0 < limbs;) {
+      if (n1 == 32 || n1 == 16 || n1 == 8) {
+        // every limb in one grid, each CTA on its limb's path
+        static_assert(kThreads % kBsgsRegCoeffs == 0, "a tile of whole CTAs");
+        const dim3 rgrid(ng * (kThreads / kBsgsRegCoeffs), C.N / kThreads, limbs);
+        auto kern = n1 == 32 ? bsgs_inner_reg_kernel<32> : n1 == 16 ? bsgs_inner_reg_kernel<16>
+                                                                    : bsgs_inner_reg_kernel<8>;
+        kern<<<rgrid, kBsgsRegThreads, 0, C.stream>>>(bp, ng, dg, ip, C.logN, n2, 0, acc, C.d_mods);
+      }
+      // generic n1: runs of limbs with primes below kFpPrime take the
+      // float64 products, the others (the 60-bit first prime) the integer ones
+      for (int l0 = 0; l0 < limbs && !(n1 == 32 || n1 == 16 || n1 == 8);) {
         const bool fp = C.moduli[l0] < kFpPrime;
         int l1 = l0 + 1;
         while (l1 < limbs && (C.moduli[l1] < kFpPrime) == fp) ++l1;
         const dim3 grid(n2, C.N / kThreads, l1 - l0);
-        if (n1 == 32 || n1 == 16 || n1 == 8) {
-          static_assert(kThreads % kBsgsRegCoeffs == 0, "a tile of whole CTAs");
-          const dim3 rgrid(ng * (kThreads / kBsgsRegCoeffs), C.N / kThreads, l1 - l0);
-          auto kern = fp ? (n1 == 32   ? bsgs_inner_reg_kernel<32>
-                            : n1 == 16 ? bsgs_inner_reg_kernel<16>
-                                       : bsgs_inner_reg_kernel<8>)
-                         : (n1 == 32   ? bsgs_inner_reg_int_kernel<32>
-                            : n1 == 16 ? bsgs_inner_reg_int_kernel<16>
-                                       : bsgs_inner_reg_int_kernel<8>);
-          kern<<<rgrid, kBsgsRegThreads, 0, C.stream>>>(bp, ng, dg, ip, C.logN, n2, l0, acc, C.d_mods);
-        } else if (fp) {
+        if (fp) {
           bsgs_inner_fp_kernel<<<grid, dim3(kBsgsThreads, ng), 0, C.stream>>>(bp, ng, n1, dg, ip, limbs, C.logN, n2,
                                                                                l0, acc, C.d_mods);
         } else {
