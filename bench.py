@@ -454,12 +454,42 @@ def run_engine(args):
                 "launches": d["launches"], "ms_per_launch": per_launch_ms,
                 # share of device time in the fully profiled warm-up step
                 "share": prof_all[name]["ms"] / sum(v["ms"] for v in prof_all.values())}
+    released_bytes = 0  # diagonal cache handed back to the context's allocator
     if roof is not None:
         # the metric's key-switch part (ks bytes = (l + 2 beta (l + K) + 2 l) limbs)
         roof["keyswitch"] = keyswitch
         if rank == 0 and not args.no_sweep:
-            block.release_cache()  # room for the sweep's contexts
+            released_bytes += block.release_cache()  # room for the sweep's contexts
             roof["keyswitch_sweep"] = [keyswitch_point(eng, torch, *pt, device=local) for pt in SWEEP]
+
+    # the 12-block + head model on one sequence (one sequence per GPU):
+    # a warm-up pass, then one timed pass
+    model_rec = None
+    if rank == 0 and not args.no_model:
+        released = released_bytes + block.release_cache()
+        ws = [plain_block.synthetic_weights(100 + b, d=d_model, mlp=mlp) for b in range(12)]
+        hw = plain_block.synthetic_head_weights(99, d=d_model)
+        free, _ = torch.cuda.mem_get_info(local)
+        cached = max(1, int(((free + released) / 2**30 - 70) // 27))
+        model = eng.EncryptedModel(cc, ws, hw, args.tokens, heads=heads, cached_blocks=min(cached, 12))
+        cc.EvalRotateKeyGen(sorted(set(model.rotation_indices()) - set(block.rotation_indices())))
+        h_ref, m_ref = plain_block.model(x, ws, hw, heads=heads)
+        model.forward(x)
+        barrier()
+        m0 = torch.cuda.Event(enable_timing=True)
+        m1 = torch.cuda.Event(enable_timing=True)
+        m0.record(stream)
+        h, m = model.forward(x)
+        m1.record(stream)
+        m1.synchronize()
+        dev = sum(b.report()["seconds"].get("evaluate_events", 0.0) for b in model.blocks)
+        dev += model.head.report()["seconds"].get("head_total", 0.0)
+        model_rec = {"workload": f"12 blocks + head (768 -> 2 readout margin), one sequence of {args.tokens} "
+                                 "tokens, full-hidden-state client refresh between blocks",
+                     "value": dev, "e2e": m0.elapsed_time(m1) / 1e3, "unit": UNIT, "steps": 1, "warmup": 1,
+                     "cached_blocks": model.cached_blocks,
+                     "rel_inf_vs_plaintext": plain_block.rel_inf(h_ref, h), "margin": m, "margin_plaintext": m_ref}
+        del model
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
@@ -508,6 +538,7 @@ def run_engine(args):
             "gpu_launches": launches,
             "clocks": clk.summary(),
             "cpu_baseline": cpu,
+            "model_12_blocks_head": model_rec,
         }
         print(json.dumps(line), flush=True)
     if dist is not None:
@@ -787,6 +818,7 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--no-sweep", action="store_true")
+    ap.add_argument("--no-model", action="store_true")
     # a smaller token count only for profiler captures (the benchmark is 103)
     ap.add_argument("--tokens", type=int, default=TOKENS)
     # primitive-operation sweep instead of the block (one configuration per run)
