@@ -417,6 +417,55 @@ __global__ void __launch_bounds__(kThreads) modup_conv_batch_kernel(KsBatch b, c
   }
 }
 
+// sum_j ext_j[src pair] * key_j for both key halves over the item's digits,
+// two adjacent residues: every digit's loads are issued before any product
+// when the digit count is a compile-time 1..4 (the runtime loop would wait
+// one memory round trip per digit)
+template <int BETA>
+__device__ __forceinline__ void ks_digit_products(const uint64_t* __restrict__ ext, const uint64_t* __restrict__ key,
+                                                  size_t E, size_t P, int t, int pt, int N, uint32_t src, int n,
+                                                  U128& a0, U128& a1, U128& b0, U128& b1) {
+  ulonglong2 v[BETA], k0[BETA], k1[BETA];
+#pragma unroll
+  for (int j = 0; j < BETA; ++j) {
+    v[j] = *reinterpret_cast<const ulonglong2*>(ext + ((size_t)j * E + t) * N + (src & ~1u));
+    k0[j] = *reinterpret_cast<const ulonglong2*>(key + ((size_t)j * 2 * P + pt) * N + n);
+    k1[j] = *reinterpret_cast<const ulonglong2*>(key + ((size_t)j * 2 * P + P + pt) * N + n);
+  }
+  const bool swap = src & 1u;
+#pragma unroll
+  for (int j = 0; j < BETA; ++j) {
+    const uint64_t v0 = swap ? v[j].y : v[j].x, v1 = swap ? v[j].x : v[j].y;
+    mac_wide(a0, v0, k0[j].x);
+    mac_wide(a1, v1, k0[j].y);
+    mac_wide(b0, v0, k1[j].x);
+    mac_wide(b1, v1, k1[j].y);
+  }
+}
+
+__device__ __forceinline__ void ks_digits(const uint64_t* __restrict__ ext, const uint64_t* __restrict__ key, int beta,
+                                          size_t E, size_t P, int t, int pt, int N, uint32_t src, int n, U128& a0,
+                                          U128& a1, U128& b0, U128& b1) {
+  switch (beta) {
+    case 1: ks_digit_products<1>(ext, key, E, P, t, pt, N, src, n, a0, a1, b0, b1); return;
+    case 2: ks_digit_products<2>(ext, key, E, P, t, pt, N, src, n, a0, a1, b0, b1); return;
+    case 3: ks_digit_products<3>(ext, key, E, P, t, pt, N, src, n, a0, a1, b0, b1); return;
+    case 4: ks_digit_products<4>(ext, key, E, P, t, pt, N, src, n, a0, a1, b0, b1); return;
+    default: break;
+  }
+  const bool swap = src & 1u;
+  for (int j = 0; j < beta; ++j) {
+    const ulonglong2 v = *reinterpret_cast<const ulonglong2*>(ext + ((size_t)j * E + t) * N + (src & ~1u));
+    const uint64_t v0 = swap ? v.y : v.x, v1 = swap ? v.x : v.y;
+    const ulonglong2 k0 = *reinterpret_cast<const ulonglong2*>(key + ((size_t)j * 2 * P + pt) * N + n);
+    const ulonglong2 k1 = *reinterpret_cast<const ulonglong2*>(key + ((size_t)j * 2 * P + P + pt) * N + n);
+    mac_wide(a0, v0, k0.x);
+    mac_wide(a1, v1, k0.y);
+    mac_wide(b0, v0, k1.x);
+    mac_wide(b1, v1, k1.y);
+  }
+}
+
 __global__ void __launch_bounds__(kThreads) ks_inner_batch_kernel(KsBatch b, const uint64_t* __restrict__ ext_all,
                                                                   bool shared, uint64_t* __restrict__ acc_all,
                                                                   int limbs, int L, int K, int P, int beta, int logN,
@@ -433,18 +482,8 @@ __global__ void __launch_bounds__(kThreads) ks_inner_batch_kernel(KsBatch b, con
   const uint64_t* ext = ext_all + (shared ? 0 : (size_t)m * beta * E * N);
   const uint64_t* key = b.key[m];
   const uint32_t src = (g == 1u) ? (uint32_t)n : auto_index((uint32_t)n, g, logN);
-  const bool swap = src & 1u;
   U128 a0{0, 0}, a1{0, 0}, b0{0, 0}, b1{0, 0};
-  for (int j = 0; j < beta; ++j) {
-    const ulonglong2 v = *reinterpret_cast<const ulonglong2*>(ext + ((size_t)j * E + t) * N + (src & ~1u));
-    const uint64_t v0 = swap ? v.y : v.x, v1 = swap ? v.x : v.y;
-    const ulonglong2 k0 = *reinterpret_cast<const ulonglong2*>(key + ((size_t)j * 2 * P + pt) * N + n);
-    const ulonglong2 k1 = *reinterpret_cast<const ulonglong2*>(key + ((size_t)j * 2 * P + P + pt) * N + n);
-    mac_wide(a0, v0, k0.x);
-    mac_wide(a1, v1, k0.y);
-    mac_wide(b0, v0, k1.x);
-    mac_wide(b1, v1, k1.y);
-  }
+  ks_digits(ext, key, beta, E, P, t, pt, N, src, n, a0, a1, b0, b1);
   uint64_t* acc = acc_all + (size_t)m * 2 * E * N;
   *reinterpret_cast<ulonglong2*>(acc + (size_t)t * N + n) = make_ulonglong2(reduce128(a0, md), reduce128(a1, md));
   *reinterpret_cast<ulonglong2*>(acc + ((size_t)E + t) * N + n) =
@@ -471,19 +510,8 @@ __global__ void __launch_bounds__(kThreads) ks_inner_sum_kernel(KsBatch b, const
   for (int m = 0; m < b.M; ++m) {
     const uint32_t g = b.g[m];
     const uint32_t src = (g == 1u) ? (uint32_t)n : auto_index((uint32_t)n, g, logN);
-    const bool swap = src & 1u;
     const uint64_t* ext = ext_all + (size_t)m * beta * E * N;
-    const uint64_t* key = b.key[m];
-    for (int j = 0; j < beta; ++j) {
-      const ulonglong2 v = *reinterpret_cast<const ulonglong2*>(ext + ((size_t)j * E + t) * N + (src & ~1u));
-      const uint64_t v0 = swap ? v.y : v.x, v1 = swap ? v.x : v.y;
-      const ulonglong2 k0 = *reinterpret_cast<const ulonglong2*>(key + ((size_t)j * 2 * P + pt) * N + n);
-      const ulonglong2 k1 = *reinterpret_cast<const ulonglong2*>(key + ((size_t)j * 2 * P + P + pt) * N + n);
-      mac_wide(a0, v0, k0.x);
-      mac_wide(a1, v1, k0.y);
-      mac_wide(b0, v0, k1.x);
-      mac_wide(b1, v1, k1.y);
-    }
+    ks_digits(ext, b.key[m], beta, E, P, t, pt, N, src, n, a0, a1, b0, b1);
     if ((m + 1) % fold == 0) {
       a0 = U128{reduce128(a0, md), 0};
       a1 = U128{reduce128(a1, md), 0};
@@ -756,18 +784,8 @@ __global__ void __launch_bounds__(kThreads) ks_inner_multi_kernel(KsBatch b, con
   const uint64_t* ext = ext_all + (size_t)b.src[m] * beta * E * N;
   const uint64_t* key = b.key[m];
   const uint32_t src = auto_index((uint32_t)n, g, logN);
-  const bool swap = src & 1u;
   U128 a0{0, 0}, a1{0, 0}, b0{0, 0}, b1{0, 0};
-  for (int j = 0; j < beta; ++j) {
-    const ulonglong2 v = *reinterpret_cast<const ulonglong2*>(ext + ((size_t)j * E + t) * N + (src & ~1u));
-    const uint64_t v0 = swap ? v.y : v.x, v1 = swap ? v.x : v.y;
-    const ulonglong2 k0 = *reinterpret_cast<const ulonglong2*>(key + ((size_t)j * 2 * P + pt) * N + n);
-    const ulonglong2 k1 = *reinterpret_cast<const ulonglong2*>(key + ((size_t)j * 2 * P + P + pt) * N + n);
-    mac_wide(a0, v0, k0.x);
-    mac_wide(a1, v1, k0.y);
-    mac_wide(b0, v0, k1.x);
-    mac_wide(b1, v1, k1.y);
-  }
+  ks_digits(ext, key, beta, E, P, t, pt, N, src, n, a0, a1, b0, b1);
   uint64_t* acc = acc_all + (size_t)m * 2 * E * N;
   *reinterpret_cast<ulonglong2*>(acc + (size_t)t * N + n) = make_ulonglong2(reduce128(a0, md), reduce128(a1, md));
   *reinterpret_cast<ulonglong2*>(acc + ((size_t)E + t) * N + n) =
