@@ -84,9 +84,9 @@ int ckks_relin_keygen(ckks_ctx* ctx);
 int ckks_rotkey_gen(ckks_ctx* ctx, const int* indices, int count);
 /* Both generate, besides the key over all K special primes, a one-digit key
  * over the first K_low special primes when the parameters allow it
- * (log2(p_0 ... p_{K_low-1}) >= log2(q_0 ... q_3) + 20 with K_low < K and
- * alpha >= 4): key switches at <= 4 limbs then use it (fewer limbs to
- * extend, transform and divide).  ckks_ctx_low_set reports (4, K_low) or
+ * (log2(p_0 ... p_{K_low-1}) >= log2(q_0 q_1 q_2) + 19.5 with K_low < K and
+ * alpha >= 3): key switches at <= 3 limbs then use it (fewer limbs to
+ * extend, transform and divide).  ckks_ctx_low_set reports (3, K_low) or
  * (0, 0). */
 int ckks_ctx_low_set(const ckks_ctx* ctx, int* low_limbs, int* low_special);
 /* key material to host: which = 0 secret (P*N), 1 public (2*L*N),

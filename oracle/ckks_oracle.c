@@ -293,14 +293,15 @@ oc_ctx* oc_create(int logN, int L, int dnum, int first_bits, int scale_bits,
      * scaling prime; each rescale by q_{l-1} maps s -> s*s/q_{l-1}. */
     c->scales[L] = (L >= 2) ? (double)c->q[L - 1] : ldexp(1.0, scale_bits);
     for (int l = L; l >= 2; l--) c->scales[l - 1] = c->scales[l] * c->scales[l] / (double)c->q[l - 1];
-    /* reduced special-prime set for one-digit key switches at <= 4 limbs */
+    /* reduced special-prime set for one-digit key switches at <= 3 limbs:
+     * the fewest leading special primes with log2 P' >= log2 Q_3 + 19.5 */
     {
-        const int lo = c->alpha < 4 ? c->alpha : 4;
+        const int lo = c->alpha < 3 ? c->alpha : 3;
         double qbits = 0.0, pbits = 0.0;
         for (int i = 0; i < lo; i++) qbits += log2((double)c->q[i]);
         int k = 0;
-        while (k < c->K && pbits < qbits + 20.0) pbits += log2((double)c->q[L + k++]);
-        if (L >= lo && lo >= 1 && pbits >= qbits + 20.0 && k < c->K) {
+        while (k < c->K && pbits < qbits + 19.5) pbits += log2((double)c->q[L + k++]);
+        if (L >= lo && lo >= 1 && pbits >= qbits + 19.5 && k < c->K) {
             c->low_limbs = lo;
             c->K_low = k;
         }

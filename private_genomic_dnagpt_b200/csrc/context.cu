@@ -242,15 +242,16 @@ Context::Context(const Params& p) : params(p) {
   d_w1ninv = upload(w1ninv);
   d_pmod = upload(pmod);
 
-  // reduced special-prime set for one-digit key switches at <= 4 limbs: the
-  // fewest leading special primes whose product exceeds Q_{low} by 2^20
+  // reduced special-prime set for one-digit key switches at <= 3 limbs: the
+  // fewest leading special primes whose product exceeds Q_3 by 2^19.5 (three
+  // 60-bit primes over a 60 + 2 x 50-bit Q_3)
   {
-    const int lo = std::min(4, alpha);
+    const int lo = std::min(3, alpha);
     double qbits = 0.0, pbits = 0.0;
     for (int i = 0; i < lo; ++i) qbits += std::log2((double)moduli[i]);
     int k = 0;
-    while (k < K && pbits < qbits + 20.0) pbits += std::log2((double)moduli[L + k++]);
-    if (L >= lo && lo >= 1 && pbits >= qbits + 20.0 && k < K) {
+    while (k < K && pbits < qbits + 19.5) pbits += std::log2((double)moduli[L + k++]);
+    if (L >= lo && lo >= 1 && pbits >= qbits + 19.5 && k < K) {
       low_limbs = lo;
       K_low = k;
     }

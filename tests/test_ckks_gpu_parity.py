@@ -468,7 +468,7 @@ def pair_wide():
 
 def test_reduced_set_keys_bit_exact(pair_wide):
     o, cc = pair_wide
-    assert (cc.low_limbs, cc.K_low) == (o.low_limbs, o.K_low) == (4, 4)
+    assert (cc.low_limbs, cc.K_low) == (o.low_limbs, o.K_low) == (3, 3)
     assert np.array_equal(cc.key_array(2), o.switch_key(0))
     assert np.array_equal(cc.key_array(4), o.switch_key_low(0))
     for k in (1, -7, 32):

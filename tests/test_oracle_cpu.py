@@ -266,7 +266,7 @@ def test_keyswitch_matches_definition(small):
 
 @pytest.fixture(scope="module")
 def wide():
-    """alpha = K = 8: key switches at <= 4 limbs use the 4-prime set."""
+    """alpha = K = 8: key switches at <= 3 limbs use the 3-prime set."""
     o = Oracle(logN=10, L=8, dnum=1, seed=17)
     o.keygen()
     o.relin_keygen()
@@ -276,11 +276,11 @@ def wide():
 
 def test_reduced_special_prime_set_is_chosen_by_bits(wide):
     o = wide
-    assert (o.low_limbs, o.K_low) == (4, 4) and o.K == 8
+    assert (o.low_limbs, o.K_low) == (3, 3) and o.K == 8
     q = o.moduli
-    assert sum(np.log2(float(p)) for p in q[o.L:o.L + 4]) >= sum(np.log2(float(p)) for p in q[:4]) + 20
+    assert sum(np.log2(float(p)) for p in q[o.L:o.L + 3]) >= sum(np.log2(float(p)) for p in q[:3]) + 19.5
     key = o.switch_key_low(0)
-    used = list(range(4)) + list(range(o.L, o.L + 4))
+    used = list(range(3)) + list(range(o.L, o.L + 3))
     unused = [t for t in range(o.L + o.K) if t not in used]
     assert not key[:, unused].any() and key[:, used].all(axis=-1).any()
 
