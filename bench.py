@@ -598,8 +598,10 @@ def run_shard(args):
             e1.synchronize()
             steps.append(e0.elapsed_time(e1) / 1e3)
             # this rank's span from encrypted inputs resident to encrypted
-            # outputs resident (exchanges included)
-            evals.append(block.report()["seconds"]["evaluate_events"])
+            # outputs resident (exchanges included); a helper rank owns no
+            # token group and finishes none: the owners' spans, which wait
+            # for the helpers' partial sums, carry the block's latency
+            evals.append(block.report()["seconds"].get("evaluate_events", 0.0))
         cc.Synchronize()
         dist.barrier()
     t = torch.tensor([float(np.mean(evals)), float(np.mean(steps))], device="cuda", dtype=torch.float64)
