@@ -272,37 +272,57 @@ def ntt_launch_sizes(prof: dict, logn: int) -> dict:
 SWEEP = [(15, 24, 3), (17, 24, 3), (16, 8, 3), (16, 16, 3), (16, 32, 3), (16, 24, 2), (16, 24, 4)]
 
 
-def keyswitch_point(eng, torch, logn: int, limbs: int, dnum: int, device: int, R: int = 32, steps: int = 3):
-    """EvalRotate over R ciphertexts at one (N, limbs, dnum): one ckks_rotate
-    call each (indices 1..512), event-timed on the engine stream."""
+def rotation_rates(eng, torch, cc, R: int = 32, steps: int = 3):
+    """Seconds per EvalRotate over R ciphertexts (indices 1..512, keys
+    generated by the caller): batched (one ckks_rotate_batch call, the form
+    the block uses for independent switches) and one ckks_rotate call each;
+    event-timed on the engine stream after one untimed step."""
+    stream = torch.cuda.ExternalStream(cc.stream_handle())
+    rng = np.random.default_rng(cc.N + cc.L)
+    cts = [cc.Encrypt(cc.MakeCKKSPackedPlaintext(rng.uniform(-1, 1, cc.slots))) for _ in range(R)]
+    outs = [eng.Ciphertext(cc) for _ in range(R)]
+    ks = [ROT_INDICES[r % len(ROT_INDICES)] for r in range(R)]
+    lib = eng.lib()
+
+    def single():
+        for r in range(R):
+            eng._check(lib.ckks_rotate(cc.h, cts[r].h, ks[r], outs[r].h))
+
+    def batched():
+        cc.rotate_batch(cts, ks)
+
+    res = []
+    for fn in (batched, single):
+        fn()
+        fn()  # the allocator's blocks of these sizes exist from here on
+        cc.Synchronize()
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(steps):
+            fn()
+        e1.record(stream)
+        e1.synchronize()
+        res.append(e0.elapsed_time(e1) / 1e3 / (R * steps))
+    return res
+
+
+def keyswitch_record(cc, per_batch: float, per_single: float, limbs: int, logn: int, dnum: int) -> dict:
+    ks_b = keyswitch_bytes(limbs, cc.K, cc.alpha, cc.N)
+    peak, kind = measured_peaks()
+    return {"logN": logn, "limbs": limbs, "dnum": dnum, "EvalRotate/s": round(1.0 / per_batch, 1),
+            "us_per_rotation": round(per_batch * 1e6, 2), "GBps": round(ks_b / per_batch / 1e9, 1),
+            "frac": round(ks_b / per_batch / 1e9 / peak, 4), "peak_kind": kind,
+            "us_per_rotation_single_call": round(per_single * 1e6, 2), "algorithmic_bytes": ks_b}
+
+
+def keyswitch_point(eng, torch, logn: int, limbs: int, dnum: int, device: int):
+    """The key-switch record at one (N, limbs, dnum) on a fresh context."""
     cc = eng.GenCryptoContext(eng.CCParams(ring_dim_log=logn, limbs=limbs, dnum=dnum, seed=3, device=device))
     cc.KeyGen()
     cc.EvalRotateKeyGen(ROT_INDICES)
-    stream = torch.cuda.ExternalStream(cc.stream_handle())
-    rng = np.random.default_rng(logn * 100 + limbs)
-    cts = [cc.Encrypt(cc.MakeCKKSPackedPlaintext(rng.uniform(-1, 1, cc.slots))) for _ in range(R)]
-    outs = [eng.Ciphertext(cc) for _ in range(R)]
-    lib = eng.lib()
-
-    def step():
-        for r in range(R):
-            eng._check(lib.ckks_rotate(cc.h, cts[r].h, ROT_INDICES[r % len(ROT_INDICES)], outs[r].h))
-
-    step()
-    cc.Synchronize()
-    e0 = torch.cuda.Event(enable_timing=True)
-    e1 = torch.cuda.Event(enable_timing=True)
-    e0.record(stream)
-    for _ in range(steps):
-        step()
-    e1.record(stream)
-    e1.synchronize()
-    per = e0.elapsed_time(e1) / 1e3 / (R * steps)
-    ks_b = keyswitch_bytes(limbs, cc.K, cc.alpha, cc.N)
-    peak, _ = measured_peaks()
-    return {"logN": logn, "limbs": limbs, "dnum": dnum, "us_per_rotation": round(per * 1e6, 2),
-            "EvalRotate/s": round(1.0 / per, 1), "GBps": round(ks_b / per / 1e9, 1),
-            "frac": round(ks_b / per / 1e9 / peak, 4)}
+    pb, ps = rotation_rates(eng, torch, cc)
+    return keyswitch_record(cc, pb, ps, limbs, logn, dnum)
 
 
 def run_engine(args):
@@ -410,37 +430,15 @@ def run_engine(args):
         cold_s.append(block.report()["seconds"]["evaluate_events"])
 
     # EvalRotate/s and key-switch GB/s on the primitive configuration
-    R = 32
-    cts = [cc.Encrypt(cc.MakeCKKSPackedPlaintext(np.random.default_rng(r).uniform(-1, 1, cc.slots)))
-           for r in range(R)]
-    outs = [eng.Ciphertext(cc) for _ in range(R)]
-    lib = eng.lib()
-
-    def rot_step():
-        for r in range(R):
-            eng._check(lib.ckks_rotate(cc.h, cts[r].h, ROT_INDICES[r % len(ROT_INDICES)], outs[r].h))
-
-    for _ in range(3):
-        rot_step()
-    barrier()
-    r0 = torch.cuda.Event(enable_timing=True)
-    r1 = torch.cuda.Event(enable_timing=True)
-    rsteps = 5
-    r0.record(stream)
-    for _ in range(rsteps):
-        rot_step()
-    r1.record(stream)
-    barrier()
-    per_rot_s = r0.elapsed_time(r1) / 1e3 / (R * rsteps)
-    peak, peak_kind = measured_peaks()
-    ks_b = keyswitch_bytes(LIMBS, cc.K, cc.alpha, cc.N)
-    keyswitch = {"EvalRotate/s": 1.0 / per_rot_s * world, "GBps": ks_b / per_rot_s / 1e9,
-                 "frac": ks_b / per_rot_s / 1e9 / peak, "peak_kind": peak_kind,
-                 "us_per_rotation": per_rot_s * 1e6, "algorithmic_bytes": ks_b,
-                 "config": f"EvalRotate N=2^{args.logn}, {LIMBS} limbs, dnum={DNUM}, {R} ciphertexts x "
-                           f"indices 1..512, one ckks_rotate call each"}
+    # (24 limbs, dnum 3), on this context and its keys
+    pb, ps = rotation_rates(eng, torch, cc)
+    keyswitch = keyswitch_record(cc, pb, ps, LIMBS, args.logn, DNUM)
+    keyswitch["EvalRotate/s"] = round(keyswitch["EvalRotate/s"] * world, 1)  # all ranks
+    keyswitch["config"] = (f"EvalRotate N=2^{args.logn}, {LIMBS} limbs, dnum={DNUM}, 32 ciphertexts x indices "
+                           f"1..512: one ckks_rotate_batch call (us_per_rotation_single_call: one ckks_rotate each)")
 
     roof = None
+    peak, peak_kind = measured_peaks()
     if dominant is not None and dominant in prof:
         name, d = dominant, prof[dominant]
         per_launch_ms = d["ms"] / d["launches"]
