@@ -699,29 +699,43 @@ __global__ void __launch_bounds__(kThreads) ks_inner_hoist_kernel(HoistKeys h, c
   U128 s0[kHoistItems], s1[kHoistItems];
 #pragma unroll
   for (int i = 0; i < kHoistItems; ++i) s0[i] = s1[i] = U128{0, 0};
-  for (int r = 0; r < h.R; ++r) {
+  // the (rotation, digit) steps in order, the next step's key residues and
+  // ModUp residues loaded while the current one's products run
+  const int steps = h.R * beta;
+  uint64_t k0 = 0, k1 = 0, v[kHoistItems];
+  auto load = [&](int x, uint64_t& a0, uint64_t& a1, uint64_t* w) {
+    const int r = x / beta, j = x - r * beta;
     const uint32_t src = auto_index((uint32_t)n, h.g[r], logN);
     const uint64_t* key = h.key[r];
-    for (int j = 0; j < beta; ++j) {
-      const uint64_t k0 = key[((size_t)j * 2 * P + pt) * N + n];
-      const uint64_t k1 = key[((size_t)j * 2 * P + P + pt) * N + n];
-      const uint64_t* ej = ext + (size_t)r * rstride + (size_t)j * E * N + src;
+    a0 = key[((size_t)j * 2 * P + pt) * N + n];
+    a1 = key[((size_t)j * 2 * P + P + pt) * N + n];
+    const uint64_t* ej = ext + (size_t)r * rstride + (size_t)j * E * N + src;
 #pragma unroll
-      for (int i = 0; i < kHoistItems; ++i) {
-        if (i < cnt) {
-          const uint64_t v = ej[(size_t)i * istride];
-          mac_wide(s0[i], v, k0);
-          mac_wide(s1[i], v, k1);
-        }
+    for (int i = 0; i < kHoistItems; ++i) w[i] = i < cnt ? ej[(size_t)i * istride] : 0;
+  };
+  if (steps > 0) load(0, k0, k1, v);
+  for (int x = 0; x < steps; ++x) {
+    uint64_t nk0 = 0, nk1 = 0, nv[kHoistItems] = {};
+    if (x + 1 < steps) load(x + 1, nk0, nk1, nv);
+#pragma unroll
+    for (int i = 0; i < kHoistItems; ++i) {
+      if (i < cnt) {
+        mac_wide(s0[i], v[i], k0);
+        mac_wide(s1[i], v[i], k1);
       }
     }
-    if ((r + 1) % fold == 0) {
+    const int r = x / beta;
+    if (x - r * beta == beta - 1 && (r + 1) % fold == 0) {
 #pragma unroll
       for (int i = 0; i < kHoistItems; ++i) {
         s0[i] = U128{reduce128(s0[i], md), 0};
         s1[i] = U128{reduce128(s1[i], md), 0};
       }
     }
+    k0 = nk0;
+    k1 = nk1;
+#pragma unroll
+    for (int i = 0; i < kHoistItems; ++i) v[i] = nv[i];
   }
 #pragma unroll
   for (int i = 0; i < kHoistItems; ++i) {
