@@ -810,6 +810,75 @@ def run_primitive(args):
     print(json.dumps(line), flush=True)
 
 
+def run_bsgs(args):
+    """One BSGS matrix product (T123.cpp:1264-1295) of a seeded 768 x 768
+    weight over 4 token groups, n1 = n2 = 32, at the context's limbs: the
+    diagonals are encoded once, the baby steps computed once, and each step
+    is one ckks_bsgs_matmul (inner sums, grouped giant-step rotations,
+    rescale).  The inner-sum kernel is timed from the engine's launch events.
+    The baby steps, warm-up and timed products are inside a profiler range,
+    so `ncu --profile-from-start off` on this command captures their kernels
+    (about 2.5 GB on the device at 4 limbs, N = 2^16)."""
+    import torch
+    import private_genomic_dnagpt_b200 as eng
+
+    torch.cuda.set_device(0)
+    B, n1, n2, groups, D = 32, 32, 32, 4, 768
+    cc = eng.GenCryptoContext(eng.CCParams(ring_dim_log=args.logn, limbs=args.limbs, dnum=args.dnum, seed=1))
+    cc.KeyGen()
+    cc.EvalRotateKeyGen([B * j for j in range(1, n1)] + [B * n1 * g for g in range(1, n2)])
+    L, N = args.limbs, cc.N
+    rng = np.random.default_rng(7)
+    W = rng.normal(0.0, 0.02, (D, D))
+    diags = cc.bsgs_diagonals(W, B, n1, L)
+    x = [cc.Encrypt(cc.MakeCKKSPackedPlaintext(rng.uniform(-1, 1, cc.slots))) for _ in range(groups)]
+    stream = torch.cuda.ExternalStream(cc.stream_handle())
+    # the profiler range also holds the baby steps (hoisted rotations: the
+    # key products of keyswitch_hoisted_multi) and the warm-up products
+    torch.cuda.cudart().cudaProfilerStart()
+    babies = [cc.bsgs_babies(x, B, n1)]
+    for _ in range(args.warmup):
+        cc.bsgs_matmul([diags], babies)
+    cc.Synchronize()
+    cc.profile_reset()
+    cc.profile_only("bsgs_inner")
+    cc.profile(True)
+    with ClockSampler(0) as clk:
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(args.steps):
+            cc.bsgs_matmul([diags], babies)
+        e1.record(stream)
+        e1.synchronize()
+    torch.cuda.cudart().cudaProfilerStop()
+    cc.Synchronize()
+    prof = cc.profile_report()
+    cc.profile(False)
+    cc.profile_only(None)
+    sec = e0.elapsed_time(e1) / 1e3 / args.steps
+    inner = prof.get("bsgs_inner", {})
+    inner_s = inner.get("ms", 0.0) / 1e3 / max(1, inner.get("launches", 1))
+    peak, peak_kind = measured_peaks()
+    lb = 8.0 * N
+    # diagonals, baby residues, inner sums written (algorithmic bytes)
+    inner_bytes = (n1 * n2 * L + groups * (2.0 * n1 * L + 2.0 * n2 * L)) * lb
+    line = {
+        "metric": "BSGS product latency (s)", "value": sec, "unit": "s", "n_gpus": 1, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": sec * 1e3, "higher_is_better": False, "scaling": "weak",
+        "vs_baseline": None, "dtype": "u64/f64", "data": "synthetic",
+        "config": {"workload": f"BSGS product, 768x768 weight, n1=n2=32, {groups} token groups, "
+                               f"N=2^{args.logn}, {L} limbs, dnum={args.dnum}",
+                   "flush": "diagonals > L2"},
+        "inner": {"us_per_launch": inner_s * 1e6, "launches": inner.get("launches", 0),
+                  "achieved_GBps": inner_bytes / inner_s / 1e9 if inner_s else None,
+                  "frac": inner_bytes / inner_s / 1e9 / peak if inner_s else None, "peak": peak,
+                  "peak_kind": peak_kind, "bytes": inner_bytes},
+        "clocks": clk.summary(),
+    }
+    print(json.dumps(line), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -823,6 +892,8 @@ def main():
     ap.add_argument("--tokens", type=int, default=TOKENS)
     # primitive-operation sweep instead of the block (one configuration per run)
     ap.add_argument("--primitive", action="store_true")
+    # one BSGS matrix product at --logn / --limbs instead of the block
+    ap.add_argument("--bsgs", action="store_true")
     ap.add_argument("--logn", type=int, default=LOG_N)
     ap.add_argument("--limbs", type=int, default=LIMBS)
     ap.add_argument("--dnum", type=int, default=DNUM)
@@ -839,6 +910,8 @@ def main():
         run_reference(args)
     elif args.primitive:
         run_primitive(args)
+    elif args.bsgs:
+        run_bsgs(args)
     elif args.blocks > 1 or args.head:
         run_model(args)
     elif args.shard or (int(os.environ.get("WORLD_SIZE", "1")) > 1 and not args.replicas):

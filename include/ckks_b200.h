@@ -71,7 +71,10 @@ int ckks_ctx_info(const ckks_ctx* ctx, int* ring_dim, int* limbs, int* special, 
 int ckks_ctx_moduli(const ckks_ctx* ctx, uint64_t* out, int count);
 /* FLEXIBLEAUTO scaling factor of a fresh encoding at `level` */
 double ckks_ctx_scale(const ckks_ctx* ctx, int level);
-/* Synchronize() (T123.cpp:1626, 1662, 1671) */
+/* Synchronize() (T123.cpp:1626, 1662, 1671).  Also reports, as CKKS_ECUDA,
+ * a bounded device wait that gave up since the last call (a bulk copy into
+ * shared memory that did not complete within one second); the outputs of
+ * the calls since then are not valid, and the context stays usable. */
 int ckks_sync(ckks_ctx* ctx);
 /* the cudaStream_t the context enqueues on (for event timing by callers) */
 void* ckks_ctx_stream(ckks_ctx* ctx);
@@ -399,6 +402,12 @@ int ckks_schedule_diagonal(const double* W, int out_dim, int in_dim, int ld, int
  * first call on a device looks up the array's address (make it before any
  * stream capture); calls that overlap on the GPU race on the shared array. */
 int ckks_rotate_noalloc(ckks_ctx* ctx, const uint64_t* in_dev, int limbs, int k, uint64_t* out_dev);
+
+/* Diagnostic of the bounded waits: one CTA stages 4 KiB through a bulk copy
+ * into shared memory and back.  starve = 0: CKKS_OK when the data came back
+ * intact.  starve = 1: the barrier expects more bytes than are copied, the
+ * wait gives up after one second, and ckks_sync's CKKS_ECUDA is returned. */
+int ckks_selftest_bulk_wait(ckks_ctx* ctx, int starve);
 
 #ifdef __cplusplus
 }

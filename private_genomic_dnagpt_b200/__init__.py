@@ -138,6 +138,7 @@ _SIGS = [
     ("ckks_profile_only", ctypes.c_int, [_vp, ctypes.c_char_p]),
     ("ckks_ntt_forward_device", ctypes.c_int, [_vp, _vp, ctypes.c_int, ctypes.c_int]),
     ("ckks_rotate_noalloc", ctypes.c_int, [_vp, _vp, ctypes.c_int, ctypes.c_int, _vp]),
+    ("ckks_selftest_bulk_wait", ctypes.c_int, [_vp, ctypes.c_int]),
     ("ckks_block_create", ctypes.c_int, [_vp] + [_f64p] * 6 + [ctypes.c_int] * 4 + [ctypes.POINTER(_vp)]),
     ("ckks_block_destroy", ctypes.c_int, [_vp]),
     ("ckks_block_rotation_indices", ctypes.c_int, [_vp, ctypes.POINTER(ctypes.c_int), ctypes.c_int]),

@@ -258,110 +258,95 @@ __global__ void __launch_bounds__(kBsgsThreads * kMaxGroups) bsgs_inner_fp_kerne
   *reinterpret_cast<ulonglong2*>(out.c1[q][g] + off) = r1;
 }
 
-// Float64 inner sums with the baby residues held in registers (as doubles):
-// kBsgsSplit lanes share one coefficient of one token group and one limb,
-// each holding n1 / kBsgsSplit of the babies, looping over the n2 giant steps
-// and streaming their diagonals (8-byte loads over the tile-major store); the
-// lanes' sums meet by shuffles once per giant step.  The CTAs of the token
-// groups of one tile are adjacent in the grid, so each diagonal tile comes
-// from HBM once and from L2 for the other groups, and no baby residue is
-// read twice.
+// Inner sums with the baby residues held in registers: SPLIT lanes share
+// one coefficient of one token group and one limb, each holding n1 / SPLIT
+// of the babies, looping over the n2 giant steps and streaming their
+// diagonals (8-byte cp.async over the tile-major store, double-buffered in
+// shared memory); the lanes' sums meet by shuffles once per giant step.  The
+// CTAs of the token groups of one tile are adjacent in the grid, so each
+// diagonal tile comes from HBM once and from L2 for the other groups, and no
+// baby residue is read twice.
+//
+// On a limb whose prime is below kFpPrime every product is the exact
+// float64 one (fp_mod_product), summed in CHAINS independent accumulators
+// per output that are re-centred every four products.  On the 60-bit first
+// prime the residues are split into 30-bit halves, d = dh 2^30 + dl: each
+// product is four 32 x 32 -> 64-bit multiply-adds into four sums (dl bl,
+// dl bh, dh bl, dh bh; 16 products of halves below 2^30 stay below 2^64, so
+// no carries), recombined into a 128-bit value and Barrett-reduced once per
+// giant step (a 64 x 64 -> 128-bit multiply-accumulate costs the same four
+// partial products plus its carry chain).  The float64 and the integer
+// instances are separate kernels, each with its own register budget.
 constexpr int kBsgsRegThreads = 128;
-constexpr int kBsgsSplit = 2;                                   // lanes per coefficient
-constexpr int kBsgsRegCoeffs = kBsgsRegThreads / kBsgsSplit;  // coefficients per CTA
-template <int NB>
-__device__ __forceinline__ void bsgs_inner_reg_fp(const BabyPtrs& babies, int ng, const uint64_t* __restrict__ diag,
-                                                  const InnerPtrs& out, int logN, int n2, int l, bool accumulate,
-                                                  const ckks::Mod* __restrict__ mods,
-                                                  double (*sd)[NB / kBsgsSplit][kBsgsRegThreads]) {
-  constexpr int H = NB / kBsgsSplit;  // babies per lane
-  const int N = 1 << logN;
-  const int q = blockIdx.x % ng, part = blockIdx.x / ng;
-  const int tile = blockIdx.y;
-  const int half = threadIdx.x % kBsgsSplit;
-  const int c = part * kBsgsRegCoeffs + threadIdx.x / kBsgsSplit;  // coefficient within the tile
-  const size_t off = (size_t)l * N + (size_t)tile * kThreads + c;
-  double b0[H], b1[H];
-#pragma unroll
-  for (int j = 0; j < H; ++j) {
-    b0[j] = u2d(babies.c0[q][half * H + j][off]);
-    b1[j] = u2d(babies.c1[q][half * H + j][off]);
+template <int NB, int SPLIT>
+struct BsgsShape {
+  static constexpr int H = NB / SPLIT;                         // babies per lane
+  static constexpr int kCoeffs = kBsgsRegThreads / SPLIT;      // coefficients per CTA
+  static constexpr int kParts = kThreads / kCoeffs;            // CTAs per coefficient tile and group
+};
+constexpr int kRegSplit = 2, kFpChains = 2, kRegMinBlocks = 4;
+constexpr int kSplitBits = 30;  // half width of the integer instance's split products
+
+// sums of products of residues split into halves below 2^kSplitBits
+struct SplitSums {
+  uint64_t lo = 0, mid = 0, mid2 = 0, hi = 0;
+  __device__ __forceinline__ void mac(uint32_t dl, uint32_t dh, uint32_t bl, uint32_t bh) {
+    lo += (uint64_t)dl * bl;
+    mid += (uint64_t)dl * bh;
+    mid2 += (uint64_t)dh * bl;
+    hi += (uint64_t)dh * bh;
   }
-  const double* dt = reinterpret_cast<const double*>(diag) +
-                     ((size_t)l * (N / kThreads) + tile) * (size_t)(NB * n2) * kThreads + (size_t)half * H * kThreads +
-                     c;
-  // the next giant step's diagonals stream into this thread's own
-  // shared-memory slots while the current one is computed (cp.async, two
-  // buffers; each thread reads only what it copied, so no barrier)
-  auto prefetch = [&](int g, int buf) {
-    const double* dg = dt + (size_t)g * NB * kThreads;
-#pragma unroll
-    for (int j = 0; j < H; ++j) {
-      const uint32_t dst = (uint32_t)__cvta_generic_to_shared(&sd[buf][j][threadIdx.x]);
-      asm volatile("cp.async.ca.shared.global [%0], [%1], 8;\n" ::"r"(dst), "l"(dg + (size_t)j * kThreads));
-    }
-    asm volatile("cp.async.commit_group;\n" ::);
-  };
-  const double qd = (double)mods[l].q, qinv = 1.0 / qd;
-  prefetch(0, 0);
-  for (int g = 0; g < n2; ++g) {
-    if (g + 1 < n2) {
-      prefetch(g + 1, (g + 1) & 1);
-      asm volatile("cp.async.wait_group 1;\n" ::);
-    } else {
-      asm volatile("cp.async.wait_group 0;\n" ::);
-    }
-    const int buf = g & 1;
-    double a0 = 0.0, a1 = 0.0;
-#pragma unroll
-    for (int j = 0; j < H; ++j) {
-      const double d = sd[buf][j][threadIdx.x];
-      a0 = __dadd_rn(a0, fp_mod_product(d, b0[j], qd, qinv));
-      a1 = __dadd_rn(a1, fp_mod_product(d, b1[j], qd, qinv));
-      if ((j & 3) == 3) {
-        a0 = fp_center(a0, qd, qinv);
-        a1 = fp_center(a1, qd, qinv);
-      }
-    }
-    // |a| < 0.51 q per lane: sums of up to eight lanes stay exact (< 4.1 q)
-#pragma unroll
-    for (int m = 1; m < kBsgsSplit; m <<= 1) {
-      a0 = __dadd_rn(a0, __shfl_xor_sync(0xffffffffu, a0, m));
-      a1 = __dadd_rn(a1, __shfl_xor_sync(0xffffffffu, a1, m));
-    }
-    if (half < 2) {
-      uint64_t* dst = half == 0 ? out.c0[q][g] : out.c1[q][g];
-      uint64_t r = fp_canonical(fp_center(half == 0 ? a0 : a1, qd, qinv), qd);
-      if (accumulate) r = ckks::add_mod(r, dst[off], mods[l].q);
-      dst[off] = r;
-    }
+  __device__ __forceinline__ uint64_t reduce(const ckks::Mod& m) const {
+    constexpr int SB = kSplitBits;
+    ckks::U128 x{lo, 0};
+    ckks::add_wide(x, ckks::U128{mid << SB, mid >> (64 - SB)});
+    ckks::add_wide(x, ckks::U128{mid2 << SB, mid2 >> (64 - SB)});
+    ckks::add_wide(x, ckks::U128{hi << (2 * SB), hi >> (64 - 2 * SB)});
+    return ckks::reduce128(x, m);
   }
+};
+
+__device__ __forceinline__ void split_residue(uint64_t v, uint32_t& l, uint32_t& h) {
+  l = (uint32_t)v & ((1u << kSplitBits) - 1u);
+  h = (uint32_t)(v >> kSplitBits);
 }
 
-// The same structure for a limb whose prime is too large for the float64
-// products (the 60-bit first prime): 64-bit baby residues in registers,
-// 128-bit multiply-accumulate chains, the lane pair's sums added as 128-bit
-// values (each below 2^124) and reduced once.
-template <int NB>
-__device__ __forceinline__ void bsgs_inner_reg_int(const BabyPtrs& babies, int ng, const uint64_t* __restrict__ diag,
-                                                   const InnerPtrs& out, int logN, int n2, int l, bool accumulate,
-                                                   const ckks::Mod* __restrict__ mods,
-                                                   uint64_t (*sd)[NB / kBsgsSplit][kBsgsRegThreads]) {
-  constexpr int H = NB / kBsgsSplit;
+template <int NB, int SPLIT, int CHAINS, int MINB, bool FP>
+__global__ void __launch_bounds__(kBsgsRegThreads, MINB)
+    bsgs_inner_reg_kernel(BabyPtrs babies, int ng, const uint64_t* __restrict__ diag, InnerPtrs out, int logN, int n2,
+                          int l0, bool accumulate, const ckks::Mod* __restrict__ mods) {
+  using S = BsgsShape<NB, SPLIT>;
+  constexpr int H = S::H;
+  static_assert(FP || H <= 16, "at most 16 split products per sum");
+  static_assert(!FP || (H % CHAINS == 0 && (H / CHAINS) % 4 == 0), "whole groups of four products per chain");
+  static_assert(SPLIT >= 2, "one lane writes c0, another c1");
+  __shared__ uint64_t sd[2][H][kBsgsRegThreads];
   const int N = 1 << logN;
+  const int l = l0 + blockIdx.z;
   const int q = blockIdx.x % ng, part = blockIdx.x / ng;
   const int tile = blockIdx.y;
-  const int half = threadIdx.x % kBsgsSplit;
-  const int c = part * kBsgsRegCoeffs + threadIdx.x / kBsgsSplit;
+  const int lane = threadIdx.x % SPLIT;
+  const int c = part * S::kCoeffs + threadIdx.x / SPLIT;  // coefficient within the tile
   const size_t off = (size_t)l * N + (size_t)tile * kThreads + c;
-  uint64_t b0[H], b1[H];
+  // babies: doubles (FP) or 30-bit halves
+  double b0d[FP ? H : 1], b1d[FP ? H : 1];
+  uint32_t b0l[FP ? 1 : H], b0h[FP ? 1 : H], b1l[FP ? 1 : H], b1h[FP ? 1 : H];
 #pragma unroll
   for (int j = 0; j < H; ++j) {
-    b0[j] = babies.c0[q][half * H + j][off];
-    b1[j] = babies.c1[q][half * H + j][off];
+    const uint64_t v0 = babies.c0[q][lane * H + j][off], v1 = babies.c1[q][lane * H + j][off];
+    if constexpr (FP) {
+      b0d[j] = u2d(v0);
+      b1d[j] = u2d(v1);
+    } else {
+      split_residue(v0, b0l[j], b0h[j]);
+      split_residue(v1, b1l[j], b1h[j]);
+    }
   }
   const uint64_t* dt =
-      diag + ((size_t)l * (N / kThreads) + tile) * (size_t)(NB * n2) * kThreads + (size_t)half * H * kThreads + c;
+      diag + ((size_t)l * (N / kThreads) + tile) * (size_t)(NB * n2) * kThreads + (size_t)lane * H * kThreads + c;
+  // the next giant step's diagonals stream into this thread's own
+  // shared-memory slots while the current one is computed (each thread
+  // reads only what it copied, so no barrier)
   auto prefetch = [&](int g, int buf) {
     const uint64_t* dg = dt + (size_t)g * NB * kThreads;
 #pragma unroll
@@ -372,6 +357,7 @@ __device__ __forceinline__ void bsgs_inner_reg_int(const BabyPtrs& babies, int n
     asm volatile("cp.async.commit_group;\n" ::);
   };
   const ckks::Mod m = mods[l];
+  const double qd = (double)m.q, qinv = 1.0 / qd;
   prefetch(0, 0);
   for (int g = 0; g < n2; ++g) {
     if (g + 1 < n2) {
@@ -381,46 +367,85 @@ __device__ __forceinline__ void bsgs_inner_reg_int(const BabyPtrs& babies, int n
       asm volatile("cp.async.wait_group 0;\n" ::);
     }
     const int buf = g & 1;
-    ckks::U128 a0{0, 0}, a1{0, 0};
+    uint64_t r0, r1;
+    if constexpr (FP) {
+      double a0[CHAINS], a1[CHAINS];
 #pragma unroll
-    for (int j = 0; j < H; ++j) {
-      const uint64_t d = sd[buf][j][threadIdx.x];
-      ckks::mac_wide(a0, d, b0[j]);
-      ckks::mac_wide(a1, d, b1[j]);
-    }
+      for (int k = 0; k < CHAINS; ++k) a0[k] = a1[k] = 0.0;
 #pragma unroll
-    for (int s = 1; s < kBsgsSplit; s <<= 1) {
-      ckks::add_wide(a0, ckks::U128{__shfl_xor_sync(0xffffffffu, a0.lo, s), __shfl_xor_sync(0xffffffffu, a0.hi, s)});
-      ckks::add_wide(a1, ckks::U128{__shfl_xor_sync(0xffffffffu, a1.lo, s), __shfl_xor_sync(0xffffffffu, a1.hi, s)});
+      for (int j = 0; j < H; ++j) {
+        const int k = j % CHAINS;
+        const double d = __longlong_as_double((long long)sd[buf][j][threadIdx.x]);
+        a0[k] = __dadd_rn(a0[k], fp_mod_product(d, b0d[j], qd, qinv));
+        a1[k] = __dadd_rn(a1[k], fp_mod_product(d, b1d[j], qd, qinv));
+        if ((j / CHAINS) % 4 == 3) {  // four products since this chain's last re-centring
+          a0[k] = fp_center(a0[k], qd, qinv);
+          a1[k] = fp_center(a1[k], qd, qinv);
+        }
+      }
+      // |a[k]| < 0.51 q: the chains and lanes add up to < 0.51 q CHAINS
+      // SPLIT <= 4.1 q, exact
+      double t0 = a0[0], t1 = a1[0];
+#pragma unroll
+      for (int k = 1; k < CHAINS; ++k) {
+        t0 = __dadd_rn(t0, a0[k]);
+        t1 = __dadd_rn(t1, a1[k]);
+      }
+#pragma unroll
+      for (int sh = 1; sh < SPLIT; sh <<= 1) {
+        t0 = __dadd_rn(t0, __shfl_xor_sync(0xffffffffu, t0, sh));
+        t1 = __dadd_rn(t1, __shfl_xor_sync(0xffffffffu, t1, sh));
+      }
+      const double t = lane == 0 ? t0 : t1;
+      r0 = r1 = fp_canonical(fp_center(t, qd, qinv), qd);
+    } else {
+      SplitSums s0, s1;
+#pragma unroll
+      for (int j = 0; j < H; ++j) {
+        uint32_t dl, dh;
+        split_residue(sd[buf][j][threadIdx.x], dl, dh);
+        s0.mac(dl, dh, b0l[j], b0h[j]);
+        s1.mac(dl, dh, b1l[j], b1h[j]);
+      }
+      r0 = s0.reduce(m);
+      r1 = s1.reduce(m);
+#pragma unroll
+      for (int sh = 1; sh < SPLIT; sh <<= 1) {
+        r0 = ckks::add_mod(r0, __shfl_xor_sync(0xffffffffu, r0, sh), m.q);
+        r1 = ckks::add_mod(r1, __shfl_xor_sync(0xffffffffu, r1, sh), m.q);
+      }
     }
-    if (half < 2) {
-      uint64_t* dst = half == 0 ? out.c0[q][g] : out.c1[q][g];
-      uint64_t r = ckks::reduce128(half == 0 ? a0 : a1, m);
+    if (lane < 2) {
+      uint64_t* dst = lane == 0 ? out.c0[q][g] : out.c1[q][g];
+      uint64_t r = lane == 0 ? r0 : r1;
       if (accumulate) r = ckks::add_mod(r, dst[off], m.q);
       dst[off] = r;
     }
   }
 }
 
-// Inner sums over limbs l0 .. l0 + gridDim.z - 1 in one grid: each CTA takes
-// the float64 products when its limb's prime allows them and the 128-bit
-// integer chains otherwise, so the 60-bit first limb's CTAs (launched first,
-// about 2.7x the work of a float64 limb) run beside the others instead of in
-// a launch of their own, on the integer pipe while the others use FP64.
+// Inner sums of one product term over limbs [0, limbs): each run of limbs
+// whose primes allow float64 products goes to the FP instance, each other
+// run (the 60-bit first prime) to the all-integer one.
 template <int NB>
-__global__ void __launch_bounds__(kBsgsRegThreads, NB >= 32 ? 3 : 4) bsgs_inner_reg_kernel(BabyPtrs babies, int ng,
-                                                                              const uint64_t* __restrict__ diag,
-                                                                              InnerPtrs out, int logN, int n2, int l0,
-                                                                              bool accumulate,
-                                                                              const ckks::Mod* __restrict__ mods) {
-  constexpr int H = NB / kBsgsSplit;
-  __shared__ uint64_t sd[2][H][kBsgsRegThreads];
-  const int l = l0 + blockIdx.z;
-  if (mods[l].q < kFpPrime)
-    bsgs_inner_reg_fp<NB>(babies, ng, diag, out, logN, n2, l, accumulate, mods,
-                          reinterpret_cast<double (*)[H][kBsgsRegThreads]>(sd));
-  else
-    bsgs_inner_reg_int<NB>(babies, ng, diag, out, logN, n2, l, accumulate, mods, sd);
+void launch_bsgs_inner_reg(const ckks::Context& C, const BabyPtrs& bp, int ng, const uint64_t* dg, const InnerPtrs& ip,
+                           int limbs, int n2, bool acc) {
+  using S = BsgsShape<NB, kRegSplit>;
+  static_assert(kThreads % S::kCoeffs == 0, "a tile of whole CTAs");
+  constexpr int CH = S::H / 4 < kFpChains ? S::H / 4 : kFpChains;
+  for (int l0 = 0; l0 < limbs;) {
+    const bool fp = C.moduli[l0] < kFpPrime;
+    int l1 = l0 + 1;
+    while (l1 < limbs && (C.moduli[l1] < kFpPrime) == fp) ++l1;
+    const dim3 grid(ng * S::kParts, C.N / kThreads, l1 - l0);
+    if (fp)
+      bsgs_inner_reg_kernel<NB, kRegSplit, CH, kRegMinBlocks, true>
+          <<<grid, kBsgsRegThreads, 0, C.stream>>>(bp, ng, dg, ip, C.logN, n2, l0, acc, C.d_mods);
+    else
+      bsgs_inner_reg_kernel<NB, kRegSplit, CH, kRegMinBlocks, false>
+          <<<grid, kBsgsRegThreads, 0, C.stream>>>(bp, ng, dg, ip, C.logN, n2, l0, acc, C.d_mods);
+    l0 = l1;
+  }
 }
 
 // ---- client-side float64 transforms, on the device ------------------------
@@ -649,17 +674,18 @@ std::vector<Ciphertext> bsgs_products(ckks_b200::CryptoContextImpl& cc, ckks::Co
           C, "bsgs_inner",
           ((double)n1 * n2 * limbs + ng * (2.0 * n1 * limbs + (acc ? 4.0 : 2.0) * n2 * limbs)) * C.limb_bytes(),
           C.stream);
-      if (n1 == 32 || n1 == 16 || n1 == 8) {
-        // every limb in one grid, each CTA on its limb's path
-        static_assert(kThreads % kBsgsRegCoeffs == 0, "a tile of whole CTAs");
-        const dim3 rgrid(ng * (kThreads / kBsgsRegCoeffs), C.N / kThreads, limbs);
-        auto kern = n1 == 32 ? bsgs_inner_reg_kernel<32> : n1 == 16 ? bsgs_inner_reg_kernel<16>
-                                                                    : bsgs_inner_reg_kernel<8>;
-        kern<<<rgrid, kBsgsRegThreads, 0, C.stream>>>(bp, ng, dg, ip, C.logN, n2, 0, acc, C.d_mods);
-      }
+      // the split products of the integer instance need primes below 2^60
+      bool reg = n1 == 32 || n1 == 16 || n1 == 8;
+      for (int l = 0; l < limbs; ++l) reg = reg && C.moduli[l] < (1ull << 60);
+      if (reg && n1 == 32)
+        launch_bsgs_inner_reg<32>(C, bp, ng, dg, ip, limbs, n2, acc);
+      else if (reg && n1 == 16)
+        launch_bsgs_inner_reg<16>(C, bp, ng, dg, ip, limbs, n2, acc);
+      else if (reg)
+        launch_bsgs_inner_reg<8>(C, bp, ng, dg, ip, limbs, n2, acc);
       // generic n1: runs of limbs with primes below kFpPrime take the
       // float64 products, the others (the 60-bit first prime) the integer ones
-      for (int l0 = 0; l0 < limbs && !(n1 == 32 || n1 == 16 || n1 == 8);) {
+      for (int l0 = 0; l0 < limbs && !reg;) {
         const bool fp = C.moduli[l0] < kFpPrime;
         int l1 = l0 + 1;
         while (l1 < limbs && (C.moduli[l1] < kFpPrime) == fp) ++l1;

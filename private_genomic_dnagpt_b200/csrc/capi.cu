@@ -655,7 +655,34 @@ double ckks_ctx_scale(const ckks_ctx* ctx, int level) {
 }
 
 int ckks_sync(ckks_ctx* ctx) {
-  return guard([&] { CKKS_CUDA(cudaStreamSynchronize(C(ctx).stream)); });
+  return guard([&] {
+    Context& c = C(ctx);
+    CKKS_CUDA(cudaStreamSynchronize(c.stream));
+    const unsigned int f = ckks::take_device_faults(c);
+    if (f)
+      throw Error(CKKS_ECUDA, std::to_string(f) +
+                                  " bounded device wait(s) gave up (a bulk copy into shared memory did not complete); "
+                                  "the outputs since the last synchronisation are not valid");
+  });
+}
+
+int ckks_selftest_bulk_wait(ckks_ctx* ctx, int starve) {
+  return guard([&] {
+    Context& c = C(ctx);
+    constexpr int kWords = 512;
+    std::vector<uint64_t> h(kWords), back(kWords, 0);
+    for (int i = 0; i < kWords; ++i) h[i] = 0x9e3779b97f4a7c15ull * (uint64_t)(i + 1);
+    uint64_t* d = (uint64_t*)c.alloc(2 * kWords * sizeof(uint64_t));
+    CKKS_CUDA(cudaMemcpyAsync(d, h.data(), kWords * sizeof(uint64_t), cudaMemcpyHostToDevice, c.stream));
+    CKKS_CUDA(cudaMemsetAsync(d + kWords, 0, kWords * sizeof(uint64_t), c.stream));
+    ckks::bulk_wait_probe(c, d, d + kWords, starve != 0, c.stream);
+    CKKS_CUDA(cudaMemcpyAsync(back.data(), d + kWords, kWords * sizeof(uint64_t), cudaMemcpyDeviceToHost, c.stream));
+    CKKS_CUDA(cudaStreamSynchronize(c.stream));
+    c.release(d);
+    const unsigned int f = ckks::take_device_faults(c);
+    if (f) throw Error(CKKS_ECUDA, "bounded bulk-copy wait gave up");
+    need(back == h, CKKS_ECUDA, "bulk copy through shared memory returned different data");
+  });
 }
 
 void* ckks_ctx_stream(ckks_ctx* ctx) { return (ctx && ctx->c) ? (void*)ctx->c->stream : nullptr; }

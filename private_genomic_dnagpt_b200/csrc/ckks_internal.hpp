@@ -167,6 +167,7 @@ class Context {
 
   // device tables
   Mod* d_mods = nullptr;            // [P]
+  unsigned int* d_faults = nullptr;  // bounded device waits that gave up (bulk copies)
   ulonglong2* d_tw = nullptr;       // [P][N] forward (w, w')
   ulonglong2* d_itw = nullptr;      // [P][N] inverse (w, w')
   double2* d_twd = nullptr;         // [P][N] forward (w, fl(w/q)) as doubles (primes below 2^50.3)
@@ -393,6 +394,14 @@ struct KsBatch {
   int M;
 };
 void keyswitch_batch(const Context& c, int limbs, const KsBatch& b, bool shared_input, cudaStream_t st);
+// Count of bounded device waits that gave up since the last call (each
+// leaves its CTA's outputs unwritten), read after the stream drains and
+// reset to zero.
+unsigned int take_device_faults(const Context& c);
+// One CTA stages 4 KiB of src through a bulk copy and writes it to dst;
+// with `starve` its barrier expects twice the bytes copied, so its wait
+// runs out and counts one fault (tests of the bounded wait).
+void bulk_wait_probe(const Context& c, const uint64_t* src, uint64_t* dst, bool starve, cudaStream_t st);
 // Hoisted rotations of G inputs (d = c1 pointers, c0 = their c0) by the same
 // R rotations (h): one ModUp per input, then the key products and ModDowns of
 // up to 32 (input, rotation) items per launch sequence, the items of one key

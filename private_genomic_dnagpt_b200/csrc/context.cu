@@ -234,6 +234,8 @@ Context::Context(const Params& p) : params(p) {
     pmod[i] = shoup_pair(i < L ? pm : 0, q);
   }
   d_mods = upload(mods);
+  CKKS_CUDA(cudaMalloc(&d_faults, sizeof(unsigned int)));
+  CKKS_CUDA(cudaMemset(d_faults, 0, sizeof(unsigned int)));
   d_tw = upload(tw);
   d_itw = upload(itw);
   d_twd = upload(twd);
@@ -418,6 +420,7 @@ Context::~Context() {
   for (auto& kv : rot_keys_low) cudaFree(kv.second);
   cudaFree(d_rlk_low);
   cudaFree(d_mods);
+  cudaFree(d_faults);
   cudaFree(d_tw);
   cudaFree(d_itw);
   cudaFree(d_twd);

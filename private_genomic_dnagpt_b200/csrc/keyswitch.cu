@@ -806,7 +806,186 @@ __global__ void __launch_bounds__(kThreads) ks_inner_multi_kernel(KsBatch b, con
       make_ulonglong2(reduce128(b0, md), reduce128(b1, md));
 }
 
+// ---- key products with bulk-copied operands ---------------------------------
+// The 2 kThreads outputs of one CTA read, per digit, 2 kThreads residues of
+// each key half at the outputs' own positions and the ModUp residues at the
+// automorphism's sources.  Those sources are one aligned span of the same
+// size: with k = hi 2^9 + lo, the varying low bits lo of the output become
+// the top bits of e = 2 bitrev(k) + 1, e g (g odd) runs over every value of
+// those bits, and the bit reversal brings them back to the low bits of the
+// source, while the high bits stay fixed by hi.  So one thread issues 3 beta
+// contiguous 4 KiB copies (cp.async.bulk, completing on one mbarrier) and
+// the products read shared memory only.
+constexpr int kSpan = 2 * kThreads;
+constexpr uint32_t kSpanBytes = kSpan * sizeof(uint64_t);
+constexpr uint64_t kBulkWaitNs = 1000000000ull;  // one second
+
+__device__ __forceinline__ uint32_t smem_addr(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
+
+__device__ __forceinline__ uint64_t global_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+__device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count) : "memory");
+  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+
+__device__ __forceinline__ void mbar_expect_tx(uint32_t bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
+}
+
+__device__ __forceinline__ void bulk_load(uint32_t dst, const void* src, uint32_t bytes, uint32_t bar) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(dst),
+               "l"(src), "r"(bytes), "r"(bar)
+               : "memory");
+}
+
+__device__ __forceinline__ bool mbar_test(uint32_t bar, uint32_t parity) {
+  uint32_t done;
+  asm volatile(
+      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
+      : "=r"(done)
+      : "r"(bar), "r"(parity)
+      : "memory");
+  return done != 0;
+}
+
+// waits for the barrier's phase `parity` to complete; gives up after
+// kBulkWaitNs of global time or 2^22 polls, whichever comes first
+__device__ __forceinline__ bool mbar_wait_bounded(uint32_t bar, uint32_t parity) {
+  const uint64_t t0 = global_ns();
+  for (uint32_t i = 0; i < (1u << 22); ++i) {
+    if (mbar_test(bar, parity)) return true;
+    if ((i & 31u) == 31u && global_ns() - t0 > kBulkWaitNs) return false;
+  }
+  return false;
+}
+
+// BULK_MULTI false: item m = blockIdx.z, ModUp output per item unless
+// `shared` (keyswitch_batch's grid); true: item m = blockIdx.x with the ModUp
+// output of input b.src[m] (keyswitch_hoisted_multi's grid, the items of one
+// key adjacent).
+template <int BETA, bool BULK_MULTI>
+__global__ void __launch_bounds__(kThreads) ks_inner_bulk_kernel(KsBatch b, const uint64_t* __restrict__ ext_all,
+                                                                 bool shared, uint64_t* __restrict__ acc_all,
+                                                                 int limbs, int L, int K, int P, int logN,
+                                                                 const Mod* __restrict__ mods,
+                                                                 unsigned int* __restrict__ faults) {
+  __shared__ alignas(128) uint64_t sx[BETA][kSpan];
+  __shared__ alignas(128) uint64_t sk[BETA][2][kSpan];
+  __shared__ alignas(8) uint64_t bar;
+  const int N = 1 << logN;
+  const int m = BULK_MULTI ? blockIdx.x : blockIdx.z;
+  const int n0 = (BULK_MULTI ? blockIdx.y : blockIdx.x) * kSpan;
+  const int t = BULK_MULTI ? blockIdx.z : blockIdx.y;
+  const int E = limbs + K;
+  const int pt = t < limbs ? t : L + (t - limbs);
+  const uint32_t g = b.g[m];
+  const uint64_t* ext =
+      ext_all + (BULK_MULTI ? (size_t)b.src[m] * BETA * E * N : (shared ? 0 : (size_t)m * BETA * E * N));
+  const uint64_t* key = b.key[m];
+  const uint32_t s0 = g == 1u ? (uint32_t)n0 : auto_index((uint32_t)n0, g, logN) & ~(uint32_t)(kSpan - 1);
+  const uint32_t mb = smem_addr(&bar);
+  if (threadIdx.x == 0) mbar_init(mb, 1);
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    mbar_expect_tx(mb, 3u * BETA * kSpanBytes);
+#pragma unroll
+    for (int j = 0; j < BETA; ++j) {
+      bulk_load(smem_addr(sx[j]), ext + ((size_t)j * E + t) * N + s0, kSpanBytes, mb);
+      bulk_load(smem_addr(sk[j][0]), key + ((size_t)j * 2 * P + pt) * N + n0, kSpanBytes, mb);
+      bulk_load(smem_addr(sk[j][1]), key + ((size_t)j * 2 * P + P + pt) * N + n0, kSpanBytes, mb);
+    }
+  }
+  if (!mbar_wait_bounded(mb, 0)) {
+    // record it for the host, give the copies one more bounded wait, and
+    // leave this CTA's outputs unwritten
+    if (threadIdx.x == 0) atomicAdd(faults, 1u);
+    mbar_wait_bounded(mb, 0);
+    return;
+  }
+  const int i = 2 * threadIdx.x, n = n0 + i;
+  const uint32_t src = g == 1u ? (uint32_t)n : auto_index((uint32_t)n, g, logN);
+  const uint32_t so = (src & ~1u) & (uint32_t)(kSpan - 1);  // = (src & ~1) - s0
+  const bool swap = src & 1u;
+  U128 a0{0, 0}, a1{0, 0}, b0{0, 0}, b1{0, 0};
+#pragma unroll
+  for (int j = 0; j < BETA; ++j) {
+    const ulonglong2 v = *reinterpret_cast<const ulonglong2*>(&sx[j][so]);
+    const ulonglong2 k0 = *reinterpret_cast<const ulonglong2*>(&sk[j][0][i]);
+    const ulonglong2 k1 = *reinterpret_cast<const ulonglong2*>(&sk[j][1][i]);
+    const uint64_t v0 = swap ? v.y : v.x, v1 = swap ? v.x : v.y;
+    mac_wide(a0, v0, k0.x);
+    mac_wide(a1, v1, k0.y);
+    mac_wide(b0, v0, k1.x);
+    mac_wide(b1, v1, k1.y);
+  }
+  const Mod md = mods[pt];
+  uint64_t* acc = acc_all + (size_t)m * 2 * E * N;
+  *reinterpret_cast<ulonglong2*>(acc + (size_t)t * N + n) = make_ulonglong2(reduce128(a0, md), reduce128(a1, md));
+  *reinterpret_cast<ulonglong2*>(acc + ((size_t)E + t) * N + n) =
+      make_ulonglong2(reduce128(b0, md), reduce128(b1, md));
+}
+
+// one CTA stages a span whose barrier expects `expect` bytes while `issue`
+// bytes are copied: with expect > issue the wait runs out (the barrier is
+// never completed) and the fault counter records it, which is how the
+// bounded wait is tested without a fault
+__global__ void bulk_wait_probe_kernel(const uint64_t* __restrict__ src, uint64_t* __restrict__ dst, uint32_t issue,
+                                       uint32_t expect, unsigned int* __restrict__ faults) {
+  __shared__ alignas(128) uint64_t sx[kSpan];
+  __shared__ alignas(8) uint64_t bar;
+  const uint32_t mb = smem_addr(&bar);
+  if (threadIdx.x == 0) mbar_init(mb, 1);
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    mbar_expect_tx(mb, expect);
+    if (issue) bulk_load(smem_addr(sx), src, issue, mb);
+  }
+  if (!mbar_wait_bounded(mb, 0)) {
+    if (threadIdx.x == 0) atomicAdd(faults, 1u);
+    mbar_wait_bounded(mb, 0);
+    return;
+  }
+  for (uint32_t k = threadIdx.x; k < issue / sizeof(uint64_t); k += blockDim.x) dst[k] = sx[k];
+}
+
+bool bulk_inner_fits(const Context& c, int beta) { return beta >= 1 && beta <= 3 && c.N >= 2 * kSpan; }
+
+void launch_ks_inner_bulk(const Context& c, bool multi, dim3 grid, const KsBatch& b, const uint64_t* ext, bool shared,
+                          uint64_t* acc, int limbs, int beta, cudaStream_t st) {
+#define CKKS_BULK_LAUNCH(BETA)                                                                                   \
+  (multi ? ks_inner_bulk_kernel<BETA, true> : ks_inner_bulk_kernel<BETA, false>)<<<grid, kThreads, 0, st>>>( \
+      b, ext, shared, acc, limbs, c.L, c.Kx(limbs), c.P, c.logN, c.d_mods, c.d_faults)
+  switch (beta) {
+    case 1: CKKS_BULK_LAUNCH(1); break;
+    case 2: CKKS_BULK_LAUNCH(2); break;
+    default: CKKS_BULK_LAUNCH(3); break;
+  }
+#undef CKKS_BULK_LAUNCH
+}
+
 }  // namespace
+
+unsigned int take_device_faults(const Context& c) {
+  unsigned int v = 0;
+  CKKS_CUDA(cudaMemcpyAsync(&v, c.d_faults, sizeof(v), cudaMemcpyDeviceToHost, c.stream));
+  CKKS_CUDA(cudaStreamSynchronize(c.stream));
+  if (v) {
+    CKKS_CUDA(cudaMemsetAsync(c.d_faults, 0, sizeof(unsigned int), c.stream));
+    CKKS_CUDA(cudaStreamSynchronize(c.stream));
+  }
+  return v;
+}
+
+void bulk_wait_probe(const Context& c, const uint64_t* src, uint64_t* dst, bool starve, cudaStream_t st) {
+  bulk_wait_probe_kernel<<<1, kThreads, 0, st>>>(src, dst, kSpanBytes, starve ? 2 * kSpanBytes : kSpanBytes,
+                                                 c.d_faults);
+  CKKS_CUDA(cudaGetLastError());
+}
 
 void keyswitch_batch(const Context& c, int limbs, const KsBatch& b, bool shared, cudaStream_t st) {
   if (c.alpha > kMaxAlpha || c.Kx(limbs) > kMaxK) throw Error(kErrArgument, "digit size above 16 is not supported");
@@ -850,8 +1029,11 @@ void keyswitch_batch(const Context& c, int limbs, const KsBatch& b, bool shared,
   // key inner products
   {
     ProfScope ps(c, "ks_inner", M * (2.0 * lt.beta * E + 2.0 * E) * lb + Mu * (double)lt.beta * E * lb, st);
-    ks_inner_batch_kernel<<<dim3((N / 2 + kThreads - 1) / kThreads, E, M), kThreads, 0, st>>>(
-        b, ext, shared, acc, limbs, c.L, c.Kx(limbs), c.P, lt.beta, c.logN, c.d_mods);
+    if (bulk_inner_fits(c, lt.beta))
+      launch_ks_inner_bulk(c, false, dim3(N / kSpan, E, M), b, ext, shared, acc, limbs, lt.beta, st);
+    else
+      ks_inner_batch_kernel<<<dim3((N / 2 + kThreads - 1) / kThreads, E, M), kThreads, 0, st>>>(
+          b, ext, shared, acc, limbs, c.L, c.Kx(limbs), c.P, lt.beta, c.logN, c.d_mods);
   }
   CKKS_CUDA(cudaGetLastError());
   // ModDown
@@ -948,8 +1130,11 @@ void keyswitch_hoisted_multi(const Context& c, int limbs, const uint64_t* const*
     {
       // acc writes, each key once, the gathered ext residues
       ProfScope ps(c, "ks_inner", (M * (2.0 * E + (double)lt.beta * E) + (r1 - r0) * 2.0 * lt.beta * E) * lb, st);
-      ks_inner_multi_kernel<<<dim3(M, (N / 2 + kThreads - 1) / kThreads, E), kThreads, 0, st>>>(
-          b, ext, acc, limbs, c.L, c.Kx(limbs), c.P, lt.beta, c.logN, c.d_mods);
+      if (bulk_inner_fits(c, lt.beta))
+        launch_ks_inner_bulk(c, true, dim3(M, N / kSpan, E), b, ext, false, acc, limbs, lt.beta, st);
+      else
+        ks_inner_multi_kernel<<<dim3(M, (N / 2 + kThreads - 1) / kThreads, E), kThreads, 0, st>>>(
+            b, ext, acc, limbs, c.L, c.Kx(limbs), c.P, lt.beta, c.logN, c.d_mods);
     }
     CKKS_CUDA(cudaGetLastError());
     {

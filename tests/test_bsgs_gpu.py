@@ -96,7 +96,7 @@ def check_products(o, cc, logN, limbs, n1, groups, terms, seed):
 def pair13():
     # 9 limbs: the 60-bit first prime (integer inner sums) and 8 primes of
     # ~50 bits (float64 inner sums); lane-shift keys for every delta
-    rot = set(bsgs_keys(1 << 13, 8)) | set(bsgs_keys(1 << 13, 4))
+    rot = set(bsgs_keys(1 << 13, 8)) | set(bsgs_keys(1 << 13, 4)) | set(bsgs_keys(1 << 13, 16))
     for dl in range(1, B):
         rot |= {dl, dl - B}
     return make_pair(13, 9, 3, 41, sorted(rot))
@@ -115,6 +115,13 @@ def test_bsgs_matmul_summed_terms_bit_exact(pair13):
     o, cc = pair13
     cc.set_encrypt_counter(0)
     check_products(o, cc, 13, limbs=7, n1=8, groups=4, terms=3, seed=2)
+
+
+def test_bsgs_matmul_n1_16_bit_exact(pair13):
+    # n1 = 16, n2 = 8: sixteen-baby register kernels, two summed terms
+    o, cc = pair13
+    cc.set_encrypt_counter(0)
+    check_products(o, cc, 13, limbs=9, n1=16, groups=3, terms=2, seed=5)
 
 
 def test_bsgs_matmul_generic_split_bit_exact(pair13):
