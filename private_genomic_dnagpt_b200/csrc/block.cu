@@ -44,6 +44,7 @@
 #include "../../include/ckks_b200.h"
 #include "../../include/ckks_b200.hpp"
 #include "capi_types.hpp"
+#include "bulk.cuh"
 #include "ckks_internal.hpp"
 
 using ckks_b200::Ciphertext;
@@ -145,29 +146,36 @@ __device__ __forceinline__ double u2d(uint64_t v) {
   return __dsub_rn(__longlong_as_double((long long)(v | 0x4330000000000000ull)), 4503599627370496.0);
 }
 
-// Encoded diagonals are stored tile-major, [limb][coefficient tile][diagonal]
-// [kThreads residues], so that one CTA of the product streams one contiguous
-// span: this transposes a chunk of plaintext-major encodings into place.
-// Limbs whose prime is below kFpPrime hold their residues as doubles.
+// Encoded diagonals are stored tile-major, [limb][tile of kDiagTile
+// coefficients][diagonal][kDiagTile residues], so that the n1 diagonals of
+// one giant step over the coefficients of one CTA of the product are one
+// contiguous span (16 KiB at n1 = 32), streamed by a single bulk copy: this
+// transposes a chunk of plaintext-major encodings into place.  Limbs whose
+// prime is below kFpPrime hold their residues as doubles.
+constexpr int kDiagTile = 64;
+
+// word offset of diagonal d, coefficient n of limb l in the tile-major store
+__host__ __device__ __forceinline__ size_t diag_offset(int l, int n, int d, int N, int ndiag) {
+  return (((size_t)l * (N / kDiagTile) + n / kDiagTile) * ndiag + d) * kDiagTile + n % kDiagTile;
+}
+
 __global__ void __launch_bounds__(kThreads) diag_tile_kernel(const uint64_t* __restrict__ src, int cnt, int d0,
                                                              int ndiag, int limbs, int logN,
                                                              const ckks::Mod* __restrict__ mods,
                                                              uint64_t* __restrict__ dst) {
   const int N = 1 << logN;
-  const int ntiles = N / kThreads;
-  const int tile = blockIdx.x, l = blockIdx.y, dd = blockIdx.z;
+  const int n = blockIdx.x * kThreads + threadIdx.x, l = blockIdx.y, dd = blockIdx.z;
   if (dd >= cnt) return;
-  uint64_t v = src[((size_t)dd * limbs + l) * N + (size_t)tile * kThreads + threadIdx.x];
+  uint64_t v = src[((size_t)dd * limbs + l) * N + n];
   if (mods[l].q < kFpPrime) v = (uint64_t)__double_as_longlong((double)v);
-  dst[(((size_t)l * ntiles + tile) * ndiag + (d0 + dd)) * kThreads + threadIdx.x] = v;
+  dst[diag_offset(l, n, d0 + dd, N, ndiag)] = v;
 }
 
 // inner_g = sum_j diag[g n1 + j] * baby_j.  One CTA = one giant step g, one
 // 256-coefficient tile of one limb; each thread owns two adjacent
 // coefficients (16-byte loads) and four 128-bit MAC chains, so the kernel
 // runs at full occupancy.  Consecutive CTAs share the tile, so the baby
-// residues they re-read stay in L2; each giant's 32 diagonals of the tile are
-// one contiguous 64 KiB span of the tile-major diagonal store.
+// residues they re-read stay in L2.
 constexpr int kBsgsThreads = 128;
 
 // inner sums of giant step g for `ng` token groups in one CTA of
@@ -184,12 +192,12 @@ __global__ void __launch_bounds__(kBsgsThreads * kMaxGroups) bsgs_inner_kernel(B
   const int c = 2 * threadIdx.x;  // coefficient within the tile
   const size_t off = (size_t)l * N + (size_t)tile * kThreads + c;
   const int ndiag = n1 * n2;
-  const uint64_t* dtile = diag + (((size_t)l * (N / kThreads) + tile) * ndiag + (size_t)g * n1) * kThreads + c;
+  const uint64_t* dtile = diag + diag_offset(l, tile * kThreads + c, g * n1, N, ndiag);
   ckks::U128 a00{0, 0}, a01{0, 0}, a10{0, 0}, a11{0, 0};
   for (int j = 0; j < n1; ++j) {
     const ulonglong2 b0 = *reinterpret_cast<const ulonglong2*>(babies.c0[q][j] + off);
     const ulonglong2 b1 = *reinterpret_cast<const ulonglong2*>(babies.c1[q][j] + off);
-    const ulonglong2 dv = __ldg(reinterpret_cast<const ulonglong2*>(dtile + (size_t)j * kThreads));
+    const ulonglong2 dv = __ldg(reinterpret_cast<const ulonglong2*>(dtile + (size_t)j * kDiagTile));
     ckks::mac_wide(a00, dv.x, b0.x);
     ckks::mac_wide(a01, dv.y, b0.y);
     ckks::mac_wide(a10, dv.x, b1.x);
@@ -222,14 +230,13 @@ __global__ void __launch_bounds__(kBsgsThreads * kMaxGroups) bsgs_inner_fp_kerne
   const int c = 2 * threadIdx.x;
   const size_t off = (size_t)l * N + (size_t)tile * kThreads + c;
   const int ndiag = n1 * n2;
-  const double* dtile = reinterpret_cast<const double*>(diag) +
-                        (((size_t)l * (N / kThreads) + tile) * ndiag + (size_t)g * n1) * kThreads + c;
+  const double* dtile = reinterpret_cast<const double*>(diag) + diag_offset(l, tile * kThreads + c, g * n1, N, ndiag);
   const double qd = (double)mods[l].q, qinv = 1.0 / qd;
   double a00 = 0.0, a01 = 0.0, a10 = 0.0, a11 = 0.0;
   for (int j = 0; j < n1; ++j) {
     const ulonglong2 b0 = *reinterpret_cast<const ulonglong2*>(babies.c0[q][j] + off);
     const ulonglong2 b1 = *reinterpret_cast<const ulonglong2*>(babies.c1[q][j] + off);
-    const double2 dv = __ldg(reinterpret_cast<const double2*>(dtile + (size_t)j * kThreads));
+    const double2 dv = __ldg(reinterpret_cast<const double2*>(dtile + (size_t)j * kDiagTile));
     a00 = __dadd_rn(a00, fp_mod_product(dv.x, u2d(b0.x), qd, qinv));
     a01 = __dadd_rn(a01, fp_mod_product(dv.y, u2d(b0.y), qd, qinv));
     a10 = __dadd_rn(a10, fp_mod_product(dv.x, u2d(b1.x), qd, qinv));
@@ -260,12 +267,15 @@ __global__ void __launch_bounds__(kBsgsThreads * kMaxGroups) bsgs_inner_fp_kerne
 
 // Inner sums with the baby residues held in registers: SPLIT lanes share
 // one coefficient of one token group and one limb, each holding n1 / SPLIT
-// of the babies, looping over the n2 giant steps and streaming their
-// diagonals (8-byte cp.async over the tile-major store, double-buffered in
-// shared memory); the lanes' sums meet by shuffles once per giant step.  The
-// CTAs of the token groups of one tile are adjacent in the grid, so each
-// diagonal tile comes from HBM once and from L2 for the other groups, and no
-// baby residue is read twice.
+// of the babies, looping over the n2 giant steps; the lanes' sums meet by
+// shuffles once per giant step.  Each giant step's diagonals over the CTA's
+// kDiagTile coefficients (one contiguous span of the tile-major store) come
+// in one bulk copy into a two-stage shared-memory ring: thread 0 issues the
+// copy of step g + 2 once every thread has passed step g's barrier, so the
+// copy of step g + 1 lands while step g computes.  The CTAs of the token
+// groups of one tile are adjacent in the grid, so each diagonal tile comes
+// from HBM once and from L2 for the other groups, and no baby residue is
+// read twice.
 //
 // On a limb whose prime is below kFpPrime every product is the exact
 // float64 one (fp_mod_product), summed in CHAINS independent accumulators
@@ -314,19 +324,24 @@ __device__ __forceinline__ void split_residue(uint64_t v, uint32_t& l, uint32_t&
 template <int NB, int SPLIT, int CHAINS, int MINB, bool FP>
 __global__ void __launch_bounds__(kBsgsRegThreads, MINB)
     bsgs_inner_reg_kernel(BabyPtrs babies, int ng, const uint64_t* __restrict__ diag, InnerPtrs out, int logN, int n2,
-                          int l0, bool accumulate, const ckks::Mod* __restrict__ mods) {
+                          int l0, bool accumulate, const ckks::Mod* __restrict__ mods,
+                          unsigned int* __restrict__ faults) {
   using S = BsgsShape<NB, SPLIT>;
   constexpr int H = S::H;
   static_assert(FP || H <= 16, "at most 16 split products per sum");
   static_assert(!FP || (H % CHAINS == 0 && (H / CHAINS) % 4 == 0), "whole groups of four products per chain");
   static_assert(SPLIT >= 2, "one lane writes c0, another c1");
-  __shared__ uint64_t sd[2][H][kBsgsRegThreads];
+  static_assert(S::kCoeffs == kDiagTile, "one CTA per tile of the diagonal store");
+  constexpr uint32_t kStepBytes = NB * kDiagTile * sizeof(uint64_t);
+  __shared__ alignas(128) uint64_t sd[2][NB][kDiagTile];
+  __shared__ alignas(8) uint64_t full[2];
   const int N = 1 << logN;
   const int l = l0 + blockIdx.z;
   const int q = blockIdx.x % ng, part = blockIdx.x / ng;
   const int tile = blockIdx.y;
   const int lane = threadIdx.x % SPLIT;
-  const int c = part * S::kCoeffs + threadIdx.x / SPLIT;  // coefficient within the tile
+  const int cc = threadIdx.x / SPLIT;                   // coefficient within the CTA's diagonal tile
+  const int c = part * S::kCoeffs + cc;                 // coefficient within the 256-coefficient tile
   const size_t off = (size_t)l * N + (size_t)tile * kThreads + c;
   // babies: doubles (FP) or 30-bit halves
   double b0d[FP ? H : 1], b1d[FP ? H : 1];
@@ -342,32 +357,29 @@ __global__ void __launch_bounds__(kBsgsRegThreads, MINB)
       split_residue(v1, b1l[j], b1h[j]);
     }
   }
-  const uint64_t* dt =
-      diag + ((size_t)l * (N / kThreads) + tile) * (size_t)(NB * n2) * kThreads + (size_t)lane * H * kThreads + c;
-  // the next giant step's diagonals stream into this thread's own
-  // shared-memory slots while the current one is computed (each thread
-  // reads only what it copied, so no barrier)
-  auto prefetch = [&](int g, int buf) {
-    const uint64_t* dg = dt + (size_t)g * NB * kThreads;
-#pragma unroll
-    for (int j = 0; j < H; ++j) {
-      const uint32_t dst = (uint32_t)__cvta_generic_to_shared(&sd[buf][j][threadIdx.x]);
-      asm volatile("cp.async.ca.shared.global [%0], [%1], 8;\n" ::"r"(dst), "l"(dg + (size_t)j * kThreads));
-    }
-    asm volatile("cp.async.commit_group;\n" ::);
+  // giant step g's span: diagonals g NB .. g NB + NB - 1 of this tile
+  const uint64_t* dt = diag + diag_offset(l, tile * kThreads + part * S::kCoeffs, 0, N, NB * n2);
+  const uint32_t bar0 = ckks::smem_addr(&full[0]), bar1 = ckks::smem_addr(&full[1]);
+  auto issue = [&](int g) {
+    const uint32_t bar = (g & 1) ? bar1 : bar0;
+    ckks::mbar_expect_tx(bar, kStepBytes);
+    ckks::bulk_load(ckks::smem_addr(&sd[g & 1][0][0]), dt + (size_t)g * NB * kDiagTile, kStepBytes, bar);
   };
+  if (threadIdx.x == 0) {
+    ckks::mbar_init(bar0, 1);
+    ckks::mbar_init(bar1, 1);
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    issue(0);
+    if (n2 > 1) issue(1);
+  }
   const ckks::Mod m = mods[l];
   const double qd = (double)m.q, qinv = 1.0 / qd;
-  prefetch(0, 0);
   for (int g = 0; g < n2; ++g) {
-    if (g + 1 < n2) {
-      prefetch(g + 1, (g + 1) & 1);
-      asm volatile("cp.async.wait_group 1;\n" ::);
-    } else {
-      asm volatile("cp.async.wait_group 0;\n" ::);
-    }
     const int buf = g & 1;
-    uint64_t r0, r1;
+    const bool arrived = ckks::mbar_wait_bounded(buf ? bar1 : bar0, (g >> 1) & 1);
+    uint64_t r0 = 0, r1 = 0;
     if constexpr (FP) {
       double a0[CHAINS], a1[CHAINS];
 #pragma unroll
@@ -375,7 +387,7 @@ __global__ void __launch_bounds__(kBsgsRegThreads, MINB)
 #pragma unroll
       for (int j = 0; j < H; ++j) {
         const int k = j % CHAINS;
-        const double d = __longlong_as_double((long long)sd[buf][j][threadIdx.x]);
+        const double d = __longlong_as_double((long long)sd[buf][lane * H + j][cc]);
         a0[k] = __dadd_rn(a0[k], fp_mod_product(d, b0d[j], qd, qinv));
         a1[k] = __dadd_rn(a1[k], fp_mod_product(d, b1d[j], qd, qinv));
         if ((j / CHAINS) % 4 == 3) {  // four products since this chain's last re-centring
@@ -403,7 +415,7 @@ __global__ void __launch_bounds__(kBsgsRegThreads, MINB)
 #pragma unroll
       for (int j = 0; j < H; ++j) {
         uint32_t dl, dh;
-        split_residue(sd[buf][j][threadIdx.x], dl, dh);
+        split_residue(sd[buf][lane * H + j][cc], dl, dh);
         s0.mac(dl, dh, b0l[j], b0h[j]);
         s1.mac(dl, dh, b1l[j], b1h[j]);
       }
@@ -415,6 +427,17 @@ __global__ void __launch_bounds__(kBsgsRegThreads, MINB)
         r1 = ckks::add_mod(r1, __shfl_xor_sync(0xffffffffu, r1, sh), m.q);
       }
     }
+    // every thread is done with this buffer: it takes step g + 2's copy
+    if (!__syncthreads_and(arrived)) {
+      // a copy did not arrive: count it, wait (bounded) for the copy still
+      // in flight, and leave this CTA's remaining outputs unwritten
+      if (threadIdx.x == 0) {
+        atomicAdd(faults, 1u);
+        if (g + 1 < n2) ckks::mbar_wait_bounded(buf ? bar0 : bar1, ((g + 1) >> 1) & 1);
+      }
+      return;
+    }
+    if (threadIdx.x == 0 && g + 2 < n2) issue(g + 2);
     if (lane < 2) {
       uint64_t* dst = lane == 0 ? out.c0[q][g] : out.c1[q][g];
       uint64_t r = lane == 0 ? r0 : r1;
@@ -440,10 +463,10 @@ void launch_bsgs_inner_reg(const ckks::Context& C, const BabyPtrs& bp, int ng, c
     const dim3 grid(ng * S::kParts, C.N / kThreads, l1 - l0);
     if (fp)
       bsgs_inner_reg_kernel<NB, kRegSplit, CH, kRegMinBlocks, true>
-          <<<grid, kBsgsRegThreads, 0, C.stream>>>(bp, ng, dg, ip, C.logN, n2, l0, acc, C.d_mods);
+          <<<grid, kBsgsRegThreads, 0, C.stream>>>(bp, ng, dg, ip, C.logN, n2, l0, acc, C.d_mods, C.d_faults);
     else
       bsgs_inner_reg_kernel<NB, kRegSplit, CH, kRegMinBlocks, false>
-          <<<grid, kBsgsRegThreads, 0, C.stream>>>(bp, ng, dg, ip, C.logN, n2, l0, acc, C.d_mods);
+          <<<grid, kBsgsRegThreads, 0, C.stream>>>(bp, ng, dg, ip, C.logN, n2, l0, acc, C.d_mods, C.d_faults);
     l0 = l1;
   }
 }
