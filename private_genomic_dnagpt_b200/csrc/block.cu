@@ -46,6 +46,7 @@
 #include "capi_types.hpp"
 #include "bulk.cuh"
 #include "ckks_internal.hpp"
+#include "fpmod.cuh"
 
 using ckks_b200::Ciphertext;
 using ckks_b200::Plaintext;
@@ -113,38 +114,11 @@ struct InnerPtrs {
   uint64_t* c1[kMaxGroups][kMaxBaby];
 };
 
-// Products of residues below kFpPrime are formed exactly in float64 (the
-// FP64 pipe sustains about twice the 64-bit integer multiply-add rate):
-// with d, b < q < 2^50.6 both exact doubles,
-//   hi = d*b (rounded), lo = fma(d, b, -hi)      d*b = hi + lo exactly, |lo| < 2^49
-//   k  = rint(hi / q) via fma(hi, 1/q, 1.5*2^52)  |k - d*b/q| < 1.05
-//   r  = fma(-k, q, hi) + lo                       exact, r = d*b mod q, |r| < 1.05 q
-// and sums of four such r (|sum| < 4.75 q < 2^53) are exact; each four
-// products the running sum is brought back to |acc| < 0.51 q the same way.
-constexpr uint64_t kFpPrime = (1ull << 50) + (1ull << 49);
-constexpr double kRoundMagic = 6755399441055744.0;  // 1.5 * 2^52
-
-__device__ __forceinline__ double fp_mod_product(double d, double b, double q, double qinv) {
-  const double hi = __dmul_rn(d, b);
-  const double lo = __fma_rn(d, b, -hi);
-  const double k = __dsub_rn(__fma_rn(hi, qinv, kRoundMagic), kRoundMagic);
-  return __dadd_rn(__fma_rn(-k, q, hi), lo);
-}
-
-__device__ __forceinline__ double fp_center(double acc, double q, double qinv) {
-  const double k = __dsub_rn(__fma_rn(acc, qinv, kRoundMagic), kRoundMagic);
-  return __fma_rn(-k, q, acc);
-}
-
-// |acc| < 0.51 q -> canonical residue
-__device__ __forceinline__ uint64_t fp_canonical(double acc, double q) {
-  return __double2ull_rn(acc < 0.0 ? __dadd_rn(acc, q) : acc);
-}
-
-// residue (< 2^52) -> the same integer as a double
-__device__ __forceinline__ double u2d(uint64_t v) {
-  return __dsub_rn(__longlong_as_double((long long)(v | 0x4330000000000000ull)), 4503599627370496.0);
-}
+using ckks::fp_canonical;
+using ckks::fp_center;
+using ckks::fp_mod_product;
+using ckks::kFpPrime;
+using ckks::u2d;
 
 // Encoded diagonals are stored tile-major, [limb][tile of kDiagTile
 // coefficients][diagonal][kDiagTile residues], so that the n1 diagonals of
@@ -295,31 +269,8 @@ struct BsgsShape {
   static constexpr int kParts = kThreads / kCoeffs;            // CTAs per coefficient tile and group
 };
 constexpr int kRegSplit = 2, kFpChains = 2, kRegMinBlocks = 4;
-constexpr int kSplitBits = 30;  // half width of the integer instance's split products
-
-// sums of products of residues split into halves below 2^kSplitBits
-struct SplitSums {
-  uint64_t lo = 0, mid = 0, mid2 = 0, hi = 0;
-  __device__ __forceinline__ void mac(uint32_t dl, uint32_t dh, uint32_t bl, uint32_t bh) {
-    lo += (uint64_t)dl * bl;
-    mid += (uint64_t)dl * bh;
-    mid2 += (uint64_t)dh * bl;
-    hi += (uint64_t)dh * bh;
-  }
-  __device__ __forceinline__ uint64_t reduce(const ckks::Mod& m) const {
-    constexpr int SB = kSplitBits;
-    ckks::U128 x{lo, 0};
-    ckks::add_wide(x, ckks::U128{mid << SB, mid >> (64 - SB)});
-    ckks::add_wide(x, ckks::U128{mid2 << SB, mid2 >> (64 - SB)});
-    ckks::add_wide(x, ckks::U128{hi << (2 * SB), hi >> (64 - 2 * SB)});
-    return ckks::reduce128(x, m);
-  }
-};
-
-__device__ __forceinline__ void split_residue(uint64_t v, uint32_t& l, uint32_t& h) {
-  l = (uint32_t)v & ((1u << kSplitBits) - 1u);
-  h = (uint32_t)(v >> kSplitBits);
-}
+using ckks::SplitSums;
+using ckks::split_residue;
 
 template <int NB, int SPLIT, int CHAINS, int MINB, bool FP>
 __global__ void __launch_bounds__(kBsgsRegThreads, MINB)
