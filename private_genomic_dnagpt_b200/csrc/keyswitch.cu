@@ -677,30 +677,70 @@ __global__ void __launch_bounds__(kThreads) rs_combine_batch_kernel(RsBatch b, c
 // hoisted sums: acc_m = sum_r sum_j ext_{m,j}[pi_r(n)] key_{r,j} -- the R
 // rotations of item m share its ModUp.  A thread owns one residue (n, t) of
 // kHoistItems items, so each key residue and automorphism index is loaded
-// once for them; 128-bit accumulators folded every `fold` products as in
-// ks_inner_sum_kernel.
+// once for them.
 constexpr int kHoistItems = 4;
 // Item i of rotation r reads its extended digits at ext_all + i * istride +
 // r * rstride: rstride = 0 for the rotations of one ModUp (hoisted sums),
 // one digit set for the giant steps of several groups (one ModUp per
 // rotated input).
-__global__ void __launch_bounds__(kThreads) ks_inner_hoist_kernel(HoistKeys h, const uint64_t* __restrict__ ext_all,
-                                                                  uint64_t* __restrict__ acc_all, int M, int limbs,
-                                                                  int L, int K, int P, int beta, int logN, int fold,
-                                                                  const Mod* __restrict__ mods, size_t istride,
-                                                                  size_t rstride) {
+// Products by the target prime: kHoistFp below kFpPrime (exact float64
+// products, sums re-centred every four steps), kHoistSplit below 2^60
+// (carry-free split products, reduced into a running residue every 16
+// steps), kHoistWide otherwise (128-bit multiply-accumulates folded to a
+// residue every `fold` rotations, so that at most 63 products are summed).
+// Each mode is its own kernel, launched over the limbs of the extended basis
+// whose primes take it (up to kTargetRuns runs of consecutive limbs, the
+// blockIdx.y-th of them in order), so each keeps its own register budget.
+enum { kHoistFp = 0, kHoistSplit = 1, kHoistWide = 2 };
+constexpr int kTargetRuns = 4;
+struct HoistTargets {
+  int start[kTargetRuns], len[kTargetRuns];
+  __device__ __forceinline__ int limb(int y) const {
+    int t = start[0] + y;
+#pragma unroll
+    for (int r = 0; r + 1 < kTargetRuns; ++r) {
+      if (y >= len[r]) {
+        y -= len[r];
+        t = start[r + 1] + y;
+      } else {
+        break;
+      }
+    }
+    return t;
+  }
+};
+
+template <int MODE>
+__global__ void __launch_bounds__(kThreads, MODE == kHoistSplit ? 2 : 3)
+    ks_inner_hoist_kernel(HoistKeys h, HoistTargets tl, const uint64_t* __restrict__ ext_all,
+                          uint64_t* __restrict__ acc_all, int M, int limbs, int L, int K, int P, int beta, int logN,
+                          int fold, const Mod* __restrict__ mods, size_t istride, size_t rstride) {
+  constexpr bool FP = MODE == kHoistFp;
+  constexpr bool SPLIT = MODE == kHoistSplit;
   const int N = 1 << logN;
   const int n = blockIdx.x * kThreads + threadIdx.x;
   if (n >= N) return;
-  const int t = blockIdx.y, m0 = blockIdx.z * kHoistItems;
+  const int t = tl.limb(blockIdx.y), m0 = blockIdx.z * kHoistItems;
   const int E = limbs + K;
   const int pt = t < limbs ? t : L + (t - limbs);
   const Mod md = mods[pt];
   const int cnt = min(kHoistItems, M - m0);
   const uint64_t* ext = ext_all + (size_t)m0 * istride + (size_t)t * N;
-  U128 s0[kHoistItems], s1[kHoistItems];
+  const double qd = (double)md.q, qinv = 1.0 / qd;
+  double f0[FP ? kHoistItems : 1], f1[FP ? kHoistItems : 1];
+  SplitSums z0[SPLIT ? kHoistItems : 1], z1[SPLIT ? kHoistItems : 1];
+  uint64_t r0[SPLIT ? kHoistItems : 1], r1[SPLIT ? kHoistItems : 1];
+  U128 w0[MODE == kHoistWide ? kHoistItems : 1], w1[MODE == kHoistWide ? kHoistItems : 1];
 #pragma unroll
-  for (int i = 0; i < kHoistItems; ++i) s0[i] = s1[i] = U128{0, 0};
+  for (int i = 0; i < kHoistItems; ++i) {
+    if constexpr (FP) {
+      f0[i] = f1[i] = 0.0;
+    } else if constexpr (SPLIT) {
+      r0[i] = r1[i] = 0;
+    } else {
+      w0[i] = w1[i] = U128{0, 0};
+    }
+  }
   // the (rotation, digit) steps in order, the next step's key residues and
   // ModUp residues loaded while the current one's products run
   const int steps = h.R * beta;
@@ -719,19 +759,54 @@ __global__ void __launch_bounds__(kThreads) ks_inner_hoist_kernel(HoistKeys h, c
   for (int x = 0; x < steps; ++x) {
     uint64_t nk0 = 0, nk1 = 0, nv[kHoistItems] = {};
     if (x + 1 < steps) load(x + 1, nk0, nk1, nv);
-#pragma unroll
-    for (int i = 0; i < kHoistItems; ++i) {
-      if (i < cnt) {
-        mac_wide(s0[i], v[i], k0);
-        mac_wide(s1[i], v[i], k1);
-      }
-    }
-    const int r = x / beta;
-    if (x - r * beta == beta - 1 && (r + 1) % fold == 0) {
+    if constexpr (FP) {
+      const double kd0 = u2d(k0), kd1 = u2d(k1);
 #pragma unroll
       for (int i = 0; i < kHoistItems; ++i) {
-        s0[i] = U128{reduce128(s0[i], md), 0};
-        s1[i] = U128{reduce128(s1[i], md), 0};
+        if (i < cnt) {
+          const double a = u2d(v[i]);
+          f0[i] = __dadd_rn(f0[i], fp_mod_product(a, kd0, qd, qinv));
+          f1[i] = __dadd_rn(f1[i], fp_mod_product(a, kd1, qd, qinv));
+          if ((x & 3) == 3) {
+            f0[i] = fp_center(f0[i], qd, qinv);
+            f1[i] = fp_center(f1[i], qd, qinv);
+          }
+        }
+      }
+    } else if constexpr (SPLIT) {
+      uint32_t kl0, kh0, kl1, kh1;
+      split_residue(k0, kl0, kh0);
+      split_residue(k1, kl1, kh1);
+#pragma unroll
+      for (int i = 0; i < kHoistItems; ++i) {
+        if (i < cnt) {
+          uint32_t vl, vh;
+          split_residue(v[i], vl, vh);
+          z0[i].mac(vl, vh, kl0, kh0);
+          z1[i].mac(vl, vh, kl1, kh1);
+          if ((x & 15) == 15) {
+            r0[i] = add_mod(r0[i], z0[i].reduce(md), md.q);
+            r1[i] = add_mod(r1[i], z1[i].reduce(md), md.q);
+            z0[i] = SplitSums{};
+            z1[i] = SplitSums{};
+          }
+        }
+      }
+    } else {
+#pragma unroll
+      for (int i = 0; i < kHoistItems; ++i) {
+        if (i < cnt) {
+          mac_wide(w0[i], v[i], k0);
+          mac_wide(w1[i], v[i], k1);
+        }
+      }
+      const int r = x / beta;
+      if (x - r * beta == beta - 1 && (r + 1) % fold == 0) {
+#pragma unroll
+        for (int i = 0; i < kHoistItems; ++i) {
+          w0[i] = U128{reduce128(w0[i], md), 0};
+          w1[i] = U128{reduce128(w1[i], md), 0};
+        }
       }
     }
     k0 = nk0;
@@ -743,9 +818,56 @@ __global__ void __launch_bounds__(kThreads) ks_inner_hoist_kernel(HoistKeys h, c
   for (int i = 0; i < kHoistItems; ++i) {
     if (i < cnt) {
       uint64_t* acc = acc_all + (size_t)(m0 + i) * 2 * E * N;
-      acc[(size_t)t * N + n] = reduce128(s0[i], md);
-      acc[((size_t)E + t) * N + n] = reduce128(s1[i], md);
+      uint64_t a, b;
+      if constexpr (FP) {
+        a = fp_canonical(fp_center(f0[i], qd, qinv), qd);
+        b = fp_canonical(fp_center(f1[i], qd, qinv), qd);
+      } else if constexpr (SPLIT) {
+        a = add_mod(r0[i], z0[i].reduce(md), md.q);
+        b = add_mod(r1[i], z1[i].reduce(md), md.q);
+      } else {
+        a = reduce128(w0[i], md);
+        b = reduce128(w1[i], md);
+      }
+      acc[(size_t)t * N + n] = a;
+      acc[((size_t)E + t) * N + n] = b;
     }
+  }
+}
+
+// the hoisted key products of M items over every limb of the extended basis
+// (Q_limbs and the K special primes), one launch per product mode
+void launch_ks_inner_hoist(const Context& c, const HoistKeys& h, const uint64_t* ext, uint64_t* acc, int M,
+                           int limbs, int beta, size_t istride, size_t rstride, cudaStream_t st) {
+  const int K = c.Kx(limbs), E = limbs + K;
+  HoistTargets tl[3]{};
+  int cnt[3] = {0, 0, 0}, runs[3] = {0, 0, 0};
+  for (int t = 0; t < E; ++t) {
+    const uint64_t q = c.moduli[t < limbs ? t : c.L + (t - limbs)];
+    const int mode = q < kFpPrime ? kHoistFp : q < (1ull << 60) ? kHoistSplit : kHoistWide;
+    HoistTargets& x = tl[mode];
+    int& r = runs[mode];
+    if (r > 0 && x.start[r - 1] + x.len[r - 1] == t) {
+      ++x.len[r - 1];
+    } else {
+      if (r == kTargetRuns) throw Error(kErrArgument, "prime sizes alternate too often along the extended basis");
+      x.start[r] = t;
+      x.len[r] = 1;
+      ++r;
+    }
+    ++cnt[mode];
+  }
+  const int fold = 63 / beta;
+  const int N = c.N;
+  for (int mode = 0; mode < 3; ++mode) {
+    if (!cnt[mode]) continue;
+    const dim3 grid((N + kThreads - 1) / kThreads, cnt[mode], (M + kHoistItems - 1) / kHoistItems);
+    auto kern = mode == kHoistFp      ? ks_inner_hoist_kernel<kHoistFp>
+                : mode == kHoistSplit ? ks_inner_hoist_kernel<kHoistSplit>
+                                      : ks_inner_hoist_kernel<kHoistWide>;
+    kern<<<grid, kThreads, 0, st>>>(h, tl[mode], ext, acc, M, limbs, c.L, K, c.P, beta, c.logN, fold, c.d_mods,
+                                    istride, rstride);
+    CKKS_CUDA(cudaGetLastError());
   }
 }
 
@@ -1288,11 +1410,8 @@ void keyswitch_sum_groups(const Context& c, int limbs, const KsBatch* bs, SumGro
       h.key[m] = bs[0].key[m];
       h.g[m] = bs[0].g[m];
     }
-    const int fold = 63 / lt.beta;
     ProfScope ps(c, "ks_inner_sum", ((double)G * M * lt.beta * E + 2.0 * M * lt.beta * E + 2.0 * G * E) * lb, st);
-    ks_inner_hoist_kernel<<<dim3((N + kThreads - 1) / kThreads, E, (G + kHoistItems - 1) / kHoistItems), kThreads, 0,
-                            st>>>(h, ext, acc, G, limbs, c.L, c.Kx(limbs), c.P, lt.beta, c.logN, fold, c.d_mods,
-                                  (size_t)M * item, item);
+    launch_ks_inner_hoist(c, h, ext, acc, G, limbs, lt.beta, (size_t)M * item, item, st);
   }
   CKKS_CUDA(cudaGetLastError());
   // one ModDown per group
@@ -1373,12 +1492,9 @@ void keyswitch_hoisted_sum(const Context& c, int limbs, const KsBatch& b, const 
   }
   // the R key inner products of each item, summed
   {
-    const int fold = 63 / lt.beta;
     ProfScope ps(c, "ks_inner_hoist", (M * (lt.beta * (1.0 + 2.0 * h.R) + 2.0) * E + 2.0 * h.R * lt.beta * E) * lb,
                  st);
-    ks_inner_hoist_kernel<<<dim3((N + kThreads - 1) / kThreads, E, (M + kHoistItems - 1) / kHoistItems), kThreads,
-                            0, st>>>(h, ext, acc, M, limbs, c.L, c.Kx(limbs), c.P, lt.beta, c.logN, fold, c.d_mods,
-                                     (size_t)lt.beta * E * N, 0);
+    launch_ks_inner_hoist(c, h, ext, acc, M, limbs, lt.beta, (size_t)lt.beta * E * N, 0, st);
   }
   CKKS_CUDA(cudaGetLastError());
   // one ModDown per item
