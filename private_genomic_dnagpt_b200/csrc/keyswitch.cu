@@ -993,6 +993,8 @@ __global__ void __launch_bounds__(kThreads) ks_inner_bulk_kernel(KsBatch b, cons
   ulonglong2 ra, rb;
   if (md.q < kFpPrime) {
     // exact float64 products: sums of at most three, |sum| < 3.2 q, exact
+    // (the other primes keep 128-bit multiply-accumulates: 30-bit split
+    // products measured slower here)
     const double qd = (double)md.q, qinv = 1.0 / qd;
     double a0 = 0.0, a1 = 0.0, b0 = 0.0, b1 = 0.0;
 #pragma unroll
@@ -1009,27 +1011,20 @@ __global__ void __launch_bounds__(kThreads) ks_inner_bulk_kernel(KsBatch b, cons
     ra = make_ulonglong2(fp_canonical(fp_center(a0, qd, qinv), qd), fp_canonical(fp_center(a1, qd, qinv), qd));
     rb = make_ulonglong2(fp_canonical(fp_center(b0, qd, qinv), qd), fp_canonical(fp_center(b1, qd, qinv), qd));
   } else {
-    // primes below 2^60 (checked on the host): carry-free split products
-    SplitSums a0, a1, b0, b1;
+    U128 a0{0, 0}, a1{0, 0}, b0{0, 0}, b1{0, 0};
 #pragma unroll
     for (int j = 0; j < BETA; ++j) {
       const ulonglong2 v = *reinterpret_cast<const ulonglong2*>(&sx[j][so]);
       const ulonglong2 k0 = *reinterpret_cast<const ulonglong2*>(&sk[j][0][i]);
       const ulonglong2 k1 = *reinterpret_cast<const ulonglong2*>(&sk[j][1][i]);
-      uint32_t v0l, v0h, v1l, v1h, kl, kh;
-      split_residue(swap ? v.y : v.x, v0l, v0h);
-      split_residue(swap ? v.x : v.y, v1l, v1h);
-      split_residue(k0.x, kl, kh);
-      a0.mac(v0l, v0h, kl, kh);
-      split_residue(k0.y, kl, kh);
-      a1.mac(v1l, v1h, kl, kh);
-      split_residue(k1.x, kl, kh);
-      b0.mac(v0l, v0h, kl, kh);
-      split_residue(k1.y, kl, kh);
-      b1.mac(v1l, v1h, kl, kh);
+      const uint64_t v0 = swap ? v.y : v.x, v1 = swap ? v.x : v.y;
+      mac_wide(a0, v0, k0.x);
+      mac_wide(a1, v1, k0.y);
+      mac_wide(b0, v0, k1.x);
+      mac_wide(b1, v1, k1.y);
     }
-    ra = make_ulonglong2(a0.reduce(md), a1.reduce(md));
-    rb = make_ulonglong2(b0.reduce(md), b1.reduce(md));
+    ra = make_ulonglong2(reduce128(a0, md), reduce128(a1, md));
+    rb = make_ulonglong2(reduce128(b0, md), reduce128(b1, md));
   }
   uint64_t* acc = acc_all + (size_t)m * 2 * E * N;
   *reinterpret_cast<ulonglong2*>(acc + (size_t)t * N + n) = ra;
@@ -1059,14 +1054,7 @@ __global__ void bulk_wait_probe_kernel(const uint64_t* __restrict__ src, uint64_
   for (uint32_t k = threadIdx.x; k < issue / sizeof(uint64_t); k += blockDim.x) dst[k] = sx[k];
 }
 
-// the bulk kernel's integer products need every prime of the extended
-// basis below 2^60
-bool bulk_inner_fits(const Context& c, int beta) {
-  if (beta < 1 || beta > 3 || c.N < 2 * kSpan) return false;
-  for (uint64_t q : c.moduli)
-    if (q >= (1ull << 60)) return false;
-  return true;
-}
+bool bulk_inner_fits(const Context& c, int beta) { return beta >= 1 && beta <= 3 && c.N >= 2 * kSpan; }
 
 void launch_ks_inner_bulk(const Context& c, bool multi, dim3 grid, const KsBatch& b, const uint64_t* ext, bool shared,
                           uint64_t* acc, int limbs, int beta, cudaStream_t st) {
