@@ -392,8 +392,8 @@ int ckks_schedule_active_shifts(int tokens, int batch, int qg, int kg, int* out,
 int ckks_schedule_diagonal(const double* W, int out_dim, int in_dim, int ld, int pack_width, int batch, int n1, int g,
                            int j, double* out_slots);
 
-/* EvalRotate for callers that cannot allocate device memory (graph
- * capture, allocation-free request paths, fixed memory budgets).  No
+/* EvalRotate for callers that cannot allocate device memory (request
+ * paths that must not enter the CUDA allocator, fixed memory budgets).  No
  * counterpart in the reference: it has no allocation-free entry point.
  * in_dev / out_dev: device buffers of 2*limbs*N words (c0 limbs then c1
  * limbs, NTT form), not overlapping.  Key-switching temporaries come from one

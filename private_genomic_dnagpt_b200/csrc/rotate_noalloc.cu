@@ -2,13 +2,13 @@
 // memory.
 //
 // Who needs it: code that runs where cudaMalloc / cudaFree are not allowed
-// or not wanted -- a caller recording work into a CUDA graph (allocation is
-// not a capturable operation), a host thread that must not take the driver's
-// allocation locks while other threads launch, or a service with a fixed
-// device-memory budget that must not grow per request.  The regular
-// ckks_rotate takes its key-switching temporaries from the stream-ordered
-// pool; this variant takes them from one fixed array compiled into the
-// library instead, and the caller supplies input and output buffers.
+// or not wanted -- a host thread that must not take the driver's allocation
+// locks while other threads launch, or a service with a fixed device-memory
+// budget that must not grow per request.  The regular ckks_rotate takes its
+// key-switching temporaries from the context's device-memory cache, which
+// calls cudaMalloc whenever it needs a block it does not hold; this variant
+// takes them from one fixed array compiled into the library instead, and the
+// caller supplies input and output buffers.
 //
 // The array is a file-scope static __device__ array of kScratchBytes
 // (128 MiB).  Every GPU that loads the library holds it until the process

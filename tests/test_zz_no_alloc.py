@@ -1,7 +1,7 @@
 """ckks_rotate_noalloc: rotation for callers that cannot allocate device memory.
 
-Such callers (code recording into a CUDA graph, request paths that must not
-take the allocator's locks, services on a fixed memory budget) pass their
+Such callers (request paths that must not take the allocator's locks,
+services on a fixed device-memory budget) pass their
 own input and output device buffers; the key-switching temporaries come from
 a fixed array inside the library.  These tests check, through the C ABI, that
 two such calls in a row give exactly the limbs of the allocating ckks_rotate,
