@@ -160,6 +160,7 @@ class Context {
 
   Params params;
   int logN, N, L, K, alpha, beta_top, P;
+  int sms = 148;  // multiprocessors of the context's device
   std::vector<uint64_t> moduli;  // L + K
   std::vector<uint64_t> psi;
   std::vector<double> scales;  // [limbs], 1..L

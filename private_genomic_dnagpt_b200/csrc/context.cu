@@ -183,6 +183,7 @@ Context::Context(const Params& p) : params(p) {
       p.scale_mod_bits <= p.log_n + 1 || p.special_mod_bits <= p.log_n + 1)
     throw Error(kErrArgument, "parameters out of range (log_n 6..17, limbs >= 2, prime bits <= 61)");
   CKKS_CUDA(cudaSetDevice(p.device));
+  CKKS_CUDA(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, p.device));
   logN = p.log_n;
   N = 1 << logN;
   L = p.limbs;

@@ -479,7 +479,7 @@ __global__ void __launch_bounds__(PassShape<R_LOG>::kThreads, PassShape<R_LOG>::
 }
 
 template <int S_LOG, bool INV, bool STRIDED>
-void launch_pass(uint64_t* data, int nlimbs, const PassArgs& a0, cudaStream_t st) {
+void launch_pass(uint64_t* data, int nlimbs, const PassArgs& a0, int sms, cudaStream_t st) {
   // strided passes: 16 residues per thread (four stages per register group,
   // twice the loads in flight per thread); contiguous passes, whose
   // shared-memory exchanges favour more resident warps: 8
@@ -490,6 +490,10 @@ void launch_pass(uint64_t* data, int nlimbs, const PassArgs& a0, cudaStream_t st
   const int subs = N / S;  // sub-transforms per limb
   int per = PassShape<R_LOG>::kThreads / T;
   if (per > subs) per = subs;
+  // small batches: smaller CTAs (fewer sub-transforms each, at least one
+  // warp) until the grid holds four CTAs per SM, so the work spreads over
+  // every SM instead of a partly filled second wave on a few of them
+  while (per > 1 && per * T > 32 && (subs / per) * nlimbs < 4 * sms) per >>= 1;
   PassArgs a = a0;
   a.per_cta = per;
   const dim3 grid(subs / per, nlimbs);
@@ -501,15 +505,15 @@ void launch_pass(uint64_t* data, int nlimbs, const PassArgs& a0, cudaStream_t st
 }
 
 template <bool INV, bool STRIDED>
-void dispatch_pass(int s_log, uint64_t* data, int nlimbs, const PassArgs& a, cudaStream_t st) {
+void dispatch_pass(int s_log, uint64_t* data, int nlimbs, const PassArgs& a, int sms, cudaStream_t st) {
   switch (s_log) {
-    case 3: launch_pass<3, INV, STRIDED>(data, nlimbs, a, st); break;
-    case 4: launch_pass<4, INV, STRIDED>(data, nlimbs, a, st); break;
-    case 5: launch_pass<5, INV, STRIDED>(data, nlimbs, a, st); break;
-    case 6: launch_pass<6, INV, STRIDED>(data, nlimbs, a, st); break;
-    case 7: launch_pass<7, INV, STRIDED>(data, nlimbs, a, st); break;
-    case 8: launch_pass<8, INV, STRIDED>(data, nlimbs, a, st); break;
-    case 9: launch_pass<9, INV, STRIDED>(data, nlimbs, a, st); break;
+    case 3: launch_pass<3, INV, STRIDED>(data, nlimbs, a, sms, st); break;
+    case 4: launch_pass<4, INV, STRIDED>(data, nlimbs, a, sms, st); break;
+    case 5: launch_pass<5, INV, STRIDED>(data, nlimbs, a, sms, st); break;
+    case 6: launch_pass<6, INV, STRIDED>(data, nlimbs, a, sms, st); break;
+    case 7: launch_pass<7, INV, STRIDED>(data, nlimbs, a, sms, st); break;
+    case 8: launch_pass<8, INV, STRIDED>(data, nlimbs, a, sms, st); break;
+    case 9: launch_pass<9, INV, STRIDED>(data, nlimbs, a, sms, st); break;
     default: break;
   }
 }
@@ -542,11 +546,11 @@ void ntt_forward(const Context& c, uint64_t* data, int nlimbs, LimbMap map, cuda
       a1.has_src = true;
       a1.src = *src;
     }
-    dispatch_pass<false, true>(s1, data, nlimbs, a1, st);
+    dispatch_pass<false, true>(s1, data, nlimbs, a1, c.sms, st);
   }
   {
     ProfScope ps(c, "ntt_fwd_cols", bytes, st);
-    dispatch_pass<false, false>(s2, data, nlimbs, a, st);
+    dispatch_pass<false, false>(s2, data, nlimbs, a, c.sms, st);
   }
   CKKS_CUDA(cudaGetLastError());
 }
@@ -574,11 +578,11 @@ void ntt_inverse(const Context& c, uint64_t* data, int nlimbs, LimbMap map, cuda
       a1.has_src = true;
       a1.src = *src;
     }
-    dispatch_pass<true, false>(s2, data, nlimbs, a1, st);
+    dispatch_pass<true, false>(s2, data, nlimbs, a1, c.sms, st);
   }
   {
     ProfScope ps(c, "ntt_inv_rows", bytes, st);
-    dispatch_pass<true, true>(s1, data, nlimbs, a, st);
+    dispatch_pass<true, true>(s1, data, nlimbs, a, c.sms, st);
   }
   CKKS_CUDA(cudaGetLastError());
 }
