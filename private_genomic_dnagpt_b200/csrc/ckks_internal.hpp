@@ -11,6 +11,7 @@
 #include <unordered_map>
 #include <stdexcept>
 #include <string>
+#include <utility>
 #include <vector>
 
 #include "modarith.cuh"
@@ -36,6 +37,34 @@ enum : int {
 
 void cuda_check(cudaError_t e, const char* what);
 #define CKKS_CUDA(x) ::ckks::cuda_check((x), #x)
+
+// Programmatic dependent launch.  A kernel started by launch_pdl may begin
+// while the previous kernel in its stream is still finishing, so it runs
+// CKKS_PDL_ENTRY() before touching global memory: griddepcontrol.wait
+// returns once the preceding grids have completed and their writes are
+// visible; launch_dependents lets the next programmatic dependent start once
+// every CTA of this grid has started (so its CTAs take the SMs that this
+// grid's last wave frees).
+#define CKKS_PDL_ENTRY()                                 \
+  do {                                                   \
+    asm volatile("griddepcontrol.wait;" ::: "memory");   \
+    asm volatile("griddepcontrol.launch_dependents;");   \
+  } while (0)
+
+template <class... KArgs, class... Args>
+void launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st, Args&&... args) {
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  CKKS_CUDA(cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...));
+}
 
 // Maps batch limb index -> global prime index.  A batch holds polynomials of
 // `nper` limbs each; the first `lq` limbs of every polynomial are the Q primes

@@ -376,6 +376,7 @@ __global__ void __launch_bounds__(kThreads) modup_conv_batch_kernel(KsBatch b, c
                                                                     int K, int alpha, int beta, int logN, int nchunks,
                                                                     const Mod* __restrict__ mods,
                                                                     const uint64_t* __restrict__ hat) {
+  CKKS_PDL_ENTRY();
   const int N = 1 << logN;
   const int n = 2 * (blockIdx.x * kThreads + threadIdx.x);
   if (n >= N) return;
@@ -472,6 +473,7 @@ __global__ void __launch_bounds__(kThreads) ks_inner_batch_kernel(KsBatch b, con
                                                                   bool shared, uint64_t* __restrict__ acc_all,
                                                                   int limbs, int L, int K, int P, int beta, int logN,
                                                                   const Mod* __restrict__ mods) {
+  CKKS_PDL_ENTRY();
   // two adjacent residues per thread (src(n + 1) = src(n) ^ 1)
   const int N = 1 << logN;
   const int n = 2 * (blockIdx.x * kThreads + threadIdx.x);
@@ -499,6 +501,7 @@ __global__ void __launch_bounds__(kThreads) ks_inner_sum_kernel(KsBatch b, const
                                                                 uint64_t* __restrict__ acc, int limbs, int L, int K,
                                                                 int P, int beta, int logN, int fold,
                                                                 const Mod* __restrict__ mods) {
+  CKKS_PDL_ENTRY();
   // two adjacent residues per thread (src(n + 1) = src(n) ^ 1): 16-byte
   // loads and stores
   const int N = 1 << logN;
@@ -534,6 +537,7 @@ __global__ void __launch_bounds__(kThreads) moddown_combine_sum_kernel(KsBatch b
                                                                       uint64_t* __restrict__ out1, int limbs, int K,
                                                                       int logN, const Mod* __restrict__ mods,
                                                                       const ulonglong2* __restrict__ pinv) {
+  CKKS_PDL_ENTRY();
   const int N = 1 << logN;
   const int n = blockIdx.x * kThreads + threadIdx.x;
   if (n >= N) return;
@@ -566,6 +570,7 @@ __global__ void __launch_bounds__(kThreads) moddown_combine_groups_kernel(SumGro
                                                                          int limbs, int K, int logN,
                                                                          const Mod* __restrict__ mods,
                                                                          const ulonglong2* __restrict__ pinv) {
+  CKKS_PDL_ENTRY();
   const int N = 1 << logN;
   const int n = blockIdx.x * kThreads + threadIdx.x;
   if (n >= N) return;
@@ -596,6 +601,7 @@ __global__ void __launch_bounds__(kThreads) moddown_conv_batch_kernel(const uint
                                                                       int L, int K, int logN, int nchunks,
                                                                       const Mod* __restrict__ mods,
                                                                       const uint64_t* __restrict__ phat) {
+  CKKS_PDL_ENTRY();
   const int N = 1 << logN;
   const int n = 2 * (blockIdx.x * kThreads + threadIdx.x);
   if (n >= N) return;
@@ -632,6 +638,7 @@ __global__ void __launch_bounds__(kThreads) moddown_combine_batch_kernel(KsBatch
                                                                         int limbs, int K, int logN,
                                                                         const Mod* __restrict__ mods,
                                                                         const ulonglong2* __restrict__ pinv) {
+  CKKS_PDL_ENTRY();
   const int N = 1 << logN;
   const int n = blockIdx.x * kThreads + threadIdx.x;
   if (n >= N) return;
@@ -660,6 +667,7 @@ __global__ void __launch_bounds__(kThreads) moddown_combine_batch_kernel(KsBatch
 __global__ void __launch_bounds__(kThreads) rs_combine_batch_kernel(RsBatch b, const uint64_t* __restrict__ tmp,
                                                                     int limbs, int logN, const Mod* __restrict__ mods,
                                                                     const ulonglong2* __restrict__ inv) {
+  CKKS_PDL_ENTRY();
   const int N = 1 << logN;
   const int n = blockIdx.x * kThreads + threadIdx.x;
   if (n >= N) return;
@@ -715,6 +723,7 @@ __global__ void __launch_bounds__(kThreads, MODE == kHoistSplit ? 2 : 3)
     ks_inner_hoist_kernel(HoistKeys h, HoistTargets tl, const uint64_t* __restrict__ ext_all,
                           uint64_t* __restrict__ acc_all, int M, int limbs, int L, int K, int P, int beta, int logN,
                           int fold, const Mod* __restrict__ mods, size_t istride, size_t rstride) {
+  CKKS_PDL_ENTRY();
   constexpr bool FP = MODE == kHoistFp;
   constexpr bool SPLIT = MODE == kHoistSplit;
   const int N = 1 << logN;
@@ -865,8 +874,7 @@ void launch_ks_inner_hoist(const Context& c, const HoistKeys& h, const uint64_t*
     auto kern = mode == kHoistFp      ? ks_inner_hoist_kernel<kHoistFp>
                 : mode == kHoistSplit ? ks_inner_hoist_kernel<kHoistSplit>
                                       : ks_inner_hoist_kernel<kHoistWide>;
-    kern<<<grid, kThreads, 0, st>>>(h, tl[mode], ext, acc, M, limbs, c.L, K, c.P, beta, c.logN, fold, c.d_mods,
-                                    istride, rstride);
+    launch_pdl(kern, grid, kThreads, 0, st, h, tl[mode], ext, acc, M, limbs, c.L, K, c.P, beta, c.logN, fold, c.d_mods, istride, rstride);
     CKKS_CUDA(cudaGetLastError());
   }
 }
@@ -879,6 +887,7 @@ __global__ void __launch_bounds__(kThreads) moddown_combine_hoist_kernel(KsBatch
                                                                         int limbs, int K, int logN,
                                                                         const Mod* __restrict__ mods,
                                                                         const ulonglong2* __restrict__ pinv) {
+  CKKS_PDL_ENTRY();
   const int N = 1 << logN;
   const int n = blockIdx.x * kThreads + threadIdx.x;
   if (n >= N) return;
@@ -907,6 +916,7 @@ __global__ void __launch_bounds__(kThreads) ks_inner_multi_kernel(KsBatch b, con
                                                                   uint64_t* __restrict__ acc_all, int limbs, int L,
                                                                   int K, int P, int beta, int logN,
                                                                   const Mod* __restrict__ mods) {
+  CKKS_PDL_ENTRY();
   // two adjacent residues n, n + 1 per thread: the automorphism maps the
   // aligned pair onto an aligned pair (src(n + 1) = src(n) ^ 1), so every
   // load and store is 16 bytes
@@ -952,6 +962,7 @@ __global__ void __launch_bounds__(kThreads) ks_inner_bulk_kernel(KsBatch b, cons
                                                                  int limbs, int L, int K, int P, int logN,
                                                                  const Mod* __restrict__ mods,
                                                                  unsigned int* __restrict__ faults) {
+  CKKS_PDL_ENTRY();
   __shared__ alignas(128) uint64_t sx[BETA][kSpan];
   __shared__ alignas(128) uint64_t sk[BETA][2][kSpan];
   __shared__ alignas(8) uint64_t bar;
@@ -1058,9 +1069,9 @@ bool bulk_inner_fits(const Context& c, int beta) { return beta >= 1 && beta <= 3
 
 void launch_ks_inner_bulk(const Context& c, bool multi, dim3 grid, const KsBatch& b, const uint64_t* ext, bool shared,
                           uint64_t* acc, int limbs, int beta, cudaStream_t st) {
-#define CKKS_BULK_LAUNCH(BETA)                                                                                   \
-  (multi ? ks_inner_bulk_kernel<BETA, true> : ks_inner_bulk_kernel<BETA, false>)<<<grid, kThreads, 0, st>>>( \
-      b, ext, shared, acc, limbs, c.L, c.Kx(limbs), c.P, c.logN, c.d_mods, c.d_faults)
+#define CKKS_BULK_LAUNCH(BETA)                                                                        \
+  launch_pdl(multi ? ks_inner_bulk_kernel<BETA, true> : ks_inner_bulk_kernel<BETA, false>, grid, kThreads, 0, st, \
+             b, ext, shared, acc, limbs, c.L, c.Kx(limbs), c.P, c.logN, c.d_mods, c.d_faults)
   switch (beta) {
     case 1: CKKS_BULK_LAUNCH(1); break;
     case 2: CKKS_BULK_LAUNCH(2); break;
@@ -1117,8 +1128,7 @@ void keyswitch_batch(const Context& c, int limbs, const KsBatch& b, bool shared,
                 : c.alpha <= 8 ? modup_conv_batch_kernel<8>
                 : c.alpha <= 12 ? modup_conv_batch_kernel<12>
                                 : modup_conv_batch_kernel<16>;
-    kern<<<dim3((N / 2 + kThreads - 1) / kThreads, lt.beta * nch_up, Mu), kThreads, 0, st>>>(
-        b, dc, ext, limbs, c.L, c.Kx(limbs), c.alpha, lt.beta, c.logN, nch_up, c.d_mods, lt.d_up_hat);
+    launch_pdl(kern, dim3((N / 2 + kThreads - 1) / kThreads, lt.beta * nch_up, Mu), kThreads, 0, st, b, dc, ext, limbs, c.L, c.Kx(limbs), c.alpha, lt.beta, c.logN, nch_up, c.d_mods, lt.d_up_hat);
   }
   CKKS_CUDA(cudaGetLastError());
   {
@@ -1133,8 +1143,7 @@ void keyswitch_batch(const Context& c, int limbs, const KsBatch& b, bool shared,
     if (bulk_inner_fits(c, lt.beta))
       launch_ks_inner_bulk(c, false, dim3(N / kSpan, E, M), b, ext, shared, acc, limbs, lt.beta, st);
     else
-      ks_inner_batch_kernel<<<dim3((N / 2 + kThreads - 1) / kThreads, E, M), kThreads, 0, st>>>(
-          b, ext, shared, acc, limbs, c.L, c.Kx(limbs), c.P, lt.beta, c.logN, c.d_mods);
+      launch_pdl(ks_inner_batch_kernel, dim3((N / 2 + kThreads - 1) / kThreads, E, M), kThreads, 0, st, b, ext, shared, acc, limbs, c.L, c.Kx(limbs), c.P, lt.beta, c.logN, c.d_mods);
   }
   CKKS_CUDA(cudaGetLastError());
   // ModDown
@@ -1150,15 +1159,13 @@ void keyswitch_batch(const Context& c, int limbs, const KsBatch& b, bool shared,
                 : c.Kx(limbs) <= 8 ? moddown_conv_batch_kernel<8>
                 : c.Kx(limbs) <= 12 ? moddown_conv_batch_kernel<12>
                             : moddown_conv_batch_kernel<16>;
-    kern<<<dim3((N / 2 + kThreads - 1) / kThreads, 2 * nch_dn, M), kThreads, 0, st>>>(
-        acc, conv, limbs, c.L, c.Kx(limbs), c.logN, nch_dn, c.d_mods, lt.d_down_phat);
+    launch_pdl(kern, dim3((N / 2 + kThreads - 1) / kThreads, 2 * nch_dn, M), kThreads, 0, st, acc, conv, limbs, c.L, c.Kx(limbs), c.logN, nch_dn, c.d_mods, lt.d_down_phat);
   }
   CKKS_CUDA(cudaGetLastError());
   ntt_forward(c, conv, M * 2 * limbs, LimbMap::q(limbs, c.L), st);
   {
     ProfScope ps(c, "moddown_combine", M * 8.0 * limbs * lb, st);
-    moddown_combine_batch_kernel<<<dim3((N + kThreads - 1) / kThreads, 2 * limbs, M), kThreads, 0, st>>>(
-        b, acc, conv, limbs, c.Kx(limbs), c.logN, c.d_mods, lt.d_down_pinv);
+    launch_pdl(moddown_combine_batch_kernel, dim3((N + kThreads - 1) / kThreads, 2 * limbs, M), kThreads, 0, st, b, acc, conv, limbs, c.Kx(limbs), c.logN, c.d_mods, lt.d_down_pinv);
   }
   CKKS_CUDA(cudaGetLastError());
   c.release(dc);
@@ -1197,8 +1204,7 @@ void keyswitch_hoisted_multi(const Context& c, int limbs, const uint64_t* const*
                 : c.alpha <= 8 ? modup_conv_batch_kernel<8>
                 : c.alpha <= 12 ? modup_conv_batch_kernel<12>
                                 : modup_conv_batch_kernel<16>;
-    kern<<<dim3((N / 2 + kThreads - 1) / kThreads, lt.beta * nch_up, G), kThreads, 0, st>>>(
-        bu, dc, ext, limbs, c.L, c.Kx(limbs), c.alpha, lt.beta, c.logN, nch_up, c.d_mods, lt.d_up_hat);
+    launch_pdl(kern, dim3((N / 2 + kThreads - 1) / kThreads, lt.beta * nch_up, G), kThreads, 0, st, bu, dc, ext, limbs, c.L, c.Kx(limbs), c.alpha, lt.beta, c.logN, nch_up, c.d_mods, lt.d_up_hat);
   }
   CKKS_CUDA(cudaGetLastError());
   {
@@ -1234,8 +1240,7 @@ void keyswitch_hoisted_multi(const Context& c, int limbs, const uint64_t* const*
       if (bulk_inner_fits(c, lt.beta))
         launch_ks_inner_bulk(c, true, dim3(M, N / kSpan, E), b, ext, false, acc, limbs, lt.beta, st);
       else
-        ks_inner_multi_kernel<<<dim3(M, (N / 2 + kThreads - 1) / kThreads, E), kThreads, 0, st>>>(
-            b, ext, acc, limbs, c.L, c.Kx(limbs), c.P, lt.beta, c.logN, c.d_mods);
+        launch_pdl(ks_inner_multi_kernel, dim3(M, (N / 2 + kThreads - 1) / kThreads, E), kThreads, 0, st, b, ext, acc, limbs, c.L, c.Kx(limbs), c.P, lt.beta, c.logN, c.d_mods);
     }
     CKKS_CUDA(cudaGetLastError());
     {
@@ -1250,15 +1255,13 @@ void keyswitch_hoisted_multi(const Context& c, int limbs, const uint64_t* const*
                   : c.Kx(limbs) <= 8 ? moddown_conv_batch_kernel<8>
                   : c.Kx(limbs) <= 12 ? moddown_conv_batch_kernel<12>
                               : moddown_conv_batch_kernel<16>;
-      kern<<<dim3((N / 2 + kThreads - 1) / kThreads, 2 * nch_dn, M), kThreads, 0, st>>>(
-          acc, conv, limbs, c.L, c.Kx(limbs), c.logN, nch_dn, c.d_mods, lt.d_down_phat);
+      launch_pdl(kern, dim3((N / 2 + kThreads - 1) / kThreads, 2 * nch_dn, M), kThreads, 0, st, acc, conv, limbs, c.L, c.Kx(limbs), c.logN, nch_dn, c.d_mods, lt.d_down_phat);
     }
     CKKS_CUDA(cudaGetLastError());
     ntt_forward(c, conv, M * 2 * limbs, LimbMap::q(limbs, c.L), st);
     {
       ProfScope ps(c, "moddown_combine", M * 8.0 * limbs * lb, st);
-      moddown_combine_batch_kernel<<<dim3((N + kThreads - 1) / kThreads, 2 * limbs, M), kThreads, 0, st>>>(
-          b, acc, conv, limbs, c.Kx(limbs), c.logN, c.d_mods, lt.d_down_pinv);
+      launch_pdl(moddown_combine_batch_kernel, dim3((N + kThreads - 1) / kThreads, 2 * limbs, M), kThreads, 0, st, b, acc, conv, limbs, c.Kx(limbs), c.logN, c.d_mods, lt.d_down_pinv);
     }
     CKKS_CUDA(cudaGetLastError());
   }
@@ -1294,8 +1297,7 @@ void keyswitch_sum(const Context& c, int limbs, const KsBatch& b, uint64_t* out0
                 : c.alpha <= 8 ? modup_conv_batch_kernel<8>
                 : c.alpha <= 12 ? modup_conv_batch_kernel<12>
                                 : modup_conv_batch_kernel<16>;
-    kern<<<dim3((N / 2 + kThreads - 1) / kThreads, lt.beta * nch_up, M), kThreads, 0, st>>>(
-        b, dc, ext, limbs, c.L, c.Kx(limbs), c.alpha, lt.beta, c.logN, nch_up, c.d_mods, lt.d_up_hat);
+    launch_pdl(kern, dim3((N / 2 + kThreads - 1) / kThreads, lt.beta * nch_up, M), kThreads, 0, st, b, dc, ext, limbs, c.L, c.Kx(limbs), c.alpha, lt.beta, c.logN, nch_up, c.d_mods, lt.d_up_hat);
   }
   CKKS_CUDA(cudaGetLastError());
   {
@@ -1308,8 +1310,7 @@ void keyswitch_sum(const Context& c, int limbs, const KsBatch& b, uint64_t* out0
   {
     const int fold = 63 / lt.beta;
     ProfScope ps(c, "ks_inner_sum", (M * 3.0 * lt.beta * E + 2.0 * E) * lb, st);
-    ks_inner_sum_kernel<<<dim3((N / 2 + kThreads - 1) / kThreads, E), kThreads, 0, st>>>(
-        b, ext, acc, limbs, c.L, c.Kx(limbs), c.P, lt.beta, c.logN, fold, c.d_mods);
+    launch_pdl(ks_inner_sum_kernel, dim3((N / 2 + kThreads - 1) / kThreads, E), kThreads, 0, st, b, ext, acc, limbs, c.L, c.Kx(limbs), c.P, lt.beta, c.logN, fold, c.d_mods);
   }
   CKKS_CUDA(cudaGetLastError());
   // one ModDown
@@ -1325,15 +1326,13 @@ void keyswitch_sum(const Context& c, int limbs, const KsBatch& b, uint64_t* out0
                 : c.Kx(limbs) <= 8 ? moddown_conv_batch_kernel<8>
                 : c.Kx(limbs) <= 12 ? moddown_conv_batch_kernel<12>
                             : moddown_conv_batch_kernel<16>;
-    kern<<<dim3((N / 2 + kThreads - 1) / kThreads, 2 * nch_dn, 1), kThreads, 0, st>>>(
-        acc, conv, limbs, c.L, c.Kx(limbs), c.logN, nch_dn, c.d_mods, lt.d_down_phat);
+    launch_pdl(kern, dim3((N / 2 + kThreads - 1) / kThreads, 2 * nch_dn, 1), kThreads, 0, st, acc, conv, limbs, c.L, c.Kx(limbs), c.logN, nch_dn, c.d_mods, lt.d_down_phat);
   }
   CKKS_CUDA(cudaGetLastError());
   ntt_forward(c, conv, 2 * limbs, LimbMap::q(limbs, c.L), st);
   {
     ProfScope ps(c, "moddown_combine_sum", (6.0 + M) * limbs * lb, st);
-    moddown_combine_sum_kernel<<<dim3((N + kThreads - 1) / kThreads, 2 * limbs), kThreads, 0, st>>>(
-        b, acc, conv, out0, out1, limbs, c.Kx(limbs), c.logN, c.d_mods, lt.d_down_pinv);
+    launch_pdl(moddown_combine_sum_kernel, dim3((N + kThreads - 1) / kThreads, 2 * limbs), kThreads, 0, st, b, acc, conv, out0, out1, limbs, c.Kx(limbs), c.logN, c.d_mods, lt.d_down_pinv);
   }
   CKKS_CUDA(cudaGetLastError());
   c.release(dc);
@@ -1381,8 +1380,7 @@ void keyswitch_sum_groups(const Context& c, int limbs, const KsBatch* bs, SumGro
                   : c.alpha <= 8 ? modup_conv_batch_kernel<8>
                   : c.alpha <= 12 ? modup_conv_batch_kernel<12>
                                   : modup_conv_batch_kernel<16>;
-      kern<<<dim3((N / 2 + kThreads - 1) / kThreads, lt.beta * nch_up, M), kThreads, 0, st>>>(
-          b, dc, eg, limbs, c.L, c.Kx(limbs), c.alpha, lt.beta, c.logN, nch_up, c.d_mods, lt.d_up_hat);
+      launch_pdl(kern, dim3((N / 2 + kThreads - 1) / kThreads, lt.beta * nch_up, M), kThreads, 0, st, b, dc, eg, limbs, c.L, c.Kx(limbs), c.alpha, lt.beta, c.logN, nch_up, c.d_mods, lt.d_up_hat);
     }
     CKKS_CUDA(cudaGetLastError());
     LimbMap m = LimbMap::ext(limbs, c.Kx(limbs), c.L);
@@ -1415,8 +1413,7 @@ void keyswitch_sum_groups(const Context& c, int limbs, const KsBatch* bs, SumGro
                 : c.Kx(limbs) <= 8 ? moddown_conv_batch_kernel<8>
                 : c.Kx(limbs) <= 12 ? moddown_conv_batch_kernel<12>
                             : moddown_conv_batch_kernel<16>;
-    kern<<<dim3((N / 2 + kThreads - 1) / kThreads, 2 * nch_dn, G), kThreads, 0, st>>>(
-        acc, conv, limbs, c.L, c.Kx(limbs), c.logN, nch_dn, c.d_mods, lt.d_down_phat);
+    launch_pdl(kern, dim3((N / 2 + kThreads - 1) / kThreads, 2 * nch_dn, G), kThreads, 0, st, acc, conv, limbs, c.L, c.Kx(limbs), c.logN, nch_dn, c.d_mods, lt.d_down_phat);
   }
   CKKS_CUDA(cudaGetLastError());
   ntt_forward(c, conv, G * 2 * limbs, LimbMap::q(limbs, c.L), st);
@@ -1428,8 +1425,7 @@ void keyswitch_sum_groups(const Context& c, int limbs, const KsBatch* bs, SumGro
     double extra = 0.0;
     for (int gi = 0; gi < G; ++gi) extra += (s.id0[gi] ? 1.0 : 0.0) + (s.id1[gi] ? 1.0 : 0.0);
     ProfScope ps(c, "moddown_combine_sum", (G * (6.0 + M) + extra) * limbs * lb, st);
-    moddown_combine_groups_kernel<<<dim3((N + kThreads - 1) / kThreads, 2 * limbs, G), kThreads, 0, st>>>(
-        s, acc, conv, limbs, c.Kx(limbs), c.logN, c.d_mods, lt.d_down_pinv);
+    launch_pdl(moddown_combine_groups_kernel, dim3((N + kThreads - 1) / kThreads, 2 * limbs, G), kThreads, 0, st, s, acc, conv, limbs, c.Kx(limbs), c.logN, c.d_mods, lt.d_down_pinv);
   }
   CKKS_CUDA(cudaGetLastError());
   c.release(dc);
@@ -1468,8 +1464,7 @@ void keyswitch_hoisted_sum(const Context& c, int limbs, const KsBatch& b, const 
                 : c.alpha <= 8 ? modup_conv_batch_kernel<8>
                 : c.alpha <= 12 ? modup_conv_batch_kernel<12>
                                 : modup_conv_batch_kernel<16>;
-    kern<<<dim3((N / 2 + kThreads - 1) / kThreads, lt.beta * nch_up, M), kThreads, 0, st>>>(
-        b, dc, ext, limbs, c.L, c.Kx(limbs), c.alpha, lt.beta, c.logN, nch_up, c.d_mods, lt.d_up_hat);
+    launch_pdl(kern, dim3((N / 2 + kThreads - 1) / kThreads, lt.beta * nch_up, M), kThreads, 0, st, b, dc, ext, limbs, c.L, c.Kx(limbs), c.alpha, lt.beta, c.logN, nch_up, c.d_mods, lt.d_up_hat);
   }
   CKKS_CUDA(cudaGetLastError());
   {
@@ -1498,15 +1493,13 @@ void keyswitch_hoisted_sum(const Context& c, int limbs, const KsBatch& b, const 
                 : c.Kx(limbs) <= 8 ? moddown_conv_batch_kernel<8>
                 : c.Kx(limbs) <= 12 ? moddown_conv_batch_kernel<12>
                             : moddown_conv_batch_kernel<16>;
-    kern<<<dim3((N / 2 + kThreads - 1) / kThreads, 2 * nch_dn, M), kThreads, 0, st>>>(
-        acc, conv, limbs, c.L, c.Kx(limbs), c.logN, nch_dn, c.d_mods, lt.d_down_phat);
+    launch_pdl(kern, dim3((N / 2 + kThreads - 1) / kThreads, 2 * nch_dn, M), kThreads, 0, st, acc, conv, limbs, c.L, c.Kx(limbs), c.logN, nch_dn, c.d_mods, lt.d_down_phat);
   }
   CKKS_CUDA(cudaGetLastError());
   ntt_forward(c, conv, M * 2 * limbs, LimbMap::q(limbs, c.L), st);
   {
     ProfScope ps(c, "moddown_combine_hoist", M * (6.0 + h.R + (identity ? 2.0 : 0.0)) * limbs * lb, st);
-    moddown_combine_hoist_kernel<<<dim3((N + kThreads - 1) / kThreads, 2 * limbs, M), kThreads, 0, st>>>(
-        b, h, identity, acc, conv, limbs, c.Kx(limbs), c.logN, c.d_mods, lt.d_down_pinv);
+    launch_pdl(moddown_combine_hoist_kernel, dim3((N + kThreads - 1) / kThreads, 2 * limbs, M), kThreads, 0, st, b, h, identity, acc, conv, limbs, c.Kx(limbs), c.logN, c.d_mods, lt.d_down_pinv);
   }
   CKKS_CUDA(cudaGetLastError());
   c.release(dc);
@@ -1545,8 +1538,7 @@ void rescale_batch(const Context& c, int limbs, const RsBatch& b, cudaStream_t s
   }
   {
     ProfScope ps(c, "rescale_combine", 6.0 * M * lo * lb, st);
-    rs_combine_batch_kernel<<<dim3((N + kThreads - 1) / kThreads, 2 * lo, M), kThreads, 0, st>>>(
-        b, tmp, limbs, c.logN, c.d_mods, lt.d_rescale_inv);
+    launch_pdl(rs_combine_batch_kernel, dim3((N + kThreads - 1) / kThreads, 2 * lo, M), kThreads, 0, st, b, tmp, limbs, c.logN, c.d_mods, lt.d_rescale_inv);
   }
   CKKS_CUDA(cudaGetLastError());
   c.release(last);

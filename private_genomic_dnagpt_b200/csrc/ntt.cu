@@ -430,12 +430,7 @@ template <int S_LOG, bool INV, bool STRIDED, int R_LOG>
 __global__ void __launch_bounds__(PassShape<R_LOG>::kThreads, PassShape<R_LOG>::kMinBlocks)
     ntt_pass_kernel(uint64_t* __restrict__ data, PassArgs a) {
   extern __shared__ uint64_t sm[];
-  // launched as a programmatic dependent of the previous kernel in the
-  // stream: wait until that grid has completed and its writes are visible,
-  // then let the next dependent launch begin once every CTA of this grid
-  // has started (its CTAs take the SMs this grid's last wave frees)
-  asm volatile("griddepcontrol.wait;" ::: "memory");
-  asm volatile("griddepcontrol.launch_dependents;");
+  CKKS_PDL_ENTRY();  // launched as a programmatic dependent (launch_pdl)
   const int limb = blockIdx.y;
   if (a.map.skipped(limb)) return;
   const int prime = a.map.prime(limb);
@@ -507,20 +502,9 @@ void launch_pass(uint64_t* data, int nlimbs, const PassArgs& a0, int sms, cudaSt
   const size_t smem = (size_t)S * per * sizeof(uint64_t);
   auto k = ntt_pass_kernel<S_LOG, INV, STRIDED, R_LOG>;
   if (smem > 48 * 1024) cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-  // programmatic dependent launch: the kernel waits for its predecessor on
-  // the device (griddepcontrol.wait), so its launch can overlap the
-  // predecessor's last wave
-  cudaLaunchConfig_t cfg{};
-  cfg.gridDim = grid;
-  cfg.blockDim = dim3(threads);
-  cfg.dynamicSmemBytes = smem;
-  cfg.stream = st;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attr[0].val.programmaticStreamSerializationAllowed = 1;
-  cfg.attrs = attr;
-  cfg.numAttrs = 1;
-  CKKS_CUDA(cudaLaunchKernelEx(&cfg, k, data, a));
+  // a programmatic dependent: its launch can overlap the previous kernel's
+  // last wave (the kernel waits for that grid on the device)
+  launch_pdl(k, grid, dim3(threads), smem, st, data, a);
 }
 
 template <bool INV, bool STRIDED>
