@@ -66,6 +66,42 @@ __global__ void __launch_bounds__(kThreads) fft_stage_kernel(double2* __restrict
   vec[i + j + lenh] = b;
 }
 
+// The G stages with span above 2^lb (lg = lb+1 .. lb+G) in registers: they
+// only combine entries whose indices differ in bits lb .. lb+G-1, so the
+// 2^G entries lo + hi 2^lb (hi = 0 .. 2^G - 1) of each lo < 2^lb form a
+// closed group.  One thread applies the G stages to its group in the
+// stage kernel's order (inverse: largest span first), with the same
+// butterflies and twiddles, so the results are those of G stage passes.
+template <int G, bool INV>
+__global__ void __launch_bounds__(kThreads) fft_outer_kernel(double2* __restrict__ v, int n, int lb,
+                                                             const double2* __restrict__ ksi,
+                                                             const uint32_t* __restrict__ rot_group, int lm) {
+  constexpr int R = 1 << G;
+  const int lo = blockIdx.x * kThreads + threadIdx.x;
+  if (lo >= (1 << lb)) return;
+  double2* vec = v + (size_t)blockIdx.y * n;
+  double2 x[R];
+#pragma unroll
+  for (int h = 0; h < R; ++h) x[h] = vec[((size_t)h << lb) + lo];
+#pragma unroll
+  for (int it = 0; it < G; ++it) {
+    const int s = INV ? (G - 1 - it) : it;  // stage lg = lb + 1 + s
+    const int lg = lb + 1 + s;
+#pragma unroll
+    for (int h = 0; h < R; ++h) {
+      if (h & (1 << s)) continue;
+      const int j = ((h & ((1 << s) - 1)) << lb) + lo;  // index within the span
+      const uint32_t rg = __ldg(rot_group + j);
+      if constexpr (INV)
+        inv_bfly(x[h], x[h | (1 << s)], ksi, rg, lg, lm);
+      else
+        fwd_bfly(x[h], x[h | (1 << s)], ksi, rg, lg, lm);
+    }
+  }
+#pragma unroll
+  for (int h = 0; h < R; ++h) vec[((size_t)h << lb) + lo] = x[h];
+}
+
 // all stages with span <= blk inside one aligned block of blk entries
 __global__ void __launch_bounds__(kThreads) fft_smem_kernel(double2* __restrict__ v, int n, int lb, bool inverse,
                                                             const double2* __restrict__ ksi,
@@ -241,13 +277,35 @@ __global__ void __launch_bounds__(kThreads) take_real_kernel(const double2* __re
 
 constexpr int kSmemLog = 11;  // log2 kSmemLen
 
+// the stages with span above 2^lb: one register pass for up to 5 of them
+// (logN <= 17), else one pass per stage
+void fft_outer(const Context& c, double2* v, int batch, int lb, int ln, bool inverse, cudaStream_t st) {
+  const int G = ln - lb, n = 1 << ln, lm = c.logN + 1;
+  if (G <= 0) return;
+  const dim3 grid(((1 << lb) + kThreads - 1) / kThreads, batch);
+#define CKKS_FFT_OUTER(GG)                                                                           \
+  (inverse ? fft_outer_kernel<GG, true> : fft_outer_kernel<GG, false>)<<<grid, kThreads, 0, st>>>( \
+      v, n, lb, c.d_ksi, c.d_rot_group, lm)
+  switch (G) {
+    case 1: CKKS_FFT_OUTER(1); return;
+    case 2: CKKS_FFT_OUTER(2); return;
+    case 3: CKKS_FFT_OUTER(3); return;
+    case 4: CKKS_FFT_OUTER(4); return;
+    case 5: CKKS_FFT_OUTER(5); return;
+    default: break;
+  }
+#undef CKKS_FFT_OUTER
+  for (int k = 0; k < G; ++k) {
+    const int lg = inverse ? ln - k : lb + 1 + k;
+    fft_stage_kernel<<<dim3((n / 2 + kThreads - 1) / kThreads, batch), kThreads, 0, st>>>(v, n, lg, inverse, c.d_ksi,
+                                                                                          c.d_rot_group, lm);
+  }
+}
+
 void fft_inverse_batch(const Context& c, double2* v, int batch, cudaStream_t st) {
   const int ln = c.logN - 1, n = 1 << ln, lm = c.logN + 1;
   const int lb = ln < kSmemLog ? ln : kSmemLog;
-  for (int lg = ln; lg > lb; --lg) {
-    fft_stage_kernel<<<dim3((n / 2 + kThreads - 1) / kThreads, batch), kThreads, 0, st>>>(v, n, lg, true, c.d_ksi,
-                                                                                          c.d_rot_group, lm);
-  }
+  fft_outer(c, v, batch, lb, ln, true, st);
   fft_smem_kernel<<<dim3(n >> lb, batch), kThreads, 0, st>>>(v, n, lb, true, c.d_ksi, c.d_rot_group, lm);
   CKKS_CUDA(cudaGetLastError());
 }
@@ -256,10 +314,7 @@ void fft_forward_batch(const Context& c, double2* v, int batch, cudaStream_t st)
   const int ln = c.logN - 1, n = 1 << ln, lm = c.logN + 1;
   const int lb = ln < kSmemLog ? ln : kSmemLog;
   fft_smem_kernel<<<dim3(n >> lb, batch), kThreads, 0, st>>>(v, n, lb, false, c.d_ksi, c.d_rot_group, lm);
-  for (int lg = lb + 1; lg <= ln; ++lg) {
-    fft_stage_kernel<<<dim3((n / 2 + kThreads - 1) / kThreads, batch), kThreads, 0, st>>>(v, n, lg, false, c.d_ksi,
-                                                                                          c.d_rot_group, lm);
-  }
+  fft_outer(c, v, batch, lb, ln, false, st);
   CKKS_CUDA(cudaGetLastError());
 }
 
