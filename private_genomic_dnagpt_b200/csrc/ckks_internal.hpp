@@ -423,6 +423,23 @@ struct KsBatch {
   uint8_t src[kKsBatch];  // keyswitch_hoisted_multi: the ModUp input of each item
   int M;
 };
+
+// ModDown's combine step fused into the forward transform of the converted
+// limbs (batch limb (2 m + p) limbs + t = item m, part p, limb t): the last
+// pass stores out_p[m][t] = (acc[m][p][t] - conv) P^-1, plus add0[m]
+// permuted by the automorphism g[m] (part 0) or add1[m] (part 1), instead of
+// the converted limb.
+struct ModDownCombine {
+  const uint64_t* acc;     // [item][2][E limbs][N]
+  const ulonglong2* pinv;  // [limbs] P^-1 mod q_t as Shoup pairs
+  const uint64_t* add0[kKsBatch];
+  const uint64_t* add1[kKsBatch];
+  uint64_t* out0[kKsBatch];
+  uint64_t* out1[kKsBatch];
+  uint32_t g[kKsBatch];
+  int limbs, E;
+};
+void ntt_forward_moddown(const Context& c, uint64_t* conv, int items, const ModDownCombine& mc, cudaStream_t st);
 void keyswitch_batch(const Context& c, int limbs, const KsBatch& b, bool shared_input, cudaStream_t st);
 // Count of bounded device waits that gave up since the last call (each
 // leaves its CTA's outputs unwritten), read after the stream drains and

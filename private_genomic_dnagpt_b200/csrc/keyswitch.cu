@@ -632,38 +632,6 @@ __global__ void __launch_bounds__(kThreads) moddown_conv_batch_kernel(const uint
   }
 }
 
-__global__ void __launch_bounds__(kThreads) moddown_combine_batch_kernel(KsBatch b,
-                                                                        const uint64_t* __restrict__ acc_all,
-                                                                        const uint64_t* __restrict__ conv_all,
-                                                                        int limbs, int K, int logN,
-                                                                        const Mod* __restrict__ mods,
-                                                                        const ulonglong2* __restrict__ pinv) {
-  CKKS_PDL_ENTRY();
-  const int N = 1 << logN;
-  const int n = blockIdx.x * kThreads + threadIdx.x;
-  if (n >= N) return;
-  const int t = blockIdx.y % limbs, p = blockIdx.y / limbs, m = blockIdx.z;
-  const int E = limbs + K;
-  const uint64_t q = mods[t].q;
-  const ulonglong2 pv = pinv[t];
-  const uint64_t a = acc_all[((size_t)(2 * m + p) * E + t) * N + n];
-  const uint64_t cv = conv_all[((size_t)(2 * m + p) * limbs + t) * N + n];
-  uint64_t r = mul_shoup(sub_mod(a, cv, q), pv.x, pv.y, q);
-  if (p == 0) {
-    const uint64_t* add0 = b.add0[m];
-    if (add0) {
-      const uint32_t g = b.g[m];
-      const uint32_t src = (g == 1u) ? (uint32_t)n : auto_index((uint32_t)n, g, logN);
-      r = add_mod(r, add0[(size_t)t * N + src], q);
-    }
-    b.out0[m][(size_t)t * N + n] = r;
-  } else {
-    const uint64_t* add1 = b.add1[m];
-    if (add1) r = add_mod(r, add1[(size_t)t * N + n], q);
-    b.out1[m][(size_t)t * N + n] = r;
-  }
-}
-
 __global__ void __launch_bounds__(kThreads) rs_combine_batch_kernel(RsBatch b, const uint64_t* __restrict__ tmp,
                                                                     int limbs, int logN, const Mod* __restrict__ mods,
                                                                     const ulonglong2* __restrict__ inv) {
@@ -1099,6 +1067,25 @@ void bulk_wait_probe(const Context& c, const uint64_t* src, uint64_t* dst, bool 
   CKKS_CUDA(cudaGetLastError());
 }
 
+// ModDown's last two steps for the items of a batch: the forward transform
+// of the converted limbs with the combine step as its store
+void moddown_fused(const Context& c, const KsBatch& b, const uint64_t* acc, uint64_t* conv, int limbs,
+                   const ulonglong2* pinv, cudaStream_t st) {
+  ModDownCombine mc{};
+  mc.acc = acc;
+  mc.pinv = pinv;
+  mc.limbs = limbs;
+  mc.E = limbs + c.Kx(limbs);
+  for (int m = 0; m < b.M; ++m) {
+    mc.add0[m] = b.add0[m];
+    mc.add1[m] = b.add1[m];
+    mc.out0[m] = b.out0[m];
+    mc.out1[m] = b.out1[m];
+    mc.g[m] = b.g[m];
+  }
+  ntt_forward_moddown(c, conv, b.M, mc, st);
+}
+
 void keyswitch_batch(const Context& c, int limbs, const KsBatch& b, bool shared, cudaStream_t st) {
   if (c.alpha > kMaxAlpha || c.Kx(limbs) > kMaxK) throw Error(kErrArgument, "digit size above 16 is not supported");
   const int M = b.M;
@@ -1162,12 +1149,7 @@ void keyswitch_batch(const Context& c, int limbs, const KsBatch& b, bool shared,
     launch_pdl(kern, dim3((N / 2 + kThreads - 1) / kThreads, 2 * nch_dn, M), kThreads, 0, st, acc, conv, limbs, c.L, c.Kx(limbs), c.logN, nch_dn, c.d_mods, lt.d_down_phat);
   }
   CKKS_CUDA(cudaGetLastError());
-  ntt_forward(c, conv, M * 2 * limbs, LimbMap::q(limbs, c.L), st);
-  {
-    ProfScope ps(c, "moddown_combine", M * 8.0 * limbs * lb, st);
-    launch_pdl(moddown_combine_batch_kernel, dim3((N + kThreads - 1) / kThreads, 2 * limbs, M), kThreads, 0, st, b, acc, conv, limbs, c.Kx(limbs), c.logN, c.d_mods, lt.d_down_pinv);
-  }
-  CKKS_CUDA(cudaGetLastError());
+  moddown_fused(c, b, acc, conv, limbs, lt.d_down_pinv, st);
   c.release(dc);
   c.release(ext);
   c.release(acc);
@@ -1258,12 +1240,7 @@ void keyswitch_hoisted_multi(const Context& c, int limbs, const uint64_t* const*
       launch_pdl(kern, dim3((N / 2 + kThreads - 1) / kThreads, 2 * nch_dn, M), kThreads, 0, st, acc, conv, limbs, c.L, c.Kx(limbs), c.logN, nch_dn, c.d_mods, lt.d_down_phat);
     }
     CKKS_CUDA(cudaGetLastError());
-    ntt_forward(c, conv, M * 2 * limbs, LimbMap::q(limbs, c.L), st);
-    {
-      ProfScope ps(c, "moddown_combine", M * 8.0 * limbs * lb, st);
-      launch_pdl(moddown_combine_batch_kernel, dim3((N + kThreads - 1) / kThreads, 2 * limbs, M), kThreads, 0, st, b, acc, conv, limbs, c.Kx(limbs), c.logN, c.d_mods, lt.d_down_pinv);
-    }
-    CKKS_CUDA(cudaGetLastError());
+    moddown_fused(c, b, acc, conv, limbs, lt.d_down_pinv, st);
   }
   c.release(ext);
   c.release(acc);

@@ -426,11 +426,11 @@ __device__ __forceinline__ void ntt_pass_body_fp(const PassArgs& a, uint64_t* sm
   }
 }
 
-template <int S_LOG, bool INV, bool STRIDED, int R_LOG>
-__global__ void __launch_bounds__(PassShape<R_LOG>::kThreads, PassShape<R_LOG>::kMinBlocks)
-    ntt_pass_kernel(uint64_t* __restrict__ data, PassArgs a) {
-  extern __shared__ uint64_t sm[];
-  CKKS_PDL_ENTRY();  // launched as a programmatic dependent (launch_pdl)
+// One CTA of a pass.  The forward contiguous pass hands its output pairs
+// (coefficients n, n + 1 of batch limb `limb`, n even) to staged_store.
+template <int S_LOG, bool INV, bool STRIDED, int R_LOG, class StagedStore>
+__device__ __forceinline__ void ntt_pass_run(uint64_t* __restrict__ data, const PassArgs& a, uint64_t* sm,
+                                             StagedStore staged_store) {
   const int limb = blockIdx.y;
   if (a.map.skipped(limb)) return;
   const int prime = a.map.prime(limb);
@@ -470,13 +470,68 @@ __global__ void __launch_bounds__(PassShape<R_LOG>::kThreads, PassShape<R_LOG>::
     ntt_pass_body<S_LOG, INV, STRIDED, R_LOG>(a, sm, limb, sub_base, load0, store_last, pre_store);
   if (kStageOut) {
     __syncthreads();
-    uint64_t* dst = poly + ((size_t)sub_base << S_LOG);
+    const size_t n0 = (size_t)sub_base << S_LOG;
     for (int i = 2 * (int)threadIdx.x; i < W; i += 2 * nt) {
       const uint64_t x0 = sm[pass_saddr<S_LOG, false, R_LOG>(per, i >> S_LOG, i & ((1 << S_LOG) - 1))];
       const uint64_t x1 = sm[pass_saddr<S_LOG, false, R_LOG>(per, (i + 1) >> S_LOG, (i + 1) & ((1 << S_LOG) - 1))];
-      *reinterpret_cast<ulonglong2*>(dst + i) = make_ulonglong2(x0, x1);
+      staged_store(limb, poly, m, n0 + i, x0, x1);
     }
   }
+}
+
+template <int S_LOG, bool INV, bool STRIDED, int R_LOG>
+__global__ void __launch_bounds__(PassShape<R_LOG>::kThreads, PassShape<R_LOG>::kMinBlocks)
+    ntt_pass_kernel(uint64_t* __restrict__ data, PassArgs a) {
+  extern __shared__ uint64_t sm[];
+  CKKS_PDL_ENTRY();  // launched as a programmatic dependent (launch_pdl)
+  ntt_pass_run<S_LOG, INV, STRIDED, R_LOG>(
+      data, a, sm, [](int, uint64_t* poly, const Mod&, size_t n, uint64_t x0, uint64_t x1) {
+        *reinterpret_cast<ulonglong2*>(poly + n) = make_ulonglong2(x0, x1);
+      });
+}
+
+// The forward contiguous pass of ModDown's conversion with the combine step
+// as its store: batch limb (2 m + p) limbs + t holds conv (item m, part p,
+// limb t), and the pass writes (acc - conv) P^-1, plus the automorphism-
+// permuted c0 addend (part 0) or the c1 addend (part 1), straight to the
+// item's output instead of storing conv.
+template <int S_LOG, int R_LOG>
+__global__ void __launch_bounds__(PassShape<R_LOG>::kThreads, PassShape<R_LOG>::kMinBlocks)
+    ntt_moddown_pass_kernel(uint64_t* __restrict__ data, PassArgs a, ModDownCombine mc) {
+  extern __shared__ uint64_t sm[];
+  CKKS_PDL_ENTRY();
+  const int logN = a.logN;
+  ntt_pass_run<S_LOG, false, false, R_LOG>(
+      data, a, sm, [&](int limb, uint64_t*, const Mod& md, size_t n, uint64_t x0, uint64_t x1) {
+        const int t = limb % mc.limbs, pm = limb / mc.limbs, p = pm & 1, m = pm >> 1;
+        const size_t N = (size_t)1 << logN;
+        const uint64_t q = md.q;
+        const ulonglong2 pv = mc.pinv[t];
+        const ulonglong2 av = *reinterpret_cast<const ulonglong2*>(mc.acc + ((size_t)(2 * m + p) * mc.E + t) * N + n);
+        uint64_t r0 = mul_shoup(sub_mod(av.x, x0, q), pv.x, pv.y, q);
+        uint64_t r1 = mul_shoup(sub_mod(av.y, x1, q), pv.x, pv.y, q);
+        uint64_t* out;
+        if (p == 0) {
+          const uint64_t* add0 = mc.add0[m];
+          if (add0) {
+            const uint32_t g = mc.g[m];
+            // the automorphism maps the aligned pair onto an aligned pair
+            const uint32_t s = g == 1u ? (uint32_t)n : auto_index((uint32_t)n, g, logN);
+            r0 = add_mod(r0, add0[(size_t)t * N + s], q);
+            r1 = add_mod(r1, add0[(size_t)t * N + (s ^ 1u)], q);
+          }
+          out = mc.out0[m];
+        } else {
+          const uint64_t* add1 = mc.add1[m];
+          if (add1) {
+            const ulonglong2 bv = *reinterpret_cast<const ulonglong2*>(add1 + (size_t)t * N + n);
+            r0 = add_mod(r0, bv.x, q);
+            r1 = add_mod(r1, bv.y, q);
+          }
+          out = mc.out1[m];
+        }
+        *reinterpret_cast<ulonglong2*>(out + (size_t)t * N + n) = make_ulonglong2(r0, r1);
+      });
 }
 
 template <int S_LOG, bool INV, bool STRIDED>
@@ -505,6 +560,24 @@ void launch_pass(uint64_t* data, int nlimbs, const PassArgs& a0, int sms, cudaSt
   // a programmatic dependent: its launch can overlap the previous kernel's
   // last wave (the kernel waits for that grid on the device)
   launch_pdl(k, grid, dim3(threads), smem, st, data, a);
+}
+
+template <int S_LOG>
+void launch_moddown_pass(uint64_t* data, int nlimbs, const PassArgs& a0, const ModDownCombine& mc, int sms,
+                         cudaStream_t st) {
+  constexpr int R_LOG = 3;
+  constexpr int S = 1 << S_LOG;
+  constexpr int T = S >= (1 << R_LOG) ? S / (1 << R_LOG) : 1;
+  const int subs = (1 << a0.logN) / S;
+  int per = PassShape<R_LOG>::kThreads / T;
+  if (per > subs) per = subs;
+  while (per > 1 && per * T > 32 && (subs / per) * nlimbs < 4 * sms) per >>= 1;
+  PassArgs a = a0;
+  a.per_cta = per;
+  const size_t smem = (size_t)S * per * sizeof(uint64_t);
+  auto k = ntt_moddown_pass_kernel<S_LOG, R_LOG>;
+  if (smem > 48 * 1024) cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  launch_pdl(k, dim3(subs / per, nlimbs), dim3(per * T), smem, st, data, a, mc);
 }
 
 template <bool INV, bool STRIDED>
@@ -554,6 +627,40 @@ void ntt_forward(const Context& c, uint64_t* data, int nlimbs, LimbMap map, cuda
   {
     ProfScope ps(c, "ntt_fwd_cols", bytes, st);
     dispatch_pass<false, false>(s2, data, nlimbs, a, c.sms, st);
+  }
+  CKKS_CUDA(cudaGetLastError());
+}
+
+void ntt_forward_moddown(const Context& c, uint64_t* conv, int items, const ModDownCombine& mc, cudaStream_t st) {
+  const int nlimbs = items * 2 * mc.limbs;
+  if (nlimbs <= 0) return;
+  PassArgs a{};
+  a.tw = c.d_tw;
+  a.twd = c.d_twd;
+  a.mods = c.d_mods;
+  a.map = LimbMap::q(mc.limbs, c.L);
+  a.logN = c.logN;
+  const double lb = c.limb_bytes();
+  const int s1 = c.logN / 2, s2 = c.logN - s1;
+  {
+    ProfScope ps(c, "ntt_fwd_rows", nlimbs * lb, st);
+    dispatch_pass<false, true>(s1, conv, nlimbs, a, c.sms, st);
+  }
+  {
+    // the pass's half of the transform, the accumulator read, the addends
+    int adds = 0;
+    for (int m = 0; m < items; ++m) adds += (mc.add0[m] ? 1 : 0) + (mc.add1[m] ? 1 : 0);
+    ProfScope ps(c, "ntt_fwd_cols_moddown", (2.0 * nlimbs + (double)adds * mc.limbs) * lb, st);
+    switch (s2) {
+      case 3: launch_moddown_pass<3>(conv, nlimbs, a, mc, c.sms, st); break;
+      case 4: launch_moddown_pass<4>(conv, nlimbs, a, mc, c.sms, st); break;
+      case 5: launch_moddown_pass<5>(conv, nlimbs, a, mc, c.sms, st); break;
+      case 6: launch_moddown_pass<6>(conv, nlimbs, a, mc, c.sms, st); break;
+      case 7: launch_moddown_pass<7>(conv, nlimbs, a, mc, c.sms, st); break;
+      case 8: launch_moddown_pass<8>(conv, nlimbs, a, mc, c.sms, st); break;
+      case 9: launch_moddown_pass<9>(conv, nlimbs, a, mc, c.sms, st); break;
+      default: throw Error(kErrArgument, "ring dimension outside 2^6 .. 2^17");
+    }
   }
   CKKS_CUDA(cudaGetLastError());
 }
